@@ -1,0 +1,88 @@
+"""Throughput of the sm_100a GEMM against cuBLAS (torch.matmul) on the model's shapes.
+
+Timing: CUDA events on the launching stream after warm-up; an L2-sized buffer is rewritten
+between timed launches so every launch reads its operands from HBM.
+Usage: python -m marin_experiments_b200.benchmarks.gemm_bench [--json out.json]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from marin_experiments_b200.ops import gemm as G
+
+SHAPES = [
+    # (name, M, N, K, mode)
+    ("square8192", 8192, 8192, 8192, "fwd"),
+    ("qkv_fwd", 16384, 4608, 1536, "fwd"),
+    ("o_fwd", 16384, 1536, 1536, "fwd"),
+    ("shared_gateup_fwd", 16384, 6144, 1536, "fwd"),
+    ("shared_down_fwd", 16384, 1536, 3072, "fwd"),
+    ("lm_head_fwd", 16384, 128256, 1536, "fwd"),
+    ("o_dx", 16384, 1536, 1536, "dx"),
+    ("o_dw", 16384, 1536, 1536, "dw"),
+    ("lm_head_dw", 16384, 128256, 1536, "dw"),
+]
+
+
+def _time(fn, flush, iters=10, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        ts.append(s.elapsed_time(e))
+    ts.sort()
+    return ts[len(ts) // 2]
+
+
+def run(shapes=SHAPES):
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    rows = []
+    for name, m, n, k, mode in shapes:
+        if mode == "fwd":
+            a = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+            b = torch.randn(n, k, device="cuda").to(torch.bfloat16)
+            c = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+            mine = lambda: G.linear(a, b, out=c)
+            ref = lambda: torch.matmul(a, b.t(), out=c)
+        elif mode == "dx":
+            a = torch.randn(m, n, device="cuda").to(torch.bfloat16)  # dy
+            b = torch.randn(n, k, device="cuda").to(torch.bfloat16)  # w
+            c = torch.empty(m, k, device="cuda", dtype=torch.bfloat16)
+            mine = lambda: G.linear_dx(a, b, out=c)
+            ref = lambda: torch.matmul(a, b, out=c)
+        else:  # dw: dy [m, n], x [m, k] -> [n, k] fp32 accumulate
+            a = torch.randn(m, n, device="cuda").to(torch.bfloat16)
+            b = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+            c = torch.zeros(n, k, device="cuda", dtype=torch.float32)
+            cb = torch.empty(n, k, device="cuda", dtype=torch.bfloat16)
+            mine = lambda: G.linear_dw(a, b, out=c, accum=True)
+            ref = lambda: torch.matmul(a.t(), b, out=cb)
+        flops = 2.0 * m * n * k
+        t_mine = _time(mine, flush)
+        t_ref = _time(ref, flush)
+        rows.append({"name": name, "M": m, "N": n, "K": k, "mode": mode, "ms": t_mine, "cublas_ms": t_ref,
+                     "tflops": flops / t_mine / 1e9, "cublas_tflops": flops / t_ref / 1e9})
+        print(json.dumps(rows[-1]), flush=True)
+        del a, b, c
+    return rows
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--json", default=None)
+    args = ap.parse_args()
+    rows = run()
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(rows, f, indent=1)

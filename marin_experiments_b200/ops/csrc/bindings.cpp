@@ -1,0 +1,107 @@
+// Torch bindings of the sm_100a kernels. Every op validates shapes, dtypes, devices and
+// alignment on the host and raises on a bad argument instead of launching.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "launch.h"
+#include "kernels.h"
+
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_code(int code, const char* what) { TORCH_CHECK(code == 0, what, ": launch failed (code ", code, ")"); }
+
+void check_2d_bf16(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bf16");
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must be contiguous in its last dimension");
+}
+
+template <class T>
+T* opt_ptr(const c10::optional<at::Tensor>& t) {
+  return t.has_value() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+// C[g] = A'[g] B'[g]^T with A' = A (K-major, A is [rows, K]) or A^T (MN-major, A is [K, rows]),
+// likewise B'. See gemm_sm100.cuh for the grouping and ragged semantics.
+void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const at::Tensor& C, int64_t G,
+          int64_t M, int64_t N, int64_t K, const c10::optional<at::Tensor>& counts, int64_t ragged, int64_t a_grp,
+          int64_t b_grp, int64_t c_grp, int64_t epi, int64_t bn, bool accum, double alpha,
+          const c10::optional<at::Tensor>& C2, const c10::optional<at::Tensor>& R,
+          const c10::optional<at::Tensor>& row_scale, int64_t act_kind, const at::Tensor& err) {
+  check_2d_bf16(A, "A");
+  check_2d_bf16(B, "B");
+  TORCH_CHECK(C.is_cuda() && C.dim() == 2 && C.stride(1) == 1, "C must be a 2-D CUDA tensor, contiguous rows");
+  TORCH_CHECK(C.scalar_type() == at::kBFloat16 || C.scalar_type() == at::kFloat, "C must be bf16 or f32");
+  TORCH_CHECK(!accum || C.scalar_type() == at::kFloat, "accumulation requires an f32 C");
+  TORCH_CHECK(err.is_cuda() && err.scalar_type() == at::kInt, "err must be a CUDA int32 tensor");
+  if (counts.has_value()) {
+    TORCH_CHECK(counts->is_cuda() && counts->scalar_type() == at::kInt && counts->numel() >= G,
+                "counts must be a CUDA int32 tensor with G entries");
+  }
+  if (R.has_value()) check_2d_bf16(*R, "R");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0, "C must be 16-byte aligned");
+  TORCH_CHECK((C.stride(0) * C.element_size()) % 16 == 0, "C row stride must be a multiple of 16 bytes");
+  // Epilogues store 32-column chunks: C must be wide enough for N rounded up to 32.
+  TORCH_CHECK(C.size(1) >= ((N + 31) / 32) * 32 || epi == 1, "C must have at least round_up(N, 32) columns");
+  const c10::cuda::CUDAGuard guard(A.device());
+  mxk::GemmLaunch L{};
+  L.a = A.data_ptr();
+  L.lda = A.stride(0);
+  L.a_inner = A.size(1);
+  L.a_outer = A.size(0);
+  L.a_mn = a_mn ? 1 : 0;
+  L.b = B.data_ptr();
+  L.ldb = B.stride(0);
+  L.b_inner = B.size(1);
+  L.b_outer = B.size(0);
+  L.b_mn = b_mn ? 1 : 0;
+  L.bn = (int)bn;
+  L.epi = (int)epi;
+  mxk::GemmParams& p = L.p;
+  p.G = (int)G;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.counts = counts.has_value() ? reinterpret_cast<const int*>(counts->data_ptr()) : nullptr;
+  p.ragged = (int)ragged;
+  p.a_grp = (int)a_grp;
+  p.b_grp = (int)b_grp;
+  p.c_grp = (int)c_grp;
+  p.C = C.data_ptr();
+  p.ldc = (int)C.stride(0);
+  p.c_f32 = C.scalar_type() == at::kFloat ? 1 : 0;
+  p.c_accum = accum ? 1 : 0;
+  p.C2 = opt_ptr<void>(C2);
+  p.ldc2 = C2.has_value() ? (int)C2->stride(0) : 0;
+  p.R = opt_ptr<const void>(R);
+  p.ldr = R.has_value() ? (int)R->stride(0) : 0;
+  p.row_scale = opt_ptr<const float>(row_scale);
+  p.alpha = (float)alpha;
+  p.act_kind = (int)act_kind;
+  p.err = reinterpret_cast<int*>(err.data_ptr());
+  check_code(mxk::launch_gemm(L, cur_stream()), "gemm");
+}
+
+int64_t num_sms() { return mxk::num_sms(); }
+
+}  // namespace
+
+void register_elementwise(pybind11::module& m);
+void register_attention(pybind11::module& m);
+void register_moe(pybind11::module& m);
+void register_optim(pybind11::module& m);
+void register_comm(pybind11::module& m);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("gemm", &gemm, "sm_100a tcgen05 GEMM (grouped / ragged, fused epilogues)");
+  m.def("num_sms", &num_sms);
+  register_elementwise(m);
+  register_attention(m);
+  register_moe(m);
+  register_optim(m);
+  register_comm(m);
+}

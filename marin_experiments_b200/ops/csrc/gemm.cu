@@ -1,0 +1,115 @@
+// Host side of the sm_100a GEMM: TMA tensor-map encoding, argument validation and the
+// (BN, operand majors, epilogue) dispatch table.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "gemm_sm100.cuh"
+#include "launch.h"
+
+namespace mxk {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix [outer, inner] with row stride `ld` elements,
+// 128-byte swizzle, box {box_inner, box_outer}. Out-of-bounds elements read as zero.
+bool make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner,
+                       int box_outer) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
+  CUtensorMap ta, tb;
+  // A tile: K-major -> box {64 (K), 128 rows}; MN-major -> box {64 (M), 64 (K rows)}
+  if (!make_tmap_bf16_2d(&ta, L.a, L.a_inner, L.a_outer, L.lda, 64, A_MN ? 64 : kBM)) return kErrBadArgs;
+  if (!make_tmap_bf16_2d(&tb, L.b, L.b_inner, L.b_outer, L.ldb, 64, B_MN ? 64 : BN)) return kErrBadArgs;
+  auto kern = gemm_sm100_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  constexpr int smem = gemm_smem_bytes<BN, STAGES>();
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return kErrBadArgs;
+    attr_set = true;
+  }
+  // Upper bound on the number of tiles (ragged groups may have fewer); the kernel strides.
+  const int n_tiles = (L.p.N + BN - 1) / BN;
+  const int m_tiles = (L.p.M + kBM - 1) / kBM;
+  long long tiles = (long long)L.p.G * m_tiles * n_tiles;
+  int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+  if (grid <= 0) return 0;
+  kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, L.p);
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgs;
+}
+
+#define MXK_CASE(BN_, ST_, AMN_, BMN_, EPI_)                                                     \
+  if (L.bn == BN_ && L.a_mn == AMN_ && L.b_mn == BMN_ && L.epi == EPI_)                        \
+    return launch_impl<BN_, ST_, AMN_, BMN_, EPI_>(L, stream);
+
+int launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
+  if (L.p.G <= 0 || L.p.G > kMaxGroups || L.p.K <= 0 || L.p.N <= 0 || L.p.M <= 0) return kErrBadArgs;
+  if (L.p.K % kBK != 0 && L.p.ragged != 2) return kErrBadArgs;
+  if ((reinterpret_cast<uintptr_t>(L.a) | reinterpret_cast<uintptr_t>(L.b)) & 15) return kErrBadArgs;
+  if ((L.lda * 2) % 16 || (L.ldb * 2) % 16) return kErrBadArgs;
+  // plain stores / accumulation
+  MXK_CASE(256, 4, false, false, EPI_STORE)
+  MXK_CASE(128, 6, false, false, EPI_STORE)
+  MXK_CASE(64, 8, false, false, EPI_STORE)
+  MXK_CASE(256, 4, false, true, EPI_STORE)
+  MXK_CASE(128, 6, false, true, EPI_STORE)
+  MXK_CASE(64, 8, false, true, EPI_STORE)
+  MXK_CASE(256, 4, true, true, EPI_STORE)
+  MXK_CASE(128, 6, true, true, EPI_STORE)
+  MXK_CASE(64, 8, true, true, EPI_STORE)
+  // fused epilogues (forward, K-major x K-major)
+  MXK_CASE(256, 4, false, false, EPI_SWIGLU)
+  MXK_CASE(256, 4, false, false, EPI_RESID)
+  MXK_CASE(128, 6, false, false, EPI_RESID)
+  MXK_CASE(256, 4, false, false, EPI_GATE_MUL)
+  MXK_CASE(128, 6, false, false, EPI_GATE_MUL)
+  MXK_CASE(128, 6, false, false, EPI_SILU)
+  MXK_CASE(256, 4, false, false, EPI_ACT)
+  MXK_CASE(128, 6, false, false, EPI_ACT)
+  MXK_CASE(256, 4, false, false, EPI_ROWSCALE)
+  MXK_CASE(128, 6, false, false, EPI_ROWSCALE)
+  MXK_CASE(256, 4, false, false, EPI_CE)
+  return kErrBadArgs;
+}
+
+}  // namespace mxk

@@ -1,0 +1,26 @@
+// Argument block of the sm_100a GEMM kernel (plain C++: shared by device and host code).
+#pragma once
+#include <stdint.h>
+
+namespace mxk {
+
+struct GemmParams {
+  int G, M, N, K;
+  const int* counts;  // per-group ragged extent (device), or nullptr
+  int ragged;         // 0: none, 1: M ragged, 2: K ragged
+  int a_grp, b_grp, c_grp;
+  void* C;
+  int ldc;
+  int c_f32;
+  int c_accum;
+  void* C2;  // EPI_SWIGLU: activation output; EPI_SILU/EPI_ACT: pre-activation copy; EPI_CE: stats
+  int ldc2;
+  const void* R;  // bf16 residual / gate input
+  int ldr;
+  const float* row_scale;
+  float alpha;
+  int act_kind;  // 0 silu, 1 relu, 2 gelu(tanh)
+  int* err;
+};
+
+}  // namespace mxk

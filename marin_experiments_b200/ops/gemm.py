@@ -1,0 +1,106 @@
+"""Python front end of the sm_100a tcgen05 GEMM (``csrc/gemm_sm100.cuh``).
+
+Conventions: ``C = A' @ B'^T`` where ``A'`` is ``[M, K]`` and ``B'`` is ``[N, K]``. A K-major
+operand is passed as stored (``[rows, K]``); an MN-major operand is passed as its stored
+``[K, rows]`` tensor with ``*_mn=True``. Linear layers keep weights ``[out, in]`` so that
+
+* forward  ``y  = x @ W^T``      -> A = x (K-major),   B = W (K-major)
+* input    ``dx = dy @ W``       -> A = dy (K-major),  B = W (MN-major)
+* weight   ``dW = dy^T @ x``     -> A = dy (MN-major), B = x (MN-major)
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._ext import err_flag, ext
+
+EPI = {"store": 0, "swiglu": 1, "resid": 2, "gate_mul": 3, "silu": 4, "rowscale": 5, "ce": 6, "act": 7}
+ACT = {"silu": 0, "relu": 1, "gelu": 2}
+
+
+def _pick_bn(n: int, epi: str, b_mn: bool, a_mn: bool) -> int:
+    if epi in ("swiglu", "ce"):
+        return 256
+    if epi == "silu":
+        return 128
+    if n % 256 == 0 and n >= 1024:
+        return 256
+    if n % 128 == 0:
+        return 128
+    return 64
+
+
+def gemm(a, b, c, *, a_mn=False, b_mn=False, G=1, M=None, N=None, K=None, counts=None, ragged=0,
+         a_grp=0, b_grp=0, c_grp=0, epi="store", bn=None, accum=False, alpha=1.0, c2=None, r=None,
+         row_scale=None, act="silu"):
+    if bn is None:
+        bn = _pick_bn(N, epi, b_mn, a_mn)
+    ext().gemm(a, a_mn, b, b_mn, c, G, M, N, K, counts, ragged, a_grp, b_grp, c_grp, EPI[epi], bn, accum,
+               float(alpha), c2, r, row_scale, ACT[act], err_flag(a.device))
+    return c
+
+
+def linear(x, w, *, out=None, epi="store", **kw):
+    """``x [M, K] @ w[N, K]^T`` -> ``[M, N]`` bf16 (or into ``out``)."""
+    m, k = x.shape
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+    return gemm(x, w, out, M=m, N=n, K=k, epi=epi, **kw)
+
+
+def linear_dx(dy, w, *, out=None, accum=False):
+    """``dy [M, N] @ w [N, K]`` -> ``[M, K]``."""
+    m, n = dy.shape
+    k = w.shape[1]
+    if out is None:
+        out = torch.empty(m, k, dtype=torch.bfloat16, device=dy.device)
+    return gemm(dy, w, out, b_mn=True, M=m, N=k, K=n, accum=accum)
+
+
+def linear_dw(dy, x, *, out=None, accum=False, alpha=1.0):
+    """``dy [T, N]^T @ x [T, K]`` -> ``[N, K]`` (fp32 when accumulating into a main grad)."""
+    t, n = dy.shape
+    k = x.shape[1]
+    if out is None:
+        out = torch.empty(n, k, dtype=torch.float32, device=dy.device)
+    return gemm(dy, x, out, a_mn=True, b_mn=True, M=n, N=k, K=t, accum=accum, alpha=alpha)
+
+
+def grouped_linear(x, w, counts, *, out=None, epi="store", c2=None, **kw):
+    """Per-expert ``x[g] @ w[g]^T`` over a capacity layout.
+
+    x: ``[G*C, K]`` (expert g owns rows ``[g*C, (g+1)*C)``, only the first ``counts[g]`` valid),
+    w: ``[G*N, K]`` -> out ``[G*C, N]``; tiles past ``counts[g]`` rows are skipped."""
+    g = counts.numel()
+    cap = x.shape[0] // g
+    n = w.shape[0] // g
+    k = x.shape[1]
+    if out is None:
+        out = torch.empty(x.shape[0], n, dtype=torch.bfloat16, device=x.device)
+    return gemm(x, w, out, G=g, M=cap, N=n, K=k, counts=counts, ragged=1, a_grp=cap, b_grp=n, c_grp=cap,
+                epi=epi, c2=c2, **kw)
+
+
+def grouped_linear_dx(dy, w, counts, *, out=None):
+    """Per-expert ``dy[g] [C, N] @ w[g] [N, K]`` -> ``[G*C, K]``."""
+    g = counts.numel()
+    cap = dy.shape[0] // g
+    n = w.shape[0] // g
+    k = w.shape[1]
+    if out is None:
+        out = torch.empty(dy.shape[0], k, dtype=torch.bfloat16, device=dy.device)
+    return gemm(dy, w, out, b_mn=True, G=g, M=cap, N=k, K=n, counts=counts, ragged=1, a_grp=cap, b_grp=n,
+                c_grp=cap)
+
+
+def grouped_linear_dw(dy, x, counts, *, out, accum=True, alpha=1.0):
+    """Per-expert ``dy[g]^T @ x[g]`` contracting over the first ``counts[g]`` rows (rounded up to
+    64; rows past the count must be zero) -> ``out [G*N, K]`` fp32."""
+    g = counts.numel()
+    cap = dy.shape[0] // g
+    n = dy.shape[1]
+    k = x.shape[1]
+    return gemm(dy, x, out, a_mn=True, b_mn=True, G=g, M=n, N=k, K=cap, counts=counts, ragged=2, a_grp=cap,
+                b_grp=cap, c_grp=n, accum=accum, alpha=alpha)
