@@ -46,7 +46,7 @@ def build(verbose: bool = False):
         extra_cuda_cflags=CUDA_FLAGS,
         extra_cflags=CXX_FLAGS,
         extra_include_paths=[CSRC],
-        extra_ldflags=["-lcuda"] if False else [],
+        extra_ldflags=["-ldl"],
         build_directory=BUILD_DIR,
         verbose=verbose,
         with_cuda=True,

@@ -4,6 +4,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdio>
+#include <cstdlib>
+
 #include "launch.h"
 #include "kernels.h"
 
@@ -32,6 +35,7 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const 
           int64_t b_grp, int64_t c_grp, int64_t epi, int64_t bn, bool accum, double alpha,
           const c10::optional<at::Tensor>& C2, const c10::optional<at::Tensor>& R,
           const c10::optional<at::Tensor>& row_scale, int64_t act_kind, const at::Tensor& err) {
+  if (std::getenv("MXK_TRACE")) { std::fprintf(stderr, "[mxk] gemm binding enter\n"); std::fflush(stderr); }
   check_2d_bf16(A, "A");
   check_2d_bf16(B, "B");
   TORCH_CHECK(C.is_cuda() && C.dim() == 2 && C.stride(1) == 1, "C must be a 2-D CUDA tensor, contiguous rows");
@@ -83,6 +87,7 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const 
   p.alpha = (float)alpha;
   p.act_kind = (int)act_kind;
   p.err = reinterpret_cast<int*>(err.data_ptr());
+  if (std::getenv("MXK_TRACE")) { std::fprintf(stderr, "[mxk] binding -> launch_gemm\n"); std::fflush(stderr); }
   check_code(mxk::launch_gemm(L, cur_stream()), "gemm");
 }
 
@@ -90,18 +95,10 @@ int64_t num_sms() { return mxk::num_sms(); }
 
 }  // namespace
 
-void register_elementwise(pybind11::module& m);
-void register_attention(pybind11::module& m);
-void register_moe(pybind11::module& m);
-void register_optim(pybind11::module& m);
-void register_comm(pybind11::module& m);
+void register_ops(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "sm_100a tcgen05 GEMM (grouped / ragged, fused epilogues)");
   m.def("num_sms", &num_sms);
-  register_elementwise(m);
-  register_attention(m);
-  register_moe(m);
-  register_optim(m);
-  register_comm(m);
+  register_ops(m);
 }

@@ -1,2 +1,2 @@
-#include <torch/extension.h>
-void register_comm(pybind11::module& m) {}
+// Peer-to-peer collectives over NVLink (filled in by the expert-parallel exchange).
+#include <cuda_runtime.h>

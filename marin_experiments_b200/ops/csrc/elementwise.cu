@@ -1,2 +1,643 @@
-#include <torch/extension.h>
-void register_elementwise(pybind11::module& m) {}
+// Row-wise and elementwise sm_100a kernels: RMSNorm, embedding gather / scatter-add,
+// QK-norm + RoPE, exclusive self-attention + head gate, activation backward passes and the
+// cross-entropy gradient. All are bandwidth-bound; rows are processed one warp each with
+// 16-byte vector accesses.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.h"
+
+namespace mxk {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
+
+// ------------------------------------------------------------------------------------ RMSNorm
+// y = x * rsqrt(mean(x^2) + eps) * w ; one warp per row, D a multiple of 8.
+__global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
+                                   __nv_bfloat16* __restrict__ y, float* __restrict__ rstd, int T, int D,
+                                   float eps) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < T; row += gridDim.x * warps) {
+    const __nv_bfloat16* xr = x + (long)row * D;
+    float ss = 0.f;
+    for (int c = lane * 8; c < D; c += 256) {
+      float f[8];
+      load8(xr + c, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / D + eps);
+    if (lane == 0) rstd[row] = r;
+    for (int c = lane * 8; c < D; c += 256) {
+      float f[8];
+      load8(xr + c, f);
+      float4 w0 = *reinterpret_cast<const float4*>(w + c);
+      float4 w1 = *reinterpret_cast<const float4*>(w + c + 4);
+      float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = f[i] * r * wv[i];
+      store8(y + (long)row * D + c, f);
+    }
+  }
+}
+
+// dx = r * (g - xhat * mean(g * xhat)), g = dy * w, xhat = x * r ; dw += sum_rows dy * xhat.
+// dw partials are kept per lane in registers (column slots fixed per lane) and flushed with one
+// atomicAdd per column per block. Optional dres is added to dx (residual-stream gradient).
+template <int MAXV>
+__global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                   const float* __restrict__ w, const float* __restrict__ rstd,
+                                   const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
+                                   float* __restrict__ dw, int T, int D) {
+  extern __shared__ float sdw[];  // [D]
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) sdw[c] = 0.f;
+  __syncthreads();
+  float acc[MAXV][8];
+#pragma unroll
+  for (int v = 0; v < MAXV; ++v)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[v][i] = 0.f;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < T; row += gridDim.x * warps) {
+    const float r = rstd[row];
+    float dot = 0.f;
+#pragma unroll
+    for (int v = 0; v < MAXV; ++v) {
+      const int c = lane * 8 + v * 256;
+      if (c < D) {
+        float g[8], xv[8];
+        load8(dy + (long)row * D + c, g);
+        load8(x + (long)row * D + c, xv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float xh = xv[i] * r;
+          acc[v][i] += g[i] * xh;
+          dot += g[i] * w[c + i] * xh;
+        }
+      }
+    }
+    dot = warp_sum(dot) / D;
+#pragma unroll
+    for (int v = 0; v < MAXV; ++v) {
+      const int c = lane * 8 + v * 256;
+      if (c < D) {
+        float g[8], xv[8], o[8];
+        load8(dy + (long)row * D + c, g);
+        load8(x + (long)row * D + c, xv);
+        float rr[8];
+        if (dres) load8(dres + (long)row * D + c, rr);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          o[i] = r * (g[i] * w[c + i] - xv[i] * r * dot);
+          if (dres) o[i] += rr[i];
+        }
+        store8(dx + (long)row * D + c, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int v = 0; v < MAXV; ++v) {
+    const int c = lane * 8 + v * 256;
+    if (c < D)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) atomicAdd(&sdw[c + i], acc[v][i]);
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dw[c], sdw[c]);
+}
+
+// ----------------------------------------------------------------------------------- embedding
+__global__ void embed_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
+                                 __nv_bfloat16* __restrict__ out, int T, int D, int V) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < T; row += gridDim.x * warps) {
+    long id = ids[row];
+    if (id < 0 || id >= V) id = 0;
+    const uint4* src = reinterpret_cast<const uint4*>(table + id * (long)D);
+    uint4* dst = reinterpret_cast<uint4*>(out + (long)row * D);
+    for (int c = lane; c < D / 8; c += 32) dst[c] = src[c];
+  }
+}
+
+__global__ void embed_bwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ dout,
+                                 float* __restrict__ dtable, int T, int D, int V) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < T; row += gridDim.x * warps) {
+    long id = ids[row];
+    if (id < 0 || id >= V) continue;
+    float* dst = dtable + id * (long)D;
+    for (int c = lane * 8; c < D; c += 256) {
+      float f[8];
+      load8(dout + (long)row * D + c, f);
+      atomicAdd(reinterpret_cast<float4*>(dst + c), make_float4(f[0], f[1], f[2], f[3]));
+      atomicAdd(reinterpret_cast<float4*>(dst + c + 4), make_float4(f[4], f[5], f[6], f[7]));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------- GatedNorm / acts
+// out = y * sigmoid(z):  dy_direct = dout * s ; dz = dout * y * s * (1 - s)
+__global__ void gate_mul_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ y,
+                                    const __nv_bfloat16* __restrict__ z, __nv_bfloat16* __restrict__ dy,
+                                    __nv_bfloat16* __restrict__ dz, long n8) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
+    float d[8], yv[8], zv[8], a[8], b[8];
+    load8(dout + i * 8, d);
+    load8(y + i * 8, yv);
+    load8(z + i * 8, zv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float s = sigm(zv[k]);
+      a[k] = d[k] * s;
+      b[k] = d[k] * yv[k] * s * (1.f - s);
+    }
+    store8(dy + i * 8, a);
+    store8(dz + i * 8, b);
+  }
+}
+
+__device__ __forceinline__ float act_f(float x, int kind) {
+  if (kind == 1) return fmaxf(x, 0.f);
+  if (kind == 2) {
+    const float u = 0.7978845608f * (x + 0.044715f * x * x * x);
+    return 0.5f * x * (1.f + tanhf(u));
+  }
+  return x * sigm(x);
+}
+
+__device__ __forceinline__ float act_grad(float x, int kind) {
+  if (kind == 1) return x > 0.f ? 1.f : 0.f;
+  if (kind == 2) {
+    const float u = 0.7978845608f * (x + 0.044715f * x * x * x);
+    const float t = tanhf(u);
+    const float du = 0.7978845608f * (1.f + 3.f * 0.044715f * x * x);
+    return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * du;
+  }
+  const float s = sigm(x);
+  return s * (1.f + x * (1.f - s));
+}
+
+// dh = dact * act'(h)
+__global__ void act_bwd_kernel(const __nv_bfloat16* __restrict__ da, const __nv_bfloat16* __restrict__ h,
+                               __nv_bfloat16* __restrict__ dh, long n8, int kind) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
+    float d[8], hv[8], o[8];
+    load8(da + i * 8, d);
+    load8(h + i * 8, hv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = d[k] * act_grad(hv[k], kind);
+    store8(dh + i * 8, o);
+  }
+}
+
+// Blocked SwiGLU backward: H row = [g(128) u(128)] x I/128 ; dact row = I.
+// dg = dact * u * act'(g) ; du = dact * act(g)
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dact, const __nv_bfloat16* __restrict__ H,
+                                  __nv_bfloat16* __restrict__ dH, long rows, int I, int kind,
+                                  const int* __restrict__ counts, int cap) {
+  const long per_row = I / 8;
+  const long n = rows * per_row;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long row = i / per_row;
+    if (counts) {  // capacity layout: skip rows past the expert's rounded-up count
+      const int e = (int)(row / cap), r = (int)(row % cap);
+      const int lim = ((counts[e] + 127) / 128) * 128;
+      if (r >= lim) continue;
+    }
+    const int c = (int)(i % per_row) * 8;
+    const int blk = c / 128, off = c % 128;
+    const long gcol = (long)blk * 256 + off;
+    float d[8], g[8], u[8], dg[8], du[8];
+    load8(dact + row * I + c, d);
+    load8(H + row * 2 * I + gcol, g);
+    load8(H + row * 2 * I + gcol + 128, u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      dg[k] = d[k] * u[k] * act_grad(g[k], kind);
+      du[k] = d[k] * act_f(g[k], kind);
+    }
+    store8(dH + row * 2 * I + gcol, dg);
+    store8(dH + row * 2 * I + gcol + 128, du);
+  }
+}
+
+// ------------------------------------------------------------------------------ QK-norm + RoPE
+// qkv row: [q (H*hd) | k (Hkv*hd) | ...] with row stride ld. Writes qn [T, H, hd], kn [T, Hkv, hd].
+// One warp per (token, head); positions = token % S. hd even, hd/2 <= 128.
+__global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, int ld, __nv_bfloat16* __restrict__ qn,
+                                        __nv_bfloat16* __restrict__ kn, float* __restrict__ rstd,
+                                        const float* __restrict__ cos_t, const float* __restrict__ sin_t, int T,
+                                        int S, int H, int Hkv, int hd, int qk_norm, float qk_mult, float eps) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int NH = H + Hkv;
+  const int half = hd / 2;
+  for (long item = blockIdx.x * (long)warps + (threadIdx.x >> 5); item < (long)T * NH;
+       item += (long)gridDim.x * warps) {
+    const int t = (int)(item / NH), h = (int)(item % NH);
+    const __nv_bfloat16* src = qkv + (long)t * ld + h * hd;
+    float x1[4], x2[4];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = lane + 32 * j;
+      x1[j] = x2[j] = 0.f;
+      if (i < half) {
+        x1[j] = __bfloat162float(src[i]);
+        x2[j] = __bfloat162float(src[i + half]);
+        ss += x1[j] * x1[j] + x2[j] * x2[j];
+      }
+    }
+    float r = 1.f;
+    if (qk_norm) {
+      r = rsqrtf(warp_sum(ss) / hd + eps);
+      if (lane == 0) rstd[(long)t * NH + h] = r;
+    }
+    const float mult = h < H ? qk_mult : 1.f;
+    __nv_bfloat16* dst = h < H ? qn + ((long)t * H + h) * hd : kn + ((long)t * Hkv + (h - H)) * hd;
+    const int pos = t % S;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = lane + 32 * j;
+      if (i < half) {
+        // the normalised value is rounded to the activation dtype before RoPE, as in the oracle
+        const float a = __bfloat162float(__float2bfloat16(x1[j] * r));
+        const float b = __bfloat162float(__float2bfloat16(x2[j] * r));
+        const float c = cos_t[pos * half + i], s = sin_t[pos * half + i];
+        const float o1 = __bfloat162float(__float2bfloat16(a * c - b * s));
+        const float o2 = __bfloat162float(__float2bfloat16(b * c + a * s));
+        dst[i] = __float2bfloat16(o1 * mult);
+        dst[i + half] = __float2bfloat16(o2 * mult);
+      }
+    }
+  }
+}
+
+// Backward: dqn/dkn -> d(raw q/k) written into dqkv (row stride ld) at the q/k columns.
+__global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dqn, const __nv_bfloat16* __restrict__ dkn,
+                                        const __nv_bfloat16* __restrict__ qkv, int ld, const float* __restrict__ rstd,
+                                        const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                        __nv_bfloat16* __restrict__ dqkv, int T, int S, int H, int Hkv, int hd,
+                                        int qk_norm, float qk_mult) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int NH = H + Hkv;
+  const int half = hd / 2;
+  for (long item = blockIdx.x * (long)warps + (threadIdx.x >> 5); item < (long)T * NH;
+       item += (long)gridDim.x * warps) {
+    const int t = (int)(item / NH), h = (int)(item % NH);
+    const __nv_bfloat16* g = h < H ? dqn + ((long)t * H + h) * hd : dkn + ((long)t * Hkv + (h - H)) * hd;
+    const __nv_bfloat16* src = qkv + (long)t * ld + h * hd;
+    const float mult = h < H ? qk_mult : 1.f;
+    const float r = qk_norm ? rstd[(long)t * NH + h] : 1.f;
+    const int pos = t % S;
+    float dn1[4], dn2[4], n1[4], n2[4];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = lane + 32 * j;
+      dn1[j] = dn2[j] = n1[j] = n2[j] = 0.f;
+      if (i < half) {
+        const float c = cos_t[pos * half + i], s = sin_t[pos * half + i];
+        const float g1 = __bfloat162float(g[i]) * mult, g2 = __bfloat162float(g[i + half]) * mult;
+        // RoPE^T
+        dn1[j] = g1 * c + g2 * s;
+        dn2[j] = -g1 * s + g2 * c;
+        n1[j] = __bfloat162float(src[i]) * r;
+        n2[j] = __bfloat162float(src[i + half]) * r;
+        dot += dn1[j] * n1[j] + dn2[j] * n2[j];
+      }
+    }
+    if (qk_norm) dot = warp_sum(dot) / hd;
+    __nv_bfloat16* dst = dqkv + (long)t * ld + h * hd;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = lane + 32 * j;
+      if (i < half) {
+        float a = dn1[j], b = dn2[j];
+        if (qk_norm) {
+          a = r * (dn1[j] - n1[j] * dot);
+          b = r * (dn2[j] - n2[j] * dot);
+        }
+        dst[i] = __float2bfloat16(a);
+        dst[i + half] = __float2bfloat16(b);
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------- XSA + head gate
+// y: [T, H, hd] attention output; v at qkv[t, voff + (h/rep)*hd]; gate logit at qkv[t, goff + h].
+// out[t, h*hd + i] = gate * (y - (y.v)/(v.v + 1e-6) v), gate = 2*sigmoid(logit).
+__global__ void xsa_gate_fwd_kernel(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __restrict__ qkv,
+                                    int ld, int voff, int goff, __nv_bfloat16* __restrict__ out, int T, int H,
+                                    int Hkv, int hd, int xsa, int gate) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rep = H / Hkv;
+  for (long item = blockIdx.x * (long)warps + (threadIdx.x >> 5); item < (long)T * H;
+       item += (long)gridDim.x * warps) {
+    const int t = (int)(item / H), h = (int)(item % H);
+    const __nv_bfloat16* yr = y + ((long)t * H + h) * hd;
+    const __nv_bfloat16* vr = qkv + (long)t * ld + voff + (h / rep) * hd;
+    float yv[4], vv[4];
+    float dot = 0.f, vn = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = lane + 32 * j;
+      yv[j] = vv[j] = 0.f;
+      if (i < hd) {
+        yv[j] = __bfloat162float(yr[i]);
+        vv[j] = __bfloat162float(vr[i]);
+        dot += yv[j] * vv[j];
+        vn += vv[j] * vv[j];
+      }
+    }
+    float c = 0.f;
+    if (xsa) c = warp_sum(dot) / (warp_sum(vn) + 1e-6f);
+    const float gmul = gate ? 2.f * sigm(__bfloat162float(qkv[(long)t * ld + goff + h])) : 1.f;
+    __nv_bfloat16* o = out + (long)t * H * hd + h * hd;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = lane + 32 * j;
+      if (i < hd) o[i] = __float2bfloat16(gmul * (yv[j] - c * vv[j]));
+    }
+  }
+}
+
+// Backward. dout [T, H*hd]. Writes dy [T, H, hd]; dv contribution into dqkv v-columns
+// (summed over the q heads of a kv group, one warp per (token, kv head)); dgate into dqkv.
+__global__ void xsa_gate_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ y,
+                                    const __nv_bfloat16* __restrict__ qkv, int ld, int voff, int goff,
+                                    __nv_bfloat16* __restrict__ dy, __nv_bfloat16* __restrict__ dqkv, int T, int H,
+                                    int Hkv, int hd, int xsa, int gate) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rep = H / Hkv;
+  for (long item = blockIdx.x * (long)warps + (threadIdx.x >> 5); item < (long)T * Hkv;
+       item += (long)gridDim.x * warps) {
+    const int t = (int)(item / Hkv), kh = (int)(item % Hkv);
+    const __nv_bfloat16* vr = qkv + (long)t * ld + voff + kh * hd;
+    float vv[4], dv[4];
+    float vn = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = lane + 32 * j;
+      vv[j] = 0.f;
+      dv[j] = 0.f;
+      if (i < hd) vv[j] = __bfloat162float(vr[i]);
+      vn += vv[j] * vv[j];
+    }
+    const float n = warp_sum(vn) + 1e-6f;
+    for (int h = kh * rep; h < (kh + 1) * rep; ++h) {
+      const __nv_bfloat16* yr = y + ((long)t * H + h) * hd;
+      const __nv_bfloat16* dr = dout + (long)t * H * hd + h * hd;
+      float yv[4], dz[4];
+      float yd = 0.f, zd = 0.f;
+      const float lg = gate ? __bfloat162float(qkv[(long)t * ld + goff + h]) : 0.f;
+      const float s = sigm(lg);
+      const float gmul = gate ? 2.f * s : 1.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = lane + 32 * j;
+        yv[j] = dz[j] = 0.f;
+        if (i < hd) {
+          yv[j] = __bfloat162float(yr[i]);
+          dz[j] = __bfloat162float(dr[i]);
+        }
+        yd += yv[j] * vv[j];
+      }
+      const float c = xsa ? warp_sum(yd) / n : 0.f;
+      // dgate: d(out)/d(logit) = z * 2 s (1 - s)
+      float gd = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) gd += dz[j] * (yv[j] - c * vv[j]);
+      gd = warp_sum(gd);
+      if (gate && lane == 0) dqkv[(long)t * ld + goff + h] = __float2bfloat16(gd * 2.f * s * (1.f - s));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        dz[j] *= gmul;
+        zd += dz[j] * vv[j];
+      }
+      const float a = xsa ? warp_sum(zd) / n : 0.f;
+      __nv_bfloat16* dyr = dy + ((long)t * H + h) * hd;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = lane + 32 * j;
+        if (i < hd) dyr[i] = __float2bfloat16(dz[j] - a * vv[j]);
+        if (xsa) dv[j] += -a * yv[j] - c * dz[j] + 2.f * c * a * vv[j];
+      }
+    }
+    __nv_bfloat16* dvr = dqkv + (long)t * ld + voff + kh * hd;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = lane + 32 * j;
+      if (i < hd) dvr[i] = __float2bfloat16(dv[j]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------- cross-entropy grad
+// One block per row of a logits chunk [rows, ldl] (bf16, V valid columns) with per-tile stats
+// (max, sumexp) [rows, nt]. Computes lse, the weighted loss term, and overwrites the logits with
+// dlogits = coef * ((1 + 2 z lse) softmax - onehot(label)), coef = scale * w / wsum. Columns
+// in [V, ldl) are zeroed.
+__global__ void ce_grad_kernel(__nv_bfloat16* __restrict__ logits, int ldl, const float2* __restrict__ stats,
+                               int nt, const int64_t* __restrict__ labels, const float* __restrict__ weights,
+                               const float* __restrict__ wsum, float* __restrict__ loss_out,
+                               float* __restrict__ lse_out, int V, float z_weight, float scale) {
+  const int row = blockIdx.x;
+  __shared__ float s_red[32];
+  __shared__ float s_lse;
+  // combine per-tile stats
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < nt; i += blockDim.x) m = fmaxf(m, stats[(long)row * nt + i].x);
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? s_red[threadIdx.x] : -INFINITY;
+    v = warp_max(v);
+    if (threadIdx.x == 0) s_red[0] = v;
+  }
+  __syncthreads();
+  m = s_red[0];
+  __syncthreads();
+  float se = 0.f;
+  for (int i = threadIdx.x; i < nt; i += blockDim.x) {
+    float2 st = stats[(long)row * nt + i];
+    if (st.x > -INFINITY) se += st.y * __expf(st.x - m);
+  }
+  se = warp_sum(se);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = se;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? s_red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) s_lse = m + __logf(v);
+  }
+  __syncthreads();
+  const float lse = s_lse;
+  const float w = weights[row];
+  const long lab = labels[row];
+  __nv_bfloat16* lr = logits + (long)row * ldl;
+  if (threadIdx.x == 0) {
+    const float xl = (lab >= 0 && lab < V) ? __bfloat162float(lr[lab]) : 0.f;
+    const float nll = lse - xl + z_weight * lse * lse;
+    atomicAdd(loss_out, w * nll);
+    if (lse_out) lse_out[row] = lse;
+  }
+  __syncthreads();
+  const float coef = scale * w / fmaxf(*wsum, 1.f);
+  const float pmul = coef * (1.f + 2.f * z_weight * lse);
+  for (int c = threadIdx.x * 8; c < ldl; c += blockDim.x * 8) {
+    float f[8];
+    load8(lr + c, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int col = c + i;
+      float d = 0.f;
+      if (col < V) {
+        d = pmul * __expf(f[i] - lse);
+        if (col == lab) d -= coef;
+      }
+      f[i] = d;
+    }
+    store8(lr + c, f);
+  }
+}
+
+inline int grid_for(long work, int per_block) {
+  long g = (work + per_block - 1) / per_block;
+  if (g > 148 * 16) g = 148 * 16;
+  return g < 1 ? 1 : (int)g;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------ launchers
+void launch_rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int T, int D, float eps,
+                        cudaStream_t st) {
+  rmsnorm_fwd_kernel<<<grid_for(T, 8), 256, 0, st>>>((const __nv_bfloat16*)x, w, (__nv_bfloat16*)y, rstd, T, D, eps);
+}
+
+void launch_rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, const void* dres, void* dx,
+                        float* dw, int T, int D, cudaStream_t st) {
+  const int blocks = T < 148 * 8 * 2 ? (T + 7) / 8 : 148 * 2;
+  const size_t sm = (size_t)D * sizeof(float);
+  if (D <= 256)
+    rmsnorm_bwd_kernel<1><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd,
+                                                  (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D);
+  else if (D <= 1024)
+    rmsnorm_bwd_kernel<4><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd,
+                                                  (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D);
+  else if (D <= 2048)
+    rmsnorm_bwd_kernel<8><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd,
+                                                  (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D);
+  else
+    rmsnorm_bwd_kernel<16><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd,
+                                                   (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D);
+}
+
+void launch_embed_fwd(const int64_t* ids, const void* table, void* out, int T, int D, int V, cudaStream_t st) {
+  embed_fwd_kernel<<<grid_for(T, 8), 256, 0, st>>>(ids, (const __nv_bfloat16*)table, (__nv_bfloat16*)out, T, D, V);
+}
+
+void launch_embed_bwd(const int64_t* ids, const void* dout, float* dtable, int T, int D, int V, cudaStream_t st) {
+  embed_bwd_kernel<<<grid_for(T, 8), 256, 0, st>>>(ids, (const __nv_bfloat16*)dout, dtable, T, D, V);
+}
+
+void launch_gate_mul_bwd(const void* dout, const void* y, const void* z, void* dy, void* dz, long n,
+                         cudaStream_t st) {
+  gate_mul_bwd_kernel<<<grid_for(n / 8, 256), 256, 0, st>>>((const __nv_bfloat16*)dout, (const __nv_bfloat16*)y,
+                                                            (const __nv_bfloat16*)z, (__nv_bfloat16*)dy,
+                                                            (__nv_bfloat16*)dz, n / 8);
+}
+
+void launch_act_bwd(const void* da, const void* h, void* dh, long n, int kind, cudaStream_t st) {
+  act_bwd_kernel<<<grid_for(n / 8, 256), 256, 0, st>>>((const __nv_bfloat16*)da, (const __nv_bfloat16*)h,
+                                                       (__nv_bfloat16*)dh, n / 8, kind);
+}
+
+void launch_swiglu_bwd(const void* dact, const void* H, void* dH, long rows, int I, int kind, const int* counts,
+                       int cap, cudaStream_t st) {
+  swiglu_bwd_kernel<<<grid_for(rows * I / 8, 256), 256, 0, st>>>(
+      (const __nv_bfloat16*)dact, (const __nv_bfloat16*)H, (__nv_bfloat16*)dH, rows, I, kind, counts, cap);
+}
+
+void launch_qk_norm_rope_fwd(const void* qkv, int ld, void* qn, void* kn, float* rstd, const float* cos_t,
+                             const float* sin_t, int T, int S, int H, int Hkv, int hd, int qk_norm, float qk_mult,
+                             cudaStream_t st) {
+  qk_norm_rope_fwd_kernel<<<grid_for((long)T * (H + Hkv), 8), 256, 0, st>>>(
+      (const __nv_bfloat16*)qkv, ld, (__nv_bfloat16*)qn, (__nv_bfloat16*)kn, rstd, cos_t, sin_t, T, S, H, Hkv, hd,
+      qk_norm, qk_mult, 1e-6f);
+}
+
+void launch_qk_norm_rope_bwd(const void* dqn, const void* dkn, const void* qkv, int ld, const float* rstd,
+                             const float* cos_t, const float* sin_t, void* dqkv, int T, int S, int H, int Hkv,
+                             int hd, int qk_norm, float qk_mult, cudaStream_t st) {
+  qk_norm_rope_bwd_kernel<<<grid_for((long)T * (H + Hkv), 8), 256, 0, st>>>(
+      (const __nv_bfloat16*)dqn, (const __nv_bfloat16*)dkn, (const __nv_bfloat16*)qkv, ld, rstd, cos_t, sin_t,
+      (__nv_bfloat16*)dqkv, T, S, H, Hkv, hd, qk_norm, qk_mult);
+}
+
+void launch_xsa_gate_fwd(const void* y, const void* qkv, int ld, int voff, int goff, void* out, int T, int H,
+                         int Hkv, int hd, int xsa, int gate, cudaStream_t st) {
+  xsa_gate_fwd_kernel<<<grid_for((long)T * H, 8), 256, 0, st>>>((const __nv_bfloat16*)y, (const __nv_bfloat16*)qkv,
+                                                                ld, voff, goff, (__nv_bfloat16*)out, T, H, Hkv, hd,
+                                                                xsa, gate);
+}
+
+void launch_xsa_gate_bwd(const void* dout, const void* y, const void* qkv, int ld, int voff, int goff, void* dy,
+                         void* dqkv, int T, int H, int Hkv, int hd, int xsa, int gate, cudaStream_t st) {
+  xsa_gate_bwd_kernel<<<grid_for((long)T * Hkv, 8), 256, 0, st>>>(
+      (const __nv_bfloat16*)dout, (const __nv_bfloat16*)y, (const __nv_bfloat16*)qkv, ld, voff, goff,
+      (__nv_bfloat16*)dy, (__nv_bfloat16*)dqkv, T, H, Hkv, hd, xsa, gate);
+}
+
+void launch_ce_grad(void* logits, int ldl, const float* stats, int nt, const int64_t* labels, const float* weights,
+                    const float* wsum, float* loss_out, float* lse_out, int rows, int V, float z_weight, float scale,
+                    cudaStream_t st) {
+  ce_grad_kernel<<<rows, 256, 0, st>>>((__nv_bfloat16*)logits, ldl, (const float2*)stats, nt, labels, weights, wsum,
+                                       loss_out, lse_out, V, z_weight, scale);
+}
+
+}  // namespace mxk

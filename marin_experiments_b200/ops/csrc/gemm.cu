@@ -3,7 +3,10 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <dlfcn.h>
+
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm_sm100.cuh"
@@ -11,21 +14,49 @@
 
 namespace mxk {
 
+static bool trace_on() {
+  static int on = -1;
+  if (on < 0) on = std::getenv("MXK_TRACE") ? 1 : 0;
+  return on == 1;
+}
+#define MXK_TRACE(msg) \
+  do { if (trace_on()) { std::fprintf(stderr, "[mxk] %s\n", msg); std::fflush(stderr); } } while (0)
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// The driver's cuTensorMapEncodeTiled and cuCtxGetCurrent, resolved with dlsym from libcuda.so.1
+// (already loaded by the CUDA runtime).
+static void* driver_sym(const char* name) {
+  void* lib = dlopen("libcuda.so.1", RTLD_NOW | RTLD_NOLOAD);
+  if (!lib) lib = dlopen("libcuda.so.1", RTLD_NOW);
+  return lib ? dlsym(lib, name) : nullptr;
+}
+
 static EncodeTiledFn get_encode_fn() {
   static EncodeTiledFn fn = nullptr;
   static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
+  std::call_once(once, [] { fn = reinterpret_cast<EncodeTiledFn>(driver_sym("cuTensorMapEncodeTiled")); });
   return fn;
+}
+
+// The runtime binds its primary context to a thread lazily, on the first runtime call that needs
+// it. Threads that only queried state so far (autograd's device threads run backward on their
+// own) have no current driver context, and encoding a tensor map there faulted inside the driver.
+// Bind the context of the runtime's current device first.
+static void ensure_current_context() {
+  static CtxGetCurrentFn get = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] { get = reinterpret_cast<CtxGetCurrentFn>(driver_sym("cuCtxGetCurrent")); });
+  CUcontext ctx = nullptr;
+  if (get && get(&ctx) == CUDA_SUCCESS && ctx != nullptr) return;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaSetDevice(dev);
+  cudaFree(nullptr);
 }
 
 // 2-D bf16 tensor map over a row-major matrix [outer, inner] with row stride `ld` elements,
@@ -34,6 +65,7 @@ bool make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, int64_t inner, int64_t o
                        int box_outer) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
+  ensure_current_context();
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
   cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
@@ -56,10 +88,14 @@ int num_sms() {
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
+  MXK_TRACE("launch_impl enter");
   CUtensorMap ta, tb;
+  if (trace_on()) std::fprintf(stderr, "[mxk] tmap addr %p %p\n", (void*)&ta, (void*)&tb);
   // A tile: K-major -> box {64 (K), 128 rows}; MN-major -> box {64 (M), 64 (K rows)}
   if (!make_tmap_bf16_2d(&ta, L.a, L.a_inner, L.a_outer, L.lda, 64, A_MN ? 64 : kBM)) return kErrBadArgs;
+  MXK_TRACE("tmap A");
   if (!make_tmap_bf16_2d(&tb, L.b, L.b_inner, L.b_outer, L.ldb, 64, B_MN ? 64 : BN)) return kErrBadArgs;
+  MXK_TRACE("tmap B");
   auto kern = gemm_sm100_kernel<BN, STAGES, A_MN, B_MN, EPI>;
   constexpr int smem = gemm_smem_bytes<BN, STAGES>();
   static bool attr_set = false;
@@ -74,7 +110,9 @@ static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
   long long tiles = (long long)L.p.G * m_tiles * n_tiles;
   int grid = (int)(tiles < num_sms() ? tiles : num_sms());
   if (grid <= 0) return 0;
+  MXK_TRACE("launch");
   kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, L.p);
+  MXK_TRACE("launched");
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgs;
 }
 
@@ -83,6 +121,7 @@ static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
     return launch_impl<BN_, ST_, AMN_, BMN_, EPI_>(L, stream);
 
 int launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
+  MXK_TRACE("launch_gemm");
   if (L.p.G <= 0 || L.p.G > kMaxGroups || L.p.K <= 0 || L.p.N <= 0 || L.p.M <= 0) return kErrBadArgs;
   if (L.p.K % kBK != 0 && L.p.ragged != 2) return kErrBadArgs;
   if ((reinterpret_cast<uintptr_t>(L.a) | reinterpret_cast<uintptr_t>(L.b)) & 15) return kErrBadArgs;
@@ -97,6 +136,9 @@ int launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   MXK_CASE(256, 4, true, true, EPI_STORE)
   MXK_CASE(128, 6, true, true, EPI_STORE)
   MXK_CASE(64, 8, true, true, EPI_STORE)
+  // input-gradient GEMMs that add a second gradient term in the epilogue
+  MXK_CASE(256, 4, false, true, EPI_RESID)
+  MXK_CASE(128, 6, false, true, EPI_RESID)
   // fused epilogues (forward, K-major x K-major)
   MXK_CASE(256, 4, false, false, EPI_SWIGLU)
   MXK_CASE(256, 4, false, false, EPI_RESID)

@@ -2,3 +2,88 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+namespace mxk {
+
+constexpr int kErrBadArgsHost = 5;
+
+// elementwise.cu
+void launch_rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int T, int D, float eps, cudaStream_t st);
+void launch_rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, const void* dres, void* dx,
+                        float* dw, int T, int D, cudaStream_t st);
+void launch_embed_fwd(const int64_t* ids, const void* table, void* out, int T, int D, int V, cudaStream_t st);
+void launch_embed_bwd(const int64_t* ids, const void* dout, float* dtable, int T, int D, int V, cudaStream_t st);
+void launch_gate_mul_bwd(const void* dout, const void* y, const void* z, void* dy, void* dz, long n, cudaStream_t st);
+void launch_act_bwd(const void* da, const void* h, void* dh, long n, int kind, cudaStream_t st);
+void launch_swiglu_bwd(const void* dact, const void* H, void* dH, long rows, int I, int kind, const int* counts,
+                       int cap, cudaStream_t st);
+void launch_qk_norm_rope_fwd(const void* qkv, int ld, void* qn, void* kn, float* rstd, const float* cos_t,
+                             const float* sin_t, int T, int S, int H, int Hkv, int hd, int qk_norm, float qk_mult,
+                             cudaStream_t st);
+void launch_qk_norm_rope_bwd(const void* dqn, const void* dkn, const void* qkv, int ld, const float* rstd,
+                             const float* cos_t, const float* sin_t, void* dqkv, int T, int S, int H, int Hkv, int hd,
+                             int qk_norm, float qk_mult, cudaStream_t st);
+void launch_xsa_gate_fwd(const void* y, const void* qkv, int ld, int voff, int goff, void* out, int T, int H, int Hkv,
+                         int hd, int xsa, int gate, cudaStream_t st);
+void launch_xsa_gate_bwd(const void* dout, const void* y, const void* qkv, int ld, int voff, int goff, void* dy,
+                         void* dqkv, int T, int H, int Hkv, int hd, int xsa, int gate, cudaStream_t st);
+void launch_ce_grad(void* logits, int ldl, const float* stats, int nt, const int64_t* labels, const float* weights,
+                    const float* wsum, float* loss_out, float* lse_out, int rows, int V, float z_weight, float scale,
+                    cudaStream_t st);
+
+// moe.cu
+int launch_router_fwd(const float* logits, int ldl, const float* bias, int T, int E, int K, int adaptive,
+                      const float* theta, int k_min, float temp, int* sel, float* comb, float* topb, float* alpha,
+                      float* lse, uint8_t* keep, float* counts, float* psum, float* scalars, cudaStream_t st);
+int launch_router_bwd(const float* logits, int ldl, const float* lse, const int* sel, const float* topb,
+                      const uint8_t* keep, const float* dcomb, const float* counts, const float* dscal, int T, int E,
+                      int K, int adaptive, const float* theta, int k_min, float temp, void* dlog, int ldd,
+                      float* dtheta, cudaStream_t st);
+void launch_qb_beta(const float* logits, int ldl, const float* alpha, int T, int E, int qb_count, float* beta,
+                    cudaStream_t st);
+int plan_workspace_ints(long n, int E);
+void launch_dispatch_plan(const int* sel, const uint8_t* keep, const float* comb, long n, int K, int E, int cap,
+                          int* blk_counts, int* slot, int* perm, float* wperm, int* counts, cudaStream_t st);
+void launch_permute(const void* x, const int* perm, const int* counts, int cap, int E, int D, void* xp,
+                    cudaStream_t st);
+void launch_combine(const void* Y, const int* sel, const int* slot, const float* comb, const void* residual, void* out,
+                    int T, int K, int cap, int D, cudaStream_t st);
+void launch_combine_bwd(const void* dout, const void* Y, const int* sel, const int* slot, const int* perm,
+                        const float* wperm, const int* counts, int T, int K, int cap, int E, int D, void* dY,
+                        float* dcomb, cudaStream_t st);
+void launch_unpermute_add(const void* dxp, const int* sel, const int* slot, const void* dx_in, void* dx, int T, int K,
+                          int cap, int D, cudaStream_t st);
+
+// optim.cu
+void launch_opt_sqnorm(const void* chunks, int nchunks, const float* grad, float scale, double* out, cudaStream_t st);
+void launch_opt_step(const void* chunks, int nchunks, const float* hp, const double* gnorm2, float gscale,
+                     const float* grad, float* m, float* v, float* p, void* pb, double* mat_sums, int has_adamh,
+                     cudaStream_t st);
+void launch_ema(float* dst, const float* src, long n, float beta, cudaStream_t st);
+void launch_cast_bf16(const float* src, void* dst, long n, cudaStream_t st);
+
+// attention.cu
+struct AttnLaunch {
+  const void* q;
+  const void* k;
+  const void* v;
+  long q_tok, q_head, k_tok, k_head, v_tok, v_head;
+  void* o;
+  float* lse;
+  const int* seg;
+  int B, S, H, Hkv, hd, window;
+  float scale;
+  const void* dout;
+  float* dsum;
+  float* dq_acc;
+  void* dq;
+  void* dk;
+  long dk_tok, dk_head;
+  void* dv;
+  long dv_tok, dv_head;
+  int dv_accumulate;
+};
+int launch_flash_fwd(const AttnLaunch& L, cudaStream_t st);
+int launch_flash_bwd(const AttnLaunch& L, cudaStream_t st);
+
+}  // namespace mxk

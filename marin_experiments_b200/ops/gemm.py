@@ -24,9 +24,9 @@ def _pick_bn(n: int, epi: str, b_mn: bool, a_mn: bool) -> int:
         return 256
     if epi == "silu":
         return 128
-    if n % 256 == 0 and n >= 1024:
+    if n >= 512:
         return 256
-    if n % 128 == 0:
+    if n >= 128:
         return 128
     return 64
 

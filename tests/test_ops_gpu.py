@@ -1,0 +1,230 @@
+"""Every CUDA op (forward and hand-written backward) against the fp32 PyTorch oracle + autograd.
+
+Inputs are drawn in fp32, rounded to bf16 for the GPU path; the oracle runs in fp32 on the same
+rounded values. Tolerances are relative L2 errors sized for bf16 activations.
+"""
+
+import math
+
+import pytest
+import torch
+
+from marin_experiments_b200.ops import api
+from marin_experiments_b200.ops import reference as R
+
+pytestmark = pytest.mark.gpu
+
+
+def rel(a, b):
+    a, b = a.detach().float().cpu(), b.detach().float().cpu()
+    return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
+
+
+def bf(x):
+    return x.to(torch.bfloat16).float()
+
+
+def gpu_param(t):
+    """bf16 compute copy for >=2-D weights, fp32 for 1-D (the parameter-store convention)."""
+    dt = torch.bfloat16 if t.dim() >= 2 else torch.float32
+    p = t.detach().to("cuda", dt).requires_grad_(True)
+    p.main_grad = torch.zeros(t.shape, dtype=torch.float32, device="cuda")
+    return p
+
+
+def cpu_leaf(t):
+    return t.detach().clone().float().requires_grad_(True)
+
+
+def test_rms_gated_norm():
+    torch.manual_seed(0)
+    t, d, r = 256, 512, 128
+    x = bf(torch.randn(t, d))
+    w = 1 + 0.1 * torch.randn(d)
+    wd, wu = bf(0.05 * torch.randn(r, d)), bf(0.05 * torch.randn(d, r))
+    dout = bf(torch.randn(t, d))
+    xc, wc, wdc, wuc = cpu_leaf(x), cpu_leaf(w), cpu_leaf(wd), cpu_leaf(wu)
+    yc = api.rms_gated_norm(xc, wc, 1e-5, wdc, wuc)
+    yc.backward(dout)
+    xg = x.cuda().bfloat16().requires_grad_(True)
+    wg, wdg, wug = gpu_param(w), gpu_param(wd), gpu_param(wu)
+    yg = api.rms_gated_norm(xg, wg, 1e-5, wdg, wug)
+    yg.backward(dout.cuda().bfloat16())
+    assert rel(yg, yc) < 1e-2
+    assert rel(xg.grad, xc.grad) < 3e-2
+    assert rel(wg.main_grad, wc.grad) < 3e-2
+    assert rel(wdg.main_grad, wdc.grad) < 3e-2
+    assert rel(wug.main_grad, wuc.grad) < 3e-2
+
+
+@pytest.mark.parametrize("hd,heads,kv,window,segs,xsa_gate", [
+    (64, 4, 4, 0, False, False),
+    (96, 4, 2, 0, True, True),
+    (64, 4, 1, 100, False, True),
+    (128, 2, 2, 0, False, True),
+])
+def test_attention_block(hd, heads, kv, window, segs, xsa_gate):
+    torch.manual_seed(1)
+    b, s, d = 2, 256, 256
+    t = b * s
+    h = bf(torch.randn(t, d))
+    x = bf(torch.randn(t, d))
+    wqkv = bf(torch.randn((heads + 2 * kv) * hd, d) / math.sqrt(d))
+    gate = bf(0.1 * torch.randn(heads, d)) if xsa_gate else None
+    wo = bf(torch.randn(d, heads * hd) / math.sqrt(heads * hd))
+    seg = (torch.arange(s) // 100).repeat(b).int() if segs else None
+    shape = api.AttnShape(b, s, heads, kv, hd, window=window, qk_mult=1.0, qk_norm=True, xsa=xsa_gate,
+                          head_gate=xsa_gate)
+    dout = bf(torch.randn(t, d))
+    hc, xc, wqc, woc = cpu_leaf(h), cpu_leaf(x), cpu_leaf(wqkv), cpu_leaf(wo)
+    gc = cpu_leaf(gate) if gate is not None else None
+    oc = api.attention_block(hc, xc, wqc, gc, woc, shape, seg)
+    oc.backward(dout)
+    hg = h.cuda().bfloat16().requires_grad_(True)
+    xg = x.cuda().bfloat16().requires_grad_(True)
+    wqg, wog = gpu_param(wqkv), gpu_param(wo)
+    gg = gpu_param(gate) if gate is not None else None
+    og = api.attention_block(hg, xg, wqg, gg, wog, shape, None if seg is None else seg.cuda())
+    og.backward(dout.cuda().bfloat16())
+    assert rel(og - xg, oc - xc) < 2e-2
+    assert rel(hg.grad, hc.grad) < 4e-2
+    assert rel(xg.grad, xc.grad) < 1e-2
+    assert rel(wqg.main_grad, wqc.grad) < 4e-2
+    assert rel(wog.main_grad, woc.grad) < 3e-2
+    if gate is not None:
+        assert rel(gg.main_grad, gc.grad) < 5e-2
+
+
+@pytest.mark.parametrize("glu,act", [(True, "silu"), (False, "relu")])
+def test_dense_mlp(glu, act):
+    torch.manual_seed(2)
+    t, d, inter = 256, 256, 512
+    h = bf(torch.randn(t, d))
+    res = bf(torch.randn(t, d))
+    win = bf(torch.randn((2 if glu else 1) * inter, d) / 16)
+    wdn = bf(torch.randn(d, inter) / 22)
+    dout = bf(torch.randn(t, d))
+    hc, rc, wic, wdc = cpu_leaf(h), cpu_leaf(res), cpu_leaf(win), cpu_leaf(wdn)
+    oc = api.dense_mlp(hc, wic, wdc, glu=glu, act=act, residual=rc)
+    oc.backward(dout)
+    hg = h.cuda().bfloat16().requires_grad_(True)
+    rg = res.cuda().bfloat16().requires_grad_(True)
+    wig, wdg = gpu_param(win), gpu_param(wdn)
+    og = api.dense_mlp(hg, wig, wdg, glu=glu, act=act, residual=rg)
+    og.backward(dout.cuda().bfloat16())
+    assert rel(og - rg, oc - rc) < 2e-2
+    assert rel(hg.grad, hc.grad) < 3e-2
+    assert rel(wig.main_grad, wic.grad) < 3e-2
+    assert rel(wdg.main_grad, wdc.grad) < 3e-2
+
+
+@pytest.mark.parametrize("e,k,adaptive", [(64, 4, False), (8, 2, False), (32, 8, True)])
+def test_router(e, k, adaptive):
+    torch.manual_seed(3)
+    t, d = 512, 256
+    h = bf(torch.randn(t, d))
+    w = bf(torch.randn(e, d) / 8)
+    bias = 0.1 * torch.randn(e)
+    theta = torch.tensor(0.0 if adaptive else -4.0)
+    hc, wc, thc = cpu_leaf(h), cpu_leaf(w), cpu_leaf(theta)
+    rc = api.route(hc, wc, bias, k, adaptive=adaptive, threshold=thc, k_min=1 if adaptive else 0, qb_count=t * k // e)
+    g_comb = torch.randn(t, k)
+    loss_c = (rc.combine * g_comb).sum() + 0.3 * rc.z_loss + 0.7 * rc.lbl + 0.5 * rc.sparsity
+    loss_c.backward()
+    hg = h.cuda().bfloat16().requires_grad_(True)
+    wg = gpu_param(w)
+    thg = gpu_param(theta)
+    rg = api.route(hg, wg, bias.cuda(), k, adaptive=adaptive, threshold=thg, k_min=1 if adaptive else 0,
+                   qb_count=t * k // e)
+    loss_g = (rg.combine * g_comb.cuda()).sum() + 0.3 * rg.z_loss + 0.7 * rg.lbl + 0.5 * rg.sparsity
+    loss_g.backward()
+    assert torch.equal(rg.selected.cpu().long(), rc.selected)
+    assert rel(rg.combine, rc.combine) < 1e-3
+    assert abs(rg.z_loss.item() - rc.z_loss.item()) < 1e-3 * max(1, rc.z_loss.item())
+    assert abs(rg.lbl.item() - rc.lbl.item()) < 1e-3
+    assert torch.allclose(rg.counts.cpu(), rc.counts)
+    assert torch.allclose(rg.beta.cpu(), rc.beta, atol=1e-4)
+    assert rel(hg.grad, hc.grad) < 3e-2
+    assert rel(wg.main_grad, wc.grad) < 3e-2
+    if adaptive:
+        assert abs(thg.main_grad.item() - thc.grad.item()) < 2e-2 * max(1.0, abs(thc.grad.item()))
+
+
+def test_moe_experts():
+    torch.manual_seed(4)
+    t, d, inter, e, k = 512, 256, 256, 8, 2
+    h = bf(torch.randn(t, d))
+    res = bf(torch.randn(t, d))
+    wr = bf(torch.randn(e, d) / 8)
+    wgu = bf(torch.randn(e, 2 * inter, d) / 16)
+    wdn = bf(torch.randn(e, d, inter) / 16)
+    cap = api.capacity_for(t, k, e, 1.0)
+    dout = bf(torch.randn(t, d))
+    hc, rc_, wgc, wdc = cpu_leaf(h), cpu_leaf(res), cpu_leaf(wgu), cpu_leaf(wdn)
+    routc = api.route(hc, cpu_leaf(wr), torch.zeros(e), k, qb_count=64)
+    oc = api.moe_experts(hc, routc, wgc, wdc, capacity=cap, residual=rc_)
+    oc.backward(dout)
+    hg = h.cuda().bfloat16().requires_grad_(True)
+    rg_ = res.cuda().bfloat16().requires_grad_(True)
+    wgg, wdg = gpu_param(wgu), gpu_param(wdn)
+    routg = api.route(hg, gpu_param(wr), torch.zeros(e, device="cuda"), k, qb_count=64)
+    og = api.moe_experts(hg, routg, wgg, wdg, capacity=cap, residual=rg_)
+    og.backward(dout.cuda().bfloat16())
+    assert torch.equal(routg.selected.cpu().long(), routc.selected)
+    assert rel(og - rg_, oc - rc_) < 2e-2
+    assert rel(hg.grad, hc.grad) < 4e-2
+    assert rel(wgg.main_grad, wgc.grad) < 3e-2
+    assert rel(wdg.main_grad, wdc.grad) < 3e-2
+
+
+def test_moe_capacity_drop():
+    """Tight capacity: the GPU plan drops the same assignments as the oracle (first come, first served)."""
+    torch.manual_seed(5)
+    t, e, k = 1024, 8, 2
+    sel = torch.randint(0, 3, (t, k)).int()  # skewed onto 3 experts
+    sel[:, 1] = (sel[:, 0] + 1) % e
+    comb = torch.rand(t, k)
+    from marin_experiments_b200.ops import cuda_fns
+
+    cap = 128
+    slot, perm, wperm, counts = cuda_fns.dispatch_plan(sel.cuda(), None, comb.cuda(), e, cap)
+    ref_slot, ref_counts = R.capacity_slots(sel.long(), e, cap)
+    assert torch.equal(slot.cpu().long(), ref_slot)
+    assert torch.equal(counts.cpu().long(), ref_counts)
+
+
+def test_cross_entropy():
+    torch.manual_seed(6)
+    t, de, v = 512, 256, 1000
+    h = bf(torch.randn(t, de))
+    w = bf(torch.randn(v, de) / 16)
+    labels = torch.randint(0, v, (t,))
+    wts = torch.ones(t)
+    wts[::7] = 0
+    hc, wc = cpu_leaf(h), cpu_leaf(w)
+    lc = api.cross_entropy(hc, wc, labels, wts, z_weight=1e-4)
+    lc.backward()
+    hg = h.cuda().bfloat16().requires_grad_(True)
+    wg = gpu_param(w)
+    from marin_experiments_b200.ops import cuda_fns
+
+    lg = cuda_fns.cross_entropy(hg, wg, labels.cuda(), wts.cuda(), 1e-4, chunk=256)
+    lg.backward()
+    assert abs(lg.item() - lc.item()) < 2e-3 * lc.item()
+    assert rel(hg.grad, hc.grad) < 3e-2
+    assert rel(wg.main_grad, wc.grad) < 3e-2
+
+
+def test_embed():
+    v, d, t = 1000, 256, 512
+    table = bf(torch.randn(v, d))
+    ids = torch.randint(0, v, (t,))
+    tc = cpu_leaf(table)
+    oc = api.embed(ids, tc)
+    dout = bf(torch.randn(t, d))
+    oc.backward(dout)
+    tg = gpu_param(table)
+    og = api.embed(ids.cuda(), tg)
+    og.backward(dout.cuda().bfloat16())
+    assert rel(og, oc) == 0.0
+    assert rel(tg.main_grad, tc.grad) < 1e-5
