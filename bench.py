@@ -1,0 +1,250 @@
+"""Headline benchmark: MoE training tokens/s on the megagpt-speedrun configuration.
+
+Model (random init, bf16 compute, fp32 masters, AdamH): 24 layers, d_model 1536, 16 heads
+(head_dim 96), 64 routed experts top-4 with expert d_ff 768 plus one shared expert of d_ff 3072,
+vocab 128256, seq 2048, capacity factor 1.25, GatedNorm / QK-norm / XSA / head gate on.
+Data: synthetic uniform-random token ids (seed 2). Weak scaling: 64K tokens (32 sequences) per
+GPU per step, i.e. 512K tokens per step on 8 GPUs; experts are sharded over all ranks (EP = N).
+
+Timing: W untimed warm-up steps, then K steps bracketed by a barrier and a device synchronise,
+timed with CUDA events on the compute stream; the reported time is the max over ranks. The step's
+working set (12.8 GB of bf16 weights alone) is far larger than the 126 MB L2, so no flush is
+needed between steps. The end-to-end figure repeats K steps through ``Trainer.train_step`` with
+every step's tokens copied from pinned host memory and the loss read back to the host.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+BASELINE_TOK_S = 192000.0  # reference 8xH100 anchor (tokens/s, whole job)
+METRIC = "MoE train tokens/sec/box at 1/2/4/8 B200; MFU; exposed all-to-all ms/step"
+
+
+def megagpt_config():
+    from marin_experiments_b200.config import GrugModelConfig
+
+    return GrugModelConfig(
+        vocab_size=128256, hidden_dim=1536, intermediate_dim=768, shared_expert_intermediate_dim=3072,
+        num_experts=64, num_experts_per_token=4, num_layers=24, num_heads=16, num_kv_heads=16, head_dim=96,
+        max_seq_len=2048, sliding_window=4096, capacity_factor=1.25, router_z_loss_coef=0.001,
+    )
+
+
+def flops_per_token(cfg) -> float:
+    """Training FLOPs per token: 6 x active matmul parameters + causal attention (fwd+bwd)."""
+    d, hd, h, hkv, s = cfg.hidden_dim, cfg.inferred_head_dim, cfg.num_heads, cfg.num_kv_heads, cfg.max_seq_len
+    attn_proj = d * (h + 2 * hkv) * hd + h * hd * d + d * h
+    gated = 2 * (2 * d * cfg.gated_norm_rank)
+    experts = cfg.num_experts_per_token * 3 * d * cfg.intermediate_dim + d * cfg.num_experts
+    shared = 3 * d * cfg.shared_expert_intermediate_dim
+    per_layer = attn_proj + gated + experts + shared
+    head = cfg.vocab_size * cfg.inferred_embed_dim
+    dense = cfg.num_layers * per_layer + head + 2 * (2 * d * cfg.gated_norm_rank)
+    attn_core = cfg.num_layers * 2 * s * h * hd  # QK^T and PV, causal half, forward
+    return 6.0 * dense + 3.0 * attn_core
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks / throttle reasons in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t is not None:
+            self._t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        sm.sort()
+        med = sm[len(sm) // 2] if sm else None
+        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_arm(args):
+    """The reference is JAX/XLA (jax + levanter + flash-attn-4 + NCCL cu13); none of it is installed in
+    this image and there is no network, so its own code path cannot run here."""
+    msg = {"impl": "reference", "unavailable": "reference is a JAX/XLA program (jax, marin-levanter, flash-attn-4); "
+                                               "jax is not installed in this offline image and baseline/_ref has no "
+                                               "runnable JAX stack"}
+    try:
+        import jax  # noqa: F401
+    except Exception:
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps(msg), flush=True)
+        return 0
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps(msg), flush=True)
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
+    ap.add_argument("--seqs-per-gpu", type=int, default=32)
+    ap.add_argument("--micro-batch", type=int, default=8)
+    ap.add_argument("--layers", type=int, default=None, help="(debug only) override layer count")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    from marin_experiments_b200.config import GrugRunConfig, GrugTrainerConfig, TrainerConfig
+    from marin_experiments_b200.data.synthetic import UniformTokenBatches
+    from marin_experiments_b200.optim import GrugMoeAdamHConfig
+    from marin_experiments_b200.parallel import dist as pdist
+    from marin_experiments_b200.train.trainer import Trainer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    ctx = pdist.init(ep_size=world) if world > 1 else None
+    cfg = megagpt_config()
+    if args.layers is not None:
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, num_layers=args.layers)
+    run = GrugRunConfig(model=cfg, optimizer=GrugMoeAdamHConfig(learning_rate=0.01, adam_lr=6e-4, warmup=0.0),
+                        trainer=GrugTrainerConfig(trainer=TrainerConfig(seed=0, num_train_steps=1000)))
+    trainer = Trainer(run, device=f"cuda:{local_rank}", micro_batch=args.micro_batch, dist=ctx)
+    seqs = args.seqs_per_gpu
+    seq = cfg.max_seq_len
+    data = UniformTokenBatches(seqs, seq, cfg.vocab_size, seed=2, pin=True, rank=rank)
+
+    def barrier():
+        if ctx is not None:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        met = trainer.train_step(next(data))
+    torch.cuda.synchronize()
+    from marin_experiments_b200.ops._ext import check_kernel_errors, ext
+
+    check_kernel_errors()
+    # ------------------------------------------------------------------ device-timed steps
+    staged = [{"tokens": next(data)["tokens"].to(trainer.device)} for _ in range(args.steps)]
+    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[0])
+                          if False else local_rank)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    n0 = ext().launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        met = trainer.train_step(staged[i])
+    e1.record()
+    torch.cuda.synchronize()
+    launches = ext().launch_count() - n0
+    barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_t = torch.tensor([ms], device=trainer.device)
+    if ctx is not None:
+        torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    loss = float(met["train/loss"].item())
+    tokens_step = seqs * seq * world
+    tok_s = tokens_step / (ms / 1e3)
+    fpt = flops_per_token(cfg)
+    mfu = tok_s * fpt / (2.25e15 * world)
+    # ------------------------------------------------------------------ end to end (public API)
+    e2e = None
+    if not args.no_e2e:
+        host = [next(data) for _ in range(args.steps)]
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for i in range(args.steps):
+            m = trainer.train_step(host[i])
+            _ = float(m["train/loss"].item())
+        a1.record()
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) / args.steps
+        ems = a0.elapsed_time(a1) / args.steps
+        et = torch.tensor([ems], device=trainer.device)
+        if ctx is not None:
+            torch.distributed.all_reduce(et, op=torch.distributed.ReduceOp.MAX)
+        ems = float(et.item())
+        e2e = {"value": tokens_step / (ems / 1e3), "unit": "tokens/s", "ms_per_step": ems, "wall_ms_per_step": wall * 1e3,
+               "h2d_bytes_per_step": int(host[0]["tokens"].numel() * host[0]["tokens"].element_size()),
+               "d2h_bytes_per_step": 4}
+    check_kernel_errors()
+    out = {
+        "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": tok_s / BASELINE_TOK_S, "dtype": "bf16", "data": "synthetic (uniform random ids, seed 2; random init)",
+        "config": {"model": "megagpt-speedrun MoE: 24L d1536 16h(hd96) E64 top4 d_ff768 + shared 3072, vocab 128256",
+                   "global_batch": seqs * world, "seq_len": seq, "tokens_per_step": tokens_step,
+                   "micro_batch": args.micro_batch, "capacity_factor": cfg.capacity_factor,
+                   "parallelism": f"ep{world}" if world > 1 else "single", "l2": "working set >> L2 (no flush needed)",
+                   "layers": cfg.num_layers},
+        "mfu": mfu, "flops_per_token": fpt, "loss": loss, "clocks": clk, "gpu_launches": int(launches),
+        "e2e": e2e,
+    }
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if ctx is not None:
+        pdist.shutdown()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

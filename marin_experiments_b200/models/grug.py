@@ -324,3 +324,27 @@ def apply_qb_betas(model: Transformer, betas: torch.Tensor) -> None:
                 nb = nb - nb.mean()
                 blk.mlp.router_bias.copy_(nb.to(blk.mlp.router_bias.dtype))
                 i += 1
+
+
+def init_store_weights(store, cfg: GrugModelConfig, seed: int = 0) -> None:
+    """Initialise a model's flat parameter store in place on its device: truncated normal(-3, 3) *
+    ``initializer_std`` for weight matrices, ones for norm scales, zeros for the attention gate and
+    router bias, -4 for the adaptive threshold (megagpt-speedrun/model.py:234-253,488-519,841-842).
+    Parameters are drawn from one generator on the store's device, in store order."""
+    gen = torch.Generator(device=store.device).manual_seed(seed)
+    std = cfg.initializer_std
+    with torch.no_grad():
+        for info in store.infos:
+            v = store.master_view(info)
+            leaf = info.name.rsplit(".", 1)[-1]
+            if leaf == "weight":
+                v.fill_(1.0)
+            elif leaf in ("attn_gate", "router_bias"):
+                v.zero_()
+            elif leaf == "router_threshold":
+                v.fill_(-4.0)
+            else:
+                v.normal_(0.0, 1.0, generator=gen)
+                v.clamp_(-3.0, 3.0)
+                v.mul_(std)
+    store.sync_compute()

@@ -538,6 +538,7 @@ int run_fwd(const AttnParams& p, cudaStream_t st) {
     init = true;
   }
   dim3 grid((p.S + 127) / 128, p.H, p.B);
+  count_launch();
   flash_fwd_kernel<HD><<<grid, 256, fwd_smem<HD>(), st>>>(p);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
 }
@@ -550,8 +551,10 @@ int run_bwd(const AttnParams& p, cudaStream_t st) {
     init = true;
   }
   const long T = (long)p.B * p.S;
+  count_launch();
   flash_bwd_prep_kernel<HD><<<148 * 8, 256, 0, st>>>(p, T);
   dim3 grid((p.S + 127) / 128, p.Hkv, p.B);
+  count_launch();
   flash_bwd_kernel<HD><<<grid, 256, bwd_smem<HD>(), st>>>(p);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
 }
@@ -611,6 +614,7 @@ int launch_flash_bwd(const AttnLaunch& L, cudaStream_t st) {
   }
   if (r) return r;
   const long n = (long)L.B * L.S * L.H * L.hd;
+  count_launch();
   dq_convert_kernel<<<148 * 8, 256, 0, st>>>(L.dq_acc, (__nv_bfloat16*)L.dq, n);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
 }

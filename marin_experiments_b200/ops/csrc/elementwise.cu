@@ -556,6 +556,7 @@ inline int grid_for(long work, int per_block) {
 // ------------------------------------------------------------------------------ launchers
 void launch_rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int T, int D, float eps,
                         cudaStream_t st) {
+  count_launch();
   rmsnorm_fwd_kernel<<<grid_for(T, 8), 256, 0, st>>>((const __nv_bfloat16*)x, w, (__nv_bfloat16*)y, rstd, T, D, eps);
 }
 
@@ -563,42 +564,55 @@ void launch_rmsnorm_bwd(const void* dy, const void* x, const float* w, const flo
                         float* dw, int T, int D, cudaStream_t st) {
   const int blocks = T < 148 * 8 * 2 ? (T + 7) / 8 : 148 * 2;
   const size_t sm = (size_t)D * sizeof(float);
-  if (D <= 256)
+  if (D <= 256) {
+    count_launch();
     rmsnorm_bwd_kernel<1><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd,
                                                   (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D);
-  else if (D <= 1024)
+  }
+  else if (D <= 1024) {
+    count_launch();
     rmsnorm_bwd_kernel<4><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd,
                                                   (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D);
-  else if (D <= 2048)
+  }
+  else if (D <= 2048) {
+    count_launch();
     rmsnorm_bwd_kernel<8><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd,
                                                   (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D);
-  else
+  }
+  else {
+    count_launch();
     rmsnorm_bwd_kernel<16><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd,
                                                    (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D);
+  }
 }
 
 void launch_embed_fwd(const int64_t* ids, const void* table, void* out, int T, int D, int V, cudaStream_t st) {
+  count_launch();
   embed_fwd_kernel<<<grid_for(T, 8), 256, 0, st>>>(ids, (const __nv_bfloat16*)table, (__nv_bfloat16*)out, T, D, V);
 }
 
 void launch_embed_bwd(const int64_t* ids, const void* dout, float* dtable, int T, int D, int V, cudaStream_t st) {
+  count_launch();
   embed_bwd_kernel<<<grid_for(T, 8), 256, 0, st>>>(ids, (const __nv_bfloat16*)dout, dtable, T, D, V);
 }
 
 void launch_gate_mul_bwd(const void* dout, const void* y, const void* z, void* dy, void* dz, long n,
                          cudaStream_t st) {
+  count_launch();
   gate_mul_bwd_kernel<<<grid_for(n / 8, 256), 256, 0, st>>>((const __nv_bfloat16*)dout, (const __nv_bfloat16*)y,
                                                             (const __nv_bfloat16*)z, (__nv_bfloat16*)dy,
                                                             (__nv_bfloat16*)dz, n / 8);
 }
 
 void launch_act_bwd(const void* da, const void* h, void* dh, long n, int kind, cudaStream_t st) {
+  count_launch();
   act_bwd_kernel<<<grid_for(n / 8, 256), 256, 0, st>>>((const __nv_bfloat16*)da, (const __nv_bfloat16*)h,
                                                        (__nv_bfloat16*)dh, n / 8, kind);
 }
 
 void launch_swiglu_bwd(const void* dact, const void* H, void* dH, long rows, int I, int kind, const int* counts,
                        int cap, cudaStream_t st) {
+  count_launch();
   swiglu_bwd_kernel<<<grid_for(rows * I / 8, 256), 256, 0, st>>>(
       (const __nv_bfloat16*)dact, (const __nv_bfloat16*)H, (__nv_bfloat16*)dH, rows, I, kind, counts, cap);
 }
@@ -606,6 +620,7 @@ void launch_swiglu_bwd(const void* dact, const void* H, void* dH, long rows, int
 void launch_qk_norm_rope_fwd(const void* qkv, int ld, void* qn, void* kn, float* rstd, const float* cos_t,
                              const float* sin_t, int T, int S, int H, int Hkv, int hd, int qk_norm, float qk_mult,
                              cudaStream_t st) {
+  count_launch();
   qk_norm_rope_fwd_kernel<<<grid_for((long)T * (H + Hkv), 8), 256, 0, st>>>(
       (const __nv_bfloat16*)qkv, ld, (__nv_bfloat16*)qn, (__nv_bfloat16*)kn, rstd, cos_t, sin_t, T, S, H, Hkv, hd,
       qk_norm, qk_mult, 1e-6f);
@@ -614,6 +629,7 @@ void launch_qk_norm_rope_fwd(const void* qkv, int ld, void* qn, void* kn, float*
 void launch_qk_norm_rope_bwd(const void* dqn, const void* dkn, const void* qkv, int ld, const float* rstd,
                              const float* cos_t, const float* sin_t, void* dqkv, int T, int S, int H, int Hkv,
                              int hd, int qk_norm, float qk_mult, cudaStream_t st) {
+  count_launch();
   qk_norm_rope_bwd_kernel<<<grid_for((long)T * (H + Hkv), 8), 256, 0, st>>>(
       (const __nv_bfloat16*)dqn, (const __nv_bfloat16*)dkn, (const __nv_bfloat16*)qkv, ld, rstd, cos_t, sin_t,
       (__nv_bfloat16*)dqkv, T, S, H, Hkv, hd, qk_norm, qk_mult);
@@ -621,6 +637,7 @@ void launch_qk_norm_rope_bwd(const void* dqn, const void* dkn, const void* qkv, 
 
 void launch_xsa_gate_fwd(const void* y, const void* qkv, int ld, int voff, int goff, void* out, int T, int H,
                          int Hkv, int hd, int xsa, int gate, cudaStream_t st) {
+  count_launch();
   xsa_gate_fwd_kernel<<<grid_for((long)T * H, 8), 256, 0, st>>>((const __nv_bfloat16*)y, (const __nv_bfloat16*)qkv,
                                                                 ld, voff, goff, (__nv_bfloat16*)out, T, H, Hkv, hd,
                                                                 xsa, gate);
@@ -628,6 +645,7 @@ void launch_xsa_gate_fwd(const void* y, const void* qkv, int ld, int voff, int g
 
 void launch_xsa_gate_bwd(const void* dout, const void* y, const void* qkv, int ld, int voff, int goff, void* dy,
                          void* dqkv, int T, int H, int Hkv, int hd, int xsa, int gate, cudaStream_t st) {
+  count_launch();
   xsa_gate_bwd_kernel<<<grid_for((long)T * Hkv, 8), 256, 0, st>>>(
       (const __nv_bfloat16*)dout, (const __nv_bfloat16*)y, (const __nv_bfloat16*)qkv, ld, voff, goff,
       (__nv_bfloat16*)dy, (__nv_bfloat16*)dqkv, T, H, Hkv, hd, xsa, gate);
@@ -636,6 +654,7 @@ void launch_xsa_gate_bwd(const void* dout, const void* y, const void* qkv, int l
 void launch_ce_grad(void* logits, int ldl, const float* stats, int nt, const int64_t* labels, const float* weights,
                     const float* wsum, float* loss_out, float* lse_out, int rows, int V, float z_weight, float scale,
                     cudaStream_t st) {
+  count_launch();
   ce_grad_kernel<<<rows, 256, 0, st>>>((__nv_bfloat16*)logits, ldl, (const float2*)stats, nt, labels, weights, wsum,
                                        loss_out, lse_out, V, z_weight, scale);
 }

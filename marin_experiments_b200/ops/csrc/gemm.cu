@@ -10,6 +10,7 @@
 #include <mutex>
 
 #include "gemm_sm100.cuh"
+#include "kernels.h"
 #include "launch.h"
 
 namespace mxk {
@@ -111,6 +112,7 @@ static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
   int grid = (int)(tiles < num_sms() ? tiles : num_sms());
   if (grid <= 0) return 0;
   MXK_TRACE("launch");
+  count_launch();
   kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, L.p);
   MXK_TRACE("launched");
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgs;

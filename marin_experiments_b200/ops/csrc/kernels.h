@@ -3,9 +3,18 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace mxk {
 
 constexpr int kErrBadArgsHost = 5;
+
+// Number of kernels this library launched (read by benchmarks to report their launch count).
+inline std::atomic<long long>& launch_counter() {
+  static std::atomic<long long> c{0};
+  return c;
+}
+inline void count_launch(int n = 1) { launch_counter().fetch_add(n, std::memory_order_relaxed); }
 
 // elementwise.cu
 void launch_rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int T, int D, float eps, cudaStream_t st);

@@ -479,6 +479,7 @@ int launch_router_fwd(const float* logits, int ldl, const float* bias, int T, in
   const size_t sm = 2 * E * sizeof(float);
 #define RF(EPL) router_fwd_kernel<EPL><<<grid, 256, sm, st>>>(logits, ldl, bias, T, E, K, adaptive, theta, k_min, \
                                                              temp, sel, comb, topb, alpha, lse, keep, counts, psum, scalars)
+  count_launch();
   if (E <= 32) RF(1);
   else if (E <= 64) RF(2);
   else if (E <= 128) RF(4);
@@ -496,6 +497,7 @@ int launch_router_bwd(const float* logits, int ldl, const float* lse, const int*
 #define RB(EPL) router_bwd_kernel<EPL><<<grid, 256, 0, st>>>(logits, ldl, lse, sel, topb, keep, dcomb, counts, dscal, \
                                                             T, E, K, adaptive, theta, k_min, temp,               \
                                                             (__nv_bfloat16*)dlog, ldd, dtheta)
+  count_launch();
   if (E <= 32) RB(1);
   else if (E <= 64) RB(2);
   else if (E <= 128) RB(4);
@@ -507,6 +509,7 @@ int launch_router_bwd(const float* logits, int ldl, const float* lse, const int*
 
 void launch_qb_beta(const float* logits, int ldl, const float* alpha, int T, int E, int qb_count, float* beta,
                     cudaStream_t st) {
+  count_launch();
   qb_beta_kernel<<<E, 1024, 0, st>>>(logits, ldl, alpha, T, E, qb_count, beta);
 }
 
@@ -515,19 +518,23 @@ int plan_workspace_ints(long n, int E) { return (int)(((n + kPlanChunk - 1) / kP
 void launch_dispatch_plan(const int* sel, const uint8_t* keep, const float* comb, long n, int K, int E, int cap,
                           int* blk_counts, int* slot, int* perm, float* wperm, int* counts, cudaStream_t st) {
   const int nblk = (int)((n + kPlanChunk - 1) / kPlanChunk);
+  count_launch();
   plan_count_kernel<<<nblk, 1024, E * sizeof(int), st>>>(sel, keep, n, E, blk_counts);
+  count_launch();
   plan_assign_kernel<<<nblk, 1024, (33 * E) * sizeof(int), st>>>(sel, keep, comb, n, K, E, cap, blk_counts, nblk,
                                                                   slot, perm, wperm, counts);
 }
 
 void launch_permute(const void* x, const int* perm, const int* counts, int cap, int E, int D, void* xp,
                     cudaStream_t st) {
+  count_launch();
   permute_kernel<<<grid_for((long)E * cap, 8), 256, 0, st>>>((const __nv_bfloat16*)x, perm, counts, cap, E, D,
                                                              (__nv_bfloat16*)xp);
 }
 
 void launch_combine(const void* Y, const int* sel, const int* slot, const float* comb, const void* residual,
                     void* out, int T, int K, int cap, int D, cudaStream_t st) {
+  count_launch();
   combine_kernel<<<grid_for(T, 8), 256, 0, st>>>((const __nv_bfloat16*)Y, sel, slot, comb,
                                                  (const __nv_bfloat16*)residual, (__nv_bfloat16*)out, T, K, cap, D);
 }
@@ -535,14 +542,17 @@ void launch_combine(const void* Y, const int* sel, const int* slot, const float*
 void launch_combine_bwd(const void* dout, const void* Y, const int* sel, const int* slot, const int* perm,
                         const float* wperm, const int* counts, int T, int K, int cap, int E, int D, void* dY,
                         float* dcomb, cudaStream_t st) {
+  count_launch();
   combine_bwd_rows_kernel<<<grid_for((long)E * cap, 8), 256, 0, st>>>((const __nv_bfloat16*)dout, perm, wperm,
                                                                       counts, cap, E, D, (__nv_bfloat16*)dY);
+  count_launch();
   combine_bwd_weights_kernel<<<grid_for((long)T * K, 8), 256, 0, st>>>(
       (const __nv_bfloat16*)dout, (const __nv_bfloat16*)Y, sel, slot, T, K, cap, D, dcomb);
 }
 
 void launch_unpermute_add(const void* dxp, const int* sel, const int* slot, const void* dx_in, void* dx, int T, int K,
                           int cap, int D, cudaStream_t st) {
+  count_launch();
   unpermute_add_kernel<<<grid_for(T, 8), 256, 0, st>>>((const __nv_bfloat16*)dxp, sel, slot,
                                                        (const __nv_bfloat16*)dx_in, (__nv_bfloat16*)dx, T, K, cap, D);
 }

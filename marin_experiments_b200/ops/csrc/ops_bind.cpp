@@ -307,6 +307,7 @@ void cast_bf16(const Tensor& src, const Tensor& dst) {
 }  // namespace
 
 void register_ops(pybind11::module& m) {
+  m.def("launch_count", []() { return (int64_t)mxk::launch_counter().load(); });
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("embed_fwd", &embed_fwd);

@@ -147,6 +147,7 @@ __global__ void cast_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* _
 
 void launch_opt_sqnorm(const void* chunks, int nchunks, const float* grad, float scale, double* out,
                        cudaStream_t st) {
+  count_launch();
   if (nchunks > 0) sqnorm_kernel<<<nchunks, 256, 0, st>>>((const Chunk*)chunks, grad, scale, out);
 }
 
@@ -154,17 +155,22 @@ void launch_opt_step(const void* chunks, int nchunks, const float* hp, const dou
                      const float* grad, float* m, float* v, float* p, void* pb, double* mat_sums, int has_adamh,
                      cudaStream_t st) {
   if (nchunks <= 0) return;
+  count_launch();
   moments_kernel<<<nchunks, 256, 0, st>>>((const Chunk*)chunks, hp, gnorm2, gscale, grad, m, v, p,
                                           (__nv_bfloat16*)pb, mat_sums);
-  if (has_adamh)
+  if (has_adamh) {
+    count_launch();
     adamh_apply_kernel<<<nchunks, 256, 0, st>>>((const Chunk*)chunks, hp, m, v, p, (__nv_bfloat16*)pb, mat_sums);
+  }
 }
 
 void launch_ema(float* dst, const float* src, long n, float beta, cudaStream_t st) {
+  count_launch();
   ema_kernel<<<148 * 8, 256, 0, st>>>(dst, src, n, beta);
 }
 
 void launch_cast_bf16(const float* src, void* dst, long n, cudaStream_t st) {
+  count_launch();
   cast_bf16_kernel<<<148 * 8, 256, 0, st>>>(src, (__nv_bfloat16*)dst, n);
 }
 

@@ -1,0 +1,211 @@
+"""Fused optimizer over a ``ParamStore``.
+
+One step = (1) per-group squared gradient norms, (2) moments + Adam update / AdamH matrix sums,
+(3) AdamH scale-invariant apply, all as multi-tensor kernels over a chunk table built once
+(``csrc/optim.cu``); the bf16 compute copy is written in the same passes. Per-step
+hyper-parameters (learning rates, bias corrections) live in a small device tensor filled from
+pinned host memory, so the step can be captured in a CUDA graph. The CPU path runs the same math
+with torch ops and is the oracle of the kernels.
+
+Global-norm clipping is per group, as in the reference (each ``multi_transform`` branch chains its
+own ``clip_by_global_norm``, megagpt-speedrun/optimizer.py:38-58). ``norm_hook`` lets a
+distributed caller all-reduce the per-group squared norms of sharded groups before use.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+CHUNK = 32768
+HP = 9
+_CHUNK_DTYPE = np.dtype([("start", "<i8"), ("len", "<i4"), ("mat", "<i4"), ("group", "<i4"), ("pad", "<i4")])
+
+
+def _ns_quintic(g: torch.Tensor, steps: int) -> torch.Tensor:
+    """Newton-Schulz orthogonalisation with the quintic iteration of Muon
+    (a, b, c) = (3.4445, -4.7750, 2.0315) (Jordan et al., "Muon", 2024)."""
+    a, b, c = 3.4445, -4.7750, 2.0315
+    x = g.float()
+    transpose = x.shape[-2] > x.shape[-1]
+    if transpose:
+        x = x.transpose(-1, -2)
+    x = x / (x.norm(dim=(-2, -1), keepdim=True) + 1e-7)
+    for _ in range(steps):
+        A = x @ x.transpose(-1, -2)
+        B = b * A + c * (A @ A)
+        x = a * x + B @ x
+    if transpose:
+        x = x.transpose(-1, -2)
+    return x
+
+
+class FusedOptimizer:
+    def __init__(self, store, cfg, num_train_steps: int):
+        self.store = store
+        self.cfg = cfg
+        self.num_train_steps = num_train_steps
+        self.groups = cfg.groups(store)
+        self.names = list(self.groups)
+        self.step_count = 0
+        dev = store.device
+        self.m = torch.zeros_like(store.master)
+        self.v = torch.zeros_like(store.master)
+        self.lr_fns = {n: cfg.lr_scheduler(num_train_steps, override_lr=g["lr"]) for n, g in self.groups.items()}
+        self.norm_hook = None
+        self.last_grad_norms: dict[str, float] = {}
+        # chunk table over adam / adamh groups
+        rows = []
+        mat = 0
+        self.mat_count = 0
+        self.muon_infos = []
+        for gi, name in enumerate(self.names):
+            g = self.groups[name]
+            if g["kind"] == "muon":
+                self.muon_infos.extend(g["infos"])
+                continue
+            for info in g["infos"]:
+                mats = info.matrices if g["kind"] == "adamh" else [[(info.offset, info.numel)]]
+                for ranges in mats:
+                    for start, length in ranges:
+                        for c0 in range(0, length, CHUNK):
+                            rows.append((start + c0, min(CHUNK, length - c0), mat, gi, 0))
+                    mat += 1
+        self.mat_count = max(mat, 1)
+        self.has_adamh = any(g["kind"] == "adamh" for g in self.groups.values())
+        arr = np.array(rows, dtype=_CHUNK_DTYPE) if rows else np.zeros(0, dtype=_CHUNK_DTYPE)
+        self.nchunks = len(rows)
+        if store.cuda:
+            self.chunks = torch.from_numpy(arr.view(np.uint8).copy()).to(dev)
+            self.hp_host = torch.zeros(len(self.names), HP, dtype=torch.float32).pin_memory()
+            self.hp = torch.zeros(len(self.names), HP, dtype=torch.float32, device=dev)
+            self.gnorm2 = torch.zeros(len(self.names), dtype=torch.float64, device=dev)
+            self.mat_sums = torch.zeros(self.mat_count, 3, dtype=torch.float64, device=dev)
+        self._rows = rows
+
+    # --------------------------------------------------------------------------------- state
+    def state_dict(self) -> dict:
+        return {"step": self.step_count, "m": self.m.detach().cpu(), "v": self.v.detach().cpu()}
+
+    def load_state_dict(self, sd: dict) -> None:
+        self.step_count = int(sd["step"])
+        self.m.copy_(sd["m"].to(self.m.device))
+        self.v.copy_(sd["v"].to(self.v.device))
+
+    def current_lrs(self) -> dict[str, float]:
+        return {n: self.lr_fns[n](self.step_count) for n in self.names}
+
+    # ---------------------------------------------------------------------------------- step
+    def _fill_hp(self, t: int) -> None:
+        cfg = self.cfg
+        b1, b2 = cfg.beta1, cfg.beta2
+        for gi, name in enumerate(self.names):
+            g = self.groups[name]
+            kind = {"adam": 0.0, "adamh": 1.0, "muon": 2.0}[g["kind"]]
+            mx = cfg.max_grad_norm if cfg.max_grad_norm else 0.0
+            self.hp_host[gi] = torch.tensor([kind, self.lr_fns[name](self.step_count), b1, b2, cfg.epsilon,
+                                             g["wd"], 1 - b1 ** t, 1 - b2 ** t, mx])
+        self.hp.copy_(self.hp_host, non_blocking=True)
+
+    @torch.no_grad()
+    def step(self, grad_scale: float = 1.0, zero_grad: bool = True) -> None:
+        self.step_count += 1
+        t = self.step_count
+        st = self.store
+        if st.cuda:
+            from ..ops._ext import ext
+
+            self._fill_hp(t)
+            self.gnorm2.zero_()
+            ext().opt_sqnorm(self.chunks, self.nchunks, st.grad, grad_scale, self.gnorm2)
+            if self.norm_hook is not None:
+                self.norm_hook(self.gnorm2, self.names)
+            self.mat_sums.zero_()
+            ext().opt_step(self.chunks, self.nchunks, self.hp, self.gnorm2, grad_scale, st.grad, self.m, self.v,
+                           st.master, st.compute, self.mat_sums, self.has_adamh)
+        else:
+            self._step_cpu(t, grad_scale)
+        if self.muon_infos:
+            self._step_muon(t, grad_scale)
+        if zero_grad:
+            st.zero_grad()
+
+    def _group_norm2(self, name: str, grad_scale: float) -> float:
+        st = self.store
+        acc = 0.0
+        for info in self.groups[name]["infos"]:
+            g = st.grad[info.offset: info.offset + info.numel] * grad_scale
+            acc += float((g.double() ** 2).sum())
+        return acc
+
+    def _step_cpu(self, t: int, grad_scale: float) -> None:
+        cfg = self.cfg
+        st = self.store
+        b1, b2, eps = cfg.beta1, cfg.beta2, cfg.epsilon
+        bc1, bc2 = 1 - b1 ** t, 1 - b2 ** t
+        norms = {}
+        for name in self.names:
+            if self.groups[name]["kind"] != "muon":
+                norms[name] = self._group_norm2(name, grad_scale)
+        if self.norm_hook is not None:
+            vec = torch.tensor([norms.get(n, 0.0) for n in self.names], dtype=torch.float64)
+            self.norm_hook(vec, self.names)
+            norms = {n: float(vec[i]) for i, n in enumerate(self.names) if n in norms}
+        for name in self.names:
+            g = self.groups[name]
+            if g["kind"] == "muon":
+                continue
+            lr = self.lr_fns[name](self.step_count)
+            n = math.sqrt(norms[name])
+            self.last_grad_norms[name] = n
+            s = grad_scale
+            if cfg.max_grad_norm and n >= cfg.max_grad_norm:
+                s = grad_scale * cfg.max_grad_norm / n
+            for info in g["infos"]:
+                sl = slice(info.offset, info.offset + info.numel)
+                gr = st.grad[sl] * s
+                m = self.m[sl]
+                v = self.v[sl]
+                m.mul_(b1).add_(gr, alpha=1 - b1)
+                v.mul_(b2).addcmul_(gr, gr, value=1 - b2)
+                if g["kind"] == "adam":
+                    u = (m / bc1) / ((v / bc2).sqrt() + eps)
+                    p = st.master[sl]
+                    p.sub_(lr * (u + g["wd"] * p))
+                else:
+                    for ranges in info.matrices:
+                        idx = torch.cat([torch.arange(a, a + b) for a, b in ranges])
+                        mm, vv, pp = self.m[idx], self.v[idx], st.master[idx]
+                        u = (mm / bc1) / ((vv / bc2).sqrt() + eps)
+                        pn = pp.norm()
+                        un = u.norm().clamp_min(1e-10)
+                        new = pp - lr * u * pn / un
+                        nn_ = new.norm()
+                        if nn_ > 0:
+                            new = new / nn_ * pn
+                        st.master[idx] = new
+
+    def _step_muon(self, t: int, grad_scale: float) -> None:
+        """Muon update on the matrices of the muon group (momentum, Newton-Schulz, shape scale)."""
+        cfg = self.cfg
+        st = self.store
+        lr = self.lr_fns["muon"](self.step_count)
+        wd = self.groups["muon"]["wd"]
+        mu = getattr(cfg, "momentum", 0.95)
+        for info in self.muon_infos:
+            sl = slice(info.offset, info.offset + info.numel)
+            g = (st.grad[sl] * grad_scale).view(info.shape)
+            m = self.m[sl].view(info.shape)
+            m.mul_(mu).add_(g)
+            upd = g + mu * m if getattr(cfg, "nesterov", True) else m
+            if info.ndim < 2:
+                continue
+            mat = upd.reshape(-1, info.shape[-2], info.shape[-1])
+            o = _ns_quintic(mat, getattr(cfg, "ns_steps", 5)).reshape(info.shape)
+            scale = max(1.0, info.shape[-2] / info.shape[-1]) ** 0.5
+            p = st.master[sl].view(info.shape)
+            p.sub_(lr * (scale * o + wd * p))
+        if st.cuda:
+            st.sync_compute()

@@ -1,0 +1,77 @@
+"""Whole-model check: the grug MoE and dense models on the sm_100a path vs the fp32 CPU oracle.
+
+Both start from identical weights (the CPU store's masters loaded into the GPU store); loss and
+every parameter's gradient are compared after one forward/backward.
+"""
+
+import pytest
+import torch
+
+from marin_experiments_b200.config import GrugModelConfig, GrugRunConfig, GrugTrainerConfig, TrainerConfig
+from marin_experiments_b200.optim import GrugMoeAdamHConfig
+from marin_experiments_b200.train.trainer import Trainer
+
+pytestmark = pytest.mark.gpu
+
+MOE = GrugModelConfig(vocab_size=2048, hidden_dim=256, intermediate_dim=256, shared_expert_intermediate_dim=512,
+                      num_experts=8, num_experts_per_token=2, num_layers=2, num_heads=4, num_kv_heads=2, head_dim=64,
+                      max_seq_len=256, sliding_window=256, capacity_factor=2.0)
+DENSE = GrugModelConfig(vocab_size=2048, hidden_dim=256, intermediate_dim=512, num_experts=0, num_layers=2,
+                        num_heads=4, num_kv_heads=4, max_seq_len=256, gated_norm=False, qk_norm=False, xsa=False,
+                        head_gate=False, glu=True)
+
+
+def _pair(cfg):
+    run = GrugRunConfig(model=cfg, optimizer=GrugMoeAdamHConfig(warmup=0.0),
+                        trainer=GrugTrainerConfig(trainer=TrainerConfig(num_train_steps=10)))
+    cpu = Trainer(run, device="cpu")
+    gpu = Trainer(run, device="cuda:0")
+    gpu.store.load_state_dict(cpu.store.state_dict())
+    return cpu, gpu
+
+
+@pytest.mark.parametrize("cfg", [MOE, DENSE], ids=["moe", "dense"])
+def test_model_loss_and_grads(cfg):
+    cpu, gpu = _pair(cfg)
+    tok = torch.randint(0, cfg.vocab_size, (2, 256), generator=torch.Generator().manual_seed(0))
+    lc, _ = cpu.model.next_token_loss(tok, z_loss_weight=1e-4)
+    lc.backward()
+    lg, _ = gpu.model.next_token_loss(tok.cuda(), z_loss_weight=1e-4)
+    lg.backward()
+    torch.cuda.synchronize()
+    assert abs(lg.item() - lc.item()) < 1e-2 * lc.item()
+    bad = []
+    for info in cpu.store.infos:
+        if not info.trainable:
+            continue
+        gc = cpu.store.grad_view(info)
+        gg = gpu.store.grad_view(info).cpu()
+        if gc.norm() < 1e-8:
+            continue
+        r = ((gg - gc).norm() / gc.norm()).item()
+        # routed expert weights see the discrete top-k decisions: a few near-tied tokens route
+        # differently under bf16 activations than under the fp32 oracle
+        tol = 0.15 if (".mlp.w_" in info.name and info.ndim == 3) else 6e-2
+        if r > tol:
+            bad.append((info.name, r))
+    assert not bad, bad
+
+
+def test_train_steps_decrease_loss():
+    _, gpu = _pair(MOE)
+    tok = torch.randint(0, MOE.vocab_size, (4, 256), generator=torch.Generator().manual_seed(1)).pin_memory()
+    losses = [float(gpu.train_step({"tokens": tok})["train/loss"].item()) for _ in range(6)]
+    assert losses[-1] < losses[0], losses
+
+
+def test_optimizer_step_matches_cpu():
+    """One AdamH/Adam step on identical gradients: GPU kernels vs the CPU implementation."""
+    cpu, gpu = _pair(MOE)
+    g = torch.randn(cpu.store.numel, generator=torch.Generator().manual_seed(3)) * 1e-2
+    cpu.store.grad.copy_(g)
+    gpu.store.grad.copy_(g.cuda())
+    cpu.opt.step()
+    gpu.opt.step()
+    torch.cuda.synchronize()
+    d = (gpu.store.master.cpu() - cpu.store.master)
+    assert d.abs().max().item() < 1e-5, d.abs().max().item()
