@@ -326,13 +326,26 @@ def apply_qb_betas(model: Transformer, betas: torch.Tensor) -> None:
                 i += 1
 
 
-def init_store_weights(store, cfg: GrugModelConfig, seed: int = 0) -> None:
+def _seed_for(seed: int, name: str, sub: int = -1) -> int:
+    import zlib
+
+    return zlib.crc32(f"{seed}/{name}/{sub}".encode()) & 0x7FFFFFFF
+
+
+def init_store_weights(store, cfg: GrugModelConfig, seed: int = 0, model: Transformer | None = None) -> None:
     """Initialise a model's flat parameter store in place on its device: truncated normal(-3, 3) *
     ``initializer_std`` for weight matrices, ones for norm scales, zeros for the attention gate and
     router bias, -4 for the adaptive threshold (megagpt-speedrun/model.py:234-253,488-519,841-842).
-    Parameters are drawn from one generator on the store's device, in store order."""
-    gen = torch.Generator(device=store.device).manual_seed(seed)
+
+    Every parameter draws from its own generator seeded by (seed, name); routed-expert weights draw
+    one generator per *global* expert id, so an expert-parallel shard holds exactly the experts the
+    same model would have on one GPU."""
     std = cfg.initializer_std
+    ranges = {}
+    if model is not None:
+        for mname, mod in model.named_modules():
+            if isinstance(mod, MoEMLP):
+                ranges[mname] = mod.expert_range
     with torch.no_grad():
         for info in store.infos:
             v = store.master_view(info)
@@ -343,8 +356,12 @@ def init_store_weights(store, cfg: GrugModelConfig, seed: int = 0) -> None:
                 v.zero_()
             elif leaf == "router_threshold":
                 v.fill_(-4.0)
+            elif info.ndim == 3:
+                lo = ranges.get(info.name.rsplit(".", 1)[0], (0, info.shape[0]))[0]
+                for j in range(info.shape[0]):
+                    gen = torch.Generator(device=store.device).manual_seed(_seed_for(seed, info.name, lo + j))
+                    trunc_normal_(v[j], std, gen)
             else:
-                v.normal_(0.0, 1.0, generator=gen)
-                v.clamp_(-3.0, 3.0)
-                v.mul_(std)
+                gen = torch.Generator(device=store.device).manual_seed(_seed_for(seed, info.name))
+                trunc_normal_(v, std, gen)
     store.sync_compute()

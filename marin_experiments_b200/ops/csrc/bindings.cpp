@@ -32,9 +32,10 @@ T* opt_ptr(const c10::optional<at::Tensor>& t) {
 // likewise B'. See gemm_sm100.cuh for the grouping and ragged semantics.
 void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const at::Tensor& C, int64_t G,
           int64_t M, int64_t N, int64_t K, const c10::optional<at::Tensor>& counts, int64_t ragged, int64_t a_grp,
-          int64_t b_grp, int64_t c_grp, int64_t epi, int64_t bn, bool accum, double alpha,
+          int64_t b_grp, int64_t c_grp, int64_t epi, int64_t bn, int64_t accum, double alpha,
           const c10::optional<at::Tensor>& C2, const c10::optional<at::Tensor>& R,
-          const c10::optional<at::Tensor>& row_scale, int64_t act_kind, const at::Tensor& err) {
+          const c10::optional<at::Tensor>& row_scale, int64_t act_kind, const at::Tensor& err, int64_t b_mod,
+          int64_t c_mod) {
   if (std::getenv("MXK_TRACE")) { std::fprintf(stderr, "[mxk] gemm binding enter\n"); std::fflush(stderr); }
   check_2d_bf16(A, "A");
   check_2d_bf16(B, "B");
@@ -78,7 +79,9 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const 
   p.C = C.data_ptr();
   p.ldc = (int)C.stride(0);
   p.c_f32 = C.scalar_type() == at::kFloat ? 1 : 0;
-  p.c_accum = accum ? 1 : 0;
+  p.c_accum = (int)accum;
+  p.b_mod = (int)b_mod;
+  p.c_mod = (int)c_mod;
   p.C2 = opt_ptr<void>(C2);
   p.ldc2 = C2.has_value() ? (int)C2->stride(0) : 0;
   p.R = opt_ptr<const void>(R);

@@ -9,10 +9,13 @@ struct GemmParams {
   const int* counts;  // per-group ragged extent (device), or nullptr
   int ragged;         // 0: none, 1: M ragged, 2: K ragged
   int a_grp, b_grp, c_grp;
+  // Group index used for B / C offsets: (b_mod ? g % b_mod : g), likewise c_mod. Lets
+  // (source rank, expert) activation groups share one expert's weights and weight gradient.
+  int b_mod, c_mod;
   void* C;
   int ldc;
   int c_f32;
-  int c_accum;
+  int c_accum;  // 0: store, 1: C += acc, 2: C += acc with atomics (groups share C rows)
   void* C2;  // EPI_SWIGLU: activation output; EPI_SILU/EPI_ACT: pre-activation copy; EPI_CE: stats
   int ldc2;
   const void* R;  // bf16 residual / gate input

@@ -166,6 +166,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         TileCoord tc = decode_tile<BN>(p, prefix, tile);
+        const int bgrp = p.b_mod ? tc.g % p.b_mod : tc.g;
         for (int kb = 0; kb < tc.nkb; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -181,11 +182,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               tma_load_2d(&tmA, &full_bar[s], a_dst + j * kBK * 128, tc.mt * kBM + j * 64, tc.g * p.a_grp + kb * kBK);
           }
           if constexpr (!B_MN) {
-            tma_load_2d(&tmB, &full_bar[s], b_dst, kb * kBK, tc.g * p.b_grp + tc.nt * BN);
+            tma_load_2d(&tmB, &full_bar[s], b_dst, kb * kBK, bgrp * p.b_grp + tc.nt * BN);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(&tmB, &full_bar[s], b_dst + j * kBK * 128, tc.nt * BN + j * 64, tc.g * p.b_grp + kb * kBK);
+              tma_load_2d(&tmB, &full_bar[s], b_dst + j * kBK * 128, tc.nt * BN + j * 64, bgrp * p.b_grp + kb * kBK);
           }
         }
       }
@@ -256,7 +257,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
       const int row = tc.mt * kBM + r_in_tile;
       const bool row_ok = row < p.M;
-      const long crow = (long)tc.g * p.c_grp + row;
+      const long crow = (long)(p.c_mod ? tc.g % p.c_mod : tc.g) * p.c_grp + row;
       const int col0 = tc.nt * BN;
 
       if constexpr (EPI == EPI_SWIGLU) {
@@ -339,7 +340,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if constexpr (EPI == EPI_STORE) {
             if (p.c_f32) {
               float* Cp = reinterpret_cast<float*>(p.C) + crow * p.ldc + col;
-              if (p.c_accum) {
+              if (p.c_accum == 2) {
+#pragma unroll
+                for (int vv = 0; vv < 8; ++vv)
+                  atomicAdd(reinterpret_cast<float4*>(Cp) + vv,
+                            make_float4(p.alpha * v[4 * vv], p.alpha * v[4 * vv + 1], p.alpha * v[4 * vv + 2],
+                                        p.alpha * v[4 * vv + 3]));
+              } else if (p.c_accum) {
 #pragma unroll
                 for (int vv = 0; vv < 8; ++vv) {
                   float4 o = reinterpret_cast<float4*>(Cp)[vv];

@@ -33,11 +33,11 @@ def _pick_bn(n: int, epi: str, b_mn: bool, a_mn: bool) -> int:
 
 def gemm(a, b, c, *, a_mn=False, b_mn=False, G=1, M=None, N=None, K=None, counts=None, ragged=0,
          a_grp=0, b_grp=0, c_grp=0, epi="store", bn=None, accum=False, alpha=1.0, c2=None, r=None,
-         row_scale=None, act="silu"):
+         row_scale=None, act="silu", b_mod=0, c_mod=0):
     if bn is None:
         bn = _pick_bn(N, epi, b_mn, a_mn)
-    ext().gemm(a, a_mn, b, b_mn, c, G, M, N, K, counts, ragged, a_grp, b_grp, c_grp, EPI[epi], bn, accum,
-               float(alpha), c2, r, row_scale, ACT[act], err_flag(a.device))
+    ext().gemm(a, a_mn, b, b_mn, c, G, M, N, K, counts, ragged, a_grp, b_grp, c_grp, EPI[epi], bn, int(accum),
+               float(alpha), c2, r, row_scale, ACT[act], err_flag(a.device), b_mod, c_mod)
     return c
 
 
@@ -68,39 +68,45 @@ def linear_dw(dy, x, *, out=None, accum=False, alpha=1.0):
     return gemm(dy, x, out, a_mn=True, b_mn=True, M=n, N=k, K=t, accum=accum, alpha=alpha)
 
 
-def grouped_linear(x, w, counts, *, out=None, epi="store", c2=None, **kw):
-    """Per-expert ``x[g] @ w[g]^T`` over a capacity layout.
+def grouped_linear(x, w, counts, *, out=None, epi="store", c2=None, n_w=None, **kw):
+    """Per-group ``x[g] @ w[g % n_w]^T`` over a capacity layout.
 
-    x: ``[G*C, K]`` (expert g owns rows ``[g*C, (g+1)*C)``, only the first ``counts[g]`` valid),
-    w: ``[G*N, K]`` -> out ``[G*C, N]``; tiles past ``counts[g]`` rows are skipped."""
+    x: ``[G*C, K]`` (group g owns rows ``[g*C, (g+1)*C)``, only the first ``counts[g]`` valid),
+    w: ``[n_w*N, K]`` -> out ``[G*C, N]``; tiles past ``counts[g]`` rows are skipped. ``n_w < G`` lets
+    several activation groups (one per source rank) share an expert's weights."""
     g = counts.numel()
+    n_w = n_w or g
     cap = x.shape[0] // g
-    n = w.shape[0] // g
+    n = w.shape[0] // n_w
     k = x.shape[1]
     if out is None:
         out = torch.empty(x.shape[0], n, dtype=torch.bfloat16, device=x.device)
     return gemm(x, w, out, G=g, M=cap, N=n, K=k, counts=counts, ragged=1, a_grp=cap, b_grp=n, c_grp=cap,
-                epi=epi, c2=c2, **kw)
+                epi=epi, c2=c2, b_mod=0 if n_w == g else n_w, **kw)
 
 
-def grouped_linear_dx(dy, w, counts, *, out=None):
-    """Per-expert ``dy[g] [C, N] @ w[g] [N, K]`` -> ``[G*C, K]``."""
+def grouped_linear_dx(dy, w, counts, *, out=None, n_w=None):
+    """Per-group ``dy[g] [C, N] @ w[g % n_w] [N, K]`` -> ``[G*C, K]``."""
     g = counts.numel()
+    n_w = n_w or g
     cap = dy.shape[0] // g
-    n = w.shape[0] // g
+    n = w.shape[0] // n_w
     k = w.shape[1]
     if out is None:
         out = torch.empty(dy.shape[0], k, dtype=torch.bfloat16, device=dy.device)
     return gemm(dy, w, out, b_mn=True, G=g, M=cap, N=k, K=n, counts=counts, ragged=1, a_grp=cap, b_grp=n,
-                c_grp=cap)
+                c_grp=cap, b_mod=0 if n_w == g else n_w)
 
 
-def grouped_linear_dw(dy, x, counts, *, out, accum=True, alpha=1.0):
-    """Per-expert ``dy[g]^T @ x[g]`` contracting over the first ``counts[g]`` rows (rounded up to
-    64; rows past the count must be zero) -> ``out [G*N, K]`` fp32."""
+def grouped_linear_dw(dy, x, counts, *, out, accum=True, alpha=1.0, n_w=None):
+    """Per-group ``dy[g]^T @ x[g]`` contracting over the first ``counts[g]`` rows (rounded up to
+    64; rows past the count must be zero), accumulated into ``out [n_w*N, K]`` fp32 at weight group
+    ``g % n_w`` (with atomics when several groups share a weight group)."""
     g = counts.numel()
+    n_w = n_w or g
     cap = dy.shape[0] // g
     n = dy.shape[1]
     k = x.shape[1]
+    shared = n_w != g
     return gemm(dy, x, out, a_mn=True, b_mn=True, G=g, M=n, N=k, K=cap, counts=counts, ragged=2, a_grp=cap,
-                b_grp=cap, c_grp=n, accum=accum, alpha=alpha)
+                b_grp=cap, c_grp=n, accum=(2 if shared else accum), alpha=alpha, c_mod=n_w if shared else 0)

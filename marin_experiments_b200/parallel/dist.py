@@ -49,11 +49,9 @@ class DistContext:
             for info in st.infos:
                 if info.sharded_over is None:
                     torch_dist.broadcast(st.master_view(info), src=0, group=self.batch_group)
-            if self.ep_size > 1:
-                # different experts per rank: re-seed expert shards deterministically by rank
-                pass
             st.sync_compute()
         self._replicated = [i for i in st.infos if i.sharded_over is None and i.trainable]
+        self._sharded = [i for i in st.infos if i.sharded_over is not None and i.trainable]
 
     def setup_optimizer(self, trainer) -> None:
         opt = getattr(trainer.opt, "inner", trainer.opt)
@@ -87,10 +85,15 @@ class DistContext:
         opt.norm_hook = norm_hook
 
     def grad_sync(self, trainer) -> None:
-        """Mean-all-reduce the gradients of replicated parameters (bucketed over the flat buffer)."""
+        """Mean-all-reduce the gradients of replicated parameters (bucketed over the flat buffer).
+
+        Expert shards already hold the sum over every rank's tokens of per-rank mean-loss gradients;
+        dividing by the batch-group size turns that into the gradient of the global mean loss."""
         if self.world == 1:
             return
         st = trainer.store
+        for info in self._sharded:
+            st.grad[info.offset: info.offset + info.numel].div_(self.world)
         # contiguous runs of replicated parameters in the flat buffer
         runs = []
         for info in self._replicated:

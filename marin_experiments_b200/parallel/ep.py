@@ -1,0 +1,135 @@
+"""Expert parallelism: routed-expert MLP with experts sharded over an ``ep`` process group.
+
+Rank r owns experts ``[r*E_loc, (r+1)*E_loc)``. Each source rank plans its local tokens'
+assignments into a per-(source, expert) capacity of ``cap`` rows (first come, first served in
+token order; cap = ceil(cf * T * K / E) rounded up to 128), scatters them into a send buffer
+laid out ``[dest rank][local expert][cap][D]`` (= the single-GPU ``[E][cap]`` capacity layout), and
+one equal-split all-to-all delivers ``[source rank][local expert][cap][D]`` to every destination.
+The destination runs the grouped expert GEMMs over ``W * E_loc`` ragged groups (group
+``s*E_loc + e`` uses expert ``e``'s weights; weight gradients of groups sharing an expert accumulate
+with atomics) and a second all-to-all returns the outputs, which the source combines with its
+routing weights. Backward mirrors it (two more all-to-alls). Shapes are static; only the
+per-(source, expert) counts travel as data (a small all-to-all).
+
+This replaces the reference's ring EP (all-gather of every token to every expert shard, then
+psum-scatter; grug-moe-pp/pipeline.py:198-245), which moves W times more activation bytes.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..ops import api as ops
+
+
+def _a2a(out: torch.Tensor, inp: torch.Tensor, group) -> torch.Tensor:
+    dist.all_to_all_single(out, inp, group=group)
+    return out
+
+
+class _MoEEP(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h, comb, w_gu, w_d, residual, sel, keep, cap, group, act):
+        from ..ops import gemm as G
+        from ..ops._ext import ext
+        from ..ops.cuda_fns import _ACT, _c, dispatch_plan
+
+        h = _c(h)
+        t, d = h.shape
+        e_loc, two_i, _ = w_gu.shape
+        inter = two_i // 2
+        world = dist.get_world_size(group)
+        e = e_loc * world
+        dev = h.device
+        slot, perm, wperm, counts = dispatch_plan(sel, keep, comb, e, cap)
+        xp_send = torch.empty(e * cap, d, dtype=torch.bfloat16, device=dev)
+        ext().permute(h, perm, counts, cap, xp_send)
+        counts_recv = _a2a(torch.empty_like(counts), counts, group)
+        xp_recv = _a2a(torch.empty_like(xp_send), xp_send, group)
+        Hh = torch.empty(e * cap, two_i, dtype=torch.bfloat16, device=dev)
+        A = torch.empty(e * cap, inter, dtype=torch.bfloat16, device=dev)
+        G.grouped_linear(xp_recv, w_gu.view(e_loc * two_i, d), counts_recv, out=Hh, epi="swiglu", c2=A, n_w=e_loc)
+        y_recv = G.grouped_linear(A, w_d.view(e_loc * d, inter), counts_recv, n_w=e_loc)
+        y_send = _a2a(torch.empty_like(y_recv), y_recv, group)
+        out = torch.empty(t, d, dtype=torch.bfloat16, device=dev)
+        ext().combine(y_send, sel, slot, _c(comb.detach().float()), None if residual is None else _c(residual), out,
+                      cap)
+        ctx.save_for_backward(xp_recv, Hh, A, y_send, sel, slot, perm, wperm, counts, counts_recv)
+        ctx.w_gu, ctx.w_d, ctx.cap, ctx.group, ctx.act, ctx.t = w_gu, w_d, cap, group, _ACT[act], t
+        ctx.has_res = residual is not None
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        from ..ops import gemm as G
+        from ..ops._ext import ext
+        from ..ops.cuda_fns import _c, _mg
+
+        xp_recv, Hh, A, y_send, sel, slot, perm, wperm, counts, counts_recv = ctx.saved_tensors
+        dout = _c(dout)
+        w_gu, w_d, cap, group = ctx.w_gu, ctx.w_d, ctx.cap, ctx.group
+        e_loc, two_i, d = w_gu.shape
+        inter = two_i // 2
+        dev = dout.device
+        dy_send = torch.empty_like(y_send)
+        dcomb = torch.empty(sel.shape, dtype=torch.float32, device=dev)
+        ext().combine_bwd(dout, y_send, sel, slot, perm, wperm, counts, cap, dy_send, dcomb)
+        dy_recv = _a2a(torch.empty_like(dy_send), dy_send, group)
+        dA = G.grouped_linear_dx(dy_recv, w_d.view(e_loc * d, inter), counts_recv, n_w=e_loc)
+        G.grouped_linear_dw(dy_recv, A, counts_recv, out=_mg(w_d).view(e_loc * d, inter), n_w=e_loc)
+        dH = torch.empty_like(Hh)
+        ext().swiglu_bwd(dA, Hh, dH, ctx.act, counts_recv, cap)
+        dxp_recv = G.grouped_linear_dx(dH, w_gu.view(e_loc * two_i, d), counts_recv, n_w=e_loc)
+        G.grouped_linear_dw(dH, xp_recv, counts_recv, out=_mg(w_gu).view(e_loc * two_i, d), n_w=e_loc)
+        dxp_send = _a2a(torch.empty_like(dxp_recv), dxp_recv, group)
+        dh = torch.empty(ctx.t, d, dtype=torch.bfloat16, device=dev)
+        ext().unpermute_add(dxp_send, sel, slot, None, dh, cap)
+        ctx.w_gu = ctx.w_d = None
+        return dh, dcomb, None, None, (dout if ctx.has_res else None), None, None, None, None, None
+
+
+def _moe_ep_cpu(h, r, w_gu, w_d, cap, group, residual, act):
+    """Differentiable CPU/gloo version (torch ops + autograd all-to-all); the oracle of the GPU path."""
+    from torch.distributed.nn.functional import all_to_all_single
+
+    from ..ops import reference as R
+    from ..ops.layout import split_gate_up
+
+    t, d = h.shape
+    e_loc = w_gu.shape[0]
+    inter = w_d.shape[2]
+    world = dist.get_world_size(group)
+    e = e_loc * world
+    keep = None if bool(r.keep.all()) else r.keep
+    slots, counts = R.capacity_slots(r.selected, e, cap, keep)
+    valid = slots >= 0
+    rows = (r.selected * cap + slots.clamp_min(0))[valid]
+    tok = torch.arange(t).unsqueeze(1).expand_as(r.selected)[valid]
+    send = torch.zeros(e * cap, d, dtype=h.dtype)
+    send = send.index_copy(0, rows, h[tok])
+    cnt_recv = torch.empty_like(counts)
+    dist.all_to_all_single(cnt_recv, counts.contiguous(), group=group)
+    recv = all_to_all_single(torch.empty_like(send), send, group=group)
+    outs = []
+    for g in range(world * e_loc):
+        ex = g % e_loc
+        xg = recv[g * cap:(g + 1) * cap]
+        hg = xg @ w_gu[ex].t()
+        gg, uu = split_gate_up(hg, inter)
+        outs.append((R.activation(gg, act) * uu) @ w_d[ex].t())
+    y_recv = torch.cat(outs, 0)
+    y_send = all_to_all_single(torch.empty_like(y_recv), y_recv, group=group)
+    w = (r.combine * valid.to(r.combine.dtype))[valid]
+    contrib = y_send[rows] * w.unsqueeze(1).to(y_send.dtype)
+    out = torch.zeros(t, d, dtype=h.dtype).index_add(0, tok, contrib)
+    return out if residual is None else residual + out
+
+
+def moe_experts_ep(h, r, w_gate_up, w_down, capacity, group, residual=None, act: str = "silu"):
+    t = h.shape[0]
+    cap = capacity if capacity is not None else ops.capacity_for(t, r.selected.shape[1], 1, 1.0)
+    if not h.is_cuda:
+        return _moe_ep_cpu(h, r, w_gate_up, w_down, cap, group, residual, act)
+    keep = None if r.keep is None else r.keep.to(torch.uint8)
+    return _MoEEP.apply(h, r.combine, w_gate_up, w_down, residual, r.selected, keep, cap, group, act)

@@ -61,7 +61,7 @@ class Trainer:
             model = Transformer(cfg, local_experts=local)
         self.model = model
         self.store = ParamStore(model, self.device)
-        init_store_weights(self.store, cfg, self.seed)
+        init_store_weights(self.store, cfg, self.seed, model)
         if self.dist is not None:
             self.dist.setup_model(self)
         opt_cfg = self.cfg.optimizer
