@@ -1,0 +1,441 @@
+// Flash attention forward on the 5th-generation tensor cores (sm_100a).
+//
+// CTA = one 128-query tile of one head: warps 0-3 run the softmax (thread = query row = TMEM
+// lane), warp 4 issues tcgen05.mma (one elected thread), warp 5 issues the TMA loads. For each
+// 128-key block j:
+//   S_j = Q K_j^T            (SS MMA: Q, K_j from 128B-swizzled smem; S_j in TMEM, fp32)
+//   P_j = exp2(S_j*c - m)    (softmax warps: tcgen05.ld S, tcgen05.st P as bf16 into TMEM)
+//   O  += P_j V_j            (TS MMA: A = P_j from TMEM, B = V_j MN-major from smem; O in TMEM)
+// The running max is only raised (and O, l rescaled) when a row max grows by more than 2^8, so
+// most blocks skip the O correction. 96 KB of smem and 256 TMEM columns per CTA let two CTAs
+// share an SM, so one CTA's softmax overlaps the other's MMAs. All waits are bounded.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.h"
+#include "sm100_primitives.cuh"
+
+namespace mxk {
+namespace fa100 {
+
+constexpr int BM = 128;  // queries per CTA
+constexpr int BN = 128;  // keys per block
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct FwdArgs {
+  int B, S, H, Hkv, hd;
+  int window;
+  float scale_log2;
+  const int* seg;
+  __nv_bfloat16* o;  // [T, H, hd]
+  float* lse;        // [T, H]
+  int q_x0, k_x0, v_x0;  // column offsets (elements) of head 0 in the Q / K / V tensor maps
+  int* err;
+  // Optional phase-timing counters (cycles, summed over CTAs): [0] softmax wait s_full, [1] pass 1,
+  // [2] pass 2, [3] O rescale, [4] MMA wait p_full, [5] MMA wait kv_full, [6] MMA wait o_done,
+  // [7] softmax blocks, [8] rescales.
+  unsigned long long* prof;
+};
+
+__device__ __forceinline__ void umma_ts_bf16(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ bool visible(int qi, int kj, int S, int window, const int* seg, int base) {
+  if (kj > qi || kj >= S || qi >= S) return false;
+  if (window > 0 && qi - kj >= window) return false;
+  if (seg && seg[base + qi] != seg[base + kj]) return false;
+  return true;
+}
+
+template <int HD>
+struct Smem {
+  static constexpr int KCH = (HD + 63) / 64;        // 64-element (128 B) chunks along head_dim
+  static constexpr int kTile = KCH * BM * 128;       // one [128 rows x HD] operand tile
+  // Q0, Q1, K[2 stages], V[2 stages]
+  static constexpr int kBytes = 6 * kTile + 1024 + 512;
+};
+
+// Visible key range of query qi: [lo, hi] (segments are contiguous runs of equal ids).
+__device__ __forceinline__ void key_range(int qi, int S, int window, const int* seg, int base, int& lo, int& hi) {
+  hi = qi < S ? qi : -1;
+  lo = 0;
+  if (window > 0) lo = max(lo, qi - window + 1);
+  if (seg && qi < S) {
+    // first position of qi's segment: binary search on the non-decreasing run boundary
+    const int sid = seg[base + qi];
+    int a = 0, b = qi;
+    while (a < b) {
+      const int m = (a + b) >> 1;
+      if (seg[base + m] == sid) b = m; else a = m + 1;
+    }
+    lo = max(lo, a);
+  }
+}
+
+// Ping-pong forward: CTA = two 128-query tiles (rows q0..q0+255) of one head.
+// warps 0-3: softmax of tile 0, warps 4-7: softmax of tile 1, warp 8: MMA, warp 9: TMA.
+// TMEM: S0 [0,128) S1 [128,256) O0 [256,256+HD) O1 [384,384+HD).
+constexpr int kThreadsPP = 320;
+
+template <int HD>
+__global__ void __launch_bounds__(kThreadsPP, 1)
+    fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const FwdArgs a) {
+  using SM = Smem<HD>;
+  constexpr int KCH = SM::KCH;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                    // [2][tile]
+  uint8_t* sK = smem + 2 * SM::kTile;    // [2 stages][tile]
+  uint8_t* sV = smem + 4 * SM::kTile;    // [2 stages][tile]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * SM::kTile);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2] per tile
+  uint64_t* p_full = bars + 7;    // [2] per tile
+  uint64_t* o_done = bars + 9;    // [2] per tile
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kh = h / (a.H / a.Hkv);
+  const int q0 = blockIdx.x * 2 * BM;
+  const int base = b * a.S;
+  // key blocks for the two tiles; tile 0 stops one block earlier (causal)
+  int kb_lo = 0;
+  if (a.window > 0) kb_lo = max(0, q0 - a.window + 1) / BN;
+  const int kb_hi1 = (min(a.S, q0 + 2 * BM) + BN - 1) / BN;
+  const int kb_hi0 = (min(a.S, q0 + BM) + BN - 1) / BN;
+  const int nb = max(kb_hi1 - kb_lo, 0);
+  // tile t uses blocks j in [lo_t, nb_t); tile 1 may skip early blocks outside its window
+  int lo_t[2], nb_t[2];
+  nb_t[0] = max(kb_hi0 - kb_lo, 0);
+  nb_t[1] = nb;
+  lo_t[0] = 0;
+  lo_t[1] = 0;
+  if (a.window > 0) lo_t[1] = max(0, (q0 + BM - a.window + 1) / BN - kb_lo);
+  if (q0 + BM >= a.S) nb_t[1] = 0;  // tile 1 entirely past the sequence
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 9) {
+    // ------------------------------------------------------------------------ TMA producer
+    if (lane == 0 && nb > 0) {
+      constexpr uint32_t tile = SM::kTile;
+      mbar_arrive_expect_tx(q_full, 2 * tile);
+      for (int t = 0; t < 2; ++t)
+        for (int c = 0; c < KCH; ++c)
+          tma_load_2d(&tmQ, q_full, sQ + t * tile + c * BM * 128, a.q_x0 + h * HD + c * 64, base + q0 + t * BM);
+      for (int j = 0; j < nb; ++j) {
+        const int st = j & 1;
+        const int kr = base + (kb_lo + j) * BN;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, a.err, kErrTimeoutProducer, abort_flag)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * tile);
+        for (int c = 0; c < KCH; ++c) {
+          tma_load_2d(&tmK, &kv_full[st], sK + st * tile + c * BN * 128, a.k_x0 + kh * HD + c * 64, kr);
+          tma_load_2d(&tmV, &kv_full[st], sV + st * tile + c * BN * 128, a.v_x0 + kh * HD + c * 64, kr);
+        }
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nb > 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idesc_o = make_idesc_bf16(BM, HD, false, true);
+      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      int s_cnt[2] = {0, 0};  // S/PV issue counters per tile (barrier phases)
+      bool ok = mbar_wait(q_full, 0, a.err, kErrTimeoutMma, abort_flag);
+      auto issue_qk = [&](int t, int st) {
+        const uint32_t qa = q_addr + t * SM::kTile, ka = k_addr + st * SM::kTile;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t off = (ks / 4) * BM * 128 + (ks % 4) * 32;
+          umma_bf16(tmem + t * 128, make_sdesc(qa + off, 16, 1024), make_sdesc(ka + off, 16, 1024), idesc_s,
+                    ks > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int st, bool acc) {
+        const uint32_t va = v_addr + st * SM::kTile;
+#pragma unroll
+        for (int ks = 0; ks < BN / 16; ++ks)
+          umma_ts_bf16(tmem + 256 + t * 128, tmem + t * 128 + ks * 8, make_sdesc(va + ks * 2048, BN * 128, 1024),
+                       idesc_o, (acc || ks > 0) ? 1u : 0u);
+        umma_commit(&o_done[t]);
+      };
+      unsigned long long wp = 0, wkv = 0, wo = 0;
+      for (int j = 0; j < nb && ok; ++j) {
+        const int st = j & 1;
+        long long c0 = clock64();
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
+        wkv += clock64() - c0;
+        tc_fence_after();
+        bool act[2];
+        for (int t = 0; t < 2; ++t) act[t] = j >= lo_t[t] && j < nb_t[t];
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!act[t]) continue;
+          // S_t overwrites P_t of the previous block: its PV must have completed
+          if (s_cnt[t] > 0) {
+            long long c1 = clock64();
+            if (!mbar_wait(&o_done[t], (s_cnt[t] - 1) & 1, a.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
+            wo += clock64() - c1;
+            tc_fence_after();
+          }
+          issue_qk(t, st);
+        }
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!act[t]) continue;
+          long long c2 = clock64();
+          if (!mbar_wait(&p_full[t], s_cnt[t] & 1, a.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
+          wp += clock64() - c2;
+          tc_fence_after();
+          issue_pv(t, st, s_cnt[t] > 0);
+          ++s_cnt[t];
+        }
+        umma_commit(&kv_empty[st]);
+      }
+      if (a.prof) {
+        atomicAdd(&a.prof[4], wp);
+        atomicAdd(&a.prof[5], wkv);
+        atomicAdd(&a.prof[6], wo);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------------ softmax warps
+    const int t = warp >> 2;              // tile
+    const int row = (warp & 3) * 32 + lane;
+    const int qi = q0 + t * BM + row;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + t * 128 + lane_off;
+    const uint32_t t_o = tmem + 256 + t * 128 + lane_off;
+    int klo, khi;
+    key_range(qi, a.S, a.window, a.seg, base, klo, khi);
+    float m_run = -INFINITY, l_run = 0.f;
+    bool alive = true;
+    int cnt = 0;
+    unsigned long long pw = 0, p1 = 0, p2 = 0, p3 = 0, nres = 0;
+    for (int j = lo_t[t]; j < nb_t[t]; ++j, ++cnt) {
+      long long c_a = clock64();
+      const bool got = mbar_wait(&s_full[t], cnt & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      long long c_b = clock64();
+      pw += c_b - c_a;
+      if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+      tc_fence_after();
+      const int k0 = (kb_lo + j) * BN;
+      const int lo = klo - k0, hi = khi - k0;  // visible columns [lo, hi] of this block
+      const bool full = lo <= 0 && hi >= BN - 1;
+      // S row (128 fp32 columns) into registers with all four loads in flight, one wait
+      float s0[32], s1[32], s2[32], s3[32];
+      tmem_ld32(t_s + 0, s0);
+      tmem_ld32(t_s + 32, s1);
+      tmem_ld32(t_s + 64, s2);
+      tmem_ld32(t_s + 96, s3);
+      tmem_wait_ld();
+      if (!full) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          if (c < lo || c > hi) s0[c] = -INFINITY;
+          if (c + 32 < lo || c + 32 > hi) s1[c] = -INFINITY;
+          if (c + 64 < lo || c + 64 > hi) s2[c] = -INFINITY;
+          if (c + 96 < lo || c + 96 > hi) s3[c] = -INFINITY;
+        }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) mx = fmaxf(mx, fmaxf(fmaxf(s0[c], s1[c]), fmaxf(s2[c], s3[c])));
+      mx *= a.scale_log2;
+      long long c_c = clock64();
+      p1 += c_c - c_b;
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > m_run + kRescaleThreshold || (m_run == -INFINITY && mx > -INFINITY)) {
+        if (m_run != -INFINITY) {
+          alpha = exp2f(m_run - mx);
+          rescale = true;
+        }
+        m_run = mx;
+        l_run *= alpha;
+      }
+      const float mb = m_run == -INFINITY ? 0.f : m_run;
+      const float sc = a.scale_log2;
+      float rs = 0.f;
+      // P = exp2(s*c - m) as bf16 pairs into the first 64 columns of S (all reads are done)
+      {
+        uint32_t w[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const float e0 = exp2f(fmaf(s0[c], sc, -mb)), e1 = exp2f(fmaf(s0[c + 1], sc, -mb));
+          rs += e0 + e1;
+          w[c / 2] = pack_bf16x2(e0, e1);
+        }
+        tmem_st16(t_s + 0, w);
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const float e0 = exp2f(fmaf(s1[c], sc, -mb)), e1 = exp2f(fmaf(s1[c + 1], sc, -mb));
+          rs += e0 + e1;
+          w[c / 2] = pack_bf16x2(e0, e1);
+        }
+        tmem_st16(t_s + 16, w);
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const float e0 = exp2f(fmaf(s2[c], sc, -mb)), e1 = exp2f(fmaf(s2[c + 1], sc, -mb));
+          rs += e0 + e1;
+          w[c / 2] = pack_bf16x2(e0, e1);
+        }
+        tmem_st16(t_s + 32, w);
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const float e0 = exp2f(fmaf(s3[c], sc, -mb)), e1 = exp2f(fmaf(s3[c + 1], sc, -mb));
+          rs += e0 + e1;
+          w[c / 2] = pack_bf16x2(e0, e1);
+        }
+        tmem_st16(t_s + 48, w);
+      }
+      l_run += rs;
+      long long c_d = clock64();
+      p2 += c_d - c_c;
+      if (__any_sync(0xffffffffu, rescale)) {
+        ++nres;
+        const bool g2 = mbar_wait(&o_done[t], (cnt - 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+        if (!__all_sync(0xffffffffu, g2)) { alive = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 16) {
+          float o[16];
+          tmem_ld16(t_o + c, o);
+          tmem_wait_ld();
+          uint32_t ou[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) ou[u] = __float_as_uint(o[u] * alpha);
+          tmem_st16(t_o + c, ou);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+      p3 += clock64() - c_d;
+    }
+    if (a.prof && lane == 0) {
+      atomicAdd(&a.prof[0], pw);
+      atomicAdd(&a.prof[1], p1);
+      atomicAdd(&a.prof[2], p2);
+      atomicAdd(&a.prof[3], p3);
+      atomicAdd(&a.prof[7], (unsigned long long)cnt);
+      atomicAdd(&a.prof[8], nres);
+    }
+    if (alive && cnt > 0) {
+      const bool got = mbar_wait(&o_done[t], (cnt - 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      if (__all_sync(0xffffffffu, got)) {
+        tc_fence_after();
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        __nv_bfloat16* orow = a.o + ((long)(base + qi) * a.H + h) * HD;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 16) {
+          float o[16];
+          tmem_ld16(t_o + c, o);
+          tmem_wait_ld();
+          if (qi < a.S) {
+            uint32_t pkd[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) pkd[u] = pack_bf16x2(o[2 * u] * inv, o[2 * u + 1] * inv);
+            reinterpret_cast<uint4*>(orow + c)[0] = make_uint4(pkd[0], pkd[1], pkd[2], pkd[3]);
+            reinterpret_cast<uint4*>(orow + c)[1] = make_uint4(pkd[4], pkd[5], pkd[6], pkd[7]);
+          }
+        }
+        if (qi < a.S)
+          a.lse[(long)(base + qi) * a.H + h] = l_run > 0.f ? (m_run + log2f(l_run)) * 0.6931471805599453f : INFINITY;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fa100
+
+bool make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner,
+                       int box_outer);
+
+template <int HD>
+static int run_fa_fwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
+  using namespace fa100;
+  CUtensorMap tq, tk, tv;
+  const long T = (long)L.B * L.S;
+  // 2-D maps over [tokens, row elements]; a head's 64-wide chunk starts at x = head * hd + 64 c
+  // inner extent = the heads actually present (columns past it read as zero, never past the buffer)
+  if (!make_tmap_bf16_2d(&tq, L.q, (long)L.H * HD, T, L.q_tok, 64, BM)) return kErrBadArgsHost;
+  if (!make_tmap_bf16_2d(&tk, L.k, (long)L.Hkv * HD, T, L.k_tok, 64, BN)) return kErrBadArgsHost;
+  if (!make_tmap_bf16_2d(&tv, L.v, (long)L.Hkv * HD, T, L.v_tok, 64, BN)) return kErrBadArgsHost;
+  FwdArgs a{};
+  a.B = L.B; a.S = L.S; a.H = L.H; a.Hkv = L.Hkv; a.hd = HD; a.window = L.window;
+  a.scale_log2 = L.scale * 1.4426950408889634f;
+  a.seg = L.seg;
+  a.o = (__nv_bfloat16*)L.o;
+  a.lse = L.lse;
+  a.q_x0 = 0; a.k_x0 = 0; a.v_x0 = 0;
+  a.err = err;
+  a.prof = (unsigned long long*)L.prof;
+  constexpr int smem = Smem<HD>::kBytes;
+  static bool init = false;
+  if (!init) {
+    if (cudaFuncSetAttribute(fa_fwd_sm100_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return kErrBadArgsHost;
+    init = true;
+  }
+  dim3 grid((L.S + 2 * BM - 1) / (2 * BM), L.H, L.B);
+  count_launch();
+  fa_fwd_sm100_kernel<HD><<<grid, kThreadsPP, smem, st>>>(tq, tk, tv, a);
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
+}
+
+// q / k / v: row-major [tokens, row] bf16 with the head's hd elements at column head*hd (q: H
+// heads, k / v: Hkv heads; v may start at an offset inside a wider row, passed via L.v).
+int launch_flash_fwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
+  if (L.q_head != L.hd || L.k_head != L.hd || L.v_head != L.hd) return kErrBadArgsHost;
+  if ((L.q_tok * 2) % 16 || (L.k_tok * 2) % 16 || (L.v_tok * 2) % 16) return kErrBadArgsHost;
+  if ((reinterpret_cast<uintptr_t>(L.q) | reinterpret_cast<uintptr_t>(L.k) | reinterpret_cast<uintptr_t>(L.v)) & 15)
+    return kErrBadArgsHost;
+  switch (L.hd) {
+    case 64: return run_fa_fwd_sm100<64>(L, err, st);
+    case 96: return run_fa_fwd_sm100<96>(L, err, st);
+    case 128: return run_fa_fwd_sm100<128>(L, err, st);
+    default: return kErrBadArgsHost;
+  }
+}
+
+}  // namespace mxk

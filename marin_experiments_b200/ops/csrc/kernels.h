@@ -91,8 +91,11 @@ struct AttnLaunch {
   void* dv;
   long dv_tok, dv_head;
   int dv_accumulate;
+  void* prof;  // optional phase-timing counters (debug)
 };
 int launch_flash_fwd(const AttnLaunch& L, cudaStream_t st);
 int launch_flash_bwd(const AttnLaunch& L, cudaStream_t st);
+// tcgen05 forward (attention_sm100.cu); q/k/v heads contiguous (head stride == hd)
+int launch_flash_fwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st);
 
 }  // namespace mxk

@@ -178,6 +178,15 @@ void flash_fwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& 
   ok(mxk::launch_flash_fwd(L, stream()), "flash_fwd");
 }
 
+void flash_fwd_sm100(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& lse,
+                     const OptT& seg, int64_t B, int64_t S, int64_t window, double scale, const Tensor& err,
+                     const OptT& prof) {
+  auto L = attn_args(q, k, v, o, lse, seg, B, S, window, scale);
+  L.prof = prof.has_value() ? prof->data_ptr() : nullptr;
+  c10::cuda::CUDAGuard g(q.device());
+  ok(mxk::launch_flash_fwd_sm100(L, err.data_ptr<int>(), stream()), "flash_fwd_sm100");
+}
+
 void flash_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& lse, const OptT& seg,
                int64_t B, int64_t S, int64_t window, double scale, const Tensor& dout, const Tensor& dsum,
                const Tensor& dq_acc, const Tensor& dq, const Tensor& dk, const Tensor& dv, bool dv_accumulate) {
@@ -322,6 +331,7 @@ void register_ops(pybind11::module& m) {
   m.def("ce_grad", &ce_grad);
   m.def("flash_fwd", &flash_fwd);
   m.def("flash_bwd", &flash_bwd);
+  m.def("flash_fwd_sm100", &flash_fwd_sm100);
   m.def("router_fwd", &router_fwd);
   m.def("router_bwd", &router_bwd);
   m.def("qb_beta", &qb_beta);

@@ -194,7 +194,14 @@ class _AttentionBlock(torch.autograd.Function):
         lse = torch.empty(t, nh, dtype=F32, device=h.device)
         seg = None if seg is None else _c(seg.int())
         scale = 1.0 / math.sqrt(hd)
-        ext().flash_fwd(qn, kn, v, o, lse, seg, shape.batch, s, shape.window, scale)
+        if hd in (64, 96, 128):
+            from ._ext import err_flag
+
+            # tcgen05 forward (TMEM accumulators, TMA-fed); segments must be contiguous runs
+            ext().flash_fwd_sm100(qn, kn, v, o, lse, seg, shape.batch, s, shape.window, scale, err_flag(h.device),
+                                  None)
+        else:
+            ext().flash_fwd(qn, kn, v, o, lse, seg, shape.batch, s, shape.window, scale)
         if shape.xsa or use_gate:
             o2 = torch.empty(t, nq, dtype=BF16, device=h.device)
             ext().xsa_gate_fwd(o, qkvg, nq + nk, nq + 2 * nk, o2, nh, hkv, hd, shape.xsa, use_gate)
