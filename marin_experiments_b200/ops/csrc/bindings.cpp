@@ -90,6 +90,17 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const 
   p.alpha = (float)alpha;
   p.act_kind = (int)act_kind;
   p.err = reinterpret_cast<int*>(err.data_ptr());
+  p.ksplit = 1;
+  // Output extents for the TMA stores: columns clip at N; rows clip at M for a single problem,
+  // at the buffer end for grouped problems.
+  L.c_cols = N;
+  L.c_rows = G == 1 ? std::min<int64_t>(M, C.size(0)) : C.size(0);
+  if (C2.has_value()) {
+    L.c2_f32 = C2->scalar_type() == at::kFloat ? 1 : 0;
+    L.c2_cols = epi == 1 ? N / 2 : std::min<int64_t>(N, C2->size(1));
+    L.c2_rows = G == 1 ? std::min<int64_t>(M, C2->size(0)) : C2->size(0);
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(C2->data_ptr()) % 16 == 0, "C2 must be 16-byte aligned");
+  }
   if (std::getenv("MXK_TRACE")) { std::fprintf(stderr, "[mxk] binding -> launch_gemm\n"); std::fflush(stderr); }
   check_code(mxk::launch_gemm(L, cur_stream()), "gemm");
 }

@@ -77,6 +77,23 @@ bool make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, int64_t inner, int64_t o
   return r == CUDA_SUCCESS;
 }
 
+// 2-D tensor map for an epilogue output: 64-byte-wide boxes of 32 rows (16 fp32 or 32 bf16
+// columns), 64-byte swizzle (matches the staging layout in gemm_sm100.cuh).
+bool make_tmap_epi(CUtensorMap* m, const void* ptr, bool f32, int64_t cols, int64_t rows, int64_t ld) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  ensure_current_context();
+  const int es = f32 ? 4 : 2;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
+  cuuint32_t box[2] = {(cuuint32_t)(64 / es), 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr),
+                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -90,30 +107,49 @@ int num_sms() {
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
   MXK_TRACE("launch_impl enter");
-  CUtensorMap ta, tb;
-  if (trace_on()) std::fprintf(stderr, "[mxk] tmap addr %p %p\n", (void*)&ta, (void*)&tb);
+  CUtensorMap ta, tb, tc, tc2;
   // A tile: K-major -> box {64 (K), 128 rows}; MN-major -> box {64 (M), 64 (K rows)}
   if (!make_tmap_bf16_2d(&ta, L.a, L.a_inner, L.a_outer, L.lda, 64, A_MN ? 64 : kBM)) return kErrBadArgs;
-  MXK_TRACE("tmap A");
   if (!make_tmap_bf16_2d(&tb, L.b, L.b_inner, L.b_outer, L.ldb, 64, B_MN ? 64 : BN)) return kErrBadArgs;
-  MXK_TRACE("tmap B");
+  if (!make_tmap_epi(&tc, L.p.C, L.p.c_f32 != 0, L.c_cols, L.c_rows, L.p.ldc)) return kErrBadArgs;
+  if (L.p.C2 != nullptr && EPI != EPI_CE) {
+    if (!make_tmap_epi(&tc2, L.p.C2, L.c2_f32 != 0, L.c2_cols, L.c2_rows, L.p.ldc2)) return kErrBadArgs;
+  } else {
+    tc2 = tc;
+  }
+  MXK_TRACE("tmaps");
   auto kern = gemm_sm100_kernel<BN, STAGES, A_MN, B_MN, EPI>;
   constexpr int smem = gemm_smem_bytes<BN, STAGES>();
+  static_assert(smem <= 232448, "shared memory budget exceeded");
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return kErrBadArgs;
     attr_set = true;
   }
-  // Upper bound on the number of tiles (ragged groups may have fewer); the kernel strides.
-  const int n_tiles = (L.p.N + BN - 1) / BN;
-  const int m_tiles = (L.p.M + kBM - 1) / kBM;
-  long long tiles = (long long)L.p.G * m_tiles * n_tiles;
+  GemmParams p = L.p;
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const int m_tiles = (p.M + kBM - 1) / kBM;
+  long long tiles = (long long)p.G * m_tiles * n_tiles;
+  // Split K over CTAs when a non-grouped fp32 accumulation has too few output tiles for the GPU;
+  // the partial sums are combined by the element-wise atomic TMA reduce-add.
+  p.ksplit = 1;
+  if (p.G == 1 && p.ragged == 0 && p.c_f32 && p.c_accum && tiles < 2 * num_sms()) {
+    const int nkb = (p.K + kBK - 1) / kBK;
+    int ks = (int)((2 * num_sms() + tiles - 1) / tiles);
+    ks = ks < nkb ? ks : nkb;
+    if (ks > 1) {
+      const int per = (nkb + ks - 1) / ks;
+      ks = (nkb + per - 1) / per;  // no empty splits
+      p.ksplit = ks;
+      tiles *= ks;
+    }
+  }
   int grid = (int)(tiles < num_sms() ? tiles : num_sms());
   if (grid <= 0) return 0;
   MXK_TRACE("launch");
   count_launch();
-  kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, L.p);
+  kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, tc, tc2, p);
   MXK_TRACE("launched");
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgs;
 }
@@ -124,6 +160,7 @@ static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
 
 int launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   MXK_TRACE("launch_gemm");
+  if (L.p.G > 1 && L.p.M % kBM != 0) return kErrBadArgs;  // grouped outputs are stored in whole tiles
   if (L.p.G <= 0 || L.p.G > kMaxGroups || L.p.K <= 0 || L.p.N <= 0 || L.p.M <= 0) return kErrBadArgs;
   if (L.p.K % kBK != 0 && L.p.ragged != 2) return kErrBadArgs;
   if ((reinterpret_cast<uintptr_t>(L.a) | reinterpret_cast<uintptr_t>(L.b)) & 15) return kErrBadArgs;

@@ -12,6 +12,7 @@ struct GemmParams {
   // Group index used for B / C offsets: (b_mod ? g % b_mod : g), likewise c_mod. Lets
   // (source rank, expert) activation groups share one expert's weights and weight gradient.
   int b_mod, c_mod;
+  int ksplit;  // K splits per output tile (non-grouped, accumulating fp32 C only)
   void* C;
   int ldc;
   int c_f32;

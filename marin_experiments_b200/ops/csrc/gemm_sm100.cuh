@@ -8,14 +8,18 @@
 // passes need is a descriptor choice instead of a copy.
 //
 // Grouping: G independent problems that share N and K. Group g reads A rows starting at outer
-// coordinate g*a_grp, B rows at g*b_grp and writes C rows starting at g*c_grp. A device array of
-// per-group counts makes either M (expert token counts) or K (weight-gradient contraction over
-// the tokens an expert received) ragged; tiles past the count are never scheduled.
+// coordinate g*a_grp, B rows at (b_mod ? g % b_mod : g)*b_grp and writes C rows starting at
+// (c_mod ? g % c_mod : g)*c_grp. A device array of per-group counts makes either M (expert token
+// counts) or K (weight-gradient contraction over the tokens an expert received) ragged; tiles
+// past the count are never scheduled. Non-grouped GEMMs can split K over CTAs (``ksplit``).
 //
 // CTA = 6 warps:  warp 0 = TMA producer, warp 1 = MMA issuer (+ TMEM owner),
 //                 warps 2..5 = epilogue (TMEM lane quadrant = warp % 4).
 // Accumulators are double-buffered in TMEM (2 x BN fp32 columns) so the epilogue of tile i
-// overlaps the main loop of tile i+1. One CTA per SM, grid = min(#tiles, #SMs).
+// overlaps the main loop of tile i+1. Epilogue warps stage 32-row x 64-byte boxes of their rows
+// in 64B-swizzled shared memory (a 4-deep ring per warp) and write them with TMA bulk stores;
+// fp32 accumulation into an existing C (weight gradients, split-K partials) uses the TMA bulk
+// reduce-add, which is element-wise atomic. One CTA per SM, grid = min(#tiles, #SMs).
 #pragma once
 #include "gemm_params.h"
 #include "sm100_primitives.cuh"
@@ -25,17 +29,19 @@ namespace mxk {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kGemmThreads = 192;
-constexpr int kMaxGroups = 512;
+constexpr int kMaxGroups = 256;
+constexpr int kStageBufs = 4;    // epilogue staging ring depth per warp
+constexpr int kStageBox = 2048;  // 32 rows x 64 bytes
 
 enum EpiKind : int {
-  EPI_STORE = 0,   // C = alpha*acc (bf16 or f32), or C += alpha*acc (f32, accumulate)
-  EPI_SWIGLU = 1,  // BN=256 tile = [gate 128 | up 128]: H = acc (bf16), Act = silu(gate)*up (bf16)
-  EPI_RESID = 2,   // C = acc + R (bf16); R may alias C
+  EPI_STORE = 0,     // C = alpha*acc (bf16 or f32), or C += alpha*acc (f32, TMA reduce-add)
+  EPI_SWIGLU = 1,    // BN=256 tile = [gate 128 | up 128]: H = acc (bf16), Act = silu(gate)*up (bf16)
+  EPI_RESID = 2,     // C = acc + R (bf16); R may alias C
   EPI_GATE_MUL = 3,  // C = X * sigmoid(acc) (bf16), X given in R (GatedNorm up projection)
-  EPI_SILU = 4,    // C = silu(acc) (bf16) and H = acc (bf16) (GatedNorm down projection)
+  EPI_SILU = 4,      // C = silu(acc) (bf16) and H = acc (bf16) (GatedNorm down projection)
   EPI_ROWSCALE = 5,  // C = acc * row_scale[row] (bf16)
-  EPI_CE = 6,      // logits tile: C = acc (bf16) and per-(row, n-tile) max / sum(exp(x - max))
-  EPI_ACT = 7,     // non-GLU MLP: H = acc (bf16), C = act(acc) (bf16); act in `act_kind`
+  EPI_CE = 6,        // logits tile: C = acc (bf16) and per-(row, n-tile) max / sum(exp(x - max))
+  EPI_ACT = 7,       // non-GLU MLP: H = acc (bf16), C = act(acc) (bf16); act in `act_kind`
 };
 
 template <int BN>
@@ -43,6 +49,7 @@ struct GemmSmem {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kEpiBytes = 4 * kStageBufs * kStageBox;
 };
 
 __device__ __forceinline__ int group_count(const GemmParams& p, int g) {
@@ -50,7 +57,7 @@ __device__ __forceinline__ int group_count(const GemmParams& p, int g) {
   return p.ragged == 2 ? p.K : p.M;
 }
 
-// Number of output tiles of group g.
+// Number of scheduled tiles (output tiles x K splits) of group g.
 template <int BN>
 __device__ __forceinline__ int group_tiles(const GemmParams& p, int g) {
   const int n_tiles = (p.N + BN - 1) / BN;
@@ -60,16 +67,15 @@ __device__ __forceinline__ int group_tiles(const GemmParams& p, int g) {
   }
   int m_tiles = (p.M + kBM - 1) / kBM;
   if (p.ragged == 2) return group_count(p, g) > 0 ? m_tiles * n_tiles : 0;
-  return m_tiles * n_tiles;
+  return m_tiles * n_tiles * max(p.ksplit, 1);
 }
 
 struct TileCoord {
-  int g, mt, nt, nkb;
+  int g, mt, nt, kb0, nkb;
 };
 
 template <int BN>
 __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, const int* prefix, int tile) {
-  // binary search: largest g with prefix[g] <= tile
   int lo = 0, hi = p.G - 1;
   while (lo < hi) {
     int mid = (lo + hi + 1) >> 1;
@@ -85,10 +91,20 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, const int*
   } else {
     m_tiles = (p.M + kBM - 1) / kBM;
   }
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const int kext = (p.ragged == 2) ? group_count(p, lo) : p.K;
+  const int nkb = (kext + kBK - 1) / kBK;
+  const int ks = (p.ragged == 0) ? max(p.ksplit, 1) : 1;
+  int split = 0;
+  if (ks > 1) {
+    split = local / (m_tiles * n_tiles);
+    local = local % (m_tiles * n_tiles);
+  }
   tc.mt = local % m_tiles;
   tc.nt = local / m_tiles;
-  int kext = (p.ragged == 2) ? group_count(p, lo) : p.K;
-  tc.nkb = (kext + kBK - 1) / kBK;
+  const int per = (nkb + ks - 1) / ks;
+  tc.kb0 = split * per;
+  tc.nkb = max(0, min(nkb, tc.kb0 + per) - tc.kb0);
   return tc;
 }
 
@@ -101,17 +117,76 @@ __device__ __forceinline__ float apply_act(float x, int kind) {
   return silu_f(x);
 }
 
+// Epilogue staging ring of one warp: 32-row x 64-byte boxes in 64B-swizzled smem (16-byte chunk k
+// of row r lives at chunk k ^ ((r >> 1) & 3)), written to global by TMA (only lane 0 issues and
+// tracks the bulk groups; the ring slot is warp-uniform).
+struct EpiRing {
+  uint8_t* base;
+  int slot;
+
+  __device__ __forceinline__ uint8_t* acquire(int lane) {
+    if (lane == 0) bulk_wait_read<kStageBufs - 1>();
+    __syncwarp();
+    return base + slot * kStageBox;
+  }
+  __device__ __forceinline__ static void put_row(uint8_t* buf, int r, uint4 c0, uint4 c1, uint4 c2, uint4 c3) {
+    const int sw = (r >> 1) & 3;
+    uint8_t* row = buf + r * 64;
+    *reinterpret_cast<uint4*>(row + ((0 ^ sw) << 4)) = c0;
+    *reinterpret_cast<uint4*>(row + ((1 ^ sw) << 4)) = c1;
+    *reinterpret_cast<uint4*>(row + ((2 ^ sw) << 4)) = c2;
+    *reinterpret_cast<uint4*>(row + ((3 ^ sw) << 4)) = c3;
+  }
+  __device__ __forceinline__ void issue(const CUtensorMap* tm, uint8_t* buf, int x, int y, bool reduce, int lane) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (reduce) tma_reduce_add_2d(tm, buf, x, y);
+      else tma_store_2d(tm, buf, x, y);
+      bulk_commit();
+    }
+    slot = (slot + 1) % kStageBufs;
+  }
+  // 32 fp32 values of this lane's row -> one bf16 box (32 columns) at (x, y)
+  __device__ __forceinline__ void bf16_box(const CUtensorMap* tm, const float (&v)[32], int x, int y, int lane) {
+    uint8_t* buf = acquire(lane);
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+    put_row(buf, lane, make_uint4(pk[0], pk[1], pk[2], pk[3]), make_uint4(pk[4], pk[5], pk[6], pk[7]),
+            make_uint4(pk[8], pk[9], pk[10], pk[11]), make_uint4(pk[12], pk[13], pk[14], pk[15]));
+    issue(tm, buf, x, y, false, lane);
+  }
+  // 32 fp32 values -> two fp32 boxes of 16 columns each (store, or reduce-add into C)
+  __device__ __forceinline__ void f32_boxes(const CUtensorMap* tm, const float (&v)[32], int x, int y, bool reduce,
+                                            int lane) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint8_t* buf = acquire(lane);
+      const float* w = v + 16 * h;
+      put_row(buf, lane,
+              make_uint4(__float_as_uint(w[0]), __float_as_uint(w[1]), __float_as_uint(w[2]), __float_as_uint(w[3])),
+              make_uint4(__float_as_uint(w[4]), __float_as_uint(w[5]), __float_as_uint(w[6]), __float_as_uint(w[7])),
+              make_uint4(__float_as_uint(w[8]), __float_as_uint(w[9]), __float_as_uint(w[10]), __float_as_uint(w[11])),
+              make_uint4(__float_as_uint(w[12]), __float_as_uint(w[13]), __float_as_uint(w[14]),
+                         __float_as_uint(w[15])));
+      issue(tm, buf, x + 16 * h, y, reduce, lane);
+    }
+  }
+};
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2,
                       const GemmParams p) {
   using S = GemmSmem<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // Align the dynamic smem base to 1024 B (required by the 128-B swizzle atoms).
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::kABytes;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
+  uint8_t* sEpi = smem + STAGES * S::kStageBytes;  // 1024-aligned (stage sizes are multiples of 1 KB)
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + S::kEpiBytes);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -125,7 +200,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
                                : (2 * BN <= 256) ? 256 : 512;
 
-  // Tile prefix sums over groups (every thread needs the schedule).
   if (threadIdx.x == 0) {
     int acc = 0;
     for (int g = 0; g < p.G; ++g) {
@@ -167,7 +241,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         TileCoord tc = decode_tile<BN>(p, prefix, tile);
         const int bgrp = p.b_mod ? tc.g % p.b_mod : tc.g;
-        for (int kb = 0; kb < tc.nkb; ++kb, ++it) {
+        for (int i = 0; i < tc.nkb; ++i, ++it) {
+          const int kb = tc.kb0 + i;
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutProducer, abort_flag)) { ok = false; break; }
@@ -206,14 +281,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int it = 0, tcount = 0;
       bool ok = true;
       bool issued = false;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++tcount) {
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         TileCoord tc = decode_tile<BN>(p, prefix, tile);
+        if (tc.nkb == 0) continue;  // (host never schedules empty splits; kept consistent anyway)
         const int buf = tcount & 1;
         const uint32_t tph = (tcount >> 1) & 1;
         if (!mbar_wait(&tempty_bar[buf], tph ^ 1, p.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = 0; kb < tc.nkb; ++kb, ++it) {
+        for (int i = 0; i < tc.nkb; ++i, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&full_bar[s], ph, p.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
@@ -227,13 +303,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             else adesc = make_sdesc(a_base + ks * 2048, kBK * 128, 1024);
             if constexpr (!B_MN) bdesc = make_sdesc(b_base + ks * 32, 16, 1024);
             else bdesc = make_sdesc(b_base + ks * 2048, kBK * 128, 1024);
-            umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | ks) != 0 ? 1u : 0u);
+            umma_bf16(d_tmem, adesc, bdesc, idesc, (i | ks) != 0 ? 1u : 0u);
           }
           issued = true;
           umma_commit(&empty_bar[s]);
         }
         if (!ok) break;
         umma_commit(&tfull_bar[buf]);
+        ++tcount;
       }
       if (!ok && issued) {
         // Drain: wait (bounded) until every MMA issued so far has completed before TMEM is freed.
@@ -245,19 +322,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------------ epilogue warps
     const int q = warp & 3;  // TMEM lane quadrant accessible by this warp
-    const int r_in_tile = q * 32 + lane;
+    EpiRing ring{sEpi + (warp - 2) * kStageBufs * kStageBox, 0};
+    const bool reduce = p.c_f32 && p.c_accum != 0;
     int tcount = 0;
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tcount) {
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
       TileCoord tc = decode_tile<BN>(p, prefix, tile);
+      if (tc.nkb == 0) continue;
       const int buf = tcount & 1;
       const uint32_t tph = (tcount >> 1) & 1;
+      ++tcount;
       const bool got = mbar_wait(&tfull_bar[buf], tph, p.err, kErrTimeoutEpilogue, abort_flag);
       if (!__all_sync(0xffffffffu, got)) break;  // keep the warp converged for tcgen05.ld
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
-      const int row = tc.mt * kBM + r_in_tile;
+      const int row = tc.mt * kBM + q * 32 + lane;
       const bool row_ok = row < p.M;
-      const long crow = (long)(p.c_mod ? tc.g % p.c_mod : tc.g) * p.c_grp + row;
+      const int y0 = (p.c_mod ? tc.g % p.c_mod : tc.g) * p.c_grp + tc.mt * kBM + q * 32;  // warp's first C row
+      const long crow = (long)y0 + lane;
       const int col0 = tc.nt * BN;
 
       if constexpr (EPI == EPI_SWIGLU) {
@@ -268,27 +349,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_ld32(taddr + c, gv);
           tmem_ld32(taddr + 128 + c, uv);
           tmem_wait_ld();
-          if (row_ok) {
-            __nv_bfloat16* H = reinterpret_cast<__nv_bfloat16*>(p.C) + crow * p.ldc + col0;
-            __nv_bfloat16* A2 = reinterpret_cast<__nv_bfloat16*>(p.C2) + crow * p.ldc2 + tc.nt * 128;
-            uint32_t hg[16], hu[16], ha[16];
+          float av[32];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              hg[i] = pack_bf16x2(gv[2 * i], gv[2 * i + 1]);
-              hu[i] = pack_bf16x2(uv[2 * i], uv[2 * i + 1]);
-              // activation from the bf16-rounded pre-activations so backward sees the same inputs
-              float2 g2 = unpack_bf16x2(hg[i]);
-              float2 u2 = unpack_bf16x2(hu[i]);
-              ha[i] = pack_bf16x2(silu_f(g2.x) * u2.x, silu_f(g2.y) * u2.y);
-            }
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              reinterpret_cast<uint4*>(H + c)[v] = make_uint4(hg[4 * v], hg[4 * v + 1], hg[4 * v + 2], hg[4 * v + 3]);
-              reinterpret_cast<uint4*>(H + 128 + c)[v] =
-                  make_uint4(hu[4 * v], hu[4 * v + 1], hu[4 * v + 2], hu[4 * v + 3]);
-              reinterpret_cast<uint4*>(A2 + c)[v] = make_uint4(ha[4 * v], ha[4 * v + 1], ha[4 * v + 2], ha[4 * v + 3]);
-            }
+          for (int i = 0; i < 32; ++i) {
+            // activation from the bf16-rounded pre-activations so backward sees the same inputs
+            const float g = __bfloat162float(__float2bfloat16(gv[i]));
+            const float u = __bfloat162float(__float2bfloat16(uv[i]));
+            av[i] = silu_f(g) * u;
           }
+          ring.bf16_box(&tmC, gv, col0 + c, y0, lane);
+          ring.bf16_box(&tmC, uv, col0 + 128 + c, y0, lane);
+          ring.bf16_box(&tmC2, av, tc.nt * 128 + c, y0, lane);
         }
       } else if constexpr (EPI == EPI_CE) {
         // Logits tile (bf16) plus per-row (max, sum exp(x - max)) over this tile's valid columns.
@@ -298,30 +369,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           float v[32];
           tmem_ld32(taddr + c, v);
           tmem_wait_ld();
-          uint32_t pk[16];
+          if (col0 + c >= p.N) continue;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+          for (int i = 0; i < 32; ++i) v[i] = __bfloat162float(__float2bfloat16(v[i]));
+          ring.bf16_box(&tmC, v, col0 + c, y0, lane);
           float cm = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float2 f = unpack_bf16x2(pk[i]);
-            v[2 * i] = (col0 + c + 2 * i < p.N) ? f.x : -INFINITY;
-            v[2 * i + 1] = (col0 + c + 2 * i + 1 < p.N) ? f.y : -INFINITY;
-            cm = fmaxf(cm, fmaxf(v[2 * i], v[2 * i + 1]));
+          for (int i = 0; i < 32; ++i) {
+            if (col0 + c + i >= p.N) v[i] = -INFINITY;
+            cm = fmaxf(cm, v[i]);
           }
-          float nm = fmaxf(m, cm);
+          const float nm = fmaxf(m, cm);
           if (nm > -INFINITY) {
             float acc = 0.f;
 #pragma unroll
             for (int i = 0; i < 32; ++i) acc += __expf(v[i] - nm);
             ssum = ssum * __expf(m - nm) + acc;
             m = nm;
-          }
-          if (row_ok && col0 + c < p.N) {
-            __nv_bfloat16* Cp = reinterpret_cast<__nv_bfloat16*>(p.C) + crow * p.ldc + col0 + c;
-#pragma unroll
-            for (int vv = 0; vv < 4; ++vv)
-              reinterpret_cast<uint4*>(Cp)[vv] = make_uint4(pk[4 * vv], pk[4 * vv + 1], pk[4 * vv + 2], pk[4 * vv + 3]);
           }
         }
         if (row_ok) {
@@ -336,91 +400,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_ld32(taddr + c, v);
           tmem_wait_ld();
           const int col = col0 + c;
-          if (!row_ok || col >= p.N) continue;
+          if (col >= p.N) continue;  // warp-uniform; the box would be clipped anyway
+          float o[32];
           if constexpr (EPI == EPI_STORE) {
-            if (p.c_f32) {
-              float* Cp = reinterpret_cast<float*>(p.C) + crow * p.ldc + col;
-              if (p.c_accum == 2) {
 #pragma unroll
-                for (int vv = 0; vv < 8; ++vv)
-                  atomicAdd(reinterpret_cast<float4*>(Cp) + vv,
-                            make_float4(p.alpha * v[4 * vv], p.alpha * v[4 * vv + 1], p.alpha * v[4 * vv + 2],
-                                        p.alpha * v[4 * vv + 3]));
-              } else if (p.c_accum) {
+            for (int i = 0; i < 32; ++i) o[i] = p.alpha * v[i];
+          } else if constexpr (EPI == EPI_RESID || EPI == EPI_GATE_MUL) {
+            float r[32];
+            if (row_ok) {
+              const uint4* Rp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.R) +
+                                                               crow * p.ldr + col);
 #pragma unroll
-                for (int vv = 0; vv < 8; ++vv) {
-                  float4 o = reinterpret_cast<float4*>(Cp)[vv];
-                  o.x += p.alpha * v[4 * vv];
-                  o.y += p.alpha * v[4 * vv + 1];
-                  o.z += p.alpha * v[4 * vv + 2];
-                  o.w += p.alpha * v[4 * vv + 3];
-                  reinterpret_cast<float4*>(Cp)[vv] = o;
+              for (int vv = 0; vv < 4; ++vv) {
+                const uint4 u = Rp[vv];
+                const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const float2 f = unpack_bf16x2(w4[k]);
+                  r[vv * 8 + 2 * k] = f.x;
+                  r[vv * 8 + 2 * k + 1] = f.y;
                 }
-              } else {
-#pragma unroll
-                for (int vv = 0; vv < 8; ++vv)
-                  reinterpret_cast<float4*>(Cp)[vv] = make_float4(p.alpha * v[4 * vv], p.alpha * v[4 * vv + 1],
-                                                                  p.alpha * v[4 * vv + 2], p.alpha * v[4 * vv + 3]);
               }
             } else {
-              __nv_bfloat16* Cp = reinterpret_cast<__nv_bfloat16*>(p.C) + crow * p.ldc + col;
-              uint32_t pk[16];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(p.alpha * v[2 * i], p.alpha * v[2 * i + 1]);
-#pragma unroll
-              for (int vv = 0; vv < 4; ++vv)
-                reinterpret_cast<uint4*>(Cp)[vv] = make_uint4(pk[4 * vv], pk[4 * vv + 1], pk[4 * vv + 2], pk[4 * vv + 3]);
-            }
-          } else if constexpr (EPI == EPI_RESID || EPI == EPI_GATE_MUL) {
-            const __nv_bfloat16* Rp = reinterpret_cast<const __nv_bfloat16*>(p.R) + crow * p.ldr + col;
-            __nv_bfloat16* Cp = reinterpret_cast<__nv_bfloat16*>(p.C) + crow * p.ldc + col;
-            uint4 rv[4];
-#pragma unroll
-            for (int vv = 0; vv < 4; ++vv) rv[vv] = reinterpret_cast<const uint4*>(Rp)[vv];
-            const uint32_t* ru = reinterpret_cast<const uint32_t*>(rv);
-            uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              float2 r2 = unpack_bf16x2(ru[i]);
-              if constexpr (EPI == EPI_RESID)
-                pk[i] = pack_bf16x2(v[2 * i] + r2.x, v[2 * i + 1] + r2.y);
-              else
-                pk[i] = pack_bf16x2(r2.x * sigmoid_f(v[2 * i]), r2.y * sigmoid_f(v[2 * i + 1]));
+              for (int i = 0; i < 32; ++i) r[i] = 0.f;
             }
 #pragma unroll
-            for (int vv = 0; vv < 4; ++vv)
-              reinterpret_cast<uint4*>(Cp)[vv] = make_uint4(pk[4 * vv], pk[4 * vv + 1], pk[4 * vv + 2], pk[4 * vv + 3]);
+            for (int i = 0; i < 32; ++i) o[i] = (EPI == EPI_RESID) ? v[i] + r[i] : r[i] * sigmoid_f(v[i]);
           } else if constexpr (EPI == EPI_SILU || EPI == EPI_ACT) {
-            __nv_bfloat16* Cp = reinterpret_cast<__nv_bfloat16*>(p.C) + crow * p.ldc + col;
-            __nv_bfloat16* Hp = reinterpret_cast<__nv_bfloat16*>(p.C2) + crow * p.ldc2 + col;
-            uint32_t ph[16], pa[16];
+            const int kind = (EPI == EPI_SILU) ? 0 : p.act_kind;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              ph[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-              float2 h2 = unpack_bf16x2(ph[i]);
-              const int kind = (EPI == EPI_SILU) ? 0 : p.act_kind;
-              pa[i] = pack_bf16x2(apply_act(h2.x, kind), apply_act(h2.y, kind));
-            }
-#pragma unroll
-            for (int vv = 0; vv < 4; ++vv) {
-              reinterpret_cast<uint4*>(Cp)[vv] = make_uint4(pa[4 * vv], pa[4 * vv + 1], pa[4 * vv + 2], pa[4 * vv + 3]);
-              reinterpret_cast<uint4*>(Hp)[vv] = make_uint4(ph[4 * vv], ph[4 * vv + 1], ph[4 * vv + 2], ph[4 * vv + 3]);
-            }
+            for (int i = 0; i < 32; ++i) o[i] = apply_act(__bfloat162float(__float2bfloat16(v[i])), kind);
           } else if constexpr (EPI == EPI_ROWSCALE) {
-            const float sc = p.row_scale[crow];
-            __nv_bfloat16* Cp = reinterpret_cast<__nv_bfloat16*>(p.C) + crow * p.ldc + col;
-            uint32_t pk[16];
+            const float sc = row_ok ? p.row_scale[crow] : 0.f;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(sc * v[2 * i], sc * v[2 * i + 1]);
-#pragma unroll
-            for (int vv = 0; vv < 4; ++vv)
-              reinterpret_cast<uint4*>(Cp)[vv] = make_uint4(pk[4 * vv], pk[4 * vv + 1], pk[4 * vv + 2], pk[4 * vv + 3]);
+            for (int i = 0; i < 32; ++i) o[i] = sc * v[i];
           }
+          if (p.c_f32) ring.f32_boxes(&tmC, o, col, y0, reduce, lane);
+          else ring.bf16_box(&tmC, o, col, y0, lane);
+          if constexpr (EPI == EPI_SILU || EPI == EPI_ACT) ring.bf16_box(&tmC2, v, col, y0, lane);
         }
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[buf]);
     }
+    if (lane == 0) bulk_wait_all();  // every TMA store / reduce of this warp has landed
   }
 
   tc_fence_before();
@@ -433,8 +457,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 template <int BN, int STAGES>
 constexpr int gemm_smem_bytes() {
-  // stages + barriers/scalars + prefix table + 1 KB alignment slack
-  return STAGES * GemmSmem<BN>::kStageBytes + 1024 + (kMaxGroups + 1) * 4 + 256;
+  // stages + epilogue staging + 1 KB alignment slack + barriers/scalars + tile prefix table
+  return STAGES * GemmSmem<BN>::kStageBytes + GemmSmem<BN>::kEpiBytes + 1024 + 256 + (kMaxGroups + 1) * 4;
 }
 
 }  // namespace mxk

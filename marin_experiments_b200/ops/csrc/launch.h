@@ -17,6 +17,9 @@ struct GemmLaunch {
   int b_mn;
   int bn;
   int epi;
+  // output tensor maps: C [c_rows, c_cols] (row stride p.ldc), C2 [c2_rows, c2_cols] (p.ldc2)
+  int64_t c_rows, c_cols, c2_rows, c2_cols;
+  int c2_f32;
   GemmParams p;
 };
 
