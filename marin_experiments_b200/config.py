@@ -111,6 +111,12 @@ class GrugModelConfig:
                 raise ValueError("min_experts_per_token must be <= num_experts_per_token (the K_max capacity)")
         if self.shared_expert_intermediate_dim < 0:
             raise ValueError("shared_expert_intermediate_dim must be non-negative")
+        if self.glu:
+            # gate/up weights are stored interleaved in 128-row blocks (SwiGLU in the GEMM epilogue)
+            for name in ("intermediate_dim", "shared_expert_intermediate_dim"):
+                v = getattr(self, name)
+                if v % 128:
+                    raise ValueError(f"{name}={v} must be a multiple of 128 for a GLU MLP")
 
     @property
     def is_moe(self) -> bool:
