@@ -522,5 +522,30 @@ def set_loss_grad_scale(scale: float) -> None:
     _CE_GRAD_SCALE[0] = float(scale)
 
 
+@torch.no_grad()
+def _ce_loss_only(h, w, labels, weights, z_weight, chunk):
+    """Evaluation path: the same fused GEMM + softmax epilogue, no gradient GEMMs (and no write
+    into the weight's ``main_grad``)."""
+    h = _c(h)
+    t, _ = h.shape
+    v = w.shape[0]
+    nt = (v + 255) // 256
+    labels = _c(labels.long())
+    weights = _c(weights.float())
+    wsum = weights.sum().reshape(1)
+    loss = torch.zeros(1, dtype=F32, device=h.device)
+    tc = min(chunk, t)
+    logits = torch.empty(tc, nt * 256, dtype=BF16, device=h.device)
+    stats = torch.empty(tc, 2 * nt, dtype=F32, device=h.device)
+    for c0 in range(0, t, tc):
+        n = min(tc, t - c0)
+        G.gemm(h[c0:c0 + n], w, logits[:n], M=n, N=v, K=h.shape[1], epi="ce", c2=stats[:n])
+        ext().ce_grad(logits[:n], stats[:n], labels[c0:c0 + n], weights[c0:c0 + n], wsum, loss, None, v,
+                      float(z_weight), 1.0)
+    return (loss / wsum.clamp_min(1.0)).reshape(())
+
+
 def cross_entropy(h, w_out, labels, weights, z_weight, chunk: int = 8192):
+    if not torch.is_grad_enabled() or not (h.requires_grad or w_out.requires_grad):
+        return _ce_loss_only(h, w_out, labels, weights, z_weight, chunk)
     return _CrossEntropy.apply(h, w_out, labels, weights, float(z_weight), _CE_GRAD_SCALE[0], chunk)

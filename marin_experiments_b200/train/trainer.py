@@ -138,13 +138,15 @@ class Trainer:
         return metrics
 
     # ------------------------------------------------------------------------------ loop
-    def fit(self, loader, num_steps: int, *, hooks=(), log_every: int = 1, checkpointer=None, tracker=None,
-            stop_on_nan: bool = True):
+    def fit(self, loader, num_steps: int, *, hooks=(), pre_hooks=(), log_every: int = 1, checkpointer=None,
+            tracker=None, stop_on_nan: bool = True):
         """Hot loop: batch -> step -> host read of the loss -> NaN stop -> hooks/tracker ->
         checkpoint (megagpt-speedrun/train.py:705-762)."""
         it = iter(loader)
         last = None
         while self.step < num_steps:
+            for h in pre_hooks:
+                h.before_step(self)
             t0 = time.perf_counter()
             batch = next(it)
             t_load = time.perf_counter() - t0
@@ -154,7 +156,9 @@ class Trainer:
             if stop_on_nan and not math.isfinite(loss):
                 raise FloatingPointError(f"loss is {loss} at step {self.step}")
             info = {"step": self.step, "loss": loss, "step_duration": dt, "loading_time": t_load,
-                    "tokens": int(batch["tokens"].numel()), "metrics": met}
+                    "tokens": int(batch["tokens"].numel()) * (self.dist.world if self.dist else 1),
+                    "batch_size": int(batch["tokens"].shape[0]) * (self.dist.world if self.dist else 1),
+                    "metrics": met}
             for h in hooks:
                 h(self, info)
             if tracker is not None and self.step % log_every == 0:

@@ -1,0 +1,82 @@
+"""Launchers: the tiny-stories corpus -> tokenize -> train -> checkpoint pipeline end to end on CPU,
+resume from its checkpoint, the megagpt environment arms, the heuristic and FLOP accounting."""
+
+import json
+import math
+import os
+
+import pytest
+
+from marin_experiments_b200.experiments import megagpt, tiny_stories
+from marin_experiments_b200.executor import Executor
+
+
+def test_tiny_stories_pipeline(tmp_path, capsys):
+    steps = tiny_stories.build_steps(steps=3, batch_size=4)
+    res = Executor(str(tmp_path)).run(steps)
+    out = capsys.readouterr().out
+    assert out.count("[THRUPUT] step=") == 3
+    train_dir = res["tiny-stories/tinystories-30m"]
+    ck = os.path.join(train_dir, "checkpoints", "step-3", "metadata.json")
+    assert json.load(open(ck))["step"] == 3
+    metrics = [json.loads(l) for l in open(os.path.join(train_dir, "logs", "tiny-stories-30m-cpu", "metrics.jsonl"))]
+    assert [m["step"] for m in metrics] == [1, 2, 3] and all(math.isfinite(m["train/loss"]) for m in metrics)
+    # a rerun of the same versions is skipped; the trainer itself resumes from its checkpoint
+    from marin_experiments_b200.experiments.common import run_inline
+    launch = Executor(str(tmp_path)).instantiate(steps[2])
+    import dataclasses
+    r = run_inline(dataclasses.replace(launch, steps=4))
+    assert r["restored_from"].endswith("step-3") and r["start_step"] == 3 and r["final_step"] == 4
+
+
+def test_megagpt_arms():
+    env = {"SP_HIDDEN": "1536", "SP_EXPERTS": "64", "SP_TOPK": "4", "SP_SEQ": "2048", "SP_EP": "8",
+           "SP_BATCH": "256", "SP_STEPS": "10", "SP_SCHEDULE": "constant", "SP_GLOBAL_EVERY": "6"}
+    launch, arm = megagpt.make_launch(env)
+    m = launch.model.value
+    assert (m.hidden_dim, m.num_experts, m.num_experts_per_token, m.intermediate_dim, m.max_seq_len) == \
+        (1536, 64, 4, 768, 2048)
+    assert m.global_attn_every == 6 and launch.grug_trainer.value.expert_axis_size == 8
+    assert launch.optimizer.value.lr_schedule == "constant"
+    assert launch.batch_size.value == 256 and launch.steps.value == 10
+    from marin_experiments_b200.utils.tracker import THRU  # noqa: F401
+    import re
+    arm_re = re.compile(r"\[arm\].*?D=(\d+).*?seq=(\d+).*?E=(\d+) k=(\d+).*?batch=(\d+).*?budget=([\d.eE+]+)")
+    g = arm_re.search(arm).groups()
+    assert g[:5] == ("1536", "2048", "64", "4", "256")
+    with pytest.raises(ValueError):
+        megagpt.make_launch({"SPARSITY_MODE": "weird"})
+    adaptive, _ = megagpt.make_launch({"SPARSITY_MODE": "adaptive", "SP_MIN_K": "1", "SP_COEF": "0.01",
+                                       "SP_HIDDEN": "512", "SP_EXPERTS": "32", "SP_TOPK": "8"})
+    assert adaptive.model.value.adaptive_routing and adaptive.model.value.sparsity_loss_coef == 0.01
+
+
+def test_heuristic_values():
+    from marin_experiments_b200.optim.heuristic import MoeAdamHHeuristic, build_from_heuristic, compute_tokens_and_batch
+
+    h = MoeAdamHHeuristic()
+    assert h.num_layers(1024) == round(1024 / (64 + 40 - 9))
+    assert h.kv_heads(16, 4) == 4 and h.kv_heads(12, 4) == 3 and h.kv_heads(6, 4) == 1
+    assert h.beta2(131072) == pytest.approx(0.999)
+    assert h.beta2(10 ** 9) == 0.95
+    tok, b, s = compute_tokens_and_batch(3e18, 1e9, target_steps=1000, seq_len=4096)
+    assert tok == pytest.approx(1e9) and b == 256 and s == round(1e9 / (256 * 4096))
+    m, o, b, s = build_from_heuristic(budget=1e18, hidden_dim=1024, batch_size=48)
+    assert b == 48 and o.learning_rate == pytest.approx(min(0.05, 13 / 3 * o.adam_lr))
+
+
+def test_flop_accounting():
+    from marin_experiments_b200.config import GrugModelConfig
+    from marin_experiments_b200.utils.flops import (compute_flops_per_token, fwd_components, lm_flops_per_token,
+                                                    training_flops_per_token)
+
+    c = GrugModelConfig(vocab_size=1000, hidden_dim=256, intermediate_dim=128, shared_expert_intermediate_dim=256,
+                        num_experts=8, num_experts_per_token=2, num_layers=2, num_heads=4, num_kv_heads=2,
+                        head_dim=64, max_seq_len=128)
+    f = fwd_components(c)
+    assert f["routed_experts"] == 2 * (2 * 3 * 256 * 128 * 2)
+    assert f["router_proj"] == 2 * 2 * 256 * 8
+    assert f["lm_head"] == 2 * 256 * 1000
+    assert f["gated_norms"] == 2 * 2 * (2 * 2 * 256 * 128) + 2 * (2 * 2 * 256 * 128)
+    assert compute_flops_per_token(c) == lm_flops_per_token(c) - 2 * 256 * 1000
+    assert training_flops_per_token(c, causal=False) == 3 * f["_total"]

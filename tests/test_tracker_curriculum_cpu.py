@@ -1,0 +1,63 @@
+"""Throughput lines and their monitor parser, the JSONL tracker, the step watchdog, and the
+active-expert curriculum."""
+
+import io
+import json
+import time
+
+import torch
+
+from marin_experiments_b200.config import GrugModelConfig
+from marin_experiments_b200.train.curriculum import active_k_at, parse_curriculum, set_active_k
+from marin_experiments_b200.utils.tracker import JsonlTracker, ThroughputHook, Watchdog, parse_thruput
+
+CFG = GrugModelConfig(vocab_size=512, hidden_dim=64, intermediate_dim=128, shared_expert_intermediate_dim=128,
+                      num_experts=8, num_experts_per_token=2, num_layers=2, num_heads=2, num_kv_heads=2, head_dim=32,
+                      max_seq_len=64, sliding_window=64)
+
+
+def test_thruput_roundtrip():
+    buf = io.StringIO()
+    hook = ThroughputHook(CFG, n_gpus=1, stream=buf)
+    for s in range(1, 11):
+        hook(None, {"step": s, "step_duration": 0.5, "tokens": 1000, "batch_size": 4})
+    r = parse_thruput(buf.getvalue(), warmup=5)
+    assert r["n"] == 6 and r["tok_s"] == 2000.0 and r["mfu"] is not None
+
+
+def test_jsonl_tracker(tmp_path):
+    t = JsonlTracker(str(tmp_path), "run", {"a": 1})
+    t.log({"loss": torch.tensor(2.5)}, step=3)
+    t.log_summary({"final": 1})
+    t.finish()
+    line = json.loads(open(tmp_path / "run" / "metrics.jsonl").read().splitlines()[0])
+    assert line == {"step": 3, "loss": 2.5}
+
+
+def test_watchdog_fires_and_kicks():
+    fired = []
+    wd = Watchdog(0.2, on_timeout=fired.append, poll_s=0.02, stream=io.StringIO()).start()
+    for _ in range(10):
+        time.sleep(0.05)
+        wd.kick()
+    assert not fired
+    time.sleep(0.5)
+    wd.stop()
+    assert fired and fired[0] >= 0.2
+
+
+def test_curriculum_schedule_and_swap():
+    sched = parse_curriculum("1:0.25,2:0.25,4:0.5", 100)
+    assert sched == ((1, 25), (2, 50), (4, 100))
+    assert [active_k_at(sched, s) for s in (0, 24, 25, 60, 150)] == [1, 1, 2, 4, 4]
+    from marin_experiments_b200.models.grug import Transformer
+
+    m = Transformer(CFG)
+    m.init_weights(0)
+    assert set_active_k(m, 4)
+    ks = {mod.cfg.num_experts_per_token for mod in m.modules() if getattr(mod, "cfg", None) is not None}
+    assert ks == {4}
+    assert not set_active_k(m, 4)
+    tok = torch.randint(0, 512, (2, 64))
+    loss, met = m.next_token_loss(tok)
+    assert torch.isfinite(loss)
