@@ -211,6 +211,14 @@ class Transformer(nn.Module):
             self.head_down = nn.Parameter(torch.empty(de, d)) if cfg.is_factorized_embed else None
             self.output_proj = None if cfg.tie_embeddings else nn.Parameter(torch.empty(v, de))
 
+    def global_name(self, name: str) -> str:
+        """Parameter name in the full model: a pipeline stage's ``blocks.<j>`` is layer
+        ``layer_ids[j]``, so seeds and checkpoint paths agree with the unsplit model."""
+        if name.startswith("blocks."):
+            j, rest = name[len("blocks."):].split(".", 1)
+            return f"blocks.{self.layer_ids[int(j)]}.{rest}"
+        return name
+
     # ------------------------------------------------------------------------------ init
     def init_weights(self, seed: int = 0):
         """Truncated-normal init with std ``initializer_std``; norms at 1, gates/biases at 0."""
@@ -342,6 +350,7 @@ def init_store_weights(store, cfg: GrugModelConfig, seed: int = 0, model: Transf
     same model would have on one GPU."""
     std = cfg.initializer_std
     ranges = {}
+    gname = model.global_name if model is not None and hasattr(model, "global_name") else (lambda n: n)
     if model is not None:
         for mname, mod in model.named_modules():
             if isinstance(mod, MoEMLP):
@@ -359,9 +368,9 @@ def init_store_weights(store, cfg: GrugModelConfig, seed: int = 0, model: Transf
             elif info.ndim == 3:
                 lo = ranges.get(info.name.rsplit(".", 1)[0], (0, info.shape[0]))[0]
                 for j in range(info.shape[0]):
-                    gen = torch.Generator(device=store.device).manual_seed(_seed_for(seed, info.name, lo + j))
+                    gen = torch.Generator(device=store.device).manual_seed(_seed_for(seed, gname(info.name), lo + j))
                     trunc_normal_(v[j], std, gen)
             else:
-                gen = torch.Generator(device=store.device).manual_seed(_seed_for(seed, info.name))
+                gen = torch.Generator(device=store.device).manual_seed(_seed_for(seed, gname(info.name)))
                 trunc_normal_(v, std, gen)
     store.sync_compute()

@@ -248,17 +248,23 @@ class _AttentionBlock(torch.autograd.Function):
         W = ctx.W
         dh = torch.empty(t, d, dtype=BF16, device=h.device)
         G.gemm(dqkvg, W, dh, b_mn=True, M=t, N=d, K=ld)
+        n_rows = ctx.n
         if ctx.split is None:
             wg = getattr(ctx.w_qkv, "_qkvg_grad", None)
             if wg is None:
                 wg = _mg(ctx.w_qkv)
-            G.gemm(dqkvg, h, wg, a_mn=True, b_mn=True, M=ctx.n, N=d, K=t, accum=True)
+            G.weight_grad(lambda: G.gemm(dqkvg, h, wg, a_mn=True, b_mn=True, M=n_rows, N=d, K=t, accum=True))
         else:
-            tmp = torch.zeros(ctx.n, d, dtype=F32, device=h.device)
-            G.gemm(dqkvg, h, tmp, a_mn=True, b_mn=True, M=ctx.n, N=d, K=t, accum=True)
             r0 = ctx.split[0]
-            _mg(ctx.w_qkv).add_(tmp[:r0])
-            _mg(ctx.attn_gate).add_(tmp[r0:])
+            gq, gg = _mg(ctx.w_qkv), _mg(ctx.attn_gate)
+
+            def _dw_split():
+                tmp = torch.zeros(n_rows, d, dtype=F32, device=h.device)
+                G.gemm(dqkvg, h, tmp, a_mn=True, b_mn=True, M=n_rows, N=d, K=t, accum=True)
+                gq.add_(tmp[:r0])
+                gg.add_(tmp[r0:])
+
+            G.weight_grad(_dw_split)
         ctx.W = ctx.w_qkv = ctx.attn_gate = ctx.w_o = None
         return dh, dout, None, None, None, None, None
 
@@ -378,7 +384,8 @@ class _Router(torch.autograd.Function):
                          ctx.k_min, ctx.temp, dlog, dtheta)
         dh = torch.empty(t, d, dtype=BF16, device=dev)
         G.gemm(dlog, ctx.w_router, dh, b_mn=True, M=t, N=d, K=ldd)
-        G.gemm(dlog, h, _mg(ctx.w_router), a_mn=True, b_mn=True, M=e, N=d, K=t, accum=True)
+        gr = _mg(ctx.w_router)
+        G.weight_grad(lambda: G.gemm(dlog, h, gr, a_mn=True, b_mn=True, M=e, N=d, K=t, accum=True))
         if ctx.adaptive and ctx.theta is not None:
             _mg(ctx.theta).add_(dtheta.reshape(_mg(ctx.theta).shape))
         ctx.w_router = ctx.theta = None

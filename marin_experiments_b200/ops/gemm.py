@@ -11,6 +11,9 @@ operand is passed as stored (``[rows, K]``); an MN-major operand is passed as it
 
 from __future__ import annotations
 
+import contextlib
+import threading
+
 import torch
 
 from ._ext import err_flag, ext
@@ -59,12 +62,50 @@ def linear_dx(dy, w, *, out=None, accum=False):
     return gemm(dy, w, out, b_mn=True, M=m, N=k, K=n, accum=accum)
 
 
+class _WeightGradQueue(threading.local):
+    def __init__(self):
+        self.queue = None
+
+
+_WGQ = _WeightGradQueue()
+
+
+@contextlib.contextmanager
+def defer_weight_grads(queue: list):
+    """Within this context, backward passes queue their weight-gradient GEMMs (the ones that
+    accumulate into a parameter's ``main_grad``) on ``queue`` instead of launching them, so a
+    zero-bubble pipeline schedule can run the input-gradient pass (B) now and the weight-gradient
+    pass (W) later: ``run_weight_grads(queue)``."""
+    prev = _WGQ.queue
+    _WGQ.queue = queue
+    try:
+        yield queue
+    finally:
+        _WGQ.queue = prev
+
+
+def run_weight_grads(queue: list) -> None:
+    while queue:
+        queue.pop(0)()
+
+
+def weight_grad(fn) -> None:
+    """Run ``fn`` (a weight-gradient accumulation) now, or queue it inside ``defer_weight_grads``."""
+    if _WGQ.queue is not None:
+        _WGQ.queue.append(fn)
+    else:
+        fn()
+
+
 def linear_dw(dy, x, *, out=None, accum=False, alpha=1.0):
     """``dy [T, N]^T @ x [T, K]`` -> ``[N, K]`` (fp32 when accumulating into a main grad)."""
     t, n = dy.shape
     k = x.shape[1]
     if out is None:
         out = torch.empty(n, k, dtype=torch.float32, device=dy.device)
+    if accum:
+        weight_grad(lambda: gemm(dy, x, out, a_mn=True, b_mn=True, M=n, N=k, K=t, accum=accum, alpha=alpha))
+        return out
     return gemm(dy, x, out, a_mn=True, b_mn=True, M=n, N=k, K=t, accum=accum, alpha=alpha)
 
 
@@ -108,5 +149,7 @@ def grouped_linear_dw(dy, x, counts, *, out, accum=True, alpha=1.0, n_w=None):
     n = dy.shape[1]
     k = x.shape[1]
     shared = n_w != g
-    return gemm(dy, x, out, a_mn=True, b_mn=True, G=g, M=n, N=k, K=cap, counts=counts, ragged=2, a_grp=cap,
-                b_grp=cap, c_grp=n, accum=(2 if shared else accum), alpha=alpha, c_mod=n_w if shared else 0)
+    weight_grad(lambda: gemm(dy, x, out, a_mn=True, b_mn=True, G=g, M=n, N=k, K=cap, counts=counts, ragged=2,
+                             a_grp=cap, b_grp=cap, c_grp=n, accum=(2 if shared else accum), alpha=alpha,
+                             c_mod=n_w if shared else 0))
+    return out

@@ -46,9 +46,10 @@ class DistContext:
         # replicated parameters start identical on every rank
         st = trainer.store
         if self.world > 1:
+            src = torch_dist.get_global_rank(self.batch_group, 0) if self.batch_group is not None else 0
             for info in st.infos:
                 if info.sharded_over is None:
-                    torch_dist.broadcast(st.master_view(info), src=0, group=self.batch_group)
+                    torch_dist.broadcast(st.master_view(info), src=src, group=self.batch_group)
             st.sync_compute()
         self._replicated = [i for i in st.infos if i.sharded_over is None and i.trainable]
         self._sharded = [i for i in st.infos if i.sharded_over is not None and i.trainable]

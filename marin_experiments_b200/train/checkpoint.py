@@ -109,6 +109,7 @@ def load_scalar_state(trainer, st: dict) -> None:
 
 def _leaves(trainer, buffers: dict[str, torch.Tensor], ep_size: int, ep_rank: int) -> list[_Leaf]:
     out = []
+    gname = getattr(trainer.model, "global_name", lambda n: n)
     for prefix, buf in buffers.items():
         for info in trainer.store.infos:
             sharded = info.sharded_over == "expert" and ep_size > 1
@@ -118,7 +119,7 @@ def _leaves(trainer, buffers: dict[str, torch.Tensor], ep_size: int, ep_rank: in
                 e_loc = info.shape[0]
                 gshape = (e_loc * ep_size,) + tuple(info.shape[1:])
                 start = ep_rank * e_loc
-            out.append(_Leaf(f"{prefix}/{_leaf_path(info.name)}", buf, info.offset, info.numel, tuple(info.shape),
+            out.append(_Leaf(f"{prefix}/{_leaf_path(gname(info.name))}", buf, info.offset, info.numel, tuple(info.shape),
                              gshape, start, sharded))
     return out
 

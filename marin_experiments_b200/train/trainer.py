@@ -35,7 +35,8 @@ def num_moe_layers(model: Transformer) -> int:
 
 class Trainer:
     def __init__(self, cfg: GrugRunConfig, *, device: str | torch.device | None = None, micro_batch: int | None = None,
-                 num_train_steps: int | None = None, dist=None, build_model: bool = True, seed: int | None = None):
+                 num_train_steps: int | None = None, dist=None, build_model: bool = True, seed: int | None = None,
+                 model_kwargs: dict | None = None):
         self.cfg = cfg
         self.mcfg: GrugModelConfig = cfg.model
         if device is None:
@@ -48,6 +49,7 @@ class Trainer:
         self.seed = cfg.trainer.trainer.seed if seed is None else seed
         self.z_loss_weight = cfg.trainer.z_loss_weight
         self.ema_beta = cfg.trainer.ema_beta
+        self.model_kwargs = dict(model_kwargs or {})
         if build_model:
             self._build()
 
@@ -58,7 +60,7 @@ class Trainer:
         if self.dist is not None and self.dist.ep_size > 1 and cfg.is_moe:
             local = self.dist.local_expert_range(cfg.num_experts)
         with torch.device("meta"):
-            model = Transformer(cfg, local_experts=local)
+            model = Transformer(cfg, local_experts=local, **self.model_kwargs)
         self.model = model
         self.store = ParamStore(model, self.device)
         init_store_weights(self.store, cfg, self.seed, model)

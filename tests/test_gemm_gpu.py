@@ -120,3 +120,28 @@ def test_ce_epilogue(G):
     gmax = mx.max(1, keepdim=True).values
     lse = gmax.squeeze(1) + torch.log((se * torch.exp(mx - gmax)).sum(1))
     assert torch.allclose(lse, torch.logsumexp(ref, 1), atol=5e-2, rtol=1e-3)
+
+
+def test_deferred_weight_grads_match():
+    """Zero-bubble B/W split: inside defer_weight_grads the weight-gradient GEMMs are queued, the
+    input gradient is complete, and running the queue later gives the same main_grad."""
+    from marin_experiments_b200.ops import cuda_fns
+    from marin_experiments_b200.ops import gemm as G
+
+    torch.manual_seed(0)
+    x = torch.randn(256, 512, device="cuda", dtype=torch.bfloat16)
+    w = torch.nn.Parameter(torch.randn(384, 512, device="cuda", dtype=torch.bfloat16) / 16)
+    w.main_grad = torch.zeros(384, 512, device="cuda")
+    g = torch.randn(256, 384, device="cuda", dtype=torch.bfloat16)
+    xa = x.clone().requires_grad_(True)
+    cuda_fns.linear(xa, w).backward(g)
+    ref_dx, ref_dw = xa.grad.clone(), w.main_grad.clone()
+    w.main_grad.zero_()
+    xb = x.clone().requires_grad_(True)
+    q = []
+    with G.defer_weight_grads(q):
+        cuda_fns.linear(xb, w).backward(g)
+    assert len(q) == 1 and float(w.main_grad.abs().sum()) == 0.0
+    assert torch.equal(xb.grad, ref_dx)
+    G.run_weight_grads(q)
+    assert torch.equal(w.main_grad, ref_dw)

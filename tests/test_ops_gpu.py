@@ -213,6 +213,12 @@ def test_cross_entropy():
     assert abs(lg.item() - lc.item()) < 2e-3 * lc.item()
     assert rel(hg.grad, hc.grad) < 3e-2
     assert rel(wg.main_grad, wc.grad) < 3e-2
+    # evaluation path: same loss, and the weight's main_grad is left alone
+    before = wg.main_grad.clone()
+    with torch.no_grad():
+        le = cuda_fns.cross_entropy(hg, wg, labels.cuda(), wts.cuda(), 1e-4, chunk=256)
+    assert abs(le.item() - lg.item()) < 1e-4 * lg.item()
+    assert torch.equal(wg.main_grad, before)
 
 
 def test_embed():
