@@ -66,7 +66,7 @@ void launch_unpermute_add(const void* dxp, const int* sel, const int* slot, cons
 // optim.cu
 void launch_opt_sqnorm(const void* chunks, int nchunks, const float* grad, float scale, double* out, cudaStream_t st);
 void launch_opt_step(const void* chunks, int nchunks, const float* hp, const double* gnorm2, float gscale,
-                     const float* grad, float* m, float* v, float* p, void* pb, double* mat_sums, int has_adamh,
+                     const float* grad, float* m, float* v, float* p, void* pb, double* mat_sums, int has_adamh, int phase,
                      cudaStream_t st);
 void launch_ema(float* dst, const float* src, long n, float beta, cudaStream_t st);
 void launch_cast_bf16(const float* src, void* dst, long n, cudaStream_t st);

@@ -294,12 +294,16 @@ void opt_sqnorm(const Tensor& chunks, int64_t nchunks, const Tensor& grad, doubl
 
 void opt_step(const Tensor& chunks, int64_t nchunks, const Tensor& hp, const OptT& gnorm2, double gscale,
               const Tensor& grad, const Tensor& m, const Tensor& v, const Tensor& p, const OptT& pb,
-              const Tensor& mat_sums, bool has_adamh) {
+              const Tensor& mat_sums, bool has_adamh, int64_t mv_offset, int64_t phase) {
+  // m and v may hold only the flat range [mv_offset, mv_offset + numel) of a sharded optimizer; the
+  // chunk table addresses global offsets inside that range.
   cuda_f32(grad, "grad"); cuda_f32(m, "m"); cuda_f32(v, "v"); cuda_f32(p, "p");
+  need(m.numel() == v.numel() && mv_offset >= 0 && mv_offset + m.numel() <= p.numel(), "bad moment shard");
   c10::cuda::CUDAGuard g(grad.device());
   mxk::launch_opt_step(chunks.data_ptr(), nchunks, hp.data_ptr<float>(), ptr<const double>(gnorm2), (float)gscale,
-                       grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), p.data_ptr<float>(),
-                       ptr<void>(pb), mat_sums.data_ptr<double>(), has_adamh, stream());
+                       grad.data_ptr<float>(), m.data_ptr<float>() - mv_offset, v.data_ptr<float>() - mv_offset,
+                       p.data_ptr<float>(), ptr<void>(pb), mat_sums.data_ptr<double>(), has_adamh, (int)phase,
+                       stream());
 }
 
 void ema(const Tensor& dst, const Tensor& src, double beta) {

@@ -248,12 +248,16 @@ void launch_opt_sqnorm(const void* chunks, int nchunks, const float* grad, float
 
 void launch_opt_step(const void* chunks, int nchunks, const float* hp, const double* gnorm2, float gscale,
                      const float* grad, float* m, float* v, float* p, void* pb, double* mat_sums, int has_adamh,
-                     cudaStream_t st) {
+                     int phase, cudaStream_t st) {
+  // phase 0: moments + AdamH apply; 1: moments (and Adam updates, AdamH matrix sums) only; 2: AdamH
+  // apply only -- a sharded optimizer all-reduces the matrix sums between phases 1 and 2.
   if (nchunks <= 0) return;
-  count_launch();
-  moments_kernel<<<nchunks, 256, 0, st>>>((const Chunk*)chunks, hp, gnorm2, gscale, grad, m, v, p,
-                                          (__nv_bfloat16*)pb, mat_sums);
-  if (has_adamh) {
+  if (phase != 2) {
+    count_launch();
+    moments_kernel<<<nchunks, 256, 0, st>>>((const Chunk*)chunks, hp, gnorm2, gscale, grad, m, v, p,
+                                            (__nv_bfloat16*)pb, mat_sums);
+  }
+  if (has_adamh && phase != 1) {
     count_launch();
     adamh_apply_kernel<<<nchunks, 256, 0, st>>>((const Chunk*)chunks, hp, m, v, p, (__nv_bfloat16*)pb, mat_sums);
   }

@@ -12,7 +12,6 @@ operand is passed as stored (``[rows, K]``); an MN-major operand is passed as it
 from __future__ import annotations
 
 import contextlib
-import threading
 
 import torch
 
@@ -62,9 +61,10 @@ def linear_dx(dy, w, *, out=None, accum=False):
     return gemm(dy, w, out, b_mn=True, M=m, N=k, K=n, accum=accum)
 
 
-class _WeightGradQueue(threading.local):
-    def __init__(self):
-        self.queue = None
+class _WeightGradQueue:
+    # Process-wide, not thread-local: autograd runs CUDA backward functions on its own device
+    # threads, which must see the queue the caller installed. One backward at a time per process.
+    queue = None
 
 
 _WGQ = _WeightGradQueue()

@@ -56,34 +56,52 @@ class FusedOptimizer:
         self.lr_fns = {n: cfg.lr_scheduler(num_train_steps, override_lr=g["lr"]) for n, g in self.groups.items()}
         self.norm_hook = None
         self.last_grad_norms: dict[str, float] = {}
-        # chunk table over adam / adamh groups
+        self.mat_hook = None
+        self.shard: tuple[int, int] | None = None
+        self.muon_infos = [i for g in self.groups.values() if g["kind"] == "muon" for i in g["infos"]]
+        self.has_adamh = any(g["kind"] == "adamh" for g in self.groups.values())
+        self._build_chunks()
+        if store.cuda:
+            self.hp_host = torch.zeros(len(self.names), HP, dtype=torch.float32).pin_memory()
+            self.hp = torch.zeros(len(self.names), HP, dtype=torch.float32, device=dev)
+            self.gnorm2 = torch.zeros(len(self.names), dtype=torch.float64, device=dev)
+            self.mat_sums = torch.zeros(self.mat_count, 3, dtype=torch.float64, device=dev)
+
+    def _build_chunks(self) -> None:
+        """Chunk table over the adam / adamh groups: (flat start, length, matrix id, group), each at
+        most CHUNK elements, restricted to ``self.shard`` when the optimizer state is sharded."""
+        lo, hi = self.shard if self.shard is not None else (0, 1 << 62)
         rows = []
         mat = 0
-        self.mat_count = 0
-        self.muon_infos = []
         for gi, name in enumerate(self.names):
             g = self.groups[name]
             if g["kind"] == "muon":
-                self.muon_infos.extend(g["infos"])
                 continue
             for info in g["infos"]:
                 mats = info.matrices if g["kind"] == "adamh" else [[(info.offset, info.numel)]]
                 for ranges in mats:
                     for start, length in ranges:
-                        for c0 in range(0, length, CHUNK):
-                            rows.append((start + c0, min(CHUNK, length - c0), mat, gi, 0))
+                        a, b = max(start, lo), min(start + length, hi)
+                        for c0 in range(a, b, CHUNK):
+                            rows.append((c0, min(CHUNK, b - c0), mat, gi, 0))
                     mat += 1
         self.mat_count = max(mat, 1)
-        self.has_adamh = any(g["kind"] == "adamh" for g in self.groups.values())
         arr = np.array(rows, dtype=_CHUNK_DTYPE) if rows else np.zeros(0, dtype=_CHUNK_DTYPE)
         self.nchunks = len(rows)
-        if store.cuda:
-            self.chunks = torch.from_numpy(arr.view(np.uint8).copy()).to(dev)
-            self.hp_host = torch.zeros(len(self.names), HP, dtype=torch.float32).pin_memory()
-            self.hp = torch.zeros(len(self.names), HP, dtype=torch.float32, device=dev)
-            self.gnorm2 = torch.zeros(len(self.names), dtype=torch.float64, device=dev)
-            self.mat_sums = torch.zeros(self.mat_count, 3, dtype=torch.float64, device=dev)
+        if self.store.cuda:
+            self.chunks = torch.from_numpy(arr.view(np.uint8).copy()).to(self.store.device)
         self._rows = rows
+
+    def set_shard(self, lo: int, hi: int) -> None:
+        """Keep optimizer state only for the flat range [lo, hi) (ZeRO): the moments shrink to the
+        shard, the chunk table covers it, and ``norm_hook`` / ``mat_hook`` must sum the per-group
+        squared norms and the AdamH matrix sums over the ranks holding the other shards."""
+        if self.muon_infos:
+            raise NotImplementedError("Muon with sharded optimizer state")
+        self.shard = (int(lo), int(hi))
+        self.m = torch.zeros(hi - lo, dtype=torch.float32, device=self.store.device)
+        self.v = torch.zeros_like(self.m)
+        self._build_chunks()
 
     # --------------------------------------------------------------------------------- state
     def state_dict(self) -> dict:
@@ -123,8 +141,19 @@ class FusedOptimizer:
             if self.norm_hook is not None:
                 self.norm_hook(self.gnorm2, self.names)
             self.mat_sums.zero_()
-            ext().opt_step(self.chunks, self.nchunks, self.hp, self.gnorm2, grad_scale, st.grad, self.m, self.v,
-                           st.master, st.compute, self.mat_sums, self.has_adamh)
+            off = self.shard[0] if self.shard is not None else 0
+            if self.shard is None:
+                ext().opt_step(self.chunks, self.nchunks, self.hp, self.gnorm2, grad_scale, st.grad, self.m, self.v,
+                               st.master, st.compute, self.mat_sums, self.has_adamh, 0, 0)
+            else:
+                ext().opt_step(self.chunks, self.nchunks, self.hp, self.gnorm2, grad_scale, st.grad, self.m, self.v,
+                               st.master, st.compute, self.mat_sums, self.has_adamh, off, 1)
+                if self.mat_hook is not None:
+                    self.mat_hook(self.mat_sums)
+                ext().opt_step(self.chunks, self.nchunks, self.hp, self.gnorm2, grad_scale, st.grad, self.m, self.v,
+                               st.master, st.compute, self.mat_sums, self.has_adamh, off, 2)
+        elif self.shard is not None:
+            self._step_cpu_chunks(t, grad_scale)
         else:
             self._step_cpu(t, grad_scale)
         if self.muon_infos:
@@ -186,6 +215,64 @@ class FusedOptimizer:
                         if nn_ > 0:
                             new = new / nn_ * pn
                         st.master[idx] = new
+
+    def _step_cpu_chunks(self, t: int, grad_scale: float) -> None:
+        """Chunk-table form of the step (the sharded path): per-group squared norms and AdamH
+        matrix sums are partial over this shard and completed by ``norm_hook`` / ``mat_hook``; AdamH
+        then uses ``||p - a u||^2 = S_pp - 2 a S_pu + a^2 S_uu`` with ``a = lr ||p|| / ||u||``."""
+        cfg = self.cfg
+        st = self.store
+        b1, b2, eps = cfg.beta1, cfg.beta2, cfg.epsilon
+        bc1, bc2 = 1 - b1 ** t, 1 - b2 ** t
+        off = self.shard[0]
+        gn = torch.zeros(len(self.names), dtype=torch.float64)
+        for start, ln, _, gi, _ in self._rows:
+            gn[gi] += float((st.grad[start:start + ln].double() * grad_scale).pow(2).sum())
+        if self.norm_hook is not None:
+            self.norm_hook(gn, self.names)
+        scale = []
+        for gi, name in enumerate(self.names):
+            n = math.sqrt(float(gn[gi]))
+            self.last_grad_norms[name] = n
+            s_ = grad_scale
+            if cfg.max_grad_norm and n >= cfg.max_grad_norm:
+                s_ = grad_scale * cfg.max_grad_norm / n
+            scale.append(s_)
+        sums = torch.zeros(self.mat_count, 3, dtype=torch.float64)
+        upd = {}
+        for start, ln, mat, gi, _ in self._rows:
+            g = self.groups[self.names[gi]]
+            sl = slice(start, start + ln)
+            ml = slice(start - off, start - off + ln)
+            gr = st.grad[sl] * scale[gi]
+            self.m[ml].mul_(b1).add_(gr, alpha=1 - b1)
+            self.v[ml].mul_(b2).addcmul_(gr, gr, value=1 - b2)
+            u = (self.m[ml] / bc1) / ((self.v[ml] / bc2).sqrt() + eps)
+            p = st.master[sl]
+            lr = self.lr_fns[self.names[gi]](self.step_count)
+            if g["kind"] == "adam":
+                p.sub_(lr * (u + g["wd"] * p))
+            else:
+                sums[mat, 0] += float((p.double() ** 2).sum())
+                sums[mat, 1] += float((p.double() * u.double()).sum())
+                sums[mat, 2] += float((u.double() ** 2).sum())
+                upd[start] = u
+        if self.mat_hook is not None:
+            self.mat_hook(sums)
+        for start, ln, mat, gi, _ in self._rows:
+            if start not in upd:
+                continue
+            lr = self.lr_fns[self.names[gi]](self.step_count)
+            spp, spu, suu = (float(x) for x in sums[mat])
+            pn = math.sqrt(spp)
+            un = max(math.sqrt(suu), 1e-10)
+            a = lr * pn / un
+            nn2 = spp - 2 * a * spu + a * a * suu
+            p = st.master[start:start + ln]
+            new = p - a * upd[start]
+            if nn2 > 0:
+                new = new * (pn / math.sqrt(nn2))
+            p.copy_(new)
 
     def _step_muon(self, t: int, grad_scale: float) -> None:
         """Muon update on the matrices of the muon group (momentum, Newton-Schulz, shape scale)."""

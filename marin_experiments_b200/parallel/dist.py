@@ -28,6 +28,8 @@ class DistContext:
     ep_group: object = None
     ep_rank: int = 0
     bucket_bytes: int = 256 << 20
+    # ranks holding the same expert shard (one per expert-parallel group); None when ep == world
+    expert_dp_group: object = None
 
     def local_expert_range(self, num_experts: int) -> tuple[int, int]:
         if num_experts % self.ep_size:
@@ -48,11 +50,13 @@ class DistContext:
         if self.world > 1:
             src = torch_dist.get_global_rank(self.batch_group, 0) if self.batch_group is not None else 0
             for info in st.infos:
-                if info.sharded_over is None:
+                if info.sharded_over is None or self.ep_size == 1:
                     torch_dist.broadcast(st.master_view(info), src=src, group=self.batch_group)
             st.sync_compute()
-        self._replicated = [i for i in st.infos if i.sharded_over is None and i.trainable]
-        self._sharded = [i for i in st.infos if i.sharded_over is not None and i.trainable]
+        # expert weights are shards only under expert parallelism; with ep_size 1 they are replicated
+        sharded = (lambda i: i.sharded_over is not None and self.ep_size > 1)
+        self._replicated = [i for i in st.infos if not sharded(i) and i.trainable]
+        self._sharded = [i for i in st.infos if sharded(i) and i.trainable]
 
     def setup_optimizer(self, trainer) -> None:
         opt = getattr(trainer.opt, "inner", trainer.opt)
@@ -94,7 +98,10 @@ class DistContext:
             return
         st = trainer.store
         for info in self._sharded:
-            st.grad[info.offset: info.offset + info.numel].div_(self.world)
+            g = st.grad[info.offset: info.offset + info.numel]
+            if self.expert_dp_group is not None:  # replicas of this shard in other expert groups
+                torch_dist.all_reduce(g, group=self.expert_dp_group)
+            g.div_(self.world)
         # contiguous runs of replicated parameters in the flat buffer
         runs = []
         for info in self._replicated:
@@ -128,14 +135,21 @@ def init(ep_size: int | None = None, timeout_s: float = 600.0) -> DistContext:
     batch_group = torch_dist.group.WORLD
     ep_group = batch_group
     ep_rank = rank % ep
+    expert_dp = None
     if ep != world:
         for start in range(0, world, ep):
             ranks = list(range(start, start + ep))
             g = torch_dist.new_group(ranks)
             if rank in ranks:
                 ep_group = g
+        if ep > 1:
+            for e in range(ep):
+                ranks = list(range(e, world, ep))
+                g = torch_dist.new_group(ranks)
+                if rank in ranks:
+                    expert_dp = g
     _CTX = DistContext(rank=rank, world=world, ep_size=ep, backend=backend, batch_group=batch_group,
-                       ep_group=ep_group, ep_rank=ep_rank)
+                       ep_group=ep_group, ep_rank=ep_rank, expert_dp_group=expert_dp)
     return _CTX
 
 

@@ -107,10 +107,22 @@ def load_scalar_state(trainer, st: dict) -> None:
         opt.t = int(st["delayed_t"])
 
 
+def _opt_shard(trainer):
+    inner = getattr(trainer.opt, "inner", trainer.opt)
+    return getattr(inner, "shard", None)
+
+
 def _leaves(trainer, buffers: dict[str, torch.Tensor], ep_size: int, ep_rank: int) -> list[_Leaf]:
     out = []
     gname = getattr(trainer.model, "global_name", lambda n: n)
+    n_store = trainer.store.numel
+    shard = _opt_shard(trainer)
     for prefix, buf in buffers.items():
+        if buf.numel() != n_store:
+            # optimizer state kept only for this rank's flat range (ZeRO): one leaf per range
+            lo = shard[0]
+            out.append(_Leaf(f"{prefix}/__flat__", buf, 0, buf.numel(), (buf.numel(),), (n_store,), lo, True))
+            continue
         for info in trainer.store.infos:
             sharded = info.sharded_over == "expert" and ep_size > 1
             gshape = tuple(info.shape)
@@ -173,6 +185,8 @@ def save_checkpoint(trainer, path: str, *, step: int | None = None, temporary: b
     step = int(trainer.step if step is None else step)
     pool = pool or _PinnedPool()
     writers = list(range(ep_size)) if ep_size > 1 else [0]
+    if _opt_shard(trainer) is not None:
+        writers = list(range(world))
     if rank not in writers:
         return SaveHandle(None, {})
     buffers = flat_buffers(trainer)

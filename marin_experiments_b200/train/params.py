@@ -88,7 +88,7 @@ def default_matrices(name: str, shape: tuple[int, ...], offset: int, module: nn.
 
 class ParamStore:
     def __init__(self, model: nn.Module, device: torch.device | str, *, compute_dtype=torch.bfloat16,
-                 moments: int = 2):
+                 moments: int = 2, pad_multiple: int = ALIGN):
         self.device = torch.device(device)
         self.cuda = self.device.type == "cuda"
         self.compute_dtype = compute_dtype if self.cuda else torch.float32
@@ -110,7 +110,7 @@ class ParamStore:
             self.infos.append(info)
             self._params[name] = p
             off += p.numel()
-        self.numel = (off + ALIGN - 1) // ALIGN * ALIGN
+        self.numel = (off + pad_multiple - 1) // pad_multiple * pad_multiple
         dev = self.device
         self.master = torch.zeros(self.numel, dtype=torch.float32, device=dev)
         self.grad = torch.zeros(self.numel, dtype=torch.float32, device=dev)

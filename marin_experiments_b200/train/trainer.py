@@ -62,7 +62,7 @@ class Trainer:
         with torch.device("meta"):
             model = Transformer(cfg, local_experts=local, **self.model_kwargs)
         self.model = model
-        self.store = ParamStore(model, self.device)
+        self.store = ParamStore(model, self.device, pad_multiple=getattr(self.dist, "store_pad", 64))
         init_store_weights(self.store, cfg, self.seed, model)
         if self.dist is not None:
             self.dist.setup_model(self)
@@ -131,6 +131,8 @@ class Trainer:
         if self.dist is not None:
             self.dist.grad_sync(self)
         self.opt.step()
+        if self.dist is not None and hasattr(self.dist, "post_step"):
+            self.dist.post_step(self)
         if beta_sum is not None:
             self.pending_qb = beta_sum / n_micro
         if self.ema is not None:

@@ -1,0 +1,50 @@
+"""ZeRO-2 on 2 GPUs (NCCL reduce-scatter / all-gather, sharded fused optimizer with the AdamH
+matrix sums all-reduced between its passes) against replicated data parallelism."""
+
+import datetime
+
+import pytest
+import torch
+
+from mp_util import run_ranks
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(vocab_size=4096, hidden_dim=256, intermediate_dim=256, shared_expert_intermediate_dim=512, num_experts=8,
+           num_experts_per_token=2, num_layers=2, num_heads=4, num_kv_heads=4, head_dim=64, max_seq_len=256,
+           sliding_window=256, capacity_factor=4.0)
+
+
+def _rank(rank, world, zero):
+    import torch.distributed as tdist
+
+    from marin_experiments_b200.config import GrugModelConfig, GrugRunConfig, GrugTrainerConfig, TrainerConfig
+    from marin_experiments_b200.optim import GrugMoeAdamHConfig
+    from marin_experiments_b200.parallel import dist as pdist
+    from marin_experiments_b200.parallel.fsdp import init_zero
+    from marin_experiments_b200.train.trainer import Trainer
+
+    torch.cuda.set_device(rank)
+    ctx = init_zero(120) if zero else pdist.init(ep_size=1, timeout_s=120)
+    try:
+        run = GrugRunConfig(model=GrugModelConfig(**CFG), optimizer=GrugMoeAdamHConfig(warmup=0.0),
+                            trainer=GrugTrainerConfig(trainer=TrainerConfig(num_train_steps=10, seed=0)))
+        tr = Trainer(run, device=f"cuda:{rank}", dist=ctx)
+        init = tr.store.master.clone()
+        tok = torch.randint(0, 4096, (2, 256), generator=torch.Generator().manual_seed(rank)).pin_memory()
+        tr.train_step({"tokens": tok})
+        torch.cuda.synchronize()
+        return {"upd": (tr.store.master - init).cpu().numpy(), "m_numel": tr.opt.m.numel(), "n": tr.store.numel}
+    finally:
+        pdist.shutdown()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_zero_matches_dp_on_gpu():
+    a = run_ranks(_rank, 2, True, timeout=300)
+    b = run_ranks(_rank, 2, False, timeout=300)
+    assert a[0]["m_numel"] * 2 == a[0]["n"]
+    for r in range(2):
+        ua, ub = torch.from_numpy(a[r]["upd"]), torch.from_numpy(b[r]["upd"])
+        err = ((ua - ub).norm() / ub.norm()).item()
+        assert err < 0.05, (r, err)
