@@ -144,4 +144,5 @@ def test_deferred_weight_grads_match():
     assert len(q) == 1 and float(w.main_grad.abs().sum()) == 0.0
     assert torch.equal(xb.grad, ref_dx)
     G.run_weight_grads(q)
-    assert torch.equal(w.main_grad, ref_dw)
+    # split-K partial sums are combined with atomic adds: equal up to summation order
+    assert torch.allclose(w.main_grad, ref_dw, rtol=1e-4, atol=1e-3)
