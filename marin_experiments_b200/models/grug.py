@@ -135,6 +135,7 @@ class MoEMLP(nn.Module):
         self.w_down = nn.Parameter(torch.empty(hi - lo, d, i))
         self.cfg = cfg
         self.ep_group = None  # set by parallel.ep when experts are sharded
+        self.layer_key = 0  # this layer's index (keys its expert-parallel receive buffers)
 
     def forward(self, h, residual=None, dp_group=None):
         c = self.cfg
@@ -157,7 +158,8 @@ class MoEMLP(nn.Module):
         if self.ep_group is not None:
             from ..parallel import ep
 
-            y = ep.moe_experts_ep(h, r, self.w_gate_up, self.w_down, cap, self.ep_group, residual=residual)
+            y = ep.moe_experts_ep(h, r, self.w_gate_up, self.w_down, cap, self.ep_group, residual=residual,
+                                  layer=self.layer_key, n_layers=c.num_layers)
         else:
             y = ops.moe_experts(h, r, self.w_gate_up, self.w_down, capacity=cap, residual=residual)
         stats = RouterStats(r.z_loss, r.lbl, r.sparsity, r.counts, r.entropy, beta, r.expected_active,
@@ -173,6 +175,7 @@ class Block(nn.Module):
         self.mlp_norm = NormPair(cfg)
         if cfg.is_moe:
             self.mlp = MoEMLP(cfg, local_experts)
+            self.mlp.layer_key = layer
             self.shared = (DenseMLP(cfg.hidden_dim, cfg.shared_expert_intermediate_dim, True, "silu")
                            if cfg.shared_expert_intermediate_dim > 0 else None)
         else:

@@ -1,2 +1,284 @@
-// Peer-to-peer collectives over NVLink (filled in by the expert-parallel exchange).
+// Expert-parallel token exchange over NVLink peer memory (no NCCL on this path).
+//
+// Every rank of an expert-parallel group maps the same-sized "heap" of every peer (CUDA IPC), so a
+// buffer at heap offset `off` exists on every rank and rank r can address rank p's copy directly.
+// Token rows move with 16-byte loads/stores issued by the kernels that produce or consume them:
+//
+//   dispatch (forward):  the permute kernel of source s writes each routed row straight into the
+//                        receive buffer of the expert's owner, layout [source][local expert][cap][D];
+//   combine (forward):   the combine kernel of source s reads its K expert outputs per token from
+//                        the owners' output buffers and forms sum_k w_k * y_k + residual;
+//   backward:            the combine-backward kernel pushes w * dout rows to the owners; the
+//                        unpermute kernel pulls the input-gradient rows back and sums them.
+//
+// Ordering: a producer kernel fences its stores at system scope; the last CTA to finish (found with
+// an atomic counter) then writes `epoch` into the flag slot [purpose][source] of every peer with a
+// release store. A consumer waits with acquire loads until its W flags reach `epoch` before any
+// kernel reads the exchanged rows. Every wait is bounded (kPeerWaitCycles); on timeout the waiter
+// records kErrTimeoutPeer in the error flag and returns, so the host sees the failure instead of a
+// hung GPU. Rows are never read through TMA or any cluster-multicast path from peer memory.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstring>
+
+#include "kernels.h"
+#include "sm100_primitives.cuh"
+
+namespace mxk {
+
+namespace {
+
+constexpr long long kPeerWaitCycles = 1ll << 35;  // ~17 s at 1.9 GHz: peers may lag by a whole layer
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ char* peer_ptr(const PeerTable& pt, int rank, size_t off) {
+  return static_cast<char*>(pt.base[rank]) + off;
+}
+
+// Flag slot of (purpose, source) inside a rank's flag area.
+__device__ __forceinline__ int* flag_slot(const PeerTable& pt, int rank, size_t flags_off, int purpose, int src) {
+  return reinterpret_cast<int*>(peer_ptr(pt, rank, flags_off)) + purpose * kMaxPeers + src;
+}
+
+// Called by every CTA of a producer kernel after its last store: publishes `epoch` to every peer's
+// flag (purpose, my) once all CTAs are done.
+__device__ void publish(const PeerTable& pt, int world, int my, size_t flags_off, int purpose, int epoch,
+                        unsigned int* counter) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int prev = atomicAdd(counter, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int p = 0; p < world; ++p) st_release_sys(flag_slot(pt, p, flags_off, purpose, my), epoch);
+      *counter = 0u;  // ready for the next launch (stream order)
+    }
+  }
+}
+
+__device__ __forceinline__ int round128(int c) { return (c + 127) & ~127; }
+
+__device__ __forceinline__ void acc8(float (&a)[8], uint4 u, float w) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    a[2 * i] += w * f.x;
+    a[2 * i + 1] += w * f.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&a)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(a[2 * i], a[2 * i + 1]);
+  return u;
+}
+
+// Row r = e * cap + s of the source-side [E][cap] layout lives on rank e / E_loc at row
+// ((my * E_loc) + e % E_loc) * cap + s of that rank's [W][E_loc][cap] buffer.
+__device__ __forceinline__ long remote_row(int e, int s, int e_loc, int cap, int my) {
+  return ((long)my * e_loc + (e % e_loc)) * cap + s;
+}
+
+// ------------------------------------------------------------------------------------ kernels
+// Forward dispatch: x[perm] rows (zeros on pad rows up to round128(count)) -> owners' receive buffers;
+// counts -> owners' count arrays.
+__global__ void ep_dispatch_push_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ perm,
+                                        const int* __restrict__ counts, EpArgs a) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int E = a.e_loc * a.world;
+  if (blockIdx.x == 0)
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      int* dst = reinterpret_cast<int*>(peer_ptr(a.peers, e / a.e_loc, a.counts_off));
+      dst[a.my * a.e_loc + e % a.e_loc] = counts[e];
+    }
+  for (long r = blockIdx.x * (long)warps + (threadIdx.x >> 5); r < (long)E * a.cap; r += (long)gridDim.x * warps) {
+    const int e = (int)(r / a.cap), s = (int)(r % a.cap);
+    const int c = counts[e];
+    if (s >= round128(c)) continue;
+    uint4* dst = reinterpret_cast<uint4*>(peer_ptr(a.peers, e / a.e_loc, a.buf_off)) +
+                 remote_row(e, s, a.e_loc, a.cap, a.my) * (a.D / 8);
+    if (s < c) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + (long)perm[r] * a.D);
+      for (int i = lane; i < a.D / 8; i += 32) dst[i] = src[i];
+    } else {
+      for (int i = lane; i < a.D / 8; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  publish(a.peers, a.world, a.my, a.flags_off, a.purpose, a.epoch, a.counter);
+}
+
+// Backward of the combine, pushed: dY rows = w * dout[perm] (zeros on pad rows) -> owners' buffers.
+__global__ void ep_combine_bwd_push_kernel(const __nv_bfloat16* __restrict__ dout, const int* __restrict__ perm,
+                                           const float* __restrict__ wperm, const int* __restrict__ counts, EpArgs a) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int E = a.e_loc * a.world;
+  for (long r = blockIdx.x * (long)warps + (threadIdx.x >> 5); r < (long)E * a.cap; r += (long)gridDim.x * warps) {
+    const int e = (int)(r / a.cap), s = (int)(r % a.cap);
+    const int c = counts[e];
+    if (s >= round128(c)) continue;
+    uint4* dst = reinterpret_cast<uint4*>(peer_ptr(a.peers, e / a.e_loc, a.buf_off)) +
+                 remote_row(e, s, a.e_loc, a.cap, a.my) * (a.D / 8);
+    if (s < c) {
+      const float w = wperm[r];
+      const uint4* src = reinterpret_cast<const uint4*>(dout + (long)perm[r] * a.D);
+      for (int i = lane; i < a.D / 8; i += 32) {
+        float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        acc8(v, src[i], w);
+        dst[i] = pack8(v);
+      }
+    } else {
+      for (int i = lane; i < a.D / 8; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  publish(a.peers, a.world, a.my, a.flags_off, a.purpose, a.epoch, a.counter);
+}
+
+// Forward combine, pulled: out[t] = residual[t] + sum_k w[t,k] * Y_owner[row(t,k)]; the pulled rows
+// are also stored to y_local in the source layout [E][cap][D] for the backward's weight gradient.
+__global__ void ep_combine_pull_kernel(const int* __restrict__ sel, const int* __restrict__ slot,
+                                       const float* __restrict__ comb, const __nv_bfloat16* __restrict__ residual,
+                                       __nv_bfloat16* __restrict__ out, __nv_bfloat16* __restrict__ y_local, int T,
+                                       int K, EpArgs a) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+    for (int c = lane; c < a.D / 8; c += 32) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (residual) acc8(acc, reinterpret_cast<const uint4*>(residual + (long)t * a.D)[c], 1.f);
+      for (int k = 0; k < K; ++k) {
+        const int s = slot[(long)t * K + k];
+        if (s < 0) continue;
+        const int e = sel[(long)t * K + k];
+        const uint4* src = reinterpret_cast<const uint4*>(peer_ptr(a.peers, e / a.e_loc, a.buf_off)) +
+                           remote_row(e, s, a.e_loc, a.cap, a.my) * (a.D / 8);
+        const uint4 v = __ldcv(src + c);
+        if (y_local) reinterpret_cast<uint4*>(y_local + ((long)e * a.cap + s) * a.D)[c] = v;
+        acc8(acc, v, comb[(long)t * K + k]);
+      }
+      reinterpret_cast<uint4*>(out + (long)t * a.D)[c] = pack8(acc);
+    }
+  }
+}
+
+// Backward unpermute, pulled: dx[t] = sum_k dXp_owner[row(t,k)].
+__global__ void ep_unpermute_pull_kernel(const int* __restrict__ sel, const int* __restrict__ slot,
+                                         __nv_bfloat16* __restrict__ dx, int T, int K, EpArgs a) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+    for (int c = lane; c < a.D / 8; c += 32) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int k = 0; k < K; ++k) {
+        const int s = slot[(long)t * K + k];
+        if (s < 0) continue;
+        const int e = sel[(long)t * K + k];
+        const uint4* src = reinterpret_cast<const uint4*>(peer_ptr(a.peers, e / a.e_loc, a.buf_off)) +
+                           remote_row(e, s, a.e_loc, a.cap, a.my) * (a.D / 8);
+        acc8(acc, __ldcv(src + c), 1.f);
+      }
+      reinterpret_cast<uint4*>(dx + (long)t * a.D)[c] = pack8(acc);
+    }
+  }
+}
+
+// Publish `epoch` for (purpose, my) to every peer once the previous work on the stream is done
+// (e.g. after the expert GEMMs that wrote the buffer the peers will pull).
+__global__ void ep_signal_kernel(PeerTable peers, int world, int my, size_t flags_off, int purpose, int epoch) {
+  __threadfence_system();
+  if (threadIdx.x < world) st_release_sys(flag_slot(peers, threadIdx.x, flags_off, purpose, my), epoch);
+}
+
+// Wait until every source's flag for `purpose` reached `epoch` (bounded).
+__global__ void ep_wait_kernel(PeerTable peers, int world, int my, size_t flags_off, int purpose, int epoch,
+                               int* err) {
+  if (threadIdx.x < world) {
+    const int* f = flag_slot(peers, my, flags_off, purpose, threadIdx.x);
+    const long long t0 = clock64();
+    while (ld_acquire_sys(f) < epoch) {
+      if (clock64() - t0 > kPeerWaitCycles) {
+        atomicExch(err, kErrTimeoutPeer);
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  __syncthreads();
+}
+
+inline int grid_rows(long work) {
+  long g = (work + 7) / 8;
+  if (g > 148 * 8) g = 148 * 8;
+  return g < 1 ? 1 : (int)g;
+}
+
+}  // namespace
+
+void launch_ep_dispatch_push(const void* x, const int* perm, const int* counts, const EpArgs& a, cudaStream_t st) {
+  count_launch();
+  ep_dispatch_push_kernel<<<grid_rows((long)a.e_loc * a.world * a.cap), 256, 0, st>>>(
+      (const __nv_bfloat16*)x, perm, counts, a);
+}
+
+void launch_ep_combine_bwd_push(const void* dout, const int* perm, const float* wperm, const int* counts,
+                                const EpArgs& a, cudaStream_t st) {
+  count_launch();
+  ep_combine_bwd_push_kernel<<<grid_rows((long)a.e_loc * a.world * a.cap), 256, 0, st>>>(
+      (const __nv_bfloat16*)dout, perm, wperm, counts, a);
+}
+
+void launch_ep_combine_pull(const int* sel, const int* slot, const float* comb, const void* residual, void* out,
+                            void* y_local, int T, int K, const EpArgs& a, cudaStream_t st) {
+  count_launch();
+  ep_combine_pull_kernel<<<grid_rows(T), 256, 0, st>>>(sel, slot, comb, (const __nv_bfloat16*)residual,
+                                                       (__nv_bfloat16*)out, (__nv_bfloat16*)y_local, T, K, a);
+}
+
+void launch_ep_unpermute_pull(const int* sel, const int* slot, void* dx, int T, int K, const EpArgs& a,
+                              cudaStream_t st) {
+  count_launch();
+  ep_unpermute_pull_kernel<<<grid_rows(T), 256, 0, st>>>(sel, slot, (__nv_bfloat16*)dx, T, K, a);
+}
+
+void launch_ep_signal(const EpArgs& a, cudaStream_t st) {
+  count_launch();
+  ep_signal_kernel<<<1, 32, 0, st>>>(a.peers, a.world, a.my, a.flags_off, a.purpose, a.epoch);
+}
+
+void launch_ep_wait(const EpArgs& a, int* err, cudaStream_t st) {
+  count_launch();
+  ep_wait_kernel<<<1, 32, 0, st>>>(a.peers, a.world, a.my, a.flags_off, a.purpose, a.epoch, err);
+}
+
+// ----------------------------------------------------------------------------------- host IPC
+int ipc_alloc(size_t bytes, void** ptr, void* handle_out) {
+  if (cudaMalloc(ptr, bytes) != cudaSuccess) return 1;
+  if (cudaMemset(*ptr, 0, bytes) != cudaSuccess) return 2;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, *ptr) != cudaSuccess) return 3;
+  memcpy(handle_out, &h, sizeof(h));
+  return 0;
+}
+
+int ipc_open(const void* handle, void** ptr) {
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? 0 : 1;
+}
+
+int ipc_close(void* ptr) { return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? 0 : 1; }
+
+int ipc_free(void* ptr) { return cudaFree(ptr) == cudaSuccess ? 0 : 1; }
+
+}  // namespace mxk

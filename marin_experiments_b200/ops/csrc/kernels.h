@@ -98,4 +98,32 @@ int launch_flash_bwd(const AttnLaunch& L, cudaStream_t st);
 // tcgen05 forward (attention_sm100.cu); q/k/v heads contiguous (head stride == hd)
 int launch_flash_fwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st);
 
+// ------------------------------------------------------------ expert-parallel peer exchange (comm.cu)
+constexpr int kMaxPeers = 16;
+struct PeerTable {
+  void* base[kMaxPeers];  // every rank's heap base as mapped in this process (own rank included)
+};
+struct EpArgs {
+  PeerTable peers;
+  int world, my, e_loc, cap, D;
+  size_t buf_off;     // heap offset of the exchanged row buffer ([W][E_loc][cap][D] on the owner)
+  size_t counts_off;  // heap offset of the received counts ([W][E_loc] ints; dispatch only)
+  size_t flags_off;   // heap offset of the flag area ([purpose][kMaxPeers] ints)
+  int purpose, epoch;
+  unsigned int* counter;  // local completion counter of the producer kernel
+};
+void launch_ep_dispatch_push(const void* x, const int* perm, const int* counts, const EpArgs& a, cudaStream_t st);
+void launch_ep_combine_bwd_push(const void* dout, const int* perm, const float* wperm, const int* counts,
+                                const EpArgs& a, cudaStream_t st);
+void launch_ep_combine_pull(const int* sel, const int* slot, const float* comb, const void* residual, void* out,
+                            void* y_local, int T, int K, const EpArgs& a, cudaStream_t st);
+void launch_ep_unpermute_pull(const int* sel, const int* slot, void* dx, int T, int K, const EpArgs& a,
+                              cudaStream_t st);
+void launch_ep_signal(const EpArgs& a, cudaStream_t st);
+void launch_ep_wait(const EpArgs& a, int* err, cudaStream_t st);
+int ipc_alloc(size_t bytes, void** ptr, void* handle_out);
+int ipc_open(const void* handle, void** ptr);
+int ipc_close(void* ptr);
+int ipc_free(void* ptr);
+
 }  // namespace mxk

@@ -542,9 +542,11 @@ void launch_combine(const void* Y, const int* sel, const int* slot, const float*
 void launch_combine_bwd(const void* dout, const void* Y, const int* sel, const int* slot, const int* perm,
                         const float* wperm, const int* counts, int T, int K, int cap, int E, int D, void* dY,
                         float* dcomb, cudaStream_t st) {
-  count_launch();
-  combine_bwd_rows_kernel<<<grid_for((long)E * cap, 8), 256, 0, st>>>((const __nv_bfloat16*)dout, perm, wperm,
-                                                                      counts, cap, E, D, (__nv_bfloat16*)dY);
+  if (dY) {  // the expert-parallel path pushes these rows to the owners itself
+    count_launch();
+    combine_bwd_rows_kernel<<<grid_for((long)E * cap, 8), 256, 0, st>>>((const __nv_bfloat16*)dout, perm, wperm,
+                                                                        counts, cap, E, D, (__nv_bfloat16*)dY);
+  }
   count_launch();
   combine_bwd_weights_kernel<<<grid_for((long)T * K, 8), 256, 0, st>>>(
       (const __nv_bfloat16*)dout, (const __nv_bfloat16*)Y, sel, slot, T, K, cap, D, dcomb);

@@ -269,12 +269,13 @@ void combine(const Tensor& Y, const Tensor& sel, const Tensor& slot, const Tenso
 }
 
 void combine_bwd(const Tensor& dout, const Tensor& Y, const Tensor& sel, const Tensor& slot, const Tensor& perm,
-                 const Tensor& wperm, const Tensor& counts, int64_t cap, const Tensor& dY, const Tensor& dcomb) {
-  contig(dout, "dout"); contig(dY, "dY");
+                 const Tensor& wperm, const Tensor& counts, int64_t cap, const OptT& dY, const Tensor& dcomb) {
+  contig(dout, "dout");
+  if (dY.has_value()) contig(*dY, "dY");
   c10::cuda::CUDAGuard g(Y.device());
   mxk::launch_combine_bwd(dout.data_ptr(), Y.data_ptr(), sel.data_ptr<int>(), slot.data_ptr<int>(), perm.data_ptr<int>(),
                           wperm.data_ptr<float>(), counts.data_ptr<int>(), sel.size(0), sel.size(1), cap,
-                          counts.numel(), dout.size(1), dY.data_ptr(), dcomb.data_ptr<float>(), stream());
+                          counts.numel(), dout.size(1), ptr<void>(dY), dcomb.data_ptr<float>(), stream());
 }
 
 void unpermute_add(const Tensor& dxp, const Tensor& sel, const Tensor& slot, const OptT& dx_in, const Tensor& dx,
@@ -317,6 +318,96 @@ void cast_bf16(const Tensor& src, const Tensor& dst) {
   mxk::launch_cast_bf16(src.data_ptr<float>(), dst.data_ptr(), src.numel(), stream());
 }
 
+// ---------------------------------------------------------------- expert-parallel peer exchange
+mxk::EpArgs ep_args(const std::vector<int64_t>& peers, int64_t my, int64_t e_loc, int64_t cap, int64_t D,
+                    int64_t buf_off, int64_t counts_off, int64_t flags_off, int64_t purpose, int64_t epoch,
+                    const OptT& counter) {
+  need((int64_t)peers.size() <= mxk::kMaxPeers && my < (int64_t)peers.size(), "bad peer table");
+  need(D % 8 == 0, "row width must be a multiple of 8 elements");
+  mxk::EpArgs a{};
+  for (size_t i = 0; i < peers.size(); ++i) a.peers.base[i] = reinterpret_cast<void*>(peers[i]);
+  a.world = (int)peers.size();
+  a.my = (int)my;
+  a.e_loc = (int)e_loc;
+  a.cap = (int)cap;
+  a.D = (int)D;
+  a.buf_off = (size_t)buf_off;
+  a.counts_off = (size_t)counts_off;
+  a.flags_off = (size_t)flags_off;
+  a.purpose = (int)purpose;
+  a.epoch = (int)epoch;
+  a.counter = counter.has_value() ? reinterpret_cast<unsigned int*>(counter->data_ptr()) : nullptr;
+  return a;
+}
+
+std::tuple<int64_t, Tensor> ipc_alloc(int64_t bytes) {
+  void* p = nullptr;
+  Tensor h = torch::empty({64}, torch::dtype(torch::kUInt8));
+  need(sizeof(cudaIpcMemHandle_t) <= 64, "ipc handle size");
+  const int rc = mxk::ipc_alloc((size_t)bytes, &p, h.data_ptr());
+  need(rc == 0, "ipc_alloc failed");
+  return {reinterpret_cast<int64_t>(p), h};
+}
+
+int64_t ipc_open(const Tensor& h) {
+  void* p = nullptr;
+  need(mxk::ipc_open(h.contiguous().data_ptr(), &p) == 0, "cudaIpcOpenMemHandle failed");
+  return reinterpret_cast<int64_t>(p);
+}
+
+Tensor heap_tensor(int64_t base, int64_t offset, std::vector<int64_t> shape, int64_t dtype_code, int64_t device) {
+  // dtype_code: 0 bf16, 1 f32, 2 i32
+  const auto dt = dtype_code == 0 ? torch::kBFloat16 : dtype_code == 1 ? torch::kFloat32 : torch::kInt32;
+  void* p = reinterpret_cast<char*>(base) + offset;
+  need(reinterpret_cast<uintptr_t>(p) % 16 == 0, "heap tensor must be 16-byte aligned");
+  return torch::from_blob(p, shape, [](void*) {}, torch::dtype(dt).device(torch::kCUDA, device));
+}
+
+void ep_dispatch_push(const Tensor& x, const Tensor& perm, const Tensor& counts, const std::vector<int64_t>& peers,
+                      int64_t my, int64_t e_loc, int64_t cap, int64_t buf_off, int64_t counts_off, int64_t flags_off,
+                      int64_t purpose, int64_t epoch, const Tensor& counter) {
+  c10::cuda::CUDAGuard g(x.device());
+  auto a = ep_args(peers, my, e_loc, cap, x.size(1), buf_off, counts_off, flags_off, purpose, epoch, counter);
+  mxk::launch_ep_dispatch_push(x.data_ptr(), perm.data_ptr<int>(), counts.data_ptr<int>(), a, stream());
+}
+
+void ep_combine_bwd_push(const Tensor& dout, const Tensor& perm, const Tensor& wperm, const Tensor& counts,
+                         const std::vector<int64_t>& peers, int64_t my, int64_t e_loc, int64_t cap, int64_t buf_off,
+                         int64_t flags_off, int64_t purpose, int64_t epoch, const Tensor& counter) {
+  c10::cuda::CUDAGuard g(dout.device());
+  auto a = ep_args(peers, my, e_loc, cap, dout.size(1), buf_off, 0, flags_off, purpose, epoch, counter);
+  mxk::launch_ep_combine_bwd_push(dout.data_ptr(), perm.data_ptr<int>(), wperm.data_ptr<float>(),
+                                  counts.data_ptr<int>(), a, stream());
+}
+
+void ep_combine_pull(const Tensor& sel, const Tensor& slot, const Tensor& comb, const OptT& residual, const Tensor& out,
+                     const OptT& y_local, const std::vector<int64_t>& peers, int64_t my, int64_t e_loc, int64_t cap,
+                     int64_t buf_off) {
+  c10::cuda::CUDAGuard g(out.device());
+  auto a = ep_args(peers, my, e_loc, cap, out.size(1), buf_off, 0, 0, 0, 0, c10::nullopt);
+  mxk::launch_ep_combine_pull(sel.data_ptr<int>(), slot.data_ptr<int>(), comb.data_ptr<float>(), ptr<void>(residual),
+                              out.data_ptr(), ptr<void>(y_local), (int)sel.size(0), (int)sel.size(1), a, stream());
+}
+
+void ep_unpermute_pull(const Tensor& sel, const Tensor& slot, const Tensor& dx, const std::vector<int64_t>& peers,
+                       int64_t my, int64_t e_loc, int64_t cap, int64_t buf_off) {
+  c10::cuda::CUDAGuard g(dx.device());
+  auto a = ep_args(peers, my, e_loc, cap, dx.size(1), buf_off, 0, 0, 0, 0, c10::nullopt);
+  mxk::launch_ep_unpermute_pull(sel.data_ptr<int>(), slot.data_ptr<int>(), dx.data_ptr(), (int)sel.size(0),
+                                (int)sel.size(1), a, stream());
+}
+
+void ep_signal(const std::vector<int64_t>& peers, int64_t my, int64_t flags_off, int64_t purpose, int64_t epoch) {
+  auto a = ep_args(peers, my, 1, 1, 8, 0, 0, flags_off, purpose, epoch, c10::nullopt);
+  mxk::launch_ep_signal(a, stream());
+}
+
+void ep_wait(const std::vector<int64_t>& peers, int64_t my, int64_t flags_off, int64_t purpose, int64_t epoch,
+             const Tensor& err) {
+  auto a = ep_args(peers, my, 1, 1, 8, 0, 0, flags_off, purpose, epoch, c10::nullopt);
+  mxk::launch_ep_wait(a, err.data_ptr<int>(), stream());
+}
+
 }  // namespace
 
 void register_ops(pybind11::module& m) {
@@ -349,4 +440,15 @@ void register_ops(pybind11::module& m) {
   m.def("opt_step", &opt_step);
   m.def("ema", &ema);
   m.def("cast_bf16", &cast_bf16);
+  m.def("ipc_alloc", &ipc_alloc);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", [](int64_t p) { return mxk::ipc_close(reinterpret_cast<void*>(p)); });
+  m.def("ipc_free", [](int64_t p) { return mxk::ipc_free(reinterpret_cast<void*>(p)); });
+  m.def("heap_tensor", &heap_tensor);
+  m.def("ep_dispatch_push", &ep_dispatch_push);
+  m.def("ep_combine_bwd_push", &ep_combine_bwd_push);
+  m.def("ep_combine_pull", &ep_combine_pull);
+  m.def("ep_unpermute_pull", &ep_unpermute_pull);
+  m.def("ep_signal", &ep_signal);
+  m.def("ep_wait", &ep_wait);
 }

@@ -17,6 +17,8 @@ psum-scatter; grug-moe-pp/pipeline.py:198-245), which moves W times more activat
 
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -89,6 +91,111 @@ class _MoEEP(torch.autograd.Function):
         return dh, dcomb, None, None, (dout if ctx.has_res else None), None, None, None, None, None
 
 
+# flag purposes of the peer exchange
+_DISPATCH, _Y, _DY, _DXP = 0, 1, 2, 3
+
+
+def _heap(group, dev, e, cap, d, n_layers):
+    from .symm import heap_for, nbytes
+
+    rows = e * cap
+    per_layer = nbytes((rows, d), torch.bfloat16) + nbytes((e,), torch.int32) + 512
+    shared = 3 * nbytes((rows, d), torch.bfloat16)
+    return heap_for(group, dev, per_layer * n_layers + shared + (1 << 20))
+
+
+class _MoEEPFused(torch.autograd.Function):
+    """Expert parallelism with the token exchange inside the kernels (NVLink peer stores/loads):
+    the permute pushes rows into the owners' receive buffers, the combine pulls the owners' outputs,
+    and the backward mirrors it. Per-layer receive buffers live in a symmetric heap and stay valid as
+    saved activations; the output, output-gradient and input-gradient buffers are shared by layers
+    (each is consumed before any peer can reach the next layer's exchange)."""
+
+    @staticmethod
+    def forward(ctx, h, comb, w_gu, w_d, residual, sel, keep, cap, group, act, layer, n_layers):
+        from ..ops import gemm as G
+        from ..ops._ext import err_flag, ext
+        from ..ops.cuda_fns import _ACT, _c, dispatch_plan
+
+        h = _c(h)
+        t, d = h.shape
+        e_loc, two_i, _ = w_gu.shape
+        inter = two_i // 2
+        world = dist.get_world_size(group)
+        e = e_loc * world
+        dev = h.device
+        heap = _heap(group, dev, e, cap, d, n_layers)
+        my = heap.my
+        rows = e * cap
+        off_xp = heap.alloc(("xp", layer), rows * d * 2)
+        off_cnt = heap.alloc(("cnt", layer), e * 4)
+        off_y = heap.alloc("y", rows * d * 2)
+        slot, perm, wperm, counts = dispatch_plan(sel, keep, comb, e, cap)
+        ep = heap.next_epoch(_DISPATCH)
+        ext().ep_dispatch_push(h, perm, counts, heap.peers, my, e_loc, cap, off_xp, off_cnt, 0, _DISPATCH, ep,
+                               heap.counter(_DISPATCH))
+        ext().ep_wait(heap.peers, my, 0, _DISPATCH, ep, err_flag(dev))
+        xp_recv = heap.tensor(off_xp, (rows, d), torch.bfloat16)
+        counts_recv = heap.tensor(off_cnt, (e,), torch.int32)
+        Hh = torch.empty(rows, two_i, dtype=torch.bfloat16, device=dev)
+        A = torch.empty(rows, inter, dtype=torch.bfloat16, device=dev)
+        G.grouped_linear(xp_recv, w_gu.view(e_loc * two_i, d), counts_recv, out=Hh, epi="swiglu", c2=A, n_w=e_loc)
+        y_recv = heap.tensor(off_y, (rows, d), torch.bfloat16)
+        G.grouped_linear(A, w_d.view(e_loc * d, inter), counts_recv, out=y_recv, n_w=e_loc)
+        ey = heap.next_epoch(_Y)
+        ext().ep_signal(heap.peers, my, 0, _Y, ey)
+        ext().ep_wait(heap.peers, my, 0, _Y, ey, err_flag(dev))
+        out = torch.empty(t, d, dtype=torch.bfloat16, device=dev)
+        y_local = torch.empty(rows, d, dtype=torch.bfloat16, device=dev)
+        ext().ep_combine_pull(sel, slot, _c(comb.detach().float()), None if residual is None else _c(residual), out,
+                              y_local, heap.peers, my, e_loc, cap, off_y)
+        ctx.save_for_backward(xp_recv, Hh, A, y_local, sel, slot, perm, wperm, counts, counts_recv)
+        ctx.w_gu, ctx.w_d, ctx.cap, ctx.act, ctx.t, ctx.heap = w_gu, w_d, cap, _ACT[act], t, heap
+        ctx.has_res = residual is not None
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        from ..ops import gemm as G
+        from ..ops._ext import err_flag, ext
+        from ..ops.cuda_fns import _c, _mg
+
+        xp_recv, Hh, A, y_local, sel, slot, perm, wperm, counts, counts_recv = ctx.saved_tensors
+        dout = _c(dout)
+        w_gu, w_d, cap, heap = ctx.w_gu, ctx.w_d, ctx.cap, ctx.heap
+        e_loc, two_i, d = w_gu.shape
+        inter = two_i // 2
+        dev = dout.device
+        my = heap.my
+        e = e_loc * heap.world
+        rows = e * cap
+        off_dy = heap.alloc("dy", rows * d * 2)
+        off_dxp = heap.alloc("dxp", rows * d * 2)
+        dcomb = torch.empty(sel.shape, dtype=torch.float32, device=dev)
+        ext().combine_bwd(dout, y_local, sel, slot, perm, wperm, counts, cap, None, dcomb)
+        edy = heap.next_epoch(_DY)
+        ext().ep_combine_bwd_push(dout, perm, wperm, counts, heap.peers, my, e_loc, cap, off_dy, 0, _DY, edy,
+                                  heap.counter(_DY))
+        ext().ep_wait(heap.peers, my, 0, _DY, edy, err_flag(dev))
+        dy_recv = heap.tensor(off_dy, (rows, d), torch.bfloat16)
+        # the receive buffers are reused by the next exchange: weight gradients run now, never deferred
+        with G.defer_weight_grads(None):
+            dA = G.grouped_linear_dx(dy_recv, w_d.view(e_loc * d, inter), counts_recv, n_w=e_loc)
+            G.grouped_linear_dw(dy_recv, A, counts_recv, out=_mg(w_d).view(e_loc * d, inter), n_w=e_loc)
+            dH = torch.empty_like(Hh)
+            ext().swiglu_bwd(dA, Hh, dH, ctx.act, counts_recv, cap)
+            dxp = heap.tensor(off_dxp, (rows, d), torch.bfloat16)
+            G.grouped_linear_dx(dH, w_gu.view(e_loc * two_i, d), counts_recv, out=dxp, n_w=e_loc)
+            G.grouped_linear_dw(dH, xp_recv, counts_recv, out=_mg(w_gu).view(e_loc * two_i, d), n_w=e_loc)
+        exp_ = heap.next_epoch(_DXP)
+        ext().ep_signal(heap.peers, my, 0, _DXP, exp_)
+        ext().ep_wait(heap.peers, my, 0, _DXP, exp_, err_flag(dev))
+        dh = torch.empty(ctx.t, d, dtype=torch.bfloat16, device=dev)
+        ext().ep_unpermute_pull(sel, slot, dh, heap.peers, my, e_loc, cap, off_dxp)
+        ctx.w_gu = ctx.w_d = ctx.heap = None
+        return (dh, dcomb, None, None, (dout if ctx.has_res else None), None, None, None, None, None, None, None)
+
+
 def _moe_ep_cpu(h, r, w_gu, w_d, cap, group, residual, act):
     """Differentiable CPU/gloo version (torch ops + autograd all-to-all); the oracle of the GPU path."""
     from torch.distributed.nn.functional import all_to_all_single
@@ -126,10 +233,20 @@ def _moe_ep_cpu(h, r, w_gu, w_d, cap, group, residual, act):
     return out if residual is None else residual + out
 
 
-def moe_experts_ep(h, r, w_gate_up, w_down, capacity, group, residual=None, act: str = "silu"):
+def ep_impl() -> str:
+    """``peer`` (default on GPUs): exchange inside the kernels over NVLink peer memory;
+    ``nccl``: the same capacity layout moved by NCCL all-to-alls (the baseline path)."""
+    return os.environ.get("MXK_EP_IMPL", "peer")
+
+
+def moe_experts_ep(h, r, w_gate_up, w_down, capacity, group, residual=None, act: str = "silu", layer: int = 0,
+                   n_layers: int = 1):
     t = h.shape[0]
     cap = capacity if capacity is not None else ops.capacity_for(t, r.selected.shape[1], 1, 1.0)
     if not h.is_cuda:
         return _moe_ep_cpu(h, r, w_gate_up, w_down, cap, group, residual, act)
     keep = None if r.keep is None else r.keep.to(torch.uint8)
+    if ep_impl() == "peer" and dist.get_world_size(group) <= 16:
+        return _MoEEPFused.apply(h, r.combine, w_gate_up, w_down, residual, r.selected, keep, cap, group, act, layer,
+                                 n_layers)
     return _MoEEP.apply(h, r.combine, w_gate_up, w_down, residual, r.selected, keep, cap, group, act)

@@ -88,3 +88,80 @@ def test_ep_gpu_matches_single_gpu():
         p.join(timeout=60)
     for r in range(world):
         assert all(v < 2e-2 for v in results[r]), (r, results[r])
+
+
+def _worker_impls(rank, world, port, q):
+    """Peer-memory exchange vs NCCL all-to-all on the same inputs: 2 layers x 3 iterations of
+    forward + backward (exercises the per-layer buffers, shared buffers and epochs)."""
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from marin_experiments_b200.ops import api
+        from marin_experiments_b200.ops._ext import check_kernel_errors
+        from marin_experiments_b200.parallel import ep
+
+        dev = torch.device("cuda", rank)
+        t, d, inter, e, k = 512, 256, 256, 8, 2
+        e_loc = e // world
+        lo, hi = rank * e_loc, (rank + 1) * e_loc
+
+        def param(x):
+            p = x.to(dev).requires_grad_(True)
+            p.main_grad = torch.zeros(x.shape, dtype=torch.float32, device=dev)
+            return p
+
+        g = torch.Generator().manual_seed(3)
+        layers = [((torch.randn(e, d, generator=g) / 8).bfloat16(), (torch.randn(e, 2 * inter, d, generator=g) / 16).bfloat16(),
+                   (torch.randn(e, d, inter, generator=g) / 16).bfloat16()) for _ in range(2)]
+        gx = torch.Generator().manual_seed(100 + rank)
+        xs = [torch.randn(t, d, generator=gx).bfloat16() for _ in range(3)]
+        gouts = [torch.randn(t, d, generator=gx).bfloat16() for _ in range(3)]
+        res = {}
+        for impl in ("nccl", "peer"):
+            os.environ["MXK_EP_IMPL"] = impl
+            params = [(param(wr), param(wgu[lo:hi]), param(wdn[lo:hi])) for wr, wgu, wdn in layers]
+            outs, grads = [], []
+            for it in range(3):
+                h0 = xs[it].to(dev).requires_grad_(True)
+                h = h0
+                for li, (wr, wg, wd) in enumerate(params):
+                    r = api.route(h, wr, torch.zeros(e, device=dev), k, qb_count=32)
+                    h = ep.moe_experts_ep(h, r, wg, wd, api.capacity_for(t, k, e, 2.0), dist.group.WORLD, residual=h,
+                                          layer=li, n_layers=2)
+                h.backward(gouts[it].to(dev))
+                outs.append(h.detach().float().cpu())
+                grads.append(h0.grad.float().cpu())
+            torch.cuda.synchronize()
+            check_kernel_errors()
+            res[impl] = (outs, grads, [p[1].main_grad.cpu() for p in params], [p[2].main_grad.cpu() for p in params])
+
+        def rel(a, b):
+            return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
+
+        errs = [rel(a, b) for a, b in zip(res["peer"][0] + res["peer"][1] + res["peer"][2] + res["peer"][3],
+                                          res["nccl"][0] + res["nccl"][1] + res["nccl"][2] + res["nccl"][3])]
+        q.put((rank, errs))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_peer_exchange_matches_nccl():
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 4)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_impls, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert all(v < 1e-2 for v in results[r]), (r, results[r])
