@@ -1,0 +1,456 @@
+// Flash-attention backward on the 5th-generation tensor cores (sm_100a).
+//
+// CTA = one 128-key block j of one KV head (all query heads of its GQA group). For every visible
+// 128-query block i of every head of the group:
+//   S^T  = K_j Q_i^T                 (SS MMA, keys on TMEM lanes, fp32, cols [0,128))
+//   dP^T = V_j dO_i^T                (SS MMA, cols [128,256))
+//   P^T  = exp2(S^T c - lse_i)       (compute warps: thread = key row; bf16 over S^T cols [0,64))
+//   dS^T = P^T (dP^T - D_i) * scale  (bf16 over dP^T cols [128,192), and MN-major into smem)
+//   dV  += P^T dO_i                  (TS MMA: A = P^T from TMEM, B = dO_i MN-major)
+//   dK  += dS^T Q_i                  (TS MMA: A = dS^T from TMEM, B = Q_i MN-major)
+//   dQ_i = dS K_j                    (SS MMA: A = dS from smem (MN-major), B = K_j MN-major; written
+//                                     into the free upper halves of the S^T / dP^T regions)
+// dQ partials are added into an fp32 accumulator with vector atomics by four epilogue warps; dK and
+// dV leave TMEM once, after the last block. Warps: 0-3 compute, 4 MMA (one elected thread), 5 TMA +
+// per-query scalars, 6-9 dQ epilogue. Every wait is bounded and records an error code on timeout.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.h"
+#include "sm100_primitives.cuh"
+
+namespace mxk {
+namespace fab100 {
+
+constexpr int BM = 128;  // queries per block
+constexpr int BN = 128;  // keys per CTA
+constexpr int kThreads = 320;
+
+struct BwdArgs {
+  int B, S, H, Hkv, window;
+  float scale, scale_log2;
+  const int* seg;
+  const float* lse;   // [T, H] natural-log logsumexp of the forward
+  const float* dsum;  // [T, H] rowsum(dO * O)
+  float* dq_acc;      // [T, H, HD] fp32
+  __nv_bfloat16* dk;
+  long dk_tok, dk_head;
+  __nv_bfloat16* dv;
+  long dv_tok, dv_head;
+  int dv_accumulate;
+  int* err;
+};
+
+template <int HD>
+struct Smem {
+  static constexpr int KCH = (HD + 63) / 64;
+  static constexpr int kTile = KCH * 128 * 128;  // [KCH chunks][128 rows][128 B]
+  static constexpr int kDS = 2 * 128 * 128;      // dS: 2 query chunks x 128 key rows x 128 B
+  // K, V, Q[2], dO[2], dS, then scalars and barriers
+  static constexpr int kScal = 2 * 3 * BM * 4;   // [2 buffers][lse2, dsum, key-lo] x 128
+  static constexpr int kBytes = 6 * kTile + kDS + kScal + 256 + 1024;
+};
+
+// TMEM columns
+constexpr uint32_t kColS = 0, kColDP = 128;
+template <int HD>
+struct Cols {
+  static constexpr uint32_t dV = 256;
+  static constexpr uint32_t dK = 256 + HD;
+  // dQ halves (64-column chunks of the head dim): first into the free half of S^T, second into the
+  // free half of dP^T; head_dim 64 has room after dK instead.
+  static constexpr uint32_t dQ0 = HD == 64 ? 256 + 2 * HD : 64;
+  static constexpr uint32_t dQ1 = 192;
+};
+
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// First key visible to query qi (window / segment start), and whether qi is a real position.
+__device__ __forceinline__ int query_key_lo(int qi, int S, int window, const int* seg, int base) {
+  if (qi >= S) return 1 << 30;
+  int lo = 0;
+  if (window > 0) lo = max(lo, qi - window + 1);
+  if (seg) {
+    const int sid = seg[base + qi];
+    int a = 0, b = qi;
+    while (a < b) {
+      const int m = (a + b) >> 1;
+      if (seg[base + m] == sid) b = m; else a = m + 1;
+    }
+    lo = max(lo, a);
+  }
+  return lo;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                        const BwdArgs a) {
+  using SM = Smem<HD>;
+  using C = Cols<HD>;
+  constexpr int KCH = SM::KCH;
+  constexpr uint32_t tile = SM::kTile;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + tile;
+  uint8_t* sQ = smem + 2 * tile;   // [2]
+  uint8_t* sO = smem + 4 * tile;   // [2] (dO)
+  uint8_t* sDS = smem + 6 * tile;  // dS, MN-major: [2 query chunks][128 key rows][128 B]
+  float* sScal = reinterpret_cast<float*>(sDS + SM::kDS);  // [2][3][128]: lse2, dsum, key-lo (as int)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sScal + 2 * 3 * BM);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qd_full = bars + 1;   // [2]
+  uint64_t* qd_empty = bars + 3;  // [2]
+  uint64_t* ld_full = bars + 5;   // [2]
+  uint64_t* sdp_full = bars + 7;
+  uint64_t* p_ready = bars + 8;
+  uint64_t* mma_done = bars + 9;
+  uint64_t* dq_full = bars + 10;
+  uint64_t* dq_free = bars + 11;
+  uint64_t* kv_done = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+  const int rep = a.H / a.Hkv;
+  const int base = b * a.S;
+  const int k0 = j * BN;
+  const int nqb = (a.S + BM - 1) / BM;
+  int i_lo = k0 / BM;
+  int i_hi = nqb - 1;
+  if (a.window > 0) i_hi = min(i_hi, (k0 + BN - 1 + a.window - 1) / BM);
+  const int n_i = k0 < a.S ? max(i_hi - i_lo + 1, 0) : 0;
+  const int n_it = rep * n_i;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&qd_full[t], 1);
+      mbar_init(&qd_empty[t], 1);
+      mbar_init(&ld_full[t], 32);
+    }
+    mbar_init(sdp_full, 1);
+    mbar_init(p_ready, 128);
+    mbar_init(mma_done, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
+    mbar_init(kv_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 5) {
+    // ------------------------------------------------------------------ TMA + per-query scalars
+    if (n_it > 0) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(kv_full, 2 * tile);
+        for (int c = 0; c < KCH; ++c) {
+          tma_load_2d(&tmK, kv_full, sK + c * BN * 128, kh * HD + c * 64, base + k0);
+          tma_load_2d(&tmV, kv_full, sV + c * BN * 128, kh * HD + c * 64, base + k0);
+        }
+      }
+      for (int it = 0; it < n_it; ++it) {
+        const int buf = it & 1;
+        const int h = kh * rep + it / n_i;
+        const int q0 = (i_lo + it % n_i) * BM;
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait(&qd_empty[buf], ((it >> 1) & 1) ^ 1, a.err, kErrTimeoutProducer, abort_flag);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&qd_full[buf], 2 * tile);
+          for (int c = 0; c < KCH; ++c) {
+            tma_load_2d(&tmQ, &qd_full[buf], sQ + buf * tile + c * BM * 128, h * HD + c * 64, base + q0);
+            tma_load_2d(&tmO, &qd_full[buf], sO + buf * tile + c * BM * 128, h * HD + c * 64, base + q0);
+          }
+        }
+        float* sc = sScal + buf * 3 * BM;
+#pragma unroll
+        for (int u = 0; u < BM / 32; ++u) {
+          const int q = u * 32 + lane, qi = q0 + q;
+          const bool in = qi < a.S;
+          const long idx = (long)(base + qi) * a.H + h;
+          sc[q] = in ? a.lse[idx] * 1.4426950408889634f : INFINITY;
+          sc[BM + q] = in ? a.dsum[idx] : 0.f;
+          reinterpret_cast<int*>(sc)[2 * BM + q] = query_key_lo(qi, a.S, a.window, a.seg, base);
+        }
+        __syncwarp();
+        mbar_arrive(&ld_full[buf]);
+      }
+    }
+  } else if (warp == 4) {
+    // ------------------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_it > 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(BN, BM, false, false);  // keys x queries
+      constexpr uint32_t idesc_kv = make_idesc_bf16(BN, HD, false, true);  // keys x head_dim
+      constexpr uint32_t idesc_q0 = make_idesc_bf16(BM, 64, true, true);   // queries x 64
+      constexpr uint32_t idesc_q1 = make_idesc_bf16(BM, HD > 64 ? HD - 64 : 64, true, true);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), ds_addr = smem_u32(sDS);
+      bool ok = mbar_wait(kv_full, 0, a.err, kErrTimeoutMma, abort_flag);
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int buf = it & 1;
+        const uint32_t q_addr = smem_u32(sQ + buf * tile), o_addr = smem_u32(sO + buf * tile);
+        if (!mbar_wait(&qd_full[buf], (it >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
+        if (it > 0) {
+          // S^T / dP^T overwrite P^T / dS^T / dQ of the previous block
+          if (!mbar_wait(mma_done, (it - 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
+          if (!mbar_wait(dq_free, (it - 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t off = (ks / 4) * 128 * 128 + (ks % 4) * 32;
+          umma_bf16(tmem + kColS, make_sdesc(k_addr + off, 16, 1024), make_sdesc(q_addr + off, 16, 1024), idesc_s,
+                    ks > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t off = (ks / 4) * 128 * 128 + (ks % 4) * 32;
+          umma_bf16(tmem + kColDP, make_sdesc(v_addr + off, 16, 1024), make_sdesc(o_addr + off, 16, 1024), idesc_s,
+                    ks > 0 ? 1u : 0u);
+        }
+        umma_commit(sdp_full);
+        if (!mbar_wait(p_ready, it & 1, a.err, kErrTimeoutMma, abort_flag)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < BM / 16; ++ks) {
+          umma_ts(tmem + C::dV, tmem + kColS + ks * 8, make_sdesc(o_addr + ks * 2048, BM * 128, 1024), idesc_kv,
+                  (it > 0 || ks > 0) ? 1u : 0u);
+          umma_ts(tmem + C::dK, tmem + kColDP + ks * 8, make_sdesc(q_addr + ks * 2048, BM * 128, 1024), idesc_kv,
+                  (it > 0 || ks > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int ks = 0; ks < BN / 16; ++ks)
+          umma_bf16(tmem + C::dQ0, make_sdesc(ds_addr + ks * 2048, 128 * 128, 1024),
+                    make_sdesc(k_addr + ks * 2048, BN * 128, 1024), idesc_q0, ks > 0 ? 1u : 0u);
+        if (HD > 64) {
+#pragma unroll
+          for (int ks = 0; ks < BN / 16; ++ks)
+            umma_bf16(tmem + C::dQ1, make_sdesc(ds_addr + ks * 2048, 128 * 128, 1024),
+                      make_sdesc(k_addr + BN * 128 + ks * 2048, BN * 128, 1024), idesc_q1, ks > 0 ? 1u : 0u);
+        }
+        umma_commit(mma_done);
+        umma_commit(dq_full);
+        umma_commit(&qd_empty[buf]);
+      }
+      umma_commit(kv_done);
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------------------- dQ epilogue
+    const int quarter = warp & 3;
+    const int q = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    for (int it = 0; it < n_it; ++it) {
+      const bool got = mbar_wait(dq_full, it & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      float v[HD];
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) tmem_ld32(tmem + C::dQ0 + lane_off + c, v + c);
+      if (HD == 96) tmem_ld32(tmem + C::dQ1 + lane_off, v + 64);
+      if (HD == 128) {
+        tmem_ld32(tmem + C::dQ1 + lane_off, v + 64);
+        tmem_ld32(tmem + C::dQ1 + lane_off + 32, v + 96);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(dq_free);
+      const int h = kh * rep + it / n_i;
+      const int qi = (i_lo + it % n_i) * BM + q;
+      if (qi < a.S) {
+        float4* dst = reinterpret_cast<float4*>(a.dq_acc + ((long)(base + qi) * a.H + h) * HD);
+#pragma unroll
+        for (int c = 0; c < HD / 4; ++c) atomicAdd(dst + c, make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]));
+      }
+    }
+  } else {
+    // -------------------------------------------------------------------------- compute warps
+    const int kr = warp * 32 + lane;
+    const int kj = k0 + kr;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t t_s = tmem + kColS + lane_off, t_dp = tmem + kColDP + lane_off;
+    uint8_t* ds_row = sDS + kr * 128;
+    const int sw = kr & 7;
+    bool alive = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int buf = it & 1;
+      const int q0 = (i_lo + it % n_i) * BM;
+      bool got = mbar_wait(&ld_full[buf], (it >> 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      got = got && mbar_wait(sdp_full, it & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+      tc_fence_after();
+      const float* sc = sScal + buf * 3 * BM;
+      const int* klo = reinterpret_cast<const int*>(sc + 2 * BM);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float s[32], dp[32];
+        tmem_ld32(t_s + 32 * c, s);
+        tmem_ld32(t_dp + 32 * c, dp);
+        tmem_wait_ld();
+        uint32_t pw[16], dw[16];
+#pragma unroll
+        for (int u = 0; u < 32; u += 2) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int qq = 32 * c + u + e;
+            const int qi = q0 + qq;
+            const bool vis = kj <= qi && kj >= klo[qq] && kj < a.S;
+            const float p = vis ? exp2f(fmaf(s[u + e], a.scale_log2, -sc[qq])) : 0.f;
+            pv[e] = p;
+            dv[e] = p * (dp[u + e] - sc[BM + qq]) * a.scale;
+          }
+          pw[u / 2] = pack_bf16x2(pv[0], pv[1]);
+          dw[u / 2] = pack_bf16x2(dv[0], dv[1]);
+        }
+        tmem_st16(t_s + 16 * c, pw);
+        tmem_st16(t_dp + 16 * c, dw);
+        // dS row into the MN-major operand (query chunk c/2, 16-byte units (c%2)*4 .. +3, swizzled)
+        uint8_t* chunk = ds_row + (c >> 1) * 128 * 128;
+#pragma unroll
+        for (int v4 = 0; v4 < 4; ++v4) {
+          const int unit = (c & 1) * 4 + v4;
+          *reinterpret_cast<uint4*>(chunk + ((unit ^ sw) << 4)) =
+              make_uint4(dw[4 * v4], dw[4 * v4 + 1], dw[4 * v4 + 2], dw[4 * v4 + 3]);
+        }
+      }
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_ready);
+    }
+    // ---- dK, dV out (once per CTA)
+    if (k0 < a.S) {
+      bool have = n_it > 0 && alive;
+      if (have) {
+        const bool got = mbar_wait(kv_done, 0, a.err, kErrTimeoutEpilogue, abort_flag);
+        have = __all_sync(0xffffffffu, got);
+        tc_fence_after();
+      }
+      if (n_it == 0 || have) {
+        __nv_bfloat16* dvr = a.dv + (long)(base + kj) * a.dv_tok + (long)kh * a.dv_head;
+        __nv_bfloat16* dkr = a.dk + (long)(base + kj) * a.dk_tok + (long)kh * a.dk_head;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 16) {
+          float vv[16], kk[16];
+          if (have) {
+            tmem_ld16(tmem + C::dV + lane_off + c, vv);
+            tmem_ld16(tmem + C::dK + lane_off + c, kk);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int u = 0; u < 16; ++u) vv[u] = kk[u] = 0.f;
+          }
+          if (kj < a.S) {
+            uint32_t pv[8], pk[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              float v0 = vv[2 * u], v1 = vv[2 * u + 1];
+              if (a.dv_accumulate) {
+                const __nv_bfloat162 old = reinterpret_cast<const __nv_bfloat162*>(dvr + c)[u];
+                v0 += __bfloat162float(old.x);
+                v1 += __bfloat162float(old.y);
+              }
+              pv[u] = pack_bf16x2(v0, v1);
+              pk[u] = pack_bf16x2(kk[2 * u], kk[2 * u + 1]);
+            }
+            reinterpret_cast<uint4*>(dvr + c)[0] = make_uint4(pv[0], pv[1], pv[2], pv[3]);
+            reinterpret_cast<uint4*>(dvr + c)[1] = make_uint4(pv[4], pv[5], pv[6], pv[7]);
+            reinterpret_cast<uint4*>(dkr + c)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            reinterpret_cast<uint4*>(dkr + c)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fab100
+
+bool make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner,
+                       int box_outer);
+
+template <int HD>
+static int run_fa_bwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
+  using namespace fab100;
+  CUtensorMap tq, tk, tv, to;
+  const long T = (long)L.B * L.S;
+  if (!make_tmap_bf16_2d(&tq, L.q, (long)L.H * HD, T, L.q_tok, 64, BM)) return kErrBadArgsHost;
+  if (!make_tmap_bf16_2d(&tk, L.k, (long)L.Hkv * HD, T, L.k_tok, 64, BN)) return kErrBadArgsHost;
+  if (!make_tmap_bf16_2d(&tv, L.v, (long)L.Hkv * HD, T, L.v_tok, 64, BN)) return kErrBadArgsHost;
+  if (!make_tmap_bf16_2d(&to, L.dout, (long)L.H * HD, T, (long)L.H * HD, 64, BM)) return kErrBadArgsHost;
+  BwdArgs a{};
+  a.B = L.B; a.S = L.S; a.H = L.H; a.Hkv = L.Hkv; a.window = L.window;
+  a.scale = L.scale;
+  a.scale_log2 = L.scale * 1.4426950408889634f;
+  a.seg = L.seg;
+  a.lse = L.lse;
+  a.dsum = L.dsum;
+  a.dq_acc = L.dq_acc;
+  a.dk = (__nv_bfloat16*)L.dk; a.dk_tok = L.dk_tok; a.dk_head = L.dk_head;
+  a.dv = (__nv_bfloat16*)L.dv; a.dv_tok = L.dv_tok; a.dv_head = L.dv_head;
+  a.dv_accumulate = L.dv_accumulate;
+  a.err = err;
+  constexpr int smem = Smem<HD>::kBytes;
+  static_assert(smem <= 232448, "shared memory budget");
+  static bool init = false;
+  if (!init) {
+    if (cudaFuncSetAttribute(fa_bwd_sm100_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return kErrBadArgsHost;
+    init = true;
+  }
+  dim3 grid((L.S + BN - 1) / BN, L.Hkv, L.B);
+  count_launch();
+  fa_bwd_sm100_kernel<HD><<<grid, kThreads, smem, st>>>(tq, tk, tv, to, a);
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
+}
+
+// Same contract as launch_flash_bwd (dsum / dq_acc preparation and the final dq conversion are
+// shared with it), with the tcgen05 kernel for the main pass.
+int launch_flash_bwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
+  if (L.q_head != L.hd || L.k_head != L.hd || L.v_head != L.hd) return kErrBadArgsHost;
+  if ((L.q_tok * 2) % 16 || (L.k_tok * 2) % 16 || (L.v_tok * 2) % 16) return kErrBadArgsHost;
+  if ((reinterpret_cast<uintptr_t>(L.q) | reinterpret_cast<uintptr_t>(L.k) | reinterpret_cast<uintptr_t>(L.v) |
+       reinterpret_cast<uintptr_t>(L.dout)) & 15)
+    return kErrBadArgsHost;
+  if ((L.dk_tok | L.dk_head | L.dv_tok | L.dv_head) % 8) return kErrBadArgsHost;  // 16-byte row stores
+  int r = launch_flash_bwd_prep(L, st);
+  if (r) return r;
+  switch (L.hd) {
+    case 64: r = run_fa_bwd_sm100<64>(L, err, st); break;
+    case 96: r = run_fa_bwd_sm100<96>(L, err, st); break;
+    case 128: r = run_fa_bwd_sm100<128>(L, err, st); break;
+    default: return kErrBadArgsHost;
+  }
+  if (r) return r;
+  return launch_dq_convert(L, st);
+}
+
+}  // namespace mxk
