@@ -1,4 +1,4 @@
-"""Attention kernels: tcgen05 forward vs the mma.sync forward/backward, causal, 16 heads x 96.
+"""Attention kernels: tcgen05 forward/backward vs the mma.sync ones, causal, 16 heads x 96.
 
 Usage: python -m marin_experiments_b200.benchmarks.attn_bench
 """
@@ -32,6 +32,8 @@ def run(b=8, s=2048, h=16, hkv=16, hd=96, iters=10):
         ("fwd_mma_sync", lambda: ext().flash_fwd(q, k, v, o, lse, None, b, s, 0, sc), fl),
         ("bwd_mma_sync", lambda: ext().flash_bwd(q, k, v, o, lse, None, b, s, 0, sc, do, ds, dqa, dq, dk, dv, False),
          2.5 * fl),
+        ("bwd_tcgen05", lambda: ext().flash_bwd_sm100(q, k, v, o, lse, None, b, s, 0, sc, do, ds, dqa, dq, dk, dv,
+                                                      False, err_flag(q.device)), 2.5 * fl),
     ]:
         for _ in range(3):
             fn()

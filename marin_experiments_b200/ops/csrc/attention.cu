@@ -583,6 +583,32 @@ int launch_flash_fwd(const AttnLaunch& L, cudaStream_t st) {
   }
 }
 
+// dsum = rowsum(dO * O) and dq_acc = 0 for the tcgen05 backward (attention_bwd_sm100.cu).
+int launch_flash_bwd_prep(const AttnLaunch& L, cudaStream_t st) {
+  AttnParams p{};
+  p.o = (__nv_bfloat16*)L.o;
+  p.H = L.H;
+  p.dout = (const __nv_bfloat16*)L.dout;
+  p.dsum = L.dsum;
+  p.dq_acc = L.dq_acc;
+  const long T = (long)L.B * L.S;
+  count_launch();
+  switch (L.hd) {
+    case 64: flash_bwd_prep_kernel<64><<<148 * 8, 256, 0, st>>>(p, T); break;
+    case 96: flash_bwd_prep_kernel<96><<<148 * 8, 256, 0, st>>>(p, T); break;
+    case 128: flash_bwd_prep_kernel<128><<<148 * 8, 256, 0, st>>>(p, T); break;
+    default: return kErrBadArgsHost;
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
+}
+
+int launch_dq_convert(const AttnLaunch& L, cudaStream_t st) {
+  const long n = (long)L.B * L.S * L.H * L.hd;
+  count_launch();
+  dq_convert_kernel<<<148 * 8, 256, 0, st>>>(L.dq_acc, (__nv_bfloat16*)L.dq, n);
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
+}
+
 int launch_flash_bwd(const AttnLaunch& L, cudaStream_t st) {
   AttnParams p{};
   p.q = (const __nv_bfloat16*)L.q;

@@ -48,9 +48,12 @@ struct Smem {
   static constexpr int KCH = (HD + 63) / 64;
   static constexpr int kTile = KCH * 128 * 128;  // [KCH chunks][128 rows][128 B]
   static constexpr int kDS = 2 * 128 * 128;      // dS: 2 query chunks x 128 key rows x 128 B
-  // K, V, Q[2], dO[2], dS, then scalars and barriers
-  static constexpr int kScal = 2 * 3 * BM * 4;   // [2 buffers][lse2, dsum, key-lo] x 128
-  static constexpr int kBytes = 6 * kTile + kDS + kScal + 256 + 1024;
+  // K, V, Q[2], dO[2], dS, then per-query scalars and barriers. The tiles need 1024-byte alignment;
+  // the dynamic shared memory base is expected to have it (the kernel checks and reports otherwise).
+  static constexpr int kScal = 2 * BM * (4 + 4 + 2);  // [2 buffers] x 128 x (lse2 f32, dsum f32, key-lo i16)
+  static constexpr int kBars = 128;
+  static constexpr int kUsed = 6 * kTile + kDS + kScal + kBars;
+  static constexpr int kBytes = kUsed + 128;
 };
 
 // TMEM columns
@@ -102,14 +105,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int KCH = SM::KCH;
   constexpr uint32_t tile = SM::kTile;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  if (pad + SM::kUsed > SM::kBytes) {  // misaligned base: report instead of overrunning shared memory
+    if (threadIdx.x == 0) atomicExch(a.err, kErrBadArgs);
+    return;
+  }
+  uint8_t* smem = smem_raw + pad;
   uint8_t* sK = smem;
   uint8_t* sV = smem + tile;
   uint8_t* sQ = smem + 2 * tile;   // [2]
   uint8_t* sO = smem + 4 * tile;   // [2] (dO)
   uint8_t* sDS = smem + 6 * tile;  // dS, MN-major: [2 query chunks][128 key rows][128 B]
-  float* sScal = reinterpret_cast<float*>(sDS + SM::kDS);  // [2][3][128]: lse2, dsum, key-lo (as int)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sScal + 2 * 3 * BM);
+  float* sLse = reinterpret_cast<float*>(sDS + SM::kDS);  // [2][128] lse in log2 units
+  float* sDsum = sLse + 2 * BM;                             // [2][128]
+  short* sKlo = reinterpret_cast<short*>(sDsum + 2 * BM);   // [2][128] first visible key
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKlo + 2 * BM);
   uint64_t* kv_full = bars + 0;
   uint64_t* qd_full = bars + 1;   // [2]
   uint64_t* qd_empty = bars + 3;  // [2]
@@ -184,15 +194,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(&tmO, &qd_full[buf], sO + buf * tile + c * BM * 128, h * HD + c * 64, base + q0);
           }
         }
-        float* sc = sScal + buf * 3 * BM;
 #pragma unroll
         for (int u = 0; u < BM / 32; ++u) {
           const int q = u * 32 + lane, qi = q0 + q;
           const bool in = qi < a.S;
           const long idx = (long)(base + qi) * a.H + h;
-          sc[q] = in ? a.lse[idx] * 1.4426950408889634f : INFINITY;
-          sc[BM + q] = in ? a.dsum[idx] : 0.f;
-          reinterpret_cast<int*>(sc)[2 * BM + q] = query_key_lo(qi, a.S, a.window, a.seg, base);
+          sLse[buf * BM + q] = in ? a.lse[idx] * 1.4426950408889634f : INFINITY;
+          sDsum[buf * BM + q] = in ? a.dsum[idx] : 0.f;
+          sKlo[buf * BM + q] = (short)min(query_key_lo(qi, a.S, a.window, a.seg, base), 32767);
         }
         __syncwarp();
         mbar_arrive(&ld_full[buf]);
@@ -243,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ks = 0; ks < BN / 16; ++ks)
           umma_bf16(tmem + C::dQ0, make_sdesc(ds_addr + ks * 2048, 128 * 128, 1024),
                     make_sdesc(k_addr + ks * 2048, BN * 128, 1024), idesc_q0, ks > 0 ? 1u : 0u);
-        if (HD > 64) {
+        if constexpr (HD > 64) {
 #pragma unroll
           for (int ks = 0; ks < BN / 16; ++ks)
             umma_bf16(tmem + C::dQ1, make_sdesc(ds_addr + ks * 2048, 128 * 128, 1024),
@@ -265,13 +274,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
       float v[HD];
-#pragma unroll
-      for (int c = 0; c < 64; c += 32) tmem_ld32(tmem + C::dQ0 + lane_off + c, v + c);
-      if (HD == 96) tmem_ld32(tmem + C::dQ1 + lane_off, v + 64);
-      if (HD == 128) {
-        tmem_ld32(tmem + C::dQ1 + lane_off, v + 64);
-        tmem_ld32(tmem + C::dQ1 + lane_off + 32, v + 96);
-      }
+      using R32 = float(&)[32];
+      tmem_ld32(tmem + C::dQ0 + lane_off, reinterpret_cast<R32>(v[0]));
+      tmem_ld32(tmem + C::dQ0 + lane_off + 32, reinterpret_cast<R32>(v[32]));
+      if constexpr (HD >= 96) tmem_ld32(tmem + C::dQ1 + lane_off, reinterpret_cast<R32>(v[64]));
+      if constexpr (HD == 128) tmem_ld32(tmem + C::dQ1 + lane_off + 32, reinterpret_cast<R32>(v[96]));
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(dq_free);
@@ -299,8 +306,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       got = got && mbar_wait(sdp_full, it & 1, a.err, kErrTimeoutEpilogue, abort_flag);
       if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
       tc_fence_after();
-      const float* sc = sScal + buf * 3 * BM;
-      const int* klo = reinterpret_cast<const int*>(sc + 2 * BM);
+      const float* lse2 = sLse + buf * BM;
+      const float* dsq = sDsum + buf * BM;
+      const short* klo = sKlo + buf * BM;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float s[32], dp[32];
@@ -315,10 +323,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 2; ++e) {
             const int qq = 32 * c + u + e;
             const int qi = q0 + qq;
-            const bool vis = kj <= qi && kj >= klo[qq] && kj < a.S;
-            const float p = vis ? exp2f(fmaf(s[u + e], a.scale_log2, -sc[qq])) : 0.f;
+            const bool vis = kj <= qi && kj >= (int)klo[qq] && kj < a.S;
+            const float p = vis ? exp2f(fmaf(s[u + e], a.scale_log2, -lse2[qq])) : 0.f;
             pv[e] = p;
-            dv[e] = p * (dp[u + e] - sc[BM + qq]) * a.scale;
+            dv[e] = p * (dp[u + e] - dsq[qq]) * a.scale;
           }
           pw[u / 2] = pack_bf16x2(pv[0], pv[1]);
           dw[u / 2] = pack_bf16x2(dv[0], dv[1]);
@@ -441,6 +449,7 @@ int launch_flash_bwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
        reinterpret_cast<uintptr_t>(L.dout)) & 15)
     return kErrBadArgsHost;
   if ((L.dk_tok | L.dk_head | L.dv_tok | L.dv_head) % 8) return kErrBadArgsHost;  // 16-byte row stores
+  if (L.S >= 32767) return kErrBadArgsHost;  // first-visible-key indices are kept as int16
   int r = launch_flash_bwd_prep(L, st);
   if (r) return r;
   switch (L.hd) {

@@ -97,6 +97,10 @@ int launch_flash_fwd(const AttnLaunch& L, cudaStream_t st);
 int launch_flash_bwd(const AttnLaunch& L, cudaStream_t st);
 // tcgen05 forward (attention_sm100.cu); q/k/v heads contiguous (head stride == hd)
 int launch_flash_fwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st);
+// tcgen05 backward (attention_bwd_sm100.cu) and the passes it shares with the mma.sync one
+int launch_flash_bwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st);
+int launch_flash_bwd_prep(const AttnLaunch& L, cudaStream_t st);
+int launch_dq_convert(const AttnLaunch& L, cudaStream_t st);
 
 // ------------------------------------------------------------ expert-parallel peer exchange (comm.cu)
 constexpr int kMaxPeers = 16;

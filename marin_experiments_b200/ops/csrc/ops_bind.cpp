@@ -200,6 +200,21 @@ void flash_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& 
   ok(mxk::launch_flash_bwd(L, stream()), "flash_bwd");
 }
 
+void flash_bwd_sm100(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& lse,
+                     const OptT& seg, int64_t B, int64_t S, int64_t window, double scale, const Tensor& dout,
+                     const Tensor& dsum, const Tensor& dq_acc, const Tensor& dq, const Tensor& dk, const Tensor& dv,
+                     bool dv_accumulate, const Tensor& err) {
+  auto L = attn_args(q, k, v, o, lse, seg, B, S, window, scale);
+  need(dout.is_contiguous() && dq.is_contiguous() && dq_acc.is_contiguous() && o.is_contiguous(),
+       "dout/o/dq/dq_acc must be contiguous");
+  need(dk.stride(2) == 1 && dv.stride(2) == 1, "dk/dv head_dim must be contiguous");
+  L.dout = dout.data_ptr(); L.dsum = dsum.data_ptr<float>(); L.dq_acc = dq_acc.data_ptr<float>();
+  L.dq = dq.data_ptr(); L.dk = dk.data_ptr(); L.dk_tok = dk.stride(0); L.dk_head = dk.stride(1);
+  L.dv = dv.data_ptr(); L.dv_tok = dv.stride(0); L.dv_head = dv.stride(1); L.dv_accumulate = dv_accumulate;
+  c10::cuda::CUDAGuard g(q.device());
+  ok(mxk::launch_flash_bwd_sm100(L, err.data_ptr<int>(), stream()), "flash_bwd_sm100");
+}
+
 // ------------------------------------------------------------------------------------- MoE
 void router_fwd(const Tensor& logits, const Tensor& bias, int64_t E, int64_t K, bool adaptive, const Tensor& theta,
                 int64_t k_min, double temp, const Tensor& sel, const Tensor& comb, const Tensor& topb,
@@ -440,6 +455,7 @@ void register_ops(pybind11::module& m) {
   m.def("opt_step", &opt_step);
   m.def("ema", &ema);
   m.def("cast_bf16", &cast_bf16);
+  m.def("flash_bwd_sm100", &flash_bwd_sm100);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", [](int64_t p) { return mxk::ipc_close(reinterpret_cast<void*>(p)); });

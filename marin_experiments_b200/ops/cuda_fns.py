@@ -242,8 +242,12 @@ class _AttentionBlock(torch.autograd.Function):
         dk = torch.empty(t, hkv, hd, dtype=BF16, device=h.device)
         dq_acc = torch.empty(t, nh, hd, dtype=F32, device=h.device)
         dsum = torch.empty(t, nh, dtype=F32, device=h.device)
-        ext().flash_bwd(qn, kn, v, o, lse, ctx.seg, shape.batch, s, shape.window, ctx.scale, _c(do), dsum, dq_acc,
-                        dq, dk, dv, dv_acc)
+        if hd in (64, 96, 128) and s < 32767:
+            ext().flash_bwd_sm100(qn, kn, v, o, lse, ctx.seg, shape.batch, s, shape.window, ctx.scale, _c(do), dsum,
+                                  dq_acc, dq, dk, dv, dv_acc, err_flag(h.device))
+        else:
+            ext().flash_bwd(qn, kn, v, o, lse, ctx.seg, shape.batch, s, shape.window, ctx.scale, _c(do), dsum, dq_acc,
+                            dq, dk, dv, dv_acc)
         ext().qk_norm_rope_bwd(dq, dk, qkvg, rstd, cos, sin, dqkvg, s, nh, hkv, hd, shape.qk_norm, shape.qk_mult)
         W = ctx.W
         dh = torch.empty(t, d, dtype=BF16, device=h.device)
