@@ -273,7 +273,8 @@ __global__ void flash_bwd_prep_kernel(const AttnParams p, long T) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
     if (lane == 0) const_cast<float*>(p.dsum)[i] = acc;
-    for (int d = lane; d < HD; d += 32) p.dq_acc[i * HD + d] = 0.f;
+    if (p.dq_acc)
+      for (int d = lane; d < HD; d += 32) p.dq_acc[i * HD + d] = 0.f;
   }
 }
 

@@ -1,18 +1,24 @@
-// Flash-attention backward on the 5th-generation tensor cores (sm_100a).
+// Flash-attention backward on the 5th-generation tensor cores (sm_100a), as two kernels so that no
+// partial gradient is ever accumulated with atomics.
 //
-// CTA = one 128-key block j of one KV head (all query heads of its GQA group). For every visible
-// 128-query block i of every head of the group:
+// dK/dV kernel -- CTA = one 128-key block j of one KV head (all query heads of its GQA group); for
+// every visible 128-query block i:
 //   S^T  = K_j Q_i^T                 (SS MMA, keys on TMEM lanes, fp32, cols [0,128))
 //   dP^T = V_j dO_i^T                (SS MMA, cols [128,256))
 //   P^T  = exp2(S^T c - lse_i)       (compute warps: thread = key row; bf16 over S^T cols [0,64))
-//   dS^T = P^T (dP^T - D_i) * scale  (bf16 over dP^T cols [128,192), and MN-major into smem)
-//   dV  += P^T dO_i                  (TS MMA: A = P^T from TMEM, B = dO_i MN-major)
-//   dK  += dS^T Q_i                  (TS MMA: A = dS^T from TMEM, B = Q_i MN-major)
-//   dQ_i = dS K_j                    (SS MMA: A = dS from smem (MN-major), B = K_j MN-major; written
-//                                     into the free upper halves of the S^T / dP^T regions)
-// dQ partials are added into an fp32 accumulator with vector atomics by four epilogue warps; dK and
-// dV leave TMEM once, after the last block. Warps: 0-3 compute, 4 MMA (one elected thread), 5 TMA +
-// per-query scalars, 6-9 dQ epilogue. Every wait is bounded and records an error code on timeout.
+//   dS^T = P^T (dP^T - D_i) * scale  (bf16 over dP^T cols [128,192))
+//   dV  += P^T dO_i, dK += dS^T Q_i  (TS MMAs: A from TMEM, B = dO_i / Q_i MN-major from smem)
+// dK and dV leave TMEM once, after the last block.
+//
+// dQ kernel -- CTA = one 128-query block i of one head; for every visible 128-key block j:
+//   S = Q_i K_j^T, dP = dO_i V_j^T  (S double-buffered in TMEM so the next block's S overlaps)
+//   dS = P (dP - D_i) * scale       (thread = query row; bf16 over the S columns)
+//   dQ += dS K_j                     (TS MMA: A = dS from TMEM, B = K_j MN-major)
+// dQ leaves TMEM once, as bf16.
+//
+// Warps (both kernels): 0-7 compute (warp w: TMEM lanes 32 (w % 4).., column half w / 4), 8 MMA (one
+// elected thread), 9 TMA (+ per-query scalars in the dK/dV kernel). Blocks that need no mask take a
+// branch-free path. Every wait is bounded and records an error code on timeout.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -26,7 +32,7 @@ namespace fab100 {
 
 constexpr int BM = 128;  // queries per block
 constexpr int BN = 128;  // keys per CTA
-constexpr int kThreads = 320;
+constexpr int kThreads = 320;  // warps 0-7 compute, 8 MMA, 9 TMA
 
 struct BwdArgs {
   int B, S, H, Hkv, window;
@@ -34,7 +40,7 @@ struct BwdArgs {
   const int* seg;
   const float* lse;   // [T, H] natural-log logsumexp of the forward
   const float* dsum;  // [T, H] rowsum(dO * O)
-  float* dq_acc;      // [T, H, HD] fp32
+  __nv_bfloat16* dq;  // [T, H, HD]
   __nv_bfloat16* dk;
   long dk_tok, dk_head;
   __nv_bfloat16* dv;
@@ -47,26 +53,28 @@ template <int HD>
 struct Smem {
   static constexpr int KCH = (HD + 63) / 64;
   static constexpr int kTile = KCH * 128 * 128;  // [KCH chunks][128 rows][128 B]
-  static constexpr int kDS = 2 * 128 * 128;      // dS: 2 query chunks x 128 key rows x 128 B
-  // K, V, Q[2], dO[2], dS, then per-query scalars and barriers. The tiles need 1024-byte alignment;
+  // K, V, Q[2], dO[2], then per-query scalars and barriers. The tiles need 1024-byte alignment;
   // the dynamic shared memory base is expected to have it (the kernel checks and reports otherwise).
-  static constexpr int kScal = 2 * BM * (4 + 4 + 2);  // [2 buffers] x 128 x (lse2 f32, dsum f32, key-lo i16)
+  static constexpr int kScal = 2 * BM * 12;  // [2 buffers] x 128 x (lse2 f32, dsum f32, key-lo i32)
   static constexpr int kBars = 128;
-  static constexpr int kUsed = 6 * kTile + kDS + kScal + kBars;
+  static constexpr int kUsed = 6 * kTile + kScal + kBars;
   static constexpr int kBytes = kUsed + 128;
 };
 
-// TMEM columns
+// TMEM columns of the dK/dV kernel
 constexpr uint32_t kColS = 0, kColDP = 128;
 template <int HD>
 struct Cols {
   static constexpr uint32_t dV = 256;
   static constexpr uint32_t dK = 256 + HD;
-  // dQ halves (64-column chunks of the head dim): first into the free half of S^T, second into the
-  // free half of dP^T; head_dim 64 has room after dK instead.
-  static constexpr uint32_t dQ0 = HD == 64 ? 256 + 2 * HD : 64;
-  static constexpr uint32_t dQ1 = 192;
 };
+
+// 2^x on the special-function unit (PTX ex2.approx.ftz.f32; -inf -> +0).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                         uint32_t accumulate) {
@@ -97,7 +105,7 @@ __device__ __forceinline__ int query_key_lo(int qi, int S, int window, const int
 
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
-    fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                         const BwdArgs a) {
   using SM = Smem<HD>;
@@ -115,10 +123,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sV = smem + tile;
   uint8_t* sQ = smem + 2 * tile;   // [2]
   uint8_t* sO = smem + 4 * tile;   // [2] (dO)
-  uint8_t* sDS = smem + 6 * tile;  // dS, MN-major: [2 query chunks][128 key rows][128 B]
-  float* sLse = reinterpret_cast<float*>(sDS + SM::kDS);  // [2][128] lse in log2 units
+  float* sLse = reinterpret_cast<float*>(smem + 6 * tile);  // [2][128] lse in log2 units
   float* sDsum = sLse + 2 * BM;                             // [2][128]
-  short* sKlo = reinterpret_cast<short*>(sDsum + 2 * BM);   // [2][128] first visible key
+  int* sKlo = reinterpret_cast<int*>(sDsum + 2 * BM);       // [2][128] first visible key
   uint64_t* bars = reinterpret_cast<uint64_t*>(sKlo + 2 * BM);
   uint64_t* kv_full = bars + 0;
   uint64_t* qd_full = bars + 1;   // [2]
@@ -127,8 +134,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* sdp_full = bars + 7;
   uint64_t* p_ready = bars + 8;
   uint64_t* mma_done = bars + 9;
-  uint64_t* dq_full = bars + 10;
-  uint64_t* dq_free = bars + 11;
   uint64_t* kv_done = bars + 12;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -153,15 +158,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ld_full[t], 32);
     }
     mbar_init(sdp_full, 1);
-    mbar_init(p_ready, 128);
+    mbar_init(p_ready, 256);
     mbar_init(mma_done, 1);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_free, 128);
     mbar_init(kv_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 4) {
+  if (warp == 8) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -170,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 5) {
+  if (warp == 9) {
     // ------------------------------------------------------------------ TMA + per-query scalars
     if (n_it > 0) {
       if (lane == 0) {
@@ -201,29 +204,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           const long idx = (long)(base + qi) * a.H + h;
           sLse[buf * BM + q] = in ? a.lse[idx] * 1.4426950408889634f : INFINITY;
           sDsum[buf * BM + q] = in ? a.dsum[idx] : 0.f;
-          sKlo[buf * BM + q] = (short)min(query_key_lo(qi, a.S, a.window, a.seg, base), 32767);
+          sKlo[buf * BM + q] = query_key_lo(qi, a.S, a.window, a.seg, base);
         }
         __syncwarp();
         mbar_arrive(&ld_full[buf]);
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ------------------------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_it > 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(BN, BM, false, false);  // keys x queries
       constexpr uint32_t idesc_kv = make_idesc_bf16(BN, HD, false, true);  // keys x head_dim
-      constexpr uint32_t idesc_q0 = make_idesc_bf16(BM, 64, true, true);   // queries x 64
-      constexpr uint32_t idesc_q1 = make_idesc_bf16(BM, HD > 64 ? HD - 64 : 64, true, true);
-      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), ds_addr = smem_u32(sDS);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       bool ok = mbar_wait(kv_full, 0, a.err, kErrTimeoutMma, abort_flag);
       for (int it = 0; it < n_it && ok; ++it) {
         const int buf = it & 1;
         const uint32_t q_addr = smem_u32(sQ + buf * tile), o_addr = smem_u32(sO + buf * tile);
         if (!mbar_wait(&qd_full[buf], (it >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
         if (it > 0) {
-          // S^T / dP^T overwrite P^T / dS^T / dQ of the previous block
+          // S^T / dP^T overwrite P^T / dS^T of the previous block: its dV / dK MMAs must be done
           if (!mbar_wait(mma_done, (it - 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
-          if (!mbar_wait(dq_free, (it - 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
         }
         tc_fence_after();
 #pragma unroll
@@ -243,111 +243,83 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < BM / 16; ++ks) {
-          umma_ts(tmem + C::dV, tmem + kColS + ks * 8, make_sdesc(o_addr + ks * 2048, BM * 128, 1024), idesc_kv,
+          const uint32_t pc = (ks >> 2) * 64 + (ks & 3) * 8;  // packed bf16 columns of queries 16ks..
+          umma_ts(tmem + C::dV, tmem + kColS + pc, make_sdesc(o_addr + ks * 2048, BM * 128, 1024), idesc_kv,
                   (it > 0 || ks > 0) ? 1u : 0u);
-          umma_ts(tmem + C::dK, tmem + kColDP + ks * 8, make_sdesc(q_addr + ks * 2048, BM * 128, 1024), idesc_kv,
+          umma_ts(tmem + C::dK, tmem + kColDP + pc, make_sdesc(q_addr + ks * 2048, BM * 128, 1024), idesc_kv,
                   (it > 0 || ks > 0) ? 1u : 0u);
-        }
-#pragma unroll
-        for (int ks = 0; ks < BN / 16; ++ks)
-          umma_bf16(tmem + C::dQ0, make_sdesc(ds_addr + ks * 2048, 128 * 128, 1024),
-                    make_sdesc(k_addr + ks * 2048, BN * 128, 1024), idesc_q0, ks > 0 ? 1u : 0u);
-        if constexpr (HD > 64) {
-#pragma unroll
-          for (int ks = 0; ks < BN / 16; ++ks)
-            umma_bf16(tmem + C::dQ1, make_sdesc(ds_addr + ks * 2048, 128 * 128, 1024),
-                      make_sdesc(k_addr + BN * 128 + ks * 2048, BN * 128, 1024), idesc_q1, ks > 0 ? 1u : 0u);
         }
         umma_commit(mma_done);
-        umma_commit(dq_full);
         umma_commit(&qd_empty[buf]);
       }
       umma_commit(kv_done);
     }
-  } else if (warp >= 6) {
-    // ------------------------------------------------------------------------- dQ epilogue
-    const int quarter = warp & 3;
-    const int q = quarter * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    for (int it = 0; it < n_it; ++it) {
-      const bool got = mbar_wait(dq_full, it & 1, a.err, kErrTimeoutEpilogue, abort_flag);
-      if (!__all_sync(0xffffffffu, got)) break;
-      tc_fence_after();
-      float v[HD];
-      using R32 = float(&)[32];
-      tmem_ld32(tmem + C::dQ0 + lane_off, reinterpret_cast<R32>(v[0]));
-      tmem_ld32(tmem + C::dQ0 + lane_off + 32, reinterpret_cast<R32>(v[32]));
-      if constexpr (HD >= 96) tmem_ld32(tmem + C::dQ1 + lane_off, reinterpret_cast<R32>(v[64]));
-      if constexpr (HD == 128) tmem_ld32(tmem + C::dQ1 + lane_off + 32, reinterpret_cast<R32>(v[96]));
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(dq_free);
-      const int h = kh * rep + it / n_i;
-      const int qi = (i_lo + it % n_i) * BM + q;
-      if (qi < a.S) {
-        float4* dst = reinterpret_cast<float4*>(a.dq_acc + ((long)(base + qi) * a.H + h) * HD);
-#pragma unroll
-        for (int c = 0; c < HD / 4; ++c) atomicAdd(dst + c, make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]));
-      }
-    }
   } else {
     // -------------------------------------------------------------------------- compute warps
-    const int kr = warp * 32 + lane;
+    const int hf = warp >> 2;  // query-column half [64 hf, 64 hf + 64)
+    const int kr = (warp & 3) * 32 + lane;
     const int kj = k0 + kr;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    const uint32_t t_s = tmem + kColS + lane_off, t_dp = tmem + kColDP + lane_off;
-    uint8_t* ds_row = sDS + kr * 128;
-    const int sw = kr & 7;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + kColS + lane_off + 64 * hf, t_dp = tmem + kColDP + lane_off + 64 * hf;
+    const bool plain = a.seg == nullptr;
     bool alive = true;
     for (int it = 0; it < n_it; ++it) {
       const int buf = it & 1;
-      const int q0 = (i_lo + it % n_i) * BM;
+      const int qb = (i_lo + it % n_i) * BM + 64 * hf;  // first query of this half
       bool got = mbar_wait(&ld_full[buf], (it >> 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
       got = got && mbar_wait(sdp_full, it & 1, a.err, kErrTimeoutEpilogue, abort_flag);
       if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
       tc_fence_after();
-      const float* lse2 = sLse + buf * BM;
-      const float* dsq = sDsum + buf * BM;
-      const short* klo = sKlo + buf * BM;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float s[32], dp[32];
-        tmem_ld32(t_s + 32 * c, s);
+      const float* lse2 = sLse + buf * BM + 64 * hf;
+      const float* dsq = sDsum + buf * BM + 64 * hf;
+      const int* klo = sKlo + buf * BM + 64 * hf;
+      // every (query, key) pair of this half visible: no masks
+      const bool full = plain && qb >= k0 + BN - 1 && (a.window <= 0 || qb + 63 - k0 < a.window) && qb + 63 < a.S &&
+                        k0 + BN <= a.S;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float sv[32], dp[32];
+        tmem_ld32(t_s + 32 * c, sv);
         tmem_ld32(t_dp + 32 * c, dp);
         tmem_wait_ld();
         uint32_t pw[16], dw[16];
+        if (full) {
 #pragma unroll
-        for (int u = 0; u < 32; u += 2) {
-          float pv[2], dv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int qq = 32 * c + u + e;
-            const int qi = q0 + qq;
-            const bool vis = kj <= qi && kj >= (int)klo[qq] && kj < a.S;
-            const float p = vis ? exp2f(fmaf(s[u + e], a.scale_log2, -lse2[qq])) : 0.f;
-            pv[e] = p;
-            dv[e] = p * (dp[u + e] - dsq[qq]) * a.scale;
+          for (int u = 0; u < 32; u += 4) {
+            const float4 L = *reinterpret_cast<const float4*>(lse2 + 32 * c + u);
+            const float4 D = *reinterpret_cast<const float4*>(dsq + 32 * c + u);
+            const float p0 = ex2(fmaf(sv[u], a.scale_log2, -L.x)), p1 = ex2(fmaf(sv[u + 1], a.scale_log2, -L.y));
+            const float p2 = ex2(fmaf(sv[u + 2], a.scale_log2, -L.z)), p3 = ex2(fmaf(sv[u + 3], a.scale_log2, -L.w));
+            pw[u / 2] = pack_bf16x2(p0, p1);
+            pw[u / 2 + 1] = pack_bf16x2(p2, p3);
+            dw[u / 2] = pack_bf16x2(p0 * (dp[u] - D.x) * a.scale, p1 * (dp[u + 1] - D.y) * a.scale);
+            dw[u / 2 + 1] = pack_bf16x2(p2 * (dp[u + 2] - D.z) * a.scale, p3 * (dp[u + 3] - D.w) * a.scale);
           }
-          pw[u / 2] = pack_bf16x2(pv[0], pv[1]);
-          dw[u / 2] = pack_bf16x2(dv[0], dv[1]);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 32; u += 2) {
+            float pv[2], dv[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int qq = 32 * c + u + e;
+              const int qi = qb + qq;
+              const bool vis = kj <= qi && kj >= klo[qq] && kj < a.S;
+              const float p = vis ? ex2(fmaf(sv[u + e], a.scale_log2, -lse2[qq])) : 0.f;
+              pv[e] = p;
+              dv[e] = p * (dp[u + e] - dsq[qq]) * a.scale;
+            }
+            pw[u / 2] = pack_bf16x2(pv[0], pv[1]);
+            dw[u / 2] = pack_bf16x2(dv[0], dv[1]);
+          }
         }
         tmem_st16(t_s + 16 * c, pw);
         tmem_st16(t_dp + 16 * c, dw);
-        // dS row into the MN-major operand (query chunk c/2, 16-byte units (c%2)*4 .. +3, swizzled)
-        uint8_t* chunk = ds_row + (c >> 1) * 128 * 128;
-#pragma unroll
-        for (int v4 = 0; v4 < 4; ++v4) {
-          const int unit = (c & 1) * 4 + v4;
-          *reinterpret_cast<uint4*>(chunk + ((unit ^ sw) << 4)) =
-              make_uint4(dw[4 * v4], dw[4 * v4 + 1], dw[4 * v4 + 2], dw[4 * v4 + 3]);
-        }
       }
       tmem_wait_st();
-      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_ready);
     }
-    // ---- dK, dV out (once per CTA)
+    // ---- dK, dV out (once per CTA); half hf writes head-dim columns [hf HD/2, (hf + 1) HD/2)
     if (k0 < a.S) {
       bool have = n_it > 0 && alive;
       if (have) {
@@ -359,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __nv_bfloat16* dvr = a.dv + (long)(base + kj) * a.dv_tok + (long)kh * a.dv_head;
         __nv_bfloat16* dkr = a.dk + (long)(base + kj) * a.dk_tok + (long)kh * a.dk_head;
 #pragma unroll 1
-        for (int c = 0; c < HD; c += 16) {
+        for (int c = hf * (HD / 2); c < (hf + 1) * (HD / 2); c += 16) {
           float vv[16], kk[16];
           if (have) {
             tmem_ld16(tmem + C::dV + lane_off + c, vv);
@@ -393,7 +365,239 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------ dQ kernel
+template <int HD>
+struct SmemQ {
+  static constexpr int kTile = ((HD + 63) / 64) * 128 * 128;
+  static constexpr int kUsed = 6 * kTile + 128;  // Q, dO, K[2], V[2], barriers
+  static constexpr int kBytes = kUsed + 128;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                     const BwdArgs a) {
+  using SM = SmemQ<HD>;
+  constexpr int KCH = (HD + 63) / 64;
+  constexpr uint32_t tile = SM::kTile;
+  constexpr uint32_t kColSb = 0, kColDp = 256, kColDq = 384;  // S[2], dP, dQ
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  if (pad + SM::kUsed > SM::kBytes) {
+    if (threadIdx.x == 0) atomicExch(a.err, kErrBadArgs);
+    return;
+  }
+  uint8_t* smem = smem_raw + pad;
+  uint8_t* sQ = smem;
+  uint8_t* sO = smem + tile;
+  uint8_t* sK = smem + 2 * tile;  // [2]
+  uint8_t* sV = smem + 4 * tile;  // [2]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * tile);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* dq_mma = bars + 7;    // [2]
+  uint64_t* dp_free = bars + 9;
+  uint64_t* ds_ready = bars + 10;
+  uint64_t* dq_done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kh = h / (a.H / a.Hkv);
+  const int base = b * a.S;
+  const int q0 = i * BM;
+  int j_lo = 0;
+  if (a.window > 0) j_lo = max(0, q0 - a.window + 1) / BN;
+  const int j_hi = min(i, (a.S + BN - 1) / BN - 1);
+  const int nj = q0 < a.S ? max(j_hi - j_lo + 1, 0) : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&kv_full[t], 1);
+      mbar_init(&kv_empty[t], 1);
+      mbar_init(&s_full[t], 1);
+      mbar_init(&dq_mma[t], 1);
+    }
+    mbar_init(dp_free, 256);
+    mbar_init(ds_ready, 256);
+    mbar_init(dq_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 9) {
+    // ------------------------------------------------------------------------- TMA producer
+    if (lane == 0 && nj > 0) {
+      mbar_arrive_expect_tx(q_full, 2 * tile);
+      for (int c = 0; c < KCH; ++c) {
+        tma_load_2d(&tmQ, q_full, sQ + c * BM * 128, h * HD + c * 64, base + q0);
+        tma_load_2d(&tmO, q_full, sO + c * BM * 128, h * HD + c * 64, base + q0);
+      }
+      for (int t = 0; t < nj; ++t) {
+        const int st = t & 1;
+        const int kr = base + (j_lo + t) * BN;
+        if (!mbar_wait(&kv_empty[st], ((t >> 1) & 1) ^ 1, a.err, kErrTimeoutProducer, abort_flag)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * tile);
+        for (int c = 0; c < KCH; ++c) {
+          tma_load_2d(&tmK, &kv_full[st], sK + st * tile + c * BN * 128, kh * HD + c * 64, kr);
+          tma_load_2d(&tmV, &kv_full[st], sV + st * tile + c * BN * 128, kh * HD + c * 64, kr);
+        }
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nj > 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idesc_q = make_idesc_bf16(BM, HD, false, true);
+      const uint32_t q_addr = smem_u32(sQ), o_addr = smem_u32(sO);
+      bool ok = mbar_wait(q_full, 0, a.err, kErrTimeoutMma, abort_flag);
+      // software pipeline: S/dP of block t are issued before the dQ MMA of block t-1
+      for (int t = 0; t <= nj && ok; ++t) {
+        if (t < nj) {
+          const int st = t & 1;
+          const uint32_t k_addr = smem_u32(sK + st * tile), v_addr = smem_u32(sV + st * tile);
+          if (!mbar_wait(&kv_full[st], (t >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
+          if (t >= 2 && !mbar_wait(&dq_mma[st], ((t - 2) >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < HD / 16; ++ks) {
+            const uint32_t off = (ks / 4) * 128 * 128 + (ks % 4) * 32;
+            umma_bf16(tmem + kColSb + st * 128, make_sdesc(q_addr + off, 16, 1024), make_sdesc(k_addr + off, 16, 1024),
+                      idesc_s, ks > 0 ? 1u : 0u);
+          }
+          if (t >= 1) {
+            if (!mbar_wait(dp_free, (t - 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
+            tc_fence_after();
+          }
+#pragma unroll
+          for (int ks = 0; ks < HD / 16; ++ks) {
+            const uint32_t off = (ks / 4) * 128 * 128 + (ks % 4) * 32;
+            umma_bf16(tmem + kColDp, make_sdesc(o_addr + off, 16, 1024), make_sdesc(v_addr + off, 16, 1024), idesc_s,
+                      ks > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[st]);
+        }
+        if (t >= 1) {
+          const int pt = t - 1, ps = pt & 1;
+          const uint32_t k_addr = smem_u32(sK + ps * tile);
+          if (!mbar_wait(ds_ready, pt & 1, a.err, kErrTimeoutMma, abort_flag)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < BN / 16; ++ks)
+            umma_ts(tmem + kColDq, tmem + kColSb + ps * 128 + (ks >> 2) * 64 + (ks & 3) * 8,
+                    make_sdesc(k_addr + ks * 2048, BN * 128, 1024), idesc_q, (pt > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(&dq_mma[ps]);
+          umma_commit(&kv_empty[ps]);
+        }
+      }
+      umma_commit(dq_done);
+    }
+  } else if (warp < 8) {
+    // -------------------------------------------------------------------------- compute warps
+    const int hf = warp >> 2;  // key-column half [64 hf, 64 hf + 64) of each block
+    const int q = (warp & 3) * 32 + lane;
+    const int qi = q0 + q;
+    const bool in = qi < a.S;
+    const long sidx = (long)(base + qi) * a.H + h;
+    const float lse2 = in ? a.lse[sidx] * 1.4426950408889634f : INFINITY;
+    const float dq_sum = in ? a.dsum[sidx] : 0.f;
+    const int klo = query_key_lo(qi, a.S, a.window, a.seg, base);
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const bool plain = a.seg == nullptr;
+    bool alive = true;
+    for (int t = 0; t < nj; ++t) {
+      const int st = t & 1;
+      const int kb = (j_lo + t) * BN + 64 * hf;  // first key of this half
+      const bool got = mbar_wait(&s_full[st], (t >> 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+      tc_fence_after();
+      float dp[64];
+      using R32 = float(&)[32];
+      tmem_ld32(tmem + kColDp + lane_off + 64 * hf, reinterpret_cast<R32>(dp[0]));
+      tmem_ld32(tmem + kColDp + lane_off + 64 * hf + 32, reinterpret_cast<R32>(dp[32]));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(dp_free);
+      const bool full = plain && q0 >= kb + 63 && (a.window <= 0 || q0 + BM - 1 - kb < a.window) &&
+                        q0 + BM <= a.S && kb + 64 <= a.S;
+      const uint32_t t_s = tmem + kColSb + st * 128 + lane_off + 64 * hf;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float sv[32];
+        tmem_ld32(t_s + 32 * c, sv);
+        tmem_wait_ld();
+        uint32_t dw[16];
+        if (full) {
+#pragma unroll
+          for (int u = 0; u < 32; u += 2) {
+            const float p0 = ex2(fmaf(sv[u], a.scale_log2, -lse2));
+            const float p1 = ex2(fmaf(sv[u + 1], a.scale_log2, -lse2));
+            dw[u / 2] = pack_bf16x2(p0 * (dp[32 * c + u] - dq_sum) * a.scale,
+                                    p1 * (dp[32 * c + u + 1] - dq_sum) * a.scale);
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < 32; u += 2) {
+            float dv[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int kj = kb + 32 * c + u + e;
+              const bool vis = kj <= qi && kj >= klo && kj < a.S;
+              const float p = vis ? ex2(fmaf(sv[u + e], a.scale_log2, -lse2)) : 0.f;
+              dv[e] = p * (dp[32 * c + u + e] - dq_sum) * a.scale;
+            }
+            dw[u / 2] = pack_bf16x2(dv[0], dv[1]);
+          }
+        }
+        tmem_st16(t_s + 16 * c, dw);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(ds_ready);
+    }
+    if (alive && nj > 0) {
+      const bool got = mbar_wait(dq_done, 0, a.err, kErrTimeoutEpilogue, abort_flag);
+      if (__all_sync(0xffffffffu, got)) {
+        tc_fence_after();
+        __nv_bfloat16* row = a.dq + sidx * HD;
+#pragma unroll 1
+        for (int c = hf * (HD / 2); c < (hf + 1) * (HD / 2); c += 16) {
+          float v[16];
+          tmem_ld16(tmem + kColDq + lane_off + c, v);
+          tmem_wait_ld();
+          if (in) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) pk[u] = pack_bf16x2(v[2 * u], v[2 * u + 1]);
+            reinterpret_cast<uint4*>(row + c)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            reinterpret_cast<uint4*>(row + c)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -420,28 +624,31 @@ static int run_fa_bwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
   a.seg = L.seg;
   a.lse = L.lse;
   a.dsum = L.dsum;
-  a.dq_acc = L.dq_acc;
+  a.dq = (__nv_bfloat16*)L.dq;
   a.dk = (__nv_bfloat16*)L.dk; a.dk_tok = L.dk_tok; a.dk_head = L.dk_head;
   a.dv = (__nv_bfloat16*)L.dv; a.dv_tok = L.dv_tok; a.dv_head = L.dv_head;
   a.dv_accumulate = L.dv_accumulate;
   a.err = err;
-  constexpr int smem = Smem<HD>::kBytes;
-  static_assert(smem <= 232448, "shared memory budget");
+  constexpr int smem_kv = Smem<HD>::kBytes;
+  constexpr int smem_q = SmemQ<HD>::kBytes;
+  static_assert(smem_kv <= 232448 && smem_q <= 232448, "shared memory budget");
   static bool init = false;
   if (!init) {
-    if (cudaFuncSetAttribute(fa_bwd_sm100_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(fa_bwd_dkdv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(fa_bwd_dq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q) != cudaSuccess)
       return kErrBadArgsHost;
     init = true;
   }
-  dim3 grid((L.S + BN - 1) / BN, L.Hkv, L.B);
   count_launch();
-  fa_bwd_sm100_kernel<HD><<<grid, kThreads, smem, st>>>(tq, tk, tv, to, a);
+  fa_bwd_dkdv_kernel<HD><<<dim3((L.S + BN - 1) / BN, L.Hkv, L.B), kThreads, smem_kv, st>>>(tq, tk, tv, to, a);
+  count_launch();
+  fa_bwd_dq_kernel<HD><<<dim3((L.S + BM - 1) / BM, L.H, L.B), kThreads, smem_q, st>>>(tq, tk, tv, to, a);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
 }
 
-// Same contract as launch_flash_bwd (dsum / dq_acc preparation and the final dq conversion are
-// shared with it), with the tcgen05 kernel for the main pass.
+// Same contract as launch_flash_bwd (the dsum pass is shared with it); dq is written directly, so the
+// fp32 dq accumulator is not used.
 int launch_flash_bwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
   if (L.q_head != L.hd || L.k_head != L.hd || L.v_head != L.hd) return kErrBadArgsHost;
   if ((L.q_tok * 2) % 16 || (L.k_tok * 2) % 16 || (L.v_tok * 2) % 16) return kErrBadArgsHost;
@@ -449,8 +656,9 @@ int launch_flash_bwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
        reinterpret_cast<uintptr_t>(L.dout)) & 15)
     return kErrBadArgsHost;
   if ((L.dk_tok | L.dk_head | L.dv_tok | L.dv_head) % 8) return kErrBadArgsHost;  // 16-byte row stores
-  if (L.S >= 32767) return kErrBadArgsHost;  // first-visible-key indices are kept as int16
-  int r = launch_flash_bwd_prep(L, st);
+  AttnLaunch P = L;
+  P.dq_acc = nullptr;  // dsum only
+  int r = launch_flash_bwd_prep(P, st);
   if (r) return r;
   switch (L.hd) {
     case 64: r = run_fa_bwd_sm100<64>(L, err, st); break;
@@ -458,8 +666,7 @@ int launch_flash_bwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
     case 128: r = run_fa_bwd_sm100<128>(L, err, st); break;
     default: return kErrBadArgsHost;
   }
-  if (r) return r;
-  return launch_dq_convert(L, st);
+  return r;
 }
 
 }  // namespace mxk

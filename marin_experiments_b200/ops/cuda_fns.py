@@ -243,6 +243,8 @@ class _AttentionBlock(torch.autograd.Function):
         dq_acc = torch.empty(t, nh, hd, dtype=F32, device=h.device)
         dsum = torch.empty(t, nh, dtype=F32, device=h.device)
         if hd in (64, 96, 128) and s < 32767:
+            from ._ext import err_flag
+
             ext().flash_bwd_sm100(qn, kn, v, o, lse, ctx.seg, shape.batch, s, shape.window, ctx.scale, _c(do), dsum,
                                   dq_acc, dq, dk, dv, dv_acc, err_flag(h.device))
         else:
