@@ -423,6 +423,41 @@ void ep_wait(const std::vector<int64_t>& peers, int64_t my, int64_t flags_off, i
   mxk::launch_ep_wait(a, err.data_ptr<int>(), stream());
 }
 
+// ------------------------------------------------------------------------------- decode path
+void head_norm_rope(const Tensor& x, int64_t nh, int64_t hd, const OptT& w, double eps, const Tensor& pos,
+                    const Tensor& cos_t, const Tensor& sin_t, const Tensor& out) {
+  need(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "x must be CUDA bf16 rows");
+  need(out.is_contiguous() && pos.scalar_type() == at::kInt, "out contiguous, pos int32");
+  c10::cuda::CUDAGuard g(x.device());
+  ok(mxk::launch_head_norm_rope(x.data_ptr(), x.stride(0), (int)nh, (int)hd, ptr<const float>(w), (float)eps,
+                                pos.data_ptr<int>(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), (int)x.size(0),
+                                out.data_ptr(), stream()),
+     "head_norm_rope");
+}
+
+// Rows r of k / v ([rows, Hkv, hd], row stride shared) go to cache[row_seq[r] (or r), pos[r]].
+void kv_append(const Tensor& k, const Tensor& v, const Tensor& ck, const Tensor& cv, const Tensor& pos,
+               const OptT& row_seq) {
+  need(k.stride(0) == v.stride(0) && ck.is_contiguous() && cv.is_contiguous(), "kv_append layout");
+  need(pos.numel() == k.size(0), "one position per row");
+  c10::cuda::CUDAGuard g(k.device());
+  ok(mxk::launch_kv_append(k.data_ptr(), v.data_ptr(), k.stride(0), ck.data_ptr(), cv.data_ptr(), pos.data_ptr<int>(),
+                           ptr<const int>(row_seq), (int)k.size(0), (int)ck.size(1), (int)ck.size(2), (int)ck.size(3),
+                           stream()),
+     "kv_append");
+}
+
+void decode_attention(const Tensor& q, const Tensor& ck, const Tensor& cv, const Tensor& lens, double scale,
+                      int64_t nsplit, const Tensor& part_ml, const Tensor& part_acc, const Tensor& out) {
+  need(q.is_contiguous() && ck.is_contiguous() && cv.is_contiguous() && out.is_contiguous(), "decode layout");
+  c10::cuda::CUDAGuard g(q.device());
+  ok(mxk::launch_decode_attention(q.data_ptr(), ck.data_ptr(), cv.data_ptr(), lens.data_ptr<int>(), (int)q.size(0),
+                                  (int)q.size(1), (int)ck.size(2), (int)q.size(2), (int)ck.size(1), (float)scale,
+                                  (int)nsplit, part_ml.data_ptr<float>(), part_acc.data_ptr<float>(), out.data_ptr(),
+                                  stream()),
+     "decode_attention");
+}
+
 }  // namespace
 
 void register_ops(pybind11::module& m) {
@@ -456,6 +491,9 @@ void register_ops(pybind11::module& m) {
   m.def("ema", &ema);
   m.def("cast_bf16", &cast_bf16);
   m.def("flash_bwd_sm100", &flash_bwd_sm100);
+  m.def("head_norm_rope", &head_norm_rope);
+  m.def("kv_append", &kv_append);
+  m.def("decode_attention", &decode_attention);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", [](int64_t p) { return mxk::ipc_close(reinterpret_cast<void*>(p)); });

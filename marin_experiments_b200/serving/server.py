@@ -1,0 +1,124 @@
+"""HTTP serving (tunix-delphi-rl/serving/serve.py:81-135,992-1068): ``GET /health``,
+``POST /generate`` (``prompt`` or ``prompts``), and an OpenAI-style ``POST /v1/completions``.
+
+Run: ``python -m marin_experiments_b200.serving.server --model-dir <hf snapshot> [--port 8000]``
+(``--random-tiny`` serves a small random-init model for smoke tests).
+"""
+
+from __future__ import annotations
+
+import argparse
+from typing import List, Optional
+
+from pydantic import BaseModel
+
+
+class GenerateRequest(BaseModel):
+    prompt: Optional[str] = None
+    prompts: Optional[List[str]] = None
+    max_tokens: Optional[int] = None
+    temperature: float = 0.8
+    top_p: float = 1.0
+    seed: int = 0
+    stop: Optional[List[str]] = None
+
+    def resolve_prompts(self) -> tuple[list[str], bool]:
+        if self.prompts is not None and self.prompt is not None:
+            raise ValueError("Pass exactly one of `prompt` or `prompts`.")
+        if self.prompts is not None:
+            if not self.prompts:
+                raise ValueError("`prompts` must be non-empty.")
+            return list(self.prompts), True
+        if self.prompt is not None:
+            return [self.prompt], False
+        raise ValueError("Pass `prompt` (str) or `prompts` (list[str]).")
+
+
+class GenerateResponse(BaseModel):
+    text: Optional[str] = None
+    texts: Optional[List[str]] = None
+
+
+class CompletionRequest(BaseModel):
+    prompt: str
+    max_tokens: int = 256
+    temperature: float = 0.8
+    top_p: float = 1.0
+    seed: int = 0
+    stop: Optional[List[str]] = None
+
+
+def build_app(engine, model_name: str = "qwen3"):
+    from fastapi import FastAPI, HTTPException
+
+    app = FastAPI(title="marin_experiments_b200 serving", version="0.1.0")
+
+    @app.get("/health")
+    def health() -> dict:
+        return {"ok": bool(engine.ready), "model": model_name}
+
+    @app.post("/generate", response_model=GenerateResponse)
+    def generate(req: GenerateRequest) -> GenerateResponse:
+        if not engine.ready:
+            raise HTTPException(status_code=503, detail="model loading")
+        try:
+            prompts, batched = req.resolve_prompts()
+        except ValueError as exc:
+            raise HTTPException(status_code=400, detail=str(exc)) from exc
+        texts = engine.generate(prompts, max_tokens=req.max_tokens, temperature=req.temperature, top_p=req.top_p,
+                                seed=req.seed, stop=req.stop)
+        return GenerateResponse(texts=texts) if batched else GenerateResponse(text=texts[0])
+
+    @app.post("/v1/completions")
+    def completions(req: CompletionRequest) -> dict:
+        if not engine.ready:
+            raise HTTPException(status_code=503, detail="model loading")
+        texts = engine.generate([req.prompt], max_tokens=req.max_tokens, temperature=req.temperature,
+                                top_p=req.top_p, seed=req.seed, stop=req.stop)
+        return {"object": "text_completion", "model": model_name,
+                "choices": [{"index": 0, "text": texts[0], "finish_reason": "stop"}]}
+
+    app.state.engine = engine
+    return app
+
+
+def tiny_engine(device="cpu"):
+    """A small random-init Qwen3 with the byte tokenizer (tests and smoke runs)."""
+    from ..data.tokenize import ByteTokenizer
+    from ..models.qwen3 import Qwen3Config, Qwen3Model
+    from .engine import Engine
+
+    cfg = Qwen3Config(vocab_size=512, hidden_dim=128, intermediate_dim=256, num_layers=2, num_heads=2, num_kv_heads=1,
+                      head_dim=64, rope_theta=10000.0, max_seq_len=256)
+    model = Qwen3Model(cfg).init_weights(0).to(device)
+    return Engine(model, ByteTokenizer(), device=device, max_batch=4, max_len=256)
+
+
+def main(argv=None):
+    import torch
+    import uvicorn
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model-dir", default=None)
+    ap.add_argument("--tokenizer", default=None)
+    ap.add_argument("--random-tiny", action="store_true")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--max-batch", type=int, default=8)
+    args = ap.parse_args(argv)
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    if args.random_tiny or not args.model_dir:
+        engine, name = tiny_engine(dev), "random-tiny"
+    else:
+        from ..data.tokenize import load_tokenizer
+        from ..models.qwen3 import load_hf
+        from .engine import Engine
+
+        model = load_hf(args.model_dir, device=dev)
+        engine = Engine(model, load_tokenizer(args.tokenizer or args.model_dir), device=dev, max_batch=args.max_batch)
+        name = args.model_dir
+    uvicorn.run(build_app(engine, name), host=args.host, port=args.port)
+
+
+if __name__ == "__main__":
+    main()
