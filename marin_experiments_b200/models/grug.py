@@ -137,7 +137,7 @@ class MoEMLP(nn.Module):
         self.ep_group = None  # set by parallel.ep when experts are sharded
         self.layer_key = 0  # this layer's index (keys its expert-parallel receive buffers)
 
-    def forward(self, h, residual=None, dp_group=None):
+    def forward(self, h, residual=None, dp_group=None, logit_bias=None):
         c = self.cfg
         t = h.shape[0]
         world = 1
@@ -146,7 +146,7 @@ class MoEMLP(nn.Module):
         qb_count = max(1, t * c.num_experts_per_token // c.num_experts)
         r = ops.route(h, self.router, self.router_bias, c.num_experts_per_token, adaptive=c.adaptive_routing,
                       threshold=self.router_threshold, k_min=c.min_experts_per_token, temp=c.sparsity_temp,
-                      qb_count=qb_count, need_beta=c.qb_balancing)
+                      qb_count=qb_count, need_beta=c.qb_balancing, logit_bias=logit_bias)
         beta = r.beta
         if beta is not None and world > 1:
             beta = beta.clone()
@@ -183,14 +183,14 @@ class Block(nn.Module):
             self.shared = None
         self.cfg = cfg
 
-    def forward(self, x, batch: int, seq: int, segment_ids=None, dp_group=None):
+    def forward(self, x, batch: int, seq: int, segment_ids=None, dp_group=None, logit_bias=None):
         h = self.attn_norm(x)
         x = self.attn(h, x, batch, seq, segment_ids)
         h = self.mlp_norm(x)
         if not self.cfg.is_moe:
             return self.mlp(h, residual=x), None
         base = x if self.shared is None else self.shared(h, residual=x)
-        x, stats = self.mlp(h, residual=base, dp_group=dp_group)
+        x, stats = self.mlp(h, residual=base, dp_group=dp_group, logit_bias=logit_bias)
         return x, stats
 
 
@@ -364,7 +364,7 @@ def init_store_weights(store, cfg: GrugModelConfig, seed: int = 0, model: Transf
             leaf = info.name.rsplit(".", 1)[-1]
             if leaf == "weight":
                 v.fill_(1.0)
-            elif leaf in ("attn_gate", "router_bias"):
+            elif leaf in ("attn_gate", "router_bias", "film_scale", "film_shift", "depth_bias", "halt_head"):
                 v.zero_()
             elif leaf == "router_threshold":
                 v.fill_(-4.0)

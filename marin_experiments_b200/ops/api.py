@@ -145,13 +145,16 @@ class RouterOut:
 
 
 def route(h, w_router, router_bias, k: int, *, adaptive=False, threshold=None, k_min=0, temp=1.0,
-          qb_count: int = 1, need_beta: bool = True):
+          qb_count: int = 1, need_beta: bool = True, logit_bias=None):
     """Router of megagpt-speedrun/model.py:559-634: fp32 logits, top-(K+1) on biased logits,
     sigmoid combine weights on unbiased logits, per-layer z-loss / LBL / sparsity penalty and the
-    local QB beta (the cross-rank mean is taken by the caller)."""
+    local QB beta (the cross-rank mean is taken by the caller). ``logit_bias`` ``[E]`` is an optional
+    learned additive logit bias (depth-conditioned routing), differentiated like the logits."""
     if h.is_cuda:
-        return _cuda().route(h, w_router, router_bias, k, adaptive, threshold, k_min, temp, qb_count, need_beta)
-    out = R.route(h, w_router, router_bias, k, adaptive=adaptive, threshold=threshold, k_min=k_min, temp=temp)
+        return _cuda().route(h, w_router, router_bias, k, adaptive, threshold, k_min, temp, qb_count, need_beta,
+                             logit_bias)
+    out = R.route(h, w_router, router_bias, k, adaptive=adaptive, threshold=threshold, k_min=k_min, temp=temp,
+                  logit_bias=logit_bias)
     e = w_router.shape[0]
     st = R.routing_stats(out["selected"], out["probs"], out["logits"], e, k)
     beta = R.qb_beta(out["logits"].detach(), out["alpha"].detach(), qb_count) if need_beta else None

@@ -333,7 +333,7 @@ def dense_mlp(h, w_in, w_down, glu, act, residual):
 
 class _Router(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, h, w_router, theta, bias, k, adaptive, k_min, temp, qb_count, need_beta):
+    def forward(ctx, h, w_router, theta, bias, k, adaptive, k_min, temp, qb_count, need_beta, logit_bias):
         h = _c(h)
         t, d = h.shape
         e = w_router.shape[0]
@@ -341,6 +341,9 @@ class _Router(torch.autograd.Function):
         ldl = _round(e, 32)
         logits = torch.empty(t, ldl, dtype=F32, device=dev)
         G.gemm(h, w_router, logits, M=t, N=e, K=d, bn=64)
+        if logit_bias is not None:
+            logits[:, :e] += logit_bias.detach().float()
+        ctx.has_lb = logit_bias is not None
         sel = torch.empty(t, k, dtype=torch.int32, device=dev)
         comb = torch.empty(t, k, dtype=F32, device=dev)
         topb = torch.empty(t, k, dtype=F32, device=dev)
@@ -395,14 +398,15 @@ class _Router(torch.autograd.Function):
         if ctx.adaptive and ctx.theta is not None:
             _mg(ctx.theta).add_(dtheta.reshape(_mg(ctx.theta).shape))
         ctx.w_router = ctx.theta = None
-        return dh, None, None, None, None, None, None, None, None, None
+        dlb = dlog[:, :e].float().sum(0) if ctx.has_lb else None
+        return dh, None, None, None, None, None, None, None, None, None, dlb
 
 
-def route(h, w_router, router_bias, k, adaptive, threshold, k_min, temp, qb_count, need_beta):
+def route(h, w_router, router_bias, k, adaptive, threshold, k_min, temp, qb_count, need_beta, logit_bias=None):
     from .api import RouterOut
 
     comb, z_loss, lbl, sparsity, sel, keep, counts, entropy, realized, beta = _Router.apply(
-        h, w_router, threshold, router_bias, k, adaptive, k_min, temp, qb_count, need_beta)
+        h, w_router, threshold, router_bias, k, adaptive, k_min, temp, qb_count, need_beta, logit_bias)
     e = w_router.shape[0]
     return RouterOut(sel, comb, keep.bool(), z_loss, lbl, sparsity, counts, entropy, beta, sparsity.detach(),
                      realized)

@@ -147,13 +147,15 @@ def activation(x: torch.Tensor, kind: str) -> torch.Tensor:
 
 
 def route(x_flat, router_w, router_bias, k: int, *, adaptive: bool = False, threshold=None,
-          k_min: int = 0, temp: float = 1.0):
+          k_min: int = 0, temp: float = 1.0, logit_bias=None):
     """Fp32 router (megagpt-speedrun/model.py:559-605).
 
     Returns a dict with ``logits`` [T,E], ``probs``, ``selected`` [T,K] (descending biased logit),
     ``topk_biased`` [T,K], ``alpha`` [T,1] (the (K+1)-th biased logit), ``combine`` [T,K] and, in
     adaptive mode, ``expected_active``/``realized_active`` per token."""
     logits = (x_flat @ router_w.t()).float()
+    if logit_bias is not None:  # learned additive bias (part of the logits, with gradient)
+        logits = logits + logit_bias.float()
     biased = logits + router_bias.detach().float()
     probs = torch.softmax(logits, dim=-1)
     e = logits.shape[-1]

@@ -94,6 +94,10 @@ def grug_group_of(name: str, ndim: int) -> str:
     p = name.lower()
     if "token_embed" in p:
         return "adam"
+    # zero-initialised modulation / bias parameters of the looped model: a scale-invariant step
+    # cannot move a zero matrix (reentrant/optimizer.py routes them to Adam too)
+    if "film_" in p or "depth_bias" in p or "halt_head" in p:
+        return "adam"
     if "router_bias" in p or "attn_gate" in p or ".router" in p or p.startswith("router"):
         return "adam"
     if ".mlp.w_" in p or ".shared.w_" in p or ".mlp.expert_mlp.w_" in p:

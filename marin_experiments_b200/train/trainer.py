@@ -36,7 +36,7 @@ def num_moe_layers(model: Transformer) -> int:
 class Trainer:
     def __init__(self, cfg: GrugRunConfig, *, device: str | torch.device | None = None, micro_batch: int | None = None,
                  num_train_steps: int | None = None, dist=None, build_model: bool = True, seed: int | None = None,
-                 model_kwargs: dict | None = None):
+                 model_kwargs: dict | None = None, model_factory=None):
         self.cfg = cfg
         self.mcfg: GrugModelConfig = cfg.model
         if device is None:
@@ -50,6 +50,11 @@ class Trainer:
         self.z_loss_weight = cfg.trainer.z_loss_weight
         self.ema_beta = cfg.trainer.ema_beta
         self.model_kwargs = dict(model_kwargs or {})
+        # model_factory(cfg, local_experts) -> module with next_token_loss (e.g. the looped model)
+        self.model_factory = model_factory
+        import random as _random
+
+        self._rng = _random.Random(self.seed)
         if build_model:
             self._build()
 
@@ -60,7 +65,10 @@ class Trainer:
         if self.dist is not None and self.dist.ep_size > 1 and cfg.is_moe:
             local = self.dist.local_expert_range(cfg.num_experts)
         with torch.device("meta"):
-            model = Transformer(cfg, local_experts=local, **self.model_kwargs)
+            if self.model_factory is not None:
+                model = self.model_factory(cfg, local)
+            else:
+                model = Transformer(cfg, local_experts=local, **self.model_kwargs)
         self.model = model
         self.store = ParamStore(model, self.device, pad_multiple=getattr(self.dist, "store_pad", 64))
         init_store_weights(self.store, cfg, self.seed, model)
@@ -110,11 +118,15 @@ class Trainer:
         loss_sum = torch.zeros((), device=self.device)
         beta_sum = None
         metrics: dict[str, torch.Tensor] = {}
+        extra = {}
+        if hasattr(self.model, "sample_recurrence"):  # looped model: depth drawn once per step
+            extra["recurrence"] = self.model.sample_recurrence(self._rng)
         for i in range(n_micro):
             sl = slice(i * mb, (i + 1) * mb)
             w = lw[sl] if lw is not None else default_loss_weight(mb, s, self.device)
             loss, met = self.model.next_token_loss(tokens[sl], w, None if seg is None else seg[sl],
-                                                   z_loss_weight=self.z_loss_weight, dp_group=self.dp_group)
+                                                   z_loss_weight=self.z_loss_weight, dp_group=self.dp_group,
+                                                   **extra)
             (loss / n_micro).backward()
             loss_sum = loss_sum + loss.detach()
             if "qb_beta_per_layer" in met:

@@ -1,0 +1,76 @@
+"""Re-entrant (looped) grug MoE on CPU: R = 1 equals the plain stack, zero-initialised FiLM /
+depth bias keep it identical, the extra loss terms are present and differentiable, the learned
+router logit bias gets a gradient, and depth sampling stays within the choices."""
+
+import random
+
+import pytest
+import torch
+
+from marin_experiments_b200.config import GrugModelConfig
+from marin_experiments_b200.models.grug import Transformer
+from marin_experiments_b200.models.looped import LoopedConfig, LoopedTransformer
+
+M = GrugModelConfig(vocab_size=256, hidden_dim=64, intermediate_dim=128, shared_expert_intermediate_dim=128,
+                    num_experts=4, num_experts_per_token=2, num_layers=4, num_heads=2, num_kv_heads=2, head_dim=32,
+                    max_seq_len=32, sliding_window=32)
+TOK = torch.randint(0, 256, (2, 32), generator=torch.Generator().manual_seed(0))
+
+
+def test_r1_matches_plain_stack():
+    plain = Transformer(M).init_weights(3)
+    lp = LoopedTransformer(LoopedConfig(model=M, num_prelude_layers=1, num_coda_layers=1, iteration_film=True,
+                                        depth_conditioned_routing=True)).init_weights(3)
+    la, _ = plain.next_token_loss(TOK)
+    lb, _ = lp.next_token_loss(TOK)
+    assert torch.allclose(la, lb, atol=1e-6)
+
+
+def test_looped_terms_and_gradients():
+    lc = LoopedConfig(model=M, num_prelude_layers=1, num_coda_layers=1, recurrence_steps=3, iteration_film=True,
+                      depth_conditioned_routing=True, core_consistency_weight=0.1, anytime_supervision=True,
+                      ponder_halting=True)
+    m = LoopedTransformer(lc).init_weights(1)
+    assert lc.effective_depth() == 1 + 2 * 3 + 1
+    loss, met = m.next_token_loss(TOK)
+    for k in ("train/core_consistency", "train/anytime_ce", "train/ponder_ce", "train/ponder_kl",
+              "train/ponder_expected_steps"):
+        assert k in met and torch.isfinite(met[k])
+    loss.backward()
+    for p in (m.film_scale, m.film_shift, m.depth_bias, m.halt_head):
+        assert p.grad is not None and torch.isfinite(p.grad).all()
+    assert m.depth_bias.grad.abs().sum() > 0
+    # deeper than trained: the last FiLM / bias entry is reused
+    l4, _ = m.next_token_loss(TOK, recurrence=5)
+    assert torch.isfinite(l4)
+
+
+def test_randomized_recurrence():
+    lc = LoopedConfig(model=M, num_prelude_layers=1, num_coda_layers=1, recurrence_steps=2,
+                      randomize_recurrence=True, recurrence_choices=(1, 2, 4))
+    m = LoopedTransformer(lc)
+    rng = random.Random(0)
+    seen = {m.sample_recurrence(rng) for _ in range(50)}
+    assert seen == {1, 2, 4} and lc.table_depth == 4
+    with pytest.raises(ValueError):
+        LoopedConfig(model=M, randomize_recurrence=True)
+    with pytest.raises(ValueError):
+        LoopedConfig(model=M, num_prelude_layers=3, num_coda_layers=2)
+
+
+def test_trainer_with_looped_model():
+    from marin_experiments_b200.config import GrugRunConfig, GrugTrainerConfig, TrainerConfig
+    from marin_experiments_b200.optim import GrugMoeAdamHConfig
+    from marin_experiments_b200.train.trainer import Trainer
+
+    lc = LoopedConfig(model=M, num_prelude_layers=1, num_coda_layers=1, recurrence_steps=2, iteration_film=True,
+                      depth_conditioned_routing=True, randomize_recurrence=True, recurrence_choices=(1, 2, 3))
+    run = GrugRunConfig(model=M, optimizer=GrugMoeAdamHConfig(warmup=0.0),
+                        trainer=GrugTrainerConfig(trainer=TrainerConfig(num_train_steps=5)))
+    tr = Trainer(run, device="cpu", model_factory=lambda cfg, local: LoopedTransformer(lc))
+    groups = {n: [i.name for i in g["infos"]] for n, g in tr.opt.groups.items()}
+    assert "film_scale" in groups["adam"] and "depth_bias" in groups["adam"]
+    assert float(tr.store.master_view(tr.store.by_name["film_scale"]).abs().sum()) == 0.0
+    losses = [float(tr.train_step({"tokens": TOK})["train/loss"]) for _ in range(4)]
+    assert all(l == l for l in losses)
+    assert float(tr.store.master_view(tr.store.by_name["film_scale"]).abs().sum()) > 0
