@@ -39,6 +39,21 @@ class RotaryConfig:
 
 
 @dataclass(frozen=True)
+class NgramEmbedConfig:
+    """Hashed multi-gram input embedding (Over-Encoding; tokenization/soak_config.py:15-29): one
+    ``[hash_buckets, rank]`` table per n-gram order, ``num_hashes`` hash functions each, looked-up rows
+    averaged, projected ``rank -> hidden`` and added to the token embedding. ``ratio`` scales the
+    table init relative to the model's initializer std."""
+
+    orders: tuple[int, ...] = (2, 3, 4)
+    num_hashes: int = 2
+    hash_buckets: int = 4_000_037
+    rank: int = 128
+    combine: Literal["mean"] = "mean"
+    ratio: float = 0.25
+
+
+@dataclass(frozen=True)
 class GrugModelConfig:
     """Hyperparameters for the grug transformer (dense when ``num_experts == 0``).
 
@@ -89,6 +104,7 @@ class GrugModelConfig:
     glu: bool = True
     tie_embeddings: bool = False
     rope: RotaryConfig = field(default_factory=RotaryConfig)
+    ngram: NgramEmbedConfig | None = None
 
     def __post_init__(self) -> None:
         _ = self.inferred_head_dim
@@ -297,7 +313,7 @@ def _registry() -> dict[str, type]:
     reg = {
         c.__name__: c
         for c in (
-            RotaryConfig, GrugModelConfig, CheckpointerConfig, TrainerConfig, GrugTrainerConfig,
+            RotaryConfig, NgramEmbedConfig, GrugModelConfig, CheckpointerConfig, TrainerConfig, GrugTrainerConfig,
             GrugEvalConfig, DataConfig, GrugRunConfig,
         )
     }

@@ -208,6 +208,10 @@ class Transformer(nn.Module):
             self.token_embed = nn.Parameter(torch.empty(v, de))
             self.embed_up = nn.Parameter(torch.empty(d, de)) if cfg.is_factorized_embed else None
             self.embed_norm = NormPair(cfg) if cfg.is_moe else None
+            ng = cfg.ngram
+            self.ngram_table = (nn.Parameter(torch.empty(len(ng.orders), ng.hash_buckets, ng.rank))
+                                if ng is not None else None)
+            self.ngram_proj = nn.Parameter(torch.empty(d, ng.rank)) if ng is not None else None
         self.blocks = nn.ModuleList([Block(cfg, i, local_experts) for i in self.layer_ids])
         if with_head:
             self.final_norm = NormPair(cfg)
@@ -246,6 +250,10 @@ class Transformer(nn.Module):
         x = ops.embed(tokens.reshape(-1), self.token_embed)
         if self.embed_up is not None:
             x = ops.linear(x, self.embed_up)
+        if self.ngram_table is not None:  # hashed n-gram capacity added to the token embedding
+            ng = self.cfg.ngram
+            z = ops.ngram_embed(tokens.reshape(tokens.shape[0], -1), self.ngram_table, ng.orders, ng.num_hashes)
+            x = ops.linear(z, self.ngram_proj, residual=x)
         if self.embed_norm is not None:
             x = self.embed_norm(x)
         return x
@@ -368,6 +376,9 @@ def init_store_weights(store, cfg: GrugModelConfig, seed: int = 0, model: Transf
                 v.zero_()
             elif leaf == "router_threshold":
                 v.fill_(-4.0)
+            elif leaf == "ngram_table":
+                gen = torch.Generator(device=store.device).manual_seed(_seed_for(seed, gname(info.name)))
+                trunc_normal_(v, std * cfg.ngram.ratio, gen)
             elif info.ndim == 3:
                 lo = ranges.get(info.name.rsplit(".", 1)[0], (0, info.shape[0]))[0]
                 for j in range(info.shape[0]):

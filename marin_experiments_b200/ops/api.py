@@ -191,3 +191,10 @@ def cross_entropy(h, w_out, labels, weights, *, z_weight: float = 0.0):
     if h.is_cuda:
         return _cuda().cross_entropy(h, w_out, labels, weights, z_weight)
     return R.fused_linear_cross_entropy(h, w_out, labels, weights, z_weight=z_weight)
+
+
+def ngram_embed(ids: torch.Tensor, table: torch.Tensor, orders, n_hash: int) -> torch.Tensor:
+    """Hashed n-gram input embedding ``[B*S, rank]`` (mean over orders x hashes)."""
+    if ids.is_cuda:
+        return _cuda().ngram_embed(ids, table, orders, n_hash)
+    return R.ngram_embed(ids, table, orders, n_hash)

@@ -139,4 +139,10 @@ int launch_decode_attention(const void* q, const void* ck, const void* cv, const
                             int hd, int Lmax, float scale, int nsplit, float* part_ml, float* part_acc, void* out,
                             cudaStream_t st);
 
+// ------------------------------------------------------------------- hashed n-gram embedding (ngram.cu)
+int launch_ngram_fwd(const int64_t* ids, int B, int S, const int* orders, int n_orders, int n_hash, long buckets,
+                     const void* table, int rank, void* out, cudaStream_t st);
+int launch_ngram_bwd(const int64_t* ids, int B, int S, const int* orders, int n_orders, int n_hash, long buckets,
+                     const void* dout, int rank, float* dtable, cudaStream_t st);
+
 }  // namespace mxk

@@ -458,6 +458,28 @@ void decode_attention(const Tensor& q, const Tensor& ck, const Tensor& cv, const
      "decode_attention");
 }
 
+// -------------------------------------------------------------------- hashed n-gram embedding
+void ngram_fwd(const Tensor& ids, const Tensor& orders, int64_t n_hash, int64_t buckets, const Tensor& table,
+               const Tensor& out) {
+  need(ids.dim() == 2 && ids.scalar_type() == at::kLong && ids.is_contiguous(), "ids must be [B, S] int64");
+  need(orders.scalar_type() == at::kInt && orders.is_cuda(), "orders must be CUDA int32");
+  need(table.dim() == 3 && table.is_contiguous() && out.is_contiguous(), "table [orders, buckets, rank]");
+  c10::cuda::CUDAGuard g(ids.device());
+  ok(mxk::launch_ngram_fwd(ids.data_ptr<int64_t>(), ids.size(0), ids.size(1), orders.data_ptr<int>(), orders.numel(),
+                           (int)n_hash, (long)buckets, table.data_ptr(), table.size(2), out.data_ptr(), stream()),
+     "ngram_fwd");
+}
+
+void ngram_bwd(const Tensor& ids, const Tensor& orders, int64_t n_hash, int64_t buckets, const Tensor& dout,
+               const Tensor& dtable) {
+  cuda_f32(dtable, "dtable");
+  c10::cuda::CUDAGuard g(ids.device());
+  ok(mxk::launch_ngram_bwd(ids.data_ptr<int64_t>(), ids.size(0), ids.size(1), orders.data_ptr<int>(), orders.numel(),
+                           (int)n_hash, (long)buckets, dout.data_ptr(), dtable.size(2), dtable.data_ptr<float>(),
+                           stream()),
+     "ngram_bwd");
+}
+
 }  // namespace
 
 void register_ops(pybind11::module& m) {
@@ -492,6 +514,8 @@ void register_ops(pybind11::module& m) {
   m.def("cast_bf16", &cast_bf16);
   m.def("flash_bwd_sm100", &flash_bwd_sm100);
   m.def("head_norm_rope", &head_norm_rope);
+  m.def("ngram_fwd", &ngram_fwd);
+  m.def("ngram_bwd", &ngram_bwd);
   m.def("kv_append", &kv_append);
   m.def("decode_attention", &decode_attention);
   m.def("ipc_alloc", &ipc_alloc);

@@ -566,3 +566,29 @@ def cross_entropy(h, w_out, labels, weights, z_weight, chunk: int = 8192):
     if not torch.is_grad_enabled() or not (h.requires_grad or w_out.requires_grad):
         return _ce_loss_only(h, w_out, labels, weights, z_weight, chunk)
     return _CrossEntropy.apply(h, w_out, labels, weights, float(z_weight), _CE_GRAD_SCALE[0], chunk)
+
+
+# ------------------------------------------------------------------------ hashed n-gram embedding
+class _NgramEmbed(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, table, orders, n_hash):
+        ids = _c(ids.long())
+        b, s = ids.shape
+        o, buckets, rank = table.shape
+        ords = torch.tensor(list(orders), dtype=torch.int32, device=ids.device)
+        out = torch.empty(b * s, rank, dtype=BF16, device=ids.device)
+        ext().ngram_fwd(ids, ords, n_hash, buckets, _c(table), out)
+        ctx.save_for_backward(ids, ords)
+        ctx.table, ctx.n_hash, ctx.buckets = table, n_hash, buckets
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        ids, ords = ctx.saved_tensors
+        ext().ngram_bwd(ids, ords, ctx.n_hash, ctx.buckets, _c(dout), _mg(ctx.table))
+        ctx.table = None
+        return None, None, None, None
+
+
+def ngram_embed(ids, table, orders, n_hash):
+    return _NgramEmbed.apply(ids, table, tuple(orders), int(n_hash))

@@ -284,3 +284,36 @@ def adamh_matrix_update(p, u, lr: float):
     un = u.norm()
     new = p - lr * u * pn / un.clamp_min(1e-10)
     return new / new.norm() * pn
+
+
+# ------------------------------------------------------------------------ hashed n-gram embedding
+_M64 = (1 << 64) - 1
+
+
+def ngram_buckets(ids: torch.Tensor, n: int, h: int, buckets: int) -> torch.Tensor:
+    """Bucket of the n-gram ending at every position of ``ids [B, S]`` under hash function ``h``
+    (FNV-1a-style 64-bit mix salted by (n, h); positions before the sequence start count as -1)."""
+    import numpy as np
+
+    a = ids.detach().cpu().numpy().astype(np.int64)
+    with np.errstate(over="ignore"):
+        x = np.full(a.shape, 0xcbf29ce484222325 ^ (((n * 131 + h + 1) * 0x9E3779B97F4A7C15) & _M64), dtype=np.uint64)
+        prime = np.uint64(0x100000001B3)
+        for i in range(n):
+            v = np.full(a.shape, -1, dtype=np.int64)
+            v[:, i:] = a[:, : a.shape[1] - i] if i else a
+            x ^= v.astype(np.uint64)
+            x *= prime
+            x ^= x >> np.uint64(29)
+    return torch.from_numpy((x % np.uint64(buckets)).astype(np.int64)).to(ids.device)
+
+
+def ngram_embed(ids: torch.Tensor, table: torch.Tensor, orders, n_hash: int) -> torch.Tensor:
+    """``[B*S, rank]``: mean over (order, hash) of ``table[order][bucket]``."""
+    n_o, buckets, rank = table.shape
+    acc = None
+    for oi, n in enumerate(orders):
+        for h in range(n_hash):
+            rows = table[oi].index_select(0, ngram_buckets(ids, n, h, buckets).reshape(-1))
+            acc = rows if acc is None else acc + rows
+    return acc / (len(orders) * n_hash)

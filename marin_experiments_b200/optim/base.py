@@ -92,7 +92,7 @@ class OptimizerConfig:
 def grug_group_of(name: str, ndim: int) -> str:
     """Parameter-group rule of ``grug_moe_adamh_v2`` (megagpt-speedrun/optimizer.py:80-92)."""
     p = name.lower()
-    if "token_embed" in p:
+    if "token_embed" in p or "ngram_table" in p:
         return "adam"
     # zero-initialised modulation / bias parameters of the looped model: a scale-invariant step
     # cannot move a zero matrix (reentrant/optimizer.py routes them to Adam too)

@@ -234,3 +234,21 @@ def test_embed():
     og.backward(dout.cuda().bfloat16())
     assert rel(og, oc) == 0.0
     assert rel(tg.main_grad, tc.grad) < 1e-5
+
+
+def test_ngram_embed_kernel():
+    from marin_experiments_b200.ops import cuda_fns
+
+    torch.manual_seed(9)
+    table = (torch.randn(3, 1013, 64) / 4).bfloat16()
+    ids = torch.randint(0, 5000, (4, 100))
+    tc = table.float().requires_grad_(True)
+    ref = R.ngram_embed(ids, tc, (2, 3, 4), 2)
+    g = torch.randn_like(ref)
+    ref.backward(g)
+    tg = table.cuda().requires_grad_(True)
+    tg.main_grad = torch.zeros(tg.shape, dtype=torch.float32, device="cuda")
+    out = cuda_fns.ngram_embed(ids.cuda(), tg, (2, 3, 4), 2)
+    out.backward(g.cuda().bfloat16())
+    assert rel(out, ref) < 1e-2
+    assert rel(tg.main_grad, tc.grad) < 2e-2
