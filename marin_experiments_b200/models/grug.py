@@ -67,9 +67,15 @@ class NormPair(nn.Module):
 
 
 class Attention(nn.Module):
-    def __init__(self, cfg: GrugModelConfig, layer: int):
+    tp_sharded_params = ("w_qkv", "attn_gate", "w_o")
+
+    def __init__(self, cfg: GrugModelConfig, layer: int, tp=None):
         super().__init__()
-        d, h, hkv, hd = cfg.hidden_dim, cfg.num_heads, cfg.num_kv_heads, cfg.inferred_head_dim
+        from ..parallel.tp import local_counts
+
+        d, hd = cfg.hidden_dim, cfg.inferred_head_dim
+        h, hkv = local_counts(cfg, tp)  # heads held by this tensor-parallel rank
+        self.tp = tp
         # w_qkv rows: [q heads | k heads | v heads]; attn_gate rows follow it contiguously in the
         # parameter store so one GEMM produces q, k, v and the head-gate logits.
         self.w_qkv = nn.Parameter(torch.empty((h + 2 * hkv) * hd, d))
@@ -79,11 +85,18 @@ class Attention(nn.Module):
         self.cfg = cfg
 
     def forward(self, h, x, batch: int, seq: int, segment_ids=None):
+        from ..parallel.tp import copy_to_tp, local_counts, reduce_from_tp
+
         c = self.cfg
-        shape = ops.AttnShape(batch, seq, c.num_heads, c.num_kv_heads, c.inferred_head_dim, window=self.window,
+        nh, nkv = local_counts(c, self.tp)
+        shape = ops.AttnShape(batch, seq, nh, nkv, c.inferred_head_dim, window=self.window,
                               qk_mult=c.qk_mult, qk_norm=c.qk_norm, xsa=c.xsa, head_gate=c.head_gate,
                               rope_theta=c.rope.theta, llama3=_llama3(c))
-        return ops.attention_block(h, x, self.w_qkv, self.attn_gate, self.w_o, shape, segment_ids)
+        if self.tp is None or self.tp.size == 1:
+            return ops.attention_block(h, x, self.w_qkv, self.attn_gate, self.w_o, shape, segment_ids)
+        part = ops.attention_block(copy_to_tp(h, self.tp), torch.zeros_like(x), self.w_qkv, self.attn_gate,
+                                   self.w_o, shape, segment_ids)
+        return x + reduce_from_tp(part, self.tp)
 
 
 def _llama3(c: GrugModelConfig):
@@ -97,14 +110,25 @@ def _llama3(c: GrugModelConfig):
 class DenseMLP(nn.Module):
     """SwiGLU (``glu``; blocked gate/up rows) or plain activation MLP."""
 
-    def __init__(self, dim: int, inter: int, glu: bool, act: str):
+    tp_sharded_params = ("w_gate_up", "w_down")
+
+    def __init__(self, dim: int, inter: int, glu: bool, act: str, tp=None):
         super().__init__()
+        from ..parallel.tp import local_inter
+
+        inter = local_inter(inter, tp, glu)
         self.w_gate_up = nn.Parameter(torch.empty((2 if glu else 1) * inter, dim))
         self.w_down = nn.Parameter(torch.empty(dim, inter))
-        self.glu, self.act = glu, act
+        self.glu, self.act, self.tp = glu, act, tp
 
     def forward(self, h, residual=None):
-        return ops.dense_mlp(h, self.w_gate_up, self.w_down, glu=self.glu, act=self.act, residual=residual)
+        if self.tp is None or self.tp.size == 1:
+            return ops.dense_mlp(h, self.w_gate_up, self.w_down, glu=self.glu, act=self.act, residual=residual)
+        from ..parallel.tp import copy_to_tp, reduce_from_tp
+
+        part = ops.dense_mlp(copy_to_tp(h, self.tp), self.w_gate_up, self.w_down, glu=self.glu, act=self.act)
+        y = reduce_from_tp(part, self.tp)
+        return y if residual is None else residual + y
 
 
 @dataclass
@@ -168,18 +192,18 @@ class MoEMLP(nn.Module):
 
 
 class Block(nn.Module):
-    def __init__(self, cfg: GrugModelConfig, layer: int, local_experts=None):
+    def __init__(self, cfg: GrugModelConfig, layer: int, local_experts=None, tp=None):
         super().__init__()
         self.attn_norm = NormPair(cfg)
-        self.attn = Attention(cfg, layer)
+        self.attn = Attention(cfg, layer, tp)
         self.mlp_norm = NormPair(cfg)
         if cfg.is_moe:
             self.mlp = MoEMLP(cfg, local_experts)
             self.mlp.layer_key = layer
-            self.shared = (DenseMLP(cfg.hidden_dim, cfg.shared_expert_intermediate_dim, True, "silu")
+            self.shared = (DenseMLP(cfg.hidden_dim, cfg.shared_expert_intermediate_dim, True, "silu", tp)
                            if cfg.shared_expert_intermediate_dim > 0 else None)
         else:
-            self.mlp = DenseMLP(cfg.hidden_dim, cfg.intermediate_dim, cfg.glu, cfg.mlp_activation)
+            self.mlp = DenseMLP(cfg.hidden_dim, cfg.intermediate_dim, cfg.glu, cfg.mlp_activation, tp)
             self.shared = None
         self.cfg = cfg
 
@@ -198,7 +222,7 @@ class Transformer(nn.Module):
     """Grug decoder (megagpt-speedrun/model.py:691-838; tiny-stories/model.py:138-226)."""
 
     def __init__(self, cfg: GrugModelConfig, local_experts=None, layers: range | None = None,
-                 with_embed: bool = True, with_head: bool = True):
+                 with_embed: bool = True, with_head: bool = True, tp=None):
         super().__init__()
         self.cfg = cfg
         d, de, v = cfg.hidden_dim, cfg.inferred_embed_dim, cfg.vocab_size
@@ -212,7 +236,8 @@ class Transformer(nn.Module):
             self.ngram_table = (nn.Parameter(torch.empty(len(ng.orders), ng.hash_buckets, ng.rank))
                                 if ng is not None else None)
             self.ngram_proj = nn.Parameter(torch.empty(d, ng.rank)) if ng is not None else None
-        self.blocks = nn.ModuleList([Block(cfg, i, local_experts) for i in self.layer_ids])
+        self.tp = tp
+        self.blocks = nn.ModuleList([Block(cfg, i, local_experts, tp) for i in self.layer_ids])
         if with_head:
             self.final_norm = NormPair(cfg)
             self.head_down = nn.Parameter(torch.empty(de, d)) if cfg.is_factorized_embed else None
@@ -362,6 +387,15 @@ def init_store_weights(store, cfg: GrugModelConfig, seed: int = 0, model: Transf
     std = cfg.initializer_std
     ranges = {}
     gname = model.global_name if model is not None and hasattr(model, "global_name") else (lambda n: n)
+    mods = dict(model.named_modules()) if model is not None else {}
+
+    def tp_module(name):
+        m = mods.get(name.rsplit(".", 1)[0])
+        tp = getattr(m, "tp", None)
+        leaf = name.rsplit(".", 1)[-1]
+        if tp is not None and tp.size > 1 and leaf in getattr(m, "tp_sharded_params", ()):
+            return m, tp
+        return None, None
     if model is not None:
         for mname, mod in model.named_modules():
             if isinstance(mod, MoEMLP):
@@ -386,5 +420,13 @@ def init_store_weights(store, cfg: GrugModelConfig, seed: int = 0, model: Transf
                     trunc_normal_(v[j], std, gen)
             else:
                 gen = torch.Generator(device=store.device).manual_seed(_seed_for(seed, gname(info.name)))
-                trunc_normal_(v, std, gen)
+                m, tp = tp_module(info.name)
+                if m is not None:  # tensor-parallel shard: slice of the full-size draw
+                    from ..parallel.tp import full_shape, shard
+
+                    full = torch.empty(full_shape(leaf, tuple(v.shape), m, tp), device=store.device)
+                    trunc_normal_(full, std, gen)
+                    v.copy_(shard(leaf, full, m, tp))
+                else:
+                    trunc_normal_(v, std, gen)
     store.sync_compute()

@@ -92,6 +92,21 @@ class FusedOptimizer:
             self.chunks = torch.from_numpy(arr.view(np.uint8).copy()).to(self.store.device)
         self._rows = rows
 
+    def matrix_ids(self, pred) -> list[int]:
+        """AdamH / Adam matrix ids (the chunk table's numbering) of the parameters where ``pred(info)``."""
+        out, mat = [], 0
+        for name in self.names:
+            g = self.groups[name]
+            if g["kind"] == "muon":
+                continue
+            for info in g["infos"]:
+                mats = info.matrices if g["kind"] == "adamh" else [[(info.offset, info.numel)]]
+                for _ in mats:
+                    if pred(info):
+                        out.append(mat)
+                    mat += 1
+        return out
+
     def set_shard(self, lo: int, hi: int) -> None:
         """Keep optimizer state only for the flat range [lo, hi) (ZeRO): the moments shrink to the
         shard, the chunk table covers it, and ``norm_hook`` / ``mat_hook`` must sum the per-group
@@ -142,7 +157,7 @@ class FusedOptimizer:
                 self.norm_hook(self.gnorm2, self.names)
             self.mat_sums.zero_()
             off = self.shard[0] if self.shard is not None else 0
-            if self.shard is None:
+            if self.shard is None and self.mat_hook is None:
                 ext().opt_step(self.chunks, self.nchunks, self.hp, self.gnorm2, grad_scale, st.grad, self.m, self.v,
                                st.master, st.compute, self.mat_sums, self.has_adamh, 0, 0)
             else:
@@ -152,7 +167,7 @@ class FusedOptimizer:
                     self.mat_hook(self.mat_sums)
                 ext().opt_step(self.chunks, self.nchunks, self.hp, self.gnorm2, grad_scale, st.grad, self.m, self.v,
                                st.master, st.compute, self.mat_sums, self.has_adamh, off, 2)
-        elif self.shard is not None:
+        elif self.shard is not None or self.mat_hook is not None:
             self._step_cpu_chunks(t, grad_scale)
         else:
             self._step_cpu(t, grad_scale)
@@ -224,7 +239,7 @@ class FusedOptimizer:
         st = self.store
         b1, b2, eps = cfg.beta1, cfg.beta2, cfg.epsilon
         bc1, bc2 = 1 - b1 ** t, 1 - b2 ** t
-        off = self.shard[0]
+        off = self.shard[0] if self.shard is not None else 0
         gn = torch.zeros(len(self.names), dtype=torch.float64)
         for start, ln, _, gi, _ in self._rows:
             gn[gi] += float((st.grad[start:start + ln].double() * grad_scale).pow(2).sum())

@@ -38,6 +38,7 @@ class ParamInfo:
     # AdamH matrices: list of lists of (start, length) flat ranges (relative to the buffer start)
     matrices: list[list[tuple[int, int]]] = field(default_factory=list)
     sharded_over: str | None = None  # "expert" for expert-parallel shards
+    tp_sharded: bool = False  # a tensor-parallel shard (different on every rank of the TP group)
 
     @property
     def ndim(self) -> int:
@@ -72,10 +73,13 @@ def default_matrices(name: str, shape: tuple[int, ...], offset: int, module: nn.
     if len(shape) < 2:
         return [[(offset, numel)]]
     if leaf == "w_qkv" and module is not None and hasattr(module, "cfg"):
+        from ..parallel.tp import local_counts
+
         c = module.cfg
         hd = c.inferred_head_dim
         d = shape[1]
-        nq, nk = c.num_heads * hd, c.num_kv_heads * hd
+        nh, nkv = local_counts(c, getattr(module, "tp", None))
+        nq, nk = nh * hd, nkv * hd
         return [[(offset, nq * d)], [(offset + nq * d, nk * d)], [(offset + (nq + nk) * d, nk * d)]]
     if len(shape) == 3:
         per = shape[1] * shape[2]
@@ -107,6 +111,9 @@ class ParamStore:
             info.matrices = default_matrices(name, tuple(p.shape), off, module)
             if getattr(module, "expert_range", None) is not None and leaf in ("w_gate_up", "w_down") and p.dim() == 3:
                 info.sharded_over = "expert"
+            tp = getattr(module, "tp", None)
+            if tp is not None and tp.size > 1 and leaf in getattr(module, "tp_sharded_params", ()):
+                info.tp_sharded = True
             self.infos.append(info)
             self._params[name] = p
             off += p.numel()
