@@ -35,7 +35,9 @@ def open_cache(cache_dir: str, seq_len: int, seed: int, shuffle: bool = True):
         meta = json.load(f)
     toks = [os.path.join(cache_dir, s["tokens"]) for s in meta["shards"]]
     docs = [os.path.join(cache_dir, s["docs"]) for s in meta["shards"]]
-    return rt().TokenSeqDataset(toks, docs, seq_len, seed, shuffle)
+    masks = [os.path.join(cache_dir, s["mask"]) for s in meta["shards"]] if all("mask" in s for s in meta["shards"]) \
+        else []
+    return rt().TokenSeqDataset(toks, docs, seq_len, seed, shuffle, masks)
 
 
 def build_dataset(cfg, seq_len: int, vocab_size: int, *, block_size: int = 2048, stop_strategy: str = "restart"):

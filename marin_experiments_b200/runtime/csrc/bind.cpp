@@ -100,9 +100,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            pybind11::arg("doc_len"), pybind11::arg("seed"));
   pybind11::class_<mxrt::TokenSeqDataset, mxrt::Dataset, std::shared_ptr<mxrt::TokenSeqDataset>>(
       m, "TokenSeqDataset")
-      .def(pybind11::init<const std::vector<std::string>&, const std::vector<std::string>&, int, uint64_t, bool>(),
+      .def(pybind11::init<const std::vector<std::string>&, const std::vector<std::string>&, int, uint64_t, bool,
+                          const std::vector<std::string>&>(),
            pybind11::arg("token_files"), pybind11::arg("doc_files"), pybind11::arg("seq_len"),
-           pybind11::arg("seed"), pybind11::arg("shuffle") = true)
+           pybind11::arg("seed"), pybind11::arg("shuffle") = true,
+           pybind11::arg("mask_files") = std::vector<std::string>())
       .def("total_tokens", &mxrt::TokenSeqDataset::total_tokens);
   pybind11::class_<mxrt::MixtureDataset, mxrt::Dataset, std::shared_ptr<mxrt::MixtureDataset>>(m, "MixtureDataset")
       .def(pybind11::init([](std::vector<std::shared_ptr<mxrt::Dataset>> comps, std::vector<uint64_t> starts,

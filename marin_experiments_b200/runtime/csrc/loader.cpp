@@ -88,10 +88,13 @@ void* map_file(const std::string& path, size_t& len) {
 }  // namespace
 
 TokenSeqDataset::TokenSeqDataset(const std::vector<std::string>& token_files,
-                                 const std::vector<std::string>& doc_files, int seq_len, uint64_t seed, bool shuffle)
+                                 const std::vector<std::string>& doc_files, int seq_len, uint64_t seed, bool shuffle,
+                                 const std::vector<std::string>& mask_files)
     : S_(seq_len), seed_(seed), shuffle_(shuffle) {
   if (token_files.size() != doc_files.size() || token_files.empty())
     throw std::runtime_error("token cache needs one document file per token file");
+  if (!mask_files.empty() && mask_files.size() != token_files.size())
+    throw std::runtime_error("token cache needs one mask file per token file (or none)");
   for (size_t i = 0; i < token_files.size(); ++i) {
     Shard s;
     s.map_tok = map_file(token_files[i], s.map_tok_len);
@@ -102,6 +105,11 @@ TokenSeqDataset::TokenSeqDataset(const std::vector<std::string>& token_files,
     s.ndocs = s.map_ends_len / 8;
     if (s.ndocs == 0 || s.ends[s.ndocs - 1] != s.ntok)
       throw std::runtime_error("document offsets of " + doc_files[i] + " do not end at the token count");
+    if (!mask_files.empty()) {
+      s.map_mask = map_file(mask_files[i], s.map_mask_len);
+      s.mask = static_cast<const uint8_t*>(s.map_mask);
+      if (s.map_mask_len != s.ntok) throw std::runtime_error("mask file " + mask_files[i] + " length != token count");
+    }
     base_.push_back(total_);
     total_ += s.ntok;
     shards_.push_back(s);
@@ -114,6 +122,7 @@ TokenSeqDataset::~TokenSeqDataset() {
   for (auto& s : shards_) {
     if (s.map_tok) ::munmap(s.map_tok, s.map_tok_len);
     if (s.map_ends) ::munmap(s.map_ends, s.map_ends_len);
+    if (s.map_mask) ::munmap(s.map_mask, s.map_mask_len);
   }
 }
 
@@ -146,9 +155,12 @@ void TokenSeqDataset::fill(uint64_t idx, const ExampleOut& out) const {
     while (si + 1 < base_.size() && g >= base_[si + 1]) ++si;
     out.tokens[p] = (int32_t)shards_[si].tok[g - base_[si]];
     out.segments[p] = seg;
+    // position p predicts token p + 1: stash that token's mask in loss_weight[p - 1]
+    if (p > 0) out.loss_weight[p - 1] = shards_[si].mask ? (float)shards_[si].mask[g - base_[si]] : 1.f;
   }
-  for (int p = 0; p < S_; ++p)
-    out.loss_weight[p] = (p + 1 < S_ && out.segments[p + 1] == out.segments[p]) ? 1.f : 0.f;
+  out.loss_weight[S_ - 1] = 0.f;
+  for (int p = 0; p + 1 < S_; ++p)
+    if (out.segments[p + 1] != out.segments[p]) out.loss_weight[p] = 0.f;
 }
 
 // --------------------------------------------------------------------------------- mixture

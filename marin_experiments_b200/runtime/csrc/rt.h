@@ -74,7 +74,8 @@ class SyntheticDataset : public Dataset {
 class TokenSeqDataset : public Dataset {
  public:
   TokenSeqDataset(const std::vector<std::string>& token_files, const std::vector<std::string>& doc_files,
-                  int seq_len, uint64_t seed, bool shuffle);
+                  int seq_len, uint64_t seed, bool shuffle,
+                  const std::vector<std::string>& mask_files = std::vector<std::string>());
   ~TokenSeqDataset() override;
   uint64_t size() const override { return n_seq_; }
   int seq_len() const override { return S_; }
@@ -91,6 +92,9 @@ class TokenSeqDataset : public Dataset {
     size_t map_tok_len = 0;
     void* map_ends = nullptr;
     size_t map_ends_len = 0;
+    const uint8_t* mask = nullptr;  // optional per-token loss mask (1 = train on this token)
+    void* map_mask = nullptr;
+    size_t map_mask_len = 0;
   };
   std::vector<Shard> shards_;
   std::vector<uint64_t> base_;  // first global token of each shard
