@@ -129,6 +129,10 @@ class Qwen3Model(nn.Module):
     @torch.no_grad()
     def forward_reference(self, tokens: torch.Tensor) -> torch.Tensor:
         """fp32 logits ``[B, S, V]`` with plain torch ops (the oracle of the serving path)."""
+        return self.forward_logits(tokens)
+
+    def forward_logits(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Differentiable fp32 forward (policy-gradient training of small models)."""
         c = self.cfg
         b, s = tokens.shape
         x = self.embed.float()[tokens]
