@@ -51,3 +51,21 @@ def test_learner_step_updates_policy():
     met = lr.step(n_prompts=2)
     assert set(met) >= {"loss", "reward_mean", "grad_norm"}
     assert not torch.equal(before, m.layers[0].w_q.detach())
+
+
+def test_agent_episode_in_sandbox():
+    import os
+
+    from marin_experiments_b200.rl.agent import AgentTask, LocalSandbox, run_episode
+
+    sb = LocalSandbox()
+    r = sb.exec("echo hi > a.txt && cat a.txt")
+    assert r.stdout.strip() == "hi" and r.exit_code == 0
+    assert sb.exec("sleep 5", timeout=0.5).timed_out
+    sb.close()
+    task = AgentTask("create f.txt containing 42",
+                     check=lambda s: float(open(os.path.join(s.dir, "f.txt")).read().strip() == "42"))
+    script = iter(["<cmd>echo 42 > f.txt</cmd>", "<done/>"])
+    ep = run_episode(lambda msgs: next(script), task)
+    assert ep.reward == 1.0 and ep.turns == 2
+    assert [m["role"] for m in ep.messages] == ["system", "user", "assistant", "tool", "assistant"]
