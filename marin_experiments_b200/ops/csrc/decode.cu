@@ -65,7 +65,8 @@ __global__ void head_norm_rope_kernel(const __nv_bfloat16* __restrict__ x, long 
 }
 
 // cache[seq(r), pos[r], h, :] = src[r, h, :] for keys and values; seq(r) = row_seq[r] (or r).
-__global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v, long src_tok,
+__global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v, long k_tok,
+                                 long v_tok,
                                  __nv_bfloat16* __restrict__ ck, __nv_bfloat16* __restrict__ cv, const int* __restrict__ pos,
                                  const int* __restrict__ row_seq, int rows, int Lmax, int hkv, int hd) {
   const long per = (long)hkv * hd / 8;  // uint4 per token row
@@ -73,8 +74,8 @@ __global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ k, const __nv
     const long b = i / per, c = i % per;
     const long sq = row_seq ? row_seq[b] : b;
     const long dst = ((sq * Lmax + pos[b]) * hkv * hd) / 8 + c;
-    reinterpret_cast<uint4*>(ck)[dst] = reinterpret_cast<const uint4*>(k + b * src_tok)[c];
-    reinterpret_cast<uint4*>(cv)[dst] = reinterpret_cast<const uint4*>(v + b * src_tok)[c];
+    reinterpret_cast<uint4*>(ck)[dst] = reinterpret_cast<const uint4*>(k + b * k_tok)[c];
+    reinterpret_cast<uint4*>(cv)[dst] = reinterpret_cast<const uint4*>(v + b * v_tok)[c];
   }
 }
 
@@ -198,11 +199,12 @@ int launch_head_norm_rope(const void* x, long x_tok, int nh, int hd, const float
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
 }
 
-int launch_kv_append(const void* k, const void* v, long src_tok, void* ck, void* cv, const int* pos,
+int launch_kv_append(const void* k, const void* v, long k_tok, long v_tok, void* ck, void* cv, const int* pos,
                      const int* row_seq, int rows, int Lmax, int hkv, int hd, cudaStream_t st) {
-  if ((hkv * hd) % 8 || src_tok % 8) return kErrBadArgsHost;
+  if ((hkv * hd) % 8 || k_tok % 8 || v_tok % 8) return kErrBadArgsHost;
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) return kErrBadArgsHost;
   count_launch();
-  kv_append_kernel<<<148, 256, 0, st>>>((const __nv_bfloat16*)k, (const __nv_bfloat16*)v, src_tok,
+  kv_append_kernel<<<148, 256, 0, st>>>((const __nv_bfloat16*)k, (const __nv_bfloat16*)v, k_tok, v_tok,
                                         (__nv_bfloat16*)ck, (__nv_bfloat16*)cv, pos, row_seq, rows, Lmax, hkv, hd);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
 }

@@ -133,7 +133,7 @@ int ipc_free(void* ptr);
 // ------------------------------------------------------------------------- decode path (decode.cu)
 int launch_head_norm_rope(const void* x, long x_tok, int nh, int hd, const float* w, float eps, const int* pos,
                           const float* cos_t, const float* sin_t, int T, void* out, cudaStream_t st);
-int launch_kv_append(const void* k, const void* v, long src_tok, void* ck, void* cv, const int* pos,
+int launch_kv_append(const void* k, const void* v, long k_tok, long v_tok, void* ck, void* cv, const int* pos,
                      const int* row_seq, int rows, int Lmax, int hkv, int hd, cudaStream_t st);
 int launch_decode_attention(const void* q, const void* ck, const void* cv, const int* lens, int B, int H, int hkv,
                             int hd, int Lmax, float scale, int nsplit, float* part_ml, float* part_acc, void* out,

@@ -438,10 +438,12 @@ void head_norm_rope(const Tensor& x, int64_t nh, int64_t hd, const OptT& w, doub
 // Rows r of k / v ([rows, Hkv, hd], row stride shared) go to cache[row_seq[r] (or r), pos[r]].
 void kv_append(const Tensor& k, const Tensor& v, const Tensor& ck, const Tensor& cv, const Tensor& pos,
                const OptT& row_seq) {
-  need(k.stride(0) == v.stride(0) && ck.is_contiguous() && cv.is_contiguous(), "kv_append layout");
+  need(ck.is_contiguous() && cv.is_contiguous() && k.stride(-1) == 1 && v.stride(-1) == 1, "kv_append layout");
+  need(k.size(1) * k.size(2) == k.stride(1) * k.size(1) && v.stride(1) == v.size(2), "kv_append head rows");
   need(pos.numel() == k.size(0), "one position per row");
   c10::cuda::CUDAGuard g(k.device());
-  ok(mxk::launch_kv_append(k.data_ptr(), v.data_ptr(), k.stride(0), ck.data_ptr(), cv.data_ptr(), pos.data_ptr<int>(),
+  ok(mxk::launch_kv_append(k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0), ck.data_ptr(), cv.data_ptr(),
+                           pos.data_ptr<int>(),
                            ptr<const int>(row_seq), (int)k.size(0), (int)ck.size(1), (int)ck.size(2), (int)ck.size(3),
                            stream()),
      "kv_append");
