@@ -25,6 +25,11 @@ SHAPES = [
     ("o_dx", 16384, 1536, 1536, "dx"),
     ("o_dw", 16384, 1536, 1536, "dw"),
     ("lm_head_dw", 16384, 128256, 1536, "dw"),
+    # GatedNorm (rank 128) and residual-epilogue shapes
+    ("gatednorm_up_gate_mul", 16384, 1536, 128, "gate_mul"),
+    ("gatednorm_down_silu", 16384, 128, 1536, "silu"),
+    ("o_fwd_resid", 16384, 1536, 1536, "resid"),
+    ("gatednorm_dw_up", 16384, 1536, 128, "dw"),
 ]
 
 
@@ -61,6 +66,21 @@ def run(shapes=SHAPES):
             c = torch.empty(m, k, device="cuda", dtype=torch.bfloat16)
             mine = lambda: G.linear_dx(a, b, out=c)
             ref = lambda: torch.matmul(a, b, out=c)
+        elif mode in ("gate_mul", "resid"):
+            a = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+            b = torch.randn(n, k, device="cuda").to(torch.bfloat16)
+            r = torch.randn(m, n, device="cuda").to(torch.bfloat16)
+            c = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+            mine = lambda: G.gemm(a, b, c, M=m, N=n, K=k, epi=mode, r=r)
+            ref = (lambda: torch.mul(r, torch.sigmoid(torch.matmul(a, b.t())), out=c)) if mode == "gate_mul" else \
+                (lambda: torch.add(r, torch.matmul(a, b.t()), out=c))
+        elif mode == "silu":
+            a = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+            b = torch.randn(n, k, device="cuda").to(torch.bfloat16)
+            c = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+            h = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+            mine = lambda: G.gemm(a, b, c, M=m, N=n, K=k, epi="silu", c2=h)
+            ref = lambda: torch.nn.functional.silu(torch.matmul(a, b.t(), out=h), inplace=False)
         else:  # dw: dy [m, n], x [m, k] -> [n, k] fp32 accumulate
             a = torch.randn(m, n, device="cuda").to(torch.bfloat16)
             b = torch.randn(m, k, device="cuda").to(torch.bfloat16)

@@ -100,6 +100,9 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const 
     L.c2_cols = epi == 1 ? N / 2 : std::min<int64_t>(N, C2->size(1));
     L.c2_rows = G == 1 ? std::min<int64_t>(M, C2->size(0)) : C2->size(0);
     TORCH_CHECK(reinterpret_cast<uintptr_t>(C2->data_ptr()) % 16 == 0, "C2 must be 16-byte aligned");
+    // CE statistics: two (max, sumexp) float pairs per 256-column tile and row
+    TORCH_CHECK(epi != 6 || (L.c2_f32 && C2->size(1) >= 4 * ((N + 255) / 256)),
+                "CE stats must be f32 with 4 floats per 256-column tile");
   }
   if (std::getenv("MXK_TRACE")) { std::fprintf(stderr, "[mxk] binding -> launch_gemm\n"); std::fflush(stderr); }
   check_code(mxk::launch_gemm(L, cur_stream()), "gemm");

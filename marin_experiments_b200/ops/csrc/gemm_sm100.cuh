@@ -28,9 +28,10 @@ namespace mxk {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each on one half of the tile's columns
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxGroups = 256;
-constexpr int kStageBufs = 4;    // epilogue staging ring depth per warp
+constexpr int kStageBufs = 2;    // epilogue staging ring depth per warp
 constexpr int kStageBox = 2048;  // 32 rows x 64 bytes
 
 enum EpiKind : int {
@@ -40,7 +41,7 @@ enum EpiKind : int {
   EPI_GATE_MUL = 3,  // C = X * sigmoid(acc) (bf16), X given in R (GatedNorm up projection)
   EPI_SILU = 4,      // C = silu(acc) (bf16) and H = acc (bf16) (GatedNorm down projection)
   EPI_ROWSCALE = 5,  // C = acc * row_scale[row] (bf16)
-  EPI_CE = 6,        // logits tile: C = acc (bf16) and per-(row, n-tile) max / sum(exp(x - max))
+  EPI_CE = 6,        // logits tile: C = acc (bf16) and per-(row, n-tile half) max / sum(exp(x - max))
   EPI_ACT = 7,       // non-GLU MLP: H = acc (bf16), C = act(acc) (bf16); act in `act_kind`
 };
 
@@ -49,7 +50,7 @@ struct GemmSmem {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kEpiBytes = 4 * kStageBufs * kStageBox;
+  static constexpr int kEpiBytes = kEpiWarps * kStageBufs * kStageBox;
 };
 
 __device__ __forceinline__ int group_count(const GemmParams& p, int g) {
@@ -111,8 +112,9 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, const int*
 __device__ __forceinline__ float apply_act(float x, int kind) {
   if (kind == 1) return fmaxf(x, 0.f);
   if (kind == 2) {
-    float u = 0.7978845608f * (x + 0.044715f * x * x * x);
-    return 0.5f * x * (1.f + tanhf(u));
+    // tanh-approximated GELU, 0.5 x (1 + tanh(u)) = x * sigmoid(2u)
+    const float u = 0.7978845608f * (x + 0.044715f * x * x * x);
+    return x * sigmoid_f(2.f * u);
   }
   return silu_f(x);
 }
@@ -216,7 +218,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 128);
+      mbar_init(&tempty_bar[b], 32 * kEpiWarps);
     }
     mbar_init(drain_bar, 1);
     fence_barrier_init();
@@ -322,6 +324,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------------ epilogue warps
     const int q = warp & 3;  // TMEM lane quadrant accessible by this warp
+    const int half = (warp - 2) >> 2;  // which half of the tile's columns this warp drains
+    constexpr int kHalf = BN / 2;
     EpiRing ring{sEpi + (warp - 2) * kStageBufs * kStageBox, 0};
     const bool reduce = p.c_f32 && p.c_accum != 0;
     int tcount = 0;
@@ -344,7 +348,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if constexpr (EPI == EPI_SWIGLU) {
         static_assert(BN == 256, "SwiGLU epilogue expects [gate 128 | up 128] tiles");
 #pragma unroll 1
-        for (int c = 0; c < 128; c += 32) {
+        for (int c = half * 64; c < half * 64 + 64; c += 32) {
           float gv[32], uv[32];
           tmem_ld32(taddr + c, gv);
           tmem_ld32(taddr + 128 + c, uv);
@@ -365,7 +369,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // Logits tile (bf16) plus per-row (max, sum exp(x - max)) over this tile's valid columns.
         float m = -INFINITY, ssum = 0.f;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = half * kHalf; c < (half + 1) * kHalf; c += 32) {
           float v[32];
           tmem_ld32(taddr + c, v);
           tmem_wait_ld();
@@ -389,13 +393,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
         if (row_ok) {
-          // stats row stride ldc2 is in floats; entry nt holds (max, sumexp)
-          float2* st = reinterpret_cast<float2*>(reinterpret_cast<float*>(p.C2) + crow * p.ldc2 + 2 * tc.nt);
+          // stats row stride ldc2 is in floats; entry 2 nt + half holds (max, sumexp) of the
+          // tile's column half drained by this warp
+          float2* st = reinterpret_cast<float2*>(reinterpret_cast<float*>(p.C2) + crow * p.ldc2) + 2 * tc.nt + half;
           *st = make_float2(m, ssum);
+        }
+      } else if constexpr (EPI == EPI_RESID || EPI == EPI_GATE_MUL) {
+        // R (residual / gate input) rows are read with the next chunk's loads issued before this
+        // chunk's TMEM read, so their latency overlaps the epilogue math (two chunks in flight).
+        const __nv_bfloat16* Rrow = reinterpret_cast<const __nv_bfloat16*>(p.R) + crow * p.ldr;
+        auto load_r = [&](int col, uint4 (&u)[4]) {
+          if (row_ok && col < p.N) {
+            const uint4* Rp = reinterpret_cast<const uint4*>(Rrow + col);
+#pragma unroll
+            for (int vv = 0; vv < 4; ++vv) u[vv] = Rp[vv];
+          } else {
+#pragma unroll
+            for (int vv = 0; vv < 4; ++vv) u[vv] = make_uint4(0, 0, 0, 0);
+          }
+        };
+        auto finish = [&](int c, const uint4 (&u)[4]) {
+          float v[32];
+          tmem_ld32(taddr + c, v);
+          tmem_wait_ld();
+          const int col = col0 + c;
+          if (col >= p.N) return;
+          float o[32];
+#pragma unroll
+          for (int vv = 0; vv < 4; ++vv) {
+            const uint32_t w4[4] = {u[vv].x, u[vv].y, u[vv].z, u[vv].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = unpack_bf16x2(w4[k]);
+              const int i = vv * 8 + 2 * k;
+              o[i] = (EPI == EPI_RESID) ? v[i] + f.x : f.x * sigmoid_f(v[i]);
+              o[i + 1] = (EPI == EPI_RESID) ? v[i + 1] + f.y : f.y * sigmoid_f(v[i + 1]);
+            }
+          }
+          if (p.c_f32) ring.f32_boxes(&tmC, o, col, y0, reduce, lane);
+          else ring.bf16_box(&tmC, o, col, y0, lane);
+        };
+        uint4 ra[4], rb[4];
+        static_assert(kHalf % 64 == 0, "residual epilogue drains 64-column steps");
+        const int c_lo = half * kHalf, c_hi = c_lo + kHalf;
+        load_r(col0 + c_lo, ra);
+#pragma unroll 1
+        for (int c = c_lo; c < c_hi; c += 64) {
+          load_r(col0 + c + 32, rb);
+          finish(c, ra);
+          if (c + 64 < c_hi) load_r(col0 + c + 64, ra);
+          finish(c + 32, rb);
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = half * kHalf; c < (half + 1) * kHalf; c += 32) {
           float v[32];
           tmem_ld32(taddr + c, v);
           tmem_wait_ld();
@@ -405,28 +456,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if constexpr (EPI == EPI_STORE) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = p.alpha * v[i];
-          } else if constexpr (EPI == EPI_RESID || EPI == EPI_GATE_MUL) {
-            float r[32];
-            if (row_ok) {
-              const uint4* Rp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.R) +
-                                                               crow * p.ldr + col);
-#pragma unroll
-              for (int vv = 0; vv < 4; ++vv) {
-                const uint4 u = Rp[vv];
-                const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  const float2 f = unpack_bf16x2(w4[k]);
-                  r[vv * 8 + 2 * k] = f.x;
-                  r[vv * 8 + 2 * k + 1] = f.y;
-                }
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) r[i] = 0.f;
-            }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = (EPI == EPI_RESID) ? v[i] + r[i] : r[i] * sigmoid_f(v[i]);
           } else if constexpr (EPI == EPI_SILU || EPI == EPI_ACT) {
             const int kind = (EPI == EPI_SILU) ? 0 : p.act_kind;
 #pragma unroll

@@ -249,7 +249,11 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
   return __bfloat1622float2(h);
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
-__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// Activations in epilogues and element-wise kernels use the fast exponential and the fast
+// approximate divide (two SFU operations each): a bf16 result needs 8 bits, these give ~21, and
+// the IEEE divide's ~15-instruction sequence made the GEMM epilogues instruction-bound. For very
+// negative x, 1 + e^-x overflows to inf and both return 0 (the limit).
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 }  // namespace mxk

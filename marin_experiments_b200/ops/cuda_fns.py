@@ -506,7 +506,7 @@ class _CrossEntropy(torch.autograd.Function):
         dH = torch.empty(t, de, dtype=BF16, device=dev)
         tc = min(chunk, t)
         logits = torch.empty(tc, vpad, dtype=BF16, device=dev)
-        stats = torch.empty(tc, 2 * nt, dtype=F32, device=dev)
+        stats = torch.empty(tc, 4 * nt, dtype=F32, device=dev)  # (max, sumexp) per tile half
         wg = _mg(w)
         for c0 in range(0, t, tc):
             n = min(tc, t - c0)
@@ -553,7 +553,7 @@ def _ce_loss_only(h, w, labels, weights, z_weight, chunk):
     loss = torch.zeros(1, dtype=F32, device=h.device)
     tc = min(chunk, t)
     logits = torch.empty(tc, nt * 256, dtype=BF16, device=h.device)
-    stats = torch.empty(tc, 2 * nt, dtype=F32, device=h.device)
+    stats = torch.empty(tc, 4 * nt, dtype=F32, device=h.device)
     for c0 in range(0, t, tc):
         n = min(tc, t - c0)
         G.gemm(h[c0:c0 + n], w, logits[:n], M=n, N=v, K=h.shape[1], epi="ce", c2=stats[:n])

@@ -112,8 +112,8 @@ def test_ce_epilogue(G):
     nt = (v + 255) // 256
     vpad = nt * 256
     logits = torch.empty(m, vpad, dtype=torch.bfloat16, device="cuda")
-    stats = torch.empty(m, nt, 2, dtype=torch.float32, device="cuda")
-    G.gemm(h, w, logits, M=m, N=v, K=k, epi="ce", c2=stats.view(m, nt * 2))
+    stats = torch.empty(m, 2 * nt, 2, dtype=torch.float32, device="cuda")  # one entry per tile half
+    G.gemm(h, w, logits, M=m, N=v, K=k, epi="ce", c2=stats.view(m, nt * 4))
     ref = h.float() @ w.float().t()
     assert _rel(logits[:, :v], ref) < 1e-2
     mx, se = stats[..., 0], stats[..., 1]
