@@ -6,6 +6,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+#include <initializer_list>
+
 #include "kernels.h"
 
 namespace mxk {
@@ -40,6 +43,17 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
   *reinterpret_cast<uint4*>(p) = u;
+}
+
+__device__ __forceinline__ void load8f(const float* p, float (&f)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+__device__ __forceinline__ float2 unpack2(uint32_t u) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
 }
 
 __device__ __forceinline__ float sigm(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
@@ -77,17 +91,25 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const fl
 }
 
 // dx = r * (g - xhat * mean(g * xhat)), g = dy * w, xhat = x * r ; dw += sum_rows dy * xhat.
-// dw partials are kept per lane in registers (column slots fixed per lane) and flushed with one
-// atomicAdd per column per block. Optional dres is added to dx (residual-stream gradient).
+// One warp per row; a row's dy and x vectors stay in registers between the two passes and w is
+// staged once per block in shared memory. dw partials are kept per lane in registers (column
+// slots fixed per lane) and flushed with one atomicAdd per column per block. Optional dres is
+// added to dx (residual-stream gradient).
 template <int MAXV>
-__global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
-                                   const float* __restrict__ w, const float* __restrict__ rstd,
-                                   const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
-                                   float* __restrict__ dw, int T, int D) {
-  extern __shared__ float sdw[];  // [D]
+__global__ void __launch_bounds__(256, 2)
+    rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                       const float* __restrict__ w, const float* __restrict__ rstd,
+                       const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
+                       float* __restrict__ dw, int T, int D) {
+  extern __shared__ float sm_rms[];  // [D] dw partials, [D] w
+  float* sdw = sm_rms;
+  float* sw = sm_rms + D;
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
-  for (int c = threadIdx.x; c < D; c += blockDim.x) sdw[c] = 0.f;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    sdw[c] = 0.f;
+    sw[c] = w[c];
+  }
   __syncthreads();
   float acc[MAXV][8];
 #pragma unroll
@@ -96,19 +118,30 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
     for (int i = 0; i < 8; ++i) acc[v][i] = 0.f;
   for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < T; row += gridDim.x * warps) {
     const float r = rstd[row];
+    uint4 gu[MAXV], xu[MAXV];
+#pragma unroll
+    for (int v = 0; v < MAXV; ++v) {
+      const int c = lane * 8 + v * 256;
+      if (c < D) {
+        gu[v] = *reinterpret_cast<const uint4*>(dy + (long)row * D + c);
+        xu[v] = *reinterpret_cast<const uint4*>(x + (long)row * D + c);
+      }
+    }
     float dot = 0.f;
 #pragma unroll
     for (int v = 0; v < MAXV; ++v) {
       const int c = lane * 8 + v * 256;
       if (c < D) {
-        float g[8], xv[8];
-        load8(dy + (long)row * D + c, g);
-        load8(x + (long)row * D + c, xv);
+        float wv[8];
+        load8f(sw + c, wv);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float xh = xv[i] * r;
-          acc[v][i] += g[i] * xh;
-          dot += g[i] * w[c + i] * xh;
+        for (int k = 0; k < 4; ++k) {
+          const float2 g = unpack2(reinterpret_cast<const uint32_t*>(&gu[v])[k]);
+          const float2 xv = unpack2(reinterpret_cast<const uint32_t*>(&xu[v])[k]);
+          const float xh0 = xv.x * r, xh1 = xv.y * r;
+          acc[v][2 * k] += g.x * xh0;
+          acc[v][2 * k + 1] += g.y * xh1;
+          dot += g.x * wv[2 * k] * xh0 + g.y * wv[2 * k + 1] * xh1;
         }
       }
     }
@@ -117,15 +150,19 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
     for (int v = 0; v < MAXV; ++v) {
       const int c = lane * 8 + v * 256;
       if (c < D) {
-        float g[8], xv[8], o[8];
-        load8(dy + (long)row * D + c, g);
-        load8(x + (long)row * D + c, xv);
-        float rr[8];
+        float wv[8], o[8], rr[8];
+        load8f(sw + c, wv);
         if (dres) load8(dres + (long)row * D + c, rr);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          o[i] = r * (g[i] * w[c + i] - xv[i] * r * dot);
-          if (dres) o[i] += rr[i];
+        for (int k = 0; k < 4; ++k) {
+          const float2 g = unpack2(reinterpret_cast<const uint32_t*>(&gu[v])[k]);
+          const float2 xv = unpack2(reinterpret_cast<const uint32_t*>(&xu[v])[k]);
+          o[2 * k] = r * (g.x * wv[2 * k] - xv.x * r * dot);
+          o[2 * k + 1] = r * (g.y * wv[2 * k + 1] - xv.y * r * dot);
+        }
+        if (dres) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] += rr[i];
         }
         store8(dx + (long)row * D + c, o);
       }
@@ -475,6 +512,255 @@ __global__ void xsa_gate_bwd_kernel(const __nv_bfloat16* __restrict__ dout, cons
   }
 }
 
+// ------------------------------------------------------- vectorised head kernels (hd % 16 == 0)
+// G lanes per (token, head): lane c < hd/16 of the group owns the 8-element chunks c and
+// c + hd/16 (for RoPE these hold the element pairs (i, i + hd/2)), so every global access is one
+// 16-byte vector and a per-head reduction is log2(G) xor-shuffles inside an aligned lane group.
+// Lanes past hd/16 (and past the last item) only take part in the shuffles.
+template <int G>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
+
+template <int G>
+__global__ void __launch_bounds__(256)
+    qk_norm_rope_fwd_vec(const __nv_bfloat16* __restrict__ qkv, int ld, __nv_bfloat16* __restrict__ qn,
+                         __nv_bfloat16* __restrict__ kn, float* __restrict__ rstd, const float* __restrict__ cos_t,
+                         const float* __restrict__ sin_t, int T, int S, int H, int Hkv, int hd, int qk_norm,
+                         float qk_mult, float eps) {
+  const int NH = H + Hkv, half = hd >> 1, nc = hd >> 4;
+  // block (G x heads, positions); grid (position blocks, sequences, head blocks)
+  const int pos = blockIdx.x * blockDim.y + threadIdx.y;
+  const long tl = (long)blockIdx.y * S + pos;
+  const int hh = blockIdx.z * (blockDim.x / G) + threadIdx.x / G;
+  const int c = threadIdx.x & (G - 1);
+  const bool valid = pos < S && tl < T && hh < NH;
+  const bool act = valid && c < nc;
+  const long t = valid ? tl : 0;
+  const int h = valid ? hh : 0;
+  float a[8], b[8];
+  float ss = 0.f;
+  const __nv_bfloat16* src = qkv + (long)t * ld + h * hd + 8 * c;
+  if (act) {
+    load8(src, a);
+    load8(src + half, b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += a[i] * a[i] + b[i] * b[i];
+  }
+  float r = 1.f;
+  if (qk_norm) {
+    r = rsqrtf(group_sum<G>(ss) / hd + eps);
+    if (valid && c == 0) rstd[(long)t * NH + h] = r;
+  }
+  if (!act) return;
+  float cs[8], sn[8];
+  load8f(cos_t + (long)pos * half + 8 * c, cs);
+  load8f(sin_t + (long)pos * half + 8 * c, sn);
+  const float mult = h < H ? qk_mult : 1.f;
+  float o1[8], o2[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    // the normalised value is rounded to the activation dtype before RoPE, as in the oracle
+    const float x1 = bf16r(a[i] * r), x2 = bf16r(b[i] * r);
+    o1[i] = bf16r(x1 * cs[i] - x2 * sn[i]) * mult;
+    o2[i] = bf16r(x2 * cs[i] + x1 * sn[i]) * mult;
+  }
+  __nv_bfloat16* dst = (h < H ? qn + ((long)t * H + h) * hd : kn + ((long)t * Hkv + (h - H)) * hd) + 8 * c;
+  store8(dst, o1);
+  store8(dst + half, o2);
+}
+
+template <int G>
+__global__ void __launch_bounds__(256)
+    qk_norm_rope_bwd_vec(const __nv_bfloat16* __restrict__ dqn, const __nv_bfloat16* __restrict__ dkn,
+                         const __nv_bfloat16* __restrict__ qkv, int ld, const float* __restrict__ rstd,
+                         const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                         __nv_bfloat16* __restrict__ dqkv, int T, int S, int H, int Hkv, int hd, int qk_norm,
+                         float qk_mult) {
+  const int NH = H + Hkv, half = hd >> 1, nc = hd >> 4;
+  // block (G x heads, positions); grid (position blocks, sequences, head blocks)
+  const int pos = blockIdx.x * blockDim.y + threadIdx.y;
+  const long tl = (long)blockIdx.y * S + pos;
+  const int hh = blockIdx.z * (blockDim.x / G) + threadIdx.x / G;
+  const int c = threadIdx.x & (G - 1);
+  const bool valid = pos < S && tl < T && hh < NH;
+  const bool act = valid && c < nc;
+  const long t = valid ? tl : 0;
+  const int h = valid ? hh : 0;
+  float dn1[8], dn2[8], n1[8], n2[8];
+  float dot = 0.f, r = 1.f;
+  if (act) {
+    const __nv_bfloat16* g = (h < H ? dqn + ((long)t * H + h) * hd : dkn + ((long)t * Hkv + (h - H)) * hd) + 8 * c;
+    const __nv_bfloat16* src = qkv + (long)t * ld + h * hd + 8 * c;
+    float g1[8], g2[8], cs[8], sn[8];
+    load8(g, g1);
+    load8(g + half, g2);
+    load8(src, n1);
+    load8(src + half, n2);
+    load8f(cos_t + (long)pos * half + 8 * c, cs);
+    load8f(sin_t + (long)pos * half + 8 * c, sn);
+    const float mult = h < H ? qk_mult : 1.f;
+    if (qk_norm) r = rstd[(long)t * NH + h];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float a = g1[i] * mult, b = g2[i] * mult;
+      dn1[i] = a * cs[i] + b * sn[i];  // RoPE^T
+      dn2[i] = b * cs[i] - a * sn[i];
+      n1[i] *= r;
+      n2[i] *= r;
+      dot += dn1[i] * n1[i] + dn2[i] * n2[i];
+    }
+  }
+  if (qk_norm) dot = group_sum<G>(dot) / hd;
+  if (!act) return;
+  if (qk_norm) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      dn1[i] = r * (dn1[i] - n1[i] * dot);
+      dn2[i] = r * (dn2[i] - n2[i] * dot);
+    }
+  }
+  __nv_bfloat16* dst = dqkv + (long)t * ld + h * hd + 8 * c;
+  store8(dst, dn1);
+  store8(dst + half, dn2);
+}
+
+template <int G>
+__global__ void __launch_bounds__(256)
+    xsa_gate_fwd_vec(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __restrict__ qkv, int ld, int voff,
+                     int goff, __nv_bfloat16* __restrict__ out, int T, int H, int Hkv, int hd, int xsa, int gate) {
+  const int rep = H / Hkv, nc = hd >> 4;
+  // block (G x heads, tokens); grid (token blocks, 1, head blocks)
+  const long tl = (long)blockIdx.x * blockDim.y + threadIdx.y;
+  const int hh = blockIdx.z * (blockDim.x / G) + threadIdx.x / G;
+  const int c = threadIdx.x & (G - 1);
+  const bool valid = tl < T && hh < H;
+  const bool act = valid && c < nc;
+  const long t = valid ? tl : 0;
+  const int h = valid ? hh : 0;
+  float y0[8], y1[8], v0[8], v1[8];
+  float dot = 0.f, vn = 0.f;
+  if (act) {
+    const __nv_bfloat16* yr = y + ((long)t * H + h) * hd + 8 * c;
+    const __nv_bfloat16* vr = qkv + (long)t * ld + voff + (h / rep) * hd + 8 * c;
+    load8(yr, y0);
+    load8(yr + 8 * nc, y1);
+    load8(vr, v0);
+    load8(vr + 8 * nc, v1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      dot += y0[i] * v0[i] + y1[i] * v1[i];
+      vn += v0[i] * v0[i] + v1[i] * v1[i];
+    }
+  }
+  float cc = 0.f;
+  if (xsa) cc = group_sum<G>(dot) / (group_sum<G>(vn) + 1e-6f);
+  if (!act) return;
+  const float gmul = gate ? 2.f * sigm(__bfloat162float(qkv[(long)t * ld + goff + h])) : 1.f;
+  float o0[8], o1[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    o0[i] = gmul * (y0[i] - cc * v0[i]);
+    o1[i] = gmul * (y1[i] - cc * v1[i]);
+  }
+  __nv_bfloat16* o = out + ((long)t * H + h) * hd + 8 * c;
+  store8(o, o0);
+  store8(o + 8 * nc, o1);
+}
+
+// Operands stay packed (bf16 pairs) in registers and are unpacked at each use, which keeps the
+// kernel at 3 resident blocks per SM without spills.
+__device__ __forceinline__ float pk_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float pk_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+__device__ __forceinline__ float pk_at(const uint4 (&u)[2], int i) {
+  const uint32_t w = reinterpret_cast<const uint32_t*>(&u[i >> 3])[(i & 7) >> 1];
+  return (i & 1) ? pk_hi(w) : pk_lo(w);
+}
+
+template <int G>
+__global__ void __launch_bounds__(256, 3)
+    xsa_gate_bwd_vec(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ y,
+                     const __nv_bfloat16* __restrict__ qkv, int ld, int voff, int goff, __nv_bfloat16* __restrict__ dy,
+                     __nv_bfloat16* __restrict__ dqkv, int T, int H, int Hkv, int hd, int xsa, int gate) {
+  const int rep = H / Hkv, nc = hd >> 4;
+  // block (G x kv heads, tokens); grid (token blocks, 1, kv-head blocks)
+  const long tl = (long)blockIdx.x * blockDim.y + threadIdx.y;
+  const int hh = blockIdx.z * (blockDim.x / G) + threadIdx.x / G;
+  const int c = threadIdx.x & (G - 1);
+  const bool valid = tl < T && hh < Hkv;
+  const bool act = valid && c < nc;
+  const long t = valid ? tl : 0;
+  const int kh = valid ? hh : 0;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  uint4 vp[2] = {zero, zero};
+  float dv[16];
+  float vn = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) dv[i] = 0.f;
+  if (act) {
+    const __nv_bfloat16* vr = qkv + t * ld + voff + kh * hd + 8 * c;
+    vp[0] = *reinterpret_cast<const uint4*>(vr);
+    vp[1] = *reinterpret_cast<const uint4*>(vr + 8 * nc);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) vn += pk_at(vp, i) * pk_at(vp, i);
+  }
+  const float n = group_sum<G>(vn) + 1e-6f;
+  for (int h = kh * rep; h < (kh + 1) * rep; ++h) {
+    uint4 yp[2] = {zero, zero}, zp[2] = {zero, zero};
+    float yd = 0.f;
+    if (act) {
+      const __nv_bfloat16* yr = y + (t * H + h) * hd + 8 * c;
+      const __nv_bfloat16* dr = dout + (t * H + h) * hd + 8 * c;
+      yp[0] = *reinterpret_cast<const uint4*>(yr);
+      yp[1] = *reinterpret_cast<const uint4*>(yr + 8 * nc);
+      zp[0] = *reinterpret_cast<const uint4*>(dr);
+      zp[1] = *reinterpret_cast<const uint4*>(dr + 8 * nc);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) yd += pk_at(yp, i) * pk_at(vp, i);
+    }
+    const float lg = (gate && valid) ? __bfloat162float(qkv[t * ld + goff + h]) : 0.f;
+    const float s = sigm(lg);
+    const float gmul = gate ? 2.f * s : 1.f;
+    const float cc = xsa ? group_sum<G>(yd) / n : 0.f;
+    // dgate: d(out)/d(logit) = z * 2 s (1 - s); zd = (gmul z) . v
+    float gd = 0.f, zd = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float z = pk_at(zp, i), vv = pk_at(vp, i);
+      gd += z * (pk_at(yp, i) - cc * vv);
+      zd += z * vv;
+    }
+    zd *= gmul;
+    if (gate) {
+      gd = group_sum<G>(gd);
+      if (valid && c == 0) dqkv[t * ld + goff + h] = __float2bfloat16(gd * 2.f * s * (1.f - s));
+    }
+    const float a = xsa ? group_sum<G>(zd) / n : 0.f;
+    if (act) {
+      float d[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float z = gmul * pk_at(zp, i), vv = pk_at(vp, i);
+        d[i] = z - a * vv;
+        if (xsa) dv[i] += -a * pk_at(yp, i) - cc * z + 2.f * cc * a * vv;
+      }
+      __nv_bfloat16* dyr = dy + (t * H + h) * hd + 8 * c;
+      store8(dyr, *reinterpret_cast<const float(*)[8]>(d));
+      store8(dyr + 8 * nc, *reinterpret_cast<const float(*)[8]>(d + 8));
+    }
+  }
+  if (act) {
+    __nv_bfloat16* dvr = dqkv + t * ld + voff + kh * hd + 8 * c;
+    store8(dvr, *reinterpret_cast<const float(*)[8]>(dv));
+    store8(dvr + 8 * nc, *reinterpret_cast<const float(*)[8]>(dv + 8));
+  }
+}
+
 // ------------------------------------------------------------------------- cross-entropy grad
 // One block per row of a logits chunk [rows, ldl] (bf16, V valid columns) with per-tile stats
 // (max, sumexp) [rows, nt]. Computes lse, the weighted loss term, and overwrites the logits with
@@ -563,27 +849,17 @@ void launch_rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int
 void launch_rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, const void* dres, void* dx,
                         float* dw, int T, int D, cudaStream_t st) {
   const int blocks = T < 148 * 8 * 2 ? (T + 7) / 8 : 148 * 2;
-  const size_t sm = (size_t)D * sizeof(float);
-  if (D <= 256) {
-    count_launch();
-    rmsnorm_bwd_kernel<1><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd,
-                                                  (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D);
-  }
-  else if (D <= 1024) {
-    count_launch();
-    rmsnorm_bwd_kernel<4><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd,
-                                                  (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D);
-  }
-  else if (D <= 2048) {
-    count_launch();
-    rmsnorm_bwd_kernel<8><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd,
-                                                  (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D);
-  }
-  else {
-    count_launch();
-    rmsnorm_bwd_kernel<16><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd,
-                                                   (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D);
-  }
+  const size_t sm = 2 * (size_t)D * sizeof(float);
+#define RB(V) rmsnorm_bwd_kernel<V><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd, \
+                                                            (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D)
+  count_launch();
+  if (D <= 256) RB(1);
+  else if (D <= 512) RB(2);
+  else if (D <= 1024) RB(4);
+  else if (D <= 1536) RB(6);
+  else if (D <= 2048) RB(8);
+  else RB(16);
+#undef RB
 }
 
 void launch_embed_fwd(const int64_t* ids, const void* table, void* out, int T, int D, int V, cudaStream_t st) {
@@ -617,10 +893,50 @@ void launch_swiglu_bwd(const void* dact, const void* H, void* dH, long rows, int
       (const __nv_bfloat16*)dact, (const __nv_bfloat16*)H, (__nv_bfloat16*)dH, rows, I, kind, counts, cap);
 }
 
+namespace {
+// The vectorised head kernels need hd a multiple of 16 (two 16-byte chunks per lane), hd <= 256,
+// 16-byte aligned rows and offsets; anything else takes the warp-per-head kernels.
+inline int head_group(int hd) { return hd <= 64 ? 4 : hd <= 128 ? 8 : 16; }
+inline bool vec_ok(int hd, long ld, std::initializer_list<const void*> ptrs) {
+  if (hd % 16 || hd > 256 || ld % 8) return false;
+  for (const void* q : ptrs)
+    if (reinterpret_cast<uintptr_t>(q) & 15) return false;
+  return true;
+}
+// Launch shape of the vectorised head kernels: heads_per_block heads of G lanes along x, rows
+// (positions or tokens) along y up to 256 threads, head blocks along z.
+struct HeadLaunch {
+  dim3 grid, block;
+};
+inline HeadLaunch head_launch(int g, int heads, long rows_x, int rows_y) {
+  const int hb = std::min(heads, 256 / g);
+  const int tpb = std::max(1, 256 / (g * hb));
+  HeadLaunch L;
+  L.block = dim3(g * hb, tpb, 1);
+  L.grid = dim3((unsigned)((rows_x + tpb - 1) / tpb), (unsigned)rows_y, (unsigned)((heads + hb - 1) / hb));
+  return L;
+}
+}  // namespace
+
+#define MXK_HEAD_VEC(KERNEL, HEADS, ROWS_X, ROWS_Y, ...)                               \
+  do {                                                                                 \
+    const int g_ = head_group(hd);                                                     \
+    const HeadLaunch L_ = head_launch(g_, HEADS, ROWS_X, ROWS_Y);                      \
+    if (g_ == 4) KERNEL<4><<<L_.grid, L_.block, 0, st>>>(__VA_ARGS__);                 \
+    else if (g_ == 8) KERNEL<8><<<L_.grid, L_.block, 0, st>>>(__VA_ARGS__);            \
+    else KERNEL<16><<<L_.grid, L_.block, 0, st>>>(__VA_ARGS__);                        \
+  } while (0)
+
 void launch_qk_norm_rope_fwd(const void* qkv, int ld, void* qn, void* kn, float* rstd, const float* cos_t,
                              const float* sin_t, int T, int S, int H, int Hkv, int hd, int qk_norm, float qk_mult,
                              cudaStream_t st) {
   count_launch();
+  if (vec_ok(hd, ld, {qkv, qn, kn, cos_t, sin_t})) {
+    MXK_HEAD_VEC(qk_norm_rope_fwd_vec, H + Hkv, S, (T + S - 1) / S, (const __nv_bfloat16*)qkv, ld,
+                 (__nv_bfloat16*)qn, (__nv_bfloat16*)kn, rstd, cos_t, sin_t, T, S, H, Hkv, hd, qk_norm, qk_mult,
+                 1e-6f);
+    return;
+  }
   qk_norm_rope_fwd_kernel<<<grid_for((long)T * (H + Hkv), 8), 256, 0, st>>>(
       (const __nv_bfloat16*)qkv, ld, (__nv_bfloat16*)qn, (__nv_bfloat16*)kn, rstd, cos_t, sin_t, T, S, H, Hkv, hd,
       qk_norm, qk_mult, 1e-6f);
@@ -630,6 +946,12 @@ void launch_qk_norm_rope_bwd(const void* dqn, const void* dkn, const void* qkv, 
                              const float* cos_t, const float* sin_t, void* dqkv, int T, int S, int H, int Hkv,
                              int hd, int qk_norm, float qk_mult, cudaStream_t st) {
   count_launch();
+  if (vec_ok(hd, ld, {dqn, dkn, qkv, dqkv, cos_t, sin_t})) {
+    MXK_HEAD_VEC(qk_norm_rope_bwd_vec, H + Hkv, S, (T + S - 1) / S, (const __nv_bfloat16*)dqn,
+                 (const __nv_bfloat16*)dkn, (const __nv_bfloat16*)qkv, ld, rstd, cos_t, sin_t, (__nv_bfloat16*)dqkv,
+                 T, S, H, Hkv, hd, qk_norm, qk_mult);
+    return;
+  }
   qk_norm_rope_bwd_kernel<<<grid_for((long)T * (H + Hkv), 8), 256, 0, st>>>(
       (const __nv_bfloat16*)dqn, (const __nv_bfloat16*)dkn, (const __nv_bfloat16*)qkv, ld, rstd, cos_t, sin_t,
       (__nv_bfloat16*)dqkv, T, S, H, Hkv, hd, qk_norm, qk_mult);
@@ -638,6 +960,11 @@ void launch_qk_norm_rope_bwd(const void* dqn, const void* dkn, const void* qkv, 
 void launch_xsa_gate_fwd(const void* y, const void* qkv, int ld, int voff, int goff, void* out, int T, int H,
                          int Hkv, int hd, int xsa, int gate, cudaStream_t st) {
   count_launch();
+  if (voff % 8 == 0 && vec_ok(hd, ld, {y, qkv, out})) {
+    MXK_HEAD_VEC(xsa_gate_fwd_vec, H, T, 1, (const __nv_bfloat16*)y, (const __nv_bfloat16*)qkv, ld, voff, goff,
+                 (__nv_bfloat16*)out, T, H, Hkv, hd, xsa, gate);
+    return;
+  }
   xsa_gate_fwd_kernel<<<grid_for((long)T * H, 8), 256, 0, st>>>((const __nv_bfloat16*)y, (const __nv_bfloat16*)qkv,
                                                                 ld, voff, goff, (__nv_bfloat16*)out, T, H, Hkv, hd,
                                                                 xsa, gate);
@@ -646,10 +973,17 @@ void launch_xsa_gate_fwd(const void* y, const void* qkv, int ld, int voff, int g
 void launch_xsa_gate_bwd(const void* dout, const void* y, const void* qkv, int ld, int voff, int goff, void* dy,
                          void* dqkv, int T, int H, int Hkv, int hd, int xsa, int gate, cudaStream_t st) {
   count_launch();
+  if (voff % 8 == 0 && vec_ok(hd, ld, {dout, y, qkv, dy, dqkv})) {
+    MXK_HEAD_VEC(xsa_gate_bwd_vec, Hkv, T, 1, (const __nv_bfloat16*)dout, (const __nv_bfloat16*)y,
+                 (const __nv_bfloat16*)qkv, ld, voff, goff, (__nv_bfloat16*)dy, (__nv_bfloat16*)dqkv, T, H, Hkv, hd,
+                 xsa, gate);
+    return;
+  }
   xsa_gate_bwd_kernel<<<grid_for((long)T * Hkv, 8), 256, 0, st>>>(
       (const __nv_bfloat16*)dout, (const __nv_bfloat16*)y, (const __nv_bfloat16*)qkv, ld, voff, goff,
       (__nv_bfloat16*)dy, (__nv_bfloat16*)dqkv, T, H, Hkv, hd, xsa, gate);
 }
+#undef MXK_HEAD_VEC
 
 void launch_ce_grad(void* logits, int ldl, const float* stats, int nt, const int64_t* labels, const float* weights,
                     const float* wsum, float* loss_out, float* lse_out, int rows, int V, float z_weight, float scale,

@@ -7,6 +7,8 @@
 //  dispatch_plan: capacity-layout slots in first-come-first-served token-major order.
 //  permute / combine / combine_bwd / unpermute_add: gathers between token order and the
 //                 [E, C, D] capacity layout (rows past an expert's count stay zero up to 128).
+#include <algorithm>
+
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -37,10 +39,11 @@ __global__ void router_fwd_kernel(const float* __restrict__ logits, int ldl, con
                                   float* __restrict__ topb, float* __restrict__ alpha, float* __restrict__ lse_out,
                                   uint8_t* __restrict__ keep, float* __restrict__ counts, float* __restrict__ psum,
                                   float* __restrict__ scalars /* [zsum, expected, realized] */) {
-  extern __shared__ float sm[];  // [E] counts, [E] psum
+  extern __shared__ float sm[];  // [E] counts, [E] psum, [3] block scalars
   float* s_cnt = sm;
   float* s_ps = sm + E;
-  for (int i = threadIdx.x; i < 2 * E; i += blockDim.x) sm[i] = 0.f;
+  float* s_sc = sm + 2 * E;
+  for (int i = threadIdx.x; i < 2 * E + 3; i += blockDim.x) sm[i] = 0.f;
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
@@ -130,12 +133,15 @@ __global__ void router_fwd_kernel(const float* __restrict__ logits, int ldl, con
     }
     if (KK <= K && lane == 0) alpha[t] = -INFINITY;
   }
+  // block totals first: one global atomic per block and scalar (same-address global atomics
+  // from every warp serialise in L2)
   if (lane == 0) {
-    atomicAdd(&scalars[0], z_acc);
-    atomicAdd(&scalars[1], exp_acc);
-    atomicAdd(&scalars[2], real_acc);
+    atomicAdd(&s_sc[0], z_acc);
+    atomicAdd(&s_sc[1], exp_acc);
+    atomicAdd(&s_sc[2], real_acc);
   }
   __syncthreads();
+  if (threadIdx.x < 3) atomicAdd(&scalars[threadIdx.x], s_sc[threadIdx.x]);
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     atomicAdd(&counts[e], s_cnt[e]);
     atomicAdd(&psum[e], s_ps[e]);
@@ -475,8 +481,9 @@ inline int grid_for(long work, int per_block) {
 int launch_router_fwd(const float* logits, int ldl, const float* bias, int T, int E, int K, int adaptive,
                       const float* theta, int k_min, float temp, int* sel, float* comb, float* topb, float* alpha,
                       float* lse, uint8_t* keep, float* counts, float* psum, float* scalars, cudaStream_t st) {
-  const int grid = grid_for(T, 8);
-  const size_t sm = 2 * E * sizeof(float);
+  // a few warps' worth of tokens per block keeps the per-block flush of 2E + 3 atomics small
+  const int grid = std::min(grid_for(T, 8), 148 * 4);
+  const size_t sm = (2 * E + 3) * sizeof(float);
 #define RF(EPL) router_fwd_kernel<EPL><<<grid, 256, sm, st>>>(logits, ldl, bias, T, E, K, adaptive, theta, k_min, \
                                                              temp, sel, comb, topb, alpha, lse, keep, counts, psum, scalars)
   count_launch();

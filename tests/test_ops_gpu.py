@@ -252,3 +252,39 @@ def test_ngram_embed_kernel():
     out.backward(g.cuda().bfloat16())
     assert rel(out, ref) < 1e-2
     assert rel(tg.main_grad, tc.grad) < 2e-2
+
+
+@pytest.mark.parametrize("hd,heads,kv", [(72, 3, 1), (80, 2, 2), (256, 2, 1), (64, 6, 2)])
+def test_qk_norm_rope_kernels(hd, heads, kv):
+    """QK-norm + RoPE forward and backward against fp32 autograd for head sizes on both kernel
+    paths (16-byte vectors for hd % 16 == 0, one warp per head otherwise)."""
+    from marin_experiments_b200.ops._ext import ext
+
+    torch.manual_seed(2)
+    s, t, eps, mult = 64, 128, 1e-6, 0.7
+    nq, nk = heads * hd, kv * hd
+    ld = nq + 2 * nk + 8
+    qkv = bf(torch.randn(t, ld)).cuda().bfloat16()
+    cos, sin = api.rope_tables(s, hd, 10000.0, "cuda")
+    qn = torch.empty(t, heads, hd, dtype=torch.bfloat16, device="cuda")
+    kn = torch.empty(t, kv, hd, dtype=torch.bfloat16, device="cuda")
+    rstd = torch.empty(t, heads + kv, dtype=torch.float32, device="cuda")
+    ext().qk_norm_rope_fwd(qkv, qn, kn, rstd, cos, sin, s, heads, kv, hd, True, mult)
+
+    raw = qkv.float().cpu()[:, :nq + nk].reshape(t, heads + kv, hd).requires_grad_(True)
+    n = raw * torch.rsqrt(raw.pow(2).mean(-1, keepdim=True) + eps)
+    pos = torch.arange(t) % s
+    c, sn = cos.cpu()[pos][:, None, :], sin.cpu()[pos][:, None, :]
+    x1, x2 = n[..., :hd // 2], n[..., hd // 2:]
+    ref = torch.cat([x1 * c - x2 * sn, x2 * c + x1 * sn], -1)
+    ref = ref * torch.tensor([mult] * heads + [1.0] * kv)[None, :, None]
+    assert rel(qn, ref[:, :heads]) < 1e-2
+    assert rel(kn, ref[:, heads:]) < 1e-2
+
+    g = bf(torch.randn(t, heads + kv, hd))
+    ref.backward(g)
+    dqkv = torch.zeros(t, ld, dtype=torch.bfloat16, device="cuda")
+    gq = g[:, :heads].contiguous().cuda().bfloat16()
+    gk = g[:, heads:].contiguous().cuda().bfloat16()
+    ext().qk_norm_rope_bwd(gq, gk, qkv, rstd, cos, sin, dqkv, s, heads, kv, hd, True, mult)
+    assert rel(dqkv[:, :nq + nk].reshape(t, heads + kv, hd), raw.grad) < 2e-2
