@@ -104,13 +104,27 @@ int num_sms() {
   return n;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+// CTA-pair (cta_group::2) tiles are used for BN = 256 problems whose row tiles of 256 stay
+// inside each group; MXK_GEMM_PAIR=0 turns them off.
+static bool pair_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = std::getenv("MXK_GEMM_PAIR");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR>
 static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
   MXK_TRACE("launch_impl enter");
+  constexpr int TM = PAIR ? 2 * kBM : kBM;
+  constexpr int BNL = PAIR ? BN / 2 : BN;
   CUtensorMap ta, tb, tc, tc2;
-  // A tile: K-major -> box {64 (K), 128 rows}; MN-major -> box {64 (M), 64 (K rows)}
+  // A tile: K-major -> box {64 (K), 128 rows}; MN-major -> box {64 (M), 64 (K rows)}.
+  // B tile (this CTA's BNL rows): K-major -> box {64 (K), BNL rows}; MN-major -> {64 (N), 64}.
   if (!make_tmap_bf16_2d(&ta, L.a, L.a_inner, L.a_outer, L.lda, 64, A_MN ? 64 : kBM)) return kErrBadArgs;
-  if (!make_tmap_bf16_2d(&tb, L.b, L.b_inner, L.b_outer, L.ldb, 64, B_MN ? 64 : BN)) return kErrBadArgs;
+  if (!make_tmap_bf16_2d(&tb, L.b, L.b_inner, L.b_outer, L.ldb, 64, B_MN ? 64 : BNL)) return kErrBadArgs;
   if (!make_tmap_epi(&tc, L.p.C, L.p.c_f32 != 0, L.c_cols, L.c_rows, L.p.ldc)) return kErrBadArgs;
   if (L.p.C2 != nullptr && EPI != EPI_CE) {
     if (!make_tmap_epi(&tc2, L.p.C2, L.c2_f32 != 0, L.c2_cols, L.c2_rows, L.p.ldc2)) return kErrBadArgs;
@@ -118,8 +132,8 @@ static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
     tc2 = tc;
   }
   MXK_TRACE("tmaps");
-  auto kern = gemm_sm100_kernel<BN, STAGES, A_MN, B_MN, EPI>;
-  constexpr int smem = gemm_smem_bytes<BN, STAGES>();
+  auto kern = gemm_sm100_kernel<BN, STAGES, A_MN, B_MN, EPI, PAIR>;
+  constexpr int smem = gemm_smem_bytes<BN, STAGES, PAIR>();
   static_assert(smem <= 232448, "shared memory budget exceeded");
   static bool attr_set = false;
   if (!attr_set) {
@@ -129,14 +143,15 @@ static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
   }
   GemmParams p = L.p;
   const int n_tiles = (p.N + BN - 1) / BN;
-  const int m_tiles = (p.M + kBM - 1) / kBM;
+  const int m_tiles = (p.M + TM - 1) / TM;
+  const int units = PAIR ? num_sms() / 2 : num_sms();  // concurrently running tile workers
   long long tiles = (long long)p.G * m_tiles * n_tiles;
-  // Split K over CTAs when a non-grouped fp32 accumulation has too few output tiles for the GPU;
-  // the partial sums are combined by the element-wise atomic TMA reduce-add.
+  // Split K over workers when a non-grouped fp32 accumulation has too few output tiles for the
+  // GPU; the partial sums are combined by the element-wise atomic TMA reduce-add.
   p.ksplit = 1;
-  if (p.G == 1 && p.ragged == 0 && p.c_f32 && p.c_accum && tiles < 2 * num_sms()) {
+  if (p.G == 1 && p.ragged == 0 && p.c_f32 && p.c_accum && tiles < 2 * units) {
     const int nkb = (p.K + kBK - 1) / kBK;
-    int ks = (int)((2 * num_sms() + tiles - 1) / tiles);
+    int ks = (int)((2 * units + tiles - 1) / tiles);
     ks = ks < nkb ? ks : nkb;
     if (ks > 1) {
       const int per = (nkb + ks - 1) / ks;
@@ -145,18 +160,40 @@ static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
       tiles *= ks;
     }
   }
-  int grid = (int)(tiles < num_sms() ? tiles : num_sms());
-  if (grid <= 0) return 0;
+  const int workers = (int)(tiles < units ? tiles : units);
+  if (workers <= 0) return 0;
   MXK_TRACE("launch");
   count_launch();
-  kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, tc, tc2, p);
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * workers, 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, tc2, p) != cudaSuccess) return kErrBadArgs;
+  } else {
+    kern<<<workers, kGemmThreads, smem, stream>>>(ta, tb, tc, tc2, p);
+  }
   MXK_TRACE("launched");
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgs;
 }
 
 #define MXK_CASE(BN_, ST_, AMN_, BMN_, EPI_)                                                     \
   if (L.bn == BN_ && L.a_mn == AMN_ && L.b_mn == BMN_ && L.epi == EPI_)                        \
-    return launch_impl<BN_, ST_, AMN_, BMN_, EPI_>(L, stream);
+    return launch_impl<BN_, ST_, AMN_, BMN_, EPI_, false>(L, stream);
+
+// BN = 256 cases: CTA-pair tiles (6 stages of 32 KB per CTA) when the problem allows them.
+#define MXK_CASE2(ST_, AMN_, BMN_, EPI_)                                                         \
+  if (L.bn == 256 && L.a_mn == AMN_ && L.b_mn == BMN_ && L.epi == EPI_)                        \
+    return pair ? launch_impl<256, 6, AMN_, BMN_, EPI_, true>(L, stream)                       \
+                : launch_impl<256, ST_, AMN_, BMN_, EPI_, false>(L, stream);
 
 int launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   MXK_TRACE("launch_gemm");
@@ -165,31 +202,34 @@ int launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   if (L.p.K % kBK != 0 && L.p.ragged != 2) return kErrBadArgs;
   if ((reinterpret_cast<uintptr_t>(L.a) | reinterpret_cast<uintptr_t>(L.b)) & 15) return kErrBadArgs;
   if ((L.lda * 2) % 16 || (L.ldb * 2) % 16) return kErrBadArgs;
+  // 256-row tiles: a single problem of at least 256 rows, or groups whose row extent is a
+  // multiple of 256 (grouped outputs are written in whole tiles)
+  const bool pair = pair_enabled() && L.bn == 256 && L.p.M >= 2 * kBM && (L.p.G == 1 || L.p.M % (2 * kBM) == 0);
   // plain stores / accumulation
-  MXK_CASE(256, 4, false, false, EPI_STORE)
+  MXK_CASE2(4, false, false, EPI_STORE)
   MXK_CASE(128, 6, false, false, EPI_STORE)
   MXK_CASE(64, 8, false, false, EPI_STORE)
-  MXK_CASE(256, 4, false, true, EPI_STORE)
+  MXK_CASE2(4, false, true, EPI_STORE)
   MXK_CASE(128, 6, false, true, EPI_STORE)
   MXK_CASE(64, 8, false, true, EPI_STORE)
-  MXK_CASE(256, 4, true, true, EPI_STORE)
+  MXK_CASE2(4, true, true, EPI_STORE)
   MXK_CASE(128, 6, true, true, EPI_STORE)
   MXK_CASE(64, 8, true, true, EPI_STORE)
   // input-gradient GEMMs that add a second gradient term in the epilogue
-  MXK_CASE(256, 4, false, true, EPI_RESID)
+  MXK_CASE2(4, false, true, EPI_RESID)
   MXK_CASE(128, 6, false, true, EPI_RESID)
   // fused epilogues (forward, K-major x K-major)
-  MXK_CASE(256, 4, false, false, EPI_SWIGLU)
-  MXK_CASE(256, 4, false, false, EPI_RESID)
+  MXK_CASE2(4, false, false, EPI_SWIGLU)
+  MXK_CASE2(4, false, false, EPI_RESID)
   MXK_CASE(128, 6, false, false, EPI_RESID)
-  MXK_CASE(256, 4, false, false, EPI_GATE_MUL)
+  MXK_CASE2(4, false, false, EPI_GATE_MUL)
   MXK_CASE(128, 6, false, false, EPI_GATE_MUL)
   MXK_CASE(128, 6, false, false, EPI_SILU)
-  MXK_CASE(256, 4, false, false, EPI_ACT)
+  MXK_CASE2(4, false, false, EPI_ACT)
   MXK_CASE(128, 6, false, false, EPI_ACT)
-  MXK_CASE(256, 4, false, false, EPI_ROWSCALE)
+  MXK_CASE2(4, false, false, EPI_ROWSCALE)
   MXK_CASE(128, 6, false, false, EPI_ROWSCALE)
-  MXK_CASE(256, 4, false, false, EPI_CE)
+  MXK_CASE2(4, false, false, EPI_CE)
   return kErrBadArgs;
 }
 

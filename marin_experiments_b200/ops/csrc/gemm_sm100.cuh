@@ -45,10 +45,12 @@ enum EpiKind : int {
   EPI_ACT = 7,       // non-GLU MLP: H = acc (bf16), C = act(acc) (bf16); act in `act_kind`
 };
 
-template <int BN>
+// Shared-memory plan of one CTA. PAIR: the tile is 256 x BN over a CTA pair; each CTA stages its
+// 128 rows of A and BN / 2 rows of B.
+template <int BN, bool PAIR = false>
 struct GemmSmem {
   static constexpr int kABytes = kBM * kBK * 2;
-  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kBBytes = (PAIR ? BN / 2 : BN) * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiBytes = kEpiWarps * kStageBufs * kStageBox;
 };
@@ -58,15 +60,15 @@ __device__ __forceinline__ int group_count(const GemmParams& p, int g) {
   return p.ragged == 2 ? p.K : p.M;
 }
 
-// Number of scheduled tiles (output tiles x K splits) of group g.
-template <int BN>
+// Number of scheduled tiles (output tiles of TM x BN, x K splits) of group g.
+template <int BN, int TM = kBM>
 __device__ __forceinline__ int group_tiles(const GemmParams& p, int g) {
   const int n_tiles = (p.N + BN - 1) / BN;
   if (p.ragged == 1) {
     int cnt = min(group_count(p, g), p.M);
-    return ((cnt + kBM - 1) / kBM) * n_tiles;
+    return ((cnt + TM - 1) / TM) * n_tiles;
   }
-  int m_tiles = (p.M + kBM - 1) / kBM;
+  int m_tiles = (p.M + TM - 1) / TM;
   if (p.ragged == 2) return group_count(p, g) > 0 ? m_tiles * n_tiles : 0;
   return m_tiles * n_tiles * max(p.ksplit, 1);
 }
@@ -75,7 +77,7 @@ struct TileCoord {
   int g, mt, nt, kb0, nkb;
 };
 
-template <int BN>
+template <int BN, int TM = kBM>
 __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, const int* prefix, int tile) {
   int lo = 0, hi = p.G - 1;
   while (lo < hi) {
@@ -88,9 +90,9 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, const int*
   int m_tiles;
   if (p.ragged == 1) {
     int cnt = min(group_count(p, lo), p.M);
-    m_tiles = (cnt + kBM - 1) / kBM;
+    m_tiles = (cnt + TM - 1) / TM;
   } else {
-    m_tiles = (p.M + kBM - 1) / kBM;
+    m_tiles = (p.M + TM - 1) / TM;
   }
   const int n_tiles = (p.N + BN - 1) / BN;
   const int kext = (p.ragged == 2) ? group_count(p, lo) : p.K;
@@ -177,12 +179,19 @@ struct EpiRing {
   }
 };
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+// PAIR: launched as (2, 1, 1) clusters; a cluster computes a 256 x BN tile with cta_group::2
+// MMAs issued by its even CTA (rank 0). Each CTA loads its 128 rows of A and rows
+// [rank * BN / 2, (rank + 1) * BN / 2) of B's tile; both CTAs' loads complete rank 0's full
+// barrier; MMA completion is multicast to both CTAs' empty / TMEM-full barriers; both CTAs'
+// epilogues release rank 0's TMEM-empty barrier.
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2,
                       const GemmParams p) {
-  using S = GemmSmem<BN>;
+  using S = GemmSmem<BN, PAIR>;
+  constexpr int TM = PAIR ? 2 * kBM : kBM;  // output rows of a tile
+  constexpr int BNL = PAIR ? BN / 2 : BN;  // B rows staged by this CTA
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -199,6 +208,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // first tile of this CTA / pair
+  const int tstep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
                                : (2 * BN <= 256) ? 256 : 512;
 
@@ -206,7 +218,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int acc = 0;
     for (int g = 0; g < p.G; ++g) {
       prefix[g] = acc;
-      acc += group_tiles<BN>(p, g);
+      acc += group_tiles<BN, TM>(p, g);
     }
     prefix[p.G] = acc;
     *abort_flag = 0;
@@ -218,7 +230,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 32 * kEpiWarps);
+      mbar_init(&tempty_bar[b], (PAIR ? 2 : 1) * 32 * kEpiWarps);
     }
     mbar_init(drain_bar, 1);
     fence_barrier_init();
@@ -226,11 +238,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tmap(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = prefix[p.G];
@@ -240,34 +258,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-        TileCoord tc = decode_tile<BN>(p, prefix, tile);
+      // one TMA load: PAIR loads count their bytes on rank 0's full barrier
+      auto load = [&](const CUtensorMap* tm, int s, void* dst, int x, int y) {
+        if constexpr (PAIR) tma_load_2d_pair(tm, mapa_shared(&full_bar[s], 0), dst, x, y);
+        else tma_load_2d(tm, &full_bar[s], dst, x, y);
+      };
+      for (int tile = tile0; tile < total_tiles && ok; tile += tstep) {
+        TileCoord tc = decode_tile<BN, TM>(p, prefix, tile);
         const int bgrp = p.b_mod ? tc.g % p.b_mod : tc.g;
+        const int arow = tc.mt * TM + (int)rank * kBM;  // this CTA's first A row (or M column)
+        const int brow = tc.nt * BN + (int)rank * BNL;  // this CTA's first B row (or N column)
         for (int i = 0; i < tc.nkb; ++i, ++it) {
           const int kb = tc.kb0 + i;
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutProducer, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full_bar[s], S::kStageBytes);
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], (PAIR ? 2 : 1) * S::kStageBytes);
           uint8_t* a_dst = sA + s * S::kABytes;
           uint8_t* b_dst = sB + s * S::kBBytes;
           if constexpr (!A_MN) {
-            tma_load_2d(&tmA, &full_bar[s], a_dst, kb * kBK, tc.g * p.a_grp + tc.mt * kBM);
+            load(&tmA, s, a_dst, kb * kBK, tc.g * p.a_grp + arow);
           } else {
 #pragma unroll
             for (int j = 0; j < kBM / 64; ++j)
-              tma_load_2d(&tmA, &full_bar[s], a_dst + j * kBK * 128, tc.mt * kBM + j * 64, tc.g * p.a_grp + kb * kBK);
+              load(&tmA, s, a_dst + j * kBK * 128, arow + j * 64, tc.g * p.a_grp + kb * kBK);
           }
           if constexpr (!B_MN) {
-            tma_load_2d(&tmB, &full_bar[s], b_dst, kb * kBK, bgrp * p.b_grp + tc.nt * BN);
+            load(&tmB, s, b_dst, kb * kBK, bgrp * p.b_grp + brow);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(&tmB, &full_bar[s], b_dst + j * kBK * 128, tc.nt * BN + j * 64, bgrp * p.b_grp + kb * kBK);
+            for (int j = 0; j < BNL / 64; ++j)
+              load(&tmB, s, b_dst + j * kBK * 128, brow + j * 64, bgrp * p.b_grp + kb * kBK);
           }
         }
       }
-      if (!ok) {
+      if (!ok && PAIR && rank != 0) {
+        // The peer cannot observe rank 0's full barrier: give its loads in flight a fixed
+        // (bounded) time to land before this CTA's shared memory is released.
+        long long t0 = clock64();
+        while (clock64() - t0 < (1ll << 24)) {}
+      } else if (!ok) {
         // Drain: wait (bounded) for the loads of the last STAGES issued iterations to land, so no
         // TMA write targets this CTA's shared memory after it exits.
         for (int i = (it > STAGES ? it - STAGES : 0); i < it; ++i) {
@@ -278,17 +308,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN, B_MN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(TM, BN, A_MN, B_MN);
       int it = 0, tcount = 0;
       bool ok = true;
       bool issued = false;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-        TileCoord tc = decode_tile<BN>(p, prefix, tile);
+      for (int tile = tile0; tile < total_tiles && ok; tile += tstep) {
+        TileCoord tc = decode_tile<BN, TM>(p, prefix, tile);
         if (tc.nkb == 0) continue;  // (host never schedules empty splits; kept consistent anyway)
         const int buf = tcount & 1;
         const uint32_t tph = (tcount >> 1) & 1;
-        if (!mbar_wait(&tempty_bar[buf], tph ^ 1, p.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
+        const bool freed = PAIR ? mbar_wait_cluster(&tempty_bar[buf], tph ^ 1, p.err, kErrTimeoutMma, abort_flag)
+                                : mbar_wait(&tempty_bar[buf], tph ^ 1, p.err, kErrTimeoutMma, abort_flag);
+        if (!freed) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         for (int i = 0; i < tc.nkb; ++i, ++it) {
@@ -305,18 +337,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             else adesc = make_sdesc(a_base + ks * 2048, kBK * 128, 1024);
             if constexpr (!B_MN) bdesc = make_sdesc(b_base + ks * 32, 16, 1024);
             else bdesc = make_sdesc(b_base + ks * 2048, kBK * 128, 1024);
-            umma_bf16(d_tmem, adesc, bdesc, idesc, (i | ks) != 0 ? 1u : 0u);
+            if constexpr (PAIR) umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (i | ks) != 0 ? 1u : 0u);
+            else umma_bf16(d_tmem, adesc, bdesc, idesc, (i | ks) != 0 ? 1u : 0u);
           }
           issued = true;
-          umma_commit(&empty_bar[s]);
+          if constexpr (PAIR) umma_commit_pair(&empty_bar[s], 0x3);
+          else umma_commit(&empty_bar[s]);
         }
         if (!ok) break;
-        umma_commit(&tfull_bar[buf]);
+        if constexpr (PAIR) umma_commit_pair(&tfull_bar[buf], 0x3);
+        else umma_commit(&tfull_bar[buf]);
         ++tcount;
       }
       if (!ok && issued) {
         // Drain: wait (bounded) until every MMA issued so far has completed before TMEM is freed.
-        umma_commit(drain_bar);
+        if constexpr (PAIR) umma_commit_pair(drain_bar, 0x1);
+        else umma_commit(drain_bar);
         long long t0 = clock64();
         while (!mbar_try_wait(drain_bar, 0) && clock64() - t0 < (1ll << 26)) {}
       }
@@ -329,8 +365,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     EpiRing ring{sEpi + (warp - 2) * kStageBufs * kStageBox, 0};
     const bool reduce = p.c_f32 && p.c_accum != 0;
     int tcount = 0;
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
-      TileCoord tc = decode_tile<BN>(p, prefix, tile);
+    const uint32_t tempty_c0 = PAIR ? mapa_shared(&tempty_bar[0], 0) : 0u;
+    const uint32_t tempty_c1 = PAIR ? mapa_shared(&tempty_bar[1], 0) : 0u;
+    for (int tile = tile0; tile < total_tiles; tile += tstep) {
+      TileCoord tc = decode_tile<BN, TM>(p, prefix, tile);
       if (tc.nkb == 0) continue;
       const int buf = tcount & 1;
       const uint32_t tph = (tcount >> 1) & 1;
@@ -339,9 +377,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!__all_sync(0xffffffffu, got)) break;  // keep the warp converged for tcgen05.ld
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
-      const int row = tc.mt * kBM + q * 32 + lane;
+      const int row = tc.mt * TM + (int)rank * kBM + q * 32 + lane;
       const bool row_ok = row < p.M;
-      const int y0 = (p.c_mod ? tc.g % p.c_mod : tc.g) * p.c_grp + tc.mt * kBM + q * 32;  // warp's first C row
+      const int y0 = (p.c_mod ? tc.g % p.c_mod : tc.g) * p.c_grp + tc.mt * TM + (int)rank * kBM + q * 32;  // warp's first C row
       const long crow = (long)y0 + lane;
       const int col0 = tc.nt * BN;
 
@@ -471,23 +509,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty_bar[buf]);
+      if constexpr (PAIR) mbar_arrive_remote(buf ? tempty_c1 : tempty_c0);
+      else mbar_arrive(&tempty_bar[buf]);
     }
     if (lane == 0) bulk_wait_all();  // every TMA store / reduce of this warp has landed
   }
 
   tc_fence_before();
   __syncthreads();
+  // PAIR: neither CTA leaves while the other may still arrive on its barriers or while rank 0's
+  // MMAs may read its shared memory
+  if constexpr (PAIR) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, kTmemCols);
+    else tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PAIR = false>
 constexpr int gemm_smem_bytes() {
   // stages + epilogue staging + 1 KB alignment slack + barriers/scalars + tile prefix table
-  return STAGES * GemmSmem<BN>::kStageBytes + GemmSmem<BN>::kEpiBytes + 1024 + 256 + (kMaxGroups + 1) * 4;
+  return STAGES * GemmSmem<BN, PAIR>::kStageBytes + GemmSmem<BN, PAIR>::kEpiBytes + 1024 + 256 +
+         (kMaxGroups + 1) * 4;
 }
 
 }  // namespace mxk

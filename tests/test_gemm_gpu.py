@@ -146,3 +146,39 @@ def test_deferred_weight_grads_match():
     G.run_weight_grads(q)
     # split-K partial sums are combined with atomic adds: equal up to summation order
     assert torch.allclose(w.main_grad, ref_dw, rtol=1e-4, atol=1e-3)
+
+
+def test_pair_tile_shapes(G):
+    """Shapes that take the CTA-pair (256-row) tiles: grouped problems whose per-group rows are a
+    multiple of 256 (ragged counts inside), a row count that leaves the second CTA of the last
+    pair out of range, and the residual / gate epilogues."""
+    torch.manual_seed(3)
+    g, cap, d, n = 4, 512, 256, 768
+    counts = torch.tensor([512, 3, 260, 0], dtype=torch.int32, device="cuda")
+    x = _rand(g * cap, d)
+    for e in range(g):
+        x[e * cap + counts[e]:(e + 1) * cap] = 0
+    w = _rand(g * n, d)
+    y = G.grouped_linear(x, w, counts)
+    dy = _rand(g * cap, n)
+    for e in range(g):
+        dy[e * cap + counts[e]:(e + 1) * cap] = 0
+    dx = G.grouped_linear_dx(dy, w, counts)
+    torch.cuda.synchronize()
+    for e in range(g):
+        c = int(counts[e])
+        if c:
+            xs, ws, dys = x[e * cap:e * cap + c].float(), w[e * n:(e + 1) * n].float(), dy[e * cap:e * cap + c].float()
+            assert _rel(y[e * cap:e * cap + c], xs @ ws.t()) < 1e-2
+            assert _rel(dx[e * cap:e * cap + c], dys @ ws) < 1e-2
+    m, k, n = 384, 512, 1536
+    a, b, r = _rand(m, k), _rand(n, k, scale=0.1), _rand(m, n)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    G.linear(a, b, out=out, epi="resid", r=r)
+    assert _rel(out, r.float() + a.float() @ b.float().t()) < 1e-2
+    G.linear(a, b, out=out, epi="gate_mul", r=r)
+    assert _rel(out, r.float() * torch.sigmoid(a.float() @ b.float().t())) < 1e-2
+    base = torch.randn(n, k, device="cuda")
+    acc = base.clone()
+    G.linear_dw(_rand(m, n), a, out=acc, accum=True)  # 1536-row output, split over K
+    torch.cuda.synchronize()
