@@ -91,6 +91,7 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const 
   p.act_kind = (int)act_kind;
   p.err = reinterpret_cast<int*>(err.data_ptr());
   p.ksplit = 1;
+  p.raster_n = 0;
   // Output extents for the TMA stores: columns clip at N; rows clip at M for a single problem,
   // at the buffer end for grouped problems.
   L.c_cols = N;

@@ -148,11 +148,19 @@ static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
   long long tiles = (long long)p.G * m_tiles * n_tiles;
   // Split K over workers when a non-grouped fp32 accumulation has too few output tiles for the
   // GPU; the partial sums are combined by the element-wise atomic TMA reduce-add.
+  // The split count is the smallest whose work units fill the last wave to >= 90 % (each split
+  // adds one fp32 reduce-add pass over C).
   p.ksplit = 1;
+  p.raster_n = n_tiles <= 16 ? 1 : 0;
   if (p.G == 1 && p.ragged == 0 && p.c_f32 && p.c_accum && tiles < 2 * units) {
     const int nkb = (p.K + kBK - 1) / kBK;
-    int ks = (int)((2 * units + tiles - 1) / tiles);
-    ks = ks < nkb ? ks : nkb;
+    int ks = 1;
+    for (int c = 1; c <= 16 && c <= nkb; ++c) {
+      const long long w = tiles * c;
+      const long long waves = (w + units - 1) / units;
+      ks = c;
+      if (w >= (units * 9) / 10 && w * 10 >= waves * units * 9) break;
+    }
     if (ks > 1) {
       const int per = (nkb + ks - 1) / ks;
       ks = (nkb + per - 1) / per;  // no empty splits

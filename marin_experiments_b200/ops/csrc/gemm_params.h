@@ -13,6 +13,7 @@ struct GemmParams {
   // (source rank, expert) activation groups share one expert's weights and weight gradient.
   int b_mod, c_mod;
   int ksplit;  // K splits per output tile (non-grouped, accumulating fp32 C only)
+  int raster_n;  // tile order: 1 = N tiles fastest, 0 = M tiles fastest (set by the launcher)
   void* C;
   int ldc;
   int c_f32;

@@ -103,8 +103,15 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, const int*
     split = local / (m_tiles * n_tiles);
     local = local % (m_tiles * n_tiles);
   }
-  tc.mt = local % m_tiles;
-  tc.nt = local / m_tiles;
+  // raster_n: consecutive tiles walk N first, so the tiles in flight share a few A row blocks
+  // (problems with few N tiles); otherwise M first, so they share B column blocks.
+  if (p.raster_n) {
+    tc.nt = local % n_tiles;
+    tc.mt = local / n_tiles;
+  } else {
+    tc.mt = local % m_tiles;
+    tc.nt = local / m_tiles;
+  }
   const int per = (nkb + ks - 1) / ks;
   tc.kb0 = split * per;
   tc.nkb = max(0, min(nkb, tc.kb0 + per) - tc.kb0);
