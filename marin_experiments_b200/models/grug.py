@@ -65,6 +65,12 @@ class NormPair(nn.Module):
             return ops.rms_gated_norm(x, self.rms.weight, self.rms.eps)
         return ops.rms_gated_norm(x, self.rms.weight, self.rms.eps, self.gated.w_down, self.gated.w_up)
 
+    def with_residual(self, x):
+        """``(norm(x), residual)`` -- see ``ops.rms_gated_norm_res``."""
+        g = self.gated
+        return ops.rms_gated_norm_res(x, self.rms.weight, self.rms.eps, None if g is None else g.w_down,
+                                      None if g is None else g.w_up)
+
 
 class Attention(nn.Module):
     tp_sharded_params = ("w_qkv", "attn_gate", "w_o")
@@ -208,9 +214,9 @@ class Block(nn.Module):
         self.cfg = cfg
 
     def forward(self, x, batch: int, seq: int, segment_ids=None, dp_group=None, logit_bias=None):
-        h = self.attn_norm(x)
+        h, x = self.attn_norm.with_residual(x)
         x = self.attn(h, x, batch, seq, segment_ids)
-        h = self.mlp_norm(x)
+        h, x = self.mlp_norm.with_residual(x)
         if not self.cfg.is_moe:
             return self.mlp(h, residual=x), None
         base = x if self.shared is None else self.shared(h, residual=x)

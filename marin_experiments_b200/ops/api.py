@@ -54,6 +54,14 @@ def rms_gated_norm(x, w_rms, eps: float, w_down=None, w_up=None):
     return y
 
 
+def rms_gated_norm_res(x, w_rms, eps: float, w_down=None, w_up=None):
+    """``(norm(x), residual)``: the normalised input and the tensor to use as the block's residual
+    stream (on CUDA an alias of ``x`` whose gradient is summed inside the norm's backward kernel)."""
+    if x.is_cuda:
+        return _cuda().rms_gated_norm(x, w_rms, eps, w_down, w_up, passthrough=True)
+    return rms_gated_norm(x, w_rms, eps, w_down, w_up), x
+
+
 # -------------------------------------------------------------------------------- attention
 
 

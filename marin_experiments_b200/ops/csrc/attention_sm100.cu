@@ -193,35 +193,52 @@ __global__ void __launch_bounds__(kThreadsPP, 1)
                        idesc_o, (acc || ks > 0) ? 1u : 0u);
         umma_commit(&o_done[t]);
       };
+      // Issue order per key block j: PV0_j, S0_{j+1}, PV1_j, S1_{j+1}. Tile 0's softmax of block
+      // j+1 then runs while the tensor core does PV1_j and S1_{j+1}, and tile 1's while it does
+      // PV0_{j+1} and S0_{j+2}: the two softmax groups alternate instead of contending for the
+      // SFU at the same time. S_{j+1} overwrites P_j (aliased in TMEM), so it waits for PV_j.
       unsigned long long wp = 0, wkv = 0, wo = 0;
-      for (int j = 0; j < nb && ok; ++j) {
-        const int st = j & 1;
+      auto active = [&](int t, int j) { return j >= lo_t[t] && j < nb_t[t]; };
+      if (ok) {
         long long c0 = clock64();
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
+        ok = mbar_wait(&kv_full[0], 0, a.err, kErrTimeoutMma, abort_flag);
         wkv += clock64() - c0;
         tc_fence_after();
-        bool act[2];
-        for (int t = 0; t < 2; ++t) act[t] = j >= lo_t[t] && j < nb_t[t];
+        for (int t = 0; t < 2 && ok; ++t)
+          if (active(t, 0)) issue_qk(t, 0);
+      }
+      for (int j = 0; j < nb && ok; ++j) {
+        const int st = j & 1;
+        bool next_ready = false;  // K/V of block j + 1 landed
         for (int t = 0; t < 2 && ok; ++t) {
-          if (!act[t]) continue;
-          // S_t overwrites P_t of the previous block: its PV must have completed
-          if (s_cnt[t] > 0) {
-            long long c1 = clock64();
-            if (!mbar_wait(&o_done[t], (s_cnt[t] - 1) & 1, a.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
-            wo += clock64() - c1;
+          if (active(t, j)) {
+            long long c2 = clock64();
+            if (!mbar_wait(&p_full[t], s_cnt[t] & 1, a.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
+            wp += clock64() - c2;
             tc_fence_after();
+            issue_pv(t, st, s_cnt[t] > 0);
+            ++s_cnt[t];
           }
-          issue_qk(t, st);
+          if (j + 1 < nb && active(t, j + 1)) {
+            if (!next_ready) {
+              long long c0 = clock64();
+              if (!mbar_wait(&kv_full[st ^ 1], ((j + 1) >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) {
+                ok = false;
+                break;
+              }
+              wkv += clock64() - c0;
+              next_ready = true;
+            }
+            if (s_cnt[t] > 0) {
+              long long c1 = clock64();
+              if (!mbar_wait(&o_done[t], (s_cnt[t] - 1) & 1, a.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
+              wo += clock64() - c1;
+            }
+            tc_fence_after();
+            issue_qk(t, st ^ 1);
+          }
         }
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (!act[t]) continue;
-          long long c2 = clock64();
-          if (!mbar_wait(&p_full[t], s_cnt[t] & 1, a.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
-          wp += clock64() - c2;
-          tc_fence_after();
-          issue_pv(t, st, s_cnt[t] > 0);
-          ++s_cnt[t];
-        }
+        if (!ok) break;
         umma_commit(&kv_empty[st]);
       }
       if (a.prof) {
@@ -289,37 +306,37 @@ __global__ void __launch_bounds__(kThreadsPP, 1)
       const float mb = m_run == -INFINITY ? 0.f : m_run;
       const float sc = a.scale_log2;
       float rs = 0.f;
-      // P = exp2(s*c - m) as bf16 pairs into the first 64 columns of S (all reads are done)
+      // P = exp2(s*c - m) as bf16 pairs into the first 64 columns of S (all reads are done).
+      // Arguments and the row sum use packed fp32 pairs; columns 32-63 take the FMA-pipe
+      // exponential, the rest the special-function unit.
       {
-        uint32_t w[16];
+        const uint64_t sc2 = f2_make(sc, sc), nm2 = f2_make(-mb, -mb);
+        uint64_t rs2 = f2_make(0.f, 0.f);
+        auto emit = [&](const float (&sv)[32], uint32_t col, bool poly) {
+          uint32_t w[16];
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const float e0 = exp2f(fmaf(s0[c], sc, -mb)), e1 = exp2f(fmaf(s0[c + 1], sc, -mb));
-          rs += e0 + e1;
-          w[c / 2] = pack_bf16x2(e0, e1);
-        }
-        tmem_st16(t_s + 0, w);
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const float e0 = exp2f(fmaf(s1[c], sc, -mb)), e1 = exp2f(fmaf(s1[c + 1], sc, -mb));
-          rs += e0 + e1;
-          w[c / 2] = pack_bf16x2(e0, e1);
-        }
-        tmem_st16(t_s + 16, w);
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const float e0 = exp2f(fmaf(s2[c], sc, -mb)), e1 = exp2f(fmaf(s2[c + 1], sc, -mb));
-          rs += e0 + e1;
-          w[c / 2] = pack_bf16x2(e0, e1);
-        }
-        tmem_st16(t_s + 32, w);
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const float e0 = exp2f(fmaf(s3[c], sc, -mb)), e1 = exp2f(fmaf(s3[c + 1], sc, -mb));
-          rs += e0 + e1;
-          w[c / 2] = pack_bf16x2(e0, e1);
-        }
-        tmem_st16(t_s + 48, w);
+          for (int c = 0; c < 32; c += 2) {
+            const uint64_t x = f2_fma(f2_make(sv[c], sv[c + 1]), sc2, nm2);
+            float x0, x1, e0, e1;
+            f2_split(x, x0, x1);
+            if (poly) {
+              ex2_poly2(x0, x1, e0, e1);
+            } else {
+              e0 = ex2_sfu(x0);
+              e1 = ex2_sfu(x1);
+            }
+            rs2 = f2_add(rs2, f2_make(e0, e1));
+            w[c / 2] = pack_bf16x2(e0, e1);
+          }
+          tmem_st16(t_s + col, w);
+        };
+        emit(s0, 0, false);
+        emit(s1, 16, true);
+        emit(s2, 32, false);
+        emit(s3, 48, false);
+        float r0, r1;
+        f2_split(rs2, r0, r1);
+        rs = r0 + r1;
       }
       l_run += rs;
       long long c_d = clock64();

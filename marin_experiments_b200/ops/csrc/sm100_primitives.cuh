@@ -238,6 +238,62 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool a_mn, 
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// ------------------------------------------------------------------ packed fp32 pairs, exp2
+// sm_100a executes add / mul / fma on fp32 pairs (f32x2) at one instruction per pair. A pair lives
+// in a 64-bit register (low word = first element).
+__device__ __forceinline__ uint64_t f2_make(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x on the special-function unit (one instruction; flushes subnormal results to zero).
+__device__ __forceinline__ float ex2_sfu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^x for a pair of x <= 0 on the FMA pipe, so that part of a softmax's exponentials leave the
+// special-function unit (16 results per clock per SM, fewer than the tensor cores need).
+// x = j + f with j = round(x) (adding 1.5 * 2^23 leaves j in the low mantissa bits) and
+// f in [-1/2, 1/2]; 2^f is a degree-3 polynomial fitted here by Remez exchange for minimum
+// relative error on [-1/2, 1/2] (max 7.5e-5, 26x below the bf16 half-ulp 2^-9); 2^j is added to
+// the exponent field. x is clamped at -126 so that j plus the exponent of 2^f (>= 126) stays
+// >= 0: a smaller j would borrow from the sign bit. 2^-126 is already ~0 for a probability.
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& y0, float& y1) {
+  const uint64_t x = f2_make(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t t = f2_add(x, f2_make(12582912.f, 12582912.f));
+  const uint64_t j = f2_add(t, f2_make(-12582912.f, -12582912.f));
+  const uint64_t f = f2_fma(j, f2_make(-1.f, -1.f), x);
+  uint64_t q = f2_fma(f2_make(0.0551716685f, 0.0551716685f), f, f2_make(0.2426111251f, 0.2426111251f));
+  q = f2_fma(q, f, f2_make(0.6932609677f, 0.6932609677f));
+  q = f2_fma(q, f, f2_make(0.9999280572f, 0.9999280572f));
+  float q0, q1, t0, t1;
+  f2_split(q, q0, q1);
+  f2_split(t, t0, t1);
+  y0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
 // ------------------------------------------------------------------------ CTA pairs (cta_group::2)
 // Two CTAs of a (2, 1, 1) cluster share one tcgen05 MMA of M = 256: each holds its 128 rows of A
 // and half of B's rows at the same shared-memory offsets, the even CTA issues the MMA, and each

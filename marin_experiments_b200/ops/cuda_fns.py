@@ -96,8 +96,12 @@ def linear(x, w, residual=None):
 
 
 class _RmsGatedNorm(torch.autograd.Function):
+    """RMSNorm (+ GatedNorm). With ``passthrough`` it also returns an alias of ``x`` to be used as
+    the block's residual: the residual's gradient then arrives here and is added inside the RMSNorm
+    backward kernel instead of by a separate autograd accumulation."""
+
     @staticmethod
-    def forward(ctx, x, w_rms, eps, w_down, w_up):
+    def forward(ctx, x, w_rms, eps, w_down, w_up, passthrough=False):
         x = _c(x)
         t, d = x.shape
         y = torch.empty_like(x)
@@ -107,7 +111,7 @@ class _RmsGatedNorm(torch.autograd.Function):
         ctx.w_rms = w_rms
         if not ctx.gated:
             ctx.save_for_backward(x, rstd)
-            return y
+            return (y, x.view_as(x)) if passthrough else y
         r = w_down.shape[0]
         s = torch.empty(t, r, dtype=BF16, device=x.device)
         h = torch.empty(t, r, dtype=BF16, device=x.device)
@@ -116,11 +120,12 @@ class _RmsGatedNorm(torch.autograd.Function):
         G.gemm(s, w_up, out, M=t, N=d, K=r, epi="gate_mul", r=y)
         ctx.save_for_backward(x, rstd, y, h, s)
         ctx.w_down, ctx.w_up = w_down, w_up
-        return out
+        return (out, x.view_as(x)) if passthrough else out
 
     @staticmethod
-    def backward(ctx, dout):
+    def backward(ctx, dout, dres=None):
         dout = _c(dout)
+        dres = None if dres is None else _c(dres)
         if not ctx.gated:
             x, rstd = ctx.saved_tensors
             dy = dout
@@ -144,13 +149,13 @@ class _RmsGatedNorm(torch.autograd.Function):
             G.gemm(dh, w_down, dy, b_mn=True, M=t, N=d, K=r, epi="resid", r=dy1)
             ctx.w_down = ctx.w_up = None
         dx = torch.empty_like(x)
-        ext().rmsnorm_bwd(dy, x, ctx.w_rms, rstd, None, dx, _mg(ctx.w_rms))
+        ext().rmsnorm_bwd(dy, x, ctx.w_rms, rstd, dres, dx, _mg(ctx.w_rms))
         ctx.w_rms = None
-        return dx, None, None, None, None
+        return dx, None, None, None, None, None
 
 
-def rms_gated_norm(x, w_rms, eps, w_down=None, w_up=None):
-    return _RmsGatedNorm.apply(x, w_rms, eps, w_down, w_up)
+def rms_gated_norm(x, w_rms, eps, w_down=None, w_up=None, passthrough=False):
+    return _RmsGatedNorm.apply(x, w_rms, eps, w_down, w_up, passthrough)
 
 
 # ---------------------------------------------------------------------------------- attention
