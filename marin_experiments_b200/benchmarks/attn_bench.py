@@ -11,7 +11,9 @@ import math
 import torch
 
 
-def run(b=8, s=2048, h=16, hkv=16, hd=96, iters=10):
+def run(b=8, s=2048, h=16, hkv=16, hd=96, iters=10, once=False):
+    """Time the tcgen05 and mma.sync kernels (CUDA events, ``iters`` back-to-back launches after
+    3 warm-ups). ``once``: one tcgen05 forward and one backward, untimed (a launch list for ncu)."""
     from marin_experiments_b200.ops._ext import err_flag, ext
 
     t = b * s
@@ -27,6 +29,11 @@ def run(b=8, s=2048, h=16, hkv=16, hd=96, iters=10):
     sc = 1 / math.sqrt(hd)
     fl = 4.0 * b * h * hd * s * s / 2  # causal forward FLOPs
     res = {}
+    if once:
+        ext().flash_fwd_sm100(q, k, v, o, lse, None, b, s, 0, sc, err_flag(q.device), None)
+        ext().flash_bwd_sm100(q, k, v, o, lse, None, b, s, 0, sc, do, ds, dqa, dq, dk, dv, False, err_flag(q.device))
+        torch.cuda.synchronize()
+        return res
     for name, fn, f in [
         ("fwd_tcgen05", lambda: ext().flash_fwd_sm100(q, k, v, o, lse, None, b, s, 0, sc, err_flag(q.device), None), fl),
         ("fwd_mma_sync", lambda: ext().flash_fwd(q, k, v, o, lse, None, b, s, 0, sc), fl),
@@ -51,4 +58,6 @@ def run(b=8, s=2048, h=16, hkv=16, hd=96, iters=10):
 
 
 if __name__ == "__main__":
-    run()
+    import sys
+
+    run(once="--once" in sys.argv)

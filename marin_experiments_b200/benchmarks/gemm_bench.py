@@ -50,7 +50,9 @@ def _time(fn, flush, iters=10, warmup=3):
     return ts[len(ts) // 2]
 
 
-def run(shapes=SHAPES):
+def run(shapes=SHAPES, once: bool = False):
+    """Time every shape against torch.matmul (median of 10, L2 flushed). ``once``: launch our GEMM
+    a single time per shape and time nothing (a small, fixed launch list for ncu captures)."""
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
     rows = []
     for name, m, n, k, mode in shapes:
@@ -89,6 +91,10 @@ def run(shapes=SHAPES):
             mine = lambda: G.linear_dw(a, b, out=c, accum=True)
             ref = lambda: torch.matmul(a.t(), b, out=cb)
         flops = 2.0 * m * n * k
+        if once:
+            mine()
+            torch.cuda.synchronize()
+            continue
         t_mine = _time(mine, flush)
         t_ref = _time(ref, flush)
         rows.append({"name": name, "M": m, "N": n, "K": k, "mode": mode, "ms": t_mine, "cublas_ms": t_ref,
@@ -101,8 +107,11 @@ def run(shapes=SHAPES):
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--json", default=None)
+    ap.add_argument("--only", default=None, help="comma-separated shape names")
+    ap.add_argument("--once", action="store_true", help="one untimed launch per shape (for ncu)")
     args = ap.parse_args()
-    rows = run()
+    shapes = SHAPES if args.only is None else [s for s in SHAPES if s[0] in args.only.split(",")]
+    rows = run(shapes, once=args.once)
     if args.json:
         with open(args.json, "w") as f:
             json.dump(rows, f, indent=1)

@@ -375,7 +375,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int HD>
 struct SmemQ {
   static constexpr int kTile = ((HD + 63) / 64) * 128 * 128;
-  static constexpr int kUsed = 6 * kTile + 128;  // Q, dO, K[2], V[2], barriers
+  // Q, dO, K[3], V[2], barriers. K is held from S_t to dQ_t (the dQ MMA runs one block behind),
+  // so it gets a third stage: K_{t+1} then loads while blocks t-1 and t are still in flight.
+  static constexpr int kUsed = 7 * kTile + 256;
   static constexpr int kBytes = kUsed + 128;
 };
 
@@ -397,18 +399,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_raw + pad;
   uint8_t* sQ = smem;
   uint8_t* sO = smem + tile;
-  uint8_t* sK = smem + 2 * tile;  // [2]
-  uint8_t* sV = smem + 4 * tile;  // [2]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * tile);
+  uint8_t* sK = smem + 2 * tile;  // [3]
+  uint8_t* sV = smem + 5 * tile;  // [2]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * tile);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* dq_mma = bars + 7;    // [2]
-  uint64_t* dp_free = bars + 9;
-  uint64_t* ds_ready = bars + 10;
-  uint64_t* dq_done = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* k_full = bars + 1;    // [3]
+  uint64_t* k_empty = bars + 4;   // [3]
+  uint64_t* v_full = bars + 7;    // [2]
+  uint64_t* v_empty = bars + 9;   // [2]
+  uint64_t* s_full = bars + 11;   // [2]
+  uint64_t* dq_mma = bars + 13;   // [2]
+  uint64_t* dp_free = bars + 15;
+  uint64_t* ds_ready = bars + 16;
+  uint64_t* dq_done = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -423,9 +427,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    for (int t = 0; t < 3; ++t) {
+      mbar_init(&k_full[t], 1);
+      mbar_init(&k_empty[t], 1);
+    }
     for (int t = 0; t < 2; ++t) {
-      mbar_init(&kv_full[t], 1);
-      mbar_init(&kv_empty[t], 1);
+      mbar_init(&v_full[t], 1);
+      mbar_init(&v_empty[t], 1);
       mbar_init(&s_full[t], 1);
       mbar_init(&dq_mma[t], 1);
     }
@@ -453,14 +461,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(&tmO, q_full, sO + c * BM * 128, h * HD + c * 64, base + q0);
       }
       for (int t = 0; t < nj; ++t) {
-        const int st = t & 1;
+        const int ks = t % 3, vs = t & 1;
         const int kr = base + (j_lo + t) * BN;
-        if (!mbar_wait(&kv_empty[st], ((t >> 1) & 1) ^ 1, a.err, kErrTimeoutProducer, abort_flag)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * tile);
-        for (int c = 0; c < KCH; ++c) {
-          tma_load_2d(&tmK, &kv_full[st], sK + st * tile + c * BN * 128, kh * HD + c * 64, kr);
-          tma_load_2d(&tmV, &kv_full[st], sV + st * tile + c * BN * 128, kh * HD + c * 64, kr);
-        }
+        if (!mbar_wait(&k_empty[ks], ((t / 3) & 1) ^ 1, a.err, kErrTimeoutProducer, abort_flag)) break;
+        mbar_arrive_expect_tx(&k_full[ks], tile);
+        for (int c = 0; c < KCH; ++c)
+          tma_load_2d(&tmK, &k_full[ks], sK + ks * tile + c * BN * 128, kh * HD + c * 64, kr);
+        if (!mbar_wait(&v_empty[vs], ((t >> 1) & 1) ^ 1, a.err, kErrTimeoutProducer, abort_flag)) break;
+        mbar_arrive_expect_tx(&v_full[vs], tile);
+        for (int c = 0; c < KCH; ++c)
+          tma_load_2d(&tmV, &v_full[vs], sV + vs * tile + c * BN * 128, kh * HD + c * 64, kr);
       }
     }
   } else if (warp == 8) {
@@ -474,8 +484,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t <= nj && ok; ++t) {
         if (t < nj) {
           const int st = t & 1;
-          const uint32_t k_addr = smem_u32(sK + st * tile), v_addr = smem_u32(sV + st * tile);
-          if (!mbar_wait(&kv_full[st], (t >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
+          const uint32_t k_addr = smem_u32(sK + (t % 3) * tile), v_addr = smem_u32(sV + st * tile);
+          if (!mbar_wait(&k_full[t % 3], (t / 3) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
           if (t >= 2 && !mbar_wait(&dq_mma[st], ((t - 2) >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
           tc_fence_after();
 #pragma unroll
@@ -486,8 +496,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (t >= 1) {
             if (!mbar_wait(dp_free, (t - 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
-            tc_fence_after();
           }
+          if (!mbar_wait(&v_full[st], (t >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
+          tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < HD / 16; ++ks) {
             const uint32_t off = (ks / 4) * 128 * 128 + (ks % 4) * 32;
@@ -495,10 +506,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                       ks > 0 ? 1u : 0u);
           }
           umma_commit(&s_full[st]);
+          umma_commit(&v_empty[st]);  // V_t is read by dP_t only
         }
         if (t >= 1) {
           const int pt = t - 1, ps = pt & 1;
-          const uint32_t k_addr = smem_u32(sK + ps * tile);
+          const uint32_t k_addr = smem_u32(sK + (pt % 3) * tile);
           if (!mbar_wait(ds_ready, pt & 1, a.err, kErrTimeoutMma, abort_flag)) break;
           tc_fence_after();
 #pragma unroll
@@ -506,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_ts(tmem + kColDq, tmem + kColSb + ps * 128 + (ks >> 2) * 64 + (ks & 3) * 8,
                     make_sdesc(k_addr + ks * 2048, BN * 128, 1024), idesc_q, (pt > 0 || ks > 0) ? 1u : 0u);
           umma_commit(&dq_mma[ps]);
-          umma_commit(&kv_empty[ps]);
+          umma_commit(&k_empty[pt % 3]);
         }
       }
       umma_commit(dq_done);
