@@ -32,7 +32,12 @@ namespace fab100 {
 
 constexpr int BM = 128;  // queries per block
 constexpr int BN = 128;  // keys per CTA
-constexpr int kThreads = 320;  // warps 0-7 compute, 8 MMA, 9 TMA
+constexpr int kThreads = 320;  // dQ kernel: warps 0-7 compute, 8 MMA, 9 TMA
+// dK/dV kernel: warps 0-15 compute (warp w: TMEM lanes 32 (w % 4).., query columns 32 (w / 4)..),
+// 16 MMA, 17 TMA. Four compute warps per SM sub-partition hide the latency of each warp's
+// dependent exp / scale / pack chain.
+constexpr int kThreadsKV = 576;
+constexpr int kMmaWarpKV = 16, kTmaWarpKV = 17;
 
 struct BwdArgs {
   int B, S, H, Hkv, window;
@@ -47,6 +52,9 @@ struct BwdArgs {
   long dv_tok, dv_head;
   int dv_accumulate;
   int* err;
+  // Optional phase counters of the dK/dV compute warps (cycles summed over warps), else null:
+  // [0] waiting for S^T / dP^T, [1] TMEM loads, [2] math, [3] TMEM stores + release, [4] blocks.
+  unsigned long long* prof;
 };
 
 template <int HD>
@@ -104,7 +112,7 @@ __device__ __forceinline__ int query_key_lo(int qi, int S, int window, const int
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsKV, 1)
     fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                         const BwdArgs a) {
@@ -131,10 +139,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* qd_full = bars + 1;   // [2]
   uint64_t* qd_empty = bars + 3;  // [2]
   uint64_t* ld_full = bars + 5;   // [2]
-  uint64_t* sdp_full = bars + 7;
-  uint64_t* p_ready = bars + 8;
-  uint64_t* mma_done = bars + 9;
-  uint64_t* kv_done = bars + 12;
+  uint64_t* sdp_full = bars + 7;   // [2] per query half
+  uint64_t* p_ready = bars + 9;    // [2]
+  uint64_t* mma_done = bars + 11;  // [2]
+  uint64_t* kv_done = bars + 13;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -157,14 +165,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&qd_empty[t], 1);
       mbar_init(&ld_full[t], 32);
     }
-    mbar_init(sdp_full, 1);
-    mbar_init(p_ready, 256);
-    mbar_init(mma_done, 1);
+    for (int hh = 0; hh < 2; ++hh) {
+      mbar_init(&sdp_full[hh], 1);
+      mbar_init(&p_ready[hh], 256);  // the eight compute warps of the half
+      mbar_init(&mma_done[hh], 1);
+    }
     mbar_init(kv_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 8) {
+  if (warp == kMmaWarpKV) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -173,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 9) {
+  if (warp == kTmaWarpKV) {
     // ------------------------------------------------------------------ TMA + per-query scalars
     if (n_it > 0) {
       if (lane == 0) {
@@ -202,125 +212,171 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int q = u * 32 + lane, qi = q0 + q;
           const bool in = qi < a.S;
           const long idx = (long)(base + qi) * a.H + h;
-          sLse[buf * BM + q] = in ? a.lse[idx] * 1.4426950408889634f : INFINITY;
-          sDsum[buf * BM + q] = in ? a.dsum[idx] : 0.f;
+          // negated and pre-scaled: P^T = 2^(s c + nlse), dS^T = P^T (dP^T scale + nsd)
+          sLse[buf * BM + q] = in ? -a.lse[idx] * 1.4426950408889634f : -INFINITY;
+          sDsum[buf * BM + q] = in ? -a.dsum[idx] * a.scale : 0.f;
           sKlo[buf * BM + q] = query_key_lo(qi, a.S, a.window, a.seg, base);
         }
         __syncwarp();
         mbar_arrive(&ld_full[buf]);
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == kMmaWarpKV) {
     // ------------------------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_it > 0) {
-      constexpr uint32_t idesc_s = make_idesc_bf16(BN, BM, false, false);  // keys x queries
-      constexpr uint32_t idesc_kv = make_idesc_bf16(BN, HD, false, true);  // keys x head_dim
+      // The two 64-query halves of a block are pipeline stages: S^T / dP^T of half h fill TMEM
+      // columns [64 h, 64 h + 64) of their regions, so half h of block it + 1 is computed while
+      // the other half's compute warps (and the dV / dK MMAs of half h) run. Issue order per
+      // block: dV/dK(it, 0), S/dP(it + 1, 0), dV/dK(it, 1), S/dP(it + 1, 1).
+      constexpr uint32_t idesc_s = make_idesc_bf16(BN, BM / 2, false, false);  // keys x 64 queries
+      constexpr uint32_t idesc_kv = make_idesc_bf16(BN, HD, false, true);      // keys x head_dim
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      bool ok = mbar_wait(kv_full, 0, a.err, kErrTimeoutMma, abort_flag);
-      for (int it = 0; it < n_it && ok; ++it) {
-        const int buf = it & 1;
-        const uint32_t q_addr = smem_u32(sQ + buf * tile), o_addr = smem_u32(sO + buf * tile);
-        if (!mbar_wait(&qd_full[buf], (it >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
-        if (it > 0) {
-          // S^T / dP^T overwrite P^T / dS^T of the previous block: its dV / dK MMAs must be done
-          if (!mbar_wait(mma_done, (it - 1) & 1, a.err, kErrTimeoutMma, abort_flag)) break;
-        }
-        tc_fence_after();
+      auto issue_sdp = [&](int it, int hh) {
+        const uint32_t q_addr = smem_u32(sQ + (it & 1) * tile), o_addr = smem_u32(sO + (it & 1) * tile);
+        const uint32_t roff = hh * 64 * 128;  // the half's first query row inside each 128-B chunk
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks) {
           const uint32_t off = (ks / 4) * 128 * 128 + (ks % 4) * 32;
-          umma_bf16(tmem + kColS, make_sdesc(k_addr + off, 16, 1024), make_sdesc(q_addr + off, 16, 1024), idesc_s,
-                    ks > 0 ? 1u : 0u);
+          umma_bf16(tmem + kColS + 64 * hh, make_sdesc(k_addr + off, 16, 1024),
+                    make_sdesc(q_addr + off + roff, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks) {
           const uint32_t off = (ks / 4) * 128 * 128 + (ks % 4) * 32;
-          umma_bf16(tmem + kColDP, make_sdesc(v_addr + off, 16, 1024), make_sdesc(o_addr + off, 16, 1024), idesc_s,
-                    ks > 0 ? 1u : 0u);
+          umma_bf16(tmem + kColDP + 64 * hh, make_sdesc(v_addr + off, 16, 1024),
+                    make_sdesc(o_addr + off + roff, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
         }
-        umma_commit(sdp_full);
-        if (!mbar_wait(p_ready, it & 1, a.err, kErrTimeoutMma, abort_flag)) break;
-        tc_fence_after();
+        umma_commit(&sdp_full[hh]);
+      };
+      auto issue_dkdv = [&](int it, int hh) {
+        const uint32_t q_addr = smem_u32(sQ + (it & 1) * tile), o_addr = smem_u32(sO + (it & 1) * tile);
 #pragma unroll
-        for (int ks = 0; ks < BM / 16; ++ks) {
-          const uint32_t pc = (ks >> 2) * 64 + (ks & 3) * 8;  // packed bf16 columns of queries 16ks..
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int ks = 4 * hh + k4;
+          // queries 16 ks.. were packed by column quarter ks / 2 at the start of its S^T columns
+          const uint32_t pc = (ks >> 1) * 32 + (ks & 1) * 8;
           umma_ts(tmem + C::dV, tmem + kColS + pc, make_sdesc(o_addr + ks * 2048, BM * 128, 1024), idesc_kv,
                   (it > 0 || ks > 0) ? 1u : 0u);
           umma_ts(tmem + C::dK, tmem + kColDP + pc, make_sdesc(q_addr + ks * 2048, BM * 128, 1024), idesc_kv,
                   (it > 0 || ks > 0) ? 1u : 0u);
         }
-        umma_commit(mma_done);
-        umma_commit(&qd_empty[buf]);
+        umma_commit(&mma_done[hh]);
+      };
+      bool ok = mbar_wait(kv_full, 0, a.err, kErrTimeoutMma, abort_flag);
+      ok = ok && mbar_wait(&qd_full[0], 0, a.err, kErrTimeoutMma, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_sdp(0, 0);
+        issue_sdp(0, 1);
+      }
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int buf = it & 1;
+        for (int hh = 0; hh < 2 && ok; ++hh) {
+          if (!mbar_wait(&p_ready[hh], it & 1, a.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          issue_dkdv(it, hh);
+          if (hh == 1) umma_commit(&qd_empty[buf]);
+          if (it + 1 < n_it) {
+            // the next block's Q / dO landed, and dV / dK of this half (readers of its P^T / dS^T
+            // columns) are done
+            if (hh == 0 && !mbar_wait(&qd_full[buf ^ 1], ((it + 1) >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) {
+              ok = false;
+              break;
+            }
+            if (!mbar_wait(&mma_done[hh], it & 1, a.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            issue_sdp(it + 1, hh);
+          }
+        }
       }
       umma_commit(kv_done);
     }
   } else {
     // -------------------------------------------------------------------------- compute warps
-    const int hf = warp >> 2;  // query-column half [64 hf, 64 hf + 64)
+    const int qt = warp >> 2;  // query-column quarter [32 qt, 32 qt + 32)
     const int kr = (warp & 3) * 32 + lane;
     const int kj = k0 + kr;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t t_s = tmem + kColS + lane_off + 64 * hf, t_dp = tmem + kColDP + lane_off + 64 * hf;
+    const uint32_t t_s = tmem + kColS + lane_off + 32 * qt, t_dp = tmem + kColDP + lane_off + 32 * qt;
     const bool plain = a.seg == nullptr;
     bool alive = true;
     for (int it = 0; it < n_it; ++it) {
       const int buf = it & 1;
-      const int qb = (i_lo + it % n_i) * BM + 64 * hf;  // first query of this half
+      const int qb = (i_lo + it % n_i) * BM + 32 * qt;  // first query of this quarter
+      const long long p_t0 = clock64();
       bool got = mbar_wait(&ld_full[buf], (it >> 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
-      got = got && mbar_wait(sdp_full, it & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      got = got && mbar_wait(&sdp_full[qt >> 1], it & 1, a.err, kErrTimeoutEpilogue, abort_flag);
       if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+      const long long p_t1 = clock64();
       tc_fence_after();
-      const float* lse2 = sLse + buf * BM + 64 * hf;
-      const float* dsq = sDsum + buf * BM + 64 * hf;
-      const int* klo = sKlo + buf * BM + 64 * hf;
-      // every (query, key) pair of this half visible: no masks
-      const bool full = plain && qb >= k0 + BN - 1 && (a.window <= 0 || qb + 63 - k0 < a.window) && qb + 63 < a.S &&
+      const float* lse2 = sLse + buf * BM + 32 * qt;
+      const float* dsq = sDsum + buf * BM + 32 * qt;
+      const int* klo = sKlo + buf * BM + 32 * qt;
+      // every (query, key) pair of this quarter visible: no masks
+      const bool full = plain && qb >= k0 + BN - 1 && (a.window <= 0 || qb + 31 - k0 < a.window) && qb + 31 < a.S &&
                         k0 + BN <= a.S;
+      float sv[32], dp[32];
+      tmem_ld32(t_s, sv);
+      tmem_ld32(t_dp, dp);
+      tmem_wait_ld();
+      const long long p_t2 = clock64();
+      uint32_t pw[16], dw[16];
+      if (full) {
+        // fp32 pairs (f32x2): x = s c + nlse, t = dp scale + nsd, dS = P t
+        const uint64_t c2 = f2_make(a.scale_log2, a.scale_log2), sc2 = f2_make(a.scale, a.scale);
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float sv[32], dp[32];
-        tmem_ld32(t_s + 32 * c, sv);
-        tmem_ld32(t_dp + 32 * c, dp);
-        tmem_wait_ld();
-        uint32_t pw[16], dw[16];
-        if (full) {
-#pragma unroll
-          for (int u = 0; u < 32; u += 4) {
-            const float4 L = *reinterpret_cast<const float4*>(lse2 + 32 * c + u);
-            const float4 D = *reinterpret_cast<const float4*>(dsq + 32 * c + u);
-            const float p0 = ex2(fmaf(sv[u], a.scale_log2, -L.x)), p1 = ex2(fmaf(sv[u + 1], a.scale_log2, -L.y));
-            const float p2 = ex2(fmaf(sv[u + 2], a.scale_log2, -L.z)), p3 = ex2(fmaf(sv[u + 3], a.scale_log2, -L.w));
-            pw[u / 2] = pack_bf16x2(p0, p1);
-            pw[u / 2 + 1] = pack_bf16x2(p2, p3);
-            dw[u / 2] = pack_bf16x2(p0 * (dp[u] - D.x) * a.scale, p1 * (dp[u + 1] - D.y) * a.scale);
-            dw[u / 2 + 1] = pack_bf16x2(p2 * (dp[u + 2] - D.z) * a.scale, p3 * (dp[u + 3] - D.w) * a.scale);
-          }
-        } else {
-#pragma unroll
-          for (int u = 0; u < 32; u += 2) {
-            float pv[2], dv[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int qq = 32 * c + u + e;
-              const int qi = qb + qq;
-              const bool vis = kj <= qi && kj >= klo[qq] && kj < a.S;
-              const float p = vis ? ex2(fmaf(sv[u + e], a.scale_log2, -lse2[qq])) : 0.f;
-              pv[e] = p;
-              dv[e] = p * (dp[u + e] - dsq[qq]) * a.scale;
-            }
-            pw[u / 2] = pack_bf16x2(pv[0], pv[1]);
-            dw[u / 2] = pack_bf16x2(dv[0], dv[1]);
-          }
+        for (int u = 0; u < 32; u += 4) {
+          const float4 L = *reinterpret_cast<const float4*>(lse2 + u);
+          const float4 D = *reinterpret_cast<const float4*>(dsq + u);
+          float x0, x1, x2, x3, d0, d1, d2, d3;
+          f2_split(f2_fma(f2_make(sv[u], sv[u + 1]), c2, f2_make(L.x, L.y)), x0, x1);
+          f2_split(f2_fma(f2_make(sv[u + 2], sv[u + 3]), c2, f2_make(L.z, L.w)), x2, x3);
+          const float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
+          const uint64_t t01 = f2_fma(f2_make(dp[u], dp[u + 1]), sc2, f2_make(D.x, D.y));
+          const uint64_t t23 = f2_fma(f2_make(dp[u + 2], dp[u + 3]), sc2, f2_make(D.z, D.w));
+          f2_split(f2_mul(f2_make(p0, p1), t01), d0, d1);
+          f2_split(f2_mul(f2_make(p2, p3), t23), d2, d3);
+          pw[u / 2] = pack_bf16x2(p0, p1);
+          pw[u / 2 + 1] = pack_bf16x2(p2, p3);
+          dw[u / 2] = pack_bf16x2(d0, d1);
+          dw[u / 2 + 1] = pack_bf16x2(d2, d3);
         }
-        tmem_st16(t_s + 16 * c, pw);
-        tmem_st16(t_dp + 16 * c, dw);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 32; u += 2) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int qq = u + e;
+            const int qi = qb + qq;
+            const bool vis = kj <= qi && kj >= klo[qq] && kj < a.S;
+            const float p = vis ? ex2(fmaf(sv[u + e], a.scale_log2, lse2[qq])) : 0.f;
+            pv[e] = p;
+            dv[e] = p * fmaf(dp[u + e], a.scale, dsq[qq]);
+          }
+          pw[u / 2] = pack_bf16x2(pv[0], pv[1]);
+          dw[u / 2] = pack_bf16x2(dv[0], dv[1]);
+        }
       }
+      const long long p_t3 = clock64();
+      // P^T / dS^T (bf16 pairs) over the first 16 of this quarter's own S^T / dP^T columns
+      tmem_st16(t_s, pw);
+      tmem_st16(t_dp, dw);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_ready);
+      mbar_arrive(&p_ready[qt >> 1]);
+      if (a.prof && lane == 0) {
+        const long long p_t4 = clock64();
+        atomicAdd(&a.prof[0], (unsigned long long)(p_t1 - p_t0));
+        atomicAdd(&a.prof[1], (unsigned long long)(p_t2 - p_t1));
+        atomicAdd(&a.prof[2], (unsigned long long)(p_t3 - p_t2));
+        atomicAdd(&a.prof[3], (unsigned long long)(p_t4 - p_t3));
+        atomicAdd(&a.prof[4], 1ull);
+      }
     }
+    const int hf = qt;  // the write-out uses the first eight warps, one head-dim half each
     // ---- dK, dV out (once per CTA); half hf writes head-dim columns [hf HD/2, (hf + 1) HD/2)
-    if (k0 < a.S) {
+    if (hf < 2 && k0 < a.S) {
       bool have = n_it > 0 && alive;
       if (have) {
         const bool got = mbar_wait(kv_done, 0, a.err, kErrTimeoutEpilogue, abort_flag);
@@ -365,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == kMmaWarpKV) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -641,6 +697,7 @@ static int run_fa_bwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
   a.dv = (__nv_bfloat16*)L.dv; a.dv_tok = L.dv_tok; a.dv_head = L.dv_head;
   a.dv_accumulate = L.dv_accumulate;
   a.err = err;
+  a.prof = (unsigned long long*)L.prof;
   constexpr int smem_kv = Smem<HD>::kBytes;
   constexpr int smem_q = SmemQ<HD>::kBytes;
   static_assert(smem_kv <= 232448 && smem_q <= 232448, "shared memory budget");
@@ -653,7 +710,7 @@ static int run_fa_bwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
     init = true;
   }
   count_launch();
-  fa_bwd_dkdv_kernel<HD><<<dim3((L.S + BN - 1) / BN, L.Hkv, L.B), kThreads, smem_kv, st>>>(tq, tk, tv, to, a);
+  fa_bwd_dkdv_kernel<HD><<<dim3((L.S + BN - 1) / BN, L.Hkv, L.B), kThreadsKV, smem_kv, st>>>(tq, tk, tv, to, a);
   count_launch();
   fa_bwd_dq_kernel<HD><<<dim3((L.S + BM - 1) / BM, L.H, L.B), kThreads, smem_q, st>>>(tq, tk, tv, to, a);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;

@@ -200,6 +200,14 @@ void flash_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& 
   ok(mxk::launch_flash_bwd(L, stream()), "flash_bwd");
 }
 
+// Phase counters for the tcgen05 attention backward (int64 CUDA tensor of >= 8 entries; layout in
+// attention_bwd_sm100.cu), or none. Debug instrumentation.
+static void* g_attn_bwd_prof = nullptr;
+void set_attn_bwd_prof(const OptT& prof) {
+  if (prof.has_value()) need(prof->is_cuda() && prof->numel() >= 8 && prof->element_size() == 8, "prof: 8 x int64");
+  g_attn_bwd_prof = prof.has_value() ? prof->data_ptr() : nullptr;
+}
+
 void flash_bwd_sm100(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& lse,
                      const OptT& seg, int64_t B, int64_t S, int64_t window, double scale, const Tensor& dout,
                      const Tensor& dsum, const Tensor& dq_acc, const Tensor& dq, const Tensor& dk, const Tensor& dv,
@@ -211,6 +219,7 @@ void flash_bwd_sm100(const Tensor& q, const Tensor& k, const Tensor& v, const Te
   L.dout = dout.data_ptr(); L.dsum = dsum.data_ptr<float>(); L.dq_acc = dq_acc.data_ptr<float>();
   L.dq = dq.data_ptr(); L.dk = dk.data_ptr(); L.dk_tok = dk.stride(0); L.dk_head = dk.stride(1);
   L.dv = dv.data_ptr(); L.dv_tok = dv.stride(0); L.dv_head = dv.stride(1); L.dv_accumulate = dv_accumulate;
+  L.prof = g_attn_bwd_prof;
   c10::cuda::CUDAGuard g(q.device());
   ok(mxk::launch_flash_bwd_sm100(L, err.data_ptr<int>(), stream()), "flash_bwd_sm100");
 }
@@ -515,6 +524,7 @@ void register_ops(pybind11::module& m) {
   m.def("ema", &ema);
   m.def("cast_bf16", &cast_bf16);
   m.def("flash_bwd_sm100", &flash_bwd_sm100);
+  m.def("set_attn_bwd_prof", &set_attn_bwd_prof);
   m.def("head_norm_rope", &head_norm_rope);
   m.def("ngram_fwd", &ngram_fwd);
   m.def("ngram_bwd", &ngram_bwd);
