@@ -32,8 +32,7 @@ namespace fab100 {
 
 constexpr int BM = 128;  // queries per block
 constexpr int BN = 128;  // keys per CTA
-constexpr int kThreads = 320;  // dQ kernel: warps 0-7 compute, 8 MMA, 9 TMA
-// dK/dV kernel: warps 0-15 compute (warp w: TMEM lanes 32 (w % 4).., query columns 32 (w / 4)..),
+// Both kernels: warps 0-15 compute (warp w: TMEM lanes 32 (w % 4).., block columns 32 (w / 4)..),
 // 16 MMA, 17 TMA. Four compute warps per SM sub-partition hide the latency of each warp's
 // dependent exp / scale / pack chain.
 constexpr int kThreadsKV = 576;
@@ -438,7 +437,7 @@ struct SmemQ {
 };
 
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsKV, 1)
     fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                      const BwdArgs a) {
@@ -493,13 +492,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[t], 1);
       mbar_init(&dq_mma[t], 1);
     }
-    mbar_init(dp_free, 256);
-    mbar_init(ds_ready, 256);
+    mbar_init(dp_free, 512);
+    mbar_init(ds_ready, 512);
     mbar_init(dq_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 8) {
+  if (warp == kMmaWarpKV) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -508,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 9) {
+  if (warp == kTmaWarpKV) {
     // ------------------------------------------------------------------------- TMA producer
     if (lane == 0 && nj > 0) {
       mbar_arrive_expect_tx(q_full, 2 * tile);
@@ -529,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(&tmV, &v_full[vs], sV + vs * tile + c * BN * 128, kh * HD + c * 64, kr);
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == kMmaWarpKV) {
     // ------------------------------------------------------------------------------ MMA issuer
     if (lane == 0 && nj > 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(BM, BN, false, false);
@@ -571,7 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < BN / 16; ++ks)
-            umma_ts(tmem + kColDq, tmem + kColSb + ps * 128 + (ks >> 2) * 64 + (ks & 3) * 8,
+            umma_ts(tmem + kColDq, tmem + kColSb + ps * 128 + (ks >> 1) * 32 + (ks & 1) * 8,
                     make_sdesc(k_addr + ks * 2048, BN * 128, 1024), idesc_q, (pt > 0 || ks > 0) ? 1u : 0u);
           umma_commit(&dq_mma[ps]);
           umma_commit(&k_empty[pt % 3]);
@@ -579,9 +578,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       umma_commit(dq_done);
     }
-  } else if (warp < 8) {
+  } else if (warp < kMmaWarpKV) {
     // -------------------------------------------------------------------------- compute warps
-    const int hf = warp >> 2;  // key-column half [64 hf, 64 hf + 64) of each block
+    const int qt = warp >> 2;  // key-column quarter [32 qt, 32 qt + 32) of each block
     const int q = (warp & 3) * 32 + lane;
     const int qi = q0 + q;
     const bool in = qi < a.S;
@@ -591,58 +590,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int klo = query_key_lo(qi, a.S, a.window, a.seg, base);
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const bool plain = a.seg == nullptr;
+    // fp32 pairs: x = s c - lse, t = dp scale - D scale, dS = P t
+    const uint64_t c2 = f2_make(a.scale_log2, a.scale_log2), nl2 = f2_make(-lse2, -lse2);
+    const uint64_t sc2 = f2_make(a.scale, a.scale), nd2 = f2_make(-dq_sum * a.scale, -dq_sum * a.scale);
     bool alive = true;
     for (int t = 0; t < nj; ++t) {
       const int st = t & 1;
-      const int kb = (j_lo + t) * BN + 64 * hf;  // first key of this half
+      const int kb = (j_lo + t) * BN + 32 * qt;  // first key of this quarter
       const bool got = mbar_wait(&s_full[st], (t >> 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
       if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
       tc_fence_after();
-      float dp[64];
-      using R32 = float(&)[32];
-      tmem_ld32(tmem + kColDp + lane_off + 64 * hf, reinterpret_cast<R32>(dp[0]));
-      tmem_ld32(tmem + kColDp + lane_off + 64 * hf + 32, reinterpret_cast<R32>(dp[32]));
+      const uint32_t t_s = tmem + kColSb + st * 128 + lane_off + 32 * qt;
+      float dp[32], sv[32];
+      tmem_ld32(tmem + kColDp + lane_off + 32 * qt, dp);
+      tmem_ld32(t_s, sv);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(dp_free);
-      const bool full = plain && q0 >= kb + 63 && (a.window <= 0 || q0 + BM - 1 - kb < a.window) &&
-                        q0 + BM <= a.S && kb + 64 <= a.S;
-      const uint32_t t_s = tmem + kColSb + st * 128 + lane_off + 64 * hf;
+      const bool full = plain && q0 >= kb + 31 && (a.window <= 0 || q0 + BM - 1 - kb < a.window) &&
+                        q0 + BM <= a.S && kb + 32 <= a.S;
+      uint32_t dw[16];
+      if (full) {
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float sv[32];
-        tmem_ld32(t_s + 32 * c, sv);
-        tmem_wait_ld();
-        uint32_t dw[16];
-        if (full) {
-#pragma unroll
-          for (int u = 0; u < 32; u += 2) {
-            const float p0 = ex2(fmaf(sv[u], a.scale_log2, -lse2));
-            const float p1 = ex2(fmaf(sv[u + 1], a.scale_log2, -lse2));
-            dw[u / 2] = pack_bf16x2(p0 * (dp[32 * c + u] - dq_sum) * a.scale,
-                                    p1 * (dp[32 * c + u + 1] - dq_sum) * a.scale);
-          }
-        } else {
-#pragma unroll
-          for (int u = 0; u < 32; u += 2) {
-            float dv[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int kj = kb + 32 * c + u + e;
-              const bool vis = kj <= qi && kj >= klo && kj < a.S;
-              const float p = vis ? ex2(fmaf(sv[u + e], a.scale_log2, -lse2)) : 0.f;
-              dv[e] = p * (dp[32 * c + u + e] - dq_sum) * a.scale;
-            }
-            dw[u / 2] = pack_bf16x2(dv[0], dv[1]);
-          }
+        for (int u = 0; u < 32; u += 2) {
+          float x0, x1, d0, d1;
+          f2_split(f2_fma(f2_make(sv[u], sv[u + 1]), c2, nl2), x0, x1);
+          const float p0 = ex2(x0), p1 = ex2(x1);
+          f2_split(f2_mul(f2_make(p0, p1), f2_fma(f2_make(dp[u], dp[u + 1]), sc2, nd2)), d0, d1);
+          dw[u / 2] = pack_bf16x2(d0, d1);
         }
-        tmem_st16(t_s + 16 * c, dw);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 32; u += 2) {
+          float dv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int kj = kb + u + e;
+            const bool vis = kj <= qi && kj >= klo && kj < a.S;
+            const float p = vis ? ex2(fmaf(sv[u + e], a.scale_log2, -lse2)) : 0.f;
+            dv[e] = p * (dp[u + e] - dq_sum) * a.scale;
+          }
+          dw[u / 2] = pack_bf16x2(dv[0], dv[1]);
+        }
       }
+      // dS (bf16 pairs) over the first 16 of this quarter's own S columns
+      tmem_st16(t_s, dw);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(ds_ready);
     }
-    if (alive && nj > 0) {
+    const int hf = qt;  // the write-out uses the first eight warps, one head-dim half each
+    if (hf < 2 && alive && nj > 0) {
       const bool got = mbar_wait(dq_done, 0, a.err, kErrTimeoutEpilogue, abort_flag);
       if (__all_sync(0xffffffffu, got)) {
         tc_fence_after();
@@ -665,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == kMmaWarpKV) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -712,7 +710,7 @@ static int run_fa_bwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
   count_launch();
   fa_bwd_dkdv_kernel<HD><<<dim3((L.S + BN - 1) / BN, L.Hkv, L.B), kThreadsKV, smem_kv, st>>>(tq, tk, tv, to, a);
   count_launch();
-  fa_bwd_dq_kernel<HD><<<dim3((L.S + BM - 1) / BM, L.H, L.B), kThreads, smem_q, st>>>(tq, tk, tv, to, a);
+  fa_bwd_dq_kernel<HD><<<dim3((L.S + BM - 1) / BM, L.H, L.B), kThreadsKV, smem_q, st>>>(tq, tk, tv, to, a);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
 }
 
