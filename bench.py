@@ -231,6 +231,20 @@ def main(argv=None):
         e2e = {"value": tokens_step / (ems / 1e3), "unit": "tokens/s", "ms_per_step": ems, "wall_ms_per_step": wall * 1e3,
                "h2d_bytes_per_step": int(host[0]["tokens"].numel() * host[0]["tokens"].element_size()),
                "d2h_bytes_per_step": 4}
+    # ------------------------------------------- exposed token exchange (one extra, untimed step)
+    # Device time spent in the expert-parallel exchange kernels and their cross-rank waits, summed
+    # from CUDA events around each exchange (nothing else runs on the stream meanwhile); max over ranks.
+    exposed = 0.0
+    if ctx is not None:
+        from marin_experiments_b200.parallel.ep import exchange_timing
+
+        barrier()
+        with exchange_timing() as xt:
+            trainer.train_step(staged[0])
+        exposed = xt.ms()
+        xt_t = torch.tensor([exposed], device=trainer.device)
+        torch.distributed.all_reduce(xt_t, op=torch.distributed.ReduceOp.MAX)
+        exposed = float(xt_t.item())
     check_kernel_errors()
     out = {
         "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -241,7 +255,8 @@ def main(argv=None):
                    "micro_batch": args.micro_batch, "capacity_factor": cfg.capacity_factor,
                    "parallelism": f"ep{world}" if world > 1 else "single", "l2": "working set >> L2 (no flush needed)",
                    "layers": cfg.num_layers},
-        "mfu": mfu, "flops_per_token": fpt, "loss": loss, "clocks": clk, "gpu_launches": int(launches),
+        "mfu": mfu, "exposed_all_to_all_ms_per_step": exposed, "flops_per_token": fpt, "loss": loss,
+        "clocks": clk, "gpu_launches": int(launches),
         "e2e": e2e,
     }
     if rank == 0:

@@ -26,7 +26,9 @@ from ..ops import api as ops
 
 
 def _a2a(out: torch.Tensor, inp: torch.Tensor, group) -> torch.Tensor:
+    t0 = _mark() if out.is_cuda else None
     dist.all_to_all_single(out, inp, group=group)
+    _span(t0)
     return out
 
 
@@ -104,6 +106,46 @@ def _heap(group, dev, e, cap, d, n_layers):
     return heap_for(group, dev, per_layer * n_layers + shared + (1 << 20))
 
 
+# Exchange timing: while a list is installed (``exchange_timing``), every token exchange of the peer
+# path records a (start, end) pair of CUDA events on the current stream around its kernels and
+# waits. Nothing else runs on that stream in between, so the summed intervals are the device time
+# the step spends exposed in the exchange.
+_TIMING: list | None = None
+
+
+class exchange_timing:
+    """``with exchange_timing() as t: ...; t.ms()`` -- device milliseconds spent in token exchanges
+    (dispatch, combine and their backward passes) by the code run inside the block."""
+
+    def __enter__(self):
+        global _TIMING
+        self.pairs = []
+        _TIMING = self.pairs
+        return self
+
+    def __exit__(self, *exc):
+        global _TIMING
+        _TIMING = None
+        return False
+
+    def ms(self) -> float:
+        torch.cuda.synchronize()
+        return float(sum(a.elapsed_time(b) for a, b in self.pairs))
+
+
+def _mark():
+    if _TIMING is None:
+        return None
+    ev = torch.cuda.Event(enable_timing=True)
+    ev.record()
+    return ev
+
+
+def _span(start):
+    if start is not None and _TIMING is not None:
+        _TIMING.append((start, _mark()))
+
+
 class _MoEEPFused(torch.autograd.Function):
     """Expert parallelism with the token exchange inside the kernels (NVLink peer stores/loads):
     the permute pushes rows into the owners' receive buffers, the combine pulls the owners' outputs,
@@ -132,9 +174,11 @@ class _MoEEPFused(torch.autograd.Function):
         off_y = heap.alloc("y", rows * d * 2)
         slot, perm, wperm, counts = dispatch_plan(sel, keep, comb, e, cap)
         ep = heap.next_epoch(_DISPATCH)
+        t0 = _mark()
         ext().ep_dispatch_push(h, perm, counts, heap.peers, my, e_loc, cap, off_xp, off_cnt, 0, _DISPATCH, ep,
                                heap.counter(_DISPATCH))
         ext().ep_wait(heap.peers, my, 0, _DISPATCH, ep, err_flag(dev))
+        _span(t0)
         xp_recv = heap.tensor(off_xp, (rows, d), torch.bfloat16)
         counts_recv = heap.tensor(off_cnt, (e,), torch.int32)
         Hh = torch.empty(rows, two_i, dtype=torch.bfloat16, device=dev)
@@ -143,12 +187,14 @@ class _MoEEPFused(torch.autograd.Function):
         y_recv = heap.tensor(off_y, (rows, d), torch.bfloat16)
         G.grouped_linear(A, w_d.view(e_loc * d, inter), counts_recv, out=y_recv, n_w=e_loc)
         ey = heap.next_epoch(_Y)
+        t1 = _mark()
         ext().ep_signal(heap.peers, my, 0, _Y, ey)
         ext().ep_wait(heap.peers, my, 0, _Y, ey, err_flag(dev))
         out = torch.empty(t, d, dtype=torch.bfloat16, device=dev)
         y_local = torch.empty(rows, d, dtype=torch.bfloat16, device=dev)
         ext().ep_combine_pull(sel, slot, _c(comb.detach().float()), None if residual is None else _c(residual), out,
                               y_local, heap.peers, my, e_loc, cap, off_y)
+        _span(t1)
         ctx.save_for_backward(xp_recv, Hh, A, y_local, sel, slot, perm, wperm, counts, counts_recv)
         ctx.w_gu, ctx.w_d, ctx.cap, ctx.act, ctx.t, ctx.heap = w_gu, w_d, cap, _ACT[act], t, heap
         ctx.has_res = residual is not None
@@ -174,9 +220,11 @@ class _MoEEPFused(torch.autograd.Function):
         dcomb = torch.empty(sel.shape, dtype=torch.float32, device=dev)
         ext().combine_bwd(dout, y_local, sel, slot, perm, wperm, counts, cap, None, dcomb)
         edy = heap.next_epoch(_DY)
+        t0 = _mark()
         ext().ep_combine_bwd_push(dout, perm, wperm, counts, heap.peers, my, e_loc, cap, off_dy, 0, _DY, edy,
                                   heap.counter(_DY))
         ext().ep_wait(heap.peers, my, 0, _DY, edy, err_flag(dev))
+        _span(t0)
         dy_recv = heap.tensor(off_dy, (rows, d), torch.bfloat16)
         # the receive buffers are reused by the next exchange: weight gradients run now, never deferred
         with G.defer_weight_grads(None):
@@ -188,10 +236,12 @@ class _MoEEPFused(torch.autograd.Function):
             G.grouped_linear_dx(dH, w_gu.view(e_loc * two_i, d), counts_recv, out=dxp, n_w=e_loc)
             G.grouped_linear_dw(dH, xp_recv, counts_recv, out=_mg(w_gu).view(e_loc * two_i, d), n_w=e_loc)
         exp_ = heap.next_epoch(_DXP)
+        t1 = _mark()
         ext().ep_signal(heap.peers, my, 0, _DXP, exp_)
         ext().ep_wait(heap.peers, my, 0, _DXP, exp_, err_flag(dev))
         dh = torch.empty(ctx.t, d, dtype=torch.bfloat16, device=dev)
         ext().ep_unpermute_pull(sel, slot, dh, heap.peers, my, e_loc, cap, off_dxp)
+        _span(t1)
         ctx.w_gu = ctx.w_d = ctx.heap = None
         return (dh, dcomb, None, None, (dout if ctx.has_res else None), None, None, None, None, None, None, None)
 
