@@ -52,6 +52,8 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const 
   TORCH_CHECK((C.stride(0) * C.element_size()) % 16 == 0, "C row stride must be a multiple of 16 bytes");
   // Epilogues store 32-column chunks: C must be wide enough for N rounded up to 32.
   TORCH_CHECK(C.size(1) >= ((N + 31) / 32) * 32 || epi == 1, "C must have at least round_up(N, 32) columns");
+  TORCH_CHECK(epi != 8 || (N % 128 == 0 && C.size(1) >= 2 * N && R.has_value() && R->size(1) >= 2 * N),
+              "SwiGLU backward: N a multiple of 128, C and R with 2N columns");
   const c10::cuda::CUDAGuard guard(A.device());
   mxk::GemmLaunch L{};
   L.a = A.data_ptr();
@@ -94,7 +96,7 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const 
   p.raster_n = 0;
   // Output extents for the TMA stores: columns clip at N; rows clip at M for a single problem,
   // at the buffer end for grouped problems.
-  L.c_cols = N;
+  L.c_cols = epi == 8 ? 2 * N : N;  // SwiGLU backward writes gate and up gradients: 2N columns
   L.c_rows = G == 1 ? std::min<int64_t>(M, C.size(0)) : C.size(0);
   if (C2.has_value()) {
     L.c2_f32 = C2->scalar_type() == at::kFloat ? 1 : 0;

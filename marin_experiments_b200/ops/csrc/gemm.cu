@@ -226,6 +226,8 @@ int launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   // input-gradient GEMMs that add a second gradient term in the epilogue
   MXK_CASE2(4, false, true, EPI_RESID)
   MXK_CASE(128, 6, false, true, EPI_RESID)
+  // activation-gradient GEMM with the SwiGLU backward in the epilogue
+  MXK_CASE2(4, false, true, EPI_SWIGLU_BWD)
   // fused epilogues (forward, K-major x K-major)
   MXK_CASE2(4, false, false, EPI_SWIGLU)
   MXK_CASE2(4, false, false, EPI_RESID)

@@ -43,6 +43,8 @@ enum EpiKind : int {
   EPI_ROWSCALE = 5,  // C = acc * row_scale[row] (bf16)
   EPI_CE = 6,        // logits tile: C = acc (bf16) and per-(row, n-tile half) max / sum(exp(x - max))
   EPI_ACT = 7,       // non-GLU MLP: H = acc (bf16), C = act(acc) (bf16); act in `act_kind`
+  EPI_SWIGLU_BWD = 8,  // acc = dAct [rows, I]; R = SwiGLU pre-activations H [rows, 2I] (blocked
+                       // [gate 128 | up 128] per 256 columns); C = dH [rows, 2I] (bf16), SiLU gate
 };
 
 // Shared-memory plan of one CTA. PAIR: the tile is 256 x BN over a CTA pair; each CTA stages its
@@ -409,6 +411,62 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           ring.bf16_box(&tmC, gv, col0 + c, y0, lane);
           ring.bf16_box(&tmC, uv, col0 + 128 + c, y0, lane);
           ring.bf16_box(&tmC2, av, tc.nt * 128 + c, y0, lane);
+        }
+      } else if constexpr (EPI == EPI_SWIGLU_BWD) {
+        // Activation-gradient tile -> gate / up gradients: the half of the tile drained by this warp
+        // is one 128-column activation block ab, whose gate and up columns are H[:, 256 ab + ..]
+        // and H[:, 256 ab + 128 + ..]. H chunks are loaded one chunk ahead of their use.
+        static_assert(BN == 256, "SwiGLU backward epilogue drains 128-column activation blocks");
+        const int ab = (col0 >> 7) + half;
+        const bool blk_ok = ab * 128 < p.N;  // warp-uniform
+        const __nv_bfloat16* Hrow = reinterpret_cast<const __nv_bfloat16*>(p.R) + crow * p.ldr + ab * 256;
+        auto load_h = [&](int c, uint4 (&g)[4], uint4 (&u)[4]) {
+          if (row_ok && blk_ok) {
+            const uint4* gp = reinterpret_cast<const uint4*>(Hrow + c);
+            const uint4* up = reinterpret_cast<const uint4*>(Hrow + 128 + c);
+#pragma unroll
+            for (int vv = 0; vv < 4; ++vv) {
+              g[vv] = gp[vv];
+              u[vv] = up[vv];
+            }
+          } else {
+#pragma unroll
+            for (int vv = 0; vv < 4; ++vv) g[vv] = u[vv] = make_uint4(0, 0, 0, 0);
+          }
+        };
+        uint4 ga[4], ua[4], gb[4], ub[4];
+        load_h(0, ga, ua);
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          if (c + 32 < 128) {
+            if ((c & 32) == 0) load_h(c + 32, gb, ub);
+            else load_h(c + 32, ga, ua);
+          }
+          float v[32];
+          tmem_ld32(taddr + half * 128 + c, v);
+          tmem_wait_ld();
+          if (!blk_ok) continue;
+          const uint4(&gq)[4] = (c & 32) ? gb : ga;
+          const uint4(&uq)[4] = (c & 32) ? ub : ua;
+          float dg[32], du[32];
+#pragma unroll
+          for (int vv = 0; vv < 4; ++vv) {
+            const uint32_t gw[4] = {gq[vv].x, gq[vv].y, gq[vv].z, gq[vv].w};
+            const uint32_t uw[4] = {uq[vv].x, uq[vv].y, uq[vv].z, uq[vv].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 g2 = unpack_bf16x2(gw[k]), u2 = unpack_bf16x2(uw[k]);
+              const int i = vv * 8 + 2 * k;
+              const float s0 = sigmoid_f(g2.x), s1 = sigmoid_f(g2.y);
+              // d silu(g) / dg = s (1 + g (1 - s)); d(silu(g) u) = (u silu'(g), silu(g))
+              dg[i] = v[i] * u2.x * s0 * (1.f + g2.x * (1.f - s0));
+              dg[i + 1] = v[i + 1] * u2.y * s1 * (1.f + g2.y * (1.f - s1));
+              du[i] = v[i] * g2.x * s0;
+              du[i + 1] = v[i + 1] * g2.y * s1;
+            }
+          }
+          ring.bf16_box(&tmC, dg, ab * 256 + c, y0, lane);
+          ring.bf16_box(&tmC, du, ab * 256 + 128 + c, y0, lane);
         }
       } else if constexpr (EPI == EPI_CE) {
         // Logits tile (bf16) plus per-row (max, sum exp(x - max)) over this tile's valid columns.

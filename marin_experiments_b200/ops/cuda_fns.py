@@ -316,13 +316,18 @@ class _DenseMLP(torch.autograd.Function):
     def backward(ctx, dout):
         h, H, A = ctx.saved_tensors
         dout = _c(dout)
-        dA = G.linear_dx(dout, ctx.w_down)
-        G.linear_dw(dout, A, out=_mg(ctx.w_down), accum=True)
-        dH = torch.empty_like(H)
-        if ctx.glu:
-            ext().swiglu_bwd(dA, H, dH, _ACT[ctx.act], None, 0)
+        if ctx.glu and ctx.act == "silu":
+            # the activation-gradient GEMM writes the gate/up gradients in its epilogue
+            dH = G.linear_dx(dout, ctx.w_down, swiglu_h=H)
+            G.linear_dw(dout, A, out=_mg(ctx.w_down), accum=True)
         else:
-            ext().act_bwd(dA, H, dH, _ACT[ctx.act])
+            dA = G.linear_dx(dout, ctx.w_down)
+            G.linear_dw(dout, A, out=_mg(ctx.w_down), accum=True)
+            dH = torch.empty_like(H)
+            if ctx.glu:
+                ext().swiglu_bwd(dA, H, dH, _ACT[ctx.act], None, 0)
+            else:
+                ext().act_bwd(dA, H, dH, _ACT[ctx.act])
         dh = G.linear_dx(dH, ctx.w_in)
         G.linear_dw(dH, h, out=_mg(ctx.w_in), accum=True)
         ctx.w_in = ctx.w_down = None
@@ -466,10 +471,14 @@ class _MoE(torch.autograd.Function):
         dY = torch.empty_like(Y)
         dcomb = torch.empty(sel.shape, dtype=F32, device=dev)
         ext().combine_bwd(dout, Y, sel, slot, perm, wperm, counts, cap, dY, dcomb)
-        dA = G.grouped_linear_dx(dY, w_d.view(e * d, inter), counts)
-        G.grouped_linear_dw(dY, A, counts, out=_mg(w_d).view(e * d, inter))
-        dH = torch.empty_like(Hh)
-        ext().swiglu_bwd(dA, Hh, dH, _ACT[ctx.act], counts, cap)
+        if ctx.act == "silu":
+            dH = G.grouped_linear_dx(dY, w_d.view(e * d, inter), counts, swiglu_h=Hh)
+            G.grouped_linear_dw(dY, A, counts, out=_mg(w_d).view(e * d, inter))
+        else:
+            dA = G.grouped_linear_dx(dY, w_d.view(e * d, inter), counts)
+            G.grouped_linear_dw(dY, A, counts, out=_mg(w_d).view(e * d, inter))
+            dH = torch.empty_like(Hh)
+            ext().swiglu_bwd(dA, Hh, dH, _ACT[ctx.act], counts, cap)
         dxp = G.grouped_linear_dx(dH, w_gu.view(e * two_i, d), counts)
         G.grouped_linear_dw(dH, xp, counts, out=_mg(w_gu).view(e * two_i, d))
         dh = torch.empty(ctx.t, d, dtype=BF16, device=dev)

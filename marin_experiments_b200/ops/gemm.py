@@ -17,12 +17,13 @@ import torch
 
 from ._ext import err_flag, ext
 
-EPI = {"store": 0, "swiglu": 1, "resid": 2, "gate_mul": 3, "silu": 4, "rowscale": 5, "ce": 6, "act": 7}
+EPI = {"store": 0, "swiglu": 1, "resid": 2, "gate_mul": 3, "silu": 4, "rowscale": 5, "ce": 6, "act": 7,
+       "swiglu_bwd": 8}
 ACT = {"silu": 0, "relu": 1, "gelu": 2}
 
 
 def _pick_bn(n: int, epi: str, b_mn: bool, a_mn: bool) -> int:
-    if epi in ("swiglu", "ce"):
+    if epi in ("swiglu", "ce", "swiglu_bwd"):
         return 256
     if epi == "silu":
         return 128
@@ -52,10 +53,16 @@ def linear(x, w, *, out=None, epi="store", **kw):
     return gemm(x, w, out, M=m, N=n, K=k, epi=epi, **kw)
 
 
-def linear_dx(dy, w, *, out=None, accum=False):
-    """``dy [M, N] @ w [N, K]`` -> ``[M, K]``."""
+def linear_dx(dy, w, *, out=None, accum=False, swiglu_h=None):
+    """``dy [M, N] @ w [N, K]`` -> ``[M, K]``. With ``swiglu_h`` (the SwiGLU pre-activations
+    ``[M, 2K]``, blocked gate/up) the epilogue turns the activation gradient into the gate/up
+    gradients ``[M, 2K]`` (SiLU gate)."""
     m, n = dy.shape
     k = w.shape[1]
+    if swiglu_h is not None:
+        if out is None:
+            out = torch.empty(m, 2 * k, dtype=torch.bfloat16, device=dy.device)
+        return gemm(dy, w, out, b_mn=True, M=m, N=k, K=n, epi="swiglu_bwd", r=swiglu_h)
     if out is None:
         out = torch.empty(m, k, dtype=torch.bfloat16, device=dy.device)
     return gemm(dy, w, out, b_mn=True, M=m, N=k, K=n, accum=accum)
@@ -126,17 +133,21 @@ def grouped_linear(x, w, counts, *, out=None, epi="store", c2=None, n_w=None, **
                 epi=epi, c2=c2, b_mod=0 if n_w == g else n_w, **kw)
 
 
-def grouped_linear_dx(dy, w, counts, *, out=None, n_w=None):
-    """Per-group ``dy[g] [C, N] @ w[g % n_w] [N, K]`` -> ``[G*C, K]``."""
+def grouped_linear_dx(dy, w, counts, *, out=None, n_w=None, swiglu_h=None):
+    """Per-group ``dy[g] [C, N] @ w[g % n_w] [N, K]`` -> ``[G*C, K]``. With ``swiglu_h`` (the SwiGLU
+    pre-activations ``[G*C, 2K]``, blocked gate/up rows) the product is the activation gradient and
+    the epilogue writes the gate/up gradients ``[G*C, 2K]`` instead (SiLU gate)."""
     g = counts.numel()
     n_w = n_w or g
     cap = dy.shape[0] // g
     n = w.shape[0] // n_w
     k = w.shape[1]
     if out is None:
-        out = torch.empty(dy.shape[0], k, dtype=torch.bfloat16, device=dy.device)
+        cols = 2 * k if swiglu_h is not None else k
+        out = torch.empty(dy.shape[0], cols, dtype=torch.bfloat16, device=dy.device)
+    extra = {} if swiglu_h is None else {"epi": "swiglu_bwd", "r": swiglu_h}
     return gemm(dy, w, out, b_mn=True, G=g, M=cap, N=k, K=n, counts=counts, ragged=1, a_grp=cap, b_grp=n,
-                c_grp=cap, b_mod=0 if n_w == g else n_w)
+                c_grp=cap, b_mod=0 if n_w == g else n_w, **extra)
 
 
 def grouped_linear_dw(dy, x, counts, *, out, accum=True, alpha=1.0, n_w=None):

@@ -80,10 +80,14 @@ class _MoEEP(torch.autograd.Function):
         dcomb = torch.empty(sel.shape, dtype=torch.float32, device=dev)
         ext().combine_bwd(dout, y_send, sel, slot, perm, wperm, counts, cap, dy_send, dcomb)
         dy_recv = _a2a(torch.empty_like(dy_send), dy_send, group)
-        dA = G.grouped_linear_dx(dy_recv, w_d.view(e_loc * d, inter), counts_recv, n_w=e_loc)
-        G.grouped_linear_dw(dy_recv, A, counts_recv, out=_mg(w_d).view(e_loc * d, inter), n_w=e_loc)
-        dH = torch.empty_like(Hh)
-        ext().swiglu_bwd(dA, Hh, dH, ctx.act, counts_recv, cap)
+        if ctx.act == 0:  # SiLU gate: the activation-gradient GEMM writes dH in its epilogue
+            dH = G.grouped_linear_dx(dy_recv, w_d.view(e_loc * d, inter), counts_recv, n_w=e_loc, swiglu_h=Hh)
+            G.grouped_linear_dw(dy_recv, A, counts_recv, out=_mg(w_d).view(e_loc * d, inter), n_w=e_loc)
+        else:
+            dA = G.grouped_linear_dx(dy_recv, w_d.view(e_loc * d, inter), counts_recv, n_w=e_loc)
+            G.grouped_linear_dw(dy_recv, A, counts_recv, out=_mg(w_d).view(e_loc * d, inter), n_w=e_loc)
+            dH = torch.empty_like(Hh)
+            ext().swiglu_bwd(dA, Hh, dH, ctx.act, counts_recv, cap)
         dxp_recv = G.grouped_linear_dx(dH, w_gu.view(e_loc * two_i, d), counts_recv, n_w=e_loc)
         G.grouped_linear_dw(dH, xp_recv, counts_recv, out=_mg(w_gu).view(e_loc * two_i, d), n_w=e_loc)
         dxp_send = _a2a(torch.empty_like(dxp_recv), dxp_recv, group)
@@ -228,10 +232,14 @@ class _MoEEPFused(torch.autograd.Function):
         dy_recv = heap.tensor(off_dy, (rows, d), torch.bfloat16)
         # the receive buffers are reused by the next exchange: weight gradients run now, never deferred
         with G.defer_weight_grads(None):
-            dA = G.grouped_linear_dx(dy_recv, w_d.view(e_loc * d, inter), counts_recv, n_w=e_loc)
-            G.grouped_linear_dw(dy_recv, A, counts_recv, out=_mg(w_d).view(e_loc * d, inter), n_w=e_loc)
-            dH = torch.empty_like(Hh)
-            ext().swiglu_bwd(dA, Hh, dH, ctx.act, counts_recv, cap)
+            if ctx.act == 0:  # SiLU gate: the activation-gradient GEMM writes dH in its epilogue
+                dH = G.grouped_linear_dx(dy_recv, w_d.view(e_loc * d, inter), counts_recv, n_w=e_loc, swiglu_h=Hh)
+                G.grouped_linear_dw(dy_recv, A, counts_recv, out=_mg(w_d).view(e_loc * d, inter), n_w=e_loc)
+            else:
+                dA = G.grouped_linear_dx(dy_recv, w_d.view(e_loc * d, inter), counts_recv, n_w=e_loc)
+                G.grouped_linear_dw(dy_recv, A, counts_recv, out=_mg(w_d).view(e_loc * d, inter), n_w=e_loc)
+                dH = torch.empty_like(Hh)
+                ext().swiglu_bwd(dA, Hh, dH, ctx.act, counts_recv, cap)
             dxp = heap.tensor(off_dxp, (rows, d), torch.bfloat16)
             G.grouped_linear_dx(dH, w_gu.view(e_loc * two_i, d), counts_recv, out=dxp, n_w=e_loc)
             G.grouped_linear_dw(dH, xp_recv, counts_recv, out=_mg(w_gu).view(e_loc * two_i, d), n_w=e_loc)

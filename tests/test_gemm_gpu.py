@@ -182,3 +182,42 @@ def test_pair_tile_shapes(G):
     acc = base.clone()
     G.linear_dw(_rand(m, n), a, out=acc, accum=True)  # 1536-row output, split over K
     torch.cuda.synchronize()
+
+
+def _swiglu_bwd_ref(dA, H):
+    m, inter = dA.shape
+    hb = H.float().view(m, inter // 128, 2, 128)
+    g, u = hb[:, :, 0], hb[:, :, 1]
+    d = dA.float().view(m, inter // 128, 128)
+    s = torch.sigmoid(g)
+    dg = d * u * s * (1 + g * (1 - s))
+    du = d * g * s
+    return torch.stack([dg, du], 2).reshape(m, 2 * inter)
+
+
+def test_swiglu_bwd_epilogue(G):
+    """Activation-gradient GEMM whose epilogue writes the SwiGLU gate/up gradients directly
+    (dense: single-CTA and pair tiles; grouped ragged-M over a capacity layout)."""
+    torch.manual_seed(4)
+    for m in (128, 384):
+        d, inter = 256, 512
+        dy, w = _rand(m, d), _rand(d, inter, scale=0.1)
+        H = _rand(m, 2 * inter)
+        dH = G.linear_dx(dy, w, swiglu_h=H)
+        ref = _swiglu_bwd_ref(dy.float() @ w.float(), H)
+        assert _rel(dH, ref) < 2e-2
+    g, cap, d, inter = 4, 512, 256, 768
+    counts = torch.tensor([512, 3, 260, 0], dtype=torch.int32, device="cuda")
+    dy = _rand(g * cap, d)
+    for e in range(g):
+        dy[e * cap + counts[e]:(e + 1) * cap] = 0
+    w = _rand(g * d, inter, scale=0.1)
+    H = _rand(g * cap, 2 * inter)
+    dH = G.grouped_linear_dx(dy, w, counts, swiglu_h=H)
+    torch.cuda.synchronize()
+    for e in range(g):
+        c = int(counts[e])
+        if c:
+            r = slice(e * cap, e * cap + c)
+            ref = _swiglu_bwd_ref(dy[r].float() @ w[e * d:(e + 1) * d].float(), H[r])
+            assert _rel(dH[r], ref) < 2e-2
