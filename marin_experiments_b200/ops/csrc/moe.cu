@@ -225,6 +225,65 @@ __device__ __forceinline__ float key2f(uint32_t k) {
   return __uint_as_float(u);
 }
 
+// Shared-memory variant (T <= kQbSmemKeys): one strided pass stages the expert's keys
+// (logit - alpha, order-preserving uint32) in shared memory; the 4 radix passes then read shared
+// memory, and each digit is chosen by a parallel suffix scan of the 256-bin histogram.
+constexpr int kQbSmemKeys = 49152;  // 192 KB of keys
+
+__global__ void __launch_bounds__(1024) qb_beta_smem_kernel(const float* __restrict__ logits, int ldl,
+                                                            const float* __restrict__ alpha, int T, int E,
+                                                            int qb_count, float* __restrict__ beta) {
+  extern __shared__ uint32_t keys[];  // [T]
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t warp_tot[8];
+  __shared__ uint32_t s_prefix, s_mask, s_k;
+  const int e = blockIdx.x;
+  for (int t = threadIdx.x; t < T; t += blockDim.x) keys[t] = f2key(logits[(long)t * ldl + e] - alpha[t]);
+  if (threadIdx.x == 0) {
+    s_prefix = 0;
+    s_mask = 0;
+    s_k = (uint32_t)min(max(qb_count, 1), T);
+  }
+  __syncthreads();
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    if (threadIdx.x < 256) hist[threadIdx.x] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix, mask = s_mask, k = s_k;  // written again only after the next barrier
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+      const uint32_t key = keys[t];
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    // thread i < 256 holds bin 255 - i; inclusive scan over i = counts of the i+1 largest bins
+    const int i = threadIdx.x, lane = i & 31, w = i >> 5;
+    uint32_t v = i < 256 ? hist[255 - i] : 0u;
+    uint32_t incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (i < 256 && lane == 31) warp_tot[w] = incl;
+    __syncthreads();
+    if (i < 256) {
+      uint32_t before = 0;
+      for (int q = 0; q < w; ++q) before += warp_tot[q];
+      incl += before;
+      const uint32_t excl = incl - v;
+      // the digit is the first bin (from the top) where the running count reaches k
+      if (incl >= k && excl < k) {
+        const int b = 255 - i;
+        s_k = k - excl;
+        s_prefix = prefix | ((uint32_t)b << shift);
+        s_mask = mask | (255u << shift);
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) beta[e] = key2f(s_prefix);
+}
+
 // One block per expert: exact qb_count-th largest of (logit[t, e] - alpha[t]) via 4 radix passes.
 __global__ void qb_beta_kernel(const float* __restrict__ logits, int ldl, const float* __restrict__ alpha, int T,
                                int E, int qb_count, float* __restrict__ beta) {
@@ -517,6 +576,17 @@ int launch_router_bwd(const float* logits, int ldl, const float* lse, const int*
 void launch_qb_beta(const float* logits, int ldl, const float* alpha, int T, int E, int qb_count, float* beta,
                     cudaStream_t st) {
   count_launch();
+  if (T <= kQbSmemKeys) {
+    const size_t sm = (size_t)T * sizeof(uint32_t);
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(qb_beta_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kQbSmemKeys * (int)sizeof(uint32_t));
+      attr = true;
+    }
+    qb_beta_smem_kernel<<<E, 1024, sm, st>>>(logits, ldl, alpha, T, E, qb_count, beta);
+    return;
+  }
   qb_beta_kernel<<<E, 1024, 0, st>>>(logits, ldl, alpha, T, E, qb_count, beta);
 }
 
