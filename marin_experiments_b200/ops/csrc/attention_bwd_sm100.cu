@@ -51,8 +51,11 @@ struct BwdArgs {
   long dv_tok, dv_head;
   int dv_accumulate;
   int* err;
-  // Optional phase counters of the dK/dV compute warps (cycles summed over warps), else null:
-  // [0] waiting for S^T / dP^T, [1] TMEM loads, [2] math, [3] TMEM stores + release, [4] blocks.
+  // Optional phase counters of the dK/dV kernel (cycles summed over warps / CTAs), else null:
+  // compute warps: [0] waiting for S^T / dP^T, [1] TMEM loads, [2] math, [3] TMEM stores + release,
+  // [4] blocks; MMA thread: [5] waiting for P^T / dS^T, [6] waiting for its own MMAs, [7] waiting
+  // for Q / dO, [8] MMA loop total, [9] CTA total, [10] dK / dV write-out; TMA warp: [11] waiting
+  // for a free Q / dO buffer, [12] issuing loads and staging the per-query scalars.
   unsigned long long* prof;
 };
 
@@ -146,6 +149,7 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long cta_t0 = clock64();
   const int j = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
   const int rep = a.H / a.Hkv;
   const int base = b * a.S;
@@ -197,8 +201,10 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
         const int h = kh * rep + it / n_i;
         const int q0 = (i_lo + it % n_i) * BM;
         bool ok = true;
+        const long long pw0 = clock64();
         if (lane == 0) ok = mbar_wait(&qd_empty[buf], ((it >> 1) & 1) ^ 1, a.err, kErrTimeoutProducer, abort_flag);
         if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        const long long pw1 = clock64();
         if (lane == 0) {
           mbar_arrive_expect_tx(&qd_full[buf], 2 * tile);
           for (int c = 0; c < KCH; ++c) {
@@ -206,18 +212,31 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
             tma_load_2d(&tmO, &qd_full[buf], sO + buf * tile + c * BM * 128, h * HD + c * 64, base + q0);
           }
         }
+        // All global loads first (in flight together), then the shared-memory stores: interleaved,
+        // the stores kept each next load waiting for the previous one.
+        float lv[BM / 32], dv[BM / 32];
+#pragma unroll
+        for (int u = 0; u < BM / 32; ++u) {
+          const int qi = q0 + u * 32 + lane;
+          const long idx = (long)(base + qi) * a.H + h;
+          lv[u] = qi < a.S ? __ldg(a.lse + idx) : 0.f;
+          dv[u] = qi < a.S ? __ldg(a.dsum + idx) : 0.f;
+        }
 #pragma unroll
         for (int u = 0; u < BM / 32; ++u) {
           const int q = u * 32 + lane, qi = q0 + q;
           const bool in = qi < a.S;
-          const long idx = (long)(base + qi) * a.H + h;
           // negated and pre-scaled: P^T = 2^(s c + nlse), dS^T = P^T (dP^T scale + nsd)
-          sLse[buf * BM + q] = in ? -a.lse[idx] * 1.4426950408889634f : -INFINITY;
-          sDsum[buf * BM + q] = in ? -a.dsum[idx] * a.scale : 0.f;
+          sLse[buf * BM + q] = in ? -lv[u] * 1.4426950408889634f : -INFINITY;
+          sDsum[buf * BM + q] = in ? -dv[u] * a.scale : 0.f;
           sKlo[buf * BM + q] = query_key_lo(qi, a.S, a.window, a.seg, base);
         }
         __syncwarp();
         mbar_arrive(&ld_full[buf]);
+        if (a.prof && lane == 0) {
+          atomicAdd(&a.prof[11], (unsigned long long)(pw1 - pw0));
+          atomicAdd(&a.prof[12], (unsigned long long)(clock64() - pw1));
+        }
       }
     }
   } else if (warp == kMmaWarpKV) {
@@ -261,6 +280,7 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
         }
         umma_commit(&mma_done[hh]);
       };
+      const long long loop0 = clock64();
       bool ok = mbar_wait(kv_full, 0, a.err, kErrTimeoutMma, abort_flag);
       ok = ok && mbar_wait(&qd_full[0], 0, a.err, kErrTimeoutMma, abort_flag);
       if (ok) {
@@ -271,24 +291,33 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
       for (int it = 0; it < n_it && ok; ++it) {
         const int buf = it & 1;
         for (int hh = 0; hh < 2 && ok; ++hh) {
+          long long w0 = clock64();
           if (!mbar_wait(&p_ready[hh], it & 1, a.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
+          if (a.prof) atomicAdd(&a.prof[5], (unsigned long long)(clock64() - w0));
           tc_fence_after();
           issue_dkdv(it, hh);
           if (hh == 1) umma_commit(&qd_empty[buf]);
           if (it + 1 < n_it) {
             // the next block's Q / dO landed, and dV / dK of this half (readers of its P^T / dS^T
             // columns) are done
+            w0 = clock64();
             if (hh == 0 && !mbar_wait(&qd_full[buf ^ 1], ((it + 1) >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) {
               ok = false;
               break;
             }
+            const long long w1 = clock64();
             if (!mbar_wait(&mma_done[hh], it & 1, a.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
+            if (a.prof) {
+              atomicAdd(&a.prof[7], (unsigned long long)(w1 - w0));
+              atomicAdd(&a.prof[6], (unsigned long long)(clock64() - w1));
+            }
             tc_fence_after();
             issue_sdp(it + 1, hh);
           }
         }
       }
       umma_commit(kv_done);
+      if (a.prof) atomicAdd(&a.prof[8], (unsigned long long)(clock64() - loop0));
     }
   } else {
     // -------------------------------------------------------------------------- compute warps
@@ -374,6 +403,7 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
       }
     }
     const int hf = qt;  // the write-out uses the first eight warps, one head-dim half each
+    const long long out0 = clock64();
     // ---- dK, dV out (once per CTA); half hf writes head-dim columns [hf HD/2, (hf + 1) HD/2)
     if (hf < 2 && k0 < a.S) {
       bool have = n_it > 0 && alive;
@@ -417,7 +447,9 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
         }
       }
     }
+    if (a.prof && lane == 0 && warp < 8) atomicAdd(&a.prof[10], (unsigned long long)(clock64() - out0));
   }
+  if (a.prof && threadIdx.x == 0) atomicAdd(&a.prof[9], (unsigned long long)(clock64() - cta_t0));
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarpKV) {
