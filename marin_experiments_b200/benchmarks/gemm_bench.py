@@ -30,6 +30,9 @@ SHAPES = [
     ("gatednorm_down_silu", 16384, 128, 1536, "silu"),
     ("o_fwd_resid", 16384, 1536, 1536, "resid"),
     ("gatednorm_dw_up", 16384, 1536, 128, "dw"),
+    # grouped expert weight gradients (64 experts, ragged K = 1024 tokens each, fp32 accumulate)
+    ("expert_gateup_dw", 1536, 1536, 1024, "gdw"),
+    ("expert_down_dw", 1536, 768, 1024, "gdw"),
 ]
 
 
@@ -83,6 +86,17 @@ def run(shapes=SHAPES, once: bool = False):
             h = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
             mine = lambda: G.gemm(a, b, c, M=m, N=n, K=k, epi="silu", c2=h)
             ref = lambda: torch.nn.functional.silu(torch.matmul(a, b.t(), out=h), inplace=False)
+        elif mode == "gdw":  # per expert: dy [cap, m]^T x [cap, n] -> [m, n] fp32, K = k tokens
+            ge, cap = 64, 1280
+            cnt = torch.full((ge,), k, dtype=torch.int32, device="cuda")
+            a = torch.randn(ge * cap, m, device="cuda").to(torch.bfloat16)
+            b = torch.randn(ge * cap, n, device="cuda").to(torch.bfloat16)
+            c = torch.zeros(ge * m, n, device="cuda", dtype=torch.float32)
+            a3, b3 = a.view(ge, cap, m)[:, :k], b.view(ge, cap, n)[:, :k]
+            cb = torch.empty(ge, m, n, device="cuda", dtype=torch.bfloat16)
+            mine = lambda: G.grouped_linear_dw(a, b, cnt, out=c)
+            ref = lambda: torch.bmm(a3.transpose(1, 2), b3, out=cb)
+            flops_mult = ge
         else:  # dw: dy [m, n], x [m, k] -> [n, k] fp32 accumulate
             a = torch.randn(m, n, device="cuda").to(torch.bfloat16)
             b = torch.randn(m, k, device="cuda").to(torch.bfloat16)
@@ -90,7 +104,7 @@ def run(shapes=SHAPES, once: bool = False):
             cb = torch.empty(n, k, device="cuda", dtype=torch.bfloat16)
             mine = lambda: G.linear_dw(a, b, out=c, accum=True)
             ref = lambda: torch.matmul(a.t(), b, out=cb)
-        flops = 2.0 * m * n * k
+        flops = 2.0 * m * n * k * (flops_mult if mode == "gdw" else 1)
         if once:
             mine()
             torch.cuda.synchronize()
