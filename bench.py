@@ -136,7 +136,10 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--seqs-per-gpu", type=int, default=32)
-    ap.add_argument("--micro-batch", type=int, default=8)
+    ap.add_argument("--micro-batch", type=int, default=None,
+                    help="sequences per microbatch (gradient accumulation); default 8 on one GPU, where "
+                         "~6B parameters with fp32 master, grads and moments leave room for 8 x 2048 tokens of "
+                         "activations, and 16 with expert parallelism, where the experts are sharded")
     ap.add_argument("--layers", type=int, default=None, help="(debug only) override layer count")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args(argv)
@@ -151,6 +154,8 @@ def main(argv=None):
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.micro_batch is None:
+        args.micro_batch = 8 if world == 1 else 16
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local_rank)
     ctx = pdist.init(ep_size=world) if world > 1 else None
