@@ -242,14 +242,19 @@ class _MoEEPFused(torch.autograd.Function):
                 ext().swiglu_bwd(dA, Hh, dH, ctx.act, counts_recv, cap)
             dxp = heap.tensor(off_dxp, (rows, d), torch.bfloat16)
             G.grouped_linear_dx(dH, w_gu.view(e_loc * two_i, d), counts_recv, out=dxp, n_w=e_loc)
-            G.grouped_linear_dw(dH, xp_recv, counts_recv, out=_mg(w_gu).view(e_loc * two_i, d), n_w=e_loc)
         exp_ = heap.next_epoch(_DXP)
         t1 = _mark()
         ext().ep_signal(heap.peers, my, 0, _DXP, exp_)
+        _span(t1)
+        # The gate/up weight gradient reads dH (local) and this layer's own receive buffer, never the
+        # shared dy / dxp buffers, so it runs while the peers pull this rank's dxp rows.
+        with G.defer_weight_grads(None):
+            G.grouped_linear_dw(dH, xp_recv, counts_recv, out=_mg(w_gu).view(e_loc * two_i, d), n_w=e_loc)
+        t2 = _mark()
         ext().ep_wait(heap.peers, my, 0, _DXP, exp_, err_flag(dev))
         dh = torch.empty(ctx.t, d, dtype=torch.bfloat16, device=dev)
         ext().ep_unpermute_pull(sel, slot, dh, heap.peers, my, e_loc, cap, off_dxp)
-        _span(t1)
+        _span(t2)
         ctx.w_gu = ctx.w_d = ctx.heap = None
         return (dh, dcomb, None, None, (dout if ctx.has_res else None), None, None, None, None, None, None, None)
 
