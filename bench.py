@@ -167,6 +167,16 @@ def main(argv=None):
     run = GrugRunConfig(model=cfg, optimizer=GrugMoeAdamHConfig(learning_rate=0.01, adam_lr=6e-4, warmup=0.0),
                         trainer=GrugTrainerConfig(trainer=TrainerConfig(seed=0, num_train_steps=1000)))
     trainer = Trainer(run, device=f"cuda:{local_rank}", micro_batch=args.micro_batch, dist=ctx)
+    if world > 1 and args.micro_batch > 8:
+        # Guard for the default: one 2048-token sequence of this model keeps ~4.6 GB of activations and
+        # exchange buffers (measured on one GPU: 36 GB per 8 sequences). Fall back to 8-sequence
+        # microbatches on every rank if any rank lacks the room (same decision everywhere).
+        free, _ = torch.cuda.mem_get_info()
+        fits = torch.tensor([1.0 if free > args.micro_batch * 4.6e9 * 1.1 else 0.0], device=trainer.device)
+        torch.distributed.all_reduce(fits, op=torch.distributed.ReduceOp.MIN)
+        if fits.item() < 0.5:
+            args.micro_batch = 8
+            trainer.micro_batch = 8
     seqs = args.seqs_per_gpu
     seq = cfg.max_seq_len
     data = UniformTokenBatches(seqs, seq, cfg.vocab_size, seed=2, pin=True, rank=rank)
