@@ -142,6 +142,9 @@ def main(argv=None):
                          "activations, and 16 with expert parallelism, where the experts are sharded")
     ap.add_argument("--layers", type=int, default=None, help="(debug only) override layer count")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile-trace", default=None,
+                    help="after the timed steps, run one more step under torch.profiler, write its Chrome trace "
+                         "here and a device-time breakdown by kernel family to <path>.md (shares only)")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return reference_arm(args)
@@ -193,8 +196,9 @@ def main(argv=None):
     check_kernel_errors()
     # ------------------------------------------------------------------ device-timed steps
     staged = [{"tokens": next(data)["tokens"].to(trainer.device)} for _ in range(args.steps)]
-    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[0])
-                          if False else local_rank)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+    clocks = ClockSampler(int(vis[local_rank]) if local_rank < len(vis) and vis[local_rank].strip().isdigit()
+                          else local_rank)  # nvidia-smi index of this rank's GPU
     barrier()
     torch.cuda.synchronize()
     clocks.start()
@@ -260,6 +264,15 @@ def main(argv=None):
         xt_t = torch.tensor([exposed], device=trainer.device)
         torch.distributed.all_reduce(xt_t, op=torch.distributed.ReduceOp.MAX)
         exposed = float(xt_t.item())
+    if args.profile_trace:
+        from marin_experiments_b200.utils.analysis import breakdown_table, profile_call
+
+        barrier()
+        path = args.profile_trace if world == 1 else f"{args.profile_trace}.rank{rank}"
+        b = profile_call(lambda: trainer.train_step(staged[0]), steps=1, trace_path=path)
+        if rank == 0:
+            with open(f"{args.profile_trace}.md", "w") as f:
+                f.write(breakdown_table(b) + "\n")
     check_kernel_errors()
     out = {
         "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
