@@ -33,6 +33,14 @@ SHAPES = [
     # grouped expert weight gradients (64 experts, ragged K = 1024 tokens each, fp32 accumulate)
     ("expert_gateup_dw", 1536, 1536, 1024, "gdw"),
     ("expert_down_dw", 1536, 768, 1024, "gdw"),
+    # expert forward / input-gradient GEMMs as the MoE layer runs them: 64 experts, 1280-row capacity
+    # slots holding 1024 routed tokens each; M = tokens per expert, N = out, K = in
+    ("expert_gateup_fwd_swiglu", 1024, 1536, 1536, "gfwd"),
+    ("expert_down_fwd", 1024, 1536, 768, "gfwd"),
+    ("expert_down_dx_swiglu_bwd", 1024, 1536, 768, "gdx"),
+    ("expert_gateup_dx", 1024, 1536, 1536, "gdx"),
+    ("shared_gateup_dw", 16384, 6144, 1536, "dw"),
+    ("qkv_dw", 16384, 2304, 1536, "dw"),
 ]
 
 
@@ -97,6 +105,33 @@ def run(shapes=SHAPES, once: bool = False):
             mine = lambda: G.grouped_linear_dw(a, b, cnt, out=c)
             ref = lambda: torch.bmm(a3.transpose(1, 2), b3, out=cb)
             flops_mult = ge
+        elif mode == "gfwd":  # per expert: x [tokens, k] @ w[n, k]^T; gate/up rows get the SwiGLU epilogue
+            ge, cap = 64, 1280
+            cnt = torch.full((ge,), m, dtype=torch.int32, device="cuda")
+            a = torch.randn(ge * cap, k, device="cuda").to(torch.bfloat16)
+            b = torch.randn(ge * n, k, device="cuda").to(torch.bfloat16)
+            c = torch.empty(ge * cap, n, device="cuda", dtype=torch.bfloat16)
+            sw = name.endswith("swiglu")
+            act = torch.empty(ge * cap, n // 2, device="cuda", dtype=torch.bfloat16) if sw else None
+            a3, b3 = a.view(ge, cap, k)[:, :m], b.view(ge, n, k)
+            cb = torch.empty(ge, m, n, device="cuda", dtype=torch.bfloat16)
+            mine = (lambda: G.grouped_linear(a, b, cnt, out=c, epi="swiglu", c2=act)) if sw else \
+                (lambda: G.grouped_linear(a, b, cnt, out=c))
+            ref = lambda: torch.bmm(a3, b3.transpose(1, 2), out=cb)
+            flops_mult = ge
+        elif mode == "gdx":  # per expert: dy [tokens, n] @ w[n, k]; swiglu_bwd writes gate/up grads
+            ge, cap = 64, 1280
+            cnt = torch.full((ge,), m, dtype=torch.int32, device="cuda")
+            a = torch.randn(ge * cap, n, device="cuda").to(torch.bfloat16)
+            b = torch.randn(ge * n, k, device="cuda").to(torch.bfloat16)
+            sw = name.endswith("swiglu_bwd")
+            hh = torch.randn(ge * cap, 2 * k, device="cuda").to(torch.bfloat16) if sw else None
+            a3, b3 = a.view(ge, cap, n)[:, :m], b.view(ge, n, k)
+            cb = torch.empty(ge, m, k, device="cuda", dtype=torch.bfloat16)
+            mine = lambda: G.grouped_linear_dx(a, b, cnt, swiglu_h=hh)
+            ref = lambda: torch.bmm(a3, b3, out=cb)
+            flops_mult = ge
+            c = None
         else:  # dw: dy [m, n], x [m, k] -> [n, k] fp32 accumulate
             a = torch.randn(m, n, device="cuda").to(torch.bfloat16)
             b = torch.randn(m, k, device="cuda").to(torch.bfloat16)
@@ -104,7 +139,7 @@ def run(shapes=SHAPES, once: bool = False):
             cb = torch.empty(n, k, device="cuda", dtype=torch.bfloat16)
             mine = lambda: G.linear_dw(a, b, out=c, accum=True)
             ref = lambda: torch.matmul(a.t(), b, out=cb)
-        flops = 2.0 * m * n * k * (flops_mult if mode == "gdw" else 1)
+        flops = 2.0 * m * n * k * (flops_mult if mode in ("gdw", "gfwd", "gdx") else 1)
         if once:
             mine()
             torch.cuda.synchronize()

@@ -275,7 +275,7 @@ def breakdown_table(b: dict) -> str:
     return "\n".join(lines)
 
 
-def profile_call(fn, steps: int = 1, trace_path: str | None = None) -> dict:
+def profile_call(fn, steps: int = 1, trace_path: str | None = None, top: int = 40) -> dict:
     """Run ``fn()`` ``steps`` times under ``torch.profiler`` (CPU + CUDA activity) and return
     ``profile_breakdown`` of the device events. Numbers taken this way are for shares only: the
     profiler adds overhead, so step times come from the un-profiled benchmark."""
@@ -290,7 +290,7 @@ def profile_call(fn, steps: int = 1, trace_path: str | None = None) -> dict:
         if torch.cuda.is_available():
             torch.cuda.synchronize()
     prof.export_chrome_trace(path)
-    return profile_breakdown(load_trace(path), steps=steps)
+    return profile_breakdown(load_trace(path), steps=steps, top=top)
 
 
 def main(argv=None):
