@@ -54,6 +54,10 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const 
   TORCH_CHECK(C.size(1) >= ((N + 31) / 32) * 32 || epi == 1, "C must have at least round_up(N, 32) columns");
   TORCH_CHECK(epi != 8 || (N % 128 == 0 && C.size(1) >= 2 * N && R.has_value() && R->size(1) >= 2 * N),
               "SwiGLU backward: N a multiple of 128, C and R with 2N columns");
+  // the SwiGLU backward epilogue loads R (the pre-activations) with TMA: 16-byte aligned rows
+  TORCH_CHECK(epi != 8 || (reinterpret_cast<uintptr_t>(R->data_ptr()) % 16 == 0 && (R->stride(0) * 2) % 16 == 0 &&
+                           R->stride(1) == 1 && R->size(0) >= (G == 1 ? std::min<int64_t>(M, C.size(0)) : C.size(0))),
+              "SwiGLU backward: R must be row-major with 16-byte aligned rows and cover C's rows");
   const c10::cuda::CUDAGuard guard(A.device());
   mxk::GemmLaunch L{};
   L.a = A.data_ptr();

@@ -126,14 +126,17 @@ static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
   if (!make_tmap_bf16_2d(&ta, L.a, L.a_inner, L.a_outer, L.lda, 64, A_MN ? 64 : kBM)) return kErrBadArgs;
   if (!make_tmap_bf16_2d(&tb, L.b, L.b_inner, L.b_outer, L.ldb, 64, B_MN ? 64 : BNL)) return kErrBadArgs;
   if (!make_tmap_epi(&tc, L.p.C, L.p.c_f32 != 0, L.c_cols, L.c_rows, L.p.ldc)) return kErrBadArgs;
-  if (L.p.C2 != nullptr && EPI != EPI_CE) {
+  if constexpr (EPI == EPI_SWIGLU_BWD) {
+    // second map = the SwiGLU pre-activations H, loaded by the epilogue in the store boxes' layout
+    if (!make_tmap_epi(&tc2, L.p.R, false, L.c_cols, L.c_rows, L.p.ldr)) return kErrBadArgs;
+  } else if (L.p.C2 != nullptr && EPI != EPI_CE) {
     if (!make_tmap_epi(&tc2, L.p.C2, L.c2_f32 != 0, L.c2_cols, L.c2_rows, L.p.ldc2)) return kErrBadArgs;
   } else {
     tc2 = tc;
   }
   MXK_TRACE("tmaps");
   auto kern = gemm_sm100_kernel<BN, STAGES, A_MN, B_MN, EPI, PAIR>;
-  constexpr int smem = gemm_smem_bytes<BN, STAGES, PAIR>();
+  constexpr int smem = gemm_smem_bytes<BN, STAGES, PAIR, EPI>();
   static_assert(smem <= 232448, "shared memory budget exceeded");
   static bool attr_set = false;
   if (!attr_set) {
@@ -227,7 +230,10 @@ int launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   MXK_CASE2(4, false, true, EPI_RESID)
   MXK_CASE(128, 6, false, true, EPI_RESID)
   // activation-gradient GEMM with the SwiGLU backward in the epilogue
-  MXK_CASE2(4, false, true, EPI_SWIGLU_BWD)
+  // (fewer operand stages: the epilogue stages its H chunks in shared memory)
+  if (L.bn == 256 && !L.a_mn && L.b_mn && L.epi == EPI_SWIGLU_BWD)
+    return pair ? launch_impl<256, 4, false, true, EPI_SWIGLU_BWD, true>(L, stream)
+                : launch_impl<256, 3, false, true, EPI_SWIGLU_BWD, false>(L, stream);
   // fused epilogues (forward, K-major x K-major)
   MXK_CASE2(4, false, false, EPI_SWIGLU)
   MXK_CASE2(4, false, false, EPI_RESID)

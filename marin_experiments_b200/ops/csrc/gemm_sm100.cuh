@@ -57,6 +57,33 @@ struct GemmSmem {
   static constexpr int kEpiBytes = kEpiWarps * kStageBufs * kStageBox;
 };
 
+// Epilogue shared memory. Most epilogues use a per-warp staging ring of kStageBufs store boxes.
+// The SwiGLU backward epilogue instead gives each warp kSlots slots of two boxes (gate, up): H
+// chunks are loaded into a slot by TMA, overwritten in place with the gradients and stored from
+// there; one mbarrier per slot follows the loads. Its slot count is what the shared memory left
+// after the operand stages holds (at most 3).
+constexpr int kSmemLimit = 232448;
+constexpr int kSwbSlotBytes = 2 * kStageBox;
+
+template <int BN, int STAGES, bool PAIR>
+constexpr int smem_fixed_bytes() {
+  // operand stages + 1 KB alignment slack + barriers/scalars + tile prefix table
+  return STAGES * GemmSmem<BN, PAIR>::kStageBytes + 1024 + 256 + (kMaxGroups + 1) * 4;
+}
+
+template <int BN, int STAGES, bool PAIR, int EPI>
+constexpr int epi_slots() {
+  if (EPI != EPI_SWIGLU_BWD) return kStageBufs;
+  constexpr int n = (kSmemLimit - smem_fixed_bytes<BN, STAGES, PAIR>()) / (kEpiWarps * (kSwbSlotBytes + 8));
+  return n > 3 ? 3 : n;
+}
+
+template <int BN, int STAGES, bool PAIR, int EPI>
+constexpr int epi_bytes() {
+  if (EPI != EPI_SWIGLU_BWD) return GemmSmem<BN, PAIR>::kEpiBytes;
+  return kEpiWarps * epi_slots<BN, STAGES, PAIR, EPI>() * (kSwbSlotBytes + 8);
+}
+
 __device__ __forceinline__ int group_count(const GemmParams& p, int g) {
   if (p.counts) return p.counts[g];
   return p.ragged == 2 ? p.K : p.M;
@@ -206,7 +233,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::kABytes;
   uint8_t* sEpi = smem + STAGES * S::kStageBytes;  // 1024-aligned (stage sizes are multiples of 1 KB)
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + S::kEpiBytes);
+  constexpr int kSlots = epi_slots<BN, STAGES, PAIR, EPI>();
+  static_assert(EPI != EPI_SWIGLU_BWD || kSlots >= 2, "SwiGLU backward epilogue needs two H slots per warp");
+  // SwiGLU backward: H-slot barriers after all warps' slots
+  uint64_t* h_bar = reinterpret_cast<uint64_t*>(sEpi + kEpiWarps * kSlots * kSwbSlotBytes);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + epi_bytes<BN, STAGES, PAIR, EPI>());
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -242,9 +273,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tempty_bar[b], (PAIR ? 2 : 1) * 32 * kEpiWarps);
     }
     mbar_init(drain_bar, 1);
+    if constexpr (EPI == EPI_SWIGLU_BWD) {
+      for (int i = 0; i < kEpiWarps * kSlots; ++i) mbar_init(&h_bar[i], 1);
+    }
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if constexpr (EPI == EPI_SWIGLU_BWD) prefetch_tmap(&tmC2);
   }
   if (warp == 1) {
     if constexpr (PAIR) {
@@ -376,6 +411,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int tcount = 0;
     const uint32_t tempty_c0 = PAIR ? mapa_shared(&tempty_bar[0], 0) : 0u;
     const uint32_t tempty_c1 = PAIR ? mapa_shared(&tempty_bar[1], 0) : 0u;
+    // SwiGLU backward: this warp's stream of H chunks (4 chunks of 32 activation columns per tile,
+    // in tile order) is loaded by TMA kSlots - 1 chunks ahead of its use, across tile boundaries,
+    // so the loads overlap the previous chunks' math and the wait for the next accumulator.
+    uint8_t* h_slots = sEpi + (warp - 2) * kSlots * kSwbSlotBytes;
+    uint64_t* h_bars = h_bar + (warp - 2) * kSlots;
+    int h_issued = 0, h_used = 0;
+    int la_tile = total_tiles, la_c = 0, la_x = 0, la_y = 0;  // next chunk to load
+    bool h_fail = false;
+    auto la_seek = [&](int t) {  // first tile >= t of this worker that has work: its H box origin
+      for (; t < total_tiles; t += tstep) {
+        const TileCoord lc = decode_tile<BN, TM>(p, prefix, t);
+        if (lc.nkb == 0) continue;
+        la_y = (p.c_mod ? lc.g % p.c_mod : lc.g) * p.c_grp + lc.mt * TM + (int)rank * kBM + q * 32;
+        la_x = (((lc.nt * BN) >> 7) + half) * 256;
+        break;
+      }
+      la_tile = t;
+      la_c = 0;
+    };
+    auto h_issue = [&]() {
+      if (la_tile >= total_tiles) return;
+      const int slot = h_issued % kSlots;
+      if (lane == 0) {
+        // the slot last held chunk h_issued - kSlots; only the stores of the chunk consumed since
+        // then may still be reading shared memory
+        bulk_wait_read<1>();
+        uint8_t* dst = h_slots + slot * kSwbSlotBytes;
+        mbar_arrive_expect_tx(&h_bars[slot], kSwbSlotBytes);
+        tma_load_2d(&tmC2, &h_bars[slot], dst, la_x + la_c * 32, la_y);
+        tma_load_2d(&tmC2, &h_bars[slot], dst + kStageBox, la_x + 128 + la_c * 32, la_y);
+      }
+      ++h_issued;
+      if (++la_c == 4) la_seek(la_tile + tstep);
+    };
+    if constexpr (EPI == EPI_SWIGLU_BWD) {
+      la_seek(tile0);
+      for (int i = 0; i < kSlots - 1; ++i) h_issue();
+    }
     for (int tile = tile0; tile < total_tiles; tile += tstep) {
       TileCoord tc = decode_tile<BN, TM>(p, prefix, tile);
       if (tc.nkb == 0) continue;
@@ -415,59 +488,63 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       } else if constexpr (EPI == EPI_SWIGLU_BWD) {
         // Activation-gradient tile -> gate / up gradients: the half of the tile drained by this warp
         // is one 128-column activation block ab, whose gate and up columns are H[:, 256 ab + ..]
-        // and H[:, 256 ab + 128 + ..]. H chunks are loaded one chunk ahead of their use.
+        // and H[:, 256 ab + 128 + ..]. Each 32-column chunk's H boxes arrive in a slot (64B
+        // swizzle: 16-byte piece k of row r at piece k ^ ((r >> 1) & 3)); every lane overwrites its
+        // row with dG / dU and the slot's two boxes are stored to C's matching columns.
         static_assert(BN == 256, "SwiGLU backward epilogue drains 128-column activation blocks");
         const int ab = (col0 >> 7) + half;
         const bool blk_ok = ab * 128 < p.N;  // warp-uniform
-        const __nv_bfloat16* Hrow = reinterpret_cast<const __nv_bfloat16*>(p.R) + crow * p.ldr + ab * 256;
-        auto load_h = [&](int c, uint4 (&g)[4], uint4 (&u)[4]) {
-          if (row_ok && blk_ok) {
-            const uint4* gp = reinterpret_cast<const uint4*>(Hrow + c);
-            const uint4* up = reinterpret_cast<const uint4*>(Hrow + 128 + c);
-#pragma unroll
-            for (int vv = 0; vv < 4; ++vv) {
-              g[vv] = gp[vv];
-              u[vv] = up[vv];
-            }
-          } else {
-#pragma unroll
-            for (int vv = 0; vv < 4; ++vv) g[vv] = u[vv] = make_uint4(0, 0, 0, 0);
-          }
-        };
-        uint4 ga[4], ua[4], gb[4], ub[4];
-        load_h(0, ga, ua);
+        const int sw = (lane >> 1) & 3;
 #pragma unroll 1
         for (int c = 0; c < 128; c += 32) {
-          if (c + 32 < 128) {
-            if ((c & 32) == 0) load_h(c + 32, gb, ub);
-            else load_h(c + 32, ga, ua);
-          }
+          const int slot = h_used % kSlots;
+          const uint32_t hph = (h_used / kSlots) & 1;
           float v[32];
           tmem_ld32(taddr + half * 128 + c, v);
+          const bool hok = mbar_wait(&h_bars[slot], hph, p.err, kErrTimeoutEpilogue, abort_flag);
           tmem_wait_ld();
-          if (!blk_ok) continue;
-          const uint4(&gq)[4] = (c & 32) ? gb : ga;
-          const uint4(&uq)[4] = (c & 32) ? ub : ua;
-          float dg[32], du[32];
+          if (!__all_sync(0xffffffffu, hok)) {
+            h_fail = true;
+            break;
+          }
+          ++h_used;
+          uint8_t* gbuf = h_slots + slot * kSwbSlotBytes;
+          uint8_t* grow = gbuf + lane * 64;
+          uint8_t* urow = grow + kStageBox;
+          if (blk_ok) {
 #pragma unroll
-          for (int vv = 0; vv < 4; ++vv) {
-            const uint32_t gw[4] = {gq[vv].x, gq[vv].y, gq[vv].z, gq[vv].w};
-            const uint32_t uw[4] = {uq[vv].x, uq[vv].y, uq[vv].z, uq[vv].w};
+            for (int vv = 0; vv < 4; ++vv) {
+              uint4* gp = reinterpret_cast<uint4*>(grow + ((vv ^ sw) << 4));
+              uint4* up = reinterpret_cast<uint4*>(urow + ((vv ^ sw) << 4));
+              const uint4 g4 = *gp, u4 = *up;
+              const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+              const uint32_t uw[4] = {u4.x, u4.y, u4.z, u4.w};
+              uint32_t dgw[4], duw[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 g2 = unpack_bf16x2(gw[k]), u2 = unpack_bf16x2(uw[k]);
-              const int i = vv * 8 + 2 * k;
-              const float s0 = sigmoid_f(g2.x), s1 = sigmoid_f(g2.y);
-              // d silu(g) / dg = s (1 + g (1 - s)); d(silu(g) u) = (u silu'(g), silu(g))
-              dg[i] = v[i] * u2.x * s0 * (1.f + g2.x * (1.f - s0));
-              dg[i + 1] = v[i + 1] * u2.y * s1 * (1.f + g2.y * (1.f - s1));
-              du[i] = v[i] * g2.x * s0;
-              du[i + 1] = v[i + 1] * g2.y * s1;
+              for (int k = 0; k < 4; ++k) {
+                const float2 g2 = unpack_bf16x2(gw[k]), u2 = unpack_bf16x2(uw[k]);
+                const int i = vv * 8 + 2 * k;
+                const float s0 = sigmoid_f(g2.x), s1 = sigmoid_f(g2.y);
+                // d silu(g) / dg = s (1 + g (1 - s)); d(silu(g) u) = (u silu'(g), silu(g))
+                dgw[k] = pack_bf16x2(v[i] * u2.x * s0 * (1.f + g2.x * (1.f - s0)),
+                                     v[i + 1] * u2.y * s1 * (1.f + g2.y * (1.f - s1)));
+                duw[k] = pack_bf16x2(v[i] * g2.x * s0, v[i + 1] * g2.y * s1);
+              }
+              *gp = make_uint4(dgw[0], dgw[1], dgw[2], dgw[3]);
+              *up = make_uint4(duw[0], duw[1], duw[2], duw[3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmC, gbuf, ab * 256 + c, y0);
+              tma_store_2d(&tmC, gbuf + kStageBox, ab * 256 + 128 + c, y0);
             }
           }
-          ring.bf16_box(&tmC, dg, ab * 256 + c, y0, lane);
-          ring.bf16_box(&tmC, du, ab * 256 + 128 + c, y0, lane);
+          if (lane == 0) bulk_commit();
+          __syncwarp();
+          h_issue();
         }
+        if (h_fail) break;
       } else if constexpr (EPI == EPI_CE) {
         // Logits tile (bf16) plus per-row (max, sum exp(x - max)) over this tile's valid columns.
         float m = -INFINITY, ssum = 0.f;
@@ -577,6 +654,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if constexpr (PAIR) mbar_arrive_remote(buf ? tempty_c1 : tempty_c0);
       else mbar_arrive(&tempty_bar[buf]);
     }
+    if constexpr (EPI == EPI_SWIGLU_BWD) {
+      // H loads issued but never consumed (an aborted run): let them land (bounded) before exit
+      for (int j = h_used; j < h_issued; ++j) {
+        long long t0 = clock64();
+        while (!mbar_try_wait(&h_bars[j % kSlots], (j / kSlots) & 1) && clock64() - t0 < (1ll << 26)) {}
+      }
+    }
     if (lane == 0) bulk_wait_all();  // every TMA store / reduce of this warp has landed
   }
 
@@ -592,11 +676,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-template <int BN, int STAGES, bool PAIR = false>
+template <int BN, int STAGES, bool PAIR = false, int EPI = EPI_STORE>
 constexpr int gemm_smem_bytes() {
   // stages + epilogue staging + 1 KB alignment slack + barriers/scalars + tile prefix table
-  return STAGES * GemmSmem<BN, PAIR>::kStageBytes + GemmSmem<BN, PAIR>::kEpiBytes + 1024 + 256 +
-         (kMaxGroups + 1) * 4;
+  return smem_fixed_bytes<BN, STAGES, PAIR>() + epi_bytes<BN, STAGES, PAIR, EPI>();
 }
 
 }  // namespace mxk

@@ -221,3 +221,23 @@ def test_swiglu_bwd_epilogue(G):
             r = slice(e * cap, e * cap + c)
             ref = _swiglu_bwd_ref(dy[r].float() @ w[e * d:(e + 1) * d].float(), H[r])
             assert _rel(dH[r], ref) < 2e-2
+    # more tiles than workers (the epilogue's H loads run ahead across tiles) and N = 384, whose last
+    # tile has an activation block past N: pair tiles, dense
+    m, d, inter = 16384, 256, 384
+    dy, w = _rand(m, d), _rand(d, inter, scale=0.1)
+    H = _rand(m, 2 * inter)
+    dH = G.linear_dx(dy, w, swiglu_h=H)
+    assert _rel(dH, _swiglu_bwd_ref(dy.float() @ w.float(), H)) < 2e-2
+    # single-CTA tiles (capacity 384 is not a multiple of 256), 288 tiles, grouped
+    g, cap, d, inter = 16, 384, 256, 1536
+    counts = torch.randint(200, cap + 1, (g,), dtype=torch.int32, device="cuda")
+    dy = _rand(g * cap, d)
+    for e in range(g):
+        dy[e * cap + counts[e]:(e + 1) * cap] = 0
+    w = _rand(g * d, inter, scale=0.1)
+    H = _rand(g * cap, 2 * inter)
+    dH = G.grouped_linear_dx(dy, w, counts, swiglu_h=H)
+    for e in range(g):
+        r = slice(e * cap, e * cap + int(counts[e]))
+        ref = _swiglu_bwd_ref(dy[r].float() @ w[e * d:(e + 1) * d].float(), H[r])
+        assert _rel(dH[r], ref) < 2e-2
