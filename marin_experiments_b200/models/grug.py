@@ -219,6 +219,13 @@ class Block(nn.Module):
         h, x = self.mlp_norm.with_residual(x)
         if not self.cfg.is_moe:
             return self.mlp(h, residual=x), None
+        if self.shared is not None and self.shared.tp is None and self.mlp.ep_group is not None:
+            from ..parallel import ep
+
+            if ep.overlap_shared_enabled(h, self.mlp.ep_group):
+                # shared expert on a side stream while the routed experts exchange tokens
+                return ep.with_shared_overlap(
+                    h, self.shared, lambda: self.mlp(h, residual=x, dp_group=dp_group, logit_bias=logit_bias))
         base = x if self.shared is None else self.shared(h, residual=x)
         x, stats = self.mlp(h, residual=base, dp_group=dp_group, logit_bias=logit_bias)
         return x, stats

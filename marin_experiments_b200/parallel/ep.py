@@ -296,6 +296,70 @@ def _moe_ep_cpu(h, r, w_gu, w_d, cap, group, residual, act):
     return out if residual is None else residual + out
 
 
+# ------------------------------------------------------------------ shared expert beside the exchange
+# Under the peer-memory exchange much of the MoE layer's device time is the token exchanges (NVLink
+# transfers inside the push / pull kernels and the waits for the slowest peer), which a single
+# stream cannot overlap with compute. The shared expert depends only on the layer input, so it can
+# run on a side stream meanwhile, forward and (through autograd's per-stream backward) backward.
+# Opt-in (MXK_EP_OVERLAP=1): measured on 2 GPUs it does not shorten the step (702.0 vs 702.9 ms),
+# because the shared expert's persistent GEMMs hold every SM's shared memory and the exchange
+# kernels queue behind them; a side GEMM limited to part of the SMs is the next step.
+_SIDE: dict[int, torch.cuda.Stream] = {}
+
+
+def overlap_shared_enabled(h: torch.Tensor, group) -> bool:
+    """Shared expert on a side stream: CUDA tensors, an expert-parallel group, the peer-memory
+    exchange, and ``MXK_EP_OVERLAP=1``."""
+    return (h.is_cuda and group is not None and ep_impl() == "peer"
+            and os.environ.get("MXK_EP_OVERLAP", "0") == "1")
+
+
+def side_stream(dev: torch.device) -> torch.cuda.Stream:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    s = _SIDE.get(idx)
+    if s is None:
+        s = _SIDE[idx] = torch.cuda.Stream(device=torch.device("cuda", idx))
+    return s
+
+
+class _JoinShared(torch.autograd.Function):
+    """``y + s`` where ``s`` (the shared expert's output) was computed on the side stream.
+
+    Forward: the training stream waits for the side stream, then adds. Backward: both inputs get the
+    incoming gradient; the side stream uses it (``record_stream`` keeps its memory from being reused
+    meanwhile). The shared expert's backward writes its weight gradients into ``main_grad`` outside
+    autograd, so a callback at the end of the backward pass makes the training stream wait for the
+    side stream: whatever reads the gradients next (all-reduce, optimizer) sees them complete."""
+
+    @staticmethod
+    def forward(ctx, y, s, side, main):
+        main.wait_stream(side)
+        s.record_stream(main)
+        ctx.side, ctx.main = side, main
+        return y + s
+
+    @staticmethod
+    def backward(ctx, g):
+        side, main = ctx.side, ctx.main
+        g.record_stream(side)
+        torch.autograd.Variable._execution_engine.queue_callback(lambda: main.wait_stream(side))
+        ctx.side = ctx.main = None
+        return g, g, None, None
+
+
+def with_shared_overlap(h: torch.Tensor, shared_fn, moe_fn):
+    """``moe_fn()`` (returning ``(y, extra)``, y without the shared expert) on the current stream
+    while ``shared_fn(h)`` runs on the side stream; returns ``(y + shared_fn(h), extra)``."""
+    main = torch.cuda.current_stream(h.device)
+    side = side_stream(h.device)
+    side.wait_stream(main)
+    h.record_stream(side)
+    with torch.cuda.stream(side):
+        s = shared_fn(h)
+    y, extra = moe_fn()
+    return _JoinShared.apply(y, s, side, main), extra
+
+
 def ep_impl() -> str:
     """``peer`` (default on GPUs): exchange inside the kernels over NVLink peer memory;
     ``nccl``: the same capacity layout moved by NCCL all-to-alls (the baseline path)."""

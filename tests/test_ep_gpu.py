@@ -165,3 +165,101 @@ def test_ep_peer_exchange_matches_nccl():
         p.join(timeout=60)
     for r in range(world):
         assert all(v < 1e-2 for v in results[r]), (r, results[r])
+
+
+def _worker_overlap(rank, world, port, q):
+    """Shared expert on a side stream during the exchange vs the sequential composition: 4 forward +
+    backward passes of one MoE layer each, alternating between two layers' buffers; outputs, input
+    gradients and the shared and routed experts' weight gradients (read right after backward, on the
+    training stream). One layer per pass keeps the routing identical in both modes: the two modes
+    add the shared and routed outputs to the residual in a different order, and a second layer's
+    top-k would flip for near-tied tokens on that rounding difference."""
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["MXK_EP_IMPL"] = "peer"
+    os.environ["MXK_EP_OVERLAP"] = "1"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from marin_experiments_b200.ops import api
+        from marin_experiments_b200.ops._ext import check_kernel_errors
+        from marin_experiments_b200.parallel import ep
+
+        dev = torch.device("cuda", rank)
+        t, d, inter, e, k, si = 1024, 256, 256, 8, 2, 512
+        e_loc = e // world
+        lo, hi = rank * e_loc, (rank + 1) * e_loc
+
+        def param(x):
+            p = x.to(dev).requires_grad_(True)
+            p.main_grad = torch.zeros(x.shape, dtype=torch.float32, device=dev)
+            return p
+
+        g = torch.Generator().manual_seed(5)
+        layers = [((torch.randn(e, d, generator=g) / 8).bfloat16(),
+                   (torch.randn(e, 2 * inter, d, generator=g) / 16).bfloat16(),
+                   (torch.randn(e, d, inter, generator=g) / 16).bfloat16(),
+                   (torch.randn(2 * si, d, generator=g) / 16).bfloat16(),
+                   (torch.randn(d, si, generator=g) / 16).bfloat16()) for _ in range(2)]
+        gx = torch.Generator().manual_seed(200 + rank)
+        xs = [torch.randn(t, d, generator=gx).bfloat16() for _ in range(4)]
+        gouts = [torch.randn(t, d, generator=gx).bfloat16() for _ in range(4)]
+        res = {}
+        for mode in ("sequential", "overlap"):
+            params = [(param(wr), param(wgu[lo:hi]), param(wdn[lo:hi]), param(sgu), param(sdn))
+                      for wr, wgu, wdn, sgu, sdn in layers]
+            outs, grads = [], []
+            for it in range(4):
+                h0 = xs[it].to(dev).requires_grad_(True)
+                h = h0
+                for li in (it % 2,):
+                    wr, wg, wd, sg, sd = params[li]
+                    r = api.route(h, wr, torch.zeros(e, device=dev), k, qb_count=32)
+                    cap = api.capacity_for(t, k, e, 2.0)
+                    if mode == "sequential":
+                        base = api.dense_mlp(h, sg, sd, glu=True, act="silu", residual=h)
+                        h = ep.moe_experts_ep(h, r, wg, wd, cap, dist.group.WORLD, residual=base, layer=li,
+                                              n_layers=2)
+                    else:
+                        assert ep.overlap_shared_enabled(h, dist.group.WORLD)
+                        hh, rr = h, r
+                        h, _ = ep.with_shared_overlap(
+                            hh, lambda z, sg=sg, sd=sd: api.dense_mlp(z, sg, sd, glu=True, act="silu"),
+                            lambda hh=hh, rr=rr, wg=wg, wd=wd, li=li: (
+                                ep.moe_experts_ep(hh, rr, wg, wd, cap, dist.group.WORLD, residual=hh, layer=li,
+                                                  n_layers=2), None))
+                h.backward(gouts[it].to(dev))
+                outs.append(h.detach().float().cpu())
+                grads.append(h0.grad.float().cpu())
+            mg = [[p[j].main_grad.cpu() for p in params] for j in (1, 2, 3, 4)]
+            torch.cuda.synchronize()
+            check_kernel_errors()
+            res[mode] = (outs, grads, *mg)
+
+        def rel(a, b):
+            return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
+
+        errs = [rel(a, b) for ga, gb in zip(res["overlap"], res["sequential"]) for a, b in zip(ga, gb)]
+        q.put((rank, errs))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_shared_expert_overlap_matches_sequential():
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_overlap, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert all(v < 1e-2 for v in results[r]), (r, results[r])
