@@ -1,0 +1,68 @@
+"""Named sweeps: plan expansion and local job execution."""
+
+import sys
+
+import pytest
+
+from marin_experiments_b200.experiments import megagpt, sweeps
+from marin_experiments_b200.utils import analysis
+
+
+def test_plan_expands_arms():
+    jobs = sweeps.plan("anchor", gpus=8, tag="t1")
+    assert [j.name for j in jobs] == ["t1-e64k4", "t1-e64k8", "t1-e128k8", "t1-e256k8"]
+    j = jobs[2]
+    assert j.env["SP_EXPERTS"] == "128" and j.env["SP_TOPK"] == "8" and j.env["SP_EP"] == "8"
+    assert j.env["SP_TAG"] == "t1-e128k8" and j.env["SP_HIDDEN"] == sweeps.BASE["SP_HIDDEN"]
+    assert "torch.distributed.run" in j.argv and "--nproc-per-node=8" in j.argv and "127.0.0.1" in j.argv
+    assert j.argv[-2:] == ["-m", sweeps.LAUNCHER]
+    # per-arm GPU counts and batch per GPU (weak scaling)
+    sc = {j.name: j for j in sweeps.plan("scale", tag="s")}
+    assert sc["s-g1"].gpus == 1 and sc["s-g1"].argv == [sys.executable, "-m", sweeps.LAUNCHER]
+    assert sc["s-g4"].env["SP_BATCH"] == "128" and sc["s-g4"].env["SP_EP"] == "4"
+    assert [j.name for j in sweeps.plan("lever", only=["embed512"], tag="x")] == ["x-embed512"]
+    with pytest.raises(KeyError):
+        sweeps.plan("lever", only=["nope"])
+    assert sweeps.plan("dp", gpus=2)[1].env["SP_EP"] == "1"
+
+
+def test_arms_are_launchable():
+    """Every arm's environment builds a launch config (and the salted run id differs per tag)."""
+    for name in sweeps.SWEEPS:
+        if name == "pp":
+            continue
+        for job in sweeps.plan(name, gpus=8, tag="c"):
+            env = {k: v for k, v in job.env.items() if k != "SP_PP_MODE"}
+            launch, arm = megagpt.make_launch(env)
+            assert arm.startswith("[arm] ")
+            assert "SP_TAG" in job.env
+
+
+def test_run_jobs_and_table(tmp_path, capsys):
+    fake = {"demo": {"fast": {"X_TOK": "900000"}, "slow": {"X_TOK": "100000"},
+                     "oom": {"X_TOK": "0", "X_FAIL": "1"}}}
+    code = ("import os\n"
+            "if os.environ.get('X_FAIL'):\n"
+            "    raise SystemExit('torch.OutOfMemoryError: CUDA out of memory')\n"
+            "print('[arm] ' + os.environ['SP_TAG'] + '  mode=fixed D=1536 d_e=1536(factorized=False) seq=2048 E=64 "
+            "k=4 min_k=0 coef=0.0 nominal_active_frac=6.25% batch=32 steps=12 budget=1e18')\n"
+            "for s in range(12):\n"
+            "    print(f\"[THRUPUT] step={s} dt=0.500s tok_s={int(os.environ['X_TOK']) + s} mfu=0.2000 bs=32\")\n")
+    jobs = sweeps.plan("demo", gpus=1, tag="d", sweeps=fake)
+    for j in jobs:
+        j.argv = [sys.executable, "-c", code]
+    logs = sweeps.run(jobs, str(tmp_path), timeout_s=60)
+    runs = analysis.analyze_logs(logs, warmup=8)
+    assert runs[0].tok_s == 900009.5 and runs[1].tok_s == 100009.5 and runs[2].failure == "oom"
+    table = analysis.sweep_table(runs).splitlines()
+    assert "d-fast" in table[2] and "d-slow" in table[3] and "oom" in table[4]
+    sweeps.run(jobs[:1], str(tmp_path / "dry"), dry_run=True)
+    assert "[d-fast] gpus=1" in capsys.readouterr().out
+
+
+def test_run_timeout_kills_only_the_job(tmp_path):
+    jobs = sweeps.plan("demo", gpus=1, tag="to", sweeps={"demo": {"hang": {}}})
+    jobs[0].argv = [sys.executable, "-c", "import time; print('start', flush=True); time.sleep(60)"]
+    logs = sweeps.run(jobs, str(tmp_path), timeout_s=2)
+    text = open(logs[0]).read()
+    assert "killed after 2s" in text and "exit timeout" in text
