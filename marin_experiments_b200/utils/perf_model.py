@@ -14,6 +14,11 @@ Per optimizer step and per GPU it estimates:
 * pipeline bubble from the schedule simulator (``parallel.schedules``);
 * the optimizer pass: ~48 bytes of HBM traffic per fp32 parameter held by the GPU.
 
+``pp_from_profile`` predicts pipeline parallelism from a measured expert-parallel step (the
+profile-anchored method of megagpt-speedrun/h100_pp_model.py), and ``cross_node`` compares
+synchronous data parallelism with pipeline parallelism across nodes joined by per-GPU network
+interfaces (the question of delayed-gradient-pp/pp_throughput_model.py).
+
 Peaks come from ``MEASURED_PEAKS.json`` at the repository root when present (written by the
 benchmark driver of the machine), else from the constants below.
 """
@@ -136,6 +141,120 @@ def estimate(cfg, layout: Layout, hw: Hardware | None = None) -> Estimate:
     return Estimate(step, tok_s, mfu, parts)
 
 
+# ------------------------------------------------------------------ profile-anchored PP prediction
+@dataclass(frozen=True)
+class StepProfile:
+    """A measured expert-parallel training step, split into additive device-time parts (ms):
+    ``compute`` (everything that is not the two below), ``ep_exposed`` (device time inside the token
+    exchanges, ``bench.py``'s exposed all-to-all), ``optimizer`` (the fused optimizer passes)."""
+    step_ms: float
+    ep_exposed_ms: float
+    optimizer_ms: float
+    tokens_per_gpu: int = 65536
+
+    @property
+    def compute_ms(self) -> float:
+        return self.step_ms - self.ep_exposed_ms - self.optimizer_ms
+
+
+@dataclass(frozen=True)
+class PPKnobs:
+    """The uncertain parts of a pipeline-parallel prediction. ``eta_sync``: GEMM efficiency of the
+    smaller per-microbatch GEMMs of a synchronous schedule (1 = as efficient as the measured step);
+    ``eta_async``: the same for the no-flush asynchronous schedule, whose stages run whole batches;
+    ``recompute``: compute multiplier for activation recompute; ``token_tax``: extra tokens the
+    asynchronous schedule's staleness costs to reach the same loss (a fraction)."""
+    eta_sync: float = 0.9
+    eta_async: float = 1.0
+    recompute: float = 1.0
+    token_tax: float = 0.0
+
+
+def pp_from_profile(cfg, prof: StepProfile, *, stages: int, microbatches: int, schedule: str = "1f1b",
+                    knobs: PPKnobs = PPKnobs(), hw: Hardware | None = None) -> dict:
+    """Per-GPU step time of pipeline parallelism on the same GPUs, from a measured EP step.
+
+    PP keeps each layer's experts on its stage's GPU, so the token exchange disappears; what is
+    added: the stage-boundary activation sends over NVLink (forward activation and backward gradient
+    per microbatch, ``tokens * D * 2`` bytes each way per boundary, overlapped except for the
+    pipeline fill), the schedule's bubble (``parallel.schedules`` simulator) for the synchronous
+    schedules, and the knobs. The optimizer part is kept (same parameters per GPU in total).
+    Returns step times (ms), tokens/s of the job and the speed-up over the measured step, for the
+    synchronous schedule and the asynchronous one (effective tokens/s after the token tax)."""
+    from ..parallel.schedules import SCHEDULES, simulate
+
+    hw = hw or Hardware.measured()
+    act = prof.tokens_per_gpu * cfg.hidden_dim * 2  # one direction, per step, per boundary
+    p2p_ms = 2 * act / hw.nvlink_bytes_s * 1e3 / microbatches  # the fill / drain part that stays exposed
+    sched = SCHEDULES[schedule](stages, microbatches)
+    sim = simulate(sched, 1.0, 1.0, 1.0) if schedule == "zb" else simulate(sched, 1.0, 2.0)
+    bubble = sim["bubble"]
+    sync_busy = prof.compute_ms / knobs.eta_sync * knobs.recompute
+    sync_ms = sync_busy / (1 - bubble) + p2p_ms + prof.optimizer_ms
+    async_ms = prof.compute_ms / knobs.eta_async + p2p_ms + prof.optimizer_ms
+    n_tok = prof.tokens_per_gpu
+    return {
+        "ep_ms": prof.step_ms, "sync_ms": sync_ms, "async_ms": async_ms, "bubble": bubble, "p2p_ms": p2p_ms,
+        "ep_tok_s_per_gpu": n_tok / prof.step_ms * 1e3,
+        "sync_tok_s_per_gpu": n_tok / sync_ms * 1e3,
+        "async_tok_s_per_gpu": n_tok / async_ms * 1e3 / (1 + knobs.token_tax),
+        "sync_speedup": prof.step_ms / sync_ms,
+        "async_speedup": prof.step_ms / async_ms / (1 + knobs.token_tax),
+    }
+
+
+# ------------------------------------------------------------------ across nodes
+@dataclass(frozen=True)
+class Cluster:
+    """Nodes of ``gpus_per_node`` NVSwitch-connected GPUs joined by a per-GPU network interface of
+    ``net_bytes_s`` each way (400 Gb/s per GPU: 50 GB/s); ``net_overlap`` of the cross-node gradient
+    all-reduce hides under the backward pass."""
+    nodes: int = 2
+    gpus_per_node: int = 8
+    net_bytes_s: float = 50e9
+    net_overlap: float = 0.5
+
+
+def cross_node(cfg, cl: Cluster, *, tokens_per_gpu: int = 65536, microbatches: int = 8, schedule: str = "1f1b",
+               hw: Hardware | None = None) -> dict:
+    """Synchronous data parallelism across nodes (expert parallelism inside each node) vs pipeline
+    parallelism across nodes (one stage per node, expert parallelism inside it).
+
+    DP: every step all-reduces the fp32 gradients across nodes: each GPU carries its expert shard and
+    1/gpus_per_node of the replicated parameters (reduced inside the node first), ``2 (n-1)/n`` of
+    that through its own interface, all GPUs of a node in parallel. PP: only the stage-boundary activations (forward) and their
+    gradients (backward) cross the network, ``tokens * D * 2`` bytes each way per GPU, overlapped
+    except for the fill, plus the schedule's bubble. The in-node part of both is ``estimate`` for one
+    node. Returns step times (s), tokens/s of the cluster, and the ratio of the cross-node
+    communication to the compute (above 1 the network is the bound: the regime where PP pays)."""
+    from ..parallel.schedules import SCHEDULES, simulate
+
+    hw = hw or Hardware.measured()
+    node = estimate(cfg, Layout(gpus=cl.gpus_per_node, ep=cl.gpus_per_node, tokens_per_gpu=tokens_per_gpu), hw)
+    n = cl.nodes
+    experts, other = param_split(cfg)
+    # per GPU across the network: its own expert shard, and 1/gpus_per_node of the replicated
+    # parameters (reduced inside the node over NVLink first); each GPU's interface carries its share
+    shard = (experts + other) * 4 / cl.gpus_per_node
+    dp_net = 2 * (n - 1) / n * shard / cl.net_bytes_s if n > 1 else 0.0
+    dp_step = node.step_s + (1 - cl.net_overlap) * dp_net
+    act = tokens_per_gpu * cfg.hidden_dim * 2
+    pp_net = 2 * act / cl.net_bytes_s
+    bubble = 0.0
+    if n > 1:
+        sched = SCHEDULES[schedule](n, microbatches)
+        sim = simulate(sched, 1.0, 1.0, 1.0) if schedule == "zb" else simulate(sched, 1.0, 2.0)
+        bubble = sim["bubble"]
+    # a stage holds 1/n of the layers: its per-step compute is the node's for 1/n of the model on n x
+    # the tokens per GPU, i.e. the same busy time; the network part overlaps except the fill
+    pp_step = node.step_s / (1 - bubble) + pp_net / microbatches
+    total = cl.nodes * cl.gpus_per_node * tokens_per_gpu
+    return {"dp_step_s": dp_step, "pp_step_s": pp_step, "dp_tok_s": total / dp_step, "pp_tok_s": total / pp_step,
+            "dp_net_s": dp_net, "pp_net_s": pp_net, "bubble": bubble,
+            "dp_comm_compute_ratio": dp_net / node.parts["compute_s"],
+            "pp_comm_compute_ratio": pp_net / node.parts["compute_s"]}
+
+
 def table(cfg, layouts: list[Layout], hw: Hardware | None = None) -> str:
     rows = ["| gpus | ep | pp | tp | sched | step ms | tok/s | MFU | exposed comm |", "|---|---|---|---|---|---|---|---|---|"]
     for lay in layouts:
@@ -152,6 +271,16 @@ def main():
     lays = [Layout(gpus=g, ep=g) for g in (1, 2, 4, 8)]
     lays += [Layout(gpus=8, ep=2, pp=4, microbatches=16, schedule=s) for s in ("gpipe", "1f1b", "zb")]
     print(table(cfg, lays))
+    # the measured 4-GPU EP step (731.9 ms, 131.6 ms exposed exchange, ~43 ms optimizer)
+    prof = StepProfile(step_ms=731.9, ep_exposed_ms=131.6, optimizer_ms=43.0)
+    for sched in ("1f1b", "zb"):
+        r = pp_from_profile(cfg, prof, stages=4, microbatches=16, schedule=sched)
+        print(f"PP4 {sched}: sync {r['sync_ms']:.0f} ms ({r['sync_speedup']:.2f}x), "
+              f"async {r['async_ms']:.0f} ms ({r['async_speedup']:.2f}x), bubble {r['bubble']:.3f}")
+    for nodes in (2, 4, 8):
+        r = cross_node(cfg, Cluster(nodes=nodes))
+        print(f"{nodes} nodes: DP {r['dp_tok_s']:,.0f} tok/s, PP {r['pp_tok_s']:,.0f} tok/s, "
+              f"network/compute DP {r['dp_comm_compute_ratio']:.2f} PP {r['pp_comm_compute_ratio']:.3f}")
 
 
 if __name__ == "__main__":
