@@ -15,6 +15,7 @@ distributed caller all-reduce the per-group squared norms of sharded groups befo
 from __future__ import annotations
 
 import math
+import os
 
 import numpy as np
 import torch
@@ -26,7 +27,13 @@ _CHUNK_DTYPE = np.dtype([("start", "<i8"), ("len", "<i4"), ("mat", "<i4"), ("gro
 
 def _ns_quintic(g: torch.Tensor, steps: int) -> torch.Tensor:
     """Newton-Schulz orthogonalisation with the quintic iteration of Muon
-    (a, b, c) = (3.4445, -4.7750, 2.0315) (Jordan et al., "Muon", 2024)."""
+    (a, b, c) = (3.4445, -4.7750, 2.0315) (Jordan et al., "Muon", 2024); the iteration of
+    megagpt-speedrun/async_pipeline.py:379-388. On CUDA, matrices whose sides are multiples of 64 run
+    the iterations in bf16 on the tcgen05 GEMM (``_ns_quintic_sm100``); the rest (and
+    ``MXK_NS_FP32=1``) run them in fp32."""
+    if (g.is_cuda and g.shape[-2] % 64 == 0 and g.shape[-1] % 64 == 0
+            and os.environ.get("MXK_NS_FP32", "0") != "1"):
+        return _ns_quintic_sm100(g, steps)
     a, b, c = 3.4445, -4.7750, 2.0315
     x = g.float()
     transpose = x.shape[-2] > x.shape[-1]
@@ -40,6 +47,30 @@ def _ns_quintic(g: torch.Tensor, steps: int) -> torch.Tensor:
     if transpose:
         x = x.transpose(-1, -2)
     return x
+
+
+def _ns_quintic_sm100(g: torch.Tensor, steps: int) -> torch.Tensor:
+    """The quintic Newton-Schulz iteration in bf16 on the tcgen05 GEMM, per matrix of ``g``
+    ``[..., r, c]`` (sides multiples of 64): the Frobenius normalisation in fp32, then per step
+    ``A = X X^T``, ``A A`` (A is symmetric), ``X <- a X + (b A + c A A) X`` with X the wide
+    orientation. Returns fp32."""
+    from ..ops import gemm as G
+
+    a, b, c = 3.4445, -4.7750, 2.0315
+    r, cdim = g.shape[-2], g.shape[-1]
+    flat = g.reshape(-1, r, cdim).float()
+    transpose = r > cdim
+    out = torch.empty_like(flat)
+    for i in range(flat.shape[0]):
+        xf = flat[i].t() if transpose else flat[i]
+        x = (xf / (xf.norm() + 1e-7)).to(torch.bfloat16).contiguous()
+        for _ in range(steps):
+            A = G.linear(x, x)  # x x^T  [m, m]
+            AA = G.linear(A, A)  # A A^T = A A
+            B = (b * A.float() + c * AA.float()).to(torch.bfloat16)
+            x = (a * x.float() + G.linear_dx(B, x).float()).to(torch.bfloat16)  # B [m, m] @ x [m, n]
+        out[i] = x.float().t() if transpose else x.float()
+    return out.reshape(g.shape)
 
 
 class FusedOptimizer:

@@ -288,3 +288,25 @@ def test_qk_norm_rope_kernels(hd, heads, kv):
     gk = g[:, heads:].contiguous().cuda().bfloat16()
     ext().qk_norm_rope_bwd(gq, gk, qkv, rstd, cos, sin, dqkv, s, heads, kv, hd, True, mult)
     assert rel(dqkv[:, :nq + nk].reshape(t, heads + kv, hd), raw.grad) < 2e-2
+
+
+def test_newton_schulz_tcgen05_matches_fp32(monkeypatch):
+    """Muon's quintic Newton-Schulz in bf16 on the tcgen05 GEMM vs the fp32 iteration: close, and
+    the singular values land in the quintic's band around 1."""
+    from marin_experiments_b200.ops._ext import ext
+    from marin_experiments_b200.optim.fused import _ns_quintic
+
+    torch.manual_seed(0)
+    for shape in [(256, 512), (768, 256), (3, 128, 192)]:
+        g = torch.randn(*shape, device="cuda")
+        monkeypatch.setenv("MXK_NS_FP32", "1")
+        ref = _ns_quintic(g, 5)
+        monkeypatch.delenv("MXK_NS_FP32")
+        n0 = ext().launch_count()
+        out = _ns_quintic(g, 5)
+        torch.cuda.synchronize()
+        assert ext().launch_count() > n0  # the tcgen05 GEMMs ran
+        assert out.shape == g.shape and out.dtype == torch.float32
+        assert ((out - ref).norm() / ref.norm()).item() < 0.1
+        sv = torch.linalg.svdvals(out.reshape(-1, *shape[-2:]).double())
+        assert sv.min().item() > 0.3 and sv.max().item() < 1.6
