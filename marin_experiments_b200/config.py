@@ -236,6 +236,9 @@ class TrainerConfig:
     profiler_start_step: int = 5
     profiler_num_steps: int = 5
     watchdog_timeout_s: float = 0.0
+    watch_every: int = 0  # gradient / parameter norms every N steps (0: off)
+    watch_per_param: bool = False
+    watch_hist_bins: int = 0
 
 
 @dataclass(frozen=True)

@@ -14,6 +14,7 @@ import torch
 
 from ..config import GrugRunConfig, to_dict
 from ..data.loader import DataLoader, build_dataset
+from ..utils.profiling import ProfilerHook
 from ..utils.tracker import ThroughputHook, Watchdog, make_tracker
 from .checkpoint import Checkpointer, initialize_from, restore_from_checkpoint
 from .curriculum import KCurriculumHook
@@ -91,13 +92,20 @@ def run_grug(cfg: GrugRunConfig, *, tracker: str = "jsonl", hooks=(), eval_only:
     loader = DataLoader(ds, tcfg.train_batch_size, rank=rank, world=world, start_step=trainer.step)
     thr = ThroughputHook(cfg.model, world, peak_flops_per_gpu, every=cfg.trainer.log_every)
     wd = Watchdog(tcfg.watchdog_timeout_s).start()
+    trainer.watch_every, trainer.watch_per_param = tcfg.watch_every, tcfg.watch_per_param
+    trainer.watch_hist_bins = tcfg.watch_hist_bins
     all_hooks = [thr, wd, *hooks]
+    pre = [KCurriculumHook(cfg.k_schedule)] if cfg.k_schedule else []
+    if tcfg.profiler:
+        prof = ProfilerHook(os.path.join(cfg.output_path, tcfg.log_dir, run_id, "profiler"), tcfg.profiler_start_step,
+                            tcfg.profiler_num_steps, rank)
+        pre.append(prof)
+        all_hooks.append(prof)
     if ev is not None and ev.steps_per_eval:
         def eval_hook(tr, info):
             if info["step"] % ev.steps_per_eval == 0:
                 info["eval"] = run_eval(info["step"])
         all_hooks.append(eval_hook)
-    pre = [KCurriculumHook(cfg.k_schedule)] if cfg.k_schedule else []
     try:
         last = trainer.fit(loader, tcfg.num_train_steps, hooks=all_hooks, pre_hooks=pre,
                            log_every=cfg.trainer.log_every, tracker=trk, checkpointer=ckpt)

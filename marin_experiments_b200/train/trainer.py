@@ -26,6 +26,7 @@ import torch
 
 from ..config import GrugModelConfig, GrugRunConfig
 from ..models.grug import MoEMLP, Transformer, apply_qb_betas, default_loss_weight, init_store_weights
+from ..utils.profiling import nvtx_range, watch_stats
 from .params import ParamStore
 
 
@@ -85,6 +86,7 @@ class Trainer:
         n_moe = num_moe_layers(model)
         self.pending_qb = torch.zeros(max(n_moe, 1), max(cfg.num_experts, 1), device=self.device) if n_moe else None
         self.ema = self.store.master.clone() if self.ema_beta is not None else None
+        self.watch_every, self.watch_per_param, self.watch_hist_bins = 0, False, 0  # set by run_grug
 
     @property
     def dp_group(self):
@@ -124,10 +126,11 @@ class Trainer:
         for i in range(n_micro):
             sl = slice(i * mb, (i + 1) * mb)
             w = lw[sl] if lw is not None else default_loss_weight(mb, s, self.device)
-            loss, met = self.model.next_token_loss(tokens[sl], w, None if seg is None else seg[sl],
-                                                   z_loss_weight=self.z_loss_weight, dp_group=self.dp_group,
-                                                   **extra)
-            (loss / n_micro).backward()
+            with nvtx_range(f"microbatch{i}"):
+                loss, met = self.model.next_token_loss(tokens[sl], w, None if seg is None else seg[sl],
+                                                       z_loss_weight=self.z_loss_weight, dp_group=self.dp_group,
+                                                       **extra)
+                (loss / n_micro).backward()
             loss_sum = loss_sum + loss.detach()
             if "qb_beta_per_layer" in met:
                 beta_sum = met["qb_beta_per_layer"] if beta_sum is None else beta_sum + met["qb_beta_per_layer"]
@@ -141,8 +144,13 @@ class Trainer:
         if use_pred:
             self.opt.restore_weights()
         if self.dist is not None:
-            self.dist.grad_sync(self)
-        self.opt.step()
+            with nvtx_range("grad_sync"):
+                self.dist.grad_sync(self)
+        if self.watch_every and self.step % self.watch_every == 0:
+            metrics.update(watch_stats(self.store, per_param=self.watch_per_param, hist_bins=self.watch_hist_bins,
+                                       ep_group=getattr(self.dist, "ep_group", None) if self.dist else None))
+        with nvtx_range("optimizer"):
+            self.opt.step()
         if self.dist is not None and hasattr(self.dist, "post_step"):
             self.dist.post_step(self)
         if beta_sum is not None:
