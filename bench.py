@@ -118,12 +118,6 @@ def reference_arm(args):
     msg = {"impl": "reference", "unavailable": "reference is a JAX/XLA program (jax, marin-levanter, flash-attn-4); "
                                                "jax is not installed in this offline image and baseline/_ref has no "
                                                "runnable JAX stack"}
-    try:
-        import jax  # noqa: F401
-    except Exception:
-        if int(os.environ.get("RANK", "0")) == 0:
-            print(json.dumps(msg), flush=True)
-        return 0
     if int(os.environ.get("RANK", "0")) == 0:
         print(json.dumps(msg), flush=True)
     return 0
