@@ -355,10 +355,12 @@ def combine_losses(cfg: GrugModelConfig, ce: torch.Tensor, stats: list[RouterSta
         if cfg.aux_loss_coef:
             aux = aux + cfg.aux_loss_coef * lbl.mean()
         loss = ce + aux
+        ent = torch.stack([s.entropy for s in stats]).detach()
         metrics.update({
             "train/router/router_z_loss": zl.detach().mean(),
             "train/router/load_balancing_loss": lbl.detach().mean(),
-            "train/router/routing_entropy_mean": torch.stack([s.entropy for s in stats]).detach().mean(),
+            "train/router/routing_entropy_mean": ent.mean(),
+            "routing_entropy_per_layer": ent,
             "train/router/sparsity/realized_active_frac": torch.stack([s.realized_active_frac for s in stats]).detach().mean(),
             "train/router/sparsity/expected_active_frac": torch.stack([s.expected_active_frac for s in stats]).detach().mean(),
             "train/router/sparsity/threshold_mean": torch.stack([s.threshold for s in stats]).detach().float().mean(),

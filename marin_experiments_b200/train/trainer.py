@@ -186,8 +186,11 @@ class Trainer:
             for h in hooks:
                 h(self, info)
             if tracker is not None and self.step % log_every == 0:
-                tracker.log({k: (float(v.float().mean()) if torch.is_tensor(v) else v) for k, v in met.items()
-                             if not (torch.is_tensor(v) and v.numel() > 1)}, step=self.step)
+                from ..utils.tracker import router_layer_metrics
+
+                tracker.log({**{k: (float(v.float().mean()) if torch.is_tensor(v) else v) for k, v in met.items()
+                                if not (torch.is_tensor(v) and v.numel() > 1)}, **router_layer_metrics(met)},
+                            step=self.step)
             if checkpointer is not None:
                 checkpointer.on_step(self, self.step)
             last = info

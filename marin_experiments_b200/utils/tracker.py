@@ -115,6 +115,36 @@ def parse_thruput(text: str, warmup: int = 5) -> dict | None:
     return {"tok_s": statistics.median(tps), "mfu": statistics.median(mfus) if mfus else None, "n": len(tps)}
 
 
+MAX_HIST_BUCKETS = 256
+
+
+def coarsen_counts(counts, max_buckets: int = MAX_HIST_BUCKETS) -> list[float]:
+    """Per-expert routing counts as a histogram of at most ``max_buckets`` buckets: adjacent experts
+    are summed in equal groups (the last group zero-padded), so a log entry stays bounded for large
+    expert pools (megagpt-speedrun/model.py:431-466)."""
+    c = [float(x) for x in (counts.tolist() if hasattr(counts, "tolist") else counts)]
+    if len(c) <= max_buckets:
+        return c
+    group = -(-len(c) // max_buckets)
+    c += [0.0] * (-len(c) % group)
+    return [sum(c[i:i + group]) for i in range(0, len(c), group)]
+
+
+def router_layer_metrics(metrics: dict) -> dict:
+    """Per-layer router entries for the tracker from the per-layer tensors of a step's metrics:
+    ``train/router/layer_<i>/routing_entropy`` and ``train/router/layer_<i>/routing_hist``."""
+    out = {}
+    ent = metrics.get("routing_entropy_per_layer")
+    if ent is not None:
+        for i, v in enumerate(ent.float().tolist()):
+            out[f"train/router/layer_{i}/routing_entropy"] = v
+    cnt = metrics.get("routing_counts_per_layer")
+    if cnt is not None:
+        for i, row in enumerate(cnt.float().cpu()):
+            out[f"train/router/layer_{i}/routing_hist"] = coarsen_counts(row)
+    return out
+
+
 class Watchdog:
     def __init__(self, timeout_s: float, on_timeout=None, poll_s: float | None = None, stream=None):
         self.timeout_s = timeout_s

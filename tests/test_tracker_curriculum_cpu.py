@@ -61,3 +61,20 @@ def test_curriculum_schedule_and_swap():
     tok = torch.randint(0, 512, (2, 64))
     loss, met = m.next_token_loss(tok)
     assert torch.isfinite(loss)
+
+
+def test_router_histogram_coarsening_and_layer_metrics():
+    import torch
+
+    from marin_experiments_b200.utils.tracker import coarsen_counts, router_layer_metrics
+
+    assert coarsen_counts([1, 2, 3]) == [1.0, 2.0, 3.0]
+    big = torch.arange(1024, dtype=torch.float32)
+    h = coarsen_counts(big)
+    assert len(h) == 256 and h[0] == 0 + 1 + 2 + 3 and sum(h) == float(big.sum())
+    odd = coarsen_counts(list(range(600)), max_buckets=256)  # groups of 3, last padded
+    assert len(odd) == 200 and sum(odd) == sum(range(600))
+    m = router_layer_metrics({"routing_entropy_per_layer": torch.tensor([1.5, 2.0]),
+                              "routing_counts_per_layer": torch.tensor([[3, 1], [2, 2]])})
+    assert m["train/router/layer_1/routing_entropy"] == 2.0
+    assert m["train/router/layer_0/routing_hist"] == [3.0, 1.0]
