@@ -267,6 +267,9 @@ def main(argv=None):
         if rank == 0:
             with open(f"{args.profile_trace}.md", "w") as f:
                 f.write(breakdown_table(b) + "\n")
+    peak = torch.tensor([torch.cuda.max_memory_allocated() / 1e9], device=trainer.device)  # allocator high-water
+    if ctx is not None:
+        torch.distributed.all_reduce(peak, op=torch.distributed.ReduceOp.MAX)
     check_kernel_errors()
     out = {
         "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -277,7 +280,7 @@ def main(argv=None):
                    "micro_batch": args.micro_batch, "capacity_factor": cfg.capacity_factor,
                    "parallelism": f"ep{world}" if world > 1 else "single", "l2": "working set >> L2 (no flush needed)",
                    "layers": cfg.num_layers},
-        "mfu": mfu, "exposed_all_to_all_ms_per_step": exposed, "flops_per_token": fpt, "loss": loss,
+        "mfu": mfu, "exposed_all_to_all_ms_per_step": exposed, "peak_memory_gb": float(peak.item()), "flops_per_token": fpt, "loss": loss,
         "clocks": clk, "gpu_launches": int(launches),
         "e2e": e2e,
     }
