@@ -148,6 +148,11 @@ def make_step(env=None) -> ExecutorStep:
 
 
 def main(argv=None):
+    if os.environ.get("SP_DIAG"):  # diagnostic side entries (ragged / ring / fit / attn)
+        from ..benchmarks import diag
+
+        diag.main(os.environ["SP_DIAG"])
+        return None
     mode = os.environ.get("SP_PP_MODE", "")
     if mode in ("async", "sync"):
         from ..parallel import pipeline_entry

@@ -66,3 +66,15 @@ def test_run_timeout_kills_only_the_job(tmp_path):
     logs = sweeps.run(jobs, str(tmp_path), timeout_s=2)
     text = open(logs[0]).read()
     assert "killed after 2s" in text and "exit timeout" in text
+
+
+def test_diag_side_entries_dispatch(monkeypatch):
+    from marin_experiments_b200.benchmarks import diag
+
+    called = []
+    monkeypatch.setitem(diag.MODES, "fit", lambda: called.append("fit"))
+    monkeypatch.setenv("SP_DIAG", "fit")
+    assert megagpt.main([]) is None and called == ["fit"]
+    with pytest.raises(SystemExit):
+        diag.main("bogus")
+    assert set(diag.MODES) == {"ragged", "ring", "fit", "attn"}
