@@ -80,3 +80,17 @@ def test_flop_accounting():
     assert f["gated_norms"] == 2 * 2 * (2 * 2 * 256 * 128) + 2 * (2 * 2 * 256 * 128)
     assert compute_flops_per_token(c) == lm_flops_per_token(c) - 2 * 256 * 1000
     assert training_flops_per_token(c, causal=False) == 3 * f["_total"]
+
+
+@pytest.mark.parametrize("module", ["marin_experiments_b200.experiments.megagpt",
+                                    "marin_experiments_b200.experiments.tiny_stories"])
+def test_launcher_dry_run_in_fresh_process(module, tmp_path):
+    """Every experiment launcher imports and builds its steps with --dry_run (no jobs run)."""
+    import subprocess
+    import sys
+
+    env = {**os.environ, "MARIN_PREFIX": str(tmp_path), "PYTHONPATH": os.getcwd()}
+    r = subprocess.run([sys.executable, "-m", module, "--dry_run"], env=env, capture_output=True, text=True,
+                       timeout=300, cwd=str(tmp_path))
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "[dry-run]" in r.stdout
