@@ -74,5 +74,7 @@ class GRPOLearner:
             loss.backward()
             gn = torch.nn.utils.clip_grad_norm_(self.model.parameters(), c.max_grad_norm)
             self.opt.step()
+        if hasattr(self.env, "on_step"):  # curriculum sources advance their schedule per update
+            self.env.on_step()
         return {"loss": float(loss), "reward_mean": float(rw.mean()), "grad_norm": float(gn),
                 "clip_frac": float(met["clip_frac"])}
