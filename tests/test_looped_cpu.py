@@ -74,3 +74,33 @@ def test_trainer_with_looped_model():
     losses = [float(tr.train_step({"tokens": TOK})["train/loss"]) for _ in range(4)]
     assert all(l == l for l in losses)
     assert float(tr.store.master_view(tr.store.by_name["film_scale"]).abs().sum()) > 0
+
+
+def test_depth_sweep_and_tagged_eval():
+    from marin_experiments_b200.config import GrugRunConfig, GrugTrainerConfig, TrainerConfig
+    from marin_experiments_b200.optim import GrugMoeAdamHConfig
+    from marin_experiments_b200.train.eval import evaluate, evaluate_at_depths, evaluate_tagged
+    from marin_experiments_b200.train.trainer import Trainer
+
+    lc = LoopedConfig(model=M, num_prelude_layers=1, num_coda_layers=1, recurrence_steps=2, iteration_film=True,
+                      randomize_recurrence=True, recurrence_choices=(1, 2, 3))
+    run = GrugRunConfig(model=M, optimizer=GrugMoeAdamHConfig(warmup=0.0),
+                        trainer=GrugTrainerConfig(trainer=TrainerConfig(num_train_steps=5)))
+    tr = Trainer(run, device="cpu", model_factory=lambda cfg, local: LoopedTransformer(lc))
+    for _ in range(2):
+        tr.train_step({"tokens": TOK})
+    g = torch.Generator().manual_seed(5)
+    web = [{"tokens": torch.randint(0, 256, (2, 32), generator=g)} for _ in range(2)]
+    code = [{"tokens": torch.randint(0, 256, (2, 32), generator=g)}]
+    res = evaluate_at_depths(tr, web, (1, 2, 3))
+    assert set(res) == {1, 2, 3} and "eval/R2/loss" in res[2]
+    assert res[1]["eval/R1/loss"] != res[3]["eval/R3/loss"]  # the loop count changes the function
+    with torch.no_grad():
+        direct = evaluate(tr, web, model_kwargs={"recurrence": 3})["eval/loss"]
+    assert abs(direct - res[3]["eval/R3/loss"]) < 1e-6
+    tagged = evaluate_at_depths(tr, {"web": web, "code": code}, (2,))[2]
+    lw, lc_ = tagged["eval/R2/web/loss"], tagged["eval/R2/code/loss"]
+    assert abs(tagged["eval/R2/macro_loss"] - (lw + lc_) / 2) < 1e-9
+    assert abs(tagged["eval/R2/micro_loss"] - (2 * lw + lc_) / 3) < 1e-9
+    plain = evaluate_tagged(tr, {"web": web}, prefix="x")
+    assert set(plain) == {"x/web/loss", "x/macro_loss", "x/micro_loss"}
