@@ -83,7 +83,8 @@ def test_flop_accounting():
 
 
 @pytest.mark.parametrize("module", ["marin_experiments_b200.experiments.megagpt",
-                                    "marin_experiments_b200.experiments.tiny_stories"])
+                                    "marin_experiments_b200.experiments.tiny_stories",
+                                    "marin_experiments_b200.experiments.delayed_gradient"])
 def test_launcher_dry_run_in_fresh_process(module, tmp_path):
     """Every experiment launcher imports and builds its steps with --dry_run (no jobs run)."""
     import subprocess
@@ -94,3 +95,23 @@ def test_launcher_dry_run_in_fresh_process(module, tmp_path):
                        timeout=300, cwd=str(tmp_path))
     assert r.returncode == 0, r.stderr[-2000:]
     assert "[dry-run]" in r.stdout
+
+
+def test_delayed_gradient_arms():
+    from marin_experiments_b200.experiments import delayed_gradient as dg
+    from marin_experiments_b200.optim.delayed import DelayedGrugMoeAdamHConfig, DelayedGrugMuonConfig
+
+    launch, arm = dg.make_launch({"GRUG_OPT": "muon", "GRUG_TAU": "8", "GRUG_CORRECTOR": "dc_asgd_ema",
+                                  "GRUG_STEPS": "50", "GRUG_SEQ": "1024"})
+    opt = launch.optimizer.value if hasattr(launch.optimizer, "value") else launch.optimizer
+    assert isinstance(opt, DelayedGrugMuonConfig) and opt.tau == 8 and opt.corrector == "dc_asgd_ema"
+    assert opt.learning_rate == 0.02 and "tau8" in launch.run_id and "corrector=dc_asgd_ema" in arm
+    launch2, _ = dg.make_launch({"GRUG_OPT": "adamh", "GRUG_STAGES": "4", "GRUG_TAU": "8", "GRUG_HIDDEN": "768"})
+    opt2 = launch2.optimizer.value if hasattr(launch2.optimizer, "value") else launch2.optimizer
+    model = launch2.model.value if hasattr(launch2.model, "value") else launch2.model
+    assert isinstance(opt2, DelayedGrugMoeAdamHConfig) and opt2.tau == 0 and opt2.num_stages == 4
+    assert opt2.num_layers == model.num_layers and model.hidden_dim == 768 and "S4" in launch2.run_id
+    with pytest.raises(ValueError):
+        dg.make_launch({"GRUG_OPT": "sgd"})
+    with pytest.raises(ValueError):
+        dg.make_launch({"GRUG_CORRECTOR": "magic"})
