@@ -4,14 +4,18 @@
 Environment: ``SP_PP`` (stages, default world size / ``SP_PP_EP``), ``SP_PP_EP`` (expert-parallel ranks
 per stage, default 1), ``SP_PP_SCHEDULE`` (``gpipe`` | ``1f1b`` | ``zb``, sync only), ``SP_MICRO``
 (microbatches per step, default 16), ``SP_MB`` (sequences per microbatch, default 8), ``SP_SEQ``,
-``SP_STEPS``, ``SP_WARMUP_STEPS``, ``SP_LAYERS`` (default 24), ``SP_HIDDEN`` etc. via the megagpt
-config (d_model 1536, 16 heads, 64 experts top-4 of width 768 + shared 3072), ``SP_DELAY_TAU`` (sync:
+``SP_STEPS``, ``SP_WARMUP_STEPS``, ``SP_LAYERS`` (default 24), ``SP_HIDDEN`` (heads follow at head dim
+96), ``SP_EXPERTS``, ``SP_TOPK``, ``SP_VOCAB`` over the megagpt config (d_model 1536, 16 heads, 64
+experts top-4 of width 768 + shared 3072; the ``MOE_PP_*`` names of the pipeline benchmark are
+accepted as aliases: STAGE, EP, NMICRO, MICROBATCH, SEQ, LAYERS, HIDDEN, EXPERTS, EPT, VOCAB),
+``SP_DELAY_TAU`` (sync:
 0; async: the delayed-gradient optimizer with per-stage staleness). Each measured step prints
 ``[PP_THRUPUT] step=N dt=...s tok_s=... bubble_model=...`` on the last stage.
 """
 
 from __future__ import annotations
 
+import dataclasses
 import datetime
 import os
 import time
@@ -23,8 +27,14 @@ from ..config import GrugModelConfig, GrugRunConfig, GrugTrainerConfig, TrainerC
 from .pipeline import PipelineTrainer, async_stage_delay, bubble_fraction, init_topology
 
 
+# The pipeline benchmark's names (grug-moe-pp/benchmark.py:369-389) are accepted as aliases.
+_ALIASES = {"SP_PP": "MOE_PP_STAGE", "SP_PP_EP": "MOE_PP_EP", "SP_MICRO": "MOE_PP_NMICRO", "SP_MB": "MOE_PP_MICROBATCH",
+            "SP_SEQ": "MOE_PP_SEQ", "SP_LAYERS": "MOE_PP_LAYERS", "SP_HIDDEN": "MOE_PP_HIDDEN",
+            "SP_EXPERTS": "MOE_PP_EXPERTS", "SP_TOPK": "MOE_PP_EPT", "SP_VOCAB": "MOE_PP_VOCAB"}
+
+
 def _env(k, d):
-    v = os.environ.get(k, "")
+    v = os.environ.get(k, "") or os.environ.get(_ALIASES.get(k, ""), "")
     return v if v else d
 
 
@@ -50,6 +60,13 @@ def _config(delayed: bool, pp: int, stage: int):
     from ..optim.delayed import DelayedGrugMoeAdamHConfig
 
     model = megagpt_model(int(_env("SP_LAYERS", "24")), int(_env("SP_SEQ", "2048")))
+    hidden = int(_env("SP_HIDDEN", str(model.hidden_dim)))
+    if hidden != model.hidden_dim:  # keep the head dim (96): heads follow the width
+        model = dataclasses.replace(model, hidden_dim=hidden, num_heads=max(1, hidden // 96),
+                                    num_kv_heads=max(1, hidden // 96))
+    model = dataclasses.replace(model, num_experts=int(_env("SP_EXPERTS", str(model.num_experts))),
+                                num_experts_per_token=int(_env("SP_TOPK", str(model.num_experts_per_token))),
+                                vocab_size=int(_env("SP_VOCAB", str(model.vocab_size))))
     if delayed:
         opt = DelayedGrugMoeAdamHConfig(tau=int(_env("SP_DELAY_TAU", str(async_stage_delay(pp, stage)))),
                                         corrector=_env("SP_DELAY_CORRECTOR", "none"), warmup=0.0)

@@ -115,3 +115,23 @@ def test_async_no_flush():
     last = [v for v in res.values() if v["stage"] == 1][0]
     assert len(last["losses"]) == 6 and all(l == l for l in last["losses"])
     assert all(v["steps"] == 6 for v in res.values())
+
+
+def test_pipeline_entry_env_aliases(monkeypatch):
+    from marin_experiments_b200.parallel import pipeline_entry as pe
+
+    for k in list(pe._ALIASES) + list(pe._ALIASES.values()):
+        monkeypatch.delenv(k, raising=False)
+    base = pe._config(False, 2, 0).model
+    assert base.hidden_dim == 1536 and base.num_experts == 64
+    monkeypatch.setenv("MOE_PP_HIDDEN", "768")
+    monkeypatch.setenv("MOE_PP_EXPERTS", "16")
+    monkeypatch.setenv("MOE_PP_EPT", "2")
+    monkeypatch.setenv("MOE_PP_LAYERS", "4")
+    monkeypatch.setenv("SP_SEQ", "512")  # the SP_* name wins over its alias
+    monkeypatch.setenv("MOE_PP_SEQ", "64")
+    m = pe._config(True, 2, 0).model
+    assert (m.hidden_dim, m.num_heads, m.num_experts, m.num_experts_per_token, m.num_layers, m.max_seq_len) == \
+        (768, 8, 16, 2, 4, 512)
+    monkeypatch.setenv("MOE_PP_STAGE", "4")
+    assert pe._env("SP_PP", "1") == "4"
