@@ -28,10 +28,12 @@ _CHUNK_DTYPE = np.dtype([("start", "<i8"), ("len", "<i4"), ("mat", "<i4"), ("gro
 def _ns_quintic(g: torch.Tensor, steps: int) -> torch.Tensor:
     """Newton-Schulz orthogonalisation with the quintic iteration of Muon
     (a, b, c) = (3.4445, -4.7750, 2.0315) (Jordan et al., "Muon", 2024); the iteration of
-    megagpt-speedrun/async_pipeline.py:379-388. On CUDA, matrices whose sides are multiples of 64 run
-    the iterations in bf16 on the tcgen05 GEMM (``_ns_quintic_sm100``); the rest (and
-    ``MXK_NS_FP32=1``) run them in fp32."""
-    if (g.is_cuda and g.shape[-2] % 64 == 0 and g.shape[-1] % 64 == 0
+    megagpt-speedrun/async_pipeline.py:379-388. On CUDA, a single matrix whose sides are multiples of
+    64 runs the iterations in bf16 on the tcgen05 GEMM (``_ns_quintic_sm100``); stacks of matrices
+    (the per-expert weights) run as batched fp32 products, one launch per product for the whole
+    stack, as does everything with ``MXK_NS_FP32=1``."""
+    single = g.dim() == 2 or math.prod(g.shape[:-2]) == 1
+    if (g.is_cuda and single and g.shape[-2] % 64 == 0 and g.shape[-1] % 64 == 0
             and os.environ.get("MXK_NS_FP32", "0") != "1"):
         return _ns_quintic_sm100(g, steps)
     a, b, c = 3.4445, -4.7750, 2.0315
