@@ -5,7 +5,8 @@ The reference does this with separate scripts against its cluster and W&B
 megagpt-speedrun/iso_step.py:33-95, megagpt-speedrun/analyze_profile.py:63-157). Here the inputs are
 local files written by this framework:
 
-* **sweep logs** (``analyze_logs``): one stdout log per run. The ``[arm]`` line (printed by the
+* **sweep logs** (``analyze_logs``): one stdout log per run (the CLI's ``--watch N`` re-reads them
+  every N seconds while runs are going, with glob patterns picking up new logs). The ``[arm]`` line (printed by the
   megagpt launcher) gives the geometry, the ``[THRUPUT]`` lines give per-step tokens/s and MFU (the
   median over steps >= warm-up is the run's number), and the first failure signature (out of
   memory, NCCL error, watchdog, NaN stop, segfault, CUDA fault) marks runs that died.
@@ -299,6 +300,8 @@ def main(argv=None):
     s = sub.add_parser("sweep", help="tokens/s table from run stdout logs")
     s.add_argument("logs", nargs="+")
     s.add_argument("--warmup", type=int, default=8)
+    s.add_argument("--watch", type=float, default=0.0, help="re-read the logs every N seconds (0: once)")
+    s.add_argument("--rounds", type=int, default=0, help="with --watch: stop after this many tables (0: never)")
     c = sub.add_parser("results", help="final tracker values per run")
     c.add_argument("log_dir")
     c.add_argument("--match", default=None)
@@ -314,7 +317,17 @@ def main(argv=None):
     p.add_argument("--top", type=int, default=15)
     a = ap.parse_args(argv)
     if a.cmd == "sweep":
-        print(sweep_table(analyze_logs(a.logs, a.warmup)))
+        import glob
+        import time
+
+        n = 0
+        while True:
+            paths = sorted({p for pat in a.logs for p in (glob.glob(pat) or [pat]) if os.path.exists(p)})
+            print(sweep_table(analyze_logs(paths, a.warmup)), flush=True)
+            n += 1
+            if a.watch <= 0 or (a.rounds and n >= a.rounds):
+                break
+            time.sleep(a.watch)
     elif a.cmd in ("results", "iso-step"):
         keys = a.keys.split(",")
         dirs = run_dirs(a.log_dir, a.match)

@@ -85,3 +85,10 @@ def test_profile_call_cpu(tmp_path):
     x = torch.randn(64, 64)
     b = an.profile_call(lambda: x @ x, steps=2, trace_path=str(tmp_path / "p.json"))
     assert os.path.exists(tmp_path / "p.json") and b["total_ms_per_step"] >= 0.0
+
+
+def test_sweep_cli_watch_and_glob(tmp_path, capsys):
+    (tmp_path / "r1.log").write_text(ARM + _thru(range(10), 1000))
+    an.main(["sweep", str(tmp_path / "*.log"), "--warmup", "8", "--watch", "0.01", "--rounds", "2"])
+    out = capsys.readouterr().out
+    assert out.count("| run |") == 2 and "sw-d1536-e64-k4" in out
