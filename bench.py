@@ -12,7 +12,12 @@ working set (12.8 GB of bf16 weights alone) is far larger than the 126 MB L2, so
 needed between steps. The end-to-end figure repeats K steps through ``Trainer.train_step`` with
 every step's tokens copied from pinned host memory and the loss read back to the host.
 
-Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--config megagpt|grug_dp|adaptive]
+
+``--config grug_dp`` (12 layers, d768, 8 experts top-2, seq 1024, 256 sequences per step in total,
+pure data parallel) and ``--config adaptive`` (16 layers, d1024, 32 experts with a per-token top-k in
+1..8, seq 2048, 256K tokens per step in total, EP = N) are the smaller configurations; their
+global batch is fixed, so they scale strongly. The default is the headline configuration above.
 """
 
 from __future__ import annotations
@@ -39,6 +44,34 @@ def megagpt_config():
         num_experts=64, num_experts_per_token=4, num_layers=24, num_heads=16, num_kv_heads=16, head_dim=96,
         max_seq_len=2048, sliding_window=4096, capacity_factor=1.25, router_z_loss_coef=0.001,
     )
+
+
+# (model config factory, sequences per GPU given the world size, parallelism, scaling, label, default
+# microbatch given the world size); "megagpt" is the headline and the default.
+def bench_config(name: str, world: int) -> dict:
+    from marin_experiments_b200.config import GrugModelConfig
+
+    if name == "megagpt":
+        return {"model": megagpt_config(), "seqs_per_gpu": 32, "parallel": "ep", "scaling": "weak",
+                "label": "megagpt-speedrun MoE: 24L d1536 16h(hd96) E64 top4 d_ff768 + shared 3072, vocab 128256",
+                "micro_batch": 8 if world == 1 else 16, "baseline": BASELINE_TOK_S}
+    if name == "grug_dp":  # 256 sequences of 1024 per step in total, experts replicated (pure data parallel)
+        cfg = GrugModelConfig(vocab_size=128256, hidden_dim=768, intermediate_dim=2048, shared_expert_intermediate_dim=0,
+                              num_experts=8, num_experts_per_token=2, num_layers=12, num_heads=12, num_kv_heads=12,
+                              head_dim=64, max_seq_len=1024, sliding_window=1024, capacity_factor=1.25,
+                              aux_loss_coef=0.01, initializer_std=0.02)
+        return {"model": cfg, "seqs_per_gpu": max(1, 256 // world), "parallel": "dp", "scaling": "strong",
+                "label": "grug MoE: 12L d768 12h(hd64) E8 top2 d_ff2048, vocab 128256, aux LBL 0.01",
+                "micro_batch": 32, "baseline": None}
+    if name == "adaptive":  # 256K tokens per step in total, per-token top-k in 1..8 by router-score threshold
+        cfg = GrugModelConfig(vocab_size=128256, hidden_dim=1024, intermediate_dim=512, shared_expert_intermediate_dim=1024,
+                              num_experts=32, num_experts_per_token=8, adaptive_routing=True, min_experts_per_token=1,
+                              num_layers=16, num_heads=8, num_kv_heads=8, head_dim=128, max_seq_len=2048,
+                              sliding_window=2048, capacity_factor=1.25)
+        return {"model": cfg, "seqs_per_gpu": max(1, 128 // world), "parallel": "ep", "scaling": "strong",
+                "label": "adaptive-sparsity MoE: 16L d1024 8h(hd128) E32 top-k 1..8 d_ff512 + shared 1024, vocab 128256",
+                "micro_batch": 16, "baseline": None}
+    raise ValueError(f"unknown --config {name!r}")
 
 
 def flops_per_token(cfg) -> float:
@@ -129,7 +162,10 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
-    ap.add_argument("--seqs-per-gpu", type=int, default=32)
+    ap.add_argument("--config", default="megagpt", choices=["megagpt", "grug_dp", "adaptive"],
+                    help="megagpt (headline, weak scaling with EP = N); grug_dp and adaptive: the smaller "
+                         "configurations, fixed global batch")
+    ap.add_argument("--seqs-per-gpu", type=int, default=None)
     ap.add_argument("--micro-batch", type=int, default=None,
                     help="sequences per microbatch (gradient accumulation); default 8 on one GPU, where "
                          "~6B parameters with fp32 master, grads and moments leave room for 8 x 2048 tokens of "
@@ -151,12 +187,16 @@ def main(argv=None):
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    bc = bench_config(args.config, world)
     if args.micro_batch is None:
-        args.micro_batch = 8 if world == 1 else 16
+        args.micro_batch = bc["micro_batch"]
+    if args.seqs_per_gpu is None:
+        args.seqs_per_gpu = bc["seqs_per_gpu"]
+    args.micro_batch = min(args.micro_batch, args.seqs_per_gpu)
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local_rank)
-    ctx = pdist.init(ep_size=world) if world > 1 else None
-    cfg = megagpt_config()
+    ctx = pdist.init(ep_size=world if bc["parallel"] == "ep" else 1) if world > 1 else None
+    cfg = bc["model"]
     if args.layers is not None:
         import dataclasses
 
@@ -164,7 +204,7 @@ def main(argv=None):
     run = GrugRunConfig(model=cfg, optimizer=GrugMoeAdamHConfig(learning_rate=0.01, adam_lr=6e-4, warmup=0.0),
                         trainer=GrugTrainerConfig(trainer=TrainerConfig(seed=0, num_train_steps=1000)))
     trainer = Trainer(run, device=f"cuda:{local_rank}", micro_batch=args.micro_batch, dist=ctx)
-    if world > 1 and args.micro_batch > 8:
+    if args.config == "megagpt" and world > 1 and args.micro_batch > 8:
         # Guard for the default: one 2048-token sequence of this model keeps ~4.6 GB of activations and
         # exchange buffers (measured on one GPU: 36 GB per 8 sequences). Fall back to 8-sequence
         # microbatches on every rank if any rank lacks the room (same decision everywhere).
@@ -273,12 +313,12 @@ def main(argv=None):
     check_kernel_errors()
     out = {
         "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": tok_s / BASELINE_TOK_S, "dtype": "bf16", "data": "synthetic (uniform random ids, seed 2; random init)",
-        "config": {"model": "megagpt-speedrun MoE: 24L d1536 16h(hd96) E64 top4 d_ff768 + shared 3072, vocab 128256",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": bc["scaling"],
+        "vs_baseline": tok_s / bc["baseline"] if bc["baseline"] else None, "dtype": "bf16", "data": "synthetic (uniform random ids, seed 2; random init)",
+        "config": {"model": bc["label"], "name": args.config,
                    "global_batch": seqs * world, "seq_len": seq, "tokens_per_step": tokens_step,
                    "micro_batch": args.micro_batch, "capacity_factor": cfg.capacity_factor,
-                   "parallelism": f"ep{world}" if world > 1 else "single", "l2": "working set >> L2 (no flush needed)",
+                   "parallelism": f"{bc['parallel']}{world}" if world > 1 else "single", "l2": "working set >> L2 (no flush needed)",
                    "layers": cfg.num_layers},
         "mfu": mfu, "exposed_all_to_all_ms_per_step": exposed, "peak_memory_gb": float(peak.item()), "flops_per_token": fpt, "loss": loss,
         "clocks": clk, "gpu_launches": int(launches),

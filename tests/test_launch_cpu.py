@@ -115,3 +115,32 @@ def test_delayed_gradient_arms():
         dg.make_launch({"GRUG_OPT": "sgd"})
     with pytest.raises(ValueError):
         dg.make_launch({"GRUG_CORRECTOR": "magic"})
+
+
+@pytest.mark.parametrize("name", ["grug_dp", "adaptive"])
+def test_bench_configs_build_and_train(name):
+    """The benchmark's smaller configurations are valid models: one training step of a scaled-down copy
+    (1 layer, seq 64, vocab 1024) on CPU."""
+    import dataclasses
+    import sys
+
+    import torch
+
+    sys.path.insert(0, os.getcwd())
+    import bench
+
+    from marin_experiments_b200.config import GrugRunConfig, GrugTrainerConfig, TrainerConfig
+    from marin_experiments_b200.optim import GrugMoeAdamHConfig
+    from marin_experiments_b200.train.trainer import Trainer
+
+    bc = bench.bench_config(name, 8)
+    assert bc["scaling"] == "strong" and bc["baseline"] is None
+    assert bc["seqs_per_gpu"] * 8 * bc["model"].max_seq_len in (256 * 1024, 128 * 2048)
+    cfg = dataclasses.replace(bc["model"], num_layers=1, max_seq_len=64, sliding_window=64, vocab_size=1024)
+    run = GrugRunConfig(model=cfg, optimizer=GrugMoeAdamHConfig(warmup=0.0),
+                        trainer=GrugTrainerConfig(trainer=TrainerConfig(num_train_steps=3)))
+    tr = Trainer(run, device="cpu")
+    tok = torch.randint(0, 1024, (2, 64), generator=torch.Generator().manual_seed(0))
+    met = tr.train_step({"tokens": tok})
+    assert torch.isfinite(met["train/loss"])
+    assert bench.bench_config("megagpt", 1)["micro_batch"] == 8 and bench.bench_config("megagpt", 8)["micro_batch"] == 16
