@@ -63,3 +63,33 @@ def test_nvtx_range_is_a_noop_without_cuda(monkeypatch):
     with nvtx_range("x"):
         y = 1
     assert y == 1
+
+
+def _watch_rank(rank, world):
+    import datetime
+    from types import SimpleNamespace
+
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        # two parameters: a replicated one (same values on every rank) and an expert shard (per rank)
+        grad = torch.tensor([3.0, 4.0] + [float(rank + 1)] * 4)
+        master = torch.ones(6)
+        infos = [SimpleNamespace(name="blocks.0.attn.w_o", offset=0, numel=2, sharded_over=None),
+                 SimpleNamespace(name="blocks.0.mlp.w_down", offset=2, numel=4, sharded_over="expert")]
+        store = SimpleNamespace(infos=infos, grad=grad, master=master)
+        return watch_stats(store, ep_group=dist.group.WORLD)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_watch_stats_sums_expert_shards_over_ranks():
+    from tests.mp_util import run_ranks
+
+    res = run_ranks(_watch_rank, 2)
+    for r in (0, 1):
+        w = res[r]
+        assert math.isclose(w["watch/grad_norm/attn.w_o"], 5.0)  # replicated: not summed
+        assert math.isclose(w["watch/grad_norm/mlp.w_down"], math.sqrt(4 * 1 + 4 * 4))  # both ranks' shards
+        assert math.isclose(w["watch/grad_norm/total"], math.sqrt(25 + 20))
