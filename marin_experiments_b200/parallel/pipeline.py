@@ -6,7 +6,9 @@ the final norm, head and loss) with its routed experts sharded over the stage's 
 also split the batch (megagpt-speedrun/async_pipeline.py:442-662, grug-moe-pp/pipeline_zb.py:465-876).
 Activations go stage to stage with ``isend``/``irecv`` (NCCL P2P over NVLink on GPUs, gloo on CPU);
 forward and backward traffic use two separate process groups, so a stage's forward send and its
-neighbour's backward send never wait behind each other on one communicator.
+neighbour's backward send never wait behind each other on one communicator. ``SP_PP_TRANSPORT=null``
+replaces the transfers with zeros (no traffic), the compute-only measurement of the reference's
+null-transport switch (grug-moe-pp/pipeline_zb.py:115-118).
 
 Modes:
 
@@ -23,6 +25,7 @@ Modes:
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import torch
@@ -121,6 +124,13 @@ class PipelineTrainer:
         self.act_dtype = torch.bfloat16 if self.device.type == "cuda" else torch.float32
         self.step = 0
         self._async_state = None
+        # Stage-boundary transport: "p2p" (isend / irecv, sends complete in the background) or "null"
+        # (nothing is sent, receivers get zeros: a compute-only measurement). A blocking send is not
+        # offered: under 1F1B two neighbours can each block in a send on a different communicator
+        # while the other waits to receive, a cycle.
+        self.transport = os.environ.get("SP_PP_TRANSPORT", "p2p")
+        if self.transport not in ("p2p", "null"):
+            raise ValueError(f"SP_PP_TRANSPORT must be p2p or null, got {self.transport!r}")
 
     # --------------------------------------------------------------------------- helpers
     def _chain_clip(self) -> None:
@@ -137,9 +147,13 @@ class PipelineTrainer:
         opt.norm_hook = hook
 
     def _send(self, t, dst, group, pending):
+        if self.transport == "null":
+            return
         pending.append(tdist.isend(t.contiguous(), dst, group=group))
 
     def _recv(self, shape, src, group):
+        if self.transport == "null":
+            return torch.zeros(shape, dtype=self.act_dtype, device=self.device)
         buf = torch.empty(shape, dtype=self.act_dtype, device=self.device)
         tdist.irecv(buf, src, group=group).wait()
         return buf

@@ -135,3 +135,20 @@ def test_pipeline_entry_env_aliases(monkeypatch):
         (768, 8, 16, 2, 4, 512)
     monkeypatch.setenv("MOE_PP_STAGE", "4")
     assert pe._env("SP_PP", "1") == "4"
+
+
+def _pp_transport_rank(rank, world, transport):
+    import os
+
+    os.environ["SP_PP_TRANSPORT"] = transport
+    return _pp_rank(rank, world, 2, 1, "1f1b")
+
+
+def test_pp_null_transport():
+    """The null transport (zeros at the stage boundary, no traffic) runs the same steps to a finite
+    loss that differs from the real transfer's."""
+    p2p = run_ranks(_pp_rank, 2, 2, 1, "1f1b", timeout=120)
+    null = run_ranks(_pp_transport_rank, 2, "null", timeout=120)
+    last = max(p2p, key=lambda r: p2p[r]["stage"])
+    assert null[last]["loss"] is not None and null[last]["loss"] == null[last]["loss"]
+    assert null[last]["loss"] != p2p[last]["loss"]
