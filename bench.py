@@ -33,7 +33,23 @@ import time
 import torch
 
 BASELINE_TOK_S = 192000.0  # reference 8xH100 anchor (tokens/s, whole job)
+BASELINE_NOTE = ("reference: 192,000 tokens/s for the whole 8xH100 job (24,000 per GPU) on its own anchor "
+                 "config (16 layers, seq 4096, top-8, expert d_ff 512): different hardware and config")
 METRIC = "MoE train tokens/sec/box at 1/2/4/8 B200; MFU; exposed all-to-all ms/step"
+NOMINAL_BF16 = 2.25e15  # dense bf16 tensor peak of one B200 (context only)
+FALLBACK_SUSTAINED_BF16 = 1.4e15  # cuBLAS bf16 under the 1 kW power cap, earlier measurement on this hardware
+
+
+def measured_bf16_peak() -> tuple[float, str]:
+    """Sustained cuBLAS bf16 FLOP/s of one GPU from MEASURED_PEAKS.json beside this file (the
+    roofline denominator for a kernel timed inside a long step), or the fallback figure."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops_sustained"]) * 1e12, "of measured sustained cuBLAS bf16"
+    except (OSError, KeyError, ValueError, TypeError):
+        return FALLBACK_SUSTAINED_BF16, "of fallback sustained cuBLAS bf16 (1.4 PFLOP/s)"
 
 
 def megagpt_config():
@@ -55,12 +71,18 @@ def bench_config(name: str, world: int) -> dict:
         return {"model": megagpt_config(), "seqs_per_gpu": 32, "parallel": "ep", "scaling": "weak",
                 "label": "megagpt-speedrun MoE: 24L d1536 16h(hd96) E64 top4 d_ff768 + shared 3072, vocab 128256",
                 "micro_batch": 8 if world == 1 else 16, "baseline": BASELINE_TOK_S}
+    if name in ("grug_dp", "adaptive"):
+        total = 256 if name == "grug_dp" else 128
+        if total % world:
+            raise ValueError(f"--config {name} keeps {total} sequences per step in total; {world} GPUs do not divide it")
+        if name == "adaptive" and 32 % world:
+            raise ValueError(f"--config adaptive shards 32 experts over the GPUs; {world} GPUs do not divide them")
     if name == "grug_dp":  # 256 sequences of 1024 per step in total, experts replicated (pure data parallel)
         cfg = GrugModelConfig(vocab_size=128256, hidden_dim=768, intermediate_dim=2048, shared_expert_intermediate_dim=0,
                               num_experts=8, num_experts_per_token=2, num_layers=12, num_heads=12, num_kv_heads=12,
                               head_dim=64, max_seq_len=1024, sliding_window=1024, capacity_factor=1.25,
                               aux_loss_coef=0.01, initializer_std=0.02)
-        return {"model": cfg, "seqs_per_gpu": max(1, 256 // world), "parallel": "dp", "scaling": "strong",
+        return {"model": cfg, "seqs_per_gpu": 256 // world, "parallel": "dp", "scaling": "strong",
                 "label": "grug MoE: 12L d768 12h(hd64) E8 top2 d_ff2048, vocab 128256, aux LBL 0.01",
                 "micro_batch": 32, "baseline": None}
     if name == "adaptive":  # 256K tokens per step in total, per-token top-k in 1..8 by router-score threshold
@@ -68,7 +90,7 @@ def bench_config(name: str, world: int) -> dict:
                               num_experts=32, num_experts_per_token=8, adaptive_routing=True, min_experts_per_token=1,
                               num_layers=16, num_heads=8, num_kv_heads=8, head_dim=128, max_seq_len=2048,
                               sliding_window=2048, capacity_factor=1.25)
-        return {"model": cfg, "seqs_per_gpu": max(1, 128 // world), "parallel": "ep", "scaling": "strong",
+        return {"model": cfg, "seqs_per_gpu": 128 // world, "parallel": "ep", "scaling": "strong",
                 "label": "adaptive-sparsity MoE: 16L d1024 8h(hd128) E32 top-k 1..8 d_ff512 + shared 1024, vocab 128256",
                 "micro_batch": 16, "baseline": None}
     raise ValueError(f"unknown --config {name!r}")
@@ -260,13 +282,18 @@ def main(argv=None):
     tokens_step = seqs * seq * world
     tok_s = tokens_step / (ms / 1e3)
     fpt = flops_per_token(cfg)
-    mfu = tok_s * fpt / (2.25e15 * world)
+    peak, peak_label = measured_bf16_peak()
+    mfu = tok_s * fpt / (peak * world)
+    mfu_nominal = tok_s * fpt / (NOMINAL_BF16 * world)
     # ------------------------------------------------------------------ end to end (public API)
     e2e = None
+    clk_e2e = None
     if not args.no_e2e:
         host = [next(data) for _ in range(args.steps)]
         barrier()
         torch.cuda.synchronize()
+        clocks_e2e = ClockSampler(clocks.gpu)
+        clocks_e2e.start()
         t0 = time.perf_counter()
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record()
@@ -276,6 +303,7 @@ def main(argv=None):
         a1.record()
         torch.cuda.synchronize()
         wall = (time.perf_counter() - t0) / args.steps
+        clk_e2e = clocks_e2e.stop()
         ems = a0.elapsed_time(a1) / args.steps
         et = torch.tensor([ems], device=trainer.device)
         if ctx is not None:
@@ -283,7 +311,8 @@ def main(argv=None):
         ems = float(et.item())
         e2e = {"value": tokens_step / (ems / 1e3), "unit": "tokens/s", "ms_per_step": ems, "wall_ms_per_step": wall * 1e3,
                "h2d_bytes_per_step": int(host[0]["tokens"].numel() * host[0]["tokens"].element_size()),
-               "d2h_bytes_per_step": 4}
+               "d2h_bytes_per_step": 4, "clocks": clk_e2e,
+               "ms_x_median_mhz": ems * clk_e2e["sm_mhz"] if clk_e2e.get("sm_mhz") else None}
     # ------------------------------------------- exposed token exchange (one extra, untimed step)
     # Device time spent in the expert-parallel exchange kernels and their cross-rank waits, summed
     # from CUDA events around each exchange (nothing else runs on the stream meanwhile); max over ranks.
@@ -314,13 +343,19 @@ def main(argv=None):
     out = {
         "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": bc["scaling"],
-        "vs_baseline": tok_s / bc["baseline"] if bc["baseline"] else None, "dtype": "bf16", "data": "synthetic (uniform random ids, seed 2; random init)",
+        "vs_baseline": tok_s / bc["baseline"] if bc["baseline"] else None,
+        "vs_baseline_note": BASELINE_NOTE if bc["baseline"] else None,
+        "tokens_per_s_per_gpu": tok_s / world,
+        "dtype": "bf16", "data": "synthetic (uniform random ids, seed 2; random init)",
         "config": {"model": bc["label"], "name": args.config,
                    "global_batch": seqs * world, "seq_len": seq, "tokens_per_step": tokens_step,
                    "micro_batch": args.micro_batch, "capacity_factor": cfg.capacity_factor,
                    "parallelism": f"{bc['parallel']}{world}" if world > 1 else "single", "l2": "working set >> L2 (no flush needed)",
                    "layers": cfg.num_layers},
-        "mfu": mfu, "exposed_all_to_all_ms_per_step": exposed, "peak_memory_gb": float(peak.item()), "flops_per_token": fpt, "loss": loss,
+        "mfu": mfu, "mfu_denominator": f"{peak / 1e12:.1f} TFLOP/s per GPU, {peak_label}",
+        "mfu_nominal": mfu_nominal, "mfu_nominal_denominator": "2250 TFLOP/s per GPU, nominal dense bf16",
+        "ms_x_median_mhz": ms * clk["sm_mhz"] if clk.get("sm_mhz") else None,
+        "exposed_all_to_all_ms_per_step": exposed, "peak_memory_gb": float(peak.item()), "flops_per_token": fpt, "loss": loss,
         "clocks": clk, "gpu_launches": int(launches),
         "e2e": e2e,
     }

@@ -14,9 +14,10 @@
 // Ordering: a producer kernel fences its stores at system scope; the last CTA to finish (found with
 // an atomic counter) then writes `epoch` into the flag slot [purpose][source] of every peer with a
 // release store. A consumer waits with acquire loads until its W flags reach `epoch` before any
-// kernel reads the exchanged rows. Every wait is bounded (kPeerWaitCycles); on timeout the waiter
-// records kErrTimeoutPeer in the error flag and returns, so the host sees the failure instead of a
-// hung GPU. Rows are never read through TMA or any cluster-multicast path from peer memory.
+// kernel reads the exchanged rows. Every wait is bounded (a per-call wall-time limit, 20 s by
+// default); on timeout the waiter records kErrTimeoutPeer in the error flag and returns, so the host
+// sees the failure instead of a hung GPU. Rows are never read through TMA or any cluster-multicast
+// path from peer memory.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -30,7 +31,14 @@ namespace mxk {
 
 namespace {
 
-constexpr long long kPeerWaitCycles = 1ll << 35;  // ~17 s at 1.9 GHz: peers may lag by a whole layer
+// Default limit of a wait for peers' flags: 20 s of wall time (peers may lag by a whole layer).
+constexpr long long kPeerWaitNs = 20ll * 1000 * 1000 * 1000;
+
+__device__ __forceinline__ long long global_ns() {
+  long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ int ld_acquire_sys(const int* p) {
   int v;
@@ -201,13 +209,14 @@ __global__ void ep_signal_kernel(PeerTable peers, int world, int my, size_t flag
 }
 
 // Wait until every source's flag for `purpose` reached `epoch` (bounded).
+// The limit is wall time (the global timer), so it does not depend on the SM clock.
 __global__ void ep_wait_kernel(PeerTable peers, int world, int my, size_t flags_off, int purpose, int epoch,
-                               int* err) {
+                               int* err, long long limit_ns) {
   if (threadIdx.x < world) {
     const int* f = flag_slot(peers, my, flags_off, purpose, threadIdx.x);
-    const long long t0 = clock64();
+    const long long t0 = global_ns();
     while (ld_acquire_sys(f) < epoch) {
-      if (clock64() - t0 > kPeerWaitCycles) {
+      if (global_ns() - t0 > limit_ns) {
         atomicExch(err, kErrTimeoutPeer);
         break;
       }
@@ -256,9 +265,10 @@ void launch_ep_signal(const EpArgs& a, cudaStream_t st) {
   ep_signal_kernel<<<1, 32, 0, st>>>(a.peers, a.world, a.my, a.flags_off, a.purpose, a.epoch);
 }
 
-void launch_ep_wait(const EpArgs& a, int* err, cudaStream_t st) {
+void launch_ep_wait(const EpArgs& a, int* err, long long limit_ns, cudaStream_t st) {
   count_launch();
-  ep_wait_kernel<<<1, 32, 0, st>>>(a.peers, a.world, a.my, a.flags_off, a.purpose, a.epoch, err);
+  ep_wait_kernel<<<1, 32, 0, st>>>(a.peers, a.world, a.my, a.flags_off, a.purpose, a.epoch, err,
+                                   limit_ns > 0 ? limit_ns : kPeerWaitNs);
 }
 
 // ----------------------------------------------------------------------------------- host IPC

@@ -30,7 +30,11 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each on one half of the tile's columns
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
-constexpr int kMaxGroups = 256;
+constexpr int kMaxGroups = 4096;
+// Tile-prefix table in shared memory: entry j holds the first tile of group j * gpb, where
+// gpb = ceil(G / kPrefixSlots) groups share a slot (one per slot up to 256 groups); decoding a
+// tile walks at most gpb groups from its slot's first group.
+constexpr int kPrefixSlots = 256;
 constexpr int kStageBufs = 2;    // epilogue staging ring depth per warp
 constexpr int kStageBox = 2048;  // 32 rows x 64 bytes
 
@@ -68,7 +72,7 @@ constexpr int kSwbSlotBytes = 2 * kStageBox;
 template <int BN, int STAGES, bool PAIR>
 constexpr int smem_fixed_bytes() {
   // operand stages + 1 KB alignment slack + barriers/scalars + tile prefix table
-  return STAGES * GemmSmem<BN, PAIR>::kStageBytes + 1024 + 256 + (kMaxGroups + 1) * 4;
+  return STAGES * GemmSmem<BN, PAIR>::kStageBytes + 1024 + 256 + (kPrefixSlots + 1) * 4;
 }
 
 template <int BN, int STAGES, bool PAIR, int EPI>
@@ -106,16 +110,33 @@ struct TileCoord {
   int g, mt, nt, kb0, nkb;
 };
 
+__device__ __forceinline__ int prefix_gpb(int G) { return (G + kPrefixSlots - 1) / kPrefixSlots; }
+__device__ __forceinline__ int prefix_slots(int G) {
+  const int gpb = prefix_gpb(G);
+  return (G + gpb - 1) / gpb;
+}
+
 template <int BN, int TM = kBM>
 __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, const int* prefix, int tile) {
-  int lo = 0, hi = p.G - 1;
+  const int gpb = prefix_gpb(p.G);
+  int lo = 0, hi = prefix_slots(p.G) - 1;
   while (lo < hi) {
     int mid = (lo + hi + 1) >> 1;
     if (prefix[mid] <= tile) lo = mid; else hi = mid - 1;
   }
+  // walk the slot's groups (zero-tile groups are skipped like the binary search above skips them)
+  int grp = lo * gpb, acc = prefix[lo];
+  const int gend = min(p.G, grp + gpb);
+  while (grp + 1 < gend) {
+    const int nt = group_tiles<BN, TM>(p, grp);
+    if (acc + nt > tile) break;
+    acc += nt;
+    ++grp;
+  }
   TileCoord tc;
-  tc.g = lo;
-  int local = tile - prefix[lo];
+  tc.g = grp;
+  lo = grp;
+  int local = tile - acc;
   int m_tiles;
   if (p.ragged == 1) {
     int cnt = min(group_count(p, lo), p.M);
@@ -255,12 +276,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                : (2 * BN <= 256) ? 256 : 512;
 
   if (threadIdx.x == 0) {
+    const int gpb = prefix_gpb(p.G);
     int acc = 0;
     for (int g = 0; g < p.G; ++g) {
-      prefix[g] = acc;
+      if (g % gpb == 0) prefix[g / gpb] = acc;
       acc += group_tiles<BN, TM>(p, g);
     }
-    prefix[p.G] = acc;
+    prefix[prefix_slots(p.G)] = acc;
     *abort_flag = 0;
   }
   if (warp == 0 && lane == 0) {
@@ -295,7 +317,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if constexpr (PAIR) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int total_tiles = prefix[p.G];
+  const int total_tiles = prefix[prefix_slots(p.G)];
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer

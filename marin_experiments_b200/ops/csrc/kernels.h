@@ -51,7 +51,9 @@ int launch_router_bwd(const float* logits, int ldl, const float* lse, const int*
 void launch_qb_beta(const float* logits, int ldl, const float* alpha, int T, int E, int qb_count, float* beta,
                     cudaStream_t st);
 int plan_workspace_ints(long n, int E);
-void launch_dispatch_plan(const int* sel, const uint8_t* keep, const float* comb, long n, int K, int E, int cap,
+// Largest expert count the dispatch plan accepts (bounded by one block's shared memory).
+int plan_max_experts();
+int launch_dispatch_plan(const int* sel, const uint8_t* keep, const float* comb, long n, int K, int E, int cap,
                           int* blk_counts, int* slot, int* perm, float* wperm, int* counts, cudaStream_t st);
 void launch_permute(const void* x, const int* perm, const int* counts, int cap, int E, int D, void* xp,
                     cudaStream_t st);
@@ -124,7 +126,8 @@ void launch_ep_combine_pull(const int* sel, const int* slot, const float* comb, 
 void launch_ep_unpermute_pull(const int* sel, const int* slot, void* dx, int T, int K, const EpArgs& a,
                               cudaStream_t st);
 void launch_ep_signal(const EpArgs& a, cudaStream_t st);
-void launch_ep_wait(const EpArgs& a, int* err, cudaStream_t st);
+// Bounded wait (limit_ns of wall time; <= 0 selects the 20 s default) for every peer's flag.
+void launch_ep_wait(const EpArgs& a, int* err, long long limit_ns, cudaStream_t st);
 int ipc_alloc(size_t bytes, void** ptr, void* handle_out);
 int ipc_open(const void* handle, void** ptr);
 int ipc_close(void* ptr);

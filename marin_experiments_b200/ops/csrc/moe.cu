@@ -323,6 +323,7 @@ __global__ void qb_beta_kernel(const float* __restrict__ logits, int ldl, const 
 
 // ------------------------------------------------------------------------------ dispatch plan
 constexpr int kPlanChunk = 4096;  // assignments per block
+constexpr int kPlanMaxSmem = 227 * 1024;  // opt-in dynamic shared memory limit of one block
 
 // Per-block per-expert counts of kept assignments.
 __global__ void plan_count_kernel(const int* __restrict__ sel, const uint8_t* __restrict__ keep, long n, int E,
@@ -550,6 +551,8 @@ int launch_router_fwd(const float* logits, int ldl, const float* bias, int T, in
   else if (E <= 64) RF(2);
   else if (E <= 128) RF(4);
   else if (E <= 256) RF(8);
+  else if (E <= 512) RF(16);
+  else if (E <= 1024) RF(32);
   else return kErrBadArgsHost;
 #undef RF
   return 0;
@@ -568,6 +571,8 @@ int launch_router_bwd(const float* logits, int ldl, const float* lse, const int*
   else if (E <= 64) RB(2);
   else if (E <= 128) RB(4);
   else if (E <= 256) RB(8);
+  else if (E <= 512) RB(16);
+  else if (E <= 1024) RB(32);
   else return kErrBadArgsHost;
 #undef RB
   return 0;
@@ -592,14 +597,30 @@ void launch_qb_beta(const float* logits, int ldl, const float* alpha, int T, int
 
 int plan_workspace_ints(long n, int E) { return (int)(((n + kPlanChunk - 1) / kPlanChunk) * E); }
 
-void launch_dispatch_plan(const int* sel, const uint8_t* keep, const float* comb, long n, int K, int E, int cap,
-                          int* blk_counts, int* slot, int* perm, float* wperm, int* counts, cudaStream_t st) {
+int plan_max_experts() { return kPlanMaxSmem / (33 * (int)sizeof(int)); }
+
+int launch_dispatch_plan(const int* sel, const uint8_t* keep, const float* comb, long n, int K, int E, int cap,
+                         int* blk_counts, int* slot, int* perm, float* wperm, int* counts, cudaStream_t st) {
+  if (E <= 0 || E > plan_max_experts()) return kErrBadArgsHost;
+  // The assign kernel keeps a running offset and 32 per-warp counts per expert in shared memory
+  // (33 E ints): past 48 KB (E > 372) the launch needs the dynamic shared-memory opt-in, set once
+  // per device for the largest size this launcher accepts.
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(plan_assign_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPlanMaxSmem) !=
+        cudaSuccess)
+      return kErrBadArgsHost;
+    attr_set[dev] = true;
+  }
   const int nblk = (int)((n + kPlanChunk - 1) / kPlanChunk);
   count_launch();
   plan_count_kernel<<<nblk, 1024, E * sizeof(int), st>>>(sel, keep, n, E, blk_counts);
   count_launch();
   plan_assign_kernel<<<nblk, 1024, (33 * E) * sizeof(int), st>>>(sel, keep, comb, n, K, E, cap, blk_counts, nblk,
                                                                   slot, perm, wperm, counts);
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
 }
 
 void launch_permute(const void* x, const int* perm, const int* counts, int cap, int E, int D, void* xp,

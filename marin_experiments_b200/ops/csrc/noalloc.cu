@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "kernels.h"
@@ -12,12 +13,16 @@ namespace {
 
 constexpr int kChunk = 4096;   // assignments per block (same split as the regular plan)
 constexpr int kMaxDevices = 64;
+// The assign kernel's shared memory: a running offset plus 32 per-warp counts per expert.
+constexpr int kAssignSmem = 33 * MXK_NOALLOC_MAX_EXPERTS * (int)sizeof(int);
 
 // Scratch for the per-block per-expert counts. Host code must not use this name as a device
 // address: it is a host-side stand-in; the device address comes from cudaGetSymbolAddress.
 static __device__ __align__(256) int g_plan_scratch[MXK_NOALLOC_SCRATCH_INTS];
 
-int* g_scratch_ptr[kMaxDevices] = {nullptr};
+// Per-device set-up result, published with release / read with acquire so that a host thread
+// that sees the pointer also sees the kernel attribute set before it.
+std::atomic<int*> g_scratch_ptr[kMaxDevices];
 std::mutex g_setup_mutex;
 
 __global__ void noalloc_count_kernel(const int* __restrict__ sel, const uint8_t* __restrict__ keep, long n, int E,
@@ -89,22 +94,29 @@ __global__ void noalloc_assign_kernel(const int* __restrict__ sel, const uint8_t
   }
 }
 
-// Device address of the scratch array on the current device, looked up once per device.
+// Device address of the scratch array on the current device, looked up once per device. The same
+// set-up raises the assign kernel's dynamic shared-memory limit on that device (its table needs
+// more than the 48 KB default above 372 experts).
 int scratch_for_current_device(int** out) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return MXK_NOALLOC_CUDA_ERROR + (int)err;
   if (dev < 0 || dev >= kMaxDevices) return MXK_NOALLOC_BAD_ARGS;
-  if (g_scratch_ptr[dev] == nullptr) {
+  int* p = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (g_scratch_ptr[dev] == nullptr) {
-      void* p = nullptr;
-      err = cudaGetSymbolAddress(&p, g_plan_scratch);
+    p = g_scratch_ptr[dev].load(std::memory_order_relaxed);
+    if (p == nullptr) {
+      err = cudaFuncSetAttribute(noalloc_assign_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAssignSmem);
       if (err != cudaSuccess) return MXK_NOALLOC_CUDA_ERROR + (int)err;
-      g_scratch_ptr[dev] = static_cast<int*>(p);
+      void* addr = nullptr;
+      err = cudaGetSymbolAddress(&addr, g_plan_scratch);
+      if (err != cudaSuccess) return MXK_NOALLOC_CUDA_ERROR + (int)err;
+      p = static_cast<int*>(addr);
+      g_scratch_ptr[dev].store(p, std::memory_order_release);
     }
   }
-  *out = g_scratch_ptr[dev];
+  *out = p;
   return 0;
 }
 
@@ -118,7 +130,11 @@ extern "C" int mxk_dispatch_plan_noalloc(const int32_t* selected, const uint8_t*
                                          cudaStream_t stream) {
   if (!selected || !combine || !slot || !perm || !wperm || !counts) return MXK_NOALLOC_BAD_ARGS;
   if (num_tokens <= 0 || k <= 0 || num_experts <= 0 || capacity <= 0) return MXK_NOALLOC_BAD_ARGS;
-  if (num_experts > 512) return MXK_NOALLOC_TOO_LARGE;
+  if (num_experts > MXK_NOALLOC_MAX_EXPERTS) return MXK_NOALLOC_TOO_LARGE;
+  // An error left pending by earlier, unrelated work is the caller's: report it without clearing
+  // it and launch nothing, so it is not mistaken for (or hidden by) this call's result.
+  const cudaError_t pending = cudaPeekAtLastError();
+  if (pending != cudaSuccess) return MXK_NOALLOC_PENDING_ERROR;
   const long n = (long)num_tokens * k;
   const long nblk = (n + kChunk - 1) / kChunk;
   if (nblk * (long)num_experts > MXK_NOALLOC_SCRATCH_INTS) return MXK_NOALLOC_TOO_LARGE;

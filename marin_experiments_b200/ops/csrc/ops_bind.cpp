@@ -268,11 +268,12 @@ void dispatch_plan(const Tensor& sel, const OptT& keep, const Tensor& comb, int6
                    const Tensor& counts) {
   need(sel.scalar_type() == at::kInt && sel.is_contiguous(), "sel must be contiguous int32 [T, K]");
   need(blk_counts.numel() >= mxk::plan_workspace_ints(sel.numel(), E), "plan workspace too small");
-  need(E <= 512, "at most 512 experts per plan");
+  need(E >= 1 && E <= mxk::plan_max_experts(), "expert count out of range for the dispatch plan (1..plan_max_experts)");
   c10::cuda::CUDAGuard g(sel.device());
-  mxk::launch_dispatch_plan(sel.data_ptr<int>(), ptr<const uint8_t>(keep), comb.data_ptr<float>(), sel.numel(),
-                            sel.size(1), E, cap, blk_counts.data_ptr<int>(), slot.data_ptr<int>(), perm.data_ptr<int>(),
-                            wperm.data_ptr<float>(), counts.data_ptr<int>(), stream());
+  ok(mxk::launch_dispatch_plan(sel.data_ptr<int>(), ptr<const uint8_t>(keep), comb.data_ptr<float>(), sel.numel(),
+                               sel.size(1), E, cap, blk_counts.data_ptr<int>(), slot.data_ptr<int>(),
+                               perm.data_ptr<int>(), wperm.data_ptr<float>(), counts.data_ptr<int>(), stream()),
+     "dispatch_plan");
 }
 
 void permute(const Tensor& x, const Tensor& perm, const Tensor& counts, int64_t cap, const Tensor& xp) {
@@ -427,9 +428,9 @@ void ep_signal(const std::vector<int64_t>& peers, int64_t my, int64_t flags_off,
 }
 
 void ep_wait(const std::vector<int64_t>& peers, int64_t my, int64_t flags_off, int64_t purpose, int64_t epoch,
-             const Tensor& err) {
+             const Tensor& err, int64_t limit_ns) {
   auto a = ep_args(peers, my, 1, 1, 8, 0, 0, flags_off, purpose, epoch, c10::nullopt);
-  mxk::launch_ep_wait(a, err.data_ptr<int>(), stream());
+  mxk::launch_ep_wait(a, err.data_ptr<int>(), limit_ns, stream());
 }
 
 // ------------------------------------------------------------------------------- decode path
@@ -540,5 +541,6 @@ void register_ops(pybind11::module& m) {
   m.def("ep_combine_pull", &ep_combine_pull);
   m.def("ep_unpermute_pull", &ep_unpermute_pull);
   m.def("ep_signal", &ep_signal);
-  m.def("ep_wait", &ep_wait);
+  m.def("ep_wait", &ep_wait, py::arg("peers"), py::arg("my"), py::arg("flags_off"), py::arg("purpose"),
+        py::arg("epoch"), py::arg("err"), py::arg("limit_ns") = 0);
 }

@@ -36,6 +36,16 @@ from ..ops import api as ops
 from . import schedules as S
 
 
+def stage_transport() -> str:
+    """Stage-boundary transport named by the environment: ``SP_PP_TRANSPORT`` (``p2p`` or ``null``),
+    or the reference benchmark's switch ``MOE_PP_NULL_XPORT=1`` (grug-moe-pp/pipeline_zb.py:118),
+    which selects ``null``. An explicit ``SP_PP_TRANSPORT`` wins."""
+    t = os.environ.get("SP_PP_TRANSPORT", "")
+    if t:
+        return t
+    return "null" if os.environ.get("MOE_PP_NULL_XPORT", "0") not in ("", "0") else "p2p"
+
+
 @dataclass
 class PipelineTopology:
     pp: int
@@ -128,7 +138,7 @@ class PipelineTrainer:
         # (nothing is sent, receivers get zeros: a compute-only measurement). A blocking send is not
         # offered: under 1F1B two neighbours can each block in a send on a different communicator
         # while the other waits to receive, a cycle.
-        self.transport = os.environ.get("SP_PP_TRANSPORT", "p2p")
+        self.transport = stage_transport()
         if self.transport not in ("p2p", "null"):
             raise ValueError(f"SP_PP_TRANSPORT must be p2p or null, got {self.transport!r}")
 

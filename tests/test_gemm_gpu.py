@@ -77,6 +77,26 @@ def test_grouped_ragged_fwd_dx_dw(G):
             assert (dw[e * n:(e + 1) * n] == 0).all()
 
 
+@pytest.mark.parametrize("g", [257, 1024])
+def test_grouped_many_groups(G, g):
+    """More groups than prefix-table slots (256): tiles are decoded through a slot's group walk."""
+    torch.manual_seed(1)
+    cap, d, n = 128, 128, 256
+    counts = torch.randint(0, cap + 1, (g,), dtype=torch.int32)
+    counts[::7] = 0  # empty groups inside and across slots
+    counts = counts.cuda()
+    x = _rand(g * cap, d)
+    rows = torch.arange(g * cap, device="cuda") % cap
+    x[rows >= counts.repeat_interleave(cap)] = 0
+    w = _rand(g * n, d)
+    y = torch.zeros(g * cap, n, dtype=torch.bfloat16, device="cuda")
+    G.grouped_linear(x, w, counts, out=y)
+    torch.cuda.synchronize()
+    ref = torch.einsum("gck,gnk->gcn", x.view(g, cap, d).float(), w.view(g, n, d).float()).reshape(g * cap, n)
+    valid = (rows < counts.repeat_interleave(cap)).unsqueeze(1)
+    assert _rel(y.float() * valid, ref * valid) < 1e-2
+
+
 def test_swiglu_epilogue(G):
     m, d, inter = 256, 256, 512
     x = _rand(m, d)

@@ -118,7 +118,8 @@ def test_dense_mlp(glu, act):
     assert rel(wdg.main_grad, wdc.grad) < 3e-2
 
 
-@pytest.mark.parametrize("e,k,adaptive", [(64, 4, False), (8, 2, False), (32, 8, True)])
+@pytest.mark.parametrize("e,k,adaptive", [(64, 4, False), (8, 2, False), (32, 8, True), (512, 8, False),
+                                            (1024, 8, True)])
 def test_router(e, k, adaptive):
     torch.manual_seed(3)
     t, d = 512, 256
@@ -189,6 +190,23 @@ def test_moe_capacity_drop():
     cap = 128
     slot, perm, wperm, counts = cuda_fns.dispatch_plan(sel.cuda(), None, comb.cuda(), e, cap)
     ref_slot, ref_counts = R.capacity_slots(sel.long(), e, cap)
+    assert torch.equal(slot.cpu().long(), ref_slot)
+    assert torch.equal(counts.cpu().long(), ref_counts)
+
+
+@pytest.mark.parametrize("e", [512, 1024])
+def test_dispatch_plan_many_experts(e):
+    """Above 372 experts the assign kernel's table needs the dynamic shared-memory opt-in."""
+    torch.manual_seed(7)
+    t, k = 8192, 8
+    sel = torch.stack([torch.randperm(e)[:k] for _ in range(t)]).int()
+    keep = (torch.rand(t, k) > 0.2)
+    comb = torch.rand(t, k)
+    from marin_experiments_b200.ops import cuda_fns
+
+    cap = 128
+    slot, perm, wperm, counts = cuda_fns.dispatch_plan(sel.cuda(), keep.to(torch.uint8).cuda(), comb.cuda(), e, cap)
+    ref_slot, ref_counts = R.capacity_slots(sel.long(), e, cap, keep)
     assert torch.equal(slot.cpu().long(), ref_slot)
     assert torch.equal(counts.cpu().long(), ref_counts)
 

@@ -152,3 +152,20 @@ def test_pp_null_transport():
     last = max(p2p, key=lambda r: p2p[r]["stage"])
     assert null[last]["loss"] is not None and null[last]["loss"] == null[last]["loss"]
     assert null[last]["loss"] != p2p[last]["loss"]
+
+
+def test_null_transport_reference_switch(monkeypatch):
+    """The reference benchmark's MOE_PP_NULL_XPORT=1 selects the null stage transport; an explicit
+    SP_PP_TRANSPORT wins over it."""
+    from marin_experiments_b200.parallel.pipeline import stage_transport
+
+    monkeypatch.delenv("SP_PP_TRANSPORT", raising=False)
+    monkeypatch.delenv("MOE_PP_NULL_XPORT", raising=False)
+    assert stage_transport() == "p2p"
+    monkeypatch.setenv("MOE_PP_NULL_XPORT", "1")
+    assert stage_transport() == "null"
+    monkeypatch.setenv("SP_PP_TRANSPORT", "p2p")
+    assert stage_transport() == "p2p"
+    monkeypatch.delenv("SP_PP_TRANSPORT")
+    monkeypatch.setenv("MOE_PP_NULL_XPORT", "0")
+    assert stage_transport() == "p2p"

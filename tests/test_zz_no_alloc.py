@@ -31,11 +31,12 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
 
 
-def test_noalloc_dispatch_plan_matches_op():
+@pytest.mark.parametrize("e", [64, 512, 1024])
+def test_noalloc_dispatch_plan_matches_op(e):
     from marin_experiments_b200.ops import cuda_fns
 
     f = _entry()
-    t, k, e, cap = 6000, 4, 64, 384
+    t, k, cap = 6000, 4, 384
     gen = torch.Generator().manual_seed(0)
     for call in range(2):
         sel = torch.randint(0, e, (t, k), generator=gen).int().cuda()
@@ -68,3 +69,12 @@ def test_noalloc_rejects_oversized_problem():
     rc = f(_ptr(dummy), _ptr(None), _ptr(dummy), t, k, e, 128, _ptr(dummy), _ptr(dummy), _ptr(dummy), _ptr(dummy),
            stream)
     assert rc == 1  # MXK_NOALLOC_TOO_LARGE, nothing launched
+
+
+def test_noalloc_rejects_too_many_experts():
+    f = _entry()
+    dummy = torch.zeros(16, dtype=torch.int32, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = f(_ptr(dummy), _ptr(None), _ptr(dummy), 4, 1, 1025, 128, _ptr(dummy), _ptr(dummy), _ptr(dummy), _ptr(dummy),
+           stream)
+    assert rc == 1  # MXK_NOALLOC_TOO_LARGE: above the 1024-expert limit, nothing launched
