@@ -192,6 +192,8 @@ def main(argv=None):
                     help="sequences per microbatch (gradient accumulation); default 8 on one GPU, where "
                          "~6B parameters with fp32 master, grads and moments leave room for 8 x 2048 tokens of "
                          "activations, and 16 with expert parallelism, where the experts are sharded")
+    ap.add_argument("--remat", default=None, choices=["none", "recompute_all", "save_moe"],
+                    help="activation recompute per block (default: none; the model config's value)")
     ap.add_argument("--layers", type=int, default=None, help="(debug only) override layer count")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-trace", default=None,
@@ -219,10 +221,12 @@ def main(argv=None):
     torch.cuda.set_device(local_rank)
     ctx = pdist.init(ep_size=world if bc["parallel"] == "ep" else 1) if world > 1 else None
     cfg = bc["model"]
-    if args.layers is not None:
-        import dataclasses
+    import dataclasses
 
+    if args.layers is not None:
         cfg = dataclasses.replace(cfg, num_layers=args.layers)
+    if args.remat is not None:
+        cfg = dataclasses.replace(cfg, remat_mode=args.remat)
     run = GrugRunConfig(model=cfg, optimizer=GrugMoeAdamHConfig(learning_rate=0.01, adam_lr=6e-4, warmup=0.0),
                         trainer=GrugTrainerConfig(trainer=TrainerConfig(seed=0, num_train_steps=1000)))
     trainer = Trainer(run, device=f"cuda:{local_rank}", micro_batch=args.micro_batch, dist=ctx)
@@ -351,7 +355,7 @@ def main(argv=None):
                    "global_batch": seqs * world, "seq_len": seq, "tokens_per_step": tokens_step,
                    "micro_batch": args.micro_batch, "capacity_factor": cfg.capacity_factor,
                    "parallelism": f"{bc['parallel']}{world}" if world > 1 else "single", "l2": "working set >> L2 (no flush needed)",
-                   "layers": cfg.num_layers},
+                   "layers": cfg.num_layers, "remat": cfg.remat_mode},
         "mfu": mfu, "mfu_denominator": f"{peak / 1e12:.1f} TFLOP/s per GPU, {peak_label}",
         "mfu_nominal": mfu_nominal, "mfu_nominal_denominator": "2250 TFLOP/s per GPU, nominal dense bf16",
         "ms_x_median_mhz": ms * clk["sm_mhz"] if clk.get("sm_mhz") else None,

@@ -88,8 +88,13 @@ class GrugModelConfig:
     router_z_loss_coef: float = 0.001
     aux_loss_coef: float = 0.0
     capacity_factor: float = 1.0
+    # Accepted for config compatibility and ignored: this framework has one attention kernel, one
+    # MoE path and one (exact) QB-beta selection, so there is nothing to choose between.
     attention_implementation: str | None = None
     moe_implementation: str | None = None
+    # Activation recompute per block: "none" keeps every activation; "recompute_all" keeps only each
+    # block's input and recomputes the block in backward; "save_moe" keeps the routed-expert MoE's
+    # activations and recomputes the rest of the block (norms, attention, shared expert).
     remat_mode: RematMode = "none"
     fast_qb_beta: bool = False
     qb_balancing: bool = True
@@ -108,6 +113,8 @@ class GrugModelConfig:
 
     def __post_init__(self) -> None:
         _ = self.inferred_head_dim
+        if self.remat_mode not in ("none", "recompute_all", "save_moe"):
+            raise ValueError(f"remat_mode must be none, recompute_all or save_moe, got {self.remat_mode!r}")
         if self.num_heads % self.num_kv_heads != 0:
             raise ValueError("num_heads must be divisible by num_kv_heads for grouped-query attention")
         if self.vocab_size <= 0:

@@ -214,21 +214,57 @@ class Block(nn.Module):
         self.cfg = cfg
 
     def forward(self, x, batch: int, seq: int, segment_ids=None, dp_group=None, logit_bias=None):
+        """One block. Under ``remat_mode`` (megagpt-speedrun/model.py:760-769) the block runs inside
+        ``torch.utils.checkpoint`` (non-reentrant: the saved tensors are dropped after the forward
+        and the region is re-run when backward first needs them): ``recompute_all`` checkpoints the
+        whole block, ``save_moe`` everything before the routed experts, whose activations (and
+        token exchange, under expert parallelism) are kept. Every rank re-runs the same regions in
+        the same order, so the exchanges inside a recomputed region stay matched across ranks."""
+        mode = self.cfg.remat_mode
+        if mode == "none" or not torch.is_grad_enabled():
+            return self._forward(x, batch, seq, segment_ids, dp_group, logit_bias)
+        from torch.utils.checkpoint import checkpoint
+
+        if mode == "recompute_all" or not self.cfg.is_moe:
+            return checkpoint(self._forward, x, batch, seq, segment_ids, dp_group, logit_bias, use_reentrant=False)
+        overlap = self._shared_overlap(x)
+        h, x, base = checkpoint(self._pre_moe, x, batch, seq, segment_ids, not overlap, use_reentrant=False)
+        return self._moe(h, x, base, dp_group, logit_bias, overlap)
+
+    def _shared_overlap(self, x) -> bool:
+        if self.shared is None or self.shared.tp is not None or self.mlp.ep_group is None:
+            return False
+        from ..parallel import ep
+
+        return ep.overlap_shared_enabled(x, self.mlp.ep_group)
+
+    def _pre_moe(self, x, batch: int, seq: int, segment_ids, with_shared: bool):
+        """Norms and attention (and the shared expert, unless it runs beside the routed experts):
+        ``(h, residual, base)`` where ``base`` is the routed experts' residual input."""
         h, x = self.attn_norm.with_residual(x)
         x = self.attn(h, x, batch, seq, segment_ids)
         h, x = self.mlp_norm.with_residual(x)
-        if not self.cfg.is_moe:
-            return self.mlp(h, residual=x), None
-        if self.shared is not None and self.shared.tp is None and self.mlp.ep_group is not None:
+        base = self.shared(h, residual=x) if (with_shared and self.shared is not None) else x
+        return h, x, base
+
+    def _moe(self, h, x, base, dp_group, logit_bias, overlap: bool):
+        if overlap:
             from ..parallel import ep
 
-            if ep.overlap_shared_enabled(h, self.mlp.ep_group):
-                # shared expert on a side stream while the routed experts exchange tokens
-                return ep.with_shared_overlap(
-                    h, self.shared, lambda: self.mlp(h, residual=x, dp_group=dp_group, logit_bias=logit_bias))
-        base = x if self.shared is None else self.shared(h, residual=x)
-        x, stats = self.mlp(h, residual=base, dp_group=dp_group, logit_bias=logit_bias)
-        return x, stats
+            # shared expert on a side stream while the routed experts exchange tokens
+            return ep.with_shared_overlap(
+                h, self.shared, lambda: self.mlp(h, residual=x, dp_group=dp_group, logit_bias=logit_bias))
+        return self.mlp(h, residual=base, dp_group=dp_group, logit_bias=logit_bias)
+
+    def _forward(self, x, batch: int, seq: int, segment_ids=None, dp_group=None, logit_bias=None):
+        if not self.cfg.is_moe:
+            h, x = self.attn_norm.with_residual(x)
+            x = self.attn(h, x, batch, seq, segment_ids)
+            h, x = self.mlp_norm.with_residual(x)
+            return self.mlp(h, residual=x), None
+        overlap = self._shared_overlap(x)
+        h, x, base = self._pre_moe(x, batch, seq, segment_ids, not overlap)
+        return self._moe(h, x, base, dp_group, logit_bias, overlap)
 
 
 class Transformer(nn.Module):

@@ -75,3 +75,30 @@ def test_optimizer_step_matches_cpu():
     torch.cuda.synchronize()
     d = (gpu.store.master.cpu() - cpu.store.master)
     assert d.abs().max().item() < 1e-5, d.abs().max().item()
+
+
+@pytest.mark.parametrize("mode", ["recompute_all", "save_moe"])
+def test_remat_matches_no_remat_gpu(mode):
+    """Activation recompute on the sm_100a path: same loss and gradients as keeping every
+    activation, and a lower allocator high-water mark for the same microbatch."""
+    import dataclasses
+
+    tok = torch.randint(0, MOE.vocab_size, (4, 256), generator=torch.Generator().manual_seed(2))
+    out = {}
+    for m in ("none", mode):
+        cfg = dataclasses.replace(MOE, remat_mode=m, num_layers=4)
+        run = GrugRunConfig(model=cfg, optimizer=GrugMoeAdamHConfig(warmup=0.0),
+                            trainer=GrugTrainerConfig(trainer=TrainerConfig(num_train_steps=10)))
+        tr = Trainer(run, device="cuda:0", micro_batch=4)
+        torch.cuda.synchronize()
+        torch.cuda.reset_peak_memory_stats()
+        base = torch.cuda.memory_allocated()
+        lg, _ = tr.model.next_token_loss(tok.cuda(), z_loss_weight=1e-4)
+        lg.backward()
+        torch.cuda.synchronize()
+        out[m] = (lg.item(), tr.store.grad.clone(), torch.cuda.max_memory_allocated() - base)
+        del tr, lg
+    (l0, g0, m0), (l1, g1, m1) = out["none"], out[mode]
+    assert abs(l1 - l0) < 1e-4 * abs(l0)
+    assert ((g1 - g0).norm() / g0.norm()).item() < 1e-3
+    assert m1 < m0, (m0, m1)
