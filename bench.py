@@ -286,8 +286,8 @@ def main(argv=None):
     tokens_step = seqs * seq * world
     tok_s = tokens_step / (ms / 1e3)
     fpt = flops_per_token(cfg)
-    peak, peak_label = measured_bf16_peak()
-    mfu = tok_s * fpt / (peak * world)
+    flop_peak, peak_label = measured_bf16_peak()
+    mfu = tok_s * fpt / (flop_peak * world)
     mfu_nominal = tok_s * fpt / (NOMINAL_BF16 * world)
     # ------------------------------------------------------------------ end to end (public API)
     e2e = None
@@ -356,7 +356,7 @@ def main(argv=None):
                    "micro_batch": args.micro_batch, "capacity_factor": cfg.capacity_factor,
                    "parallelism": f"{bc['parallel']}{world}" if world > 1 else "single", "l2": "working set >> L2 (no flush needed)",
                    "layers": cfg.num_layers, "remat": cfg.remat_mode},
-        "mfu": mfu, "mfu_denominator": f"{peak / 1e12:.1f} TFLOP/s per GPU, {peak_label}",
+        "mfu": mfu, "mfu_denominator": f"{flop_peak / 1e12:.1f} TFLOP/s per GPU, {peak_label}",
         "mfu_nominal": mfu_nominal, "mfu_nominal_denominator": "2250 TFLOP/s per GPU, nominal dense bf16",
         "ms_x_median_mhz": ms * clk["sm_mhz"] if clk.get("sm_mhz") else None,
         "exposed_all_to_all_ms_per_step": exposed, "peak_memory_gb": float(peak.item()), "flops_per_token": fpt, "loss": loss,

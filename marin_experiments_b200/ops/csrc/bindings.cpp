@@ -6,6 +6,8 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
+#include <vector>
 
 #include "launch.h"
 #include "kernels.h"
@@ -35,7 +37,8 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const 
           int64_t b_grp, int64_t c_grp, int64_t epi, int64_t bn, int64_t accum, double alpha,
           const c10::optional<at::Tensor>& C2, const c10::optional<at::Tensor>& R,
           const c10::optional<at::Tensor>& row_scale, int64_t act_kind, const at::Tensor& err, int64_t b_mod,
-          int64_t c_mod) {
+          int64_t c_mod, const c10::optional<at::Tensor>& peer_maps, int64_t peer_epl, int64_t peer_my,
+          int64_t peer_cap) {
   if (std::getenv("MXK_TRACE")) { std::fprintf(stderr, "[mxk] gemm binding enter\n"); std::fflush(stderr); }
   check_2d_bf16(A, "A");
   check_2d_bf16(B, "B");
@@ -48,6 +51,17 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const 
                 "counts must be a CUDA int32 tensor with G entries");
   }
   if (R.has_value()) check_2d_bf16(*R, "R");
+  if (peer_maps.has_value()) {
+    // peer-store epilogue: plain bf16 stores of whole groups, one tensor map per destination rank
+    TORCH_CHECK(epi == 0 && C.scalar_type() == at::kBFloat16 && !accum && G > 1 && c_mod == 0 && ragged == 1,
+                "peer stores: grouped ragged-M bf16 store epilogue only");
+    TORCH_CHECK(peer_epl > 0 && G % peer_epl == 0 && peer_my >= 0 && peer_cap >= M,
+                "peer stores: groups must be whole (rank, local expert) blocks");
+    TORCH_CHECK(peer_maps->is_cuda() && peer_maps->scalar_type() == at::kByte &&
+                    peer_maps->numel() >= (int64_t)sizeof(CUtensorMap) * (G / peer_epl) &&
+                    reinterpret_cast<uintptr_t>(peer_maps->data_ptr()) % 64 == 0,
+                "peer stores: peer_maps must hold one 64-byte-aligned CUtensorMap per rank on the GPU");
+  }
   TORCH_CHECK(reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0, "C must be 16-byte aligned");
   TORCH_CHECK((C.stride(0) * C.element_size()) % 16 == 0, "C row stride must be a multiple of 16 bytes");
   // Epilogues store 32-column chunks: C must be wide enough for N rounded up to 32.
@@ -98,6 +112,10 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const 
   p.err = reinterpret_cast<int*>(err.data_ptr());
   p.ksplit = 1;
   p.raster_n = 0;
+  p.peer_maps = peer_maps.has_value() ? peer_maps->data_ptr() : nullptr;
+  p.peer_epl = (int)peer_epl;
+  p.peer_my = (int)peer_my;
+  p.peer_cap = (int)peer_cap;
   // Output extents for the TMA stores: columns clip at N; rows clip at M for a single problem,
   // at the buffer end for grouped problems.
   L.c_cols = epi == 8 ? 2 * N : N;  // SwiGLU backward writes gate and up gradients: 2N columns
@@ -117,6 +135,26 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, const 
 
 int64_t num_sms() { return mxk::num_sms(); }
 
+// Tensor maps for the peer-store epilogue: one per rank, over the bf16 [rows, cols] buffer at byte
+// offset `off` of that rank's heap (peers[r] = its base as mapped in this process). Returned as
+// host bytes; the caller copies them to the GPU.
+at::Tensor peer_store_maps(const std::vector<int64_t>& peers, int64_t off, int64_t cols, int64_t rows) {
+  TORCH_CHECK(!peers.empty() && cols > 0 && rows > 0 && (cols * 2) % 16 == 0 && off % 16 == 0,
+              "peer_store_maps: bad arguments");
+  auto out = at::zeros({(int64_t)(peers.size() * sizeof(CUtensorMap))}, at::kByte);
+  for (size_t r = 0; r < peers.size(); ++r) {
+    CUtensorMap m;
+    const char* base = reinterpret_cast<const char*>(peers[r]) + off;
+    TORCH_CHECK(mxk::make_tmap_epi(&m, base, false, cols, rows, cols), "peer_store_maps: encoding failed");
+    std::memcpy(out.data_ptr<uint8_t>() + r * sizeof(CUtensorMap), &m, sizeof(CUtensorMap));
+  }
+  return out;
+}
+
+void set_stream_sm_budget(int64_t stream, int64_t sms) {
+  mxk::set_stream_sm_budget(reinterpret_cast<cudaStream_t>(stream), (int)sms);
+}
+
 }  // namespace
 
 void register_ops(pybind11::module& m);
@@ -124,5 +162,7 @@ void register_ops(pybind11::module& m);
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "sm_100a tcgen05 GEMM (grouped / ragged, fused epilogues)");
   m.def("num_sms", &num_sms);
+  m.def("peer_store_maps", &peer_store_maps);
+  m.def("set_stream_sm_budget", &set_stream_sm_budget, "cap the CTAs of persistent GEMMs on a stream");
   register_ops(m);
 }

@@ -8,6 +8,8 @@
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "gemm_sm100.cuh"
 #include "kernels.h"
@@ -104,6 +106,29 @@ int num_sms() {
   return n;
 }
 
+// Per-stream SM budgets: a persistent GEMM launched on a stream with a budget runs at most that
+// many CTAs (one per SM), leaving the other SMs to kernels of other streams -- e.g. the token
+// exchange of expert parallelism beside a side-stream GEMM.
+static std::mutex g_budget_mu;
+static std::vector<std::pair<cudaStream_t, int>> g_budget;
+
+void set_stream_sm_budget(cudaStream_t s, int sms) {
+  std::lock_guard<std::mutex> lock(g_budget_mu);
+  for (auto it = g_budget.begin(); it != g_budget.end(); ++it)
+    if (it->first == s) {
+      g_budget.erase(it);
+      break;
+    }
+  if (sms > 0) g_budget.emplace_back(s, sms);
+}
+
+static int stream_sm_budget(cudaStream_t s) {
+  std::lock_guard<std::mutex> lock(g_budget_mu);
+  for (const auto& e : g_budget)
+    if (e.first == s) return e.second;
+  return 0;
+}
+
 // CTA-pair (cta_group::2) tiles are used for BN = 256 problems whose row tiles of 256 stay
 // inside each group; MXK_GEMM_PAIR=0 turns them off.
 static bool pair_enabled() {
@@ -147,7 +172,10 @@ static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
   GemmParams p = L.p;
   const int n_tiles = (p.N + BN - 1) / BN;
   const int m_tiles = (p.M + TM - 1) / TM;
-  const int units = PAIR ? num_sms() / 2 : num_sms();  // concurrently running tile workers
+  int sms = num_sms();
+  const int budget = stream_sm_budget(stream);
+  if (budget > 0 && budget < sms) sms = budget;
+  const int units = PAIR ? (sms / 2 > 0 ? sms / 2 : 1) : sms;  // concurrently running tile workers
   long long tiles = (long long)p.G * m_tiles * n_tiles;
   // Split K over workers when a non-grouped fp32 accumulation has too few output tiles for the
   // GPU; the partial sums are combined by the element-wise atomic TMA reduce-add.

@@ -26,6 +26,12 @@ struct GemmParams {
   float alpha;
   int act_kind;  // 0 silu, 1 relu, 2 gelu(tanh)
   int* err;
+  // Peer-store epilogue (EPI_STORE, bf16 C, grouped): when peer_maps is set, group g's rows go to
+  // rank g / peer_epl through the g / peer_epl-th tensor map of the device array peer_maps (one
+  // 64-byte-aligned CUtensorMap per rank over that rank's [E][cap][N] buffer), at row
+  // (peer_my * peer_epl + g % peer_epl) * peer_cap + (row within the group).
+  const void* peer_maps;
+  int peer_epl, peer_my, peer_cap;
 };
 
 }  // namespace mxk

@@ -667,8 +667,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = sc * v[i];
           }
-          if (p.c_f32) ring.f32_boxes(&tmC, o, col, y0, reduce, lane);
-          else ring.bf16_box(&tmC, o, col, y0, lane);
+          bool stored = false;
+          if constexpr (EPI == EPI_STORE) {
+            if (p.peer_maps != nullptr) {
+              // the tile's rows belong to source rank g / peer_epl: store them into its buffer
+              const CUtensorMap* pm = reinterpret_cast<const CUtensorMap*>(p.peer_maps) + tc.g / p.peer_epl;
+              const int yp = (p.peer_my * p.peer_epl + tc.g % p.peer_epl) * p.peer_cap + (y0 - tc.g * p.c_grp);
+              ring.bf16_box(pm, o, col, yp, lane);
+              stored = true;
+            }
+          }
+          if (!stored) {
+            if (p.c_f32) ring.f32_boxes(&tmC, o, col, y0, reduce, lane);
+            else ring.bf16_box(&tmC, o, col, y0, lane);
+          }
           if constexpr (EPI == EPI_SILU || EPI == EPI_ACT) ring.bf16_box(&tmC2, v, col, y0, lane);
         }
       }
@@ -683,7 +695,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         while (!mbar_try_wait(&h_bars[j % kSlots], (j / kSlots) & 1) && clock64() - t0 < (1ll << 26)) {}
       }
     }
-    if (lane == 0) bulk_wait_all();  // every TMA store / reduce of this warp has landed
+    if (lane == 0) {
+      bulk_wait_all();  // every TMA store / reduce of this warp has landed
+      // stores into other GPUs' memory: ordered before anything this GPU signals to them afterwards
+      if (p.peer_maps != nullptr) __threadfence_system();
+    }
   }
 
   tc_fence_before();

@@ -1,6 +1,7 @@
 // Plain C++ launch interface of the sm_100a kernels (no torch types), shared by the torch
 // bindings and by the C entry points.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -25,5 +26,9 @@ struct GemmLaunch {
 
 int launch_gemm(const GemmLaunch& L, cudaStream_t stream);
 int num_sms();
+// Epilogue-store tensor map (64-byte boxes of 32 rows, 64-byte swizzle) over [rows, cols], row stride ld.
+bool make_tmap_epi(CUtensorMap* m, const void* ptr, bool f32, int64_t cols, int64_t rows, int64_t ld);
+// At most `sms` CTAs for persistent GEMMs launched on stream `s` (<= 0: no limit).
+void set_stream_sm_budget(cudaStream_t s, int sms);
 
 }  // namespace mxk

@@ -36,11 +36,14 @@ def _pick_bn(n: int, epi: str, b_mn: bool, a_mn: bool) -> int:
 
 def gemm(a, b, c, *, a_mn=False, b_mn=False, G=1, M=None, N=None, K=None, counts=None, ragged=0,
          a_grp=0, b_grp=0, c_grp=0, epi="store", bn=None, accum=False, alpha=1.0, c2=None, r=None,
-         row_scale=None, act="silu", b_mod=0, c_mod=0):
+         row_scale=None, act="silu", b_mod=0, c_mod=0, peer=None):
+    """``peer = (maps, epl, my, cap)``: store group g's rows into rank g // epl's buffer instead of
+    ``c`` (see ``PeerStore``)."""
     if bn is None:
         bn = _pick_bn(N, epi, b_mn, a_mn)
+    maps, epl, my, pcap = peer if peer is not None else (None, 0, 0, 0)
     ext().gemm(a, a_mn, b, b_mn, c, G, M, N, K, counts, ragged, a_grp, b_grp, c_grp, EPI[epi], bn, int(accum),
-               float(alpha), c2, r, row_scale, ACT[act], err_flag(a.device), b_mod, c_mod)
+               float(alpha), c2, r, row_scale, ACT[act], err_flag(a.device), b_mod, c_mod, maps, epl, my, pcap)
     return c
 
 
@@ -116,6 +119,20 @@ def linear_dw(dy, x, *, out=None, accum=False, alpha=1.0):
     return gemm(dy, x, out, a_mn=True, b_mn=True, M=n, N=k, K=t, accum=accum, alpha=alpha)
 
 
+class PeerStore:
+    """Destination of a grouped GEMM whose output rows belong to other GPUs: group ``g = s * epl + e``
+    (source rank s, local expert e) is written into rank s's ``[E][cap][N]`` buffer at rows
+    ``(my * epl + e) * cap + ...`` by the GEMM's own epilogue (TMA stores into peer memory), so the
+    transfer overlaps the math tile by tile. ``maps`` is the device array of per-rank tensor maps
+    from ``ext().peer_store_maps``."""
+
+    def __init__(self, maps: torch.Tensor, epl: int, my: int, cap: int):
+        self.maps, self.epl, self.my, self.cap = maps, epl, my, cap
+
+    def args(self):
+        return (self.maps, self.epl, self.my, self.cap)
+
+
 def grouped_linear(x, w, counts, *, out=None, epi="store", c2=None, n_w=None, **kw):
     """Per-group ``x[g] @ w[g % n_w]^T`` over a capacity layout.
 
@@ -129,11 +146,14 @@ def grouped_linear(x, w, counts, *, out=None, epi="store", c2=None, n_w=None, **
     k = x.shape[1]
     if out is None:
         out = torch.empty(x.shape[0], n, dtype=torch.bfloat16, device=x.device)
+    peer = kw.pop("peer", None)
+    if peer is not None:
+        kw["peer"] = peer.args()
     return gemm(x, w, out, G=g, M=cap, N=n, K=k, counts=counts, ragged=1, a_grp=cap, b_grp=n, c_grp=cap,
                 epi=epi, c2=c2, b_mod=0 if n_w == g else n_w, **kw)
 
 
-def grouped_linear_dx(dy, w, counts, *, out=None, n_w=None, swiglu_h=None):
+def grouped_linear_dx(dy, w, counts, *, out=None, n_w=None, swiglu_h=None, peer=None):
     """Per-group ``dy[g] [C, N] @ w[g % n_w] [N, K]`` -> ``[G*C, K]``. With ``swiglu_h`` (the SwiGLU
     pre-activations ``[G*C, 2K]``, blocked gate/up rows) the product is the activation gradient and
     the epilogue writes the gate/up gradients ``[G*C, 2K]`` instead (SiLU gate)."""
@@ -146,6 +166,8 @@ def grouped_linear_dx(dy, w, counts, *, out=None, n_w=None, swiglu_h=None):
         cols = 2 * k if swiglu_h is not None else k
         out = torch.empty(dy.shape[0], cols, dtype=torch.bfloat16, device=dy.device)
     extra = {} if swiglu_h is None else {"epi": "swiglu_bwd", "r": swiglu_h}
+    if peer is not None:
+        extra["peer"] = peer.args()
     return gemm(dy, w, out, b_mn=True, G=g, M=cap, N=k, K=n, counts=counts, ragged=1, a_grp=cap, b_grp=n,
                 c_grp=cap, b_mod=0 if n_w == g else n_w, **extra)
 

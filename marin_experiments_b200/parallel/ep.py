@@ -100,20 +100,67 @@ class _MoEEP(torch.autograd.Function):
 # flag purposes of the peer exchange
 _DISPATCH, _Y, _DY, _DXP = 0, 1, 2, 3
 
+# In-flight microbatch slots. A layer's receive and return buffers stay alive as saved activations
+# until that microbatch's backward; a pipeline schedule with several forwards in flight (1F1B)
+# gives each in-flight microbatch its own slot (``microbatch_slot``), so a later forward never
+# overwrites rows an earlier microbatch's backward still reads. Every rank of an expert-parallel
+# group runs the same schedule, so a slot names the same buffers on all of them.
+_SLOTS = 1
+_SLOT = 0
+
+
+def set_inflight_microbatches(n: int) -> None:
+    """Number of microbatches whose forward may run before an earlier one's backward (call before
+    the first expert-parallel forward: the heap is sized from it)."""
+    global _SLOTS
+    _SLOTS = max(1, int(n))
+
+
+class microbatch_slot:
+    """``with microbatch_slot(m): forward(...)`` -- buffers of slot ``m % inflight``."""
+
+    def __init__(self, m: int):
+        self.slot = int(m) % _SLOTS
+
+    def __enter__(self):
+        global _SLOT
+        self.prev, _SLOT = _SLOT, self.slot
+        return self
+
+    def __exit__(self, *exc):
+        global _SLOT
+        _SLOT = self.prev
+        return False
+
+
+def return_mode() -> str:
+    """How expert outputs (forward) and input gradients (backward) travel back to their source
+    ranks: ``store`` (default) -- the grouped GEMM's epilogue writes them straight into the source's
+    buffer with TMA stores into peer memory, tile by tile, and the source combines locally;
+    ``pull`` -- the GEMM writes locally and the source's combine kernel reads the owners' rows over
+    NVLink (``MXK_EP_RETURN``)."""
+    m = os.environ.get("MXK_EP_RETURN", "store")
+    if m not in ("store", "pull"):
+        raise ValueError(f"MXK_EP_RETURN must be store or pull, got {m!r}")
+    return m
+
 
 def _heap(group, dev, e, cap, d, n_layers):
     from .symm import heap_for, nbytes
 
     rows = e * cap
-    per_layer = nbytes((rows, d), torch.bfloat16) + nbytes((e,), torch.int32) + 512
-    shared = 3 * nbytes((rows, d), torch.bfloat16)
-    return heap_for(group, dev, per_layer * n_layers + shared + (1 << 20))
+    # per layer and in-flight slot: the receive buffer, its counts and the return buffer
+    per_layer = 2 * nbytes((rows, d), torch.bfloat16) + nbytes((e,), torch.int32) + 1024
+    # shared by layers: output-gradient rows, returned input gradients, and the pull mode's buffers
+    shared = 4 * nbytes((rows, d), torch.bfloat16)
+    return heap_for(group, dev, per_layer * n_layers * _SLOTS + shared + (1 << 20))
 
 
 # Exchange timing: while a list is installed (``exchange_timing``), every token exchange of the peer
 # path records a (start, end) pair of CUDA events on the current stream around its kernels and
 # waits. Nothing else runs on that stream in between, so the summed intervals are the device time
-# the step spends exposed in the exchange.
+# the step spends exposed in the exchange. (Rows that travel inside a GEMM's epilogue are part of
+# that GEMM's time, not of these intervals.)
 _TIMING: list | None = None
 
 
@@ -151,11 +198,17 @@ def _span(start):
 
 
 class _MoEEPFused(torch.autograd.Function):
-    """Expert parallelism with the token exchange inside the kernels (NVLink peer stores/loads):
-    the permute pushes rows into the owners' receive buffers, the combine pulls the owners' outputs,
-    and the backward mirrors it. Per-layer receive buffers live in a symmetric heap and stay valid as
-    saved activations; the output, output-gradient and input-gradient buffers are shared by layers
-    (each is consumed before any peer can reach the next layer's exchange)."""
+    """Expert parallelism with the token exchange inside the kernels (NVLink peer memory).
+
+    Forward: the permute kernel pushes routed rows into the owners' receive buffers; the owners'
+    grouped gate/up GEMM runs on them; the down GEMM's epilogue stores each output tile straight
+    into the source rank's return buffer (``return_mode() == "store"``), and after the flag wait
+    the source combines its rows locally. Backward mirrors it: the combine-backward kernel pushes
+    ``w * dout`` rows to the owners, and the gate/up input-gradient GEMM stores its tiles into the
+    sources' buffer, which they sum locally. Per-layer buffers (receive, return) live in a
+    symmetric heap and stay valid as saved activations; the output-gradient and returned
+    input-gradient buffers are shared by layers (each is consumed before any peer can reach the next
+    layer's exchange)."""
 
     @staticmethod
     def forward(ctx, h, comb, w_gu, w_d, residual, sel, keep, cap, group, act, layer, n_layers):
@@ -173,9 +226,9 @@ class _MoEEPFused(torch.autograd.Function):
         heap = _heap(group, dev, e, cap, d, n_layers)
         my = heap.my
         rows = e * cap
-        off_xp = heap.alloc(("xp", layer), rows * d * 2)
-        off_cnt = heap.alloc(("cnt", layer), e * 4)
-        off_y = heap.alloc("y", rows * d * 2)
+        key = (layer, _SLOT)
+        off_xp = heap.alloc(("xp",) + key, rows * d * 2)
+        off_cnt = heap.alloc(("cnt",) + key, e * 4)
         slot, perm, wperm, counts = dispatch_plan(sel, keep, comb, e, cap)
         ep = heap.next_epoch(_DISPATCH)
         t0 = _mark()
@@ -188,17 +241,31 @@ class _MoEEPFused(torch.autograd.Function):
         Hh = torch.empty(rows, two_i, dtype=torch.bfloat16, device=dev)
         A = torch.empty(rows, inter, dtype=torch.bfloat16, device=dev)
         G.grouped_linear(xp_recv, w_gu.view(e_loc * two_i, d), counts_recv, out=Hh, epi="swiglu", c2=A, n_w=e_loc)
-        y_recv = heap.tensor(off_y, (rows, d), torch.bfloat16)
-        G.grouped_linear(A, w_d.view(e_loc * d, inter), counts_recv, out=y_recv, n_w=e_loc)
-        ey = heap.next_epoch(_Y)
-        t1 = _mark()
-        ext().ep_signal(heap.peers, my, 0, _Y, ey)
-        ext().ep_wait(heap.peers, my, 0, _Y, ey, err_flag(dev))
         out = torch.empty(t, d, dtype=torch.bfloat16, device=dev)
-        y_local = torch.empty(rows, d, dtype=torch.bfloat16, device=dev)
-        ext().ep_combine_pull(sel, slot, _c(comb.detach().float()), None if residual is None else _c(residual), out,
-                              y_local, heap.peers, my, e_loc, cap, off_y)
-        _span(t1)
+        res = None if residual is None else _c(residual)
+        if return_mode() == "store":
+            off_yr = heap.alloc(("yret",) + key, rows * d * 2)
+            y_local = heap.tensor(off_yr, (rows, d), torch.bfloat16)  # filled by the owners' GEMMs
+            G.grouped_linear(A, w_d.view(e_loc * d, inter), counts_recv, out=y_local, n_w=e_loc,
+                             peer=heap.peer_store(off_yr, rows, d, e_loc, cap))
+            ey = heap.next_epoch(_Y)
+            t1 = _mark()
+            ext().ep_signal(heap.peers, my, 0, _Y, ey)
+            ext().ep_wait(heap.peers, my, 0, _Y, ey, err_flag(dev))
+            ext().combine(y_local, sel, slot, _c(comb.detach().float()), res, out, cap)
+            _span(t1)
+        else:
+            off_y = heap.alloc("y", rows * d * 2)
+            y_recv = heap.tensor(off_y, (rows, d), torch.bfloat16)
+            G.grouped_linear(A, w_d.view(e_loc * d, inter), counts_recv, out=y_recv, n_w=e_loc)
+            ey = heap.next_epoch(_Y)
+            t1 = _mark()
+            ext().ep_signal(heap.peers, my, 0, _Y, ey)
+            ext().ep_wait(heap.peers, my, 0, _Y, ey, err_flag(dev))
+            y_local = torch.empty(rows, d, dtype=torch.bfloat16, device=dev)
+            ext().ep_combine_pull(sel, slot, _c(comb.detach().float()), res, out, y_local, heap.peers, my, e_loc,
+                                  cap, off_y)
+            _span(t1)
         ctx.save_for_backward(xp_recv, Hh, A, y_local, sel, slot, perm, wperm, counts, counts_recv)
         ctx.w_gu, ctx.w_d, ctx.cap, ctx.act, ctx.t, ctx.heap = w_gu, w_d, cap, _ACT[act], t, heap
         ctx.has_res = residual is not None
@@ -219,8 +286,9 @@ class _MoEEPFused(torch.autograd.Function):
         my = heap.my
         e = e_loc * heap.world
         rows = e * cap
+        store = return_mode() == "store"
         off_dy = heap.alloc("dy", rows * d * 2)
-        off_dxp = heap.alloc("dxp", rows * d * 2)
+        off_dxp = heap.alloc("dxret" if store else "dxp", rows * d * 2)
         dcomb = torch.empty(sel.shape, dtype=torch.float32, device=dev)
         ext().combine_bwd(dout, y_local, sel, slot, perm, wperm, counts, cap, None, dcomb)
         edy = heap.next_epoch(_DY)
@@ -241,19 +309,24 @@ class _MoEEPFused(torch.autograd.Function):
                 dH = torch.empty_like(Hh)
                 ext().swiglu_bwd(dA, Hh, dH, ctx.act, counts_recv, cap)
             dxp = heap.tensor(off_dxp, (rows, d), torch.bfloat16)
-            G.grouped_linear_dx(dH, w_gu.view(e_loc * two_i, d), counts_recv, out=dxp, n_w=e_loc)
+            # store: each tile of input-gradient rows goes straight into its source rank's buffer
+            G.grouped_linear_dx(dH, w_gu.view(e_loc * two_i, d), counts_recv, out=dxp, n_w=e_loc,
+                                peer=heap.peer_store(off_dxp, rows, d, e_loc, cap) if store else None)
         exp_ = heap.next_epoch(_DXP)
         t1 = _mark()
         ext().ep_signal(heap.peers, my, 0, _DXP, exp_)
         _span(t1)
         # The gate/up weight gradient reads dH (local) and this layer's own receive buffer, never the
-        # shared dy / dxp buffers, so it runs while the peers pull this rank's dxp rows.
+        # shared dy / returned-gradient buffers, so it runs while the input-gradient rows travel.
         with G.defer_weight_grads(None):
             G.grouped_linear_dw(dH, xp_recv, counts_recv, out=_mg(w_gu).view(e_loc * two_i, d), n_w=e_loc)
         t2 = _mark()
         ext().ep_wait(heap.peers, my, 0, _DXP, exp_, err_flag(dev))
         dh = torch.empty(ctx.t, d, dtype=torch.bfloat16, device=dev)
-        ext().ep_unpermute_pull(sel, slot, dh, heap.peers, my, e_loc, cap, off_dxp)
+        if store:
+            ext().unpermute_add(dxp, sel, slot, None, dh, cap)
+        else:
+            ext().ep_unpermute_pull(sel, slot, dh, heap.peers, my, e_loc, cap, off_dxp)
         _span(t2)
         ctx.w_gu = ctx.w_d = ctx.heap = None
         return (dh, dcomb, None, None, (dout if ctx.has_res else None), None, None, None, None, None, None, None)
@@ -314,11 +387,24 @@ def overlap_shared_enabled(h: torch.Tensor, group) -> bool:
             and os.environ.get("MXK_EP_OVERLAP", "0") == "1")
 
 
+def comm_sms() -> int:
+    """SMs that side-stream GEMMs leave free for the exchange kernels (``MXK_EP_COMM_SMS``, default 16;
+    even, so CTA-pair GEMM tiles keep whole pairs)."""
+    n = int(os.environ.get("MXK_EP_COMM_SMS", "16"))
+    return max(0, n + (n & 1))
+
+
 def side_stream(dev: torch.device) -> torch.cuda.Stream:
+    """The device's side stream; persistent GEMMs launched on it use all but ``comm_sms()`` SMs."""
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     s = _SIDE.get(idx)
     if s is None:
+        from ..ops._ext import ext
+
         s = _SIDE[idx] = torch.cuda.Stream(device=torch.device("cuda", idx))
+        reserve = comm_sms()
+        if reserve > 0:
+            ext().set_stream_sm_budget(s.cuda_stream, max(2, ext().num_sms() - reserve))
     return s
 
 

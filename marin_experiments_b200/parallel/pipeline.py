@@ -141,6 +141,10 @@ class PipelineTrainer:
         self.transport = stage_transport()
         if self.transport not in ("p2p", "null"):
             raise ValueError(f"SP_PP_TRANSPORT must be p2p or null, got {self.transport!r}")
+        if topo.ep > 1:
+            from . import ep
+
+            ep.set_inflight_microbatches(max_inflight(schedule, topo.pp, microbatches, mode))
 
     # --------------------------------------------------------------------------- helpers
     def _chain_clip(self) -> None:
@@ -181,7 +185,9 @@ class PipelineTrainer:
             aux = aux + c.aux_loss_coef * torch.stack([s.lbl for s in stats]).sum() / n
         return aux
 
-    def _forward(self, m, tok, seg, lw, mb, s):
+    def _forward(self, m, tok, seg, lw, mb, s, slot=None):
+        """Forward of microbatch ``m`` (rows ``m*mb .. (m+1)*mb`` of ``tok``); its expert-parallel
+        buffers are those of in-flight slot ``slot`` (default ``m``)."""
         topo = self.topo
         sl = slice(m * mb, (m + 1) * mb)
         segm = None if seg is None else seg[sl].reshape(-1)
@@ -192,7 +198,10 @@ class PipelineTrainer:
             x_in = self._recv((mb * s, self.cfg.model.hidden_dim), topo.prev_rank, topo.fwd_group)
             x_in.requires_grad_(True)
             h = x_in
-        h, stats = self.model.body(h, mb, s, segm, self.tr.dp_group)
+        from . import ep
+
+        with ep.microbatch_slot(m if slot is None else slot):
+            h, stats = self.model.body(h, mb, s, segm, self.tr.dp_group)
         aux = self._aux(stats)
         beta = torch.stack([st.beta for st in stats]).detach() if stats and all(st.beta is not None for st in stats) \
             else None
@@ -346,7 +355,7 @@ class PipelineTrainer:
                         apply_qb_betas(self.model, tr.pending_qb)
                     hooks, snap = self._weights_used_by_forward()
                     with hooks:
-                        rec = self._forward(0, tok, seg, lw, tok.shape[0], tok.shape[1])
+                        rec = self._forward(0, tok, seg, lw, tok.shape[0], tok.shape[1], slot=tick)
                     if rec[1] is not None:
                         self._send(rec[1].detach(), topo.next_rank, topo.fwd_group, pending)
                     if rec[3] is not None:
@@ -377,6 +386,23 @@ class _nullctx:
 
     def __exit__(self, *a):
         return False
+
+
+def max_inflight(schedule: str, pp: int, microbatches: int, mode: str = "sync") -> int:
+    """Most microbatches any stage holds between their forward and backward: GPipe holds all ``M``,
+    1F1B / ZB-H1 up to ``P``; the async no-flush mode ``P - s`` at stage s (``P`` at most)."""
+    if mode == "async":
+        return pp
+    best = 1
+    for stage_sched in S.SCHEDULES[schedule](pp, microbatches):
+        live = 0
+        for kind, _ in stage_sched:
+            if kind == "F":
+                live += 1
+                best = max(best, live)
+            elif kind == "B":
+                live -= 1
+    return best
 
 
 def async_stage_delay(pp: int, stage: int) -> int:

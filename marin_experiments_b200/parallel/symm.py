@@ -39,6 +39,7 @@ class SymmetricHeap:
         self.top = DATA_OFF
         self.offsets: dict = {}
         self.epochs = [0] * 32
+        self._maps: dict = {}
         self.counters = ext().heap_tensor(self.local, COUNTERS_OFF, [128], _DT[torch.int32], self.device.index)
 
     def alloc(self, key, nbytes: int) -> int:
@@ -56,6 +57,19 @@ class SymmetricHeap:
 
     def tensor(self, off: int, shape, dtype) -> torch.Tensor:
         return ext().heap_tensor(self.local, off, list(shape), _DT[dtype], self.device.index)
+
+    def peer_store(self, off: int, rows: int, cols: int, epl: int, cap: int):
+        """Destination of a grouped GEMM whose epilogue stores group ``s * epl + e``'s rows into rank
+        s's bf16 ``[rows, cols]`` buffer at ``off`` (``ops.gemm.PeerStore``). The per-rank tensor maps
+        are encoded once per buffer and kept on the device."""
+        from ..ops.gemm import PeerStore
+
+        key = ("maps", off, rows, cols)
+        maps = self._maps.get(key)
+        if maps is None:
+            maps = ext().peer_store_maps(self.peers, off, cols, rows).to(self.device)
+            self._maps[key] = maps
+        return PeerStore(maps, epl, self.my, cap)
 
     def next_epoch(self, purpose: int) -> int:
         self.epochs[purpose] += 1

@@ -76,7 +76,7 @@ def _worker(rank, world, port, q):
 def test_ep_gpu_matches_single_gpu():
     import torch.multiprocessing as mp
 
-    world = min(torch.cuda.device_count(), 4)
+    world = min(torch.cuda.device_count(), 8)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -121,8 +121,10 @@ def _worker_impls(rank, world, port, q):
         xs = [torch.randn(t, d, generator=gx).bfloat16() for _ in range(3)]
         gouts = [torch.randn(t, d, generator=gx).bfloat16() for _ in range(3)]
         res = {}
-        for impl in ("nccl", "peer"):
+        for impl, ret in (("nccl", "store"), ("peer", "pull"), ("peer", "store")):
             os.environ["MXK_EP_IMPL"] = impl
+            os.environ["MXK_EP_RETURN"] = ret  # store: rows return inside the GEMM epilogues
+            impl = impl if impl == "nccl" else f"peer-{ret}"
             params = [(param(wr), param(wgu[lo:hi]), param(wdn[lo:hi])) for wr, wgu, wdn in layers]
             outs, grads = [], []
             for it in range(3):
@@ -142,8 +144,11 @@ def _worker_impls(rank, world, port, q):
         def rel(a, b):
             return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
 
-        errs = [rel(a, b) for a, b in zip(res["peer"][0] + res["peer"][1] + res["peer"][2] + res["peer"][3],
-                                          res["nccl"][0] + res["nccl"][1] + res["nccl"][2] + res["nccl"][3])]
+        errs = []
+        for name in ("peer-pull", "peer-store"):
+            got, want = res[name], res["nccl"]
+            errs += [rel(a, b) for a, b in zip(got[0] + got[1] + got[2] + got[3],
+                                               want[0] + want[1] + want[2] + want[3])]
         q.put((rank, errs))
     finally:
         dist.destroy_process_group()
@@ -153,7 +158,7 @@ def _worker_impls(rank, world, port, q):
 def test_ep_peer_exchange_matches_nccl():
     import torch.multiprocessing as mp
 
-    world = min(torch.cuda.device_count(), 4)
+    world = min(torch.cuda.device_count(), 8)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()

@@ -169,3 +169,14 @@ def test_null_transport_reference_switch(monkeypatch):
     monkeypatch.delenv("SP_PP_TRANSPORT")
     monkeypatch.setenv("MOE_PP_NULL_XPORT", "0")
     assert stage_transport() == "p2p"
+
+
+def test_max_inflight_microbatches():
+    """Expert-parallel buffers per in-flight microbatch: GPipe holds every microbatch, 1F1B at most P."""
+    from marin_experiments_b200.parallel.pipeline import max_inflight
+
+    assert max_inflight("gpipe", 4, 16) == 16
+    assert max_inflight("1f1b", 4, 16) == 4
+    assert max_inflight("zb", 4, 16) <= 4
+    assert max_inflight("1f1b", 4, 16, mode="async") == 4
+    assert max_inflight("1f1b", 1, 8) == 1
