@@ -12,12 +12,15 @@ working set (12.8 GB of bf16 weights alone) is far larger than the 126 MB L2, so
 needed between steps. The end-to-end figure repeats K steps through ``Trainer.train_step`` with
 every step's tokens copied from pinned host memory and the loss read back to the host.
 
-Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--config megagpt|grug_dp|adaptive]
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+                       [--config megagpt|grug_dp|adaptive|pp] [--pp-schedule zb|1f1b|gpipe|async]
 
 ``--config grug_dp`` (12 layers, d768, 8 experts top-2, seq 1024, 256 sequences per step in total,
 pure data parallel) and ``--config adaptive`` (16 layers, d1024, 32 experts with a per-token top-k in
 1..8, seq 2048, 256K tokens per step in total, EP = N) are the smaller configurations; their
-global batch is fixed, so they scale strongly. The default is the headline configuration above.
+global batch is fixed, so they scale strongly. ``--config pp`` runs the same architecture as
+pipeline stages x expert parallelism (see ``bench_pp``). The default is the headline configuration
+above.
 """
 
 from __future__ import annotations
@@ -167,6 +170,127 @@ class ClockSampler:
         return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def bench_pp(args) -> int:
+    """``--config pp``: pipeline x expert parallelism on the megagpt architecture (24 layers split
+    evenly over the stages), PP = N / 2 stages x EP = 2 (PP = N, EP = 1 below 4 GPUs), 16
+    microbatches of 8 x 2048 tokens per pipeline replica, delayed-gradient AdamH with staleness 1,
+    stage activations over NCCL p2p (isend / irecv, completing in the background). ``--pp-schedule``:
+    zb (ZB-H1 zero bubble, default), 1f1b, gpipe (synchronous steps) or async (1F1B without flush,
+    one microbatch per tick; a "step" is 16 ticks). Every rank times the same steps with CUDA events;
+    the reported time is the max over ranks."""
+    import datetime
+
+    import torch.distributed as tdist
+
+    from marin_experiments_b200.config import GrugRunConfig, GrugTrainerConfig, TrainerConfig
+    from marin_experiments_b200.ops._ext import check_kernel_errors, ext
+    from marin_experiments_b200.optim.delayed import DelayedGrugMoeAdamHConfig
+    from marin_experiments_b200.parallel.pipeline import PipelineTrainer, bubble_fraction, init_topology
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    if not tdist.is_initialized():
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), rank=rank, world_size=world,
+                                 init_method="env://" if world > 1 else "tcp://127.0.0.1:29599")
+    ep = 2 if world >= 4 else 1
+    pp = world // ep
+    topo = init_topology(pp, ep)
+    cfg = megagpt_config()
+    import dataclasses
+
+    if args.layers is not None:
+        cfg = dataclasses.replace(cfg, num_layers=args.layers)
+    opt = DelayedGrugMoeAdamHConfig(tau=1, corrector="none", learning_rate=0.01, adam_lr=6e-4, warmup=0.0)
+    run = GrugRunConfig(model=cfg, optimizer=opt, trainer=GrugTrainerConfig(trainer=TrainerConfig(seed=3, num_train_steps=1000)))
+    M, mb, seq = 16, 8, cfg.max_seq_len
+    sched = args.pp_schedule
+    mode = "async" if sched == "async" else "sync"
+    pt = PipelineTrainer(run, topo, device=f"cuda:{local_rank}", microbatches=1 if mode == "async" else M,
+                         schedule="1f1b" if mode == "async" else sched, mode=mode)
+    g = torch.Generator().manual_seed(3 * 1000003 + topo.e)
+
+    def batch(n):
+        return {"tokens": torch.randint(0, cfg.vocab_size, (n, seq), generator=g).pin_memory()}
+
+    def one_step(host: bool):
+        """One step; returns the last stage's loss as a device tensor (None on other stages)."""
+        if mode == "async":
+            losses = pt.run_async([batch(mb) for _ in range(M)] if host else [staged_mb[i] for i in range(M)], M,
+                                  as_tensors=True)
+            return losses[-1] if losses else None
+        out = pt.train_step(batch(M * mb) if host else staged_full)
+        return out.get("train/cross_entropy_loss")
+
+    staged_full = {"tokens": batch(M * mb)["tokens"].cuda()}
+    staged_mb = [{"tokens": batch(mb)["tokens"].cuda()} for _ in range(M)]
+    for _ in range(args.warmup):
+        one_step(False)
+    torch.cuda.synchronize()
+    check_kernel_errors()
+    clocks = ClockSampler(local_rank)
+    tdist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    n0 = ext().launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        one_step(False)
+    e1.record()
+    torch.cuda.synchronize()
+    launches = ext().launch_count() - n0
+    tdist.barrier()
+    clk = clocks.stop()
+    ms_t = torch.tensor([e0.elapsed_time(e1) / args.steps], device="cuda")
+    tdist.all_reduce(ms_t, op=tdist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    tokens_step = M * mb * seq * ep
+    tok_s = tokens_step / (ms / 1e3)
+    # end to end: every step's tokens from pinned host memory, loss read back by the last stage
+    e2e = None
+    if not args.no_e2e:
+        tdist.barrier()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(args.steps):
+            loss = one_step(True)
+            if loss is not None:
+                _ = float(loss.item())  # the last stage reads the step's loss back
+        a1.record()
+        torch.cuda.synchronize()
+        et = torch.tensor([a0.elapsed_time(a1) / args.steps], device="cuda")
+        tdist.all_reduce(et, op=tdist.ReduceOp.MAX)
+        ems = float(et.item())
+        e2e = {"value": tokens_step / (ems / 1e3), "unit": "tokens/s", "ms_per_step": ems,
+               "h2d_bytes_per_step": M * mb * seq * 8, "d2h_bytes_per_step": 4 if topo.is_last else 0}
+    peak = torch.tensor([torch.cuda.max_memory_allocated() / 1e9], device="cuda")
+    tdist.all_reduce(peak, op=tdist.ReduceOp.MAX)
+    check_kernel_errors()
+    fpt = flops_per_token(cfg)
+    flop_peak, peak_label = measured_bf16_peak()
+    out = {
+        "metric": "pipeline-parallel MoE train tokens/sec/box", "value": tok_s, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "tokens_per_s_per_gpu": tok_s / world, "dtype": "bf16",
+        "data": "synthetic (uniform random ids, seed 3; random init)",
+        "config": {"model": "megagpt-speedrun MoE split into pipeline stages", "name": "pp", "pp": pp, "ep": ep,
+                   "schedule": sched, "microbatches": M, "micro_batch": mb, "seq_len": seq, "layers": cfg.num_layers,
+                   "tokens_per_step": tokens_step, "optimizer": "delayed AdamH, staleness 1",
+                   "parallelism": f"pp{pp}xep{ep}", "l2": "working set >> L2 (no flush needed)",
+                   "bubble_model": bubble_fraction("1f1b" if mode == "async" else sched, pp, M)},
+        "mfu": tok_s * fpt / (flop_peak * world), "mfu_denominator": f"{flop_peak / 1e12:.1f} TFLOP/s per GPU, {peak_label}",
+        "peak_memory_gb": float(peak.item()), "clocks": clk, "gpu_launches": int(launches), "e2e": e2e,
+    }
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    tdist.barrier()
+    tdist.destroy_process_group()
+    return 0
+
+
 def reference_arm(args):
     """The reference is JAX/XLA (jax + levanter + flash-attn-4 + NCCL cu13); none of it is installed in
     this image and there is no network, so its own code path cannot run here."""
@@ -184,9 +308,10 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
-    ap.add_argument("--config", default="megagpt", choices=["megagpt", "grug_dp", "adaptive"],
+    ap.add_argument("--config", default="megagpt", choices=["megagpt", "grug_dp", "adaptive", "pp"],
                     help="megagpt (headline, weak scaling with EP = N); grug_dp and adaptive: the smaller "
-                         "configurations, fixed global batch")
+                         "configurations, fixed global batch; pp: pipeline x expert parallelism")
+    ap.add_argument("--pp-schedule", default="zb", choices=["zb", "1f1b", "gpipe", "async"])
     ap.add_argument("--seqs-per-gpu", type=int, default=None)
     ap.add_argument("--micro-batch", type=int, default=None,
                     help="sequences per microbatch (gradient accumulation); default 8 on one GPU, where "
@@ -202,6 +327,8 @@ def main(argv=None):
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return reference_arm(args)
+    if args.config == "pp":
+        return bench_pp(args)
 
     from marin_experiments_b200.config import GrugRunConfig, GrugTrainerConfig, TrainerConfig
     from marin_experiments_b200.data.synthetic import UniformTokenBatches

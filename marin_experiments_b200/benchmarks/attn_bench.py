@@ -1,6 +1,7 @@
-"""Attention kernels: tcgen05 forward/backward vs the mma.sync ones, causal, 16 heads x 96.
+"""Attention kernels: tcgen05 forward/backward vs the mma.sync ones and the library kernels on the
+same box (cuDNN through torch's SDPA, flash_attn 2.x), causal, 16 heads x 96, 8 x 2048 tokens.
 
-Usage: python -m marin_experiments_b200.benchmarks.attn_bench
+Usage: python -m marin_experiments_b200.benchmarks.attn_bench [--once]
 """
 
 from __future__ import annotations
@@ -34,14 +35,16 @@ def run(b=8, s=2048, h=16, hkv=16, hd=96, iters=10, once=False):
         ext().flash_bwd_sm100(q, k, v, o, lse, None, b, s, 0, sc, do, ds, dqa, dq, dk, dv, False, err_flag(q.device))
         torch.cuda.synchronize()
         return res
-    for name, fn, f in [
+    cases = [
         ("fwd_tcgen05", lambda: ext().flash_fwd_sm100(q, k, v, o, lse, None, b, s, 0, sc, err_flag(q.device), None), fl),
         ("fwd_mma_sync", lambda: ext().flash_fwd(q, k, v, o, lse, None, b, s, 0, sc), fl),
         ("bwd_mma_sync", lambda: ext().flash_bwd(q, k, v, o, lse, None, b, s, 0, sc, do, ds, dqa, dq, dk, dv, False),
          2.5 * fl),
         ("bwd_tcgen05", lambda: ext().flash_bwd_sm100(q, k, v, o, lse, None, b, s, 0, sc, do, ds, dqa, dq, dk, dv,
                                                       False, err_flag(q.device)), 2.5 * fl),
-    ]:
+    ]
+    cases += _library_cases(b, s, h, hkv, hd, fl)
+    for name, fn, f in cases:
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
@@ -55,6 +58,53 @@ def run(b=8, s=2048, h=16, hkv=16, hd=96, iters=10, once=False):
         res[name] = {"ms": ms, "tflops": f / ms / 1e9}
         print(json.dumps({name: res[name]}), flush=True)
     return res
+
+
+def _library_cases(b, s, h, hkv, hd, fl):
+    """cuDNN attention (torch SDPA restricted to the cuDNN backend) and flash_attn, forward and
+    forward+backward minus forward, on the same shape; skipped where the library is missing."""
+    out = []
+    q = torch.randn(b, h, s, hd, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(b, hkv, s, hd, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(b, hkv, s, hd, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    do = torch.randn(b, h, s, hd, device="cuda", dtype=torch.bfloat16)
+    try:
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        import torch.nn.functional as F
+
+        def cudnn_fwd():
+            with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+                return F.scaled_dot_product_attention(q, k, v, is_causal=True)
+
+        cudnn_fwd()
+        o = cudnn_fwd()
+
+        def cudnn_bwd():
+            torch.autograd.grad(o, (q, k, v), do, retain_graph=True)
+
+        cudnn_bwd()
+        out += [("fwd_cudnn", cudnn_fwd, fl), ("bwd_cudnn", cudnn_bwd, 2.5 * fl)]
+    except Exception as e:  # backend not available for this shape / build
+        print(json.dumps({"cudnn": f"unavailable: {type(e).__name__}: {e}"[:200]}), flush=True)
+    try:
+        from flash_attn import flash_attn_func
+
+        qf, kf, vf = (t.detach().transpose(1, 2).contiguous().requires_grad_(True) for t in (q, k, v))
+        dof = do.transpose(1, 2).contiguous()
+
+        def fa_fwd():
+            return flash_attn_func(qf, kf, vf, causal=True)
+
+        of = fa_fwd()
+
+        def fa_bwd():
+            torch.autograd.grad(of, (qf, kf, vf), dof, retain_graph=True)
+
+        fa_bwd()
+        out += [("fwd_flash_attn", fa_fwd, fl), ("bwd_flash_attn", fa_bwd, 2.5 * fl)]
+    except Exception as e:
+        print(json.dumps({"flash_attn": f"unavailable: {type(e).__name__}: {e}"[:200]}), flush=True)
+    return out
 
 
 if __name__ == "__main__":

@@ -28,14 +28,19 @@ _CHUNK_DTYPE = np.dtype([("start", "<i8"), ("len", "<i4"), ("mat", "<i4"), ("gro
 def _ns_quintic(g: torch.Tensor, steps: int) -> torch.Tensor:
     """Newton-Schulz orthogonalisation with the quintic iteration of Muon
     (a, b, c) = (3.4445, -4.7750, 2.0315) (Jordan et al., "Muon", 2024); the iteration of
-    megagpt-speedrun/async_pipeline.py:379-388. On CUDA, a single matrix whose sides are multiples of
-    64 runs the iterations in bf16 on the tcgen05 GEMM (``_ns_quintic_sm100``); stacks of matrices
-    (the per-expert weights) run as batched fp32 products, one launch per product for the whole
-    stack, as does everything with ``MXK_NS_FP32=1``."""
+    megagpt-speedrun/async_pipeline.py:379-388 and, per expert, grug-moe-pp/pipeline_zb.py:68-106.
+    On CUDA, a single matrix whose sides are multiples of 64 runs the iterations in bf16 on the
+    tcgen05 GEMM (``_ns_quintic_sm100``), and a stack of matrices (the per-expert weights) whose
+    short side is a multiple of 128 and long side a multiple of 64 runs them as grouped tcgen05
+    GEMMs, one launch per product for the whole stack (``_ns_quintic_sm100_grouped``). Other shapes,
+    and everything with ``MXK_NS_FP32=1``, run batched fp32 products."""
     single = g.dim() == 2 or math.prod(g.shape[:-2]) == 1
-    if (g.is_cuda and single and g.shape[-2] % 64 == 0 and g.shape[-1] % 64 == 0
-            and os.environ.get("MXK_NS_FP32", "0") != "1"):
+    fp32 = os.environ.get("MXK_NS_FP32", "0") == "1"
+    if g.is_cuda and not fp32 and single and g.shape[-2] % 64 == 0 and g.shape[-1] % 64 == 0:
         return _ns_quintic_sm100(g, steps)
+    short, long_ = min(g.shape[-2:]), max(g.shape[-2:])
+    if g.is_cuda and not fp32 and not single and short % 128 == 0 and long_ % 64 == 0:
+        return _ns_quintic_sm100_grouped(g, steps)
     a, b, c = 3.4445, -4.7750, 2.0315
     x = g.float()
     transpose = x.shape[-2] > x.shape[-1]
@@ -72,6 +77,36 @@ def _ns_quintic_sm100(g: torch.Tensor, steps: int) -> torch.Tensor:
             B = (b * A.float() + c * AA.float()).to(torch.bfloat16)
             x = (a * x.float() + G.linear_dx(B, x).float()).to(torch.bfloat16)  # B [m, m] @ x [m, n]
         out[i] = x.float().t() if transpose else x.float()
+    return out.reshape(g.shape)
+
+
+def _ns_quintic_sm100_grouped(g: torch.Tensor, steps: int) -> torch.Tensor:
+    """The quintic iteration for a stack ``[..., r, c]`` of E matrices in bf16 on grouped tcgen05
+    GEMMs (group e = matrix e): per step ``A = X X^T`` and ``A A`` as grouped K-major products and
+    ``(b A + c A A) X`` with X as the MN-major operand, each one launch for the whole stack; the
+    Frobenius normalisation and the ``a X + ...`` combination in fp32. Returns fp32."""
+    from ..ops import gemm as G
+
+    a, b, c = 3.4445, -4.7750, 2.0315
+    r, cdim = g.shape[-2], g.shape[-1]
+    flat = g.reshape(-1, r, cdim).float()
+    e = flat.shape[0]
+    transpose = r > cdim
+    xf = flat.transpose(-1, -2) if transpose else flat
+    m, n = xf.shape[-2], xf.shape[-1]  # wide orientation: m <= n, m a multiple of 128
+    x = (xf / (xf.norm(dim=(-2, -1), keepdim=True) + 1e-7)).to(torch.bfloat16).reshape(e * m, n).contiguous()
+    A = torch.empty(e * m, m, dtype=torch.bfloat16, device=g.device)
+    AA = torch.empty_like(A)
+    Y = torch.empty(e * m, n, dtype=torch.bfloat16, device=g.device)
+    for _ in range(steps):
+        G.gemm(x, x, A, G=e, M=m, N=m, K=n, a_grp=m, b_grp=m, c_grp=m)  # A_e = X_e X_e^T
+        G.gemm(A, A, AA, G=e, M=m, N=m, K=m, a_grp=m, b_grp=m, c_grp=m)  # A_e A_e^T = A_e A_e
+        B = (b * A.float() + c * AA.float()).to(torch.bfloat16)
+        G.gemm(B, x, Y, b_mn=True, G=e, M=m, N=n, K=m, a_grp=m, b_grp=m, c_grp=m)  # B_e X_e
+        x = (a * x.float() + Y.float()).to(torch.bfloat16)
+    out = x.float().reshape(e, m, n)
+    if transpose:
+        out = out.transpose(-1, -2)
     return out.reshape(g.shape)
 
 

@@ -30,6 +30,8 @@ class DistContext:
     bucket_bytes: int = 256 << 20
     # ranks holding the same expert shard (one per expert-parallel group); None when ep == world
     expert_dp_group: object = None
+    _armed: bool = False
+    _launched: set = None
 
     def local_expert_range(self, num_experts: int) -> tuple[int, int]:
         if num_experts % self.ep_size:
@@ -57,6 +59,7 @@ class DistContext:
         sharded = (lambda i: i.sharded_over is not None and self.ep_size > 1)
         self._replicated = [i for i in st.infos if not sharded(i) and i.trainable]
         self._sharded = [i for i in st.infos if sharded(i) and i.trainable]
+        self.enable_overlap(trainer)
 
     def setup_optimizer(self, trainer) -> None:
         opt = getattr(trainer.opt, "inner", trainer.opt)
@@ -93,7 +96,11 @@ class DistContext:
         """Mean-all-reduce the gradients of replicated parameters (bucketed over the flat buffer).
 
         Expert shards already hold the sum over every rank's tokens of per-rank mean-loss gradients;
-        dividing by the batch-group size turns that into the gradient of the global mean loss."""
+        dividing by the batch-group size turns that into the gradient of the global mean loss.
+
+        With overlap armed for the step's last microbatch (``arm_overlap``), the ranges of the
+        final norm / head and of every block were already all-reduced on the gradient stream as
+        backward finished them; this joins that stream and reduces only what is left."""
         if self.world == 1:
             return
         st = trainer.store
@@ -102,20 +109,113 @@ class DistContext:
             if self.expert_dp_group is not None:  # replicas of this shard in other expert groups
                 torch_dist.all_reduce(g, group=self.expert_dp_group)
             g.div_(self.world)
-        # contiguous runs of replicated parameters in the flat buffer
-        runs = []
-        for info in self._replicated:
-            s, e = info.offset, info.offset + info.numel
-            if runs and runs[-1][1] >= s - 64:
-                runs[-1][1] = e
-            else:
-                runs.append([s, e])
-        limit = self.bucket_bytes // 4
+        runs = _runs(self._replicated)
+        if self._armed:
+            torch.cuda.current_stream().wait_stream(self._grad_stream)
+            runs = _subtract(runs, sorted(self._launched))
+            self._armed, self._launched = False, set()
         for s, e in runs:
-            for c0 in range(s, e, limit):
-                buf = st.grad[c0: min(e, c0 + limit)]
-                torch_dist.all_reduce(buf, group=self.batch_group)
+            self._reduce_run(st, s, e, self.batch_group)
+
+    # ---------------------------------------------------------------- overlap with backward
+    # Per-segment hooks: a segment is a module (the final norm, then every block, in the order
+    # backward finishes them) and the replicated flat-buffer runs of its parameters. A tensor hook
+    # on the segment's input fires when backward has issued every kernel that writes the segment's
+    # weight gradients (they precede the input gradient in the graph); on the step's last
+    # microbatch the hook makes the gradient stream wait for the training stream and all-reduces
+    # the segment's runs there, on a communicator of its own, while backward continues.
+    supports_overlap = True  # a context whose grad_sync is not this one's turns it off
+
+    def enable_overlap(self, trainer) -> None:
+        if (not self.supports_overlap or self.world == 1 or self.backend != "nccl"
+                or os.environ.get("MXK_DP_OVERLAP", "1") == "0"):
+            return
+        model, st = trainer.model, trainer.store
+        ranks = list(range(self.world)) if self.batch_group is torch_dist.group.WORLD else None
+        self._grad_group = torch_dist.new_group(ranks) if ranks is not None else self.batch_group
+        self._grad_stream = torch.cuda.Stream(device=st.device)
+        rep = {i.name: i for i in self._replicated}
+        mods = []
+        if getattr(model, "final_norm", None) is not None:
+            tail = [n for n in rep if n.startswith(("final_norm.", "head_down", "output_proj"))]
+            mods.append((model.final_norm, tail))
+        for j, blk in enumerate(getattr(model, "blocks", [])):
+            mods.append((blk, [n for n in rep if n.startswith(f"blocks.{j}.")]))
+        for mod, names in mods:
+            runs = [tuple(r) for r in _runs([rep[n] for n in names])]
+            if runs:
+                mod.register_forward_pre_hook(self._pre_hook(runs, st))
+        self._overlap_on = True
+
+    def arm_overlap(self) -> None:
+        """Called before the step's last microbatch: its backward launches the segment reductions."""
+        if getattr(self, "_overlap_on", False):
+            self._armed, self._launched = True, set()
+
+    def _pre_hook(self, runs, st):
+        def pre(mod, args):
+            if not (self._armed and torch.is_grad_enabled()):
+                return None
+            x = args[0]
+            if torch.is_tensor(x) and x.requires_grad:
+                x.register_hook(lambda g: self._launch(runs, st))
+            return None
+        return pre
+
+    def _launch(self, runs, st):
+        if not self._armed or all(r in self._launched for r in runs):
+            return None
+        side = self._grad_stream
+        side.wait_stream(torch.cuda.current_stream(st.device))
+        with torch.cuda.stream(side):
+            for s, e in runs:
+                if (s, e) not in self._launched:
+                    self._reduce_run(st, s, e, self._grad_group)
+                    self._launched.add((s, e))
+        return None
+
+    def _reduce_run(self, st, s: int, e: int, group) -> None:
+        """Mean over the group of ``grad[s:e]`` in bucket-sized pieces; ``MXK_DP_WIRE=bf16`` sends
+        bf16 (half the bytes; the sum is rounded to bf16 once)."""
+        limit = self.bucket_bytes // 4
+        bf16 = os.environ.get("MXK_DP_WIRE", "fp32") == "bf16" and st.grad.is_cuda
+        for c0 in range(s, e, limit):
+            buf = st.grad[c0: min(e, c0 + limit)]
+            if bf16:
+                w = buf.to(torch.bfloat16)
+                torch_dist.all_reduce(w, group=group)
+                buf.copy_(w).div_(self.world)
+            else:
+                torch_dist.all_reduce(buf, group=group)
                 buf.div_(self.world)
+
+
+def _subtract(runs, done) -> list[list[int]]:
+    """The parts of the ``[s, e)`` runs not covered by the sorted, disjoint ``done`` intervals."""
+    out = []
+    for s, e in runs:
+        cur = s
+        for ds, de in done:
+            if de <= cur or ds >= e:
+                continue
+            if ds > cur:
+                out.append([cur, ds])
+            cur = max(cur, de)
+        if cur < e:
+            out.append([cur, e])
+    return out
+
+
+def _runs(infos) -> list[list[int]]:
+    """Contiguous flat-buffer runs covering the parameters ``infos`` (gaps of alignment padding merged)."""
+    runs = []
+    for info in sorted(infos, key=lambda i: i.offset):
+        s, e = info.offset, info.offset + info.numel
+        if runs and runs[-1][1] >= s - 64:
+            runs[-1][1] = max(runs[-1][1], e)
+        else:
+            runs.append([s, e])
+    return runs
 
 
 _CTX: DistContext | None = None

@@ -29,6 +29,8 @@ from .dist import DistContext
 
 
 class ZeroDistContext(DistContext):
+    supports_overlap = False  # the reduce-scatter runs once, after backward
+
     @property
     def store_pad(self) -> int:
         return 64 * self.world

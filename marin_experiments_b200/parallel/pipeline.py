@@ -326,11 +326,11 @@ class PipelineTrainer:
             st.master[i.offset:i.offset + i.numel].copy_(v)
         return live
 
-    def run_async(self, batches, n_ticks: int) -> list[float]:
+    def run_async(self, batches, n_ticks: int, as_tensors: bool = False) -> list:
         """Async 1F1B without flush over a stream of microbatches (each ``batches`` item is one
         microbatch). Stage ``s`` keeps ``P - 1 - s`` forwards in flight and updates its weights after
         every backward; each backward uses the weights of its own forward. Returns the last stage's
-        per-microbatch losses."""
+        per-microbatch losses (device tensors with ``as_tensors``, else floats)."""
         if self.mode != "async":
             raise RuntimeError("run_async needs mode='async'")
         from ..ops import cuda_fns  # noqa: F401
@@ -377,7 +377,7 @@ class PipelineTrainer:
                 p.wait()
         finally:
             self.M = saveM
-        return [float(x) for x in losses]
+        return losses if as_tensors else [float(x) for x in losses]
 
 
 class _nullctx:

@@ -125,6 +125,8 @@ class Trainer:
             extra["recurrence"] = self.model.sample_recurrence(self._rng)
         for i in range(n_micro):
             sl = slice(i * mb, (i + 1) * mb)
+            if i == n_micro - 1 and self.dist is not None and hasattr(self.dist, "arm_overlap"):
+                self.dist.arm_overlap()  # the last backward starts the gradient reductions
             w = lw[sl] if lw is not None else default_loss_weight(mb, s, self.device)
             with nvtx_range(f"microbatch{i}"):
                 loss, met = self.model.next_token_loss(tokens[sl], w, None if seg is None else seg[sl],

@@ -20,6 +20,7 @@ def rel(a, b):
     (96, 2, 2, 384, 200, False),
     (128, 2, 1, 256, 0, True),
     (96, 4, 4, 200, 0, False),
+    (96, 2, 2, 2048, 0, False),  # the benchmark model's sequence length and head size
 ])
 def test_fa_fwd_sm100(hd, h, hkv, s, window, segs):
     from marin_experiments_b200.ops._ext import check_kernel_errors, err_flag, ext
@@ -54,6 +55,7 @@ def test_fa_fwd_sm100(hd, h, hkv, s, window, segs):
     (96, 2, 2, 384, 200, False, False),
     (128, 2, 1, 256, 0, True, False),
     (96, 4, 4, 200, 0, False, True),
+    (96, 2, 2, 2048, 0, False, False),  # the benchmark model's sequence length and head size
 ])
 def test_fa_bwd_sm100(hd, h, hkv, s, window, segs, acc):
     """tcgen05 backward vs the fp32 oracle's autograd gradients (and dV accumulation into an

@@ -1,0 +1,73 @@
+"""Data-parallel gradient reduction overlapped with backward (2 GPUs, NCCL): the same parameters
+after two steps as reducing everything after backward, with fp32 and bf16 wire formats."""
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+MOE = dict(vocab_size=2048, hidden_dim=256, intermediate_dim=256, shared_expert_intermediate_dim=512, num_experts=8,
+           num_experts_per_token=2, num_layers=3, num_heads=4, num_kv_heads=4, head_dim=64, max_seq_len=256,
+           sliding_window=256, capacity_factor=2.0)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from marin_experiments_b200.config import GrugModelConfig, GrugRunConfig, GrugTrainerConfig, TrainerConfig
+        from marin_experiments_b200.optim import GrugMoeAdamHConfig
+        from marin_experiments_b200.parallel import dist as pdist
+        from marin_experiments_b200.train.trainer import Trainer
+
+        out = {}
+        for name, overlap, wire in (("serial", "0", "fp32"), ("overlap", "1", "fp32"), ("overlap_bf16", "1", "bf16")):
+            os.environ["MXK_DP_OVERLAP"], os.environ["MXK_DP_WIRE"] = overlap, wire
+            pdist._CTX = None
+            ctx = pdist.init(ep_size=1)
+            run = GrugRunConfig(model=GrugModelConfig(**MOE), optimizer=GrugMoeAdamHConfig(warmup=0.0),
+                                trainer=GrugTrainerConfig(trainer=TrainerConfig(num_train_steps=10, seed=0)))
+            tr = Trainer(run, device=f"cuda:{rank}", micro_batch=2, dist=ctx)
+            assert getattr(ctx, "_overlap_on", False) == (overlap == "1")
+            g = torch.Generator().manual_seed(10 + rank)
+            for _ in range(2):
+                tr.train_step({"tokens": torch.randint(0, 2048, (4, 256), generator=g)})
+            torch.cuda.synchronize()
+            out[name] = tr.store.master.cpu()
+        q.put((rank, {k: ((v - out["serial"]).norm() / out["serial"].norm()).item() for k, v in out.items()}))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_overlapped_grad_sync_matches_serial():
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert res[r]["overlap"] < 1e-6, res[r]
+        assert res[r]["overlap_bf16"] < 1e-2, res[r]

@@ -315,7 +315,8 @@ def test_newton_schulz_tcgen05_matches_fp32(monkeypatch):
     from marin_experiments_b200.optim.fused import _ns_quintic
 
     torch.manual_seed(0)
-    for shape in [(256, 512), (768, 256), (1, 128, 192), (3, 128, 192)]:
+    for shape in [(256, 512), (768, 256), (1, 128, 192), (3, 128, 192), (8, 256, 384), (4, 320, 128),
+                  (2, 192, 96)]:
         g = torch.randn(*shape, device="cuda")
         monkeypatch.setenv("MXK_NS_FP32", "1")
         ref = _ns_quintic(g, 5)
@@ -323,8 +324,10 @@ def test_newton_schulz_tcgen05_matches_fp32(monkeypatch):
         n0 = ext().launch_count()
         out = _ns_quintic(g, 5)
         torch.cuda.synchronize()
-        # single matrices run the tcgen05 GEMMs; stacks run batched fp32 products
-        assert (ext().launch_count() > n0) == (len(shape) == 2 or shape[0] == 1)
+        # single matrices and stacks with a short side that is a multiple of 128 run the tcgen05
+        # GEMMs (grouped for stacks); other stacks run batched fp32 products
+        on_tc = len(shape) == 2 or shape[0] == 1 or min(shape[-2:]) % 128 == 0
+        assert (ext().launch_count() > n0) == on_tc
         assert out.shape == g.shape and out.dtype == torch.float32
         assert ((out - ref).norm() / ref.norm()).item() < 0.1
         sv = torch.linalg.svdvals(out.reshape(-1, *shape[-2:]).double())
