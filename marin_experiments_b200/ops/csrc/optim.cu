@@ -22,12 +22,16 @@ namespace {
 
 constexpr int kHp = 9;
 
+// One work unit: `len` elements from flat offset `start` (parameter / gradient index k) of matrix
+// `mat` in group `group`. The moments of element k live at m[k - moff]: a sharded optimizer keeps
+// moments only for its ranges, packed back to back, and each chunk names its range's shift.
 struct Chunk {
   long long start;
   int len;
   int mat;
   int group;
   int pad;
+  long long moff;
 };
 
 __device__ __forceinline__ float block_sum(float v, float* sh) {
@@ -154,7 +158,7 @@ __global__ void __launch_bounds__(256) moments_kernel(const Chunk* __restrict__ 
   const Chunk c = chunks[blockIdx.x];
   const float* h = hp + c.group * kHp;
   Moments f;
-  f.grad = grad; f.m = m; f.v = v; f.p = p; f.pb = pb;
+  f.grad = grad; f.m = m - c.moff; f.v = v - c.moff; f.p = p; f.pb = pb;
   f.kind = (int)h[0];
   f.lr = h[1]; f.b1 = h[2]; f.b2 = h[3]; f.eps = h[4]; f.wd = h[5];
   f.ibc1 = 1.f / h[6]; f.ibc2 = 1.f / h[7];
@@ -219,7 +223,7 @@ __global__ void __launch_bounds__(256) adamh_apply_kernel(const Chunk* __restric
   const double a = (double)h[1] * pn / un;
   const double nn2 = spp - 2.0 * a * spu + a * a * suu;
   Apply f;
-  f.m = m; f.v = v; f.p = p; f.pb = pb;
+  f.m = m - c.moff; f.v = v - c.moff; f.p = p; f.pb = pb;
   f.ibc1 = 1.f / h[6]; f.ibc2 = 1.f / h[7]; f.eps = h[4];
   f.step = (float)a;
   f.rescale = nn2 > 0.0 ? (float)(pn / sqrt(nn2)) : 1.f;

@@ -22,7 +22,9 @@ import torch
 
 CHUNK = 32768
 HP = 9
-_CHUNK_DTYPE = np.dtype([("start", "<i8"), ("len", "<i4"), ("mat", "<i4"), ("group", "<i4"), ("pad", "<i4")])
+# (flat start, length, matrix id, group, unused, moment shift: element k's moments at m[k - moff])
+_CHUNK_DTYPE = np.dtype([("start", "<i8"), ("len", "<i4"), ("mat", "<i4"), ("group", "<i4"), ("pad", "<i4"),
+                         ("moff", "<i8")])
 
 
 def _ns_quintic(g: torch.Tensor, steps: int) -> torch.Tensor:
@@ -135,10 +137,22 @@ class FusedOptimizer:
             self.gnorm2 = torch.zeros(len(self.names), dtype=torch.float64, device=dev)
             self.mat_sums = torch.zeros(self.mat_count, 3, dtype=torch.float64, device=dev)
 
+    def _shard_ranges(self) -> list[tuple[int, int, int]]:
+        """(lo, hi, moment shift) of every flat range this optimizer keeps state for: the whole
+        buffer, or the sharded ranges with their moments packed back to back."""
+        if self.shard is None:
+            return [(0, 1 << 62, 0)]
+        out, pos = [], 0
+        for lo, hi in self.shard:
+            out.append((lo, hi, lo - pos))
+            pos += hi - lo
+        return out
+
     def _build_chunks(self) -> None:
-        """Chunk table over the adam / adamh groups: (flat start, length, matrix id, group), each at
-        most CHUNK elements, restricted to ``self.shard`` when the optimizer state is sharded."""
-        lo, hi = self.shard if self.shard is not None else (0, 1 << 62)
+        """Chunk table over the adam / adamh groups: (flat start, length, matrix id, group, moment
+        shift), each at most CHUNK elements, restricted to the shard ranges when the optimizer state
+        is sharded."""
+        shards = self._shard_ranges()
         rows = []
         mat = 0
         for gi, name in enumerate(self.names):
@@ -149,9 +163,10 @@ class FusedOptimizer:
                 mats = info.matrices if g["kind"] == "adamh" else [[(info.offset, info.numel)]]
                 for ranges in mats:
                     for start, length in ranges:
-                        a, b = max(start, lo), min(start + length, hi)
-                        for c0 in range(a, b, CHUNK):
-                            rows.append((c0, min(CHUNK, b - c0), mat, gi, 0))
+                        for lo, hi, moff in shards:
+                            a, b = max(start, lo), min(start + length, hi)
+                            for c0 in range(a, b, CHUNK):
+                                rows.append((c0, min(CHUNK, b - c0), mat, gi, 0, moff))
                     mat += 1
         self.mat_count = max(mat, 1)
         arr = np.array(rows, dtype=_CHUNK_DTYPE) if rows else np.zeros(0, dtype=_CHUNK_DTYPE)
@@ -175,14 +190,20 @@ class FusedOptimizer:
                     mat += 1
         return out
 
-    def set_shard(self, lo: int, hi: int) -> None:
-        """Keep optimizer state only for the flat range [lo, hi) (ZeRO): the moments shrink to the
-        shard, the chunk table covers it, and ``norm_hook`` / ``mat_hook`` must sum the per-group
-        squared norms and the AdamH matrix sums over the ranks holding the other shards."""
+    def set_shard(self, lo: int, hi: int, *more: tuple[int, int]) -> None:
+        """Keep optimizer state only for the flat range [lo, hi) and any ``more`` ranges (ZeRO; with
+        expert parallelism the rank's expert region is a second range): the moments shrink to the
+        ranges (packed back to back), the chunk table covers them, and ``norm_hook`` / ``mat_hook``
+        must sum the per-group squared norms and the AdamH matrix sums over the ranks holding the
+        other shards. Range bounds are multiples of 4 (vector access of the moments)."""
         if self.muon_infos:
             raise NotImplementedError("Muon with sharded optimizer state")
-        self.shard = (int(lo), int(hi))
-        self.m = torch.zeros(hi - lo, dtype=torch.float32, device=self.store.device)
+        ranges = [(int(lo), int(hi))] + [(int(a), int(b)) for a, b in more]
+        if any(a % 4 or b % 4 or b < a for a, b in ranges):
+            raise ValueError(f"shard ranges must be ordered multiples of 4: {ranges}")
+        self.shard = ranges
+        n = sum(b - a for a, b in ranges)
+        self.m = torch.zeros(n, dtype=torch.float32, device=self.store.device)
         self.v = torch.zeros_like(self.m)
         self._build_chunks()
 
@@ -224,7 +245,7 @@ class FusedOptimizer:
             if self.norm_hook is not None:
                 self.norm_hook(self.gnorm2, self.names)
             self.mat_sums.zero_()
-            off = self.shard[0] if self.shard is not None else 0
+            off = 0  # the chunks carry their moment shifts
             if self.shard is None and self.mat_hook is None:
                 ext().opt_step(self.chunks, self.nchunks, self.hp, self.gnorm2, grad_scale, st.grad, self.m, self.v,
                                st.master, st.compute, self.mat_sums, self.has_adamh, 0, 0)
@@ -307,9 +328,8 @@ class FusedOptimizer:
         st = self.store
         b1, b2, eps = cfg.beta1, cfg.beta2, cfg.epsilon
         bc1, bc2 = 1 - b1 ** t, 1 - b2 ** t
-        off = self.shard[0] if self.shard is not None else 0
         gn = torch.zeros(len(self.names), dtype=torch.float64)
-        for start, ln, _, gi, _ in self._rows:
+        for start, ln, _, gi, _, _ in self._rows:
             gn[gi] += float((st.grad[start:start + ln].double() * grad_scale).pow(2).sum())
         if self.norm_hook is not None:
             self.norm_hook(gn, self.names)
@@ -323,10 +343,10 @@ class FusedOptimizer:
             scale.append(s_)
         sums = torch.zeros(self.mat_count, 3, dtype=torch.float64)
         upd = {}
-        for start, ln, mat, gi, _ in self._rows:
+        for start, ln, mat, gi, _, moff in self._rows:
             g = self.groups[self.names[gi]]
             sl = slice(start, start + ln)
-            ml = slice(start - off, start - off + ln)
+            ml = slice(start - moff, start - moff + ln)
             gr = st.grad[sl] * scale[gi]
             self.m[ml].mul_(b1).add_(gr, alpha=1 - b1)
             self.v[ml].mul_(b2).addcmul_(gr, gr, value=1 - b2)
@@ -342,7 +362,7 @@ class FusedOptimizer:
                 upd[start] = u
         if self.mat_hook is not None:
             self.mat_hook(sums)
-        for start, ln, mat, gi, _ in self._rows:
+        for start, ln, mat, gi, _, _ in self._rows:
             if start not in upd:
                 continue
             lr = self.lr_fns[self.names[gi]](self.step_count)

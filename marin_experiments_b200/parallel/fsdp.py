@@ -1,23 +1,35 @@
-"""Fully sharded data parallelism over the flat parameter store (ZeRO stage 2).
+"""Fully sharded data parallelism over the flat parameter store (ZeRO stage 2), alone or composed
+with expert parallelism.
 
 The reference shards every weight over the ``data`` mesh axis and lets XLA insert the parameter
 all-gather and gradient reduce-scatter (megagpt-speedrun/model.py:247-250,340-342; explicit form in
-grug-moe-pp/pipeline.py:434-480). Here the unit of sharding is the flat fp32 buffer of the
-``ParamStore``: rank ``r`` owns the range ``[r * n / W, (r + 1) * n / W)``.
+grug-moe-pp/pipeline.py:434-480), next to the ``expert`` axis that shards the routed experts
+(megagpt-speedrun/model.py:245-251). Here the unit of sharding is the flat fp32 buffer of the
+``ParamStore``.
+
+* Pure data parallelism (``ep_size == 1``): rank ``r`` owns ``[r * n / W, (r + 1) * n / W)`` of the
+  whole buffer.
+* With expert parallelism (``ep_size == W``): the store lays the routed experts out last
+  (``ParamStore(expert_last=True)``); the replicated prefix ``[0, R)`` is sharded over the ranks as
+  above, and each rank keeps the full optimizer state of its own experts ``[R, n)`` -- those are
+  already distinct on every rank.
 
 One step:
 
 1. backward accumulates full-size fp32 gradients (bucketable, as in plain data parallelism);
-2. ``grad_sync`` reduce-scatters them in place, so each rank holds the mean gradient of its range;
-3. the fused optimizer updates only its range: the moments exist only for the range, the per-group
+2. ``grad_sync`` reduce-scatters the sharded region in place, so each rank holds the mean gradient
+   of its range; expert gradients (already summed over every source rank's tokens) are scaled to
+   the mean;
+3. the fused optimizer updates only its ranges: the moments exist only for them, the per-group
    squared gradient norms and the AdamH per-matrix sums ``(S_pp, S_pu, S_uu)`` are partial and
-   all-reduced between the kernel's two passes (a few KB);
-4. ``post_step`` all-gathers the updated fp32 range into every rank's master buffer and refreshes the
-   bf16 compute copy.
+   all-reduced between the kernel's two passes (a few KB) -- replicated matrices are split over
+   the ranks' shards and summed; each expert matrix lives whole on its rank, whose sums are kept
+   (the group norms sum over all ranks: every expert is counted once);
+4. ``post_step`` all-gathers the updated fp32 shards into every rank's master buffer and refreshes
+   the bf16 compute copy.
 
-Optimizer memory per rank drops from ``8 n`` to ``8 n / W`` bytes; the bytes on the wire equal a
-gradient all-reduce. Experts are replicated (pure data parallelism); combine with expert parallelism
-by sharding the replicated parameters only, which this context does not do.
+Optimizer memory per rank for the sharded region drops from ``8 n`` to ``8 n / W`` bytes; the
+bytes on the wire equal a gradient all-reduce.
 """
 
 from __future__ import annotations
@@ -35,58 +47,91 @@ class ZeroDistContext(DistContext):
     def store_pad(self) -> int:
         return 64 * self.world
 
+    @property
+    def expert_last(self) -> bool:
+        return self.ep_size > 1
+
+    def _sharded_end(self, store) -> int:
+        """End of the region sharded over the ranks: the replicated prefix (experts after it)."""
+        return store.expert_start if self.ep_size > 1 else store.numel
+
     def shard_range(self, numel: int) -> tuple[int, int]:
         per = numel // self.world
         return self.rank * per, (self.rank + 1) * per
 
     def setup_model(self, trainer) -> None:
-        if self.ep_size != 1:
-            raise ValueError("ZeRO data parallelism replicates the experts (ep_size must be 1)")
+        if self.ep_size not in (1, self.world):
+            raise ValueError("ZeRO shards the replicated parameters over all ranks and keeps each rank's "
+                             "experts local: ep_size must be 1 or the world size")
         super().setup_model(trainer)
         st = trainer.store
         align = 64 * self.world
-        if st.numel % align:
-            raise ValueError(f"flat store size {st.numel} is not a multiple of {align}")
+        if self._sharded_end(st) % align:
+            raise ValueError(f"sharded region {self._sharded_end(st)} is not a multiple of {align}")
 
     def setup_optimizer(self, trainer) -> None:
         opt = getattr(trainer.opt, "inner", trainer.opt)
-        lo, hi = self.shard_range(trainer.store.numel)
-        opt.set_shard(lo, hi)
+        st = trainer.store
+        end = self._sharded_end(st)
+        lo, hi = self.shard_range(end)
+        extra = [(end, st.numel)] if self.ep_size > 1 and st.numel > end else []
+        opt.set_shard(lo, hi, *extra)
         group = self.batch_group
 
         def allreduce(t):
             tdist.all_reduce(t, group=group)
 
+        # AdamH matrix sums: replicated matrices are split over the ranks' shards (sum them); an
+        # expert matrix id names a different expert on every rank and is complete locally.
+        local = opt.matrix_ids(lambda i: i.sharded_over == "expert") if self.ep_size > 1 else []
+        local_idx = torch.tensor(local, dtype=torch.long, device=st.device) if local else None
+
+        def mat_hook(sums):
+            if local_idx is None:
+                allreduce(sums)
+                return
+            keep = sums.index_select(0, local_idx)
+            allreduce(sums)
+            sums.index_copy_(0, local_idx, keep)
+
         opt.norm_hook = lambda g2, names: allreduce(g2)
-        opt.mat_hook = allreduce
+        opt.mat_hook = mat_hook
         self._shard = (lo, hi)
+        self._end = end
 
     def grad_sync(self, trainer) -> None:
         st = trainer.store
         lo, hi = self._shard
+        region = st.grad[: self._end]
         if self.backend == "nccl":
-            tdist.reduce_scatter_tensor(st.grad[lo:hi], st.grad, op=tdist.ReduceOp.SUM, group=self.batch_group)
+            tdist.reduce_scatter_tensor(st.grad[lo:hi], region, op=tdist.ReduceOp.SUM, group=self.batch_group)
         else:  # gloo has no reduce-scatter: all-reduce and keep the range
-            tdist.all_reduce(st.grad, group=self.batch_group)
+            tdist.all_reduce(region, group=self.batch_group)
         st.grad[lo:hi].div_(self.world)
+        if self._end < st.numel:  # this rank's experts: sum over all ranks' tokens -> mean
+            st.grad[self._end:].div_(self.world)
 
     def post_step(self, trainer) -> None:
         st = trainer.store
         lo, hi = self._shard
+        region = st.master[: self._end]
         if self.backend == "nccl":
-            tdist.all_gather_into_tensor(st.master, st.master[lo:hi].clone(), group=self.batch_group)
+            tdist.all_gather_into_tensor(region, st.master[lo:hi].clone(), group=self.batch_group)
         else:
-            parts = list(st.master.chunk(self.world))
+            parts = list(region.chunk(self.world))
             tdist.all_gather(parts, st.master[lo:hi].clone(), group=self.batch_group)
-            st.master.copy_(torch.cat(parts))
+            region.copy_(torch.cat(parts))
         st.sync_compute()
 
 
-def init_zero(timeout_s: float = 600.0) -> ZeroDistContext:
+def init_zero(timeout_s: float = 600.0, ep_size: int = 1) -> ZeroDistContext:
+    """ZeRO data parallelism over every rank; ``ep_size`` = the world size also shards the routed
+    experts over the ranks (expert parallelism)."""
     from . import dist as pdist
 
-    base = pdist.init(ep_size=1, timeout_s=timeout_s)
-    ctx = ZeroDistContext(rank=base.rank, world=base.world, ep_size=1, backend=base.backend,
-                          batch_group=base.batch_group, ep_group=base.ep_group, ep_rank=0)
+    base = pdist.init(ep_size=ep_size, timeout_s=timeout_s)
+    ctx = ZeroDistContext(rank=base.rank, world=base.world, ep_size=base.ep_size, backend=base.backend,
+                          batch_group=base.batch_group, ep_group=base.ep_group, ep_rank=base.ep_rank,
+                          expert_dp_group=base.expert_dp_group)
     pdist._CTX = ctx
     return ctx

@@ -117,11 +117,19 @@ def _leaves(trainer, buffers: dict[str, torch.Tensor], ep_size: int, ep_rank: in
     gname = getattr(trainer.model, "global_name", lambda n: n)
     n_store = trainer.store.numel
     shard = _opt_shard(trainer)
+    local_lo = getattr(trainer.store, "expert_start", None)
     for prefix, buf in buffers.items():
         if buf.numel() != n_store:
-            # optimizer state kept only for this rank's flat range (ZeRO): one leaf per range
-            lo = shard[0]
-            out.append(_Leaf(f"{prefix}/__flat__", buf, 0, buf.numel(), (buf.numel(),), (n_store,), lo, True))
+            # optimizer state kept only for this rank's flat ranges (ZeRO): one leaf per range, at its
+            # packed position in the moment buffer. Ranges inside the expert region hold this
+            # expert-parallel rank's own experts, so their leaf is named per expert-parallel rank.
+            pos = 0
+            for lo, hi in shard:
+                key = f"{prefix}/__flat__"
+                if local_lo is not None and lo >= local_lo and ep_size > 1:
+                    key = f"{prefix}/__flat_ep{ep_rank}__"
+                out.append(_Leaf(key, buf, pos, hi - lo, (hi - lo,), (n_store,), lo, True))
+                pos += hi - lo
             continue
         for info in trainer.store.infos:
             sharded = info.sharded_over == "expert" and ep_size > 1

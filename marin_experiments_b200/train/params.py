@@ -90,9 +90,18 @@ def default_matrices(name: str, shape: tuple[int, ...], offset: int, module: nn.
     return [[(offset, numel)]]
 
 
+def _is_expert(module, leaf: str, p) -> bool:
+    return getattr(module, "expert_range", None) is not None and leaf in ("w_gate_up", "w_down") and p.dim() == 3
+
+
 class ParamStore:
+    """``expert_last``: lay out every routed-expert weight after all other parameters, with the
+    expert region starting at ``expert_start`` (a multiple of ``pad_multiple``), so the replicated
+    parameters form one prefix that can be sharded over data-parallel ranks while each
+    expert-parallel rank keeps its own experts' range (ZeRO with expert parallelism)."""
+
     def __init__(self, model: nn.Module, device: torch.device | str, *, compute_dtype=torch.bfloat16,
-                 moments: int = 2, pad_multiple: int = ALIGN):
+                 moments: int = 2, pad_multiple: int = ALIGN, expert_last: bool = False):
         self.device = torch.device(device)
         self.cuda = self.device.type == "cuda"
         self.compute_dtype = compute_dtype if self.cuda else torch.float32
@@ -100,7 +109,19 @@ class ParamStore:
         self.infos: list[ParamInfo] = []
         self._params: dict[str, nn.Parameter] = {}
         off = 0
-        for name, p in model.named_parameters():
+        named = list(model.named_parameters())
+        self.expert_start = None
+        if expert_last:
+            def expert(item):
+                name, p = item
+                return _is_expert(modules.get(name.rsplit(".", 1)[0] if "." in name else ""), name.rsplit(".", 1)[-1], p)
+
+            named = [x for x in named if not expert(x)] + [x for x in named if expert(x)]
+            n_rep = sum(1 for x in named if not expert(x))
+        for idx, (name, p) in enumerate(named):
+            if expert_last and idx == n_rep:  # start of the expert region
+                off = (off + pad_multiple - 1) // pad_multiple * pad_multiple
+                self.expert_start = off
             mod_name = name.rsplit(".", 1)[0] if "." in name else ""
             module = modules.get(mod_name)
             leaf = name.rsplit(".", 1)[-1]
@@ -109,7 +130,7 @@ class ParamStore:
                 off = (off + ALIGN - 1) // ALIGN * ALIGN
             info = ParamInfo(name, tuple(p.shape), off, p.numel(), p.requires_grad)
             info.matrices = default_matrices(name, tuple(p.shape), off, module)
-            if getattr(module, "expert_range", None) is not None and leaf in ("w_gate_up", "w_down") and p.dim() == 3:
+            if _is_expert(module, leaf, p):
                 info.sharded_over = "expert"
             tp = getattr(module, "tp", None)
             if tp is not None and tp.size > 1 and leaf in getattr(module, "tp_sharded_params", ()):
@@ -118,6 +139,8 @@ class ParamStore:
             self._params[name] = p
             off += p.numel()
         self.numel = (off + pad_multiple - 1) // pad_multiple * pad_multiple
+        if expert_last and self.expert_start is None:  # no experts: the region is empty
+            self.expert_start = self.numel
         dev = self.device
         self.master = torch.zeros(self.numel, dtype=torch.float32, device=dev)
         self.grad = torch.zeros(self.numel, dtype=torch.float32, device=dev)

@@ -71,7 +71,8 @@ class Trainer:
             else:
                 model = Transformer(cfg, local_experts=local, **self.model_kwargs)
         self.model = model
-        self.store = ParamStore(model, self.device, pad_multiple=getattr(self.dist, "store_pad", 64))
+        self.store = ParamStore(model, self.device, pad_multiple=getattr(self.dist, "store_pad", 64),
+                                expert_last=getattr(self.dist, "expert_last", False))
         init_store_weights(self.store, cfg, self.seed, model)
         if self.dist is not None:
             self.dist.setup_model(self)

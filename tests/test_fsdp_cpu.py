@@ -104,3 +104,48 @@ def test_data_and_expert_parallel_match_single_process():
                     n = got.shape[0]
                     w = w[v["e"] * n:(v["e"] + 1) * n]
                 assert torch.allclose(got, w, atol=1e-6, rtol=1e-5), (world, ep, r, name)
+
+
+def _ep_rank(rank, world, zero, ckpt):
+    """Expert parallelism (EP = world) with or without ZeRO over the replicated parameters."""
+    import torch.distributed as tdist
+
+    from marin_experiments_b200.parallel import dist as pdist
+    from marin_experiments_b200.parallel.fsdp import init_zero
+
+    ctx = init_zero(120, ep_size=world) if zero else pdist.init(ep_size=world, timeout_s=120)
+    try:
+        tr = _trainer(ctx, "adamh")
+        g = torch.Generator().manual_seed(21 + rank)
+        for _ in range(2):
+            tr.train_step({"tokens": torch.randint(0, 512, (2, 32), generator=g)})
+        out = {"params": {i.name: tr.store.master_view(i).numpy().copy() for i in tr.store.infos},
+               "m_numel": tr.opt.m.numel(), "store": tr.store.numel,
+               "expert_start": tr.store.expert_start}
+        if ckpt:
+            from marin_experiments_b200.train.checkpoint import load_checkpoint, save_checkpoint
+
+            save_checkpoint(tr, ckpt)
+            tdist.barrier()
+            fresh = _trainer(ctx, "adamh")
+            load_checkpoint(fresh, ckpt)
+            out["m_equal"] = bool(torch.equal(fresh.opt.m, tr.opt.m) and torch.equal(fresh.opt.v, tr.opt.v))
+            out["p_equal"] = bool(torch.equal(fresh.store.master, tr.store.master))
+        return out
+    finally:
+        pdist.shutdown()
+
+
+def test_zero_with_expert_parallelism(tmp_path):
+    """ZeRO over the replicated parameters + experts sharded by expert parallelism: the same weights
+    as expert parallelism with replicated optimizer state; the replicated moments are split over the
+    ranks and each rank keeps its own experts' moments; the sharded checkpoint round-trips."""
+    a = run_ranks(_ep_rank, 2, True, str(tmp_path / "step-2"))
+    b = run_ranks(_ep_rank, 2, False, None)
+    for r in range(2):
+        assert a[r]["m_equal"] and a[r]["p_equal"]
+        rep, n = a[r]["expert_start"], a[r]["store"]
+        assert rep is not None and a[r]["m_numel"] == rep // 2 + (n - rep)
+        for name, want in b[r]["params"].items():
+            assert torch.allclose(torch.from_numpy(a[r]["params"][name]), torch.from_numpy(want), atol=1e-5,
+                                  rtol=1e-4), name

@@ -48,3 +48,40 @@ def test_zero_matches_dp_on_gpu():
         ua, ub = torch.from_numpy(a[r]["upd"]), torch.from_numpy(b[r]["upd"])
         err = ((ua - ub).norm() / ub.norm()).item()
         assert err < 0.05, (r, err)
+
+
+def _ep_rank(rank, world, zero):
+    from marin_experiments_b200.config import GrugModelConfig, GrugRunConfig, GrugTrainerConfig, TrainerConfig
+    from marin_experiments_b200.optim import GrugMoeAdamHConfig
+    from marin_experiments_b200.parallel import dist as pdist
+    from marin_experiments_b200.parallel.fsdp import init_zero
+    from marin_experiments_b200.train.trainer import Trainer
+
+    torch.cuda.set_device(rank)
+    ctx = init_zero(120, ep_size=world) if zero else pdist.init(ep_size=world, timeout_s=120)
+    try:
+        run = GrugRunConfig(model=GrugModelConfig(**CFG), optimizer=GrugMoeAdamHConfig(warmup=0.0),
+                            trainer=GrugTrainerConfig(trainer=TrainerConfig(num_train_steps=10, seed=0)))
+        tr = Trainer(run, device=f"cuda:{rank}", dist=ctx)
+        init = {i.name: tr.store.master_view(i).clone() for i in tr.store.infos}
+        tok = torch.randint(0, 4096, (2, 256), generator=torch.Generator().manual_seed(rank)).pin_memory()
+        tr.train_step({"tokens": tok})
+        torch.cuda.synchronize()
+        upd = {i.name: (tr.store.master_view(i) - init[i.name]).cpu().numpy() for i in tr.store.infos}
+        return {"upd": upd, "m_numel": tr.opt.m.numel(), "n": tr.store.numel, "rep": tr.store.expert_start}
+    finally:
+        pdist.shutdown()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_zero_with_expert_parallelism_on_gpu():
+    """ZeRO over the replicated parameters with the experts sharded by expert parallelism (the
+    peer-memory exchange): the same update as expert parallelism with replicated optimizer state."""
+    a = run_ranks(_ep_rank, 2, True, timeout=300)
+    b = run_ranks(_ep_rank, 2, False, timeout=300)
+    assert a[0]["m_numel"] == a[0]["rep"] // 2 + (a[0]["n"] - a[0]["rep"])
+    for r in range(2):
+        num = sum(float(((torch.from_numpy(a[r]["upd"][k]) - torch.from_numpy(v)) ** 2).sum())
+                  for k, v in b[r]["upd"].items())
+        den = sum(float((torch.from_numpy(v) ** 2).sum()) for v in b[r]["upd"].values())
+        assert (num / den) ** 0.5 < 0.05, (r, (num / den) ** 0.5)
