@@ -71,6 +71,25 @@ void launch_opt_step(const void* chunks, int nchunks, const float* hp, const dou
                      const float* grad, float* m, float* v, float* p, void* pb, double* mat_sums, int has_adamh, int phase,
                      cudaStream_t st);
 void launch_ema(float* dst, const float* src, long n, float beta, cudaStream_t st);
+
+// Delayed-gradient optimizer passes (delayed.cu). Rings are [tau_max, n] (null when tau_max == 0).
+struct DelayArgs {
+  float* grad;
+  const float* master;
+  float* grad_ring;
+  float* param_ring;  // DC-ASGD correctors only
+  float* v_ema;       // dc_asgd_ema only
+  float* m_raw;       // raw momentum of the forward predictors, or null
+  float* before;      // snapshot of the masters (the update is measured against it)
+  long long n;
+  long long t;
+  int tau_max;
+  int corrector;  // 0 none, 1 dc_asgd, 2 dc_asgd_ema
+  float dc_lambda, dc_beta2, pred_beta, grad_scale;
+};
+void launch_delayed_prep(const void* chunks, int nchunks, const DelayArgs& a, cudaStream_t st);
+void launch_delayed_finish(float* master, float* before_upd, void* compute, long long n, float damp,
+                           cudaStream_t st);
 void launch_cast_bf16(const float* src, void* dst, long n, cudaStream_t st);
 
 // attention.cu

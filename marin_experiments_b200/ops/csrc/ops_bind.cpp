@@ -1,4 +1,5 @@
 // Torch bindings of the row-wise, attention, MoE and optimizer kernels.
+#include <algorithm>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -332,6 +333,43 @@ void opt_step(const Tensor& chunks, int64_t nchunks, const Tensor& hp, const Opt
                        stream());
 }
 
+void delayed_prep(const Tensor& chunks, int64_t nchunks, const Tensor& grad, const Tensor& master,
+                  const OptT& grad_ring, const OptT& param_ring, const OptT& v_ema, const OptT& m_raw,
+                  const Tensor& before, int64_t t, int64_t tau_max, int64_t corrector, double dc_lambda,
+                  double dc_beta2, double pred_beta, double grad_scale) {
+  cuda_f32(grad, "grad"); cuda_f32(master, "master"); cuda_f32(before, "before");
+  const int64_t n = grad.numel();
+  need(master.numel() == n && before.numel() == n, "delayed_prep: buffer sizes differ");
+  need(tau_max == 0 || (grad_ring.has_value() && grad_ring->numel() == tau_max * n), "delayed_prep: gradient ring");
+  need(corrector == 0 || (param_ring.has_value() && param_ring->numel() == tau_max * n), "delayed_prep: weight ring");
+  need(corrector != 2 || (v_ema.has_value() && v_ema->numel() == n), "delayed_prep: curvature EMA");
+  need(!m_raw.has_value() || m_raw->numel() == n, "delayed_prep: raw momentum");
+  c10::cuda::CUDAGuard g(grad.device());
+  mxk::DelayArgs a{};
+  a.grad = grad.data_ptr<float>();
+  a.master = master.data_ptr<float>();
+  a.grad_ring = ptr<float>(grad_ring);
+  a.param_ring = ptr<float>(param_ring);
+  a.v_ema = ptr<float>(v_ema);
+  a.m_raw = ptr<float>(m_raw);
+  a.before = before.data_ptr<float>();
+  a.n = n;
+  a.t = t;
+  a.tau_max = (int)std::max<int64_t>(tau_max, 1);
+  a.corrector = (int)corrector;
+  a.dc_lambda = (float)dc_lambda; a.dc_beta2 = (float)dc_beta2; a.pred_beta = (float)pred_beta;
+  a.grad_scale = (float)grad_scale;
+  mxk::launch_delayed_prep(chunks.data_ptr(), nchunks, a, stream());
+}
+
+void delayed_finish(const Tensor& master, const Tensor& before_upd, const OptT& compute, double damp) {
+  cuda_f32(master, "master"); cuda_f32(before_upd, "before_upd");
+  need(master.numel() == before_upd.numel(), "delayed_finish: buffer sizes differ");
+  c10::cuda::CUDAGuard g(master.device());
+  mxk::launch_delayed_finish(master.data_ptr<float>(), before_upd.data_ptr<float>(), ptr<void>(compute),
+                             master.numel(), (float)damp, stream());
+}
+
 void ema(const Tensor& dst, const Tensor& src, double beta) {
   c10::cuda::CUDAGuard g(dst.device());
   mxk::launch_ema(dst.data_ptr<float>(), src.data_ptr<float>(), dst.numel(), (float)beta, stream());
@@ -523,6 +561,8 @@ void register_ops(pybind11::module& m) {
   m.def("opt_sqnorm", &opt_sqnorm);
   m.def("opt_step", &opt_step);
   m.def("ema", &ema);
+  m.def("delayed_prep", &delayed_prep);
+  m.def("delayed_finish", &delayed_finish);
   m.def("cast_bf16", &cast_bf16);
   m.def("flash_bwd_sm100", &flash_bwd_sm100);
   m.def("set_attn_bwd_prof", &set_attn_bwd_prof);

@@ -110,9 +110,51 @@ class DelayedOptimizer:
                 getattr(self, k).copy_(sd[k])
 
     # -------------------------------------------------------------------------------- step
+    def _delay_chunks(self):
+        """(start, len, tau) chunks covering the whole flat buffer (alignment gaps with tau 0)."""
+        import numpy as np
+
+        if getattr(self, "_chunks", None) is None:
+            rows, pos = [], 0
+            for info in sorted(self.store.infos, key=lambda i: i.offset):
+                if info.offset > pos:
+                    rows.append((pos, info.offset - pos, 0))
+                rows.append((info.offset, info.numel, self.taus[info.name]))
+                pos = info.offset + info.numel
+            if pos < self.store.numel:
+                rows.append((pos, self.store.numel - pos, 0))
+            out = []
+            for s0, ln, tau in rows:
+                for c0 in range(s0, s0 + ln, 32768):
+                    out.append((c0, min(32768, s0 + ln - c0), tau))
+            dt = np.dtype([("start", "<i8"), ("len", "<i4"), ("tau", "<i4")])
+            arr = np.array(out, dtype=dt)
+            self._chunks = torch.from_numpy(arr.view(np.uint8).copy()).to(self.store.device)
+            self._nchunks = len(out)
+        return self._chunks, self._nchunks
+
+    @torch.no_grad()
+    def _step_fused(self, grad_scale: float, zero_grad: bool) -> None:
+        """The step as two sm_100a passes around the inner optimizer (``ops/csrc/delayed.cu``)."""
+        from ..ops._ext import ext
+
+        st = self.store
+        chunks, nchunks = self._delay_chunks()
+        cid = {"dc_asgd": 1, "dc_asgd_ema": 2}.get(self.corrector, 0)
+        ext().delayed_prep(chunks, nchunks, st.grad, st.master, self.grad_ring, self.param_ring, self.v_ema,
+                           self.m_raw, self.last_update, self.t, self.tau_max, cid, self.dc_lambda, self.dc_beta2,
+                           self.pred_beta, grad_scale)
+        self.inner.step(grad_scale=grad_scale, zero_grad=False)
+        ext().delayed_finish(st.master, self.last_update, st.compute if self.damp != 1.0 else None, self.damp)
+        self.t += 1
+        if zero_grad:
+            st.zero_grad()
+
     @torch.no_grad()
     def step(self, grad_scale: float = 1.0, zero_grad: bool = True) -> None:
         st = self.store
+        if st.cuda:
+            return self._step_fused(grad_scale, zero_grad)
         g_cur = st.grad.clone()
         if self.tau_max:
             for info in st.infos:

@@ -1,5 +1,5 @@
-"""Data-parallel gradient reduction overlapped with backward (2 GPUs, NCCL): the same parameters
-after two steps as reducing everything after backward, with fp32 and bf16 wire formats."""
+"""Data-parallel gradient reduction overlapped with backward (2 GPUs, NCCL): the same synchronised
+gradients as reducing everything after backward (fp32 wire), and close with the bf16 wire."""
 
 import datetime
 import os
@@ -35,8 +35,10 @@ def _worker(rank, world, port, q):
         from marin_experiments_b200.parallel import dist as pdist
         from marin_experiments_b200.train.trainer import Trainer
 
-        out = {}
-        for name, overlap, wire in (("serial", "0", "fp32"), ("overlap", "1", "fp32"), ("overlap_bf16", "1", "bf16")):
+        out, launched = {}, {}
+        runs = (("serial", "0", "fp32"), ("serial2", "0", "fp32"), ("overlap", "1", "fp32"),
+                ("overlap_bf16", "1", "bf16"))
+        for name, overlap, wire in runs:
             os.environ["MXK_DP_OVERLAP"], os.environ["MXK_DP_WIRE"] = overlap, wire
             pdist._CTX = None
             ctx = pdist.init(ep_size=1)
@@ -44,12 +46,24 @@ def _worker(rank, world, port, q):
                                 trainer=GrugTrainerConfig(trainer=TrainerConfig(num_train_steps=10, seed=0)))
             tr = Trainer(run, device=f"cuda:{rank}", micro_batch=2, dist=ctx)
             assert getattr(ctx, "_overlap_on", False) == (overlap == "1")
+            snap, opt_step, sync = [], tr.opt.step, ctx.grad_sync
+
+            def step_with_snapshot():  # the synchronised gradients, before the optimizer clears them
+                snap.append(tr.store.grad.clone())
+                opt_step()
+
+            def sync_counting(trainer):
+                launched[name] = len(ctx._launched or ())
+                sync(trainer)
+
+            tr.opt.step, ctx.grad_sync = step_with_snapshot, sync_counting
             g = torch.Generator().manual_seed(10 + rank)
-            for _ in range(2):
-                tr.train_step({"tokens": torch.randint(0, 2048, (4, 256), generator=g)})
+            tr.train_step({"tokens": torch.randint(0, 2048, (4, 256), generator=g)})
             torch.cuda.synchronize()
-            out[name] = tr.store.master.cpu()
-        q.put((rank, {k: ((v - out["serial"]).norm() / out["serial"].norm()).item() for k, v in out.items()}))
+            out[name] = snap[0].cpu()
+        ref = out["serial"]
+        q.put((rank, {**{k: ((v - ref).norm() / ref.norm()).item() for k, v in out.items()},
+                      "launched": launched.get("overlap", 0)}))
     finally:
         dist.destroy_process_group()
 
@@ -69,5 +83,9 @@ def test_overlapped_grad_sync_matches_serial():
     for p in procs:
         p.join(timeout=60)
     for r in range(world):
-        assert res[r]["overlap"] < 1e-6, res[r]
+        # the reductions ran during backward (one per block and the final norm: 4 segments)
+        assert res[r]["launched"] >= 4, res[r]
+        # fp32 reductions are exact for two ranks: the gradients differ from a serial run only as
+        # much as two serial runs differ (atomic accumulation order in the kernels)
+        assert res[r]["overlap"] <= max(10 * res[r]["serial2"], 1e-6), res[r]
         assert res[r]["overlap_bf16"] < 1e-2, res[r]

@@ -102,3 +102,33 @@ def test_remat_matches_no_remat_gpu(mode):
     assert abs(l1 - l0) < 1e-4 * abs(l0)
     assert ((g1 - g0).norm() / g0.norm()).item() < 1e-3
     assert m1 < m0, (m0, m1)
+
+
+@pytest.mark.parametrize("corrector,tau,damp", [("none", 2, 1.0), ("dc_asgd", 2, 1.0), ("dc_asgd_ema", 1, 1.0),
+                                                ("wp_preorth", 2, 1.0), ("lr_damp", 1, 0.5)])
+def test_delayed_step_fused_matches_cpu(corrector, tau, damp):
+    """The delayed-gradient step as two sm_100a passes around the fused AdamH vs the torch
+    implementation on CPU: same weights, last update and raw momentum after 4 steps of identical
+    gradients (per-stage delays: the embedding stalest, the head fresh)."""
+    from marin_experiments_b200.optim.delayed import DelayedGrugMoeAdamHConfig
+
+    opt = DelayedGrugMoeAdamHConfig(warmup=0.0, tau=tau, corrector=corrector, lr_damp=damp, num_stages=1 + tau,
+                                    num_layers=MOE.num_layers)
+    run = GrugRunConfig(model=MOE, optimizer=opt, trainer=GrugTrainerConfig(trainer=TrainerConfig(num_train_steps=10)))
+    cpu = Trainer(run, device="cpu")
+    gpu = Trainer(run, device="cuda:0")
+    gpu.store.load_state_dict(cpu.store.state_dict())
+    gen = torch.Generator().manual_seed(4)
+    for _ in range(4):
+        g = torch.randn(cpu.store.numel, generator=gen) * 1e-2
+        cpu.store.grad.copy_(g)
+        gpu.store.grad.copy_(g.cuda())
+        cpu.opt.step()
+        gpu.opt.step()
+    torch.cuda.synchronize()
+    assert (gpu.store.master.cpu() - cpu.store.master).abs().max().item() < 1e-5
+    assert (gpu.opt.last_update.cpu() - cpu.opt.last_update).abs().max().item() < 1e-5
+    if cpu.opt.m_raw is not None:
+        assert (gpu.opt.m_raw.cpu() - cpu.opt.m_raw).abs().max().item() < 1e-6
+    # the bf16 compute copy follows the (damped) masters
+    assert (gpu.store.compute.float() - gpu.store.master.to(torch.bfloat16).float()).abs().max().item() == 0
