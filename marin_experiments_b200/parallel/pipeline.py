@@ -103,18 +103,24 @@ def stage_layers(num_layers: int, pp: int, stage: int) -> range:
     return range(stage * per, (stage + 1) * per)
 
 
-def _stage_dist(topo: PipelineTopology, backend: str):
+def _stage_dist(topo: PipelineTopology, backend: str, zero: bool = False):
+    """The data/expert-parallel context inside one stage (its ``ep`` ranks): experts sharded over
+    them, the other parameters replicated -- with ``zero``, the replicated parameters' optimizer
+    state is sharded over the stage's ranks too (pipeline x ZeRO x expert parallelism)."""
     if topo.ep == 1:
         return None
     from .dist import DistContext
+    from .fsdp import ZeroDistContext
 
-    return DistContext(rank=topo.e, world=topo.ep, ep_size=topo.ep, backend=backend, batch_group=topo.stage_group,
-                       ep_group=topo.stage_group, ep_rank=topo.e)
+    cls = ZeroDistContext if zero else DistContext
+    return cls(rank=topo.e, world=topo.ep, ep_size=topo.ep, backend=backend, batch_group=topo.stage_group,
+               ep_group=topo.stage_group, ep_rank=topo.e)
 
 
 class PipelineTrainer:
     def __init__(self, cfg, topo: PipelineTopology, *, device, microbatches: int, schedule: str = "1f1b",
-                 mode: str = "sync", num_train_steps: int | None = None, seed: int | None = None):
+                 mode: str = "sync", num_train_steps: int | None = None, seed: int | None = None,
+                 zero: bool = False):
         from ..train.trainer import Trainer
 
         self.cfg, self.topo, self.device = cfg, topo, torch.device(device)
@@ -125,7 +131,7 @@ class PipelineTrainer:
         self.layers = stage_layers(mcfg.num_layers, topo.pp, topo.stage)
         backend = "nccl" if self.device.type == "cuda" else "gloo"
         self.tr = Trainer(cfg, device=self.device, num_train_steps=num_train_steps, seed=seed,
-                          dist=_stage_dist(topo, backend),
+                          dist=_stage_dist(topo, backend, zero),
                           model_kwargs=dict(layers=self.layers, with_embed=topo.is_first, with_head=topo.is_last))
         self.model = self.tr.model
         self.n_moe_total = mcfg.num_layers if mcfg.is_moe else 0
@@ -285,6 +291,8 @@ class PipelineTrainer:
         if tr.dist is not None:
             tr.dist.grad_sync(tr)
         tr.opt.step()
+        if tr.dist is not None and hasattr(tr.dist, "post_step"):
+            tr.dist.post_step(tr)
         if beta_sum is not None:
             tr.pending_qb = beta_sum / self.M
         if tr.ema is not None:
@@ -372,6 +380,8 @@ class PipelineTrainer:
                     if tr.dist is not None:
                         tr.dist.grad_sync(tr)
                     tr.opt.step()
+                    if tr.dist is not None and hasattr(tr.dist, "post_step"):
+                        tr.dist.post_step(tr)
                     tr.step += 1
             for p in pending:
                 p.wait()

@@ -92,7 +92,8 @@ def run_pp_sync() -> dict | None:
     M, mb = int(_env("SP_MICRO", "16")), int(_env("SP_MB", "8"))
     sched = _env("SP_PP_SCHEDULE", "1f1b")
     cfg = _config(False, pp, topo.stage)
-    pt = PipelineTrainer(cfg, topo, device=dev, microbatches=M, schedule=sched, mode="sync")
+    pt = PipelineTrainer(cfg, topo, device=dev, microbatches=M, schedule=sched, mode="sync",
+                         zero=_env("SP_PP_ZERO", "0") == "1")
     steps, warm = int(_env("SP_STEPS", "4")), int(_env("SP_WARMUP_STEPS", "2"))
     seq = cfg.model.max_seq_len
     data = list(_batches(steps + warm, M * mb, seq, cfg.model.vocab_size, 3, topo.e))
@@ -127,7 +128,7 @@ def run_pp_async() -> dict | None:
     topo = init_topology(pp, ep)
     mb = int(_env("SP_MB", "8"))
     cfg = _config(True, pp, topo.stage)
-    pt = PipelineTrainer(cfg, topo, device=dev, microbatches=1, mode="async")
+    pt = PipelineTrainer(cfg, topo, device=dev, microbatches=1, mode="async", zero=_env("SP_PP_ZERO", "0") == "1")
     warm_ticks, ticks = int(_env("SP_WARMUP_TICKS", str(2 * pp))), int(_env("SP_TICKS", "16"))
     seq = cfg.model.max_seq_len
     pt.run_async(_batches(warm_ticks, mb, seq, cfg.model.vocab_size, 3, topo.e), warm_ticks)

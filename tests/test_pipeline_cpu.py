@@ -51,7 +51,7 @@ def _oracle(micro):
     return {gname(i.name): tr.store.master_view(i).clone() for i in tr.store.infos}
 
 
-def _pp_rank(rank, world, pp, ep, schedule):
+def _pp_rank(rank, world, pp, ep, schedule, zero=False):
     import torch.distributed as tdist
 
     from marin_experiments_b200.parallel.pipeline import PipelineTrainer, init_topology
@@ -59,7 +59,7 @@ def _pp_rank(rank, world, pp, ep, schedule):
     tdist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         topo = init_topology(pp, ep)
-        pt = PipelineTrainer(_run_cfg(), topo, device="cpu", microbatches=2, schedule=schedule)
+        pt = PipelineTrainer(_run_cfg(), topo, device="cpu", microbatches=2, schedule=schedule, zero=zero)
         tok = _batch()
         local = tok.shape[0] // ep
         out = pt.train_step({"tokens": tok[topo.e * local:(topo.e + 1) * local]})
@@ -90,6 +90,13 @@ def test_pp2_sync_matches_unsplit(schedule):
 
 def test_pp2_ep2_sync_matches_unsplit():
     res = run_ranks(_pp_rank, 4, 2, 2, "1f1b")
+    _check(res, _oracle(micro=2), 2)
+
+
+def test_pp2_ep2_zero_matches_unsplit():
+    """Pipeline x expert parallelism x ZeRO: each stage shards its replicated parameters' optimizer
+    state over its two ranks; the step equals the unsplit model's."""
+    res = run_ranks(_pp_rank, 4, 2, 2, "zb", True)
     _check(res, _oracle(micro=2), 2)
 
 
