@@ -226,6 +226,49 @@ __global__ void ep_wait_kernel(PeerTable peers, int world, int my, size_t flags_
   __syncthreads();
 }
 
+// ---------------------------------------------------------------- ZeRO over peer memory
+// Reduce-scatter fused with the mean: out[k] = scale * sum_r grad_r[k] for k in [lo, hi), reading
+// every rank's gradient buffer (heap offset grad_off) over NVLink. 16-byte loads; lo, hi and the
+// buffers are 16-byte aligned (the store pads its shards to 64 elements).
+__global__ void zero_rs_kernel(PeerTable peers, int world, size_t grad_off, long long lo, long long hi,
+                               float* __restrict__ out, float scale) {
+  const long long n4 = (hi - lo) >> 2;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const long long k = lo + (i << 2);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < world; ++r) {
+      const float4 v = __ldcv(reinterpret_cast<const float4*>(peer_ptr(peers, r, grad_off)) + (k >> 2));
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    acc.x *= scale; acc.y *= scale; acc.z *= scale; acc.w *= scale;
+    reinterpret_cast<float4*>(out)[k >> 2] = acc;
+  }
+}
+
+// All-gather fused with the bf16 cast: for k in [0, end), rank k / per owns element k; the other
+// ranks' elements are read from their master buffers (heap offset master_off) into `master`, and
+// every element's bf16 copy is written to `compute`.
+__global__ void zero_ag_kernel(PeerTable peers, int world, int my, size_t master_off, long long per, long long end,
+                               float* __restrict__ master, __nv_bfloat16* __restrict__ compute) {
+  const long long n4 = end >> 2;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const long long k = i << 2;
+    const int owner = (int)(k / per);
+    float4 v;
+    if (owner == my || owner >= world) {
+      v = reinterpret_cast<const float4*>(master)[i];
+    } else {
+      v = __ldcv(reinterpret_cast<const float4*>(peer_ptr(peers, owner, master_off)) + i);
+      reinterpret_cast<float4*>(master)[i] = v;
+    }
+    __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&a);
+    u.y = *reinterpret_cast<uint32_t*>(&b);
+    reinterpret_cast<uint2*>(compute)[i] = u;
+  }
+}
+
 inline int grid_rows(long work) {
   long g = (work + 7) / 8;
   if (g > 148 * 8) g = 148 * 8;
@@ -258,6 +301,18 @@ void launch_ep_unpermute_pull(const int* sel, const int* slot, void* dx, int T, 
                               cudaStream_t st) {
   count_launch();
   ep_unpermute_pull_kernel<<<grid_rows(T), 256, 0, st>>>(sel, slot, (__nv_bfloat16*)dx, T, K, a);
+}
+
+void launch_zero_rs(const PeerTable& peers, int world, size_t grad_off, long long lo, long long hi, float* out,
+                    float scale, cudaStream_t st) {
+  count_launch();
+  zero_rs_kernel<<<148 * 8, 256, 0, st>>>(peers, world, grad_off, lo, hi, out, scale);
+}
+
+void launch_zero_ag(const PeerTable& peers, int world, int my, size_t master_off, long long per, long long end,
+                    float* master, void* compute, cudaStream_t st) {
+  count_launch();
+  zero_ag_kernel<<<148 * 8, 256, 0, st>>>(peers, world, my, master_off, per, end, master, (__nv_bfloat16*)compute);
 }
 
 void launch_ep_signal(const EpArgs& a, cudaStream_t st) {

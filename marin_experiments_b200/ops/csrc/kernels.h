@@ -145,6 +145,12 @@ void launch_ep_combine_pull(const int* sel, const int* slot, const float* comb, 
 void launch_ep_unpermute_pull(const int* sel, const int* slot, void* dx, int T, int K, const EpArgs& a,
                               cudaStream_t st);
 void launch_ep_signal(const EpArgs& a, cudaStream_t st);
+// ZeRO over peer memory (comm.cu): reduce-scatter fused with the mean; all-gather fused with the
+// bf16 cast.
+void launch_zero_rs(const PeerTable& peers, int world, size_t grad_off, long long lo, long long hi, float* out,
+                    float scale, cudaStream_t st);
+void launch_zero_ag(const PeerTable& peers, int world, int my, size_t master_off, long long per, long long end,
+                    float* master, void* compute, cudaStream_t st);
 // Bounded wait (limit_ns of wall time; <= 0 selects the 20 s default) for every peer's flag.
 void launch_ep_wait(const EpArgs& a, int* err, long long limit_ns, cudaStream_t st);
 int ipc_alloc(size_t bytes, void** ptr, void* handle_out);

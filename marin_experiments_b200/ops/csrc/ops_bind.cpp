@@ -465,6 +465,33 @@ void ep_signal(const std::vector<int64_t>& peers, int64_t my, int64_t flags_off,
   mxk::launch_ep_signal(a, stream());
 }
 
+mxk::PeerTable peer_table(const std::vector<int64_t>& peers) {
+  need(!peers.empty() && (int64_t)peers.size() <= mxk::kMaxPeers, "bad peer table");
+  mxk::PeerTable t{};
+  for (size_t i = 0; i < peers.size(); ++i) t.base[i] = reinterpret_cast<void*>(peers[i]);
+  return t;
+}
+
+void zero_rs(const std::vector<int64_t>& peers, int64_t grad_off, int64_t lo, int64_t hi, const Tensor& out,
+             double scale) {
+  cuda_f32(out, "out");
+  need(lo % 4 == 0 && hi % 4 == 0 && hi >= lo && grad_off % 16 == 0, "zero_rs: 16-byte aligned range");
+  need(out.numel() >= hi && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0, "zero_rs: output buffer");
+  c10::cuda::CUDAGuard g(out.device());
+  mxk::launch_zero_rs(peer_table(peers), (int)peers.size(), (size_t)grad_off, lo, hi, out.data_ptr<float>(),
+                      (float)scale, stream());
+}
+
+void zero_ag(const std::vector<int64_t>& peers, int64_t my, int64_t master_off, int64_t per, int64_t end,
+             const Tensor& master, const Tensor& compute) {
+  cuda_f32(master, "master");
+  need(per % 4 == 0 && end % 4 == 0 && master_off % 16 == 0 && master.numel() >= end && compute.numel() >= end,
+       "zero_ag: 16-byte aligned shards");
+  c10::cuda::CUDAGuard g(master.device());
+  mxk::launch_zero_ag(peer_table(peers), (int)peers.size(), (int)my, (size_t)master_off, per, end,
+                      master.data_ptr<float>(), compute.data_ptr(), stream());
+}
+
 void ep_wait(const std::vector<int64_t>& peers, int64_t my, int64_t flags_off, int64_t purpose, int64_t epoch,
              const Tensor& err, int64_t limit_ns) {
   auto a = ep_args(peers, my, 1, 1, 8, 0, 0, flags_off, purpose, epoch, c10::nullopt);
@@ -576,6 +603,8 @@ void register_ops(pybind11::module& m) {
   m.def("ipc_close", [](int64_t p) { return mxk::ipc_close(reinterpret_cast<void*>(p)); });
   m.def("ipc_free", [](int64_t p) { return mxk::ipc_free(reinterpret_cast<void*>(p)); });
   m.def("heap_tensor", &heap_tensor);
+  m.def("zero_rs", &zero_rs);
+  m.def("zero_ag", &zero_ag);
   m.def("ep_dispatch_push", &ep_dispatch_push);
   m.def("ep_combine_bwd_push", &ep_combine_bwd_push);
   m.def("ep_combine_pull", &ep_combine_pull);

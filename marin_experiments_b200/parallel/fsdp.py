@@ -34,14 +34,58 @@ bytes on the wire equal a gradient all-reduce.
 
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as tdist
 
 from .dist import DistContext
 
+# flag purposes of the peer-memory ZeRO exchanges (a heap of their own)
+_RS_READY, _RS_DONE, _AG_READY = 4, 5, 6
+
 
 class ZeroDistContext(DistContext):
+    """On GPUs the gradient reduce-scatter and the parameter all-gather run as this framework's own
+    kernels over peer memory (``MXK_ZERO_P2P``, on by default): the store's fp32 master and gradient
+    buffers live in a symmetric heap (every rank maps every other rank's), each rank sums its shard
+    of everyone's gradients straight from their buffers with the mean applied in the same pass, and
+    pulls the other ranks' updated shards into its masters while writing the bf16 copy. Release /
+    acquire flags order the passes: gradients complete before anyone reads them, nobody clears its
+    gradients before every rank has read them, shards updated before anyone pulls them."""
+
     supports_overlap = False  # the reduce-scatter runs once, after backward
+
+    @property
+    def p2p(self) -> bool:
+        return self.backend == "nccl" and os.environ.get("MXK_ZERO_P2P", "1") == "1"
+
+    @property
+    def store_alloc(self):
+        if not self.p2p:
+            return None
+
+        def alloc(numel: int):
+            from .symm import heap_for
+
+            dev = torch.device("cuda", torch.cuda.current_device())
+            nbytes = 4 * numel
+            heap = heap_for(self.batch_group, dev, 2 * nbytes + (2 << 20), name="zero")
+            self._heap = heap
+            self._master_off = heap.alloc("zero_master", nbytes)
+            self._grad_off = heap.alloc("zero_grad", nbytes)
+            return (heap.tensor(self._master_off, (numel,), torch.float32),
+                    heap.tensor(self._grad_off, (numel,), torch.float32))
+
+        return alloc
+
+    def _flag(self, purpose: int) -> None:
+        from ..ops._ext import err_flag, ext
+
+        h = self._heap
+        e = h.next_epoch(purpose)
+        ext().ep_signal(h.peers, h.my, 0, purpose, e)
+        ext().ep_wait(h.peers, h.my, 0, purpose, e, err_flag(h.device))
 
     @property
     def store_pad(self) -> int:
@@ -103,6 +147,15 @@ class ZeroDistContext(DistContext):
         st = trainer.store
         lo, hi = self._shard
         region = st.grad[: self._end]
+        if getattr(self, "_heap", None) is not None:
+            from ..ops._ext import ext
+
+            self._flag(_RS_READY)  # every rank's gradients are complete
+            ext().zero_rs(self._heap.peers, self._grad_off, lo, hi, st.grad, 1.0 / self.world)
+            self._flag(_RS_DONE)  # every rank has read its shard of everyone's gradients
+            if self._end < st.numel:
+                st.grad[self._end:].div_(self.world)
+            return
         if self.backend == "nccl":
             tdist.reduce_scatter_tensor(st.grad[lo:hi], region, op=tdist.ReduceOp.SUM, group=self.batch_group)
         else:  # gloo has no reduce-scatter: all-reduce and keep the range
@@ -115,6 +168,14 @@ class ZeroDistContext(DistContext):
         st = trainer.store
         lo, hi = self._shard
         region = st.master[: self._end]
+        if getattr(self, "_heap", None) is not None:
+            from ..ops._ext import ext
+
+            self._flag(_AG_READY)  # every rank's shard is updated
+            ext().zero_ag(self._heap.peers, self._heap.my, self._master_off, hi - lo, self._end, st.master, st.compute)
+            if self._end < st.numel:  # this rank's experts: their bf16 copy
+                ext().cast_bf16(st.master[self._end:], st.compute[self._end:])
+            return
         if self.backend == "nccl":
             tdist.all_gather_into_tensor(region, st.master[lo:hi].clone(), group=self.batch_group)
         else:

@@ -82,9 +82,10 @@ class SymmetricHeap:
 _HEAPS: dict = {}
 
 
-def heap_for(group, device, min_bytes: int) -> SymmetricHeap:
-    """The group's heap, created (collectively) on first use with at least ``min_bytes``."""
-    key = (id(group), torch.device(device).index)
+def heap_for(group, device, min_bytes: int, name: str = "ep") -> SymmetricHeap:
+    """The group's heap called ``name``, created (collectively) on first use with at least
+    ``min_bytes``."""
+    key = (id(group), torch.device(device).index, name)
     h = _HEAPS.get(key)
     if h is None:
         h = SymmetricHeap(group, min_bytes, device)

@@ -95,13 +95,14 @@ def _is_expert(module, leaf: str, p) -> bool:
 
 
 class ParamStore:
-    """``expert_last``: lay out every routed-expert weight after all other parameters, with the
+    """``alloc(numel) -> (master, grad)`` places the two fp32 buffers (default: ordinary device
+    tensors). ``expert_last``: lay out every routed-expert weight after all other parameters, with the
     expert region starting at ``expert_start`` (a multiple of ``pad_multiple``), so the replicated
     parameters form one prefix that can be sharded over data-parallel ranks while each
     expert-parallel rank keeps its own experts' range (ZeRO with expert parallelism)."""
 
     def __init__(self, model: nn.Module, device: torch.device | str, *, compute_dtype=torch.bfloat16,
-                 moments: int = 2, pad_multiple: int = ALIGN, expert_last: bool = False):
+                 moments: int = 2, pad_multiple: int = ALIGN, expert_last: bool = False, alloc=None):
         self.device = torch.device(device)
         self.cuda = self.device.type == "cuda"
         self.compute_dtype = compute_dtype if self.cuda else torch.float32
@@ -142,8 +143,13 @@ class ParamStore:
         if expert_last and self.expert_start is None:  # no experts: the region is empty
             self.expert_start = self.numel
         dev = self.device
-        self.master = torch.zeros(self.numel, dtype=torch.float32, device=dev)
-        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=dev)
+        if alloc is not None:  # e.g. buffers other GPUs read directly (a symmetric heap)
+            self.master, self.grad = alloc(self.numel)
+            self.master.zero_()
+            self.grad.zero_()
+        else:
+            self.master = torch.zeros(self.numel, dtype=torch.float32, device=dev)
+            self.grad = torch.zeros(self.numel, dtype=torch.float32, device=dev)
         self.compute = torch.zeros(self.numel, dtype=torch.bfloat16, device=dev) if self.cuda else None
         with torch.no_grad():
             for info in self.infos:

@@ -72,7 +72,8 @@ class Trainer:
                 model = Transformer(cfg, local_experts=local, **self.model_kwargs)
         self.model = model
         self.store = ParamStore(model, self.device, pad_multiple=getattr(self.dist, "store_pad", 64),
-                                expert_last=getattr(self.dist, "expert_last", False))
+                                expert_last=getattr(self.dist, "expert_last", False),
+                                alloc=getattr(self.dist, "store_alloc", None))
         init_store_weights(self.store, cfg, self.seed, model)
         if self.dist is not None:
             self.dist.setup_model(self)
