@@ -85,3 +85,22 @@ def test_zero_with_expert_parallelism_on_gpu():
                   for k, v in b[r]["upd"].items())
         den = sum(float((torch.from_numpy(v) ** 2).sum()) for v in b[r]["upd"].values())
         assert (num / den) ** 0.5 < 0.05, (r, (num / den) ** 0.5)
+
+
+def _p2p_rank(rank, world, p2p):
+    import os
+
+    os.environ["MXK_ZERO_P2P"] = "1" if p2p else "0"
+    out = _rank(rank, world, True)
+    return out
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_zero_peer_memory_matches_nccl():
+    """ZeRO's reduce-scatter and all-gather as peer-memory kernels vs NCCL's collectives: the same
+    parameter update (fp32 sums of two ranks are exact in either order)."""
+    a = run_ranks(_p2p_rank, 2, True, timeout=300)
+    b = run_ranks(_p2p_rank, 2, False, timeout=300)
+    for r in range(2):
+        ua, ub = torch.from_numpy(a[r]["upd"]), torch.from_numpy(b[r]["upd"])
+        assert ((ua - ub).norm() / ub.norm()).item() < 1e-2, r
