@@ -317,6 +317,9 @@ def main(argv=None):
                     help="sequences per microbatch (gradient accumulation); default 8 on one GPU, where "
                          "~6B parameters with fp32 master, grads and moments leave room for 8 x 2048 tokens of "
                          "activations, and 16 with expert parallelism, where the experts are sharded")
+    ap.add_argument("--zero", action="store_true",
+                    help="ZeRO: shard the replicated parameters' optimizer state over the ranks (gradient "
+                         "reduce-scatter / parameter all-gather over peer memory; MXK_ZERO_P2P=0 for NCCL)")
     ap.add_argument("--remat", default=None, choices=["none", "recompute_all", "save_moe"],
                     help="activation recompute per block (default: none; the model config's value)")
     ap.add_argument("--layers", type=int, default=None, help="(debug only) override layer count")
@@ -346,7 +349,13 @@ def main(argv=None):
     args.micro_batch = min(args.micro_batch, args.seqs_per_gpu)
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local_rank)
-    ctx = pdist.init(ep_size=world if bc["parallel"] == "ep" else 1) if world > 1 else None
+    ep_size = world if bc["parallel"] == "ep" else 1
+    if world > 1 and args.zero:
+        from marin_experiments_b200.parallel.fsdp import init_zero
+
+        ctx = init_zero(ep_size=ep_size)
+    else:
+        ctx = pdist.init(ep_size=ep_size) if world > 1 else None
     cfg = bc["model"]
     import dataclasses
 
@@ -481,8 +490,8 @@ def main(argv=None):
         "config": {"model": bc["label"], "name": args.config,
                    "global_batch": seqs * world, "seq_len": seq, "tokens_per_step": tokens_step,
                    "micro_batch": args.micro_batch, "capacity_factor": cfg.capacity_factor,
-                   "parallelism": f"{bc['parallel']}{world}" if world > 1 else "single", "l2": "working set >> L2 (no flush needed)",
-                   "layers": cfg.num_layers, "remat": cfg.remat_mode},
+                   "parallelism": (f"{bc['parallel']}{world}" + ("+zero" if args.zero else "")) if world > 1 else "single", "l2": "working set >> L2 (no flush needed)",
+                   "layers": cfg.num_layers, "remat": cfg.remat_mode, "zero": bool(args.zero and world > 1)},
         "mfu": mfu, "mfu_denominator": f"{flop_peak / 1e12:.1f} TFLOP/s per GPU, {peak_label}",
         "mfu_nominal": mfu_nominal, "mfu_nominal_denominator": "2250 TFLOP/s per GPU, nominal dense bf16",
         "ms_x_median_mhz": ms * clk["sm_mhz"] if clk.get("sm_mhz") else None,

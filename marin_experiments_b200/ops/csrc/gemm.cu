@@ -140,6 +140,16 @@ static bool pair_enabled() {
   return on == 1;
 }
 
+// Operand stages of the CTA-pair weight-gradient GEMM (MXK_GEMM_DW_STAGES: 4 or 6).
+static int dw_stages() {
+  static int n = -1;
+  if (n < 0) {
+    const char* e = std::getenv("MXK_GEMM_DW_STAGES");
+    n = (e && e[0] == '6') ? 6 : 4;
+  }
+  return n;
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool PAIR>
 static int launch_impl(const GemmLaunch& L, cudaStream_t stream) {
   MXK_TRACE("launch_impl enter");
@@ -251,7 +261,14 @@ int launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   MXK_CASE2(4, false, true, EPI_STORE)
   MXK_CASE(128, 6, false, true, EPI_STORE)
   MXK_CASE(64, 8, false, true, EPI_STORE)
-  MXK_CASE2(4, true, true, EPI_STORE)
+  // weight gradients (both operands MN-major; fp32 reduce-add into the gradient): CTA pairs with 4
+  // operand stages leave room for a 6-deep store ring per epilogue warp (MXK_GEMM_DW_STAGES=6
+  // keeps 6 operand stages and a 2-deep ring)
+  if (L.bn == 256 && L.a_mn && L.b_mn && L.epi == EPI_STORE) {
+    if (!pair) return launch_impl<256, 4, true, true, EPI_STORE, false>(L, stream);
+    return dw_stages() == 6 ? launch_impl<256, 6, true, true, EPI_STORE, true>(L, stream)
+                            : launch_impl<256, 4, true, true, EPI_STORE, true>(L, stream);
+  }
   MXK_CASE(128, 6, true, true, EPI_STORE)
   MXK_CASE(64, 8, true, true, EPI_STORE)
   // input-gradient GEMMs that add a second gradient term in the epilogue

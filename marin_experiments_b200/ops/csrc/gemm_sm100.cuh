@@ -35,7 +35,7 @@ constexpr int kMaxGroups = 4096;
 // gpb = ceil(G / kPrefixSlots) groups share a slot (one per slot up to 256 groups); decoding a
 // tile walks at most gpb groups from its slot's first group.
 constexpr int kPrefixSlots = 256;
-constexpr int kStageBufs = 2;    // epilogue staging ring depth per warp
+constexpr int kStageBufs = 2;    // minimum epilogue staging ring depth per warp
 constexpr int kStageBox = 2048;  // 32 rows x 64 bytes
 
 enum EpiKind : int {
@@ -75,16 +75,25 @@ constexpr int smem_fixed_bytes() {
   return STAGES * GemmSmem<BN, PAIR>::kStageBytes + 1024 + 256 + (kPrefixSlots + 1) * 4;
 }
 
+// Store-ring depth per epilogue warp: as many 2 KB boxes as the shared memory left after the
+// operand stages holds (at least kStageBufs, at most 8). More boxes in flight keep more TMA stores /
+// reduce-adds outstanding per SM, which is what an fp32-accumulating epilogue is bound by.
+template <int BN, int STAGES, bool PAIR>
+constexpr int epi_ring() {
+  constexpr int n = (kSmemLimit - smem_fixed_bytes<BN, STAGES, PAIR>()) / (kEpiWarps * kStageBox);
+  return n < kStageBufs ? kStageBufs : (n > 8 ? 8 : n);
+}
+
 template <int BN, int STAGES, bool PAIR, int EPI>
 constexpr int epi_slots() {
-  if (EPI != EPI_SWIGLU_BWD) return kStageBufs;
+  if (EPI != EPI_SWIGLU_BWD) return epi_ring<BN, STAGES, PAIR>();
   constexpr int n = (kSmemLimit - smem_fixed_bytes<BN, STAGES, PAIR>()) / (kEpiWarps * (kSwbSlotBytes + 8));
   return n > 3 ? 3 : n;
 }
 
 template <int BN, int STAGES, bool PAIR, int EPI>
 constexpr int epi_bytes() {
-  if (EPI != EPI_SWIGLU_BWD) return GemmSmem<BN, PAIR>::kEpiBytes;
+  if (EPI != EPI_SWIGLU_BWD) return kEpiWarps * epi_ring<BN, STAGES, PAIR>() * kStageBox;
   return kEpiWarps * epi_slots<BN, STAGES, PAIR, EPI>() * (kSwbSlotBytes + 8);
 }
 
@@ -181,12 +190,13 @@ __device__ __forceinline__ float apply_act(float x, int kind) {
 // Epilogue staging ring of one warp: 32-row x 64-byte boxes in 64B-swizzled smem (16-byte chunk k
 // of row r lives at chunk k ^ ((r >> 1) & 3)), written to global by TMA (only lane 0 issues and
 // tracks the bulk groups; the ring slot is warp-uniform).
+template <int DEPTH>
 struct EpiRing {
   uint8_t* base;
   int slot;
 
   __device__ __forceinline__ uint8_t* acquire(int lane) {
-    if (lane == 0) bulk_wait_read<kStageBufs - 1>();
+    if (lane == 0) bulk_wait_read<DEPTH - 1>();
     __syncwarp();
     return base + slot * kStageBox;
   }
@@ -206,7 +216,7 @@ struct EpiRing {
       else tma_store_2d(tm, buf, x, y);
       bulk_commit();
     }
-    slot = (slot + 1) % kStageBufs;
+    slot = (slot + 1) % DEPTH;
   }
   // 32 fp32 values of this lane's row -> one bf16 box (32 columns) at (x, y)
   __device__ __forceinline__ void bf16_box(const CUtensorMap* tm, const float (&v)[32], int x, int y, int lane) {
@@ -428,7 +438,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;  // TMEM lane quadrant accessible by this warp
     const int half = (warp - 2) >> 2;  // which half of the tile's columns this warp drains
     constexpr int kHalf = BN / 2;
-    EpiRing ring{sEpi + (warp - 2) * kStageBufs * kStageBox, 0};
+    constexpr int kRing = epi_ring<BN, STAGES, PAIR>();
+    EpiRing<kRing> ring{sEpi + (warp - 2) * kRing * kStageBox, 0};
     const bool reduce = p.c_f32 && p.c_accum != 0;
     int tcount = 0;
     const uint32_t tempty_c0 = PAIR ? mapa_shared(&tempty_bar[0], 0) : 0u;

@@ -42,11 +42,17 @@ def one_f_one_b(P: int, M: int) -> list[list[Action]]:
     return out
 
 
-def zb_h1(P: int, M: int, t_f: int = 1, t_b: int = 1, t_w: int = 1) -> list[list[Action]]:
-    """Greedy wavefront with integer action costs; returns each stage's action order."""
+def zb_h1(P: int, M: int, t_f: int = 1, t_b: int = 1, t_w: int = 1, w_slack: int = 1) -> list[list[Action]]:
+    """Greedy wavefront with integer action costs; returns each stage's action order.
+
+    A microbatch's activations stay alive until its W (the weight gradient reads them), so a stage
+    starts a new forward only while fewer than ``P - s + w_slack`` microbatches lack their W: the
+    deferred W passes fill bubbles, but never hold more activations than 1F1B does plus ``w_slack``
+    microbatches (without the bound a stage with no bubbles would defer every W to the end)."""
     done: dict[tuple[str, int, int], int] = {}  # (kind, stage, mb) -> finish time
     nxt_f = [0] * P
     nxt_b = [0] * P
+    w_done = [0] * P
     pending_w: list[list[int]] = [[] for _ in range(P)]
     busy_until = [0] * P
     order: list[list[Action]] = [[] for _ in range(P)]
@@ -63,7 +69,8 @@ def zb_h1(P: int, M: int, t_f: int = 1, t_b: int = 1, t_w: int = 1) -> list[list
                 dep = done.get(("B", s + 1, m)) if s + 1 < P else done.get(("F", s, m))
                 if dep is not None and dep <= t:
                     choice = ("B", m)
-            if choice is None and nxt_f[s] < M and nxt_f[s] - nxt_b[s] < P - s:
+            if (choice is None and nxt_f[s] < M and nxt_f[s] - nxt_b[s] < P - s
+                    and nxt_f[s] - w_done[s] < P - s + w_slack):
                 m = nxt_f[s]
                 dep = done.get(("F", s - 1, m)) if s > 0 else 0
                 if dep is not None and dep <= t:
@@ -80,6 +87,7 @@ def zb_h1(P: int, M: int, t_f: int = 1, t_b: int = 1, t_w: int = 1) -> list[list
                 pending_w[s].append(m)
             else:
                 pending_w[s].pop(0)
+                w_done[s] += 1
             order[s].append(choice)
             busy_until[s] = t + cost[k]
             done[(k, s, m)] = t + cost[k]
