@@ -150,7 +150,11 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long cta_t0 = clock64();
-  const int j = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+  // Longest first (linear block order): key block j sees the queries after it, so small j first,
+  // with heads and batches fastest.
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int nhb = gridDim.y * gridDim.z;
+  const int j = lin / nhb, kh = (lin % nhb) % gridDim.y, b = (lin % nhb) / gridDim.y;
   const int rep = a.H / a.Hkv;
   const int base = b * a.S;
   const int k0 = j * BN;
@@ -503,7 +507,11 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int i = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // Longest first (linear block order): query block i sees the keys up to it, so large i first,
+  // with heads and batches fastest.
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int nhb = gridDim.y * gridDim.z;
+  const int i = gridDim.x - 1 - lin / nhb, h = (lin % nhb) % gridDim.y, b = (lin % nhb) / gridDim.y;
   const int kh = h / (a.H / a.Hkv);
   const int base = b * a.S;
   const int q0 = i * BM;

@@ -108,9 +108,14 @@ __global__ void __launch_bounds__(kThreadsPP, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y, b = blockIdx.z;
+  // Longest first: CTAs start in linear block order, so the tile index is the slowest-varying
+  // one and descending (a causal tile's work grows with its index), heads and batches fastest;
+  // the last wave then holds the shortest tiles instead of a tail of the longest.
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int nhb = gridDim.y * gridDim.z;
+  const int h = (lin % nhb) % gridDim.y, b = (lin % nhb) / gridDim.y;
   const int kh = h / (a.H / a.Hkv);
-  const int q0 = blockIdx.x * 2 * BM;
+  const int q0 = (gridDim.x - 1 - lin / nhb) * 2 * BM;
   const int base = b * a.S;
   // key blocks for the two tiles; tile 0 stops one block earlier (causal)
   int kb_lo = 0;
