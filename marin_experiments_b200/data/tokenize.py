@@ -34,6 +34,7 @@ class TokenizeConfig:
     sample_count: int | None = None
     shard_tokens: int = 1 << 28
     line_docs: bool = False
+    prepend_bos: bool = False  # start every document with the tokenizer's begin-of-sequence token
 
 
 class ByteTokenizer:
@@ -56,11 +57,16 @@ class HFTokenizer:
         self.name = path
         self.vocab_size = self.tok.get_vocab_size()
         eos = None
-        for cand in ("<|endoftext|>", "</s>", "<|end_of_text|>", "<eos>"):
+        for cand in ("<|endoftext|>", "</s>", "<|end_of_text|>", "<eos>", "<|eos|>"):
             eos = self.tok.token_to_id(cand)
             if eos is not None:
                 break
         self.eos_id = eos if eos is not None else self.vocab_size - 1
+        self.bos_id = None
+        for cand in ("<|begin_of_text|>", "<s>", "<bos>", "<|bos|>"):
+            self.bos_id = self.tok.token_to_id(cand)
+            if self.bos_id is not None:
+                break
 
     def encode(self, text: str) -> list[int]:
         return self.tok.encode(text, add_special_tokens=False).ids
@@ -141,8 +147,9 @@ def tokenize(cfg: TokenizeConfig) -> dict:
         shards.append({"tokens": tname, "docs": dname, "num_tokens": int(shard_len), "num_docs": len(ends)})
         buf, ends, shard_len = [], [], 0
 
+    bos = [tok.bos_id] if cfg.prepend_bos and getattr(tok, "bos_id", None) is not None else []
     for text in iter_documents(cfg):
-        ids = np.asarray(tok.encode(text) + [tok.eos_id], dtype=np.uint32)
+        ids = np.asarray(bos + tok.encode(text) + [tok.eos_id], dtype=np.uint32)
         buf.append(ids)
         shard_len += len(ids)
         ends.append(shard_len)
