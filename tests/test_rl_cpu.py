@@ -69,3 +69,23 @@ def test_agent_episode_in_sandbox():
     ep = run_episode(lambda msgs: next(script), task)
     assert ep.reward == 1.0 and ep.turns == 2
     assert [m["role"] for m in ep.messages] == ["system", "user", "assistant", "tool", "assistant"]
+
+
+def test_namespace_sandbox_isolation():
+    from marin_experiments_b200.rl import agent
+
+    if not agent.namespaces_available():
+        import pytest
+
+        pytest.skip("unshare is not permitted on this host")
+    sb = agent.make_sandbox("auto")
+    try:
+        assert isinstance(sb, agent.NamespaceSandbox)
+        assert sb.exec("echo $$").stdout.strip() == "1"  # own PID namespace
+        assert sb.exec("ps -e --no-headers | wc -l").stdout.strip() in ("2", "3")  # bash, ps (, wc)
+        r = sb.exec("python3 -c \"import socket; socket.create_connection(('1.1.1.1', 53), 2)\"", timeout=20)
+        assert r.exit_code != 0 and "unreachable" in r.stderr.lower()
+        assert sb.exec("echo x > f && cat f").stdout.strip() == "x"  # working directory persists
+        assert sb.exec("sleep 30 & sleep 30", timeout=0.5).timed_out
+    finally:
+        sb.close()
