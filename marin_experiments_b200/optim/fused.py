@@ -129,6 +129,7 @@ class FusedOptimizer:
         self.mat_hook = None
         self.shard: tuple[int, int] | None = None
         self.muon_infos = [i for g in self.groups.values() if g["kind"] == "muon" for i in g["infos"]]
+        self.muon_owned = list(self.muon_infos)  # the Muon matrices whose update this rank computes
         self.has_adamh = any(g["kind"] == "adamh" for g in self.groups.values())
         self._build_chunks()
         if store.cuda:
@@ -196,11 +197,19 @@ class FusedOptimizer:
         ranges (packed back to back), the chunk table covers them, and ``norm_hook`` / ``mat_hook``
         must sum the per-group squared norms and the AdamH matrix sums over the ranks holding the
         other shards. Range bounds are multiples of 4 (vector access of the moments)."""
-        if self.muon_infos:
-            raise NotImplementedError("Muon with sharded optimizer state")
         ranges = [(int(lo), int(hi))] + [(int(a), int(b)) for a, b in more]
         if any(a % 4 or b % 4 or b < a for a, b in ranges):
             raise ValueError(f"shard ranges must be ordered multiples of 4: {ranges}")
+        # Muon orthogonalises whole matrices: each one must lie inside a range (this rank runs its
+        # Newton-Schulz step) or outside all of them (another rank does)
+        owned = []
+        for info in self.muon_infos:
+            s, e = info.offset, info.offset + info.numel
+            if any(a <= s and e <= b for a, b in ranges):
+                owned.append(info)
+            elif any(a < e and s < b for a, b in ranges):
+                raise ValueError(f"Muon matrix {info.name} [{s}, {e}) straddles a shard boundary {ranges}")
+        self.muon_owned = owned
         self.shard = ranges
         n = sum(b - a for a, b in ranges)
         self.m = torch.zeros(n, dtype=torch.float32, device=self.store.device)
@@ -377,17 +386,25 @@ class FusedOptimizer:
                 new = new * (pn / math.sqrt(nn2))
             p.copy_(new)
 
+    def _moment_shift(self, k: int) -> int:
+        for lo, hi, moff in self._shard_ranges():
+            if lo <= k < hi:
+                return moff
+        raise IndexError(f"flat index {k} outside the optimizer's ranges")
+
     def _step_muon(self, t: int, grad_scale: float) -> None:
-        """Muon update on the matrices of the muon group (momentum, Newton-Schulz, shape scale)."""
+        """Muon update on the matrices of the muon group (momentum, Newton-Schulz, shape scale);
+        with sharded state, on the matrices this rank owns."""
         cfg = self.cfg
         st = self.store
         lr = self.lr_fns["muon"](self.step_count)
         wd = self.groups["muon"]["wd"]
         mu = getattr(cfg, "momentum", 0.95)
-        for info in self.muon_infos:
+        for info in self.muon_owned:
             sl = slice(info.offset, info.offset + info.numel)
             g = (st.grad[sl] * grad_scale).view(info.shape)
-            m = self.m[sl].view(info.shape)
+            mo = info.offset - self._moment_shift(info.offset)
+            m = self.m[mo: mo + info.numel].view(info.shape)
             m.mul_(mu).add_(g)
             upd = g + mu * m if getattr(cfg, "nesterov", True) else m
             if info.ndim < 2:
@@ -397,5 +414,9 @@ class FusedOptimizer:
             scale = max(1.0, info.shape[-2] / info.shape[-1]) ** 0.5
             p = st.master[sl].view(info.shape)
             p.sub_(lr * (scale * o + wd * p))
-        if st.cuda:
+            if st.cuda and self.shard is not None:
+                from ..ops._ext import ext
+
+                ext().cast_bf16(st.master[sl], st.compute[sl])
+        if st.cuda and self.shard is None:
             st.sync_compute()

@@ -30,6 +30,13 @@ One step:
 
 Optimizer memory per rank for the sharded region drops from ``8 n`` to ``8 n / W`` bytes; the
 bytes on the wire equal a gradient all-reduce.
+
+Muon orthogonalises whole matrices, so its matrices are not split: a rank's optimizer range is its
+reduce-scatter range with each boundary moved forward past a Muon matrix that crosses it, and the
+rank holding a matrix's first element owns its momentum and its Newton-Schulz step. The only extra
+traffic is for the matrices that cross a boundary: after the reduce-scatter, each rank hands the
+part of its range that belongs to an earlier rank's matrix to that owner (one small all-gather),
+and after the step the owners hand the updated parameters back before the all-gather of the shards.
 """
 
 from __future__ import annotations
@@ -119,7 +126,14 @@ class ZeroDistContext(DistContext):
         end = self._sharded_end(st)
         lo, hi = self.shard_range(end)
         extra = [(end, st.numel)] if self.ep_size > 1 and st.numel > end else []
-        opt.set_shard(lo, hi, *extra)
+        spans = sorted((i.offset, (i.offset + i.numel + 3) // 4 * 4) for i in getattr(opt, "muon_infos", ())
+                       if i.offset < end)
+        self._end = end
+        self._bounds = muon_bounds(spans, end, self.world)
+        # exchange sizes: the longest foreign part (gradients to owners), the longest tail (parameters back)
+        self._xg = max(b - a for a, b in map(self._foreign, range(self.world)))
+        self._xp = max(b - a for a, b in map(self._outside, range(self.world)))
+        opt.set_shard(self._bounds[self.rank], self._bounds[self.rank + 1], *extra)
         group = self.batch_group
 
         def allreduce(t):
@@ -143,6 +157,52 @@ class ZeroDistContext(DistContext):
         self._shard = (lo, hi)
         self._end = end
 
+    # ------------------------------------------------------------------ Muon matrices across shards
+    def _foreign(self, q: int) -> tuple[int, int]:
+        """Part of rank q's reduce-scatter range that an earlier rank's Muon matrix owns."""
+        per = self._end // self.world
+        lo, hi = q * per, (q + 1) * per
+        return lo, max(lo, min(self._bounds[q], hi))
+
+    def _outside(self, r: int) -> tuple[int, int]:
+        """Part of rank r's optimizer range beyond its reduce-scatter range (matrix tails)."""
+        per = self._end // self.world
+        a, b = max(self._bounds[r], (r + 1) * per), self._bounds[r + 1]
+        return a, max(a, b)
+
+    def _gather_pieces(self, src: torch.Tensor, span: tuple[int, int], size: int) -> torch.Tensor:
+        piece = torch.zeros(size, dtype=src.dtype, device=src.device)
+        piece[: span[1] - span[0]] = src[span[0]: span[1]]
+        if self.backend == "nccl":
+            out = torch.empty(self.world * size, dtype=src.dtype, device=src.device)
+            tdist.all_gather_into_tensor(out, piece, group=self.batch_group)
+            return out.view(self.world, size)
+        parts = [torch.empty_like(piece) for _ in range(self.world)]
+        tdist.all_gather(parts, piece, group=self.batch_group)
+        return torch.stack(parts)
+
+    def _muon_grads_to_owners(self, st) -> None:
+        if not self._xg:
+            return
+        got = self._gather_pieces(st.grad, self._foreign(self.rank), self._xg)
+        a, b = self._outside(self.rank)
+        for q in range(self.rank + 1, self.world):
+            f0, f1 = self._foreign(q)
+            x0, x1 = max(a, f0), min(b, f1)
+            if x1 > x0:
+                st.grad[x0:x1] = got[q, x0 - f0: x1 - f0]
+
+    def _muon_params_from_owners(self, st) -> None:
+        if not self._xp:
+            return
+        got = self._gather_pieces(st.master, self._outside(self.rank), self._xp)
+        f0, f1 = self._foreign(self.rank)
+        for r in range(self.rank):
+            a, b = self._outside(r)
+            x0, x1 = max(a, f0), min(b, f1)
+            if x1 > x0:
+                st.master[x0:x1] = got[r, x0 - a: x1 - a]
+
     def grad_sync(self, trainer) -> None:
         st = trainer.store
         lo, hi = self._shard
@@ -155,6 +215,7 @@ class ZeroDistContext(DistContext):
             self._flag(_RS_DONE)  # every rank has read its shard of everyone's gradients
             if self._end < st.numel:
                 st.grad[self._end:].div_(self.world)
+            self._muon_grads_to_owners(st)
             return
         if self.backend == "nccl":
             tdist.reduce_scatter_tensor(st.grad[lo:hi], region, op=tdist.ReduceOp.SUM, group=self.batch_group)
@@ -163,11 +224,13 @@ class ZeroDistContext(DistContext):
         st.grad[lo:hi].div_(self.world)
         if self._end < st.numel:  # this rank's experts: sum over all ranks' tokens -> mean
             st.grad[self._end:].div_(self.world)
+        self._muon_grads_to_owners(st)
 
     def post_step(self, trainer) -> None:
         st = trainer.store
         lo, hi = self._shard
         region = st.master[: self._end]
+        self._muon_params_from_owners(st)
         if getattr(self, "_heap", None) is not None:
             from ..ops._ext import ext
 
@@ -183,6 +246,20 @@ class ZeroDistContext(DistContext):
             tdist.all_gather(parts, st.master[lo:hi].clone(), group=self.batch_group)
             region.copy_(torch.cat(parts))
         st.sync_compute()
+
+
+def muon_bounds(spans: list[tuple[int, int]], end: int, world: int) -> list[int]:
+    """Optimizer range boundaries ``[a_0 = 0, ..., a_W = end]``: the equal reduce-scatter
+    boundaries, each moved forward to the end of a Muon matrix span ``[s, e)`` that contains it."""
+    per = end // world
+    out = []
+    for r in range(world + 1):
+        b = min(r * per, end) if r < world else end
+        for s, e in spans:
+            if s < b < e:
+                b = e
+        out.append(max(b, out[-1]) if out else b)
+    return out
 
 
 def init_zero(timeout_s: float = 600.0, ep_size: int = 1) -> ZeroDistContext:

@@ -125,6 +125,8 @@ def _leaves(trainer, buffers: dict[str, torch.Tensor], ep_size: int, ep_rank: in
             # expert-parallel rank's own experts, so their leaf is named per expert-parallel rank.
             pos = 0
             for lo, hi in shard:
+                if hi <= lo:  # a rank whose range is empty (its span belongs to another rank's matrix)
+                    continue
                 key = f"{prefix}/__flat__"
                 if local_lo is not None and lo >= local_lo and ep_size > 1:
                     key = f"{prefix}/__flat_ep{ep_rank}__"

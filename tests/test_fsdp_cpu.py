@@ -15,7 +15,13 @@ def _trainer(ctx, opt="adamh"):
     from marin_experiments_b200.optim import AdamConfig, GrugMoeAdamHConfig
     from marin_experiments_b200.train.trainer import Trainer
 
-    o = GrugMoeAdamHConfig(warmup=0.0, max_grad_norm=0.3) if opt == "adamh" else AdamConfig(warmup=0.0, weight_decay=0.1)
+    if opt == "muon":
+        from marin_experiments_b200.optim.configs import MuonConfig
+
+        o = MuonConfig(warmup=0.0, weight_decay=0.1)
+    else:
+        o = GrugMoeAdamHConfig(warmup=0.0, max_grad_norm=0.3) if opt == "adamh" else \
+            AdamConfig(warmup=0.0, weight_decay=0.1)
     run = GrugRunConfig(model=GrugModelConfig(**CFG), optimizer=o,
                         trainer=GrugTrainerConfig(trainer=TrainerConfig(num_train_steps=10, seed=0)))
     return Trainer(run, device="cpu", dist=ctx)
@@ -149,3 +155,47 @@ def test_zero_with_expert_parallelism(tmp_path):
         for name, want in b[r]["params"].items():
             assert torch.allclose(torch.from_numpy(a[r]["params"][name]), torch.from_numpy(want), atol=1e-5,
                                   rtol=1e-4), name
+
+
+def test_muon_bounds_move_past_matrices():
+    from marin_experiments_b200.parallel.fsdp import muon_bounds
+
+    # spans [0,40) [40,200) [200,256); world 4, equal ranges of 64
+    assert muon_bounds([(0, 40), (40, 200), (200, 256)], 256, 4) == [0, 200, 200, 200, 256]
+    assert muon_bounds([(10, 20)], 256, 4) == [0, 64, 128, 192, 256]
+    assert muon_bounds([(60, 70), (120, 130)], 256, 4) == [0, 70, 130, 192, 256]
+
+
+def _muon_rank(rank, world, zero, steps=3):
+    from marin_experiments_b200.parallel import dist as pdist
+    from marin_experiments_b200.parallel.fsdp import init_zero
+
+    ctx = init_zero(120) if zero else pdist.init(ep_size=1, timeout_s=120)
+    try:
+        tr = _trainer(ctx, "muon")
+        g = torch.Generator().manual_seed(11 + rank)
+        for _ in range(steps):
+            tr.train_step({"tokens": torch.randint(0, 512, (2, 32), generator=g)})
+        inner = getattr(tr.opt, "inner", tr.opt)
+        b = getattr(ctx, "_bounds", None)
+        crossing = b is not None and any(b[r] != r * (ctx._end // world) for r in range(1, world))
+        return {"master": tr.store.master.numpy().copy(), "owned": len(inner.muon_owned),
+                "all": len(inner.muon_infos), "m_numel": inner.m.numel(), "crossing": crossing}
+    finally:
+        pdist.shutdown()
+
+
+def test_zero_muon_matches_replicated_dp():
+    """Muon under ZeRO: each matrix is orthogonalised whole by one owner (some cross the equal
+    reduce-scatter boundaries), and the parameters equal replicated data parallelism's."""
+    for world in (2, 3):
+        a = run_ranks(_muon_rank, world, True)
+        b = run_ranks(_muon_rank, world, False)
+        assert any(a[r]["crossing"] for r in range(world))
+        assert sum(a[r]["owned"] for r in range(world)) == a[0]["all"]
+        for r in range(world):  # the ZeRO store is padded to a multiple of 64 x world elements
+            n = min(a[r]["master"].size, b[r]["master"].size)
+            assert torch.allclose(torch.from_numpy(a[r]["master"][:n]), torch.from_numpy(b[r]["master"][:n]),
+                                  atol=1e-5, rtol=1e-4)
+        assert all(torch.equal(torch.from_numpy(a[0]["master"]), torch.from_numpy(a[r]["master"]))
+                   for r in range(world))

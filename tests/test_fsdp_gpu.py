@@ -15,11 +15,12 @@ CFG = dict(vocab_size=4096, hidden_dim=256, intermediate_dim=256, shared_expert_
            sliding_window=256, capacity_factor=4.0)
 
 
-def _rank(rank, world, zero):
+def _rank(rank, world, zero, opt="adamh"):
     import torch.distributed as tdist
 
     from marin_experiments_b200.config import GrugModelConfig, GrugRunConfig, GrugTrainerConfig, TrainerConfig
     from marin_experiments_b200.optim import GrugMoeAdamHConfig
+    from marin_experiments_b200.optim.configs import MuonConfig
     from marin_experiments_b200.parallel import dist as pdist
     from marin_experiments_b200.parallel.fsdp import init_zero
     from marin_experiments_b200.train.trainer import Trainer
@@ -27,7 +28,8 @@ def _rank(rank, world, zero):
     torch.cuda.set_device(rank)
     ctx = init_zero(120) if zero else pdist.init(ep_size=1, timeout_s=120)
     try:
-        run = GrugRunConfig(model=GrugModelConfig(**CFG), optimizer=GrugMoeAdamHConfig(warmup=0.0),
+        o = GrugMoeAdamHConfig(warmup=0.0) if opt == "adamh" else MuonConfig(warmup=0.0, weight_decay=0.1)
+        run = GrugRunConfig(model=GrugModelConfig(**CFG), optimizer=o,
                             trainer=GrugTrainerConfig(trainer=TrainerConfig(num_train_steps=10, seed=0)))
         tr = Trainer(run, device=f"cuda:{rank}", dist=ctx)
         init = tr.store.master.clone()
@@ -46,6 +48,19 @@ def test_zero_matches_dp_on_gpu():
     assert a[0]["m_numel"] * 2 == a[0]["n"]
     for r in range(2):
         ua, ub = torch.from_numpy(a[r]["upd"]), torch.from_numpy(b[r]["upd"])
+        err = ((ua - ub).norm() / ub.norm()).item()
+        assert err < 0.05, (r, err)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_zero_muon_matches_dp_on_gpu():
+    """Muon under ZeRO on GPUs: matrices orthogonalised whole by their owner rank, crossing
+    matrices handed over around the peer-memory reduce-scatter and all-gather."""
+    a = run_ranks(_rank, 2, True, "muon", timeout=300)
+    b = run_ranks(_rank, 2, False, "muon", timeout=300)
+    for r in range(2):
+        n = min(a[r]["upd"].size, b[r]["upd"].size)
+        ua, ub = torch.from_numpy(a[r]["upd"][:n]), torch.from_numpy(b[r]["upd"][:n])
         err = ((ua - ub).norm() / ub.norm()).item()
         assert err < 0.05, (r, err)
 
