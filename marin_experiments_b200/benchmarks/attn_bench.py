@@ -1,7 +1,11 @@
 """Attention kernels: tcgen05 forward/backward vs the mma.sync ones and the library kernels on the
 same box (cuDNN through torch's SDPA, flash_attn 2.x), causal, 16 heads x 96, 8 x 2048 tokens.
 
-Usage: python -m marin_experiments_b200.benchmarks.attn_bench [--once]
+Usage: python -m marin_experiments_b200.benchmarks.attn_bench [--once] [--prof]
+
+``--prof`` runs one forward with the kernel's phase counters on and prints their per-block means
+(softmax warps: waiting for S, loads + row max, exponentials + P stores, rescale + release; MMA
+thread: waiting for P, for K / V, for its own PV products).
 """
 
 from __future__ import annotations
@@ -10,6 +14,30 @@ import json
 import math
 
 import torch
+
+
+def fwd_phases(b=8, s=2048, h=16, hkv=16, hd=96) -> dict:
+    """Per-block means of the tcgen05 forward's phase counters (SM clock cycles)."""
+    from marin_experiments_b200.ops._ext import err_flag, ext
+
+    t = b * s
+    q = torch.randn(t, h, hd, device="cuda").bfloat16()
+    k = torch.randn(t, hkv, hd, device="cuda").bfloat16()
+    v = torch.randn(t, hkv, hd, device="cuda").bfloat16()
+    o = torch.empty(t, h, hd, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(t, h, device="cuda")
+    prof = torch.zeros(16, dtype=torch.int64, device="cuda")
+    ext().flash_fwd_sm100(q, k, v, o, lse, None, b, s, 0, 1 / math.sqrt(hd), err_flag(q.device), None)
+    ext().flash_fwd_sm100(q, k, v, o, lse, None, b, s, 0, 1 / math.sqrt(hd), err_flag(q.device), prof)
+    torch.cuda.synchronize()
+    p = prof.cpu().tolist()
+    blocks = max(p[7], 1)
+    ctas = (s + 255) // 256 * h * b
+    res = {"softmax_wait_s": p[0] / blocks, "softmax_load_max": p[1] / blocks, "softmax_exp_store": p[2] / blocks,
+           "softmax_rescale_release": p[3] / blocks, "mma_wait_p_per_cta": p[4] / ctas,
+           "mma_wait_kv_per_cta": p[5] / ctas, "mma_wait_o_per_cta": p[6] / ctas, "rescales_per_block": p[8] / blocks}
+    print(json.dumps({"fwd_phases": res}), flush=True)
+    return res
 
 
 def run(b=8, s=2048, h=16, hkv=16, hd=96, iters=10, once=False):
@@ -110,4 +138,7 @@ def _library_cases(b, s, h, hkv, hd, fl):
 if __name__ == "__main__":
     import sys
 
-    run(once="--once" in sys.argv)
+    if "--prof" in sys.argv:
+        fwd_phases()
+    else:
+        run(once="--once" in sys.argv)
