@@ -23,6 +23,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "kernels.h"
 #include "sm100_primitives.cuh"
@@ -59,15 +60,43 @@ struct BwdArgs {
   unsigned long long* prof;
 };
 
-template <int HD>
+// A [128 rows x HD] bf16 operand tile as stored by the dK/dV kernel: head-dim columns 0-63 as one
+// chunk in the 128-byte swizzle (rows of 128 B), then columns 64..HD-1 -- 32 of them for HD = 96,
+// in the 64-byte swizzle (rows of 64 B), so the tile is not padded to 128 columns (24 KB instead of
+// 32 KB for HD = 96), or 64 for HD = 128 in the 128-byte swizzle.
+template <int HD, bool UNPAD = true>
+struct TileFmt {
+  // columns of the second chunk: 0, 32 or 64 (UNPAD = false pads HD = 96 to a second 64-column chunk)
+  static constexpr int W1 = UNPAD || HD <= 64 ? HD - 64 : 64;
+  static constexpr int P1 = 2 * W1;   // its row pitch in bytes
+  static constexpr int kC0 = 128 * 128;
+  static constexpr int kBytes = kC0 + 128 * P1;
+  static constexpr uint32_t kLay1 = W1 == 32 ? 4u : 2u;  // descriptor layout of the second chunk
+  static constexpr bool kNarrow = W1 == 32;
+  // K-major descriptor of k-step ks (head-dim columns 16 ks..) for the rows from `row`
+  static __device__ __forceinline__ uint64_t kmaj(uint32_t base, int ks, int row) {
+    if (ks < 4) return make_sdesc(base + row * 128 + ks * 32, 16, 1024);
+    return make_sdesc_l(base + kC0 + row * P1 + (ks - 4) * 32, 16, 8 * P1, kLay1);
+  }
+  // MN-major descriptor (head dim = N) of K rows [16 kr, 16 kr + 16): the whole tile as one operand
+  // (N = HD, chunks at a 16 KB stride) when both chunks share the 128-byte swizzle, else chunk c
+  static __device__ __forceinline__ uint64_t mnmaj(uint32_t base, int c, int kr) {
+    if (c == 0) return make_sdesc(base + kr * 2048, kC0, 1024);
+    return make_sdesc_l(base + kC0 + kr * 16 * P1, 128 * P1, 8 * P1, kLay1);
+  }
+};
+
+template <int HD, bool UNPAD = true>
 struct Smem {
   static constexpr int KCH = (HD + 63) / 64;
-  static constexpr int kTile = KCH * 128 * 128;  // [KCH chunks][128 rows][128 B]
-  // K, V, Q[2], dO[2], then per-query scalars and barriers. The tiles need 1024-byte alignment;
+  static constexpr int kTile = TileFmt<HD, UNPAD>::kBytes;
+  // Q / dO stages: three when they fit beside K and V (unpadded HD = 96 tiles: 8 x 24 KB)
+  static constexpr int NQ = (2 + 6) * kTile + 3 * BM * 12 + 256 <= 227 * 1024 - 128 ? 3 : 2;
+  // K, V, Q[NQ], dO[NQ], then per-query scalars and barriers. The tiles need 1024-byte alignment;
   // the dynamic shared memory base is expected to have it (the kernel checks and reports otherwise).
-  static constexpr int kScal = 2 * BM * 12;  // [2 buffers] x 128 x (lse2 f32, dsum f32, key-lo i32)
-  static constexpr int kBars = 128;
-  static constexpr int kUsed = 6 * kTile + kScal + kBars;
+  static constexpr int kScal = NQ * BM * 12;  // [NQ buffers] x 128 x (lse2 f32, dsum f32, key-lo i32)
+  static constexpr int kBars = 256;
+  static constexpr int kUsed = (2 + 2 * NQ) * kTile + kScal + kBars;
   static constexpr int kBytes = kUsed + 128;
 };
 
@@ -113,14 +142,19 @@ __device__ __forceinline__ int query_key_lo(int qi, int S, int window, const int
   return lo;
 }
 
-template <int HD>
+template <int HD, bool UNPAD>
 __global__ void __launch_bounds__(kThreadsKV, 1)
     fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                        const __grid_constant__ CUtensorMap tmQn, const __grid_constant__ CUtensorMap tmKn,
+                        const __grid_constant__ CUtensorMap tmVn, const __grid_constant__ CUtensorMap tmOn,
                         const BwdArgs a) {
-  using SM = Smem<HD>;
+  // tm*: 64-column boxes in the 128-byte swizzle; tm*n: 32-column boxes in the 64-byte swizzle
+  // (the second chunk of an HD = 96 tile)
+  using SM = Smem<HD, UNPAD>;
   using C = Cols<HD>;
-  constexpr int KCH = SM::KCH;
+  using TF = TileFmt<HD, UNPAD>;
+  constexpr int NQ = SM::NQ;
   constexpr uint32_t tile = SM::kTile;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
@@ -131,21 +165,21 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
   uint8_t* smem = smem_raw + pad;
   uint8_t* sK = smem;
   uint8_t* sV = smem + tile;
-  uint8_t* sQ = smem + 2 * tile;   // [2]
-  uint8_t* sO = smem + 4 * tile;   // [2] (dO)
-  float* sLse = reinterpret_cast<float*>(smem + 6 * tile);  // [2][128] lse in log2 units
-  float* sDsum = sLse + 2 * BM;                             // [2][128]
-  int* sKlo = reinterpret_cast<int*>(sDsum + 2 * BM);       // [2][128] first visible key
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sKlo + 2 * BM);
+  uint8_t* sQ = smem + 2 * tile;         // [NQ]
+  uint8_t* sO = smem + (2 + NQ) * tile;  // [NQ] (dO)
+  float* sLse = reinterpret_cast<float*>(smem + (2 + 2 * NQ) * tile);  // [NQ][128] lse in log2 units
+  float* sDsum = sLse + NQ * BM;                                       // [NQ][128]
+  int* sKlo = reinterpret_cast<int*>(sDsum + NQ * BM);                 // [NQ][128] first visible key
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKlo + NQ * BM);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;   // [2]
-  uint64_t* qd_empty = bars + 3;  // [2]
-  uint64_t* ld_full = bars + 5;   // [2]
-  uint64_t* sdp_full = bars + 7;   // [2] per query half
-  uint64_t* p_ready = bars + 9;    // [2]
-  uint64_t* mma_done = bars + 11;  // [2]
-  uint64_t* kv_done = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* qd_full = bars + 1;            // [NQ]
+  uint64_t* qd_empty = bars + 1 + NQ;      // [NQ]
+  uint64_t* ld_full = bars + 1 + 2 * NQ;   // [NQ]
+  uint64_t* sdp_full = bars + 1 + 3 * NQ;  // [2] per query half
+  uint64_t* p_ready = sdp_full + 2;        // [2]
+  uint64_t* mma_done = sdp_full + 4;       // [2]
+  uint64_t* kv_done = sdp_full + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sdp_full + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -167,7 +201,7 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < NQ; ++t) {
       mbar_init(&qd_full[t], 1);
       mbar_init(&qd_empty[t], 1);
       mbar_init(&ld_full[t], 32);
@@ -193,28 +227,31 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
   if (warp == kTmaWarpKV) {
     // ------------------------------------------------------------------ TMA + per-query scalars
     if (n_it > 0) {
+      // chunk 0 (columns 0-63) through the 128-byte-swizzle maps, chunk 1 through the narrow maps
+      // for HD = 96, else through the same maps
+      auto load_tile = [&](const CUtensorMap* m, const CUtensorMap* mn, uint64_t* bar, uint8_t* dst, int col0,
+                           int row0) {
+        tma_load_2d(m, bar, dst, col0, row0);
+        if constexpr (TF::W1 > 0) tma_load_2d(TF::kNarrow ? mn : m, bar, dst + TF::kC0, col0 + 64, row0);
+      };
       if (lane == 0) {
         mbar_arrive_expect_tx(kv_full, 2 * tile);
-        for (int c = 0; c < KCH; ++c) {
-          tma_load_2d(&tmK, kv_full, sK + c * BN * 128, kh * HD + c * 64, base + k0);
-          tma_load_2d(&tmV, kv_full, sV + c * BN * 128, kh * HD + c * 64, base + k0);
-        }
+        load_tile(&tmK, &tmKn, kv_full, sK, kh * HD, base + k0);
+        load_tile(&tmV, &tmVn, kv_full, sV, kh * HD, base + k0);
       }
       for (int it = 0; it < n_it; ++it) {
-        const int buf = it & 1;
+        const int buf = it % NQ;
         const int h = kh * rep + it / n_i;
         const int q0 = (i_lo + it % n_i) * BM;
         bool ok = true;
         const long long pw0 = clock64();
-        if (lane == 0) ok = mbar_wait(&qd_empty[buf], ((it >> 1) & 1) ^ 1, a.err, kErrTimeoutProducer, abort_flag);
+        if (lane == 0) ok = mbar_wait(&qd_empty[buf], ((it / NQ) & 1) ^ 1, a.err, kErrTimeoutProducer, abort_flag);
         if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         const long long pw1 = clock64();
         if (lane == 0) {
           mbar_arrive_expect_tx(&qd_full[buf], 2 * tile);
-          for (int c = 0; c < KCH; ++c) {
-            tma_load_2d(&tmQ, &qd_full[buf], sQ + buf * tile + c * BM * 128, h * HD + c * 64, base + q0);
-            tma_load_2d(&tmO, &qd_full[buf], sO + buf * tile + c * BM * 128, h * HD + c * 64, base + q0);
-          }
+          load_tile(&tmQ, &tmQn, &qd_full[buf], sQ + buf * tile, h * HD, base + q0);
+          load_tile(&tmO, &tmOn, &qd_full[buf], sO + buf * tile, h * HD, base + q0);
         }
         // All global loads first (in flight together), then the shared-memory stores: interleaved,
         // the stores kept each next load waiting for the previous one.
@@ -251,36 +288,36 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
       // the other half's compute warps (and the dV / dK MMAs of half h) run. Issue order per
       // block: dV/dK(it, 0), S/dP(it + 1, 0), dV/dK(it, 1), S/dP(it + 1, 1).
       constexpr uint32_t idesc_s = make_idesc_bf16(BN, BM / 2, false, false);  // keys x 64 queries
-      constexpr uint32_t idesc_kv = make_idesc_bf16(BN, HD, false, true);      // keys x head_dim
+      // keys x head_dim: one MMA over the whole tile, or (HD = 96) one per chunk, 64 + 32 columns
+      constexpr uint32_t idesc_kv = make_idesc_bf16(BN, TF::kNarrow ? 64 : HD, false, true);
+      constexpr uint32_t idesc_kv1 = make_idesc_bf16(BN, TF::kNarrow ? 32 : HD, false, true);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       auto issue_sdp = [&](int it, int hh) {
-        const uint32_t q_addr = smem_u32(sQ + (it & 1) * tile), o_addr = smem_u32(sO + (it & 1) * tile);
-        const uint32_t roff = hh * 64 * 128;  // the half's first query row inside each 128-B chunk
+        const uint32_t q_addr = smem_u32(sQ + (it % NQ) * tile), o_addr = smem_u32(sO + (it % NQ) * tile);
 #pragma unroll
-        for (int ks = 0; ks < HD / 16; ++ks) {
-          const uint32_t off = (ks / 4) * 128 * 128 + (ks % 4) * 32;
-          umma_bf16(tmem + kColS + 64 * hh, make_sdesc(k_addr + off, 16, 1024),
-                    make_sdesc(q_addr + off + roff, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
-        }
+        for (int ks = 0; ks < HD / 16; ++ks)  // the half's 64 query rows start at row 64 hh
+          umma_bf16(tmem + kColS + 64 * hh, TF::kmaj(k_addr, ks, 0), TF::kmaj(q_addr, ks, 64 * hh), idesc_s,
+                    ks > 0 ? 1u : 0u);
 #pragma unroll
-        for (int ks = 0; ks < HD / 16; ++ks) {
-          const uint32_t off = (ks / 4) * 128 * 128 + (ks % 4) * 32;
-          umma_bf16(tmem + kColDP + 64 * hh, make_sdesc(v_addr + off, 16, 1024),
-                    make_sdesc(o_addr + off + roff, 16, 1024), idesc_s, ks > 0 ? 1u : 0u);
-        }
+        for (int ks = 0; ks < HD / 16; ++ks)
+          umma_bf16(tmem + kColDP + 64 * hh, TF::kmaj(v_addr, ks, 0), TF::kmaj(o_addr, ks, 64 * hh), idesc_s,
+                    ks > 0 ? 1u : 0u);
         umma_commit(&sdp_full[hh]);
       };
       auto issue_dkdv = [&](int it, int hh) {
-        const uint32_t q_addr = smem_u32(sQ + (it & 1) * tile), o_addr = smem_u32(sO + (it & 1) * tile);
+        const uint32_t q_addr = smem_u32(sQ + (it % NQ) * tile), o_addr = smem_u32(sO + (it % NQ) * tile);
 #pragma unroll
         for (int k4 = 0; k4 < 4; ++k4) {
           const int ks = 4 * hh + k4;
           // queries 16 ks.. were packed by column quarter ks / 2 at the start of its S^T columns
           const uint32_t pc = (ks >> 1) * 32 + (ks & 1) * 8;
-          umma_ts(tmem + C::dV, tmem + kColS + pc, make_sdesc(o_addr + ks * 2048, BM * 128, 1024), idesc_kv,
-                  (it > 0 || ks > 0) ? 1u : 0u);
-          umma_ts(tmem + C::dK, tmem + kColDP + pc, make_sdesc(q_addr + ks * 2048, BM * 128, 1024), idesc_kv,
-                  (it > 0 || ks > 0) ? 1u : 0u);
+          const uint32_t acc = (it > 0 || ks > 0) ? 1u : 0u;
+          umma_ts(tmem + C::dV, tmem + kColS + pc, TF::mnmaj(o_addr, 0, ks), idesc_kv, acc);
+          umma_ts(tmem + C::dK, tmem + kColDP + pc, TF::mnmaj(q_addr, 0, ks), idesc_kv, acc);
+          if constexpr (TF::kNarrow) {
+            umma_ts(tmem + C::dV + 64, tmem + kColS + pc, TF::mnmaj(o_addr, 1, ks), idesc_kv1, acc);
+            umma_ts(tmem + C::dK + 64, tmem + kColDP + pc, TF::mnmaj(q_addr, 1, ks), idesc_kv1, acc);
+          }
         }
         umma_commit(&mma_done[hh]);
       };
@@ -293,7 +330,7 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
         issue_sdp(0, 1);
       }
       for (int it = 0; it < n_it && ok; ++it) {
-        const int buf = it & 1;
+        const int buf = it % NQ;
         for (int hh = 0; hh < 2 && ok; ++hh) {
           long long w0 = clock64();
           if (!mbar_wait(&p_ready[hh], it & 1, a.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
@@ -305,7 +342,8 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
             // the next block's Q / dO landed, and dV / dK of this half (readers of its P^T / dS^T
             // columns) are done
             w0 = clock64();
-            if (hh == 0 && !mbar_wait(&qd_full[buf ^ 1], ((it + 1) >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) {
+            if (hh == 0 && !mbar_wait(&qd_full[(it + 1) % NQ], ((it + 1) / NQ) & 1, a.err, kErrTimeoutMma,
+                                      abort_flag)) {
               ok = false;
               break;
             }
@@ -333,10 +371,10 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
     const bool plain = a.seg == nullptr;
     bool alive = true;
     for (int it = 0; it < n_it; ++it) {
-      const int buf = it & 1;
+      const int buf = it % NQ;
       const int qb = (i_lo + it % n_i) * BM + 32 * qt;  // first query of this quarter
       const long long p_t0 = clock64();
-      bool got = mbar_wait(&ld_full[buf], (it >> 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      bool got = mbar_wait(&ld_full[buf], (it / NQ) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
       got = got && mbar_wait(&sdp_full[qt >> 1], it & 1, a.err, kErrTimeoutEpilogue, abort_flag);
       if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
       const long long p_t1 = clock64();
@@ -713,16 +751,34 @@ __global__ void __launch_bounds__(kThreadsKV, 1)
 
 bool make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner,
                        int box_outer);
+bool make_tmap_bf16_2d_sw64(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld,
+                            int box_inner, int box_outer);
 
 template <int HD>
 static int run_fa_bwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
   using namespace fab100;
-  CUtensorMap tq, tk, tv, to;
+  CUtensorMap tq, tk, tv, to, tqn, tkn, tvn, ton;
   const long T = (long)L.B * L.S;
   if (!make_tmap_bf16_2d(&tq, L.q, (long)L.H * HD, T, L.q_tok, 64, BM)) return kErrBadArgsHost;
   if (!make_tmap_bf16_2d(&tk, L.k, (long)L.Hkv * HD, T, L.k_tok, 64, BN)) return kErrBadArgsHost;
   if (!make_tmap_bf16_2d(&tv, L.v, (long)L.Hkv * HD, T, L.v_tok, 64, BN)) return kErrBadArgsHost;
   if (!make_tmap_bf16_2d(&to, L.dout, (long)L.H * HD, T, (long)L.H * HD, 64, BM)) return kErrBadArgsHost;
+  // HD = 96 tiles stay padded to 128 columns (two Q / dO stages) unless MXK_ATTN_BWD_UNPAD=1: the
+  // unpadded three-stage form measured 8 % slower on one B200 (0.766 vs 0.707 ms for 8 x 2048 x 16 x 96
+  // causal): splitting each dV / dK product into N = 64 and N = 32 MMAs costs more than the third
+  // stage saves
+  static const bool unpad = [] {
+    const char* e = getenv("MXK_ATTN_BWD_UNPAD");
+    return e && e[0] == '1';
+  }();
+  if (TileFmt<HD>::kNarrow) {  // 32-column boxes for the second chunk of an unpadded HD = 96 tile
+    if (!make_tmap_bf16_2d_sw64(&tqn, L.q, (long)L.H * HD, T, L.q_tok, 32, BM)) return kErrBadArgsHost;
+    if (!make_tmap_bf16_2d_sw64(&tkn, L.k, (long)L.Hkv * HD, T, L.k_tok, 32, BN)) return kErrBadArgsHost;
+    if (!make_tmap_bf16_2d_sw64(&tvn, L.v, (long)L.Hkv * HD, T, L.v_tok, 32, BN)) return kErrBadArgsHost;
+    if (!make_tmap_bf16_2d_sw64(&ton, L.dout, (long)L.H * HD, T, (long)L.H * HD, 32, BM)) return kErrBadArgsHost;
+  } else {
+    tqn = tq; tkn = tk; tvn = tv; ton = to;
+  }
   BwdArgs a{};
   a.B = L.B; a.S = L.S; a.H = L.H; a.Hkv = L.Hkv; a.window = L.window;
   a.scale = L.scale;
@@ -736,19 +792,25 @@ static int run_fa_bwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
   a.dv_accumulate = L.dv_accumulate;
   a.err = err;
   a.prof = (unsigned long long*)L.prof;
-  constexpr int smem_kv = Smem<HD>::kBytes;
+  constexpr int smem_kv = Smem<HD, true>::kBytes, smem_kv_pad = Smem<HD, false>::kBytes;
   constexpr int smem_q = SmemQ<HD>::kBytes;
-  static_assert(smem_kv <= 232448 && smem_q <= 232448, "shared memory budget");
+  static_assert(smem_kv <= 232448 && smem_kv_pad <= 232448 && smem_q <= 232448, "shared memory budget");
   static bool init = false;
   if (!init) {
-    if (cudaFuncSetAttribute(fa_bwd_dkdv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv) !=
+    if (cudaFuncSetAttribute(fa_bwd_dkdv_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv) !=
             cudaSuccess ||
+        cudaFuncSetAttribute(fa_bwd_dkdv_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem_kv_pad) != cudaSuccess ||
         cudaFuncSetAttribute(fa_bwd_dq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q) != cudaSuccess)
       return kErrBadArgsHost;
     init = true;
   }
   count_launch();
-  fa_bwd_dkdv_kernel<HD><<<dim3((L.S + BN - 1) / BN, L.Hkv, L.B), kThreadsKV, smem_kv, st>>>(tq, tk, tv, to, a);
+  const dim3 grid_kv((L.S + BN - 1) / BN, L.Hkv, L.B);
+  if (unpad || !TileFmt<HD>::kNarrow)
+    fa_bwd_dkdv_kernel<HD, true><<<grid_kv, kThreadsKV, smem_kv, st>>>(tq, tk, tv, to, tqn, tkn, tvn, ton, a);
+  else
+    fa_bwd_dkdv_kernel<HD, false><<<grid_kv, kThreadsKV, smem_kv_pad, st>>>(tq, tk, tv, to, tq, tk, tv, to, a);
   count_launch();
   fa_bwd_dq_kernel<HD><<<dim3((L.S + BM - 1) / BM, L.H, L.B), kThreadsKV, smem_q, st>>>(tq, tk, tv, to, a);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;

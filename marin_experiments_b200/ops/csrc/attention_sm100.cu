@@ -1,18 +1,21 @@
 // Flash attention forward on the 5th-generation tensor cores (sm_100a).
 //
-// CTA = one 128-query tile of one head: warps 0-3 run the softmax (thread = query row = TMEM
-// lane), warp 4 issues tcgen05.mma (one elected thread), warp 5 issues the TMA loads. For each
-// 128-key block j:
+// CTA = two 128-query tiles of one head, ping-ponged: softmax warps (thread = query row = TMEM
+// lane; in the default split-row kernel two warps per row, 64 key columns each), one MMA warp
+// (one elected thread issues tcgen05.mma), one TMA warp. For each 128-key block j:
 //   S_j = Q K_j^T            (SS MMA: Q, K_j from 128B-swizzled smem; S_j in TMEM, fp32)
 //   P_j = exp2(S_j*c - m)    (softmax warps: tcgen05.ld S, tcgen05.st P as bf16 into TMEM)
 //   O  += P_j V_j            (TS MMA: A = P_j from TMEM, B = V_j MN-major from smem; O in TMEM)
 // The running max is only raised (and O, l rescaled) when a row max grows by more than 2^8, so
-// most blocks skip the O correction. 96 KB of smem and 256 TMEM columns per CTA let two CTAs
-// share an SM, so one CTA's softmax overlaps the other's MMAs. All waits are bounded.
+// most blocks skip the O correction. The two tiles' softmax phases alternate so that one tile's
+// exponentials overlap the other tile's MMAs. All waits are bounded.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
+
+#include <string>
 
 #include "kernels.h"
 #include "sm100_primitives.cuh"
@@ -407,6 +410,351 @@ __global__ void __launch_bounds__(kThreadsPP, 1)
   }
 }
 
+// Split-row forward: the same two-tile ping-pong, with each tile's softmax spread over eight warps
+// -- two per TMEM subpartition, each owning 64 of a block's 128 key columns for its 32 rows -- so
+// the per-block softmax latency, which bounds the tensor core's duty cycle (a tile's next S waits
+// for its P), roughly halves. The two halves of a row agree on the block's row max through a
+// shared-memory exchange gated by a per-subpartition mbarrier (64 arrivals per block, bounded
+// waits); their partial row sums are combined once at the end. P of keys 0-63 goes to TMEM
+// columns 0-31 of the tile's S region and P of keys 64-127 to columns 64-95, so each half only
+// overwrites S columns it has already read itself.
+constexpr int kThreadsSR = 576;  // softmax warps 0-15 (tile = warp / 8), MMA warp 16, TMA warp 17
+
+template <int HD>
+struct SmemSR {
+  static constexpr int KCH = (HD + 63) / 64;
+  static constexpr int kTile = KCH * BM * 128;
+  static constexpr int kBarOff = 6 * kTile;                      // Q0, Q1, K[2], V[2] before it
+  static constexpr int kMaxOff = kBarOff + 256;                  // float [2 parity][2 tiles][2 halves][BM]
+  static constexpr int kSumOff = kMaxOff + 2 * 2 * 2 * BM * 4;   // float [2 tiles][2 halves][BM]
+  static constexpr int kBytes = kSumOff + 2 * 2 * BM * 4 + 1024;  // + base alignment slack
+};
+
+// 2^x of 32 scores as bf16 pairs into 16 TMEM columns; the first NP pairs on the FMA pipe.
+template <int NP>
+__device__ __forceinline__ void softmax_emit32(const float (&sv)[32], uint32_t taddr, uint64_t sc2, uint64_t nm2,
+                                               uint64_t& acc0, uint64_t& acc1) {
+  uint32_t w[16];
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    const uint64_t x = f2_fma(f2_make(sv[c], sv[c + 1]), sc2, nm2);
+    float x0, x1, e0, e1;
+    f2_split(x, x0, x1);
+    if (c / 2 < NP) {
+      ex2_poly2(x0, x1, e0, e1);
+    } else {
+      e0 = ex2_sfu(x0);
+      e1 = ex2_sfu(x1);
+    }
+    if ((c / 2) & 1) acc1 = f2_add(acc1, f2_make(e0, e1));
+    else acc0 = f2_add(acc0, f2_make(e0, e1));
+    w[c / 2] = pack_bf16x2(e0, e1);
+  }
+  tmem_st16(taddr, w);
+}
+
+template <int HD, int NP0, int NP1>
+__global__ void __launch_bounds__(kThreadsSR, 1)
+    fa_fwd_sm100_split_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                              const __grid_constant__ CUtensorMap tmV, const FwdArgs a) {
+  using SM = SmemSR<HD>;
+  constexpr int KCH = SM::KCH;
+  constexpr int HH = HD / 2;  // O columns per half
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + 2 * SM::kTile;
+  uint8_t* sV = smem + 4 * SM::kTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBarOff);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2] per tile
+  uint64_t* p_full = bars + 7;    // [2] per tile, 256 arrivals
+  uint64_t* o_done = bars + 9;    // [2] per tile
+  uint64_t* xbar = bars + 11;     // [2 tiles][4 subpartitions], 64 arrivals
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xmax = reinterpret_cast<float*>(smem + SM::kMaxOff);
+  float* xsum = reinterpret_cast<float*>(smem + SM::kSumOff);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Longest first (see fa_fwd_sm100_kernel).
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int nhb = gridDim.y * gridDim.z;
+  const int h = (lin % nhb) % gridDim.y, b = (lin % nhb) / gridDim.y;
+  const int kh = h / (a.H / a.Hkv);
+  const int q0 = (gridDim.x - 1 - lin / nhb) * 2 * BM;
+  const int base = b * a.S;
+  int kb_lo = 0;
+  if (a.window > 0) kb_lo = max(0, q0 - a.window + 1) / BN;
+  const int kb_hi1 = (min(a.S, q0 + 2 * BM) + BN - 1) / BN;
+  const int kb_hi0 = (min(a.S, q0 + BM) + BN - 1) / BN;
+  const int nb = max(kb_hi1 - kb_lo, 0);
+  int lo_t[2], nb_t[2];
+  nb_t[0] = max(kb_hi0 - kb_lo, 0);
+  nb_t[1] = nb;
+  lo_t[0] = 0;
+  lo_t[1] = 0;
+  if (a.window > 0) lo_t[1] = max(0, (q0 + BM - a.window + 1) / BN - kb_lo);
+  if (q0 + BM >= a.S) nb_t[1] = 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 256);
+      mbar_init(&o_done[i], 1);
+    }
+    for (int i = 0; i < 8; ++i) mbar_init(&xbar[i], 64);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 16) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 17) {
+    // ------------------------------------------------------------------------ TMA producer
+    if (lane == 0 && nb > 0) {
+      constexpr uint32_t tile = SM::kTile;
+      mbar_arrive_expect_tx(q_full, 2 * tile);
+      for (int t = 0; t < 2; ++t)
+        for (int c = 0; c < KCH; ++c)
+          tma_load_2d(&tmQ, q_full, sQ + t * tile + c * BM * 128, a.q_x0 + h * HD + c * 64, base + q0 + t * BM);
+      for (int j = 0; j < nb; ++j) {
+        const int st = j & 1;
+        const int kr = base + (kb_lo + j) * BN;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, a.err, kErrTimeoutProducer, abort_flag)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * tile);
+        for (int c = 0; c < KCH; ++c) {
+          tma_load_2d(&tmK, &kv_full[st], sK + st * tile + c * BN * 128, a.k_x0 + kh * HD + c * 64, kr);
+          tma_load_2d(&tmV, &kv_full[st], sV + st * tile + c * BN * 128, a.v_x0 + kh * HD + c * 64, kr);
+        }
+      }
+    }
+  } else if (warp == 16) {
+    // ------------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nb > 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idesc_o = make_idesc_bf16(BM, HD, false, true);
+      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      int s_cnt[2] = {0, 0};
+      bool ok = mbar_wait(q_full, 0, a.err, kErrTimeoutMma, abort_flag);
+      auto issue_qk = [&](int t, int st) {
+        const uint32_t qa = q_addr + t * SM::kTile, ka = k_addr + st * SM::kTile;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t off = (ks / 4) * BM * 128 + (ks % 4) * 32;
+          umma_bf16(tmem + t * 128, make_sdesc(qa + off, 16, 1024), make_sdesc(ka + off, 16, 1024), idesc_s,
+                    ks > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int st, bool acc) {
+        const uint32_t va = v_addr + st * SM::kTile;
+#pragma unroll
+        for (int ks = 0; ks < BN / 16; ++ks)  // P of keys 16ks.. at column 8ks, +32 for the upper half
+          umma_ts_bf16(tmem + 256 + t * 128, tmem + t * 128 + ks * 8 + (ks >= 4 ? 32 : 0),
+                       make_sdesc(va + ks * 2048, BN * 128, 1024), idesc_o, (acc || ks > 0) ? 1u : 0u);
+        umma_commit(&o_done[t]);
+      };
+      unsigned long long wp = 0, wkv = 0, wo = 0;
+      auto active = [&](int t, int j) { return j >= lo_t[t] && j < nb_t[t]; };
+      if (ok) {
+        long long c0 = clock64();
+        ok = mbar_wait(&kv_full[0], 0, a.err, kErrTimeoutMma, abort_flag);
+        wkv += clock64() - c0;
+        tc_fence_after();
+        for (int t = 0; t < 2 && ok; ++t)
+          if (active(t, 0)) issue_qk(t, 0);
+      }
+      for (int j = 0; j < nb && ok; ++j) {
+        const int st = j & 1;
+        bool next_ready = false;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (active(t, j)) {
+            long long c2 = clock64();
+            if (!mbar_wait(&p_full[t], s_cnt[t] & 1, a.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
+            wp += clock64() - c2;
+            tc_fence_after();
+            issue_pv(t, st, s_cnt[t] > 0);
+            ++s_cnt[t];
+          }
+          if (j + 1 < nb && active(t, j + 1)) {
+            if (!next_ready) {
+              long long c0 = clock64();
+              if (!mbar_wait(&kv_full[st ^ 1], ((j + 1) >> 1) & 1, a.err, kErrTimeoutMma, abort_flag)) {
+                ok = false;
+                break;
+              }
+              wkv += clock64() - c0;
+              next_ready = true;
+            }
+            if (s_cnt[t] > 0) {
+              long long c1 = clock64();
+              if (!mbar_wait(&o_done[t], (s_cnt[t] - 1) & 1, a.err, kErrTimeoutMma, abort_flag)) { ok = false; break; }
+              wo += clock64() - c1;
+            }
+            tc_fence_after();
+            issue_qk(t, st ^ 1);
+          }
+        }
+        if (!ok) break;
+        umma_commit(&kv_empty[st]);
+      }
+      if (a.prof) {
+        atomicAdd(&a.prof[4], wp);
+        atomicAdd(&a.prof[5], wkv);
+        atomicAdd(&a.prof[6], wo);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------------ softmax warps
+    const int t = warp >> 3, sp = warp & 3, hf = (warp >> 2) & 1;
+    const int row = sp * 32 + lane;
+    const int qi = q0 + t * BM + row;
+    const uint32_t lane_off = (uint32_t)(sp * 32) << 16;
+    const uint32_t t_s = tmem + t * 128 + lane_off;
+    const uint32_t t_o = tmem + 256 + t * 128 + lane_off + hf * HH;
+    uint64_t* xb = &xbar[t * 4 + sp];
+    int klo, khi;
+    key_range(qi, a.S, a.window, a.seg, base, klo, khi);
+    float m_run = -INFINITY, l_run = 0.f;
+    bool alive = true;
+    int cnt = 0;
+    unsigned long long pw = 0, p1 = 0, p2 = 0, p3 = 0, nres = 0;
+    for (int j = lo_t[t]; j < nb_t[t]; ++j, ++cnt) {
+      long long c_a = clock64();
+      const bool got = mbar_wait(&s_full[t], cnt & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      long long c_b = clock64();
+      pw += c_b - c_a;
+      if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+      tc_fence_after();
+      const int k0 = (kb_lo + j) * BN + hf * 64;
+      const int lo = klo - k0, hi = khi - k0;  // visible columns [lo, hi] of this half-block
+      const bool full = lo <= 0 && hi >= 63;
+      float s0[32], s1[32];
+      tmem_ld32(t_s + hf * 64, s0);
+      tmem_ld32(t_s + hf * 64 + 32, s1);
+      tmem_wait_ld();
+      if (!full) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          if (c < lo || c > hi) s0[c] = -INFINITY;
+          if (c + 32 < lo || c + 32 > hi) s1[c] = -INFINITY;
+        }
+      }
+      float mxa = -INFINITY, mxb = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 32; c += 2) {
+        mxa = fmaxf(mxa, fmaxf(s0[c], s1[c]));
+        mxb = fmaxf(mxb, fmaxf(s0[c + 1], s1[c + 1]));
+      }
+      float mx = fmaxf(mxa, mxb);
+      const int par = cnt & 1;
+      xmax[((par * 2 + t) * 2 + hf) * BM + row] = mx;
+      mbar_arrive(xb);
+      const bool gx = mbar_wait(xb, par, a.err, kErrTimeoutEpilogue, abort_flag);
+      if (!__all_sync(0xffffffffu, gx)) { alive = false; break; }
+      mx = fmaxf(mx, xmax[((par * 2 + t) * 2 + (hf ^ 1)) * BM + row]) * a.scale_log2;
+      long long c_c = clock64();
+      p1 += c_c - c_b;
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > m_run + kRescaleThreshold || (m_run == -INFINITY && mx > -INFINITY)) {
+        if (m_run != -INFINITY) {
+          alpha = exp2f(m_run - mx);
+          rescale = true;
+        }
+        m_run = mx;
+        l_run *= alpha;
+      }
+      const float mb = m_run == -INFINITY ? 0.f : m_run;
+      {
+        const uint64_t sc2 = f2_make(a.scale_log2, a.scale_log2), nm2 = f2_make(-mb, -mb);
+        uint64_t acc0 = f2_make(0.f, 0.f), acc1 = f2_make(0.f, 0.f);
+        softmax_emit32<NP0>(s0, t_s + hf * 64, sc2, nm2, acc0, acc1);
+        softmax_emit32<NP1>(s1, t_s + hf * 64 + 16, sc2, nm2, acc0, acc1);
+        float r0, r1, r2, r3;
+        f2_split(acc0, r0, r1);
+        f2_split(acc1, r2, r3);
+        l_run += (r0 + r1) + (r2 + r3);
+      }
+      long long c_d = clock64();
+      p2 += c_d - c_c;
+      if (__any_sync(0xffffffffu, rescale)) {
+        ++nres;
+        const bool g2 = mbar_wait(&o_done[t], (cnt - 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+        if (!__all_sync(0xffffffffu, g2)) { alive = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < HH; c += 16) {
+          float o[16];
+          tmem_ld16(t_o + c, o);
+          tmem_wait_ld();
+          uint32_t ou[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) ou[u] = __float_as_uint(o[u] * alpha);
+          tmem_st16(t_o + c, ou);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+      p3 += clock64() - c_d;
+    }
+    if (a.prof && lane == 0) {
+      atomicAdd(&a.prof[0], pw);
+      atomicAdd(&a.prof[1], p1);
+      atomicAdd(&a.prof[2], p2);
+      atomicAdd(&a.prof[3], p3);
+      atomicAdd(&a.prof[7], (unsigned long long)cnt);
+      atomicAdd(&a.prof[8], nres);
+    }
+    if (alive && cnt > 0) {
+      xsum[(t * 2 + hf) * BM + row] = l_run;
+      mbar_arrive(xb);
+      bool got = mbar_wait(xb, cnt & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      got = got && mbar_wait(&o_done[t], (cnt - 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      if (__all_sync(0xffffffffu, got)) {
+        tc_fence_after();
+        const float l_tot = l_run + xsum[(t * 2 + (hf ^ 1)) * BM + row];
+        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+        __nv_bfloat16* orow = a.o + ((long)(base + qi) * a.H + h) * HD + hf * HH;
+#pragma unroll 1
+        for (int c = 0; c < HH; c += 16) {
+          float o[16];
+          tmem_ld16(t_o + c, o);
+          tmem_wait_ld();
+          if (qi < a.S) {
+            uint32_t pkd[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) pkd[u] = pack_bf16x2(o[2 * u] * inv, o[2 * u + 1] * inv);
+            reinterpret_cast<uint4*>(orow + c)[0] = make_uint4(pkd[0], pkd[1], pkd[2], pkd[3]);
+            reinterpret_cast<uint4*>(orow + c)[1] = make_uint4(pkd[4], pkd[5], pkd[6], pkd[7]);
+          }
+        }
+        if (qi < a.S && hf == 0)
+          a.lse[(long)(base + qi) * a.H + h] = l_tot > 0.f ? (m_run + log2f(l_tot)) * 0.6931471805599453f : INFINITY;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 16) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace fa100
 
 bool make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner,
@@ -431,6 +779,41 @@ static int run_fa_fwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
   a.q_x0 = 0; a.k_x0 = 0; a.v_x0 = 0;
   a.err = err;
   a.prof = (unsigned long long*)L.prof;
+  dim3 grid((L.S + 2 * BM - 1) / (2 * BM), L.H, L.B);
+  // MXK_ATTN_FWD=pp selects the four-warps-per-tile softmax; the default spreads it over eight
+  static const bool split = [] {
+    const char* e = getenv("MXK_ATTN_FWD");
+    return !(e && std::string(e) == "pp");
+  }();
+  if (split) {
+    // share of the exponentials on the FMA pipe (MXK_ATTN_POLY: 25, 50 or 75 percent). Measured on
+    // one B200 (8 x 2048, 16 x 96, causal): 0.206 / 0.218 / 0.219 ms -- the special-function unit
+    // is not the limiter (27 % busy), so a quarter stays the default
+    static const int poly = [] {
+      const char* e = getenv("MXK_ATTN_POLY");
+      return e ? atoi(e) : 25;
+    }();
+    constexpr int smem = SmemSR<HD>::kBytes;
+    static bool init = false;
+    if (!init) {
+      if (cudaFuncSetAttribute(fa_fwd_sm100_split_kernel<HD, 0, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem) != cudaSuccess ||
+          cudaFuncSetAttribute(fa_fwd_sm100_split_kernel<HD, 8, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem) != cudaSuccess ||
+          cudaFuncSetAttribute(fa_fwd_sm100_split_kernel<HD, 16, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem) != cudaSuccess)
+        return kErrBadArgsHost;
+      init = true;
+    }
+    count_launch();
+    if (poly >= 75)
+      fa_fwd_sm100_split_kernel<HD, 16, 8><<<grid, kThreadsSR, smem, st>>>(tq, tk, tv, a);
+    else if (poly >= 50)
+      fa_fwd_sm100_split_kernel<HD, 8, 8><<<grid, kThreadsSR, smem, st>>>(tq, tk, tv, a);
+    else
+      fa_fwd_sm100_split_kernel<HD, 0, 8><<<grid, kThreadsSR, smem, st>>>(tq, tk, tv, a);
+    return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
+  }
   constexpr int smem = Smem<HD>::kBytes;
   static bool init = false;
   if (!init) {
@@ -439,7 +822,6 @@ static int run_fa_fwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
       return kErrBadArgsHost;
     init = true;
   }
-  dim3 grid((L.S + 2 * BM - 1) / (2 * BM), L.H, L.B);
   count_launch();
   fa_fwd_sm100_kernel<HD><<<grid, kThreadsPP, smem, st>>>(tq, tk, tv, a);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;

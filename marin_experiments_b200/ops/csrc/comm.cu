@@ -24,6 +24,9 @@
 
 #include <cstring>
 
+#include <cstdlib>
+#include <string>
+
 #include "kernels.h"
 #include "sm100_primitives.cuh"
 
@@ -201,6 +204,92 @@ __global__ void ep_unpermute_pull_kernel(const int* __restrict__ sel, const int*
   }
 }
 
+// Pulls with all of a token's K rows in flight at once. The kernels above walk k inside the chunk
+// loop, so each 16-byte peer load waits for the previous one (and the slot / expert lookups are
+// repeated per chunk): a chain of K dependent NVLink round trips per chunk. Here lanes 0..K-1 read
+// the token's K (slot, expert, weight) once and broadcast them, the K row pointers are formed once,
+// and every chunk issues its K loads back to back before accumulating.
+template <int KMAX>
+__device__ __forceinline__ int token_rows(const int* sel, const int* slot, const float* comb, long t, int K,
+                                          const EpArgs& a, const uint4* (&src)[KMAX], float (&w)[KMAX],
+                                          long (&lrow)[KMAX]) {
+  const int lane = threadIdx.x & 31;
+  int s = -1, e = 0;
+  float wk = 0.f;
+  if (lane < K) {
+    s = slot[t * K + lane];
+    e = sel[t * K + lane];
+    if (comb) wk = comb[t * K + lane];
+  }
+  int n = 0;
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    const int sk = __shfl_sync(0xffffffffu, s, k), ek = __shfl_sync(0xffffffffu, e, k);
+    w[k] = __shfl_sync(0xffffffffu, wk, k);
+    src[k] = nullptr;
+    lrow[k] = -1;
+    if (k < K && sk >= 0) {
+      src[k] = reinterpret_cast<const uint4*>(peer_ptr(a.peers, ek / a.e_loc, a.buf_off)) +
+               remote_row(ek, sk, a.e_loc, a.cap, a.my) * (a.D / 8);
+      lrow[k] = (long)ek * a.cap + sk;
+      ++n;
+    }
+  }
+  return n;
+}
+
+template <int KMAX>
+__global__ void ep_combine_pull_v2_kernel(const int* __restrict__ sel, const int* __restrict__ slot,
+                                          const float* __restrict__ comb, const __nv_bfloat16* __restrict__ residual,
+                                          __nv_bfloat16* __restrict__ out, __nv_bfloat16* __restrict__ y_local, int T,
+                                          int K, EpArgs a) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+    const uint4* src[KMAX];
+    float w[KMAX];
+    long lrow[KMAX];
+    token_rows<KMAX>(sel, slot, comb, t, K, a, src, w, lrow);
+    for (int c = lane; c < a.D / 8; c += 32) {
+      uint4 v[KMAX];
+#pragma unroll
+      for (int k = 0; k < KMAX; ++k)
+        if (src[k]) v[k] = __ldcv(src[k] + c);
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (residual) acc8(acc, reinterpret_cast<const uint4*>(residual + (long)t * a.D)[c], 1.f);
+#pragma unroll
+      for (int k = 0; k < KMAX; ++k)
+        if (src[k]) {
+          if (y_local) reinterpret_cast<uint4*>(y_local + lrow[k] * a.D)[c] = v[k];
+          acc8(acc, v[k], w[k]);
+        }
+      reinterpret_cast<uint4*>(out + (long)t * a.D)[c] = pack8(acc);
+    }
+  }
+}
+
+template <int KMAX>
+__global__ void ep_unpermute_pull_v2_kernel(const int* __restrict__ sel, const int* __restrict__ slot,
+                                            __nv_bfloat16* __restrict__ dx, int T, int K, EpArgs a) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+    const uint4* src[KMAX];
+    float w[KMAX];
+    long lrow[KMAX];
+    token_rows<KMAX>(sel, slot, nullptr, t, K, a, src, w, lrow);
+    for (int c = lane; c < a.D / 8; c += 32) {
+      uint4 v[KMAX];
+#pragma unroll
+      for (int k = 0; k < KMAX; ++k)
+        if (src[k]) v[k] = __ldcv(src[k] + c);
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int k = 0; k < KMAX; ++k)
+        if (src[k]) acc8(acc, v[k], 1.f);
+      reinterpret_cast<uint4*>(dx + (long)t * a.D)[c] = pack8(acc);
+    }
+  }
+}
+
 // Publish `epoch` for (purpose, my) to every peer once the previous work on the stream is done
 // (e.g. after the expert GEMMs that wrote the buffer the peers will pull).
 __global__ void ep_signal_kernel(PeerTable peers, int world, int my, size_t flags_off, int purpose, int epoch) {
@@ -290,17 +379,39 @@ void launch_ep_combine_bwd_push(const void* dout, const int* perm, const float* 
       (const __nv_bfloat16*)dout, perm, wperm, counts, a);
 }
 
+// MXK_EP_PULL=v1 selects the one-load-at-a-time pull kernels (kept as the baseline)
+static bool pull_v2() {
+  static const bool v2 = [] {
+    const char* e = std::getenv("MXK_EP_PULL");
+    return !(e && std::string(e) == "v1");
+  }();
+  return v2;
+}
+
 void launch_ep_combine_pull(const int* sel, const int* slot, const float* comb, const void* residual, void* out,
                             void* y_local, int T, int K, const EpArgs& a, cudaStream_t st) {
   count_launch();
-  ep_combine_pull_kernel<<<grid_rows(T), 256, 0, st>>>(sel, slot, comb, (const __nv_bfloat16*)residual,
-                                                       (__nv_bfloat16*)out, (__nv_bfloat16*)y_local, T, K, a);
+  const auto* r = (const __nv_bfloat16*)residual;
+  auto* o = (__nv_bfloat16*)out;
+  auto* y = (__nv_bfloat16*)y_local;
+  if (pull_v2() && K <= 4)
+    ep_combine_pull_v2_kernel<4><<<grid_rows(T), 256, 0, st>>>(sel, slot, comb, r, o, y, T, K, a);
+  else if (pull_v2() && K <= 8)
+    ep_combine_pull_v2_kernel<8><<<grid_rows(T), 256, 0, st>>>(sel, slot, comb, r, o, y, T, K, a);
+  else
+    ep_combine_pull_kernel<<<grid_rows(T), 256, 0, st>>>(sel, slot, comb, r, o, y, T, K, a);
 }
 
 void launch_ep_unpermute_pull(const int* sel, const int* slot, void* dx, int T, int K, const EpArgs& a,
                               cudaStream_t st) {
   count_launch();
-  ep_unpermute_pull_kernel<<<grid_rows(T), 256, 0, st>>>(sel, slot, (__nv_bfloat16*)dx, T, K, a);
+  auto* d = (__nv_bfloat16*)dx;
+  if (pull_v2() && K <= 4)
+    ep_unpermute_pull_v2_kernel<4><<<grid_rows(T), 256, 0, st>>>(sel, slot, d, T, K, a);
+  else if (pull_v2() && K <= 8)
+    ep_unpermute_pull_v2_kernel<8><<<grid_rows(T), 256, 0, st>>>(sel, slot, d, T, K, a);
+  else
+    ep_unpermute_pull_kernel<<<grid_rows(T), 256, 0, st>>>(sel, slot, d, T, K, a);
 }
 
 void launch_zero_rs(const PeerTable& peers, int world, size_t grad_off, long long lo, long long hi, float* out,

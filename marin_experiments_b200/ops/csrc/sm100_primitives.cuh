@@ -230,6 +230,20 @@ __device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_byte
   return d;
 }
 
+// The same with an explicit layout type in bits [61,64): 2 = 128-byte swizzle, 4 = 64-byte swizzle.
+// 64-byte swizzle: K-major rows of 64 B in 512-byte eight-row atoms (SBO = 512 when packed);
+// MN-major atoms of 32 bf16 along MN by eight 64-byte K rows (SBO = 512 between K groups).
+__device__ __forceinline__ uint64_t make_sdesc_l(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                                 uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)(layout & 7) << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::f16 with bf16 A/B, fp32 D.
 //   bits [4,6) D format (1 = f32); [7,10) A format (1 = bf16); [10,13) B format (1 = bf16);
 //   bit 15 A major (1 = MN); bit 16 B major (1 = MN); [17,23) N >> 3; [24,29) M >> 4.
