@@ -114,7 +114,7 @@ def main(argv=None):
         raise RuntimeError(f"exchange wait timed out (error {int(err.item())})")
     if rank == 0:
         print(json.dumps({"ep_bench": {"world": world, "tokens": t, "k": k, "experts": e, "d": d, "cap": cap,
-                                       "impl": os.environ.get("MXK_EP_PULL", "v2"), "results": res}}), flush=True)
+                                       "impl": os.environ.get("MXK_EP_XCHG", "v2"), "results": res}}), flush=True)
     dist.destroy_process_group()
 
 
