@@ -755,6 +755,369 @@ __global__ void __launch_bounds__(kThreadsSR, 1)
   }
 }
 
+// Separate-P forward (HD <= 96): keys in blocks of BNS = 96, so that each tile's S (96 columns)
+// and P (48 columns of bf16 pairs) no longer share TMEM columns. The softmax releases S as soon as
+// it has loaded it, the MMA thread then computes the tile's next S while the exponentials still run,
+// and only the P buffer waits for the previous PV. Per tile the chain becomes
+//   softmax_j (S_{j+1} computed meanwhile) -> softmax_{j+1} ...
+// instead of softmax_j -> PV_j -> S_{j+1} -> softmax_{j+1}.
+// TMEM: S0 [0, 96), S1 [128, 224), O0 [256, 256 + HD), O1 [384, 384 + HD); P_t in the spare columns
+// (k-steps 0-3 of P0 at 96.., 4-5 at 224..; of P1 at 352.., 480..). Warps 0-3 / 4-7 softmax of tile
+// 0 / 1 (thread = query row), warp 8 MMA, warp 9 TMA; three K / V stages.
+constexpr int BNS = 96;
+constexpr int kStagesSP = 3;
+
+template <int HD>
+struct SmemSP {
+  static constexpr int KCH = (HD + 63) / 64;
+  static constexpr int kTileQ = KCH * BM * 128;   // [128 rows x HD] in 64-column chunks
+  static constexpr int kTileKV = KCH * BNS * 128;  // [96 rows x HD]
+  static constexpr int kBarOff = 2 * kTileQ + 2 * kStagesSP * kTileKV;
+  static constexpr int kBytes = kBarOff + 256 + 1024;
+};
+
+// TMEM column of P's k-step ks (16 keys = 8 columns of bf16 pairs) for tile t
+__device__ __forceinline__ uint32_t p_col(int t, int ks) {
+  const uint32_t b0 = t ? 352u : 96u, b1 = t ? 480u : 224u;
+  return ks < 4 ? b0 + ks * 8 : b1 + (ks - 4) * 8;
+}
+
+template <int NP>
+__device__ __forceinline__ void softmax_pack32(const float (&sv)[32], uint32_t (&w)[16], uint64_t sc2, uint64_t nm2,
+                                               uint64_t& acc0, uint64_t& acc1) {
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    const uint64_t x = f2_fma(f2_make(sv[c], sv[c + 1]), sc2, nm2);
+    float x0, x1, e0, e1;
+    f2_split(x, x0, x1);
+    if (c / 2 < NP) {
+      ex2_poly2(x0, x1, e0, e1);
+    } else {
+      e0 = ex2_sfu(x0);
+      e1 = ex2_sfu(x1);
+    }
+    if ((c / 2) & 1) acc1 = f2_add(acc1, f2_make(e0, e1));
+    else acc0 = f2_add(acc0, f2_make(e0, e1));
+    w[c / 2] = pack_bf16x2(e0, e1);
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreadsPP, 1)
+    fa_fwd_sm100_sp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, const FwdArgs a) {
+  static_assert(HD <= 96, "separate-P layout needs O to fit 96 columns per tile");
+  using SM = SmemSP<HD>;
+  constexpr int KCH = SM::KCH;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                    // [2][tileQ]
+  uint8_t* sK = smem + 2 * SM::kTileQ;   // [stages][tileKV]
+  uint8_t* sV = sK + kStagesSP * SM::kTileKV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBarOff);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;                 // [stages]
+  uint64_t* kv_empty = bars + 1 + kStagesSP;    // [stages]
+  uint64_t* s_full = bars + 1 + 2 * kStagesSP;  // [2] per tile
+  uint64_t* s_free = s_full + 2;                // [2] per tile, 128 arrivals
+  uint64_t* p_full = s_full + 4;                // [2] per tile, 128 arrivals
+  uint64_t* o_done = s_full + 6;                // [2] per tile
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Longest first (see fa_fwd_sm100_kernel).
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int nhb = gridDim.y * gridDim.z;
+  const int h = (lin % nhb) % gridDim.y, b = (lin % nhb) / gridDim.y;
+  const int kh = h / (a.H / a.Hkv);
+  const int q0 = (gridDim.x - 1 - lin / nhb) * 2 * BM;
+  const int base = b * a.S;
+  int kb_lo = 0;
+  if (a.window > 0) kb_lo = max(0, q0 - a.window + 1) / BNS;
+  const int kb_hi1 = (min(a.S, q0 + 2 * BM) + BNS - 1) / BNS;
+  const int kb_hi0 = (min(a.S, q0 + BM) + BNS - 1) / BNS;
+  const int nb = max(kb_hi1 - kb_lo, 0);
+  int lo_t[2], nb_t[2];
+  nb_t[0] = max(kb_hi0 - kb_lo, 0);
+  nb_t[1] = nb;
+  lo_t[0] = 0;
+  lo_t[1] = 0;
+  if (a.window > 0) lo_t[1] = max(0, (q0 + BM - a.window + 1) / BNS - kb_lo);
+  if (q0 + BM >= a.S) nb_t[1] = 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kStagesSP; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 9) {
+    // ------------------------------------------------------------------------ TMA producer
+    if (lane == 0 && nb > 0) {
+      mbar_arrive_expect_tx(q_full, 2 * SM::kTileQ);
+      for (int t = 0; t < 2; ++t)
+        for (int c = 0; c < KCH; ++c)
+          tma_load_2d(&tmQ, q_full, sQ + t * SM::kTileQ + c * BM * 128, a.q_x0 + h * HD + c * 64,
+                      base + q0 + t * BM);
+      for (int j = 0; j < nb; ++j) {
+        const int st = j % kStagesSP;
+        const int kr = base + (kb_lo + j) * BNS;
+        if (!mbar_wait(&kv_empty[st], ((j / kStagesSP) & 1) ^ 1, a.err, kErrTimeoutProducer, abort_flag)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * SM::kTileKV);
+        for (int c = 0; c < KCH; ++c) {
+          tma_load_2d(&tmK, &kv_full[st], sK + st * SM::kTileKV + c * BNS * 128, a.k_x0 + kh * HD + c * 64, kr);
+          tma_load_2d(&tmV, &kv_full[st], sV + st * SM::kTileKV + c * BNS * 128, a.v_x0 + kh * HD + c * 64, kr);
+        }
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nb > 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(BM, BNS, false, false);
+      constexpr uint32_t idesc_o = make_idesc_bf16(BM, HD, false, true);
+      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      auto issue_s = [&](int t, int st) {
+        const uint32_t qa = q_addr + t * SM::kTileQ, ka = k_addr + st * SM::kTileKV;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t oq = (ks / 4) * BM * 128 + (ks % 4) * 32, ok_ = (ks / 4) * BNS * 128 + (ks % 4) * 32;
+          umma_bf16(tmem + t * 128, make_sdesc(qa + oq, 16, 1024), make_sdesc(ka + ok_, 16, 1024), idesc_s,
+                    ks > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int st, bool acc) {
+        const uint32_t va = v_addr + st * SM::kTileKV;
+#pragma unroll
+        for (int ks = 0; ks < BNS / 16; ++ks)
+          umma_ts_bf16(tmem + 256 + t * 128, tmem + p_col(t, ks), make_sdesc(va + ks * 2048, BNS * 128, 1024),
+                       idesc_o, (acc || ks > 0) ? 1u : 0u);
+        umma_commit(&o_done[t]);
+      };
+      // Event loop: each pass issues every product whose inputs are ready, so neither tile waits
+      // behind the other. Tile t's S for block j needs K_j and its S of block j - 1 loaded by the
+      // softmax (s_free); its PV for block j needs P_j (p_full). A K / V stage is released once
+      // every active tile has issued its PV for that block. Each barrier can run at most one phase
+      // ahead of the parity tested here (a softmax cannot load an S or store a P that was not
+      // issued or whose previous PV is outstanding), so the parity tests are unambiguous.
+      unsigned long long wp = 0, wkv = 0, ws = 0;
+      bool ok = mbar_wait(q_full, 0, a.err, kErrTimeoutMma, abort_flag);
+      int ns[2] = {lo_t[0], lo_t[1]}, np[2] = {lo_t[0], lo_t[1]};
+      int rel = 0;
+      long long t_last = clock64(), t_iter = t_last;
+      while (ok) {
+        bool prog = false;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (ns[t] < nb_t[t]) {
+            const int j = ns[t];
+            bool ready = mbar_test(&kv_full[j % kStagesSP], (j / kStagesSP) & 1);
+            if (ready && j > lo_t[t]) ready = mbar_test(&s_free[t], (j - 1 - lo_t[t]) & 1);
+            if (ready) {
+              tc_fence_after();
+              issue_s(t, j % kStagesSP);
+              ++ns[t];
+              prog = true;
+            }
+          }
+          if (np[t] < ns[t]) {
+            const int j = np[t];
+            if (mbar_test(&p_full[t], (j - lo_t[t]) & 1)) {
+              tc_fence_after();
+              issue_pv(t, j % kStagesSP, j > lo_t[t]);
+              ++np[t];
+              prog = true;
+            }
+          }
+        }
+        while (rel < nb) {
+          bool done = true;
+#pragma unroll
+          for (int t = 0; t < 2; ++t)
+            if (rel >= lo_t[t] && rel < nb_t[t] && np[t] <= rel) done = false;
+          if (!done) break;
+          umma_commit(&kv_empty[rel % kStagesSP]);
+          ++rel;
+        }
+        if (rel >= nb && np[0] >= nb_t[0] && np[1] >= nb_t[1]) break;
+        const long long now = clock64();
+        if (prog) {
+          t_last = now;
+        } else {
+          wp += now - t_iter;  // cycles spent polling with nothing ready
+          if (*abort_flag) break;
+          if (now - t_last > kWaitCycles) {
+            atomicExch(a.err, kErrTimeoutMma);
+            *abort_flag = 1;
+            break;
+          }
+        }
+        t_iter = now;
+      }
+      if (a.prof) {
+        atomicAdd(&a.prof[4], wp);
+        atomicAdd(&a.prof[5], wkv);
+        atomicAdd(&a.prof[6], ws);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------------ softmax warps
+    const int t = warp >> 2;
+    const int row = (warp & 3) * 32 + lane;
+    const int qi = q0 + t * BM + row;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + t * 128 + lane_off;
+    const uint32_t t_o = tmem + 256 + t * 128 + lane_off;
+    int klo, khi;
+    key_range(qi, a.S, a.window, a.seg, base, klo, khi);
+    float m_run = -INFINITY, l_run = 0.f;
+    bool alive = true;
+    int cnt = 0;
+    unsigned long long pw = 0, p1 = 0, p2 = 0, p3 = 0, nres = 0;
+    for (int j = lo_t[t]; j < nb_t[t]; ++j, ++cnt) {
+      long long c_a = clock64();
+      const bool got = mbar_wait(&s_full[t], cnt & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      long long c_b = clock64();
+      pw += c_b - c_a;
+      if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+      tc_fence_after();
+      float s0[32], s1[32], s2[32];
+      tmem_ld32(t_s + 0, s0);
+      tmem_ld32(t_s + 32, s1);
+      tmem_ld32(t_s + 64, s2);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_free[t]);  // the MMA thread may now overwrite S with the next block's
+      const int k0 = (kb_lo + j) * BNS;
+      const int lo = klo - k0, hi = khi - k0;  // visible columns [lo, hi] of this block
+      if (!(lo <= 0 && hi >= BNS - 1)) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          if (c < lo || c > hi) s0[c] = -INFINITY;
+          if (c + 32 < lo || c + 32 > hi) s1[c] = -INFINITY;
+          if (c + 64 < lo || c + 64 > hi) s2[c] = -INFINITY;
+        }
+      }
+      float mxa = -INFINITY, mxb = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 32; c += 2) {
+        mxa = fmaxf(mxa, fmaxf(fmaxf(s0[c], s1[c]), s2[c]));
+        mxb = fmaxf(mxb, fmaxf(fmaxf(s0[c + 1], s1[c + 1]), s2[c + 1]));
+      }
+      const float mx = fmaxf(mxa, mxb) * a.scale_log2;
+      long long c_c = clock64();
+      p1 += c_c - c_b;
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > m_run + kRescaleThreshold || (m_run == -INFINITY && mx > -INFINITY)) {
+        if (m_run != -INFINITY) {
+          alpha = exp2f(m_run - mx);
+          rescale = true;
+        }
+        m_run = mx;
+        l_run *= alpha;
+      }
+      const float mb = m_run == -INFINITY ? 0.f : m_run;
+      uint32_t w0[16], w1[16], w2[16];
+      {
+        const uint64_t sc2 = f2_make(a.scale_log2, a.scale_log2), nm2 = f2_make(-mb, -mb);
+        uint64_t acc0 = f2_make(0.f, 0.f), acc1 = f2_make(0.f, 0.f);
+        softmax_pack32<4>(s0, w0, sc2, nm2, acc0, acc1);
+        softmax_pack32<4>(s1, w1, sc2, nm2, acc0, acc1);
+        softmax_pack32<4>(s2, w2, sc2, nm2, acc0, acc1);
+        float r0, r1, r2, r3;
+        f2_split(acc0, r0, r1);
+        f2_split(acc1, r2, r3);
+        l_run += (r0 + r1) + (r2 + r3);
+      }
+      long long c_d = clock64();
+      p2 += c_d - c_c;
+      // P's buffer and O are free once the previous block's PV has completed
+      if (cnt > 0) {
+        const bool g2 = mbar_wait(&o_done[t], (cnt - 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+        if (!__all_sync(0xffffffffu, g2)) { alive = false; break; }
+        tc_fence_after();
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        ++nres;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 16) {
+          float o[16];
+          tmem_ld16(t_o + c, o);
+          tmem_wait_ld();
+          uint32_t ou[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) ou[u] = __float_as_uint(o[u] * alpha);
+          tmem_st16(t_o + c, ou);
+        }
+      }
+      tmem_st16(tmem + lane_off + p_col(t, 0), w0);
+      tmem_st16(tmem + lane_off + p_col(t, 2), w1);
+      tmem_st16(tmem + lane_off + p_col(t, 4), w2);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+      p3 += clock64() - c_d;
+    }
+    if (a.prof && lane == 0) {
+      atomicAdd(&a.prof[0], pw);
+      atomicAdd(&a.prof[1], p1);
+      atomicAdd(&a.prof[2], p2);
+      atomicAdd(&a.prof[3], p3);
+      atomicAdd(&a.prof[7], (unsigned long long)cnt);
+      atomicAdd(&a.prof[8], nres);
+    }
+    if (alive && cnt > 0) {
+      const bool got = mbar_wait(&o_done[t], (cnt - 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      if (__all_sync(0xffffffffu, got)) {
+        tc_fence_after();
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        __nv_bfloat16* orow = a.o + ((long)(base + qi) * a.H + h) * HD;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 16) {
+          float o[16];
+          tmem_ld16(t_o + c, o);
+          tmem_wait_ld();
+          if (qi < a.S) {
+            uint32_t pkd[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) pkd[u] = pack_bf16x2(o[2 * u] * inv, o[2 * u + 1] * inv);
+            reinterpret_cast<uint4*>(orow + c)[0] = make_uint4(pkd[0], pkd[1], pkd[2], pkd[3]);
+            reinterpret_cast<uint4*>(orow + c)[1] = make_uint4(pkd[4], pkd[5], pkd[6], pkd[7]);
+          }
+        }
+        if (qi < a.S)
+          a.lse[(long)(base + qi) * a.H + h] = l_run > 0.f ? (m_run + log2f(l_run)) * 0.6931471805599453f : INFINITY;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace fa100
 
 bool make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner,
@@ -780,11 +1143,32 @@ static int run_fa_fwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
   a.err = err;
   a.prof = (unsigned long long*)L.prof;
   dim3 grid((L.S + 2 * BM - 1) / (2 * BM), L.H, L.B);
-  // MXK_ATTN_FWD=pp selects the four-warps-per-tile softmax; the default spreads it over eight
-  static const bool split = [] {
+  // MXK_ATTN_FWD: "split" (default; eight softmax warps per tile), "pp" (four per tile) or "sp"
+  // (96-key blocks with S and P in separate TMEM columns; head dimension <= 96)
+  static const int variant = [] {
     const char* e = getenv("MXK_ATTN_FWD");
-    return !(e && std::string(e) == "pp");
+    const std::string v = e ? e : "split";
+    return v == "pp" ? 0 : v == "sp" ? 2 : 1;
   }();
+  if constexpr (HD <= 96) {
+    if (variant == 2) {
+      CUtensorMap tk96, tv96;
+      if (!make_tmap_bf16_2d(&tk96, L.k, (long)L.Hkv * HD, T, L.k_tok, 64, BNS)) return kErrBadArgsHost;
+      if (!make_tmap_bf16_2d(&tv96, L.v, (long)L.Hkv * HD, T, L.v_tok, 64, BNS)) return kErrBadArgsHost;
+      constexpr int smem = SmemSP<HD>::kBytes;
+      static bool init = false;
+      if (!init) {
+        if (cudaFuncSetAttribute(fa_fwd_sm100_sp_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
+          return kErrBadArgsHost;
+        init = true;
+      }
+      count_launch();
+      fa_fwd_sm100_sp_kernel<HD><<<grid, kThreadsPP, smem, st>>>(tq, tk96, tv96, a);
+      return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
+    }
+  }
+  const bool split = variant != 0;
   if (split) {
     // share of the exponentials on the FMA pipe (MXK_ATTN_POLY: 25, 50 or 75 percent). Measured on
     // one B200 (8 x 2048, 16 x 96, causal): 0.206 / 0.218 / 0.219 ms -- the special-function unit

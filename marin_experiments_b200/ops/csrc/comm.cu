@@ -204,6 +204,62 @@ __global__ void ep_unpermute_pull_kernel(const int* __restrict__ sel, const int*
   }
 }
 
+// Pushes with two rows per warp in flight: both rows' source indices, then all of both rows' 16-byte
+// loads, then the peer stores (the generic kernels above load and store one chunk at a time).
+// V = D / 256 chunks per lane.
+template <int V, bool SCALED>
+__global__ void ep_push_v2_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ perm,
+                                  const float* __restrict__ wperm, const int* __restrict__ counts, EpArgs a) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int E = a.e_loc * a.world;
+  if (!SCALED && blockIdx.x == 0)
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      int* dst = reinterpret_cast<int*>(peer_ptr(a.peers, e / a.e_loc, a.counts_off));
+      dst[a.my * a.e_loc + e % a.e_loc] = counts[e];
+    }
+  const long rows = (long)E * a.cap;
+  const long stride = (long)gridDim.x * warps;
+  for (long r0 = blockIdx.x * (long)warps + (threadIdx.x >> 5); r0 < rows; r0 += 2 * stride) {
+    long r[2] = {r0, r0 + stride};
+    uint4* dst[2] = {nullptr, nullptr};
+    const uint4* src[2] = {nullptr, nullptr};
+    float w[2] = {1.f, 1.f};
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (r[u] >= rows) continue;
+      const int e = (int)(r[u] / a.cap), s = (int)(r[u] % a.cap);
+      const int c = counts[e];
+      if (s >= round128(c)) continue;
+      dst[u] = reinterpret_cast<uint4*>(peer_ptr(a.peers, e / a.e_loc, a.buf_off)) +
+               remote_row(e, s, a.e_loc, a.cap, a.my) * (a.D / 8);
+      if (s < c) {
+        src[u] = reinterpret_cast<const uint4*>(x + (long)perm[r[u]] * a.D);
+        if (SCALED) w[u] = wperm[r[u]];
+      }
+    }
+    uint4 v[2][V];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int k = 0; k < V; ++k) v[u][k] = src[u] ? src[u][lane + 32 * k] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (!dst[u]) continue;
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        if (SCALED && src[u]) {
+          float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+          acc8(f, v[u][k], w[u]);
+          dst[u][lane + 32 * k] = pack8(f);
+        } else {
+          dst[u][lane + 32 * k] = v[u][k];
+        }
+      }
+    }
+  }
+  publish(a.peers, a.world, a.my, a.flags_off, a.purpose, a.epoch, a.counter);
+}
+
 // Pulls with all of a token's K rows in flight at once. The kernels above walk k inside the chunk
 // loop, so each 16-byte peer load waits for the previous one (and the slot / expert lookups are
 // repeated per chunk): a chain of K dependent NVLink round trips per chunk. Here lanes 0..K-1 read
@@ -366,8 +422,34 @@ inline int grid_rows(long work) {
 
 }  // namespace
 
+// MXK_EP_XCHG=v1 selects the one-chunk-at-a-time exchange kernels (kept as the baseline)
+static bool xchg_v2() {
+  static const bool v2 = [] {
+    const char* e = std::getenv("MXK_EP_XCHG");
+    return !(e && std::string(e) == "v1");
+  }();
+  return v2;
+}
+
+template <bool SCALED>
+static bool launch_push_v2(const void* x, const int* perm, const float* wperm, const int* counts, const EpArgs& a,
+                           cudaStream_t st) {
+  if (!xchg_v2() || a.D % 256) return false;
+  const int g = grid_rows((long)a.e_loc * a.world * a.cap);
+  const auto* xb = (const __nv_bfloat16*)x;
+  switch (a.D / 256) {
+    case 2: ep_push_v2_kernel<2, SCALED><<<g, 256, 0, st>>>(xb, perm, wperm, counts, a); return true;
+    case 3: ep_push_v2_kernel<3, SCALED><<<g, 256, 0, st>>>(xb, perm, wperm, counts, a); return true;
+    case 4: ep_push_v2_kernel<4, SCALED><<<g, 256, 0, st>>>(xb, perm, wperm, counts, a); return true;
+    case 6: ep_push_v2_kernel<6, SCALED><<<g, 256, 0, st>>>(xb, perm, wperm, counts, a); return true;
+    case 8: ep_push_v2_kernel<8, SCALED><<<g, 256, 0, st>>>(xb, perm, wperm, counts, a); return true;
+    default: return false;
+  }
+}
+
 void launch_ep_dispatch_push(const void* x, const int* perm, const int* counts, const EpArgs& a, cudaStream_t st) {
   count_launch();
+  if (launch_push_v2<false>(x, perm, nullptr, counts, a, st)) return;
   ep_dispatch_push_kernel<<<grid_rows((long)a.e_loc * a.world * a.cap), 256, 0, st>>>(
       (const __nv_bfloat16*)x, perm, counts, a);
 }
@@ -375,18 +457,12 @@ void launch_ep_dispatch_push(const void* x, const int* perm, const int* counts, 
 void launch_ep_combine_bwd_push(const void* dout, const int* perm, const float* wperm, const int* counts,
                                 const EpArgs& a, cudaStream_t st) {
   count_launch();
+  if (launch_push_v2<true>(dout, perm, wperm, counts, a, st)) return;
   ep_combine_bwd_push_kernel<<<grid_rows((long)a.e_loc * a.world * a.cap), 256, 0, st>>>(
       (const __nv_bfloat16*)dout, perm, wperm, counts, a);
 }
 
-// MXK_EP_PULL=v1 selects the one-load-at-a-time pull kernels (kept as the baseline)
-static bool pull_v2() {
-  static const bool v2 = [] {
-    const char* e = std::getenv("MXK_EP_PULL");
-    return !(e && std::string(e) == "v1");
-  }();
-  return v2;
-}
+static bool pull_v2() { return xchg_v2(); }
 
 void launch_ep_combine_pull(const int* sel, const int* slot, const float* comb, const void* residual, void* out,
                             void* y_local, int T, int K, const EpArgs& a, cudaStream_t st) {
