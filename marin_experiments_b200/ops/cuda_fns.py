@@ -109,6 +109,7 @@ class _RmsGatedNorm(torch.autograd.Function):
         ext().rmsnorm_fwd(x, w_rms, y, rstd, eps)
         ctx.gated = w_down is not None
         ctx.w_rms = w_rms
+        ctx.set_materialize_grads(False)  # a missing residual gradient is passed on as None
         if not ctx.gated:
             ctx.save_for_backward(x, rstd)
             return (y, x.view_as(x)) if passthrough else y
@@ -124,6 +125,8 @@ class _RmsGatedNorm(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dout, dres=None):
+        if dout is None:
+            dout = torch.zeros_like(ctx.saved_tensors[0])
         dout = _c(dout)
         dres = None if dres is None else _c(dres)
         if not ctx.gated:
@@ -379,6 +382,9 @@ class _Router(torch.autograd.Function):
         ctx.save_for_backward(h, logits, lse, sel, topb, keep, counts, th)
         ctx.w_router, ctx.theta = w_router, theta
         ctx.k, ctx.adaptive, ctx.k_min, ctx.temp, ctx.e = k, adaptive, k_min, temp, e
+        # unused outputs (statistics, an auxiliary loss with weight 0) get no zero-filled gradient
+        # tensors: the backward treats a missing gradient as zero
+        ctx.set_materialize_grads(False)
         ctx.mark_non_differentiable(sel, keep, counts, entropy, realized)
         if beta is not None:
             ctx.mark_non_differentiable(beta)
