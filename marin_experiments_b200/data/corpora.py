@@ -1,7 +1,7 @@
 """Named corpus mixtures over local token caches (the role of megagpt-speedrun/data.py:48-410, which
 builds Nemotron-CC / FineWeb-Edu / SFT mixtures from object storage): a recipe maps component names
 to native cache directories under a local root. ``data.remote`` covers the object-store side -- the
-reference's TreeCache splits under an S3 prefix, mirrored and converted once).
+reference's TreeCache splits under an S3 prefix, mirrored and converted once.
 
 ``Recipe(name, components={component: (relative_cache_dir, weight)})``; ``recipe.data_config(root)``
 gives a ``DataConfig(source="mixture")`` over the components that exist (``missing="error"`` raises

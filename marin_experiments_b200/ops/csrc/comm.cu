@@ -111,7 +111,7 @@ __global__ void ep_dispatch_push_kernel(const __nv_bfloat16* __restrict__ x, con
                                         const int* __restrict__ counts, EpArgs a) {
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int E = a.e_loc * a.world;
-  if (blockIdx.x == 0)
+  if (blockIdx.x == 0 && a.s_lo == 0)
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
       int* dst = reinterpret_cast<int*>(peer_ptr(a.peers, e / a.e_loc, a.counts_off));
       dst[a.my * a.e_loc + e % a.e_loc] = counts[e];
@@ -119,7 +119,7 @@ __global__ void ep_dispatch_push_kernel(const __nv_bfloat16* __restrict__ x, con
   for (long r = blockIdx.x * (long)warps + (threadIdx.x >> 5); r < (long)E * a.cap; r += (long)gridDim.x * warps) {
     const int e = (int)(r / a.cap), s = (int)(r % a.cap);
     const int c = counts[e];
-    if (s >= round128(c)) continue;
+    if (s >= round128(c) || s < a.s_lo || s >= a.s_hi) continue;
     uint4* dst = reinterpret_cast<uint4*>(peer_ptr(a.peers, e / a.e_loc, a.buf_off)) +
                  remote_row(e, s, a.e_loc, a.cap, a.my) * (a.D / 8);
     if (s < c) {
@@ -140,7 +140,7 @@ __global__ void ep_combine_bwd_push_kernel(const __nv_bfloat16* __restrict__ dou
   for (long r = blockIdx.x * (long)warps + (threadIdx.x >> 5); r < (long)E * a.cap; r += (long)gridDim.x * warps) {
     const int e = (int)(r / a.cap), s = (int)(r % a.cap);
     const int c = counts[e];
-    if (s >= round128(c)) continue;
+    if (s >= round128(c) || s < a.s_lo || s >= a.s_hi) continue;
     uint4* dst = reinterpret_cast<uint4*>(peer_ptr(a.peers, e / a.e_loc, a.buf_off)) +
                  remote_row(e, s, a.e_loc, a.cap, a.my) * (a.D / 8);
     if (s < c) {
@@ -212,7 +212,7 @@ __global__ void ep_push_v2_kernel(const __nv_bfloat16* __restrict__ x, const int
                                   const float* __restrict__ wperm, const int* __restrict__ counts, EpArgs a) {
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int E = a.e_loc * a.world;
-  if (!SCALED && blockIdx.x == 0)
+  if (!SCALED && blockIdx.x == 0 && a.s_lo == 0)
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
       int* dst = reinterpret_cast<int*>(peer_ptr(a.peers, e / a.e_loc, a.counts_off));
       dst[a.my * a.e_loc + e % a.e_loc] = counts[e];
@@ -229,7 +229,7 @@ __global__ void ep_push_v2_kernel(const __nv_bfloat16* __restrict__ x, const int
       if (r[u] >= rows) continue;
       const int e = (int)(r[u] / a.cap), s = (int)(r[u] % a.cap);
       const int c = counts[e];
-      if (s >= round128(c)) continue;
+      if (s >= round128(c) || s < a.s_lo || s >= a.s_hi) continue;
       dst[u] = reinterpret_cast<uint4*>(peer_ptr(a.peers, e / a.e_loc, a.buf_off)) +
                remote_row(e, s, a.e_loc, a.cap, a.my) * (a.D / 8);
       if (s < c) {
@@ -435,7 +435,8 @@ template <bool SCALED>
 static bool launch_push_v2(const void* x, const int* perm, const float* wperm, const int* counts, const EpArgs& a,
                            cudaStream_t st) {
   if (!xchg_v2() || a.D % 256) return false;
-  const int g = grid_rows((long)a.e_loc * a.world * a.cap);
+  int g = grid_rows((long)a.e_loc * a.world * a.cap);
+  if (a.max_blocks > 0 && g > a.max_blocks) g = a.max_blocks;
   const auto* xb = (const __nv_bfloat16*)x;
   switch (a.D / 256) {
     case 2: ep_push_v2_kernel<2, SCALED><<<g, 256, 0, st>>>(xb, perm, wperm, counts, a); return true;
@@ -450,16 +451,18 @@ static bool launch_push_v2(const void* x, const int* perm, const float* wperm, c
 void launch_ep_dispatch_push(const void* x, const int* perm, const int* counts, const EpArgs& a, cudaStream_t st) {
   count_launch();
   if (launch_push_v2<false>(x, perm, nullptr, counts, a, st)) return;
-  ep_dispatch_push_kernel<<<grid_rows((long)a.e_loc * a.world * a.cap), 256, 0, st>>>(
-      (const __nv_bfloat16*)x, perm, counts, a);
+  int g = grid_rows((long)a.e_loc * a.world * a.cap);
+  if (a.max_blocks > 0 && g > a.max_blocks) g = a.max_blocks;
+  ep_dispatch_push_kernel<<<g, 256, 0, st>>>((const __nv_bfloat16*)x, perm, counts, a);
 }
 
 void launch_ep_combine_bwd_push(const void* dout, const int* perm, const float* wperm, const int* counts,
                                 const EpArgs& a, cudaStream_t st) {
   count_launch();
   if (launch_push_v2<true>(dout, perm, wperm, counts, a, st)) return;
-  ep_combine_bwd_push_kernel<<<grid_rows((long)a.e_loc * a.world * a.cap), 256, 0, st>>>(
-      (const __nv_bfloat16*)dout, perm, wperm, counts, a);
+  int g = grid_rows((long)a.e_loc * a.world * a.cap);
+  if (a.max_blocks > 0 && g > a.max_blocks) g = a.max_blocks;
+  ep_combine_bwd_push_kernel<<<g, 256, 0, st>>>((const __nv_bfloat16*)dout, perm, wperm, counts, a);
 }
 
 static bool pull_v2() { return xchg_v2(); }

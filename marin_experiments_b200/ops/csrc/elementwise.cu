@@ -179,6 +179,86 @@ __global__ void __launch_bounds__(256, 2)
   for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dw[c], sdw[c]);
 }
 
+// The same backward with the weight-gradient partials in shared memory: each warp owns a private
+// [MAXV * 8][32] float region (conflict-free: lane = fastest index) instead of MAXV * 8 registers per
+// thread, so three 8-warp blocks fit an SM (24 warps against 16) and more rows' loads are in flight.
+template <int MAXV>
+__global__ void __launch_bounds__(256, 3)
+    rmsnorm_bwd_smem_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                            const float* __restrict__ w, const float* __restrict__ rstd,
+                            const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
+                            float* __restrict__ dw, int T, int D) {
+  extern __shared__ float sm_rms2[];
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* sw = sm_rms2;                                  // [D]
+  float* pacc = sm_rms2 + D + warp * (MAXV * 8 * 32);  // this warp's [MAXV * 8][32] partials
+  for (int c = threadIdx.x; c < D; c += blockDim.x) sw[c] = w[c];
+#pragma unroll
+  for (int i = 0; i < MAXV * 8; ++i) pacc[i * 32 + lane] = 0.f;
+  __syncthreads();
+  for (int row = blockIdx.x * warps + warp; row < T; row += gridDim.x * warps) {
+    const float r = rstd[row];
+    uint4 gu[MAXV], xu[MAXV];
+#pragma unroll
+    for (int v = 0; v < MAXV; ++v) {
+      const int c = lane * 8 + v * 256;
+      if (c < D) {
+        gu[v] = *reinterpret_cast<const uint4*>(dy + (long)row * D + c);
+        xu[v] = *reinterpret_cast<const uint4*>(x + (long)row * D + c);
+      }
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int v = 0; v < MAXV; ++v) {
+      const int c = lane * 8 + v * 256;
+      if (c < D) {
+        float wv[8];
+        load8f(sw + c, wv);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 g = unpack2(reinterpret_cast<const uint32_t*>(&gu[v])[k]);
+          const float2 xv = unpack2(reinterpret_cast<const uint32_t*>(&xu[v])[k]);
+          const float xh0 = xv.x * r, xh1 = xv.y * r;
+          pacc[(v * 8 + 2 * k) * 32 + lane] += g.x * xh0;
+          pacc[(v * 8 + 2 * k + 1) * 32 + lane] += g.y * xh1;
+          dot += g.x * wv[2 * k] * xh0 + g.y * wv[2 * k + 1] * xh1;
+        }
+      }
+    }
+    dot = warp_sum(dot) / D;
+#pragma unroll
+    for (int v = 0; v < MAXV; ++v) {
+      const int c = lane * 8 + v * 256;
+      if (c < D) {
+        float wv[8], o[8], rr[8];
+        load8f(sw + c, wv);
+        if (dres) load8(dres + (long)row * D + c, rr);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 g = unpack2(reinterpret_cast<const uint32_t*>(&gu[v])[k]);
+          const float2 xv = unpack2(reinterpret_cast<const uint32_t*>(&xu[v])[k]);
+          o[2 * k] = r * (g.x * wv[2 * k] - xv.x * r * dot);
+          o[2 * k + 1] = r * (g.y * wv[2 * k + 1] - xv.y * r * dot);
+        }
+        if (dres) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] += rr[i];
+        }
+        store8(dx + (long)row * D + c, o);
+      }
+    }
+  }
+  __syncthreads();
+  // column c = 256 v + 8 lane + i lives at [(8 v + i) * 32 + lane] of every warp's region
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    const int v = c >> 8, ln = (c & 255) >> 3, i = c & 7;
+    float sum = 0.f;
+    for (int wp = 0; wp < warps; ++wp) sum += sm_rms2[D + wp * (MAXV * 8 * 32) + (v * 8 + i) * 32 + ln];
+    atomicAdd(&dw[c], sum);
+  }
+}
+
 // ----------------------------------------------------------------------------------- embedding
 __global__ void embed_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                                  __nv_bfloat16* __restrict__ out, int T, int D, int V) {
@@ -853,6 +933,31 @@ void launch_rmsnorm_bwd(const void* dy, const void* x, const float* w, const flo
 #define RB(V) rmsnorm_bwd_kernel<V><<<blocks, 256, sm, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, rstd, \
                                                             (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dw, T, D)
   count_launch();
+  if (D % 256 == 0 && D <= 1536) {
+    // shared-memory partials: [D] weights + 8 warps x [D / 256 * 8][32] floats
+    const size_t sm2 = (size_t)D * sizeof(float) + 8 * (size_t)(D / 256) * 8 * 32 * sizeof(float);
+    const int blocks2 = T < 148 * 8 * 3 ? (T + 7) / 8 : 148 * 3;
+#define RB2(V)                                                                                                  \
+  do {                                                                                                          \
+    static bool attr = false;                                                                                   \
+    if (!attr) {                                                                                                \
+      cudaFuncSetAttribute(rmsnorm_bwd_smem_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2); \
+      attr = true;                                                                                              \
+    }                                                                                                           \
+    rmsnorm_bwd_smem_kernel<V><<<blocks2, 256, sm2, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, w, \
+                                                          rstd, (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, \
+                                                          dw, T, D);                                            \
+  } while (0)
+    switch (D / 256) {
+      case 1: RB2(1); return;
+      case 2: RB2(2); return;
+      case 3: RB2(3); return;
+      case 4: RB2(4); return;
+      case 5: RB2(5); return;
+      case 6: RB2(6); return;
+    }
+#undef RB2
+  }
   if (D <= 256) RB(1);
   else if (D <= 512) RB(2);
   else if (D <= 1024) RB(4);

@@ -136,6 +136,9 @@ struct EpArgs {
   size_t flags_off;   // heap offset of the flag area ([purpose][kMaxPeers] ints)
   int purpose, epoch;
   unsigned int* counter;  // local completion counter of the producer kernel
+  // push kernels: only capacity slots [s_lo, s_hi) of each expert (the received counts travel with
+  // the chunk that starts at slot 0), on at most max_blocks CTAs (0: the default grid)
+  int s_lo = 0, s_hi = 1 << 30, max_blocks = 0;
 };
 void launch_ep_dispatch_push(const void* x, const int* perm, const int* counts, const EpArgs& a, cudaStream_t st);
 void launch_ep_combine_bwd_push(const void* dout, const int* perm, const float* wperm, const int* counts,

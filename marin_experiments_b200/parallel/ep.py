@@ -99,6 +99,7 @@ class _MoEEP(torch.autograd.Function):
 
 # flag purposes of the peer exchange
 _DISPATCH, _Y, _DY, _DXP = 0, 1, 2, 3
+_DISPATCH_B = 4  # second capacity-slot chunk of a chunked dispatch
 
 # In-flight microbatch slots. A layer's receive and return buffers stay alive as saved activations
 # until that microbatch's backward; a pipeline schedule with several forwards in flight (1F1B)
@@ -198,6 +199,51 @@ def _span(start):
         _TIMING.append((start, _mark()))
 
 
+def _dispatch_chunked(h, perm, counts, heap, e_loc, cap, half, off_xp, off_cnt, xp_recv, counts_recv, w_gu2d, Hh,
+                      A, dev):
+    """Forward dispatch in two capacity-slot chunks overlapped with the gate/up GEMM of the first
+    (``dispatch_chunks() == 2``). The comm stream pushes chunk A (slots [0, half), with the counts)
+    and chunk B (slots [half, cap)) on ``comm_sms()`` CTAs, each publishing its own flag; the training
+    stream, with its persistent GEMMs capped at the other SMs, waits for chunk A's flags, runs the
+    SwiGLU GEMM over rows [g C, g C + min(count, half)) of every group, then waits for chunk B and
+    runs it over rows [g C + half, g C + count) (the same tensors viewed ``half`` rows later)."""
+    from ..ops import gemm as G
+    from ..ops._ext import err_flag, ext
+
+    my, e = heap.my, counts.numel()
+    two_i, d = w_gu2d.shape[0] // e_loc, w_gu2d.shape[1]
+    nblk = max(2, comm_sms())
+    main = torch.cuda.current_stream(dev)
+    cs = comm_stream(dev)
+    ea, eb = heap.next_epoch(_DISPATCH), heap.next_epoch(_DISPATCH_B)
+    cs.wait_stream(main)
+    with torch.cuda.stream(cs):
+        ext().ep_dispatch_push(h, perm, counts, heap.peers, my, e_loc, cap, off_xp, off_cnt, 0, _DISPATCH, ea,
+                               heap.counter(_DISPATCH), 0, half, nblk)
+        ext().ep_dispatch_push(h, perm, counts, heap.peers, my, e_loc, cap, off_xp, off_cnt, 0, _DISPATCH_B, eb,
+                               heap.counter(_DISPATCH_B), half, 1 << 30, nblk)
+    for t in (h, perm, counts):
+        t.record_stream(cs)
+    budget = max(2, ext().num_sms() - nblk)
+    ext().set_stream_sm_budget(main.cuda_stream, budget)
+    try:
+        t0 = _mark()
+        ext().ep_wait(heap.peers, my, 0, _DISPATCH, ea, err_flag(dev))
+        _span(t0)
+        cnt_a = counts_recv.clamp(max=half)
+        G.gemm(xp_recv, w_gu2d, Hh, G=e, M=half, N=two_i, K=d, counts=cnt_a, ragged=1, a_grp=cap, b_grp=two_i,
+               c_grp=cap, epi="swiglu", c2=A, b_mod=e_loc)
+        t1 = _mark()
+        ext().ep_wait(heap.peers, my, 0, _DISPATCH_B, eb, err_flag(dev))
+        _span(t1)
+        cnt_b = (counts_recv - half).clamp(min=0).to(torch.int32)
+        G.gemm(xp_recv[half:], w_gu2d, Hh[half:], G=e, M=cap - half, N=two_i, K=d, counts=cnt_b, ragged=1,
+               a_grp=cap, b_grp=two_i, c_grp=cap, epi="swiglu", c2=A[half:], b_mod=e_loc)
+    finally:
+        ext().set_stream_sm_budget(main.cuda_stream, 0)
+    main.wait_stream(cs)
+
+
 class _MoEEPFused(torch.autograd.Function):
     """Expert parallelism with the token exchange inside the kernels (NVLink peer memory).
 
@@ -231,17 +277,23 @@ class _MoEEPFused(torch.autograd.Function):
         off_xp = heap.alloc(("xp",) + key, rows * d * 2)
         off_cnt = heap.alloc(("cnt",) + key, e * 4)
         slot, perm, wperm, counts = dispatch_plan(sel, keep, comb, e, cap)
-        ep = heap.next_epoch(_DISPATCH)
-        t0 = _mark()
-        ext().ep_dispatch_push(h, perm, counts, heap.peers, my, e_loc, cap, off_xp, off_cnt, 0, _DISPATCH, ep,
-                               heap.counter(_DISPATCH))
-        ext().ep_wait(heap.peers, my, 0, _DISPATCH, ep, err_flag(dev))
-        _span(t0)
         xp_recv = heap.tensor(off_xp, (rows, d), torch.bfloat16)
         counts_recv = heap.tensor(off_cnt, (e,), torch.int32)
         Hh = torch.empty(rows, two_i, dtype=torch.bfloat16, device=dev)
         A = torch.empty(rows, inter, dtype=torch.bfloat16, device=dev)
-        G.grouped_linear(xp_recv, w_gu.view(e_loc * two_i, d), counts_recv, out=Hh, epi="swiglu", c2=A, n_w=e_loc)
+        half = cap // 2
+        if dispatch_chunks() == 2 and half % 256 == 0 and cap % 256 == 0:
+            _dispatch_chunked(h, perm, counts, heap, e_loc, cap, half, off_xp, off_cnt, xp_recv, counts_recv,
+                              w_gu.view(e_loc * two_i, d), Hh, A, dev)
+        else:
+            ep = heap.next_epoch(_DISPATCH)
+            t0 = _mark()
+            ext().ep_dispatch_push(h, perm, counts, heap.peers, my, e_loc, cap, off_xp, off_cnt, 0, _DISPATCH, ep,
+                                   heap.counter(_DISPATCH))
+            ext().ep_wait(heap.peers, my, 0, _DISPATCH, ep, err_flag(dev))
+            _span(t0)
+            G.grouped_linear(xp_recv, w_gu.view(e_loc * two_i, d), counts_recv, out=Hh, epi="swiglu", c2=A,
+                             n_w=e_loc)
         out = torch.empty(t, d, dtype=torch.bfloat16, device=dev)
         res = None if residual is None else _c(residual)
         if return_mode() == "store":
@@ -386,6 +438,28 @@ def overlap_shared_enabled(h: torch.Tensor, group) -> bool:
     exchange, and ``MXK_EP_OVERLAP=1``."""
     return (h.is_cuda and group is not None and ep_impl() == "peer"
             and os.environ.get("MXK_EP_OVERLAP", "0") == "1")
+
+
+def dispatch_chunks() -> int:
+    """Forward dispatch in capacity-slot chunks (``MXK_EP_CHUNKS``: 1, the default, or 2). With 2, a
+    comm stream pushes slots [0, C/2) and then [C/2, C) of every expert on ``comm_sms()`` CTAs while
+    the training stream, capped at the remaining SMs, waits for the first chunk's flags and runs the
+    gate/up GEMM on those rows as the second chunk crosses NVLink."""
+    n = int(os.environ.get("MXK_EP_CHUNKS", "1"))
+    if n not in (1, 2):
+        raise ValueError(f"MXK_EP_CHUNKS must be 1 or 2, got {n}")
+    return n
+
+
+_COMM: dict[int, torch.cuda.Stream] = {}
+
+
+def comm_stream(dev: torch.device) -> torch.cuda.Stream:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    s = _COMM.get(idx)
+    if s is None:
+        s = _COMM[idx] = torch.cuda.Stream(device=torch.device("cuda", idx))
+    return s
 
 
 def comm_sms() -> int:

@@ -105,7 +105,7 @@ def _worker_impls(rank, world, port, q):
         from marin_experiments_b200.parallel import ep
 
         dev = torch.device("cuda", rank)
-        t, d, inter, e, k = 512, 256, 256, 8, 2
+        t, d, inter, e, k = 2048, 256, 256, 8, 2  # capacity 1024: two 512-slot dispatch chunks
         e_loc = e // world
         lo, hi = rank * e_loc, (rank + 1) * e_loc
 
@@ -121,10 +121,16 @@ def _worker_impls(rank, world, port, q):
         xs = [torch.randn(t, d, generator=gx).bfloat16() for _ in range(3)]
         gouts = [torch.randn(t, d, generator=gx).bfloat16() for _ in range(3)]
         res = {}
-        for impl, ret in (("nccl", "store"), ("peer", "pull"), ("peer", "store")):
+        from marin_experiments_b200.ops._ext import ext
+
+        variants = [("nccl", "store", "1"), ("peer", "pull", "1"), ("peer", "store", "1")]
+        if "s_lo" in (ext().ep_dispatch_push.__doc__ or ""):  # a build with the chunked dispatch
+            variants.append(("peer", "pull", "2"))
+        for impl, ret, chunks in variants:
             os.environ["MXK_EP_IMPL"] = impl
             os.environ["MXK_EP_RETURN"] = ret  # store: rows return inside the GEMM epilogues
-            impl = impl if impl == "nccl" else f"peer-{ret}"
+            os.environ["MXK_EP_CHUNKS"] = chunks  # 2: dispatch in two chunks beside the first GEMM
+            impl = impl if impl == "nccl" else f"peer-{ret}" + ("-chunked" if chunks == "2" else "")
             params = [(param(wr), param(wgu[lo:hi]), param(wdn[lo:hi])) for wr, wgu, wdn in layers]
             outs, grads = [], []
             for it in range(3):
@@ -145,7 +151,7 @@ def _worker_impls(rank, world, port, q):
             return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
 
         errs = []
-        for name in ("peer-pull", "peer-store"):
+        for name in [n for n in ("peer-pull", "peer-store", "peer-pull-chunked") if n in res]:
             got, want = res[name], res["nccl"]
             errs += [rel(a, b) for a, b in zip(got[0] + got[1] + got[2] + got[3],
                                                want[0] + want[1] + want[2] + want[3])]
