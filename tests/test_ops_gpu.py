@@ -57,6 +57,26 @@ def test_rms_gated_norm():
     assert rel(wug.main_grad, wuc.grad) < 3e-2
 
 
+@pytest.mark.parametrize("t,d", [(4096, 1536), (1000, 768), (513, 320)])
+def test_rms_norm_plain(t, d):
+    """Plain RMSNorm at the model width (shared-memory weight-gradient partials for widths that are
+    multiples of 256, the register form otherwise), against the fp32 oracle."""
+    torch.manual_seed(1)
+    x = bf(torch.randn(t, d))
+    w = 1 + 0.1 * torch.randn(d)
+    dout = bf(torch.randn(t, d))
+    xc, wc = cpu_leaf(x), cpu_leaf(w)
+    yc = api.rms_gated_norm(xc, wc, 1e-5)
+    yc.backward(dout)
+    xg = x.cuda().bfloat16().requires_grad_(True)
+    wg = gpu_param(w)
+    yg = api.rms_gated_norm(xg, wg, 1e-5)
+    yg.backward(dout.cuda().bfloat16())
+    assert rel(yg, yc) < 1e-2
+    assert rel(xg.grad, xc.grad) < 2e-2
+    assert rel(wg.main_grad, wc.grad) < 1e-2
+
+
 @pytest.mark.parametrize("hd,heads,kv,window,segs,xsa_gate", [
     (64, 4, 4, 0, False, False),
     (96, 4, 2, 0, True, True),
