@@ -440,9 +440,13 @@ void ep_dispatch_push(const Tensor& x, const Tensor& perm, const Tensor& counts,
 
 void ep_combine_bwd_push(const Tensor& dout, const Tensor& perm, const Tensor& wperm, const Tensor& counts,
                          const std::vector<int64_t>& peers, int64_t my, int64_t e_loc, int64_t cap, int64_t buf_off,
-                         int64_t flags_off, int64_t purpose, int64_t epoch, const Tensor& counter) {
+                         int64_t flags_off, int64_t purpose, int64_t epoch, const Tensor& counter, int64_t s_lo,
+                         int64_t s_hi, int64_t max_blocks) {
   c10::cuda::CUDAGuard g(dout.device());
   auto a = ep_args(peers, my, e_loc, cap, dout.size(1), buf_off, 0, flags_off, purpose, epoch, counter);
+  a.s_lo = (int)s_lo;
+  a.s_hi = (int)s_hi;
+  a.max_blocks = (int)max_blocks;
   mxk::launch_ep_combine_bwd_push(dout.data_ptr(), perm.data_ptr<int>(), wperm.data_ptr<float>(),
                                   counts.data_ptr<int>(), a, stream());
 }
@@ -613,7 +617,10 @@ void register_ops(pybind11::module& m) {
         py::arg("my"), py::arg("e_loc"), py::arg("cap"), py::arg("buf_off"), py::arg("counts_off"),
         py::arg("flags_off"), py::arg("purpose"), py::arg("epoch"), py::arg("counter"), py::arg("s_lo") = 0,
         py::arg("s_hi") = 1 << 30, py::arg("max_blocks") = 0);
-  m.def("ep_combine_bwd_push", &ep_combine_bwd_push);
+  m.def("ep_combine_bwd_push", &ep_combine_bwd_push, py::arg("dout"), py::arg("perm"), py::arg("wperm"),
+        py::arg("counts"), py::arg("peers"), py::arg("my"), py::arg("e_loc"), py::arg("cap"), py::arg("buf_off"),
+        py::arg("flags_off"), py::arg("purpose"), py::arg("epoch"), py::arg("counter"), py::arg("s_lo") = 0,
+        py::arg("s_hi") = 1 << 30, py::arg("max_blocks") = 0);
   m.def("ep_combine_pull", &ep_combine_pull);
   m.def("ep_unpermute_pull", &ep_unpermute_pull);
   m.def("ep_signal", &ep_signal);

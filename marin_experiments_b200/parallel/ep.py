@@ -100,6 +100,7 @@ class _MoEEP(torch.autograd.Function):
 # flag purposes of the peer exchange
 _DISPATCH, _Y, _DY, _DXP = 0, 1, 2, 3
 _DISPATCH_B = 4  # second capacity-slot chunk of a chunked dispatch
+_DY_B = 5  # second chunk of a chunked output-gradient push
 
 # In-flight microbatch slots. A layer's receive and return buffers stay alive as saved activations
 # until that microbatch's backward; a pipeline schedule with several forwards in flight (1F1B)
@@ -244,6 +245,49 @@ def _dispatch_chunked(h, perm, counts, heap, e_loc, cap, half, off_xp, off_cnt, 
     main.wait_stream(cs)
 
 
+def _dy_push_chunked(dout, perm, wperm, counts, heap, e_loc, cap, half, off_dy, dy_recv, counts_recv, w_d2d, Hh,
+                     dev):
+    """Backward mirror of ``_dispatch_chunked``: the comm stream pushes the ``w * dout`` rows in two
+    capacity-slot chunks while the training stream runs the SwiGLU-backward activation-gradient GEMM
+    on the first chunk's rows; returns dH ``[rows, 2I]``."""
+    from ..ops import gemm as G
+    from ..ops._ext import err_flag, ext
+
+    my, e = heap.my, counts.numel()
+    d, inter = w_d2d.shape[0] // e_loc, w_d2d.shape[1]
+    rows = e * cap
+    nblk = max(2, comm_sms())
+    main = torch.cuda.current_stream(dev)
+    cs = comm_stream(dev)
+    ea, eb = heap.next_epoch(_DY), heap.next_epoch(_DY_B)
+    cs.wait_stream(main)
+    with torch.cuda.stream(cs):
+        ext().ep_combine_bwd_push(dout, perm, wperm, counts, heap.peers, my, e_loc, cap, off_dy, 0, _DY, ea,
+                                  heap.counter(_DY), 0, half, nblk)
+        ext().ep_combine_bwd_push(dout, perm, wperm, counts, heap.peers, my, e_loc, cap, off_dy, 0, _DY_B, eb,
+                                  heap.counter(_DY_B), half, 1 << 30, nblk)
+    for t in (dout, perm, wperm, counts):
+        t.record_stream(cs)
+    dH = torch.empty(rows, 2 * inter, dtype=torch.bfloat16, device=dev)
+    ext().set_stream_sm_budget(main.cuda_stream, max(2, ext().num_sms() - nblk))
+    try:
+        t0 = _mark()
+        ext().ep_wait(heap.peers, my, 0, _DY, ea, err_flag(dev))
+        _span(t0)
+        G.gemm(dy_recv, w_d2d, dH, b_mn=True, G=e, M=half, N=inter, K=d, counts=counts_recv.clamp(max=half),
+               ragged=1, a_grp=cap, b_grp=d, c_grp=cap, b_mod=e_loc, epi="swiglu_bwd", r=Hh)
+        t1 = _mark()
+        ext().ep_wait(heap.peers, my, 0, _DY_B, eb, err_flag(dev))
+        _span(t1)
+        G.gemm(dy_recv[half:], w_d2d, dH[half:], b_mn=True, G=e, M=cap - half, N=inter, K=d,
+               counts=(counts_recv - half).clamp(min=0).to(torch.int32), ragged=1, a_grp=cap, b_grp=d, c_grp=cap,
+               b_mod=e_loc, epi="swiglu_bwd", r=Hh[half:])
+    finally:
+        ext().set_stream_sm_budget(main.cuda_stream, 0)
+    main.wait_stream(cs)
+    return dH
+
+
 class _MoEEPFused(torch.autograd.Function):
     """Expert parallelism with the token exchange inside the kernels (NVLink peer memory).
 
@@ -344,17 +388,25 @@ class _MoEEPFused(torch.autograd.Function):
         off_dxp = heap.alloc("dxret" if store else "dxp", rows * d * 2)
         dcomb = torch.empty(sel.shape, dtype=torch.float32, device=dev)
         ext().combine_bwd(dout, y_local, sel, slot, perm, wperm, counts, cap, None, dcomb)
-        edy = heap.next_epoch(_DY)
-        t0 = _mark()
-        ext().ep_combine_bwd_push(dout, perm, wperm, counts, heap.peers, my, e_loc, cap, off_dy, 0, _DY, edy,
-                                  heap.counter(_DY))
-        ext().ep_wait(heap.peers, my, 0, _DY, edy, err_flag(dev))
-        _span(t0)
         dy_recv = heap.tensor(off_dy, (rows, d), torch.bfloat16)
+        half = cap // 2
+        chunked = dispatch_chunks() == 2 and ctx.act == 0 and half % 256 == 0 and cap % 256 == 0
+        if chunked:
+            dH = _dy_push_chunked(dout, perm, wperm, counts, heap, e_loc, cap, half, off_dy, dy_recv, counts_recv,
+                                  w_d.view(e_loc * d, inter), Hh, dev)
+        else:
+            edy = heap.next_epoch(_DY)
+            t0 = _mark()
+            ext().ep_combine_bwd_push(dout, perm, wperm, counts, heap.peers, my, e_loc, cap, off_dy, 0, _DY, edy,
+                                      heap.counter(_DY))
+            ext().ep_wait(heap.peers, my, 0, _DY, edy, err_flag(dev))
+            _span(t0)
         # the receive buffers are reused by the next exchange: weight gradients run now, never deferred
         with G.defer_weight_grads(None):
             if ctx.act == 0:  # SiLU gate: the activation-gradient GEMM writes dH in its epilogue
-                dH = G.grouped_linear_dx(dy_recv, w_d.view(e_loc * d, inter), counts_recv, n_w=e_loc, swiglu_h=Hh)
+                if not chunked:
+                    dH = G.grouped_linear_dx(dy_recv, w_d.view(e_loc * d, inter), counts_recv, n_w=e_loc,
+                                             swiglu_h=Hh)
                 G.grouped_linear_dw(dy_recv, A, counts_recv, out=_mg(w_d).view(e_loc * d, inter), n_w=e_loc)
             else:
                 dA = G.grouped_linear_dx(dy_recv, w_d.view(e_loc * d, inter), counts_recv, n_w=e_loc)
