@@ -456,17 +456,19 @@ def main(argv=None):
     # ------------------------------------------- exposed token exchange (one extra, untimed step)
     # Device time spent in the expert-parallel exchange kernels and their cross-rank waits, summed
     # from CUDA events around each exchange (nothing else runs on the stream meanwhile); max over ranks.
-    exposed = 0.0
+    # The same step also times the training stream's gradient synchronisation (the data-parallel
+    # all-reduce or ZeRO reduce-scatter / all-gather that backward did not hide).
+    exposed = exposed_dp = 0.0
     if ctx is not None:
+        from marin_experiments_b200.parallel.dist import dp_timing
         from marin_experiments_b200.parallel.ep import exchange_timing
 
         barrier()
-        with exchange_timing() as xt:
+        with exchange_timing() as xt, dp_timing() as dt:
             trainer.train_step(staged[0])
-        exposed = xt.ms()
-        xt_t = torch.tensor([exposed], device=trainer.device)
+        xt_t = torch.tensor([xt.ms(), dt.ms()], device=trainer.device)
         torch.distributed.all_reduce(xt_t, op=torch.distributed.ReduceOp.MAX)
-        exposed = float(xt_t.item())
+        exposed, exposed_dp = (float(v) for v in xt_t.tolist())
     if args.profile_trace:
         from marin_experiments_b200.utils.analysis import breakdown_table, profile_call
 
@@ -495,7 +497,7 @@ def main(argv=None):
         "mfu": mfu, "mfu_denominator": f"{flop_peak / 1e12:.1f} TFLOP/s per GPU, {peak_label}",
         "mfu_nominal": mfu_nominal, "mfu_nominal_denominator": "2250 TFLOP/s per GPU, nominal dense bf16",
         "ms_x_median_mhz": ms * clk["sm_mhz"] if clk.get("sm_mhz") else None,
-        "exposed_all_to_all_ms_per_step": exposed, "peak_memory_gb": float(peak.item()), "flops_per_token": fpt, "loss": loss,
+        "exposed_all_to_all_ms_per_step": exposed, "exposed_dp_sync_ms_per_step": exposed_dp, "peak_memory_gb": float(peak.item()), "flops_per_token": fpt, "loss": loss,
         "clocks": clk, "gpu_launches": int(launches),
         "e2e": e2e,
     }

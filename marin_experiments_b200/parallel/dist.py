@@ -17,6 +17,45 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as torch_dist
 
+# Gradient-sync timing: while installed (``dp_timing``), each ``grad_sync`` records CUDA events on
+# the training stream around its part of the step -- the wait for reductions still running on the
+# gradient stream plus the reductions left to do -- i.e. the data-parallel communication the step
+# does not hide behind backward.
+_DP_TIMING: list | None = None
+
+
+class dp_timing:
+    """``with dp_timing() as t: ...; t.ms()`` -- device milliseconds the training stream spent in
+    gradient synchronisation inside the block."""
+
+    def __enter__(self):
+        global _DP_TIMING
+        self.pairs = []
+        _DP_TIMING = self.pairs
+        return self
+
+    def __exit__(self, *exc):
+        global _DP_TIMING
+        _DP_TIMING = None
+        return False
+
+    def ms(self) -> float:
+        torch.cuda.synchronize()
+        return float(sum(a.elapsed_time(b) for a, b in self.pairs))
+
+
+def _dp_mark():
+    if _DP_TIMING is None or not torch.cuda.is_available():
+        return None
+    ev = torch.cuda.Event(enable_timing=True)
+    ev.record()
+    return ev
+
+
+def _dp_span(start):
+    if start is not None and _DP_TIMING is not None:
+        _DP_TIMING.append((start, _dp_mark()))
+
 
 @dataclass
 class DistContext:
@@ -93,6 +132,11 @@ class DistContext:
         opt.norm_hook = norm_hook
 
     def grad_sync(self, trainer) -> None:
+        t0 = _dp_mark()
+        self._grad_sync(trainer)
+        _dp_span(t0)
+
+    def _grad_sync(self, trainer) -> None:
         """Mean-all-reduce the gradients of replicated parameters (bucketed over the flat buffer).
 
         Expert shards already hold the sum over every rank's tokens of per-rank mean-loss gradients;

@@ -203,7 +203,7 @@ class ZeroDistContext(DistContext):
             if x1 > x0:
                 st.master[x0:x1] = got[r, x0 - a: x1 - a]
 
-    def grad_sync(self, trainer) -> None:
+    def _grad_sync(self, trainer) -> None:
         st = trainer.store
         lo, hi = self._shard
         region = st.grad[: self._end]
@@ -227,6 +227,13 @@ class ZeroDistContext(DistContext):
         self._muon_grads_to_owners(st)
 
     def post_step(self, trainer) -> None:
+        from .dist import _dp_mark, _dp_span
+
+        t0 = _dp_mark()
+        self._post_step(trainer)
+        _dp_span(t0)
+
+    def _post_step(self, trainer) -> None:
         st = trainer.store
         lo, hi = self._shard
         region = st.master[: self._end]
