@@ -456,6 +456,46 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ Y, const int* _
   }
 }
 
+// The same two gathers with all of a token's K rows in flight: lanes 0..K-1 read the token's
+// (slot, expert, weight) once and broadcast them, and each 16-byte chunk issues its K loads before
+// accumulating (the loops above wait for one row's load at a time). W = nullptr: unit weights.
+template <int KMAX>
+__global__ void gather_k_kernel(const __nv_bfloat16* __restrict__ Y, const int* __restrict__ sel,
+                                const int* __restrict__ slot, const float* __restrict__ W,
+                                const __nv_bfloat16* __restrict__ add, __nv_bfloat16* __restrict__ out, int T, int K,
+                                int cap, int D) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+    int s = -1, e = 0;
+    float wk = 1.f;
+    if (lane < K) {
+      s = slot[(long)t * K + lane];
+      e = sel[(long)t * K + lane];
+      if (W) wk = W[(long)t * K + lane];
+    }
+    const uint4* src[KMAX];
+    float w[KMAX];
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      const int sk = __shfl_sync(0xffffffffu, s, k), ek = __shfl_sync(0xffffffffu, e, k);
+      w[k] = __shfl_sync(0xffffffffu, wk, k);
+      src[k] = (k < K && sk >= 0) ? reinterpret_cast<const uint4*>(Y + ((long)ek * cap + sk) * D) : nullptr;
+    }
+    for (int c = lane; c < D / 8; c += 32) {
+      uint4 v[KMAX];
+#pragma unroll
+      for (int k = 0; k < KMAX; ++k)
+        if (src[k]) v[k] = src[k][c];
+      float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (add) acc8(a, reinterpret_cast<const uint4*>(add + (long)t * D)[c], 1.f);
+#pragma unroll
+      for (int k = 0; k < KMAX; ++k)
+        if (src[k]) acc8(a, v[k], w[k]);
+      reinterpret_cast<uint4*>(out + (long)t * D)[c] = pack8(a);
+    }
+  }
+}
+
 // dY[e*C+s] = wperm * dout[perm] (zeros on pad rows up to round128(count)).
 __global__ void combine_bwd_rows_kernel(const __nv_bfloat16* __restrict__ dout, const int* __restrict__ perm,
                                         const float* __restrict__ wperm, const int* __restrict__ counts, int cap,
@@ -630,9 +670,26 @@ void launch_permute(const void* x, const int* perm, const int* counts, int cap, 
                                                              (__nv_bfloat16*)xp);
 }
 
+static bool gather_k(const void* Y, const int* sel, const int* slot, const float* W, const void* add, void* out,
+                     int T, int K, int cap, int D, cudaStream_t st) {
+  const auto* y = (const __nv_bfloat16*)Y;
+  const auto* ad = (const __nv_bfloat16*)add;
+  auto* o = (__nv_bfloat16*)out;
+  if (K <= 4) {
+    gather_k_kernel<4><<<grid_for(T, 8), 256, 0, st>>>(y, sel, slot, W, ad, o, T, K, cap, D);
+    return true;
+  }
+  if (K <= 8) {
+    gather_k_kernel<8><<<grid_for(T, 8), 256, 0, st>>>(y, sel, slot, W, ad, o, T, K, cap, D);
+    return true;
+  }
+  return false;
+}
+
 void launch_combine(const void* Y, const int* sel, const int* slot, const float* comb, const void* residual,
                     void* out, int T, int K, int cap, int D, cudaStream_t st) {
   count_launch();
+  if (gather_k(Y, sel, slot, comb, residual, out, T, K, cap, D, st)) return;
   combine_kernel<<<grid_for(T, 8), 256, 0, st>>>((const __nv_bfloat16*)Y, sel, slot, comb,
                                                  (const __nv_bfloat16*)residual, (__nv_bfloat16*)out, T, K, cap, D);
 }
@@ -653,6 +710,7 @@ void launch_combine_bwd(const void* dout, const void* Y, const int* sel, const i
 void launch_unpermute_add(const void* dxp, const int* sel, const int* slot, const void* dx_in, void* dx, int T, int K,
                           int cap, int D, cudaStream_t st) {
   count_launch();
+  if (gather_k(dxp, sel, slot, nullptr, dx_in, dx, T, K, cap, D, st)) return;
   unpermute_add_kernel<<<grid_for(T, 8), 256, 0, st>>>((const __nv_bfloat16*)dxp, sel, slot,
                                                        (const __nv_bfloat16*)dx_in, (__nv_bfloat16*)dx, T, K, cap, D);
 }
