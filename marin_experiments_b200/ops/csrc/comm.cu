@@ -260,6 +260,122 @@ __global__ void ep_push_v2_kernel(const __nv_bfloat16* __restrict__ x, const int
   publish(a.peers, a.world, a.my, a.flags_off, a.purpose, a.epoch, a.counter);
 }
 
+// Pushes through the copy engine: one warp per CTA streams its rows through a ring of kPushSlots
+// shared-memory row slots -- a bulk load of the local source row (x[perm[r]]), then, kPushLag rows
+// later, a bulk store of the slot into the owner's buffer -- so a handful of CTAs keeps megabytes in
+// flight (the thread-copy kernels need most of the GPU's warps for the same bandwidth). Pad rows are
+// stored from a zero row. SCALED: the warp multiplies the row by its combine weight in shared memory
+// between the load and the store. The slot of row n was last stored by row n - kPushSlots; waiting
+// until at most kPushLag - 1 bulk groups are still reading shared memory retires that store.
+constexpr int kPushSlots = 32, kPushLag = 16;
+
+template <bool SCALED>
+__global__ void __launch_bounds__(32) ep_push_bulk_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const int* __restrict__ perm,
+                                                          const float* __restrict__ wperm,
+                                                          const int* __restrict__ counts, EpArgs a) {
+  extern __shared__ __align__(128) uint8_t sm_push[];
+  __shared__ int abort_sm;
+  const int lane = threadIdx.x;
+  const uint32_t rb = (uint32_t)a.D * 2;  // row bytes, a multiple of 16
+  uint8_t* zero = sm_push;
+  uint8_t* slots = sm_push + rb;
+  uint64_t* full = reinterpret_cast<uint64_t*>(slots + (size_t)kPushSlots * rb);
+  uint64_t* meta_dst = full + kPushSlots;                               // [slots] destination row
+  float* meta_w = reinterpret_cast<float*>(meta_dst + kPushSlots);     // [slots] weight (SCALED)
+  int* meta_kind = reinterpret_cast<int*>(meta_w + kPushSlots);        // [slots] 0 row, 1 zero row
+  const int E = a.e_loc * a.world;
+  if (!SCALED && blockIdx.x == 0 && a.s_lo == 0)
+    for (int e = lane; e < E; e += 32) {
+      int* dst = reinterpret_cast<int*>(peer_ptr(a.peers, e / a.e_loc, a.counts_off));
+      dst[a.my * a.e_loc + e % a.e_loc] = counts[e];
+    }
+  for (uint32_t i = lane; i < rb / 16; i += 32) reinterpret_cast<uint4*>(zero)[i] = make_uint4(0, 0, 0, 0);
+  if (lane == 0) {
+    for (int i = 0; i < kPushSlots; ++i) mbar_init(&full[i], 1);
+    abort_sm = 0;
+    fence_barrier_init();
+  }
+  fence_proxy_async_smem();  // the zero row is read by bulk stores
+  __syncwarp();
+  const long total = (long)E * a.cap;
+  long r = blockIdx.x;
+  bool more = true, ok = true;
+  int n = 0, rows = -1;  // rows: number of this CTA's rows, known once the scan ends
+  for (;; ++n) {
+    // issue row n
+    if (more) {
+      int e = 0, s = 0, c = 0;
+      bool found = false;
+      for (; r < total; r += gridDim.x) {
+        e = (int)(r / a.cap);
+        s = (int)(r % a.cap);
+        c = counts[e];
+        if (s < round128(c) && s >= a.s_lo && s < a.s_hi) {
+          found = true;
+          break;
+        }
+      }
+      if (!found) {
+        more = false;
+        rows = n;
+      } else {
+        const int slot = n % kPushSlots;
+        if (lane == 0) {
+          if (n >= kPushSlots) bulk_wait_read<kPushLag - 1>();
+          uint4* dst = reinterpret_cast<uint4*>(peer_ptr(a.peers, e / a.e_loc, a.buf_off)) +
+                       remote_row(e, s, a.e_loc, a.cap, a.my) * (a.D / 8);
+          meta_dst[slot] = reinterpret_cast<uint64_t>(dst);
+          meta_kind[slot] = s < c ? 0 : 1;
+          if (SCALED) meta_w[slot] = s < c ? wperm[r] : 0.f;
+          if (s < c) {
+            mbar_arrive_expect_tx(&full[slot], rb);
+            bulk_load(slots + (size_t)slot * rb, x + (long)perm[r] * a.D, rb, &full[slot]);
+          } else {
+            mbar_arrive(&full[slot]);
+          }
+        }
+        r += gridDim.x;
+      }
+    }
+    // finish row n - kPushLag
+    const int m = n - kPushLag;
+    if (m >= 0 && (rows < 0 || m < rows)) {
+      const int slot = m % kPushSlots;
+      bool got = true;
+      // a failed wait skips the publish: the peers' bounded flag waits then report the timeout
+      if (lane == 0) got = mbar_wait(&full[slot], (m / kPushSlots) & 1, nullptr, kErrTimeoutPeer, &abort_sm);
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) {
+        ok = false;
+        break;
+      }
+      __syncwarp();
+      const int kind = meta_kind[slot];
+      uint8_t* src = kind ? zero : slots + (size_t)slot * rb;
+      if (SCALED && kind == 0) {
+        const float w = meta_w[slot];
+        uint4* row = reinterpret_cast<uint4*>(src);
+        for (uint32_t i = lane; i < rb / 16; i += 32) {
+          float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+          acc8(f, row[i], w);
+          row[i] = pack8(f);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
+      if (lane == 0) {
+        bulk_store(reinterpret_cast<void*>(meta_dst[slot]), src, rb);
+        bulk_commit();
+      }
+    }
+    if (!more && m + 1 >= rows) break;
+  }
+  if (lane == 0) bulk_wait_all();  // every store has landed in the peers' memory
+  __syncwarp();
+  if (ok) publish(a.peers, a.world, a.my, a.flags_off, a.purpose, a.epoch, a.counter);
+}
+
 // Pulls with all of a token's K rows in flight at once. The kernels above walk k inside the chunk
 // loop, so each 16-byte peer load waits for the previous one (and the slot / expert lookups are
 // repeated per chunk): a chain of K dependent NVLink round trips per chunk. Here lanes 0..K-1 read
@@ -431,9 +547,39 @@ static bool xchg_v2() {
   return v2;
 }
 
+// MXK_EP_PUSH=bulk: copy-engine pushes for the single-exchange path too (chunked dispatches, which
+// run beside a GEMM on few CTAs, always use them)
+static bool push_bulk_default() {
+  static const bool on = [] {
+    const char* e = std::getenv("MXK_EP_PUSH");
+    return e && std::string(e) == "bulk";
+  }();
+  return on;
+}
+
+template <bool SCALED>
+static bool launch_push_bulk(const void* x, const int* perm, const float* wperm, const int* counts, const EpArgs& a,
+                             cudaStream_t st) {
+  if (!(a.max_blocks > 0 || push_bulk_default()) || a.D % 8) return false;
+  const size_t rb = (size_t)a.D * 2;
+  const size_t smem = rb * (kPushSlots + 1) + kPushSlots * (8 + 8 + 4 + 4);
+  if (smem > 220 * 1024) return false;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(ep_push_bulk_kernel<SCALED>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) !=
+        cudaSuccess)
+      return false;
+    attr = true;
+  }
+  const int g = a.max_blocks > 0 ? a.max_blocks : 64;
+  ep_push_bulk_kernel<SCALED><<<g, 32, smem, st>>>((const __nv_bfloat16*)x, perm, wperm, counts, a);
+  return true;
+}
+
 template <bool SCALED>
 static bool launch_push_v2(const void* x, const int* perm, const float* wperm, const int* counts, const EpArgs& a,
                            cudaStream_t st) {
+  if (launch_push_bulk<SCALED>(x, perm, wperm, counts, a, st)) return true;
   if (!xchg_v2() || a.D % 256) return false;
   int g = grid_rows((long)a.e_loc * a.world * a.cap);
   if (a.max_blocks > 0 && g > a.max_blocks) g = a.max_blocks;

@@ -123,6 +123,21 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* tm, const v
                : "memory");
 }
 
+// Untiled bulk copies (the copy engine moves `bytes` -- a multiple of 16, both addresses 16-byte
+// aligned -- without the issuing thread touching the data): global -> this CTA's shared memory
+// (completion counted on an mbarrier), and shared memory -> global (a bulk group).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_store(void* gdst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(smem_src)),
+               "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Wait until at most N bulk groups of this thread still read their smem source.

@@ -217,7 +217,7 @@ CATEGORIES = [
     (r"gemm_sm100", "GEMM (tcgen05)"),
     (r"gemm|cutlass|cublas|\bsm\d+_xmma", "GEMM (library)"),
     (r"router|qb_beta", "router / QB"),
-    (r"plan_|noalloc_|permute|combine", "MoE dispatch / combine"),
+    (r"plan_|noalloc_|permute|combine|gather_k|ep_push|ep_wait|ep_signal|ep_dispatch|ep_unpermute", "MoE dispatch / combine"),
     (r"\bce_", "cross-entropy"),
     (r"adamh|moments_|sqnorm|\bema_|optim", "optimizer"),
     (r"rmsnorm|qk_norm|head_norm|xsa_gate|gate_mul", "norms / rope / gates"),
