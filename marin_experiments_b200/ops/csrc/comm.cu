@@ -260,14 +260,14 @@ __global__ void ep_push_v2_kernel(const __nv_bfloat16* __restrict__ x, const int
   publish(a.peers, a.world, a.my, a.flags_off, a.purpose, a.epoch, a.counter);
 }
 
-// Pushes through the copy engine: one warp per CTA streams its rows through a ring of kPushSlots
-// shared-memory row slots -- a bulk load of the local source row (x[perm[r]]), then, kPushLag rows
-// later, a bulk store of the slot into the owner's buffer -- so a handful of CTAs keeps megabytes in
-// flight (the thread-copy kernels need most of the GPU's warps for the same bandwidth). Pad rows are
-// stored from a zero row. SCALED: the warp multiplies the row by its combine weight in shared memory
-// between the load and the store. The slot of row n was last stored by row n - kPushSlots; waiting
-// until at most kPushLag - 1 bulk groups are still reading shared memory retires that store.
-constexpr int kPushSlots = 32, kPushLag = 16;
+// Pushes through the copy engine, by tiles of 32 consecutive capacity slots of one expert: the
+// warp's 32 lanes each issue one row's bulk load (x[perm[r]], local) into the tile's shared-memory
+// slot, pad rows are zero-filled in place, and one bulk store moves the whole tile (up to 96 KB,
+// contiguous in the owner's buffer) over NVLink. Two tile slots alternate, so a tile's loads run
+// while the previous tile is being stored; a handful of CTAs keeps NVLink busy, which is what a
+// dispatch running beside a GEMM on few SMs needs. SCALED: the warp multiplies each row by its
+// combine weight in shared memory between the loads and the store.
+constexpr int kTileRows = 32;
 
 template <bool SCALED>
 __global__ void __launch_bounds__(32) ep_push_bulk_kernel(const __nv_bfloat16* __restrict__ x,
@@ -275,101 +275,108 @@ __global__ void __launch_bounds__(32) ep_push_bulk_kernel(const __nv_bfloat16* _
                                                           const float* __restrict__ wperm,
                                                           const int* __restrict__ counts, EpArgs a) {
   extern __shared__ __align__(128) uint8_t sm_push[];
+  __shared__ uint64_t full[2];
   __shared__ int abort_sm;
   const int lane = threadIdx.x;
-  const uint32_t rb = (uint32_t)a.D * 2;  // row bytes, a multiple of 16
-  uint8_t* zero = sm_push;
-  uint8_t* slots = sm_push + rb;
-  uint64_t* full = reinterpret_cast<uint64_t*>(slots + (size_t)kPushSlots * rb);
-  uint64_t* meta_dst = full + kPushSlots;                               // [slots] destination row
-  float* meta_w = reinterpret_cast<float*>(meta_dst + kPushSlots);     // [slots] weight (SCALED)
-  int* meta_kind = reinterpret_cast<int*>(meta_w + kPushSlots);        // [slots] 0 row, 1 zero row
+  const uint32_t rb = (uint32_t)a.D * 2;                     // row bytes, a multiple of 16
+  const size_t tile_bytes = (size_t)kTileRows * rb;
   const int E = a.e_loc * a.world;
   if (!SCALED && blockIdx.x == 0 && a.s_lo == 0)
     for (int e = lane; e < E; e += 32) {
       int* dst = reinterpret_cast<int*>(peer_ptr(a.peers, e / a.e_loc, a.counts_off));
       dst[a.my * a.e_loc + e % a.e_loc] = counts[e];
     }
-  for (uint32_t i = lane; i < rb / 16; i += 32) reinterpret_cast<uint4*>(zero)[i] = make_uint4(0, 0, 0, 0);
   if (lane == 0) {
-    for (int i = 0; i < kPushSlots; ++i) mbar_init(&full[i], 1);
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
     abort_sm = 0;
     fence_barrier_init();
   }
-  fence_proxy_async_smem();  // the zero row is read by bulk stores
   __syncwarp();
-  const long total = (long)E * a.cap;
-  long r = blockIdx.x;
-  bool more = true, ok = true;
-  int n = 0, rows = -1;  // rows: number of this CTA's rows, known once the scan ends
-  for (;; ++n) {
-    // issue row n
-    if (more) {
-      int e = 0, s = 0, c = 0;
-      bool found = false;
-      for (; r < total; r += gridDim.x) {
-        e = (int)(r / a.cap);
-        s = (int)(r % a.cap);
+  // tiles of expert e: slots [lo, hi) = [s_lo, min(s_hi, round128(count))) in steps of 32; the CTA
+  // takes global tile indices blockIdx.x, blockIdx.x + gridDim.x, ... (walking the experts once)
+  int e = 0, t0 = 0;  // expert of the next tile, global index of that expert's first tile
+  auto tiles_of = [&](int ee) {
+    const int hi = min(a.s_hi, round128(counts[ee])), lo = a.s_lo;
+    return hi > lo ? (hi - lo + kTileRows - 1) / kTileRows : 0;
+  };
+  int nt_e = E > 0 ? tiles_of(0) : 0;
+  bool ok = true;
+  int it = 0;
+  int pend_e = -1, pend_s0 = 0, pend_n = 0, pend_c = 0;  // the tile whose loads are in flight
+  for (int t = blockIdx.x;; t += gridDim.x, ++it) {
+    // locate global tile t (t only grows, so the expert walk is shared by the whole loop)
+    bool have = false;
+    int te = 0, s0 = 0, n = 0, c = 0;
+    while (e < E) {
+      if (t < t0 + nt_e) {
+        te = e;
         c = counts[e];
-        if (s < round128(c) && s >= a.s_lo && s < a.s_hi) {
-          found = true;
-          break;
-        }
+        s0 = a.s_lo + (t - t0) * kTileRows;
+        n = min(kTileRows, min(a.s_hi, round128(c)) - s0);
+        have = true;
+        break;
       }
-      if (!found) {
-        more = false;
-        rows = n;
-      } else {
-        const int slot = n % kPushSlots;
-        if (lane == 0) {
-          if (n >= kPushSlots) bulk_wait_read<kPushLag - 1>();
-          uint4* dst = reinterpret_cast<uint4*>(peer_ptr(a.peers, e / a.e_loc, a.buf_off)) +
-                       remote_row(e, s, a.e_loc, a.cap, a.my) * (a.D / 8);
-          meta_dst[slot] = reinterpret_cast<uint64_t>(dst);
-          meta_kind[slot] = s < c ? 0 : 1;
-          if (SCALED) meta_w[slot] = s < c ? wperm[r] : 0.f;
-          if (s < c) {
-            mbar_arrive_expect_tx(&full[slot], rb);
-            bulk_load(slots + (size_t)slot * rb, x + (long)perm[r] * a.D, rb, &full[slot]);
-          } else {
-            mbar_arrive(&full[slot]);
-          }
+      t0 += nt_e;
+      ++e;
+      if (e < E) nt_e = tiles_of(e);
+    }
+    if (have) {
+      const int slot = it & 1;
+      uint8_t* buf = sm_push + slot * tile_bytes;
+      if (lane == 0) {
+        if (it >= 2) bulk_wait_read<0>();  // the slot's previous tile has been read by its store
+        uint32_t real = 0;
+        for (int i = 0; i < n; ++i) real += (s0 + i < c) ? rb : 0;
+        mbar_arrive_expect_tx(&full[slot], real);
+      }
+      __syncwarp();
+      const int s = s0 + lane;
+      if (lane < n) {
+        uint8_t* row = buf + (size_t)lane * rb;
+        if (s < c) {
+          bulk_load(row, x + (long)perm[(long)te * a.cap + s] * a.D, rb, &full[slot]);
+        } else {
+          for (uint32_t i = 0; i < rb / 16; ++i) reinterpret_cast<uint4*>(row)[i] = make_uint4(0, 0, 0, 0);
         }
-        r += gridDim.x;
       }
     }
-    // finish row n - kPushLag
-    const int m = n - kPushLag;
-    if (m >= 0 && (rows < 0 || m < rows)) {
-      const int slot = m % kPushSlots;
-      bool got = true;
-      // a failed wait skips the publish: the peers' bounded flag waits then report the timeout
-      if (lane == 0) got = mbar_wait(&full[slot], (m / kPushSlots) & 1, nullptr, kErrTimeoutPeer, &abort_sm);
-      got = __shfl_sync(0xffffffffu, got, 0);
-      if (!got) {
+    // store the tile loaded in the previous iteration
+    if (pend_e >= 0) {
+      const int slot = (it - 1) & 1;
+      uint8_t* buf = sm_push + slot * tile_bytes;
+      // every lane observes the phase (the scaling reads the loaded rows)
+      const bool got = mbar_wait(&full[slot], ((it - 1) >> 1) & 1, nullptr, kErrTimeoutPeer, &abort_sm);
+      if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
       }
-      __syncwarp();
-      const int kind = meta_kind[slot];
-      uint8_t* src = kind ? zero : slots + (size_t)slot * rb;
-      if (SCALED && kind == 0) {
-        const float w = meta_w[slot];
-        uint4* row = reinterpret_cast<uint4*>(src);
-        for (uint32_t i = lane; i < rb / 16; i += 32) {
-          float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-          acc8(f, row[i], w);
-          row[i] = pack8(f);
+      if (SCALED) {
+        for (int i = 0; i < pend_n; ++i) {
+          if (pend_s0 + i >= pend_c) break;
+          const float w = wperm[(long)pend_e * a.cap + pend_s0 + i];
+          uint4* row = reinterpret_cast<uint4*>(buf + (size_t)i * rb);
+          for (uint32_t k = lane; k < rb / 16; k += 32) {
+            float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            acc8(f, row[k], w);
+            row[k] = pack8(f);
+          }
         }
-        fence_proxy_async_smem();
-        __syncwarp();
       }
+      fence_proxy_async_smem();  // zero-filled pad rows (and scaled rows) are read by the bulk store
+      __syncwarp();
       if (lane == 0) {
-        bulk_store(reinterpret_cast<void*>(meta_dst[slot]), src, rb);
+        uint4* dst = reinterpret_cast<uint4*>(peer_ptr(a.peers, pend_e / a.e_loc, a.buf_off)) +
+                     remote_row(pend_e, pend_s0, a.e_loc, a.cap, a.my) * (a.D / 8);
+        bulk_store(dst, buf, (uint32_t)pend_n * rb);
         bulk_commit();
       }
     }
-    if (!more && m + 1 >= rows) break;
+    if (!have) break;
+    pend_e = te;
+    pend_s0 = s0;
+    pend_n = n;
+    pend_c = c;
   }
   if (lane == 0) bulk_wait_all();  // every store has landed in the peers' memory
   __syncwarp();
@@ -562,7 +569,7 @@ static bool launch_push_bulk(const void* x, const int* perm, const float* wperm,
                              cudaStream_t st) {
   if (!(a.max_blocks > 0 || push_bulk_default()) || a.D % 8) return false;
   const size_t rb = (size_t)a.D * 2;
-  const size_t smem = rb * (kPushSlots + 1) + kPushSlots * (8 + 8 + 4 + 4);
+  const size_t smem = 2 * kTileRows * rb;  // two 32-row tile slots
   if (smem > 220 * 1024) return false;
   static bool attr = false;
   if (!attr) {
@@ -571,7 +578,7 @@ static bool launch_push_bulk(const void* x, const int* perm, const float* wperm,
       return false;
     attr = true;
   }
-  const int g = a.max_blocks > 0 ? a.max_blocks : 64;
+  const int g = a.max_blocks > 0 ? a.max_blocks : 32;
   ep_push_bulk_kernel<SCALED><<<g, 32, smem, st>>>((const __nv_bfloat16*)x, perm, wperm, counts, a);
   return true;
 }
