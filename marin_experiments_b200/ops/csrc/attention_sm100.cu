@@ -1118,6 +1118,369 @@ __global__ void __launch_bounds__(kThreadsPP, 1)
   }
 }
 
+// Persistent separate-P forward: one CTA per SM loops over work items (a pair of 128-query tiles of
+// one head), so a CTA's start-up -- TMEM allocation, barrier set-up, the Q load and the first K / V
+// loads -- is paid once, and each item's epilogue (O normalised and stored by the softmax warps)
+// overlaps the next item's Q / K / V loads and first S products. Items are taken round-robin in the
+// longest-first order. Every barrier keeps counting phases across items: the MMA issuer and the
+// softmax warps track global S / PV / block counts per tile; O is reused by the next item's first PV
+// only after the softmax warps have read it (o_free), and Q only after the item's last S (q_empty).
+struct SpItem {
+  int h, b, kh, q0, base, kb_lo, nb, lo_t[2], nb_t[2];
+};
+
+__device__ __forceinline__ SpItem sp_item(int item, const FwdArgs& a, int nqt) {
+  SpItem w;
+  const int nhb = a.H * a.B;
+  w.h = (item % nhb) % a.H;
+  w.b = (item % nhb) / a.H;
+  w.kh = w.h / (a.H / a.Hkv);
+  w.q0 = (nqt - 1 - item / nhb) * 2 * BM;
+  w.base = w.b * a.S;
+  w.kb_lo = 0;
+  if (a.window > 0) w.kb_lo = max(0, w.q0 - a.window + 1) / BNS;
+  const int kb_hi1 = (min(a.S, w.q0 + 2 * BM) + BNS - 1) / BNS;
+  const int kb_hi0 = (min(a.S, w.q0 + BM) + BNS - 1) / BNS;
+  w.nb = max(kb_hi1 - w.kb_lo, 0);
+  w.nb_t[0] = max(kb_hi0 - w.kb_lo, 0);
+  w.nb_t[1] = w.nb;
+  w.lo_t[0] = 0;
+  w.lo_t[1] = 0;
+  if (a.window > 0) w.lo_t[1] = max(0, (w.q0 + BM - a.window + 1) / BNS - w.kb_lo);
+  if (w.q0 + BM >= a.S) w.nb_t[1] = 0;
+  return w;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreadsPP, 1)
+    fa_fwd_sm100_spp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                            const __grid_constant__ CUtensorMap tmV, const FwdArgs a, int n_items) {
+  static_assert(HD <= 96, "separate-P layout needs O to fit 96 columns per tile");
+  using SM = SmemSP<HD>;
+  constexpr int KCH = SM::KCH;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + 2 * SM::kTileQ;
+  uint8_t* sV = sK + kStagesSP * SM::kTileKV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBarOff);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* kv_full = bars + 2;                 // [stages]
+  uint64_t* kv_empty = bars + 2 + kStagesSP;    // [stages]
+  uint64_t* s_full = bars + 2 + 2 * kStagesSP;  // [2] per tile
+  uint64_t* s_free = s_full + 2;                // [2], 128 arrivals
+  uint64_t* p_full = s_full + 4;                // [2], 128 arrivals
+  uint64_t* o_done = s_full + 6;                // [2]
+  uint64_t* o_free = s_full + 8;                // [2], 128 arrivals
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqt = (a.S + 2 * BM - 1) / (2 * BM);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int i = 0; i < kStagesSP; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+      mbar_init(&o_free[i], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 9) {
+    // ------------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int qi = 0;
+      long kvc = 0;  // global K / V block count: stage and phase
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        const SpItem w = sp_item(item, a, nqt);
+        if (w.nb == 0) continue;
+        if (!mbar_wait(q_empty, (qi & 1) ^ 1, a.err, kErrTimeoutProducer, abort_flag)) break;
+        mbar_arrive_expect_tx(q_full, 2 * SM::kTileQ);
+        for (int t = 0; t < 2; ++t)
+          for (int c = 0; c < KCH; ++c)
+            tma_load_2d(&tmQ, q_full, sQ + t * SM::kTileQ + c * BM * 128, a.q_x0 + w.h * HD + c * 64,
+                        w.base + w.q0 + t * BM);
+        ++qi;
+        for (int j = 0; j < w.nb; ++j, ++kvc) {
+          const int st = (int)(kvc % kStagesSP);
+          const int kr = w.base + (w.kb_lo + j) * BNS;
+          if (!mbar_wait(&kv_empty[st], ((kvc / kStagesSP) & 1) ^ 1, a.err, kErrTimeoutProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&kv_full[st], 2 * SM::kTileKV);
+          for (int c = 0; c < KCH; ++c) {
+            tma_load_2d(&tmK, &kv_full[st], sK + st * SM::kTileKV + c * BNS * 128, a.k_x0 + w.kh * HD + c * 64, kr);
+            tma_load_2d(&tmV, &kv_full[st], sV + st * SM::kTileKV + c * BNS * 128, a.v_x0 + w.kh * HD + c * 64, kr);
+          }
+        }
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(BM, BNS, false, false);
+      constexpr uint32_t idesc_o = make_idesc_bf16(BM, HD, false, true);
+      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      long gs[2] = {0, 0}, gp[2] = {0, 0};  // global S / PV counts per tile
+      int oi[2] = {0, 0};                    // items whose O tile t has drained
+      int qi = 0;
+      long kvc0 = 0;  // global index of the item's first K / V block
+      bool ok = true;
+      unsigned long long wp = 0;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        const SpItem w = sp_item(item, a, nqt);
+        if (w.nb == 0) continue;
+        if (!mbar_wait(q_full, qi & 1, a.err, kErrTimeoutMma, abort_flag)) break;
+        ++qi;
+        auto issue_s = [&](int t, long kb) {
+          const int st = (int)(kb % kStagesSP);
+          const uint32_t qa = q_addr + t * SM::kTileQ, ka = k_addr + st * SM::kTileKV;
+#pragma unroll
+          for (int ks = 0; ks < HD / 16; ++ks) {
+            const uint32_t oq = (ks / 4) * BM * 128 + (ks % 4) * 32, ok_ = (ks / 4) * BNS * 128 + (ks % 4) * 32;
+            umma_bf16(tmem + t * 128, make_sdesc(qa + oq, 16, 1024), make_sdesc(ka + ok_, 16, 1024), idesc_s,
+                      ks > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[t]);
+        };
+        auto issue_pv = [&](int t, long kb, bool acc) {
+          const uint32_t va = v_addr + (int)(kb % kStagesSP) * SM::kTileKV;
+#pragma unroll
+          for (int ks = 0; ks < BNS / 16; ++ks)
+            umma_ts_bf16(tmem + 256 + t * 128, tmem + p_col(t, ks), make_sdesc(va + ks * 2048, BNS * 128, 1024),
+                         idesc_o, (acc || ks > 0) ? 1u : 0u);
+          umma_commit(&o_done[t]);
+        };
+        int ns[2] = {w.lo_t[0], w.lo_t[1]}, np[2] = {w.lo_t[0], w.lo_t[1]};
+        int rel = 0;
+        long long t_last = clock64(), t_iter = t_last;
+        while (true) {
+          bool prog = false;
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (ns[t] < w.nb_t[t]) {
+              const long kb = kvc0 + ns[t];
+              bool ready = mbar_test(&kv_full[kb % kStagesSP], (kb / kStagesSP) & 1);
+              if (ready && gs[t] > 0) ready = mbar_test(&s_free[t], (gs[t] - 1) & 1);
+              if (ready) {
+                tc_fence_after();
+                issue_s(t, kb);
+                ++ns[t];
+                ++gs[t];
+                prog = true;
+              }
+            }
+            if (np[t] < ns[t]) {
+              const bool first = np[t] == w.lo_t[t];
+              bool ready = mbar_test(&p_full[t], gp[t] & 1);
+              if (ready && first && oi[t] > 0) ready = mbar_test(&o_free[t], (oi[t] - 1) & 1);
+              if (ready) {
+                tc_fence_after();
+                issue_pv(t, kvc0 + np[t], !first);
+                ++np[t];
+                ++gp[t];
+                prog = true;
+              }
+            }
+          }
+          while (rel < w.nb) {
+            bool done = true;
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+              if (rel >= w.lo_t[t] && rel < w.nb_t[t] && np[t] <= rel) done = false;
+            if (!done) break;
+            umma_commit(&kv_empty[(kvc0 + rel) % kStagesSP]);
+            ++rel;
+          }
+          if (rel >= w.nb && np[0] >= w.nb_t[0] && np[1] >= w.nb_t[1]) break;
+          const long long now = clock64();
+          if (prog) {
+            t_last = now;
+          } else {
+            wp += now - t_iter;
+            if (*abort_flag) {
+              ok = false;
+              break;
+            }
+            if (now - t_last > kWaitCycles) {
+              atomicExch(a.err, kErrTimeoutMma);
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+          }
+          t_iter = now;
+        }
+        umma_commit(q_empty);  // Q is free once this item's S products have completed
+        kvc0 += w.nb;
+        for (int t = 0; t < 2; ++t)
+          if (w.nb_t[t] > w.lo_t[t]) ++oi[t];
+      }
+      if (a.prof) atomicAdd(&a.prof[4], wp);
+    }
+  } else {
+    // ------------------------------------------------------------------------ softmax warps
+    const int t = warp >> 2;
+    const int row = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + t * 128 + lane_off;
+    const uint32_t t_o = tmem + 256 + t * 128 + lane_off;
+    long gcnt = 0;  // global blocks of this tile
+    bool alive = true;
+    unsigned long long pw = 0, p1 = 0, p2 = 0, p3 = 0, nblk = 0;
+    for (int item = blockIdx.x; item < n_items && alive; item += gridDim.x) {
+      const SpItem w = sp_item(item, a, nqt);
+      if (w.nb == 0 || w.nb_t[t] <= w.lo_t[t]) continue;
+      const int qi = w.q0 + t * BM + row;
+      int klo, khi;
+      key_range(qi, a.S, a.window, a.seg, w.base, klo, khi);
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int j = w.lo_t[t]; j < w.nb_t[t]; ++j, ++gcnt) {
+        long long c_a = clock64();
+        const bool got = mbar_wait(&s_full[t], gcnt & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+        long long c_b = clock64();
+        pw += c_b - c_a;
+        if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+        tc_fence_after();
+        float s0[32], s1[32], s2[32];
+        tmem_ld32(t_s + 0, s0);
+        tmem_ld32(t_s + 32, s1);
+        tmem_ld32(t_s + 64, s2);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&s_free[t]);
+        const int k0 = (w.kb_lo + j) * BNS;
+        const int lo = klo - k0, hi = khi - k0;
+        if (!(lo <= 0 && hi >= BNS - 1)) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            if (c < lo || c > hi) s0[c] = -INFINITY;
+            if (c + 32 < lo || c + 32 > hi) s1[c] = -INFINITY;
+            if (c + 64 < lo || c + 64 > hi) s2[c] = -INFINITY;
+          }
+        }
+        float mxa = -INFINITY, mxb = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          mxa = fmaxf(mxa, fmaxf(fmaxf(s0[c], s1[c]), s2[c]));
+          mxb = fmaxf(mxb, fmaxf(fmaxf(s0[c + 1], s1[c + 1]), s2[c + 1]));
+        }
+        const float mx = fmaxf(mxa, mxb) * a.scale_log2;
+        long long c_c = clock64();
+        p1 += c_c - c_b;
+        float alpha = 1.f;
+        bool rescale = false;
+        if (mx > m_run + kRescaleThreshold || (m_run == -INFINITY && mx > -INFINITY)) {
+          if (m_run != -INFINITY) {
+            alpha = exp2f(m_run - mx);
+            rescale = true;
+          }
+          m_run = mx;
+          l_run *= alpha;
+        }
+        const float mb = m_run == -INFINITY ? 0.f : m_run;
+        uint32_t w0[16], w1[16], w2[16];
+        {
+          const uint64_t sc2 = f2_make(a.scale_log2, a.scale_log2), nm2 = f2_make(-mb, -mb);
+          uint64_t acc0 = f2_make(0.f, 0.f), acc1 = f2_make(0.f, 0.f);
+          softmax_pack32<4>(s0, w0, sc2, nm2, acc0, acc1);
+          softmax_pack32<4>(s1, w1, sc2, nm2, acc0, acc1);
+          softmax_pack32<4>(s2, w2, sc2, nm2, acc0, acc1);
+          float r0, r1, r2, r3;
+          f2_split(acc0, r0, r1);
+          f2_split(acc1, r2, r3);
+          l_run += (r0 + r1) + (r2 + r3);
+        }
+        long long c_d = clock64();
+        p2 += c_d - c_c;
+        // P's buffer (and O for a rescale) are free once the previous PV of this tile completed
+        if (gcnt > 0) {
+          const bool g2 = mbar_wait(&o_done[t], (gcnt - 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+          if (!__all_sync(0xffffffffu, g2)) { alive = false; break; }
+          tc_fence_after();
+        }
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int c = 0; c < HD; c += 16) {
+            float o[16];
+            tmem_ld16(t_o + c, o);
+            tmem_wait_ld();
+            uint32_t ou[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) ou[u] = __float_as_uint(o[u] * alpha);
+            tmem_st16(t_o + c, ou);
+          }
+        }
+        tmem_st16(tmem + lane_off + p_col(t, 0), w0);
+        tmem_st16(tmem + lane_off + p_col(t, 2), w1);
+        tmem_st16(tmem + lane_off + p_col(t, 4), w2);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[t]);
+        p3 += clock64() - c_d;
+        ++nblk;
+      }
+      if (!alive) break;
+      // epilogue: the item's last PV, then O normalised and stored; O is then free for the next item
+      const bool got = mbar_wait(&o_done[t], (gcnt - 1) & 1, a.err, kErrTimeoutEpilogue, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) { alive = false; break; }
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      __nv_bfloat16* orow = a.o + ((long)(w.base + qi) * a.H + w.h) * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 16) {
+        float o[16];
+        tmem_ld16(t_o + c, o);
+        tmem_wait_ld();
+        if (qi < a.S) {
+          uint32_t pkd[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) pkd[u] = pack_bf16x2(o[2 * u] * inv, o[2 * u + 1] * inv);
+          reinterpret_cast<uint4*>(orow + c)[0] = make_uint4(pkd[0], pkd[1], pkd[2], pkd[3]);
+          reinterpret_cast<uint4*>(orow + c)[1] = make_uint4(pkd[4], pkd[5], pkd[6], pkd[7]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&o_free[t]);
+      if (qi < a.S)
+        a.lse[(long)(w.base + qi) * a.H + w.h] = l_run > 0.f ? (m_run + log2f(l_run)) * 0.6931471805599453f : INFINITY;
+    }
+    if (a.prof && lane == 0) {
+      atomicAdd(&a.prof[0], pw);
+      atomicAdd(&a.prof[1], p1);
+      atomicAdd(&a.prof[2], p2);
+      atomicAdd(&a.prof[3], p3);
+      atomicAdd(&a.prof[7], nblk);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace fa100
 
 bool make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner,
@@ -1149,9 +1512,30 @@ static int run_fa_fwd_sm100(const AttnLaunch& L, int* err, cudaStream_t st) {
   static const int variant = [] {
     const char* e = getenv("MXK_ATTN_FWD");
     const std::string v = e ? e : "sp";
-    return v == "pp" ? 0 : v == "split" ? 1 : 2;
+    return v == "pp" ? 0 : v == "split" ? 1 : v == "spp" ? 3 : 2;
   }();
   if constexpr (HD <= 96) {
+    if (variant == 3) {  // persistent separate-P: one CTA per SM looping over the work items
+      CUtensorMap tk96, tv96;
+      if (!make_tmap_bf16_2d(&tk96, L.k, (long)L.Hkv * HD, T, L.k_tok, 64, BNS)) return kErrBadArgsHost;
+      if (!make_tmap_bf16_2d(&tv96, L.v, (long)L.Hkv * HD, T, L.v_tok, 64, BNS)) return kErrBadArgsHost;
+      constexpr int smem = SmemSP<HD>::kBytes;
+      static bool init = false;
+      static int sms = 0;
+      if (!init) {
+        if (cudaFuncSetAttribute(fa_fwd_sm100_spp_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
+          return kErrBadArgsHost;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        init = true;
+      }
+      const int n_items = (int)(grid.x * grid.y * grid.z);
+      count_launch();
+      fa_fwd_sm100_spp_kernel<HD><<<min(n_items, sms), kThreadsPP, smem, st>>>(tq, tk96, tv96, a, n_items);
+      return cudaGetLastError() == cudaSuccess ? 0 : kErrBadArgsHost;
+    }
     if (variant == 2) {
       CUtensorMap tk96, tv96;
       if (!make_tmap_bf16_2d(&tk96, L.k, (long)L.Hkv * HD, T, L.k_tok, 64, BNS)) return kErrBadArgsHost;
