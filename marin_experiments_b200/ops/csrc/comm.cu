@@ -104,6 +104,14 @@ __device__ __forceinline__ long remote_row(int e, int s, int e_loc, int cap, int
   return ((long)my * e_loc + (e % e_loc)) * cap + s;
 }
 
+// Push order: every source walks the [E][cap] rows starting at the first row of the next rank's
+// experts (rank my + 1), so at any moment the sources write to different destinations. In expert
+// order all eight sources would write to rank 0's experts first, then rank 1's: one destination's
+// NVLink ingress at a time (measured at 8 GPUs: the pushes reached half of the pulls' rate).
+__device__ __forceinline__ long push_rotation(const EpArgs& a) {
+  return (long)((a.my + 1) % a.world) * a.e_loc * a.cap;
+}
+
 // ------------------------------------------------------------------------------------ kernels
 // Forward dispatch: x[perm] rows (zeros on pad rows up to round128(count)) -> owners' receive buffers;
 // counts -> owners' count arrays.
@@ -116,7 +124,9 @@ __global__ void ep_dispatch_push_kernel(const __nv_bfloat16* __restrict__ x, con
       int* dst = reinterpret_cast<int*>(peer_ptr(a.peers, e / a.e_loc, a.counts_off));
       dst[a.my * a.e_loc + e % a.e_loc] = counts[e];
     }
-  for (long r = blockIdx.x * (long)warps + (threadIdx.x >> 5); r < (long)E * a.cap; r += (long)gridDim.x * warps) {
+  const long total = (long)E * a.cap, rot = push_rotation(a);
+  for (long q = blockIdx.x * (long)warps + (threadIdx.x >> 5); q < total; q += (long)gridDim.x * warps) {
+    const long r = (q + rot) % total;
     const int e = (int)(r / a.cap), s = (int)(r % a.cap);
     const int c = counts[e];
     if (s >= round128(c) || s < a.s_lo || s >= a.s_hi) continue;
@@ -137,7 +147,9 @@ __global__ void ep_combine_bwd_push_kernel(const __nv_bfloat16* __restrict__ dou
                                            const float* __restrict__ wperm, const int* __restrict__ counts, EpArgs a) {
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   const int E = a.e_loc * a.world;
-  for (long r = blockIdx.x * (long)warps + (threadIdx.x >> 5); r < (long)E * a.cap; r += (long)gridDim.x * warps) {
+  const long total = (long)E * a.cap, rot = push_rotation(a);
+  for (long q = blockIdx.x * (long)warps + (threadIdx.x >> 5); q < total; q += (long)gridDim.x * warps) {
+    const long r = (q + rot) % total;
     const int e = (int)(r / a.cap), s = (int)(r % a.cap);
     const int c = counts[e];
     if (s >= round128(c) || s < a.s_lo || s >= a.s_hi) continue;
@@ -217,10 +229,13 @@ __global__ void ep_push_v2_kernel(const __nv_bfloat16* __restrict__ x, const int
       int* dst = reinterpret_cast<int*>(peer_ptr(a.peers, e / a.e_loc, a.counts_off));
       dst[a.my * a.e_loc + e % a.e_loc] = counts[e];
     }
-  const long rows = (long)E * a.cap;
+  const long rows = (long)E * a.cap, rot = push_rotation(a);
   const long stride = (long)gridDim.x * warps;
-  for (long r0 = blockIdx.x * (long)warps + (threadIdx.x >> 5); r0 < rows; r0 += 2 * stride) {
-    long r[2] = {r0, r0 + stride};
+  for (long q0 = blockIdx.x * (long)warps + (threadIdx.x >> 5); q0 < rows; q0 += 2 * stride) {
+    long r[2] = {q0, q0 + stride};
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+      if (r[u] < rows) r[u] = (r[u] + rot) % rows;
     uint4* dst[2] = {nullptr, nullptr};
     const uint4* src[2] = {nullptr, nullptr};
     float w[2] = {1.f, 1.f};
