@@ -493,7 +493,10 @@ def main(argv=None):
                    "global_batch": seqs * world, "seq_len": seq, "tokens_per_step": tokens_step,
                    "micro_batch": args.micro_batch, "capacity_factor": cfg.capacity_factor,
                    "parallelism": (f"{bc['parallel']}{world}" + ("+zero" if args.zero else "")) if world > 1 else "single", "l2": "working set >> L2 (no flush needed)",
-                   "layers": cfg.num_layers, "remat": cfg.remat_mode, "zero": bool(args.zero and world > 1)},
+                   "layers": cfg.num_layers, "remat": cfg.remat_mode, "zero": bool(args.zero and world > 1),
+                   "ep_shared_overlap": bool(world > 1 and cfg.num_experts > 0 and ep_size > 1
+                                             and os.environ.get("MXK_EP_OVERLAP", "1") == "1"
+                                             and os.environ.get("MXK_EP_IMPL", "peer") == "peer")},
         "mfu": mfu, "mfu_denominator": f"{flop_peak / 1e12:.1f} TFLOP/s per GPU, {peak_label}",
         "mfu_nominal": mfu_nominal, "mfu_nominal_denominator": "2250 TFLOP/s per GPU, nominal dense bf16",
         "ms_x_median_mhz": ms * clk["sm_mhz"] if clk.get("sm_mhz") else None,
