@@ -14,9 +14,12 @@ executor does not reuse an earlier success). Here a sweep runs on this node:
   ``<name>.cmd`` (its environment and command) per arm and returns the logs; ``main`` then prints
   ``utils.analysis.sweep_table`` over them (median ``[THRUPUT]`` after the warm-up steps, failure
   kind per run).
+* ``submit`` instead sends every arm as a job to the client that ``MXK_CLUSTER`` names (``cluster``:
+  this node's GPU-slot scheduler, so arms that fit run side by side, or another host over SSH); with
+  ``--wait`` it collects each job's log into ``<log_dir>`` and prints the same table.
 
 Usage: ``python -m marin_experiments_b200.experiments.sweeps <sweep> [--only a,b] [--tag T]
-[--gpus N] [--log-dir D] [--timeout S] [--dry-run]``.
+[--gpus N] [--log-dir D] [--timeout S] [--dry-run] [--submit [--wait]]``.
 """
 
 from __future__ import annotations
@@ -150,6 +153,41 @@ def run(jobs: list[Job], log_dir: str, *, timeout_s: float = 3600.0, dry_run: bo
     return logs
 
 
+def submit(jobs: list[Job], client, *, timeout_s: float = 3600.0, retries: int = 0) -> list:
+    """Send each arm to ``client`` (``cluster.LocalClient`` / ``SSHClient``); returns the job handles.
+    The client starts a multi-GPU Python job under ``torch.distributed.run`` itself, so an arm's own
+    torchrun prefix is dropped."""
+    from .. import cluster as C
+
+    handles = []
+    for job in jobs:
+        argv = list(job.argv)
+        if argv[1:3] == ["-m", "torch.distributed.run"]:
+            argv = [argv[0]] + argv[argv.index("-m", 3):]
+        req = C.JobRequest(job.name, C.Entrypoint.from_command(*argv), C.ResourceConfig(gpus=job.gpus),
+                           dict(job.env), retries, timeout_s)
+        handles.append(client.submit(req))
+    return handles
+
+
+def collect(handles: list, names: list[str], log_dir: str) -> list[str]:
+    """Wait for submitted arms and copy each job's log to ``<log_dir>/<name>.log``."""
+    import shutil
+
+    os.makedirs(log_dir, exist_ok=True)
+    logs = []
+    for h, name in zip(handles, names):
+        state = h.wait(raise_on_failure=False)
+        path = os.path.join(log_dir, f"{name}.log")
+        if os.path.exists(h.log_path()):
+            shutil.copyfile(h.log_path(), path)
+        with open(path, "a") as f:
+            f.write(f"\n[sweep] job {h.job_id} {state} exit {h.exit_code}\n")
+        print(f"[sweep] {name}: {state} -> {path}", flush=True)
+        logs.append(path)
+    return logs
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(prog="python -m marin_experiments_b200.experiments.sweeps")
     ap.add_argument("sweep", choices=sorted(SWEEPS))
@@ -160,9 +198,21 @@ def main(argv=None):
     ap.add_argument("--timeout", type=float, default=3600.0)
     ap.add_argument("--warmup", type=int, default=8, help="steps excluded from the tokens/s median")
     ap.add_argument("--dry-run", action="store_true")
+    ap.add_argument("--submit", action="store_true", help="send the arms to a job scheduler instead of running them")
+    ap.add_argument("--wait", action="store_true", help="with --submit: wait and analyse the logs")
     a = ap.parse_args(argv)
     jobs = plan(a.sweep, gpus=a.gpus, tag=a.tag, only=a.only.split(",") if a.only else None)
-    logs = run(jobs, a.log_dir, timeout_s=a.timeout, dry_run=a.dry_run)
+    if a.submit and not a.dry_run:
+        from ..cluster import current_client
+
+        handles = submit(jobs, current_client(), timeout_s=a.timeout)
+        for h, job in zip(handles, jobs):
+            print(f"[sweep] submitted {job.name} -> {h.job_id}", flush=True)
+        if not a.wait:
+            return 0
+        logs = collect(handles, [j.name for j in jobs], a.log_dir)
+    else:
+        logs = run(jobs, a.log_dir, timeout_s=a.timeout, dry_run=a.dry_run)
     if not a.dry_run:
         from ..utils.analysis import analyze_logs, sweep_table
 

@@ -78,3 +78,37 @@ def test_diag_side_entries_dispatch(monkeypatch):
     with pytest.raises(SystemExit):
         diag.main("bogus")
     assert set(diag.MODES) == {"ragged", "ring", "fit", "attn"}
+
+
+def test_submit_arms_to_scheduler(tmp_path):
+    """Arms sent to the node scheduler run side by side on its GPUs; their logs feed the same table."""
+    from marin_experiments_b200 import cluster as C
+
+    code = ("import os, time\n"
+            "print('[arm] ' + os.environ['SP_TAG'] + '  mode=fixed D=1536 d_e=1536(factorized=False) seq=2048 E=64 "
+            "k=4 min_k=0 coef=0.0 nominal_active_frac=6.25% batch=32 steps=12 budget=1e18')\n"
+            "for s in range(12):\n"
+            "    print(f\"[THRUPUT] step={s} dt=0.500s tok_s={int(os.environ['X_TOK']) + s} mfu=0.2000 bs=32\")\n"
+            "print('devices', os.environ['CUDA_VISIBLE_DEVICES'])\n")
+    fake = {"demo": {"a": {"X_TOK": "500000"}, "b": {"X_TOK": "700000"}}}
+    jobs = sweeps.plan("demo", gpus=1, tag="q", sweeps=fake)
+    for j in jobs:
+        j.argv = [sys.executable, "-c", code]
+    client = C.LocalClient(str(tmp_path / "jobs"), gpus=[0, 1])
+    handles = sweeps.submit(jobs, client, timeout_s=120)
+    logs = sweeps.collect(handles, [j.name for j in jobs], str(tmp_path / "logs"))
+    runs = analysis.analyze_logs(logs, warmup=8)
+    assert runs[0].tok_s == 500009.5 and runs[1].tok_s == 700009.5
+    devs = {open(p).read().split("devices ")[1].split()[0] for p in logs}
+    assert devs <= {"0", "1"} and "SUCCEEDED" in open(logs[0]).read()
+    # a torchrun arm is handed to the client as the plain module (the client adds torchrun itself)
+    two = sweeps.plan("anchor", gpus=2, tag="t", only=["e64k4"])[0]
+
+    class Rec:
+        def submit(self, req):
+            self.req = req
+            return req
+
+    r = Rec()
+    sweeps.submit([two], r)
+    assert list(r.req.entrypoint.command) == [sys.executable, "-m", sweeps.LAUNCHER] and r.req.resources.gpus == 2
