@@ -114,3 +114,61 @@ def run_chat_sft(model, tok, conversations: list[list[dict]], cfg: ChatSFTConfig
             print(f"[chat_sft] step={step} loss={losses[-1]:.4f}", flush=True)
     after = [generate(model, tok, p, cfg.eval_tokens, cfg.eval_temperature, cfg.seed) for p in eval_prompts]
     return {"losses": losses, "before": before, "after": after}
+
+
+# ------------------------------------------------------------------ transcript (segment) SFT
+def pack_segments(transcripts: list[list[tuple[str, int]]], tok, seq_len: int, pad_id: int = 0):
+    """Rows of ``seq_len`` tokens from transcripts given as ``[(text, trained)]`` segments (the
+    execution-format warm-up of tunix-delphi-rl/training/agentic_sft.py): each transcript is
+    encoded segment by segment, so a trained segment's tokens are exactly its own; one transcript
+    per row (cut at ``seq_len``), padding untrained. The mask marks the targets that are trained."""
+    rows, masks = [], []
+    for segs in transcripts:
+        ids, m = [], []
+        for text, trained in segs:
+            enc = tok.encode(text)
+            ids += enc
+            m += [int(bool(trained))] * len(enc)
+        ids, m = ids[:seq_len], m[:seq_len]
+        rows.append(ids + [pad_id] * (seq_len - len(ids)))
+        masks.append(m + [0] * (seq_len - len(m)))
+    return torch.tensor(rows, dtype=torch.long), torch.tensor(masks, dtype=torch.float32)
+
+
+def run_segment_sft(model, tok, transcripts: list[list[tuple[str, int]]], cfg: ChatSFTConfig) -> list[float]:
+    """Masked next-token SFT over segment transcripts; returns the loss curve."""
+    dev = next(model.parameters()).device
+    tokens, mask = pack_segments(transcripts, tok, cfg.max_seq_len)
+    tokens, mask = tokens.to(dev), mask.to(dev)
+    params = [p for p in model.parameters() if p.requires_grad]
+    opt = torch.optim.AdamW(params, lr=cfg.lr, weight_decay=cfg.weight_decay)
+    rng = random.Random(cfg.seed)
+    losses = []
+    for step in range(cfg.steps):
+        if cfg.warmup:
+            for g in opt.param_groups:
+                g["lr"] = cfg.lr * min(1.0, (step + 1) / cfg.warmup)
+        rows = [rng.randrange(tokens.shape[0]) for _ in range(min(cfg.batch_size, tokens.shape[0]))]
+        loss = masked_lm_loss(model, tokens[rows], mask[rows])
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        if cfg.max_grad_norm:
+            torch.nn.utils.clip_grad_norm_(params, cfg.max_grad_norm)
+        opt.step()
+        losses.append(float(loss.detach()))
+    return losses
+
+
+@torch.no_grad()
+def complete(model, tok, text: str, max_tokens: int, stops: tuple[str, ...] = ("\nEND",)) -> str:
+    """Greedy continuation of raw ``text`` (base-model prompting), cut after the first stop string."""
+    ids = tok.encode(text)
+    out: list[int] = []
+    dev = next(model.parameters()).device
+    for _ in range(max_tokens):
+        logits = model.forward_logits(torch.tensor([ids + out], device=dev))[0, -1]
+        out.append(int(logits.argmax()))
+        s = tok.decode(out)
+        if any(st in s for st in stops):
+            break
+    return tok.decode(out)

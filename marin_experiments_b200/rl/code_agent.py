@@ -104,7 +104,12 @@ def coding_task(rng: random.Random) -> CodingTask:
     return CodingTask(prompt, sol, r.stdout)
 
 
-def coding_tasks(n: int, seed: int) -> list[CodingTask]:
+def coding_tasks(n: int, seed: int, tiers: tuple[int, ...] | None = None) -> list[CodingTask]:
+    """``n`` tasks; with ``tiers``, drawn from those tiers of ``rl.code_tasks`` instead."""
+    if tiers is not None:
+        from .code_tasks import sample_tasks
+
+        return [CodingTask(t.prompt, t.solution, t.gold) for t in sample_tasks(n, seed, tuple(tiers))]
     rng = random.Random(seed)
     return [coding_task(rng) for _ in range(n)]
 

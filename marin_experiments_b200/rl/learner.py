@@ -76,5 +76,5 @@ class GRPOLearner:
             self.opt.step()
         if hasattr(self.env, "on_step"):  # curriculum sources advance their schedule per update
             self.env.on_step()
-        return {"loss": float(loss), "reward_mean": float(rw.mean()), "grad_norm": float(gn),
+        return {"loss": float(loss.detach()), "reward_mean": float(rw.mean()), "grad_norm": float(gn),
                 "clip_frac": float(met["clip_frac"])}

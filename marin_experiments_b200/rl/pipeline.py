@@ -1,0 +1,175 @@
+"""Idempotent runner of the coding tuning ladders (tunix-delphi-rl/training/pipeline.py,
+tunix-delphi-rl/training/train_coding.py, tunix-delphi-rl/training/train_multiturn.py).
+
+Each round of tuning is a ``Stage`` declared as data: how many SFT transcripts to warm up on, how
+many GRPO steps to take afterwards, and whether the episodes are single-turn (write one program,
+``rl.code_tasks``) or multi-turn (write, run, read the output, revise: ``rl.code_agent``). Running
+a stage starts from a fresh policy (``make_model()``), warms it up with masked SFT on transcripts
+in the RL prompt format (multi-turn transcripts include repair rounds), optionally runs GRPO
+(``rl.learner.GRPOLearner`` over ``CodeTaskEnv`` or ``rl.multiturn.MultiTurnGRPO`` over
+``CodeAgentEnv``), evaluates greedily on the held-out ladder and writes
+``<results_dir>/<experiment>/<stage>.json``. A stage whose results file exists is skipped, so
+re-running resumes the ladder; deleting one file re-runs that stage. ``plan`` (and ``--dry-run``)
+lists which stages would run without building a model.
+
+Ladders: ``coding`` -- few-shot only, SFT on 150 / 300 / 1000 transcripts, SFT 300 + GRPO;
+``multiturn`` -- few-shot, SFT with repair rounds, SFT + multi-turn GRPO, on tiers 3-5.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import random
+import time
+from collections.abc import Callable
+from dataclasses import asdict, dataclass, field, replace
+
+from . import code_agent, code_tasks
+from .chat_sft import ChatSFTConfig, complete, run_segment_sft
+
+
+@dataclass(frozen=True)
+class Stage:
+    name: str
+    sft_examples: int = 0
+    sft_steps: int = 0  # 0 -> 2 passes over the transcripts at the batch size
+    grpo_steps: int = 0
+    multiturn: bool = False
+    tiers: tuple[int, ...] = code_tasks.TIERS
+    lr_sft: float = 3e-4
+    lr_rl: float = 1e-5
+    group_size: int = 8
+    prompts_per_step: int = 4
+    extra: dict = field(default_factory=dict)
+
+
+_HARD = (3, 4, 5)
+EXPERIMENTS: dict[str, list[Stage]] = {
+    "coding": [Stage("fewshot"), Stage("sft150", 150), Stage("sft300", 300), Stage("sft1000", 1000),
+               Stage("sft300_grpo", 300, grpo_steps=60)],
+    "multiturn": [Stage("fewshot", multiturn=True, tiers=_HARD), Stage("sft300", 300, multiturn=True, tiers=_HARD),
+                  Stage("sft300_grpo", 300, grpo_steps=60, multiturn=True, tiers=_HARD)],
+}
+
+
+def results_path(results_dir: str, experiment: str, stage: str) -> str:
+    return os.path.join(results_dir, experiment, f"{stage}.json")
+
+
+def plan(experiment: str, results_dir: str, only: str | None = None) -> list[tuple[Stage, bool]]:
+    """``[(stage, done)]`` for the ladder (or one stage of it)."""
+    stages = EXPERIMENTS[experiment]
+    if only is not None:
+        stages = [s for s in stages if s.name == only]
+        if not stages:
+            raise KeyError(f"experiment {experiment!r} has no stage {only!r}")
+    return [(s, os.path.exists(results_path(results_dir, experiment, s.name))) for s in stages]
+
+
+def _transcripts(stage: Stage, seed: int) -> list[list[tuple[str, int]]]:
+    if stage.multiturn:
+        rng = random.Random(seed + 1)
+        tasks = code_agent.coding_tasks(stage.sft_examples, seed, stage.tiers)
+        prefix = [(f"{code_agent.SYSTEM_PROMPT}\n", 0)]
+        return [prefix + code_agent.sft_transcript(rng, t, fix_prob=0.3) for t in tasks]
+    return [code_tasks.sft_segments(t) for t in code_tasks.sample_tasks(stage.sft_examples, seed, stage.tiers)]
+
+
+def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_per_family: int = 1,
+              max_program_tokens: int = 160, sft_batch: int = 8, seq_len: int = 1024, max_rounds: int = 3) -> dict:
+    model = make_model()
+    t0 = time.time()
+    out: dict = {"stage": asdict(stage), "seed": seed}
+    if stage.sft_examples:
+        steps = stage.sft_steps or max(1, 2 * stage.sft_examples // sft_batch)
+        cfg = ChatSFTConfig(steps=steps, batch_size=sft_batch, lr=stage.lr_sft, max_seq_len=seq_len, seed=seed)
+        losses = run_segment_sft(model, tok, _transcripts(stage, seed), cfg)
+        out["sft"] = {"steps": steps, "first_loss": losses[0], "last_loss": losses[-1]}
+    if stage.grpo_steps:
+        if stage.multiturn:
+            from .multiturn import MultiTurnConfig, MultiTurnGRPO
+
+            tasks = iter(code_agent.coding_tasks(stage.grpo_steps * stage.prompts_per_step, seed + 7, stage.tiers))
+            lr = MultiTurnGRPO(model, tok, lambda: next(tasks),
+                               lambda t: code_agent.CodeAgentEnv(t, max_rounds=max_rounds),
+                               MultiTurnConfig(group_size=stage.group_size, lr=stage.lr_rl, stop="\nEND\n",
+                                               max_turn_tokens=max_program_tokens, max_total_tokens=seq_len,
+                                               seed=seed))
+        else:
+            from .learner import GRPOConfig, GRPOLearner
+
+            lr = GRPOLearner(model, tok, code_tasks.CodeTaskEnv(seed + 7, stage.tiers),
+                             GRPOConfig(group_size=stage.group_size, lr=stage.lr_rl,
+                                        max_new_tokens=max_program_tokens, seed=seed))
+        hist = [lr.step(n_prompts=stage.prompts_per_step) for _ in range(stage.grpo_steps)]
+        out["grpo"] = {"steps": len(hist), "reward_first": hist[0]["reward_mean"], "reward_last": hist[-1]["reward_mean"]}
+    model.eval()
+    ladder = [t for t in code_tasks.eval_tasks(eval_per_family) if t.tier in stage.tiers]
+    if stage.multiturn:
+        tasks = [code_agent.CodingTask(t.prompt, t.solution, t.gold) for t in ladder]
+        ev = code_agent.evaluate_multiturn(lambda text: complete(model, tok, text, max_program_tokens),
+                                           tasks, max_rounds=max_rounds)
+        ev.pop("envs")
+    else:
+        ev = code_tasks.evaluate(lambda p: complete(model, tok, p, max_program_tokens), ladder)
+    out["eval"] = ev
+    out["seconds"] = time.time() - t0
+    return out
+
+
+def run(experiment: str, make_model: Callable, tok, results_dir: str, *, only: str | None = None,
+        overrides: dict | None = None, **kw) -> dict[str, dict]:
+    """Run the stages of ``experiment`` that have no results yet; returns every stage's results."""
+    res = {}
+    for stage, done in plan(experiment, results_dir, only):
+        path = results_path(results_dir, experiment, stage.name)
+        if done:
+            with open(path) as f:
+                res[stage.name] = json.load(f)
+            continue
+        st = replace(stage, **(overrides or {}))
+        r = run_stage(st, make_model, tok, **kw)
+        os.makedirs(os.path.dirname(path), exist_ok=True)
+        tmp = path + ".tmp"
+        with open(tmp, "w") as f:
+            json.dump(r, f, indent=1)
+        os.replace(tmp, path)
+        res[stage.name] = r
+    return res
+
+
+def main(argv=None) -> int:
+    import argparse
+
+    ap = argparse.ArgumentParser(prog="python -m marin_experiments_b200.rl.pipeline")
+    ap.add_argument("--experiment", choices=sorted(EXPERIMENTS), default="coding")
+    ap.add_argument("--stage", default=None)
+    ap.add_argument("--results-dir", default="rl_results")
+    ap.add_argument("--model-dir", default=os.environ.get("MXK_POLICY_DIR", ""),
+                    help="Hugging Face Qwen3 checkpoint directory (safetensors + tokenizer.json)")
+    ap.add_argument("--dry-run", action="store_true")
+    a = ap.parse_args(argv)
+    for stage, done in plan(a.experiment, a.results_dir, a.stage):
+        print(f"[{'done' if done else 'todo'}] {a.experiment}/{stage.name}: sft={stage.sft_examples} "
+              f"grpo={stage.grpo_steps} multiturn={stage.multiturn} tiers={list(stage.tiers)}")
+    if a.dry_run:
+        return 0
+    if not a.model_dir:
+        raise SystemExit("--model-dir (or MXK_POLICY_DIR) is required to run stages")
+    import torch
+
+    from ..data.tokenize import load_tokenizer
+    from ..models.qwen3 import load_hf
+
+    tok = load_tokenizer(a.model_dir)
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    res = run(a.experiment, lambda: load_hf(a.model_dir, device=dev, dtype=torch.float32), tok, a.results_dir,
+              only=a.stage)
+    for name, r in res.items():
+        print(name, json.dumps(r["eval"]))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

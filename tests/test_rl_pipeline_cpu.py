@@ -1,0 +1,68 @@
+"""Segment SFT, greedy completion and the idempotent tuning-ladder runner on a tiny policy."""
+
+import json
+import os
+
+import torch
+
+from marin_experiments_b200.data.tokenize import ByteTokenizer
+from marin_experiments_b200.models.qwen3 import Qwen3Config, Qwen3Model
+from marin_experiments_b200.rl import chat_sft, code_tasks, pipeline
+
+
+def _tiny():
+    cfg = Qwen3Config(vocab_size=257, hidden_dim=64, intermediate_dim=128, num_layers=1, num_heads=2, num_kv_heads=1,
+                      head_dim=32, max_seq_len=1024)
+    return Qwen3Model(cfg).init_weights(0)
+
+
+def test_pack_segments_masks_only_trained_text():
+    tok = ByteTokenizer()
+    t, m = chat_sft.pack_segments([[("ab", 0), ("cd", 1)], [("x", 1)]], tok, 6)
+    assert t.shape == (2, 6) and m[0].tolist() == [0, 0, 1, 1, 0, 0] and m[1].tolist() == [1, 0, 0, 0, 0, 0]
+    assert tok.decode(t[0, :4].tolist()) == "abcd"
+
+
+def test_segment_sft_memorises_a_program():
+    torch.manual_seed(0)
+    tok = ByteTokenizer()
+    m = _tiny()
+    task = code_tasks.eval_tasks()[0]
+    segs = [code_tasks.sft_segments(task)]
+    losses = chat_sft.run_segment_sft(m, tok, segs, chat_sft.ChatSFTConfig(steps=60, batch_size=1, lr=3e-3,
+                                                                         max_seq_len=512))
+    assert losses[-1] < 0.2 * losses[0]
+    out = chat_sft.complete(m, tok, code_tasks.build_prompt(task.prompt), 40)
+    assert code_tasks.extract_program(out) == task.solution
+
+
+def test_ladder_runs_idempotently(tmp_path, monkeypatch):
+    tiny = {"coding": [pipeline.Stage("fewshot", tiers=(0,)),
+                       pipeline.Stage("sft", 4, sft_steps=2, tiers=(0,)),
+                       pipeline.Stage("sft_grpo", 4, sft_steps=1, grpo_steps=1, group_size=2, prompts_per_step=1,
+                                      tiers=(0,))],
+            "multiturn": [pipeline.Stage("sft_grpo", 2, sft_steps=1, grpo_steps=1, group_size=2, prompts_per_step=1,
+                                         multiturn=True, tiers=(3,))]}
+    monkeypatch.setattr(pipeline, "EXPERIMENTS", tiny)
+    tok = ByteTokenizer()
+    built = []
+
+    def make():
+        built.append(1)
+        return _tiny()
+
+    d = str(tmp_path)
+    assert [done for _, done in pipeline.plan("coding", d)] == [False, False, False]
+    res = pipeline.run("coding", make, tok, d, max_program_tokens=8, seq_len=512)
+    assert len(built) == 3 and set(res) == {"fewshot", "sft", "sft_grpo"}
+    r = json.load(open(pipeline.results_path(d, "coding", "sft_grpo")))
+    assert r["eval"]["total"] == len(code_tasks.FAMILIES[0]) and "grpo" in r and "sft" in r
+    again = pipeline.run("coding", make, tok, d)  # everything is done: nothing is built or run
+    assert len(built) == 3 and again["sft"]["eval"] == res["sft"]["eval"]
+    os.remove(pipeline.results_path(d, "coding", "sft"))
+    pipeline.run("coding", make, tok, d, max_program_tokens=8, seq_len=512)
+    assert len(built) == 4
+    mt = pipeline.run("multiturn", make, tok, d, max_program_tokens=8, seq_len=768, max_rounds=2)
+    ev = mt["sft_grpo"]["eval"]
+    assert set(ev) == {"first_solve", "best_solve", "mean_rounds"} and 1.0 <= ev["mean_rounds"] <= 2.0
+    assert pipeline.main(["--experiment", "coding", "--results-dir", d, "--dry-run"]) == 0
