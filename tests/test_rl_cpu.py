@@ -89,3 +89,10 @@ def test_namespace_sandbox_isolation():
         assert sb.exec("sleep 30 & sleep 30", timeout=0.5).timed_out
     finally:
         sb.close()
+
+
+def test_toy_grpo_learns():
+    from marin_experiments_b200.rl.toy import train_toy
+
+    r = train_toy(steps=25)
+    assert r.first < 0.45 and r.last > 0.8, r.rewards

@@ -48,3 +48,40 @@ def test_http_api():
     assert client.post("/generate", json={"prompt": "a", "prompts": ["b"]}).status_code == 400
     r = client.post("/v1/completions", json={"prompt": "hey", "max_tokens": 3, "temperature": 0.0})
     assert r.json()["object"] == "text_completion" and len(r.json()["choices"]) == 1
+
+
+def test_http_client_against_live_server():
+    import socket
+    import threading
+    import time
+
+    import uvicorn
+
+    from marin_experiments_b200.serving import client
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    server = uvicorn.Server(uvicorn.Config(build_app(tiny_engine("cpu"), "tiny"), host="127.0.0.1", port=port,
+                                           log_level="warning"))
+    th = threading.Thread(target=server.run, daemon=True)
+    th.start()
+    url = f"http://127.0.0.1:{port}"
+    try:
+        t0 = time.time()
+        while not server.started:
+            assert time.time() - t0 < 30
+            time.sleep(0.05)
+        assert client.health(url) == {"ok": True, "model": "tiny"}
+        one = client.generate(url, "hi", max_tokens=4, temperature=0.0)
+        assert isinstance(one, str) and one == client.generate(url, "hi", max_tokens=4, temperature=0.0)
+        assert len(client.generate(url, ["a", "b"], max_tokens=3, temperature=0.0)) == 2
+        assert isinstance(client.complete(url, "hey", max_tokens=3, temperature=0.0), str)
+        import pytest
+
+        with pytest.raises(client.ServingError, match="HTTP 4"):
+            client.generate(url, [], max_tokens=3)
+    finally:
+        server.should_exit = True
+        th.join(timeout=10)
