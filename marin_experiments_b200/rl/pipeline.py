@@ -2,18 +2,21 @@
 tunix-delphi-rl/training/train_coding.py, tunix-delphi-rl/training/train_multiturn.py).
 
 Each round of tuning is a ``Stage`` declared as data: how many SFT transcripts to warm up on, how
-many GRPO steps to take afterwards, and whether the episodes are single-turn (write one program,
-``rl.code_tasks``) or multi-turn (write, run, read the output, revise: ``rl.code_agent``). Running
-a stage starts from a fresh policy (``make_model()``), warms it up with masked SFT on transcripts
-in the RL prompt format (multi-turn transcripts include repair rounds), optionally runs GRPO
-(``rl.learner.GRPOLearner`` over ``CodeTaskEnv`` or ``rl.multiturn.MultiTurnGRPO`` over
-``CodeAgentEnv``), evaluates greedily on the held-out ladder and writes
+many GRPO steps to take afterwards, and the kind of episode -- ``coding`` (write one program,
+``rl.code_tasks``), ``multiturn`` (write, run, read the output, revise: ``rl.code_agent``) or
+``tools`` (chained calculator calls of a given depth, ``rl.tools``; train_agentic.py of the same
+project). Running a stage starts from a fresh policy (``make_model()``), warms it up with masked
+SFT on transcripts in the RL prompt format (multi-turn transcripts include repair rounds, tool
+transcripts their tool results as context), optionally runs GRPO (``rl.learner.GRPOLearner`` over
+``CodeTaskEnv``, or ``rl.multiturn.MultiTurnGRPO`` over ``CodeAgentEnv`` / ``CalcToolEnv``),
+evaluates greedily on held-out tasks and writes
 ``<results_dir>/<experiment>/<stage>.json``. A stage whose results file exists is skipped, so
 re-running resumes the ladder; deleting one file re-runs that stage. ``plan`` (and ``--dry-run``)
 lists which stages would run without building a model.
 
 Ladders: ``coding`` -- few-shot only, SFT on 150 / 300 / 1000 transcripts, SFT 300 + GRPO;
-``multiturn`` -- few-shot, SFT with repair rounds, SFT + multi-turn GRPO, on tiers 3-5.
+``multiturn`` -- few-shot, SFT with repair rounds, SFT + multi-turn GRPO, on tiers 3-5; ``tools``
+-- few-shot and SFT + GRPO at depths 1, 2 and 3 (stages T0-T2).
 """
 
 from __future__ import annotations
@@ -35,7 +38,8 @@ class Stage:
     sft_examples: int = 0
     sft_steps: int = 0  # 0 -> 2 passes over the transcripts at the batch size
     grpo_steps: int = 0
-    multiturn: bool = False
+    kind: str = "coding"  # coding | multiturn | tools
+    depth: int = 1  # tools: calculator calls per task
     tiers: tuple[int, ...] = code_tasks.TIERS
     lr_sft: float = 3e-4
     lr_rl: float = 1e-5
@@ -48,8 +52,11 @@ _HARD = (3, 4, 5)
 EXPERIMENTS: dict[str, list[Stage]] = {
     "coding": [Stage("fewshot"), Stage("sft150", 150), Stage("sft300", 300), Stage("sft1000", 1000),
                Stage("sft300_grpo", 300, grpo_steps=60)],
-    "multiturn": [Stage("fewshot", multiturn=True, tiers=_HARD), Stage("sft300", 300, multiturn=True, tiers=_HARD),
-                  Stage("sft300_grpo", 300, grpo_steps=60, multiturn=True, tiers=_HARD)],
+    "multiturn": [Stage("fewshot", kind="multiturn", tiers=_HARD), Stage("sft300", 300, kind="multiturn", tiers=_HARD),
+                  Stage("sft300_grpo", 300, grpo_steps=60, kind="multiturn", tiers=_HARD)],
+    "tools": [Stage("fewshot", kind="tools"), Stage("t0", 200, grpo_steps=40, kind="tools", depth=1),
+              Stage("t1", 200, grpo_steps=40, kind="tools", depth=2),
+              Stage("t2", 200, grpo_steps=40, kind="tools", depth=3)],
 }
 
 
@@ -67,8 +74,26 @@ def plan(experiment: str, results_dir: str, only: str | None = None) -> list[tup
     return [(s, os.path.exists(results_path(results_dir, experiment, s.name))) for s in stages]
 
 
+def tool_transcript(task) -> list[tuple[str, int]]:
+    """A solved chain in the tool environment's rendering: calls and the final answer trained."""
+    from . import tools
+
+    segs = [(f"{tools.SYSTEM_PROMPT}\n{task.prompt}\n", 0)]
+    acc = task.operands[0]
+    for v in task.operands[1:]:
+        segs.append((f"CALC({acc} * {v})\n", 1))
+        acc *= v
+        segs.append((f"Tool result: {acc}\n", 0))
+    segs.append((f"{acc}\n", 1))
+    return segs
+
+
 def _transcripts(stage: Stage, seed: int) -> list[list[tuple[str, int]]]:
-    if stage.multiturn:
+    if stage.kind == "tools":
+        from . import tools
+
+        return [tool_transcript(t) for t in tools.chain_tasks(stage.sft_examples, seed, stage.depth)]
+    if stage.kind == "multiturn":
         rng = random.Random(seed + 1)
         tasks = code_agent.coding_tasks(stage.sft_examples, seed, stage.tiers)
         prefix = [(f"{code_agent.SYSTEM_PROMPT}\n", 0)]
@@ -77,7 +102,8 @@ def _transcripts(stage: Stage, seed: int) -> list[list[tuple[str, int]]]:
 
 
 def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_per_family: int = 1,
-              max_program_tokens: int = 160, sft_batch: int = 8, seq_len: int = 1024, max_rounds: int = 3) -> dict:
+              max_program_tokens: int = 160, sft_batch: int = 8, seq_len: int = 1024, max_rounds: int = 3,
+              eval_tools: int = 50) -> dict:
     model = make_model()
     t0 = time.time()
     out: dict = {"stage": asdict(stage), "seed": seed}
@@ -86,8 +112,19 @@ def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_pe
         cfg = ChatSFTConfig(steps=steps, batch_size=sft_batch, lr=stage.lr_sft, max_seq_len=seq_len, seed=seed)
         losses = run_segment_sft(model, tok, _transcripts(stage, seed), cfg)
         out["sft"] = {"steps": steps, "first_loss": losses[0], "last_loss": losses[-1]}
+    if stage.kind not in ("coding", "multiturn", "tools"):
+        raise ValueError(f"unknown stage kind {stage.kind!r}")
     if stage.grpo_steps:
-        if stage.multiturn:
+        if stage.kind == "tools":
+            from . import tools
+            from .multiturn import MultiTurnConfig, MultiTurnGRPO
+
+            chains = iter(tools.chain_tasks(stage.grpo_steps * stage.prompts_per_step, seed + 7, stage.depth))
+            lr = MultiTurnGRPO(model, tok, lambda: next(chains), lambda t: tools.CalcToolEnv(t),
+                               MultiTurnConfig(group_size=stage.group_size, lr=stage.lr_rl, stop="\n",
+                                               max_turn_tokens=32, max_total_tokens=seq_len, seed=seed),
+                               reward_fn=tools.total_reward)
+        elif stage.kind == "multiturn":
             from .multiturn import MultiTurnConfig, MultiTurnGRPO
 
             tasks = iter(code_agent.coding_tasks(stage.grpo_steps * stage.prompts_per_step, seed + 7, stage.tiers))
@@ -106,7 +143,13 @@ def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_pe
         out["grpo"] = {"steps": len(hist), "reward_first": hist[0]["reward_mean"], "reward_last": hist[-1]["reward_mean"]}
     model.eval()
     ladder = [t for t in code_tasks.eval_tasks(eval_per_family) if t.tier in stage.tiers]
-    if stage.multiturn:
+    if stage.kind == "tools":
+        from . import tools
+
+        held = tools.chain_tasks(eval_tools, 1_000_003 + stage.depth, stage.depth)
+        envs = [tools.rollout(lambda text: complete(model, tok, text, 32, stops=("\n",)), t) for t in held]
+        ev = tools.metrics(envs, [tools.total_reward(e) for e in envs])
+    elif stage.kind == "multiturn":
         tasks = [code_agent.CodingTask(t.prompt, t.solution, t.gold) for t in ladder]
         ev = code_agent.evaluate_multiturn(lambda text: complete(model, tok, text, max_program_tokens),
                                            tasks, max_rounds=max_rounds)
@@ -152,7 +195,7 @@ def main(argv=None) -> int:
     a = ap.parse_args(argv)
     for stage, done in plan(a.experiment, a.results_dir, a.stage):
         print(f"[{'done' if done else 'todo'}] {a.experiment}/{stage.name}: sft={stage.sft_examples} "
-              f"grpo={stage.grpo_steps} multiturn={stage.multiturn} tiers={list(stage.tiers)}")
+              f"grpo={stage.grpo_steps} kind={stage.kind} tiers={list(stage.tiers)} depth={stage.depth}")
     if a.dry_run:
         return 0
     if not a.model_dir:

@@ -3,6 +3,7 @@
 import json
 import os
 
+import pytest
 import torch
 
 from marin_experiments_b200.data.tokenize import ByteTokenizer
@@ -42,7 +43,9 @@ def test_ladder_runs_idempotently(tmp_path, monkeypatch):
                        pipeline.Stage("sft_grpo", 4, sft_steps=1, grpo_steps=1, group_size=2, prompts_per_step=1,
                                       tiers=(0,))],
             "multiturn": [pipeline.Stage("sft_grpo", 2, sft_steps=1, grpo_steps=1, group_size=2, prompts_per_step=1,
-                                         multiturn=True, tiers=(3,))]}
+                                         kind="multiturn", tiers=(3,))],
+            "tools": [pipeline.Stage("t1", 3, sft_steps=1, grpo_steps=1, group_size=2, prompts_per_step=1,
+                                     kind="tools", depth=2)]}
     monkeypatch.setattr(pipeline, "EXPERIMENTS", tiny)
     tok = ByteTokenizer()
     built = []
@@ -65,4 +68,18 @@ def test_ladder_runs_idempotently(tmp_path, monkeypatch):
     mt = pipeline.run("multiturn", make, tok, d, max_program_tokens=8, seq_len=768, max_rounds=2)
     ev = mt["sft_grpo"]["eval"]
     assert set(ev) == {"first_solve", "best_solve", "mean_rounds"} and 1.0 <= ev["mean_rounds"] <= 2.0
+    tl = pipeline.run("tools", make, tok, d, seq_len=512, eval_tools=3)["t1"]
+    assert set(tl["eval"]) == {"tool/tool_call_rate", "tool/arg_acc", "arithmetic/solve_ratio"} and "grpo" in tl
     assert pipeline.main(["--experiment", "coding", "--results-dir", d, "--dry-run"]) == 0
+
+
+def test_tool_transcript_matches_environment():
+    from marin_experiments_b200.rl import tools
+
+    task = tools.chain_tasks(1, seed=4, depth=2)[0]
+    segs = pipeline.tool_transcript(task)
+    script = iter([t for t, m in segs if m])
+    env = tools.rollout(lambda _: next(script), task)
+    assert tools.total_reward(env) == pytest.approx(1.9)
+    # the transcript is exactly what the environment renders for that episode
+    assert "".join(t for t, _ in segs) == env.render()
