@@ -11,7 +11,13 @@ path is kept off the network during training by localizing the caches first
   once (``utils.s3.localize``), converts its rows to the native loader's shards
   (``data.treecache.to_native_cache``) and returns ``{component: native cache dir}``; finished
   components are reused;
-* ``data_config(mix, local_root)`` is the ``DataConfig(source="mixture")`` over them.
+* ``data_config(mix, local_root)`` is the ``DataConfig(source="mixture")`` over them;
+* ``mirror_mix(mix, src_prefix, dst_prefix)`` copies the components' caches from one object store to
+  another (megagpt-speedrun/mirror_to_cw.py: a cluster-local copy of the caches): components are
+  sized first and copied smallest first, so a run can start on the first finished one; objects move
+  many at a time and an object already present with the same size is skipped; after each component
+  ``MANIFEST.json`` at the destination root lists the finished ones (a later run skips them), and
+  ``max_bytes`` stops before a component that would pass the cap.
 
 The component tables below follow the reference's named mixtures (component names and weights);
 their prefix defaults to ``MXK_CORPUS_PREFIX`` (the object-store root that holds ``tokenized/``).
@@ -106,3 +112,39 @@ def data_config(mix: RemoteMix, local_root: str, *, seed: int = 0, smoke: bool =
     table = mix.table(smoke, only)
     return DataConfig(source="mixture", components=tuple((c, caches[c], float(table[c][1])) for c in caches),
                       seed=seed)
+
+
+def mirror_mix(mix: RemoteMix, src_prefix: str, dst_prefix: str, src_client=None, dst_client=None, *,
+               only: list[str] | None = None, max_bytes: int = 0, workers: int = 32) -> dict:
+    """Copy ``mix``'s component caches (their ``split``) between object stores; returns the manifest."""
+    import json
+
+    from ..utils import s3
+
+    src = src_client or s3.S3Client()
+    dst = dst_client or s3.S3Client()
+    sroot, droot = src_prefix.rstrip("/"), dst_prefix.rstrip("/")
+    db, dkey = s3.split_url(droot)
+    man_key = (dkey + "/" if dkey else "") + "MANIFEST.json"
+    try:
+        manifest = json.loads(dst.get(db, man_key))
+    except s3.S3Error as e:
+        if e.status != 404:
+            raise
+        manifest = {"mix": mix.name, "split": mix.split, "components": {}}
+    sizes = {}
+    for comp, (rel, _w) in mix.table(only=only).items():
+        if comp in manifest["components"]:
+            continue
+        b, k = s3.split_url(f"{sroot}/{rel}/{mix.split}")
+        sizes[comp] = sum(o["size"] for o in src.list(b, k.rstrip("/") + "/"))
+    total = sum(c["bytes"] for c in manifest["components"].values())
+    for comp in sorted(sizes, key=lambda c: (sizes[c], c)):
+        if max_bytes and total + sizes[comp] > max_bytes:
+            break
+        rel = mix.components.get(comp, mix.smoke.get(comp))[0]
+        st = s3.mirror_prefix(src, f"{sroot}/{rel}/{mix.split}", dst, f"{droot}/{rel}/{mix.split}", workers=workers)
+        manifest["components"][comp] = {"rel": rel, "bytes": sizes[comp], "objects": st["objects"]}
+        total += sizes[comp]
+        dst.put(db, man_key, json.dumps(manifest, indent=1).encode())
+    return manifest

@@ -190,3 +190,39 @@ def localize(url: str, local_dir: str, client: S3Client | None = None, marker: s
     with open(os.path.join(local_dir, marker), "w") as f:
         f.write("ok\n")
     return local_dir
+
+
+def mirror_prefix(src: S3Client, src_url: str, dst: S3Client, dst_url: str, *, workers: int = 32) -> dict:
+    """Copy every object under ``src_url`` to the same relative key under ``dst_url`` (two stores,
+    or two places in one), ``workers`` objects at a time: the caches are many objects of about a
+    megabyte, so the copy is latency-bound and wants many requests in flight. An object already at
+    the destination with the same size is skipped, so an interrupted mirror resumes where it
+    stopped. Returns ``{"objects", "copied", "skipped", "bytes"}`` (bytes copied)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    sb, sp = split_url(src_url)
+    db, dp = split_url(dst_url)
+    sp = sp.rstrip("/") + "/" if sp else ""
+    dp = dp.rstrip("/") + "/" if dp else ""
+    have = {o["key"][len(dp):]: o["size"] for o in dst.list(db, dp)}
+    todo, skipped = [], 0
+    for o in src.list(sb, sp):
+        rel = o["key"][len(sp):]
+        if not rel or rel.endswith("/"):
+            continue
+        if have.get(rel) == o["size"]:
+            skipped += 1
+        else:
+            todo.append((o["key"], rel, o["size"]))
+
+    def copy(item):
+        key, rel, size = item
+        data = src.get(sb, key)
+        if len(data) != size:
+            raise S3Error(0, f"{key}: read {len(data)} bytes, listed {size}")
+        dst.put(db, dp + rel, data)
+        return size
+
+    with ThreadPoolExecutor(max_workers=max(1, workers)) as ex:
+        copied = sum(ex.map(copy, todo))
+    return {"objects": len(todo) + skipped, "copied": len(todo), "skipped": skipped, "bytes": copied}

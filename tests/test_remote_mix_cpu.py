@@ -91,3 +91,31 @@ def test_named_mixtures_and_prefix():
     finally:
         if old is not None:
             os.environ["MXK_CORPUS_PREFIX"] = old
+
+
+def test_mirror_between_stores(client, tmp_path):
+    """Components copied smallest first, resumable by size, with a manifest and a byte cap."""
+    sizes = {"a": 5, "b": 2, "c": 9}
+    mix = remote.RemoteMix("m", {k: (f"tokenized/{k}-h", 1.0) for k in sizes})
+    for k, n in sizes.items():
+        for i in range(n):
+            client.put("src", f"root/tokenized/{k}-h/train/chunk-{i}.bin", bytes([i]) * (100 + i))
+        client.put("src", f"root/tokenized/{k}-h/validation/x.bin", b"not copied")
+    man = remote.mirror_mix(mix, "s3://src/root", "s3://dst/mirror", client, client, max_bytes=2 * 101 * 5 + 600)
+    assert list(man["components"]) == ["b", "a"]  # smallest first; c would pass the cap
+    got = {o["key"] for o in client.list("dst", "mirror/")}
+    assert "mirror/tokenized/b-h/train/chunk-1.bin" in got and not any("validation" in k for k in got)
+    assert client.get("dst", "mirror/tokenized/a-h/train/chunk-3.bin") == bytes([3]) * 103
+    # resume: finished components are skipped, the rest is copied; a damaged object is copied again
+    client.put("dst", "mirror/tokenized/c-h/train/chunk-0.bin", b"short")
+    st = s3.mirror_prefix(client, "s3://src/root/tokenized/c-h/train", client, "s3://dst/mirror/tokenized/c-h/train",
+                          workers=4)
+    assert st == {"objects": 9, "copied": 9, "skipped": 0, "bytes": sum(100 + i for i in range(9))}
+    again = s3.mirror_prefix(client, "s3://src/root/tokenized/c-h/train", client,
+                             "s3://dst/mirror/tokenized/c-h/train")
+    assert again["copied"] == 0 and again["skipped"] == 9
+    man = remote.mirror_mix(mix, "s3://src/root", "s3://dst/mirror", client, client)
+    assert list(man["components"]) == ["b", "a", "c"] and man["components"]["c"]["objects"] == 9
+    import json
+
+    assert json.loads(client.get("dst", "mirror/MANIFEST.json")) == man
