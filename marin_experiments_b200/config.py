@@ -92,11 +92,11 @@ class GrugModelConfig:
     # MoE path and one (exact) QB-beta selection, so there is nothing to choose between.
     attention_implementation: str | None = None
     moe_implementation: str | None = None
+    fast_qb_beta: bool = False
     # Activation recompute per block: "none" keeps every activation; "recompute_all" keeps only each
     # block's input and recomputes the block in backward; "save_moe" keeps the routed-expert MoE's
     # activations and recomputes the rest of the block (norms, attention, shared expert).
     remat_mode: RematMode = "none"
-    fast_qb_beta: bool = False
     qb_balancing: bool = True
     # Architecture switches. The megagpt grug MoE has all of them on; the tiny dense template
     # has GatedNorm/QK-norm/XSA/head-gate off and a ReLU MLP.

@@ -17,8 +17,7 @@ across ranks is done by ``parallel.ep``.
 
 from __future__ import annotations
 
-import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import torch
 from torch import nn

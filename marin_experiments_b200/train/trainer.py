@@ -20,7 +20,6 @@ from __future__ import annotations
 
 import math
 import time
-from dataclasses import dataclass, field
 
 import torch
 

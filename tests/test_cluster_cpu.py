@@ -3,7 +3,6 @@ GPU used) and the SSH client's remote command (fake runner)."""
 
 import json
 import os
-import sys
 import time
 
 import pytest

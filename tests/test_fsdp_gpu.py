@@ -1,8 +1,6 @@
 """ZeRO-2 on 2 GPUs (NCCL reduce-scatter / all-gather, sharded fused optimizer with the AdamH
 matrix sums all-reduced between its passes) against replicated data parallelism."""
 
-import datetime
-
 import pytest
 import torch
 
@@ -16,8 +14,6 @@ CFG = dict(vocab_size=4096, hidden_dim=256, intermediate_dim=256, shared_expert_
 
 
 def _rank(rank, world, zero, opt="adamh"):
-    import torch.distributed as tdist
-
     from marin_experiments_b200.config import GrugModelConfig, GrugRunConfig, GrugTrainerConfig, TrainerConfig
     from marin_experiments_b200.optim import GrugMoeAdamHConfig
     from marin_experiments_b200.optim.configs import MuonConfig
