@@ -115,9 +115,11 @@ def coding_tasks(n: int, seed: int, tiers: tuple[int, ...] | None = None) -> lis
 
 
 def extract_program(text: str) -> str:
+    """The turn's program: its lines up to ``END`` (or up to a ``Tool result:`` / ``Task:`` line the
+    policy wrote itself), code-fence lines dropped."""
     lines = []
     for ln in (text or "").split("\n"):
-        if ln.strip() == "END":
+        if ln.strip() == "END" or ln.startswith(("Tool result:", "Task:")):
             break
         if ln.strip().startswith("```"):
             continue

@@ -80,6 +80,8 @@ def test_code_agent_first_and_best():
     wrong = ca.run_episode(lambda _: "print('nope')\nEND\n", TASKS[0], max_rounds=3)
     assert not wrong.solved and len(wrong.history) == 3 and wrong.reward() < 1.0
     assert wrong.history[0][1] == "nope"
+    assert ca.extract_program("print(1)\nTool result: 1\nprint(2)") == "print(1)"
+    assert ca.extract_program("```python\nprint(3)\n```\nEND") == "print(3)"
 
 
 def test_code_agent_feedback_and_grades():
