@@ -32,7 +32,8 @@ TINY_MODEL = GrugModelConfig(vocab_size=128_256, hidden_dim=128, intermediate_di
 
 
 def _accelerator() -> str:
-    return "gpu" if torch.cuda.is_available() else "cpu"
+    acc = os.environ.get("ACCELERATOR", "").lower()
+    return acc if acc in ("cpu", "gpu") else ("gpu" if torch.cuda.is_available() else "cpu")
 
 
 @dataclass(frozen=True)

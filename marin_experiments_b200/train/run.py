@@ -23,7 +23,14 @@ from .trainer import Trainer
 
 
 def _device() -> torch.device:
-    if torch.cuda.is_available():
+    """``ACCELERATOR`` (``cpu`` / ``gpu``, the launchers' switch of tiny-stories/launch.py:55-84)
+    picks the device; unset, a GPU is used when there is one."""
+    acc = os.environ.get("ACCELERATOR", "").lower()
+    if acc not in ("", "cpu", "gpu"):
+        raise ValueError(f"ACCELERATOR={acc!r}: this framework runs on cpu or gpu")
+    if acc == "gpu" and not torch.cuda.is_available():
+        raise RuntimeError("ACCELERATOR=gpu but no CUDA device is visible")
+    if acc != "cpu" and torch.cuda.is_available():
         idx = int(os.environ.get("LOCAL_RANK", "0"))
         torch.cuda.set_device(idx)
         return torch.device("cuda", idx)

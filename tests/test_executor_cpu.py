@@ -87,3 +87,21 @@ def test_dry_run_and_run_only(tmp_path, capsys):
     assert "[dry-run] train/b" in capsys.readouterr().out
     Executor(str(tmp_path), run_only=["raw/a"]).run([b])
     assert CALLS == [("produce", 1)]
+
+
+def test_accelerator_switch(monkeypatch):
+    import pytest
+
+    from marin_experiments_b200.train import run
+
+    monkeypatch.setenv("ACCELERATOR", "cpu")
+    assert run._device().type == "cpu"
+    monkeypatch.setenv("ACCELERATOR", "tpu")
+    with pytest.raises(ValueError, match="cpu or gpu"):
+        run._device()
+    import torch
+
+    if not torch.cuda.is_available():
+        monkeypatch.setenv("ACCELERATOR", "gpu")
+        with pytest.raises(RuntimeError, match="no CUDA device"):
+            run._device()
