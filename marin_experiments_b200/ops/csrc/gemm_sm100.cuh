@@ -482,6 +482,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       la_seek(tile0);
       for (int i = 0; i < kSlots - 1; ++i) h_issue();
     }
+    // Residual / gate epilogues: this lane's R row segment (the warp's column half of a tile) is
+    // prefetched into L2 one tile ahead -- when the tile before it starts draining -- so the drain's
+    // R loads hit L2 instead of waiting on DRAM. Bounds as in the loads themselves.
+    auto prefetch_r = [&](int t) {
+      if constexpr (EPI == EPI_RESID || EPI == EPI_GATE_MUL) {
+        if (t >= total_tiles) return;
+        const TileCoord pc = decode_tile<BN, TM>(p, prefix, t);
+        if (pc.nkb == 0 || pc.mt * TM + (int)rank * kBM + q * 32 + lane >= p.M) return;
+        const long pr = (long)((p.c_mod ? pc.g % p.c_mod : pc.g) * p.c_grp + pc.mt * TM + (int)rank * kBM + q * 32) +
+                        lane;
+        const int c0 = pc.nt * BN + half * kHalf;
+        const __nv_bfloat16* rp = reinterpret_cast<const __nv_bfloat16*>(p.R) + pr * p.ldr + c0;
+#pragma unroll
+        for (int off = 0; off < kHalf; off += 64) {
+          if (c0 + off < p.N) prefetch_l2(rp + off);
+        }
+      }
+    };
+    prefetch_r(tile0);
     for (int tile = tile0; tile < total_tiles; tile += tstep) {
       TileCoord tc = decode_tile<BN, TM>(p, prefix, tile);
       if (tc.nkb == 0) continue;
@@ -491,6 +510,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const bool got = mbar_wait(&tfull_bar[buf], tph, p.err, kErrTimeoutEpilogue, abort_flag);
       if (!__all_sync(0xffffffffu, got)) break;  // keep the warp converged for tcgen05.ld
       tc_fence_after();
+      prefetch_r(tile + tstep);
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
       const int row = tc.mt * TM + (int)rank * kBM + q * 32 + lane;
       const bool row_ok = row < p.M;
