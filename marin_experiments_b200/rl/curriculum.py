@@ -187,13 +187,16 @@ def pass_at_k(n: int, c: int, k: int) -> float:
     return 1.0 - math.comb(n - c, k) / math.comb(n, k)
 
 
-def evaluate_passk(policy: Callable[[Problem], list[str]], problems: list[Problem], k: int) -> dict[int, float]:
+def evaluate_passk(policy: Callable[[Problem], list[str]], problems: list, k: int,
+                   solved: Callable[[str, object], bool] | None = None) -> dict[int, float]:
     """Per level, the mean pass@k over ``problems``; ``policy(problem)`` returns n >= k completions
-    and a completion counts as correct when it passes every test."""
+    and a completion counts as correct when it passes every test (``solved(completion, problem)``;
+    by default the test-case environment's full reward)."""
+    ok = solved or (lambda o, p: TestCaseEnv.reward(o, p) == 1.0)
     by: dict[int, list[float]] = {}
     for p in problems:
         outs = policy(p)
-        c = sum(TestCaseEnv.reward(o, p) == 1.0 for o in outs)
+        c = sum(bool(ok(o, p)) for o in outs)
         by.setdefault(p.level, []).append(pass_at_k(len(outs), c, k))
     return {lv: sum(v) / len(v) for lv, v in sorted(by.items())}
 
