@@ -14,9 +14,14 @@ evaluates greedily on held-out tasks and writes
 re-running resumes the ladder; deleting one file re-runs that stage. ``plan`` (and ``--dry-run``)
 lists which stages would run without building a model.
 
+Two more kinds: ``arith`` (staged few-shot arithmetic, ``rl.arithmetic``, stage = ``depth``;
+train_delphi.py) and ``solve`` (the nine levels of test-graded ``def solve`` problems under the
+curriculum, ``rl.solve_problems``; train_curriculum.py).
+
 Ladders: ``coding`` -- few-shot only, SFT on 150 / 300 / 1000 transcripts, SFT 300 + GRPO;
 ``multiturn`` -- few-shot, SFT with repair rounds, SFT + multi-turn GRPO, on tiers 3-5; ``tools``
--- few-shot and SFT + GRPO at depths 1, 2 and 3 (stages T0-T2).
+-- few-shot and SFT + GRPO at depths 1, 2 and 3 (stages T0-T2); ``arithmetic`` -- SFT + GRPO at
+stages 0-3; ``curriculum`` -- few-shot, SFT, SFT + curriculum GRPO over levels 1-9.
 """
 
 from __future__ import annotations
@@ -38,7 +43,7 @@ class Stage:
     sft_examples: int = 0
     sft_steps: int = 0  # 0 -> 2 passes over the transcripts at the batch size
     grpo_steps: int = 0
-    kind: str = "coding"  # coding | multiturn | tools
+    kind: str = "coding"  # coding | multiturn | tools | arith | solve
     depth: int = 1  # tools: calculator calls per task
     tiers: tuple[int, ...] = code_tasks.TIERS
     lr_sft: float = 3e-4
@@ -49,6 +54,7 @@ class Stage:
 
 
 _HARD = (3, 4, 5)
+_ALL_LEVELS = tuple(range(1, 10))
 EXPERIMENTS: dict[str, list[Stage]] = {
     "coding": [Stage("fewshot"), Stage("sft150", 150), Stage("sft300", 300), Stage("sft1000", 1000),
                Stage("sft300_grpo", 300, grpo_steps=60)],
@@ -57,6 +63,9 @@ EXPERIMENTS: dict[str, list[Stage]] = {
     "tools": [Stage("fewshot", kind="tools"), Stage("t0", 200, grpo_steps=40, kind="tools", depth=1),
               Stage("t1", 200, grpo_steps=40, kind="tools", depth=2),
               Stage("t2", 200, grpo_steps=40, kind="tools", depth=3)],
+    "arithmetic": [Stage(f"s{k}", 200, grpo_steps=40, kind="arith", depth=k) for k in range(4)],
+    "curriculum": [Stage("fewshot", kind="solve", tiers=_ALL_LEVELS), Stage("sft300", 300, kind="solve", tiers=_ALL_LEVELS),
+                   Stage("sft300_grpo", 300, grpo_steps=80, kind="solve", tiers=_ALL_LEVELS)],
 }
 
 
@@ -89,6 +98,20 @@ def tool_transcript(task) -> list[tuple[str, int]]:
 
 
 def _transcripts(stage: Stage, seed: int) -> list[list[tuple[str, int]]]:
+    rng = random.Random(seed)
+    if stage.kind == "arith":
+        from . import arithmetic
+
+        out = []
+        for _ in range(stage.sft_examples):
+            q, gold = arithmetic.make_problem(stage.depth, rng)
+            out.append([(arithmetic.build_prompt(stage.depth, q), 0), (f" {gold}\n", 1)])
+        return out
+    if stage.kind == "solve":
+        from . import solve_problems
+
+        probs = [solve_problems.sample_problem(rng, rng.choice(stage.tiers)) for _ in range(stage.sft_examples)]
+        return [[(p.prompt, 0), (solve_problems.BY_KEY[p.family].reference + "\nEND\n", 1)] for p in probs]
     if stage.kind == "tools":
         from . import tools
 
@@ -112,7 +135,7 @@ def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_pe
         cfg = ChatSFTConfig(steps=steps, batch_size=sft_batch, lr=stage.lr_sft, max_seq_len=seq_len, seed=seed)
         losses = run_segment_sft(model, tok, _transcripts(stage, seed), cfg)
         out["sft"] = {"steps": steps, "first_loss": losses[0], "last_loss": losses[-1]}
-    if stage.kind not in ("coding", "multiturn", "tools"):
+    if stage.kind not in ("coding", "multiturn", "tools", "arith", "solve"):
         raise ValueError(f"unknown stage kind {stage.kind!r}")
     if stage.grpo_steps:
         if stage.kind == "tools":
@@ -133,6 +156,21 @@ def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_pe
                                MultiTurnConfig(group_size=stage.group_size, lr=stage.lr_rl, stop="\nEND\n",
                                                max_turn_tokens=max_program_tokens, max_total_tokens=seq_len,
                                                seed=seed))
+        elif stage.kind == "arith":
+            from .arithmetic import ArithmeticEnv
+            from .learner import GRPOConfig, GRPOLearner
+
+            lr = GRPOLearner(model, tok, ArithmeticEnv(stage.depth, seed + 7),
+                             GRPOConfig(group_size=stage.group_size, lr=stage.lr_rl, max_new_tokens=8, seed=seed))
+        elif stage.kind == "solve":
+            from .curriculum import Curriculum, CurriculumConfig, CurriculumTaskSource
+            from .learner import GRPOConfig, GRPOLearner
+            from .solve_problems import NUM_LEVELS, SolveProblemEnv
+
+            cur = Curriculum(CurriculumConfig(num_levels=NUM_LEVELS, steps_per_level=max(1, stage.grpo_steps // 10)))
+            lr = GRPOLearner(model, tok, CurriculumTaskSource(SolveProblemEnv(seed + 7), cur, seed),
+                             GRPOConfig(group_size=stage.group_size, lr=stage.lr_rl,
+                                        max_new_tokens=max_program_tokens, seed=seed))
         else:
             from .learner import GRPOConfig, GRPOLearner
 
@@ -143,7 +181,24 @@ def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_pe
         out["grpo"] = {"steps": len(hist), "reward_first": hist[0]["reward_mean"], "reward_last": hist[-1]["reward_mean"]}
     model.eval()
     ladder = [t for t in code_tasks.eval_tasks(eval_per_family) if t.tier in stage.tiers]
-    if stage.kind == "tools":
+    if stage.kind == "arith":
+        from . import arithmetic
+
+        erng = random.Random(3_000_017 + stage.depth)
+        held = [arithmetic.make_problem(stage.depth, erng) for _ in range(eval_tools)]
+        outs = [complete(model, tok, arithmetic.build_prompt(stage.depth, q), 8, stops=("\n",)) for q, _ in held]
+        ev = arithmetic.group_metrics(outs, [g for _, g in held], 1)
+        ev["arith/format_rate"] = sum(arithmetic.format_reward(o) > 0 for o in outs) / max(len(outs), 1)
+    elif stage.kind == "solve":
+        from . import solve_problems
+
+        ev = {}
+        for lv in stage.tiers:
+            probs = solve_problems.eval_problems(lv, 3 * eval_per_family)
+            ok = [solve_problems.SolveProblemEnv.solved(complete(model, tok, p.prompt, max_program_tokens), p)
+                  for p in probs]
+            ev[f"level{lv}"] = sum(ok) / len(ok)
+    elif stage.kind == "tools":
         from . import tools
 
         held = tools.chain_tasks(eval_tools, 1_000_003 + stage.depth, stage.depth)

@@ -45,7 +45,11 @@ def test_ladder_runs_idempotently(tmp_path, monkeypatch):
             "multiturn": [pipeline.Stage("sft_grpo", 2, sft_steps=1, grpo_steps=1, group_size=2, prompts_per_step=1,
                                          kind="multiturn", tiers=(3,))],
             "tools": [pipeline.Stage("t1", 3, sft_steps=1, grpo_steps=1, group_size=2, prompts_per_step=1,
-                                     kind="tools", depth=2)]}
+                                     kind="tools", depth=2)],
+            "arithmetic": [pipeline.Stage("s2", 3, sft_steps=1, grpo_steps=1, group_size=2, prompts_per_step=1,
+                                          kind="arith", depth=2)],
+            "curriculum": [pipeline.Stage("sft_grpo", 3, sft_steps=1, grpo_steps=1, group_size=2,
+                                          prompts_per_step=1, kind="solve", tiers=(1, 7))]}
     monkeypatch.setattr(pipeline, "EXPERIMENTS", tiny)
     tok = ByteTokenizer()
     built = []
@@ -70,6 +74,10 @@ def test_ladder_runs_idempotently(tmp_path, monkeypatch):
     assert set(ev) == {"first_solve", "best_solve", "mean_rounds"} and 1.0 <= ev["mean_rounds"] <= 2.0
     tl = pipeline.run("tools", make, tok, d, seq_len=512, eval_tools=3)["t1"]
     assert set(tl["eval"]) == {"tool/tool_call_rate", "tool/arg_acc", "arithmetic/solve_ratio"} and "grpo" in tl
+    ar = pipeline.run("arithmetic", make, tok, d, seq_len=512, eval_tools=4)["s2"]["eval"]
+    assert set(ar) == {"arith/solve_ratio", "arith/solve_all", "arith/solve_none", "arith/format_rate"}
+    cu = pipeline.run("curriculum", make, tok, d, seq_len=512, max_program_tokens=8)["sft_grpo"]
+    assert set(cu["eval"]) == {"level1", "level7"} and "grpo" in cu
     assert pipeline.main(["--experiment", "coding", "--results-dir", d, "--dry-run"]) == 0
 
 
