@@ -14,14 +14,18 @@ evaluates greedily on held-out tasks and writes
 re-running resumes the ladder; deleting one file re-runs that stage. ``plan`` (and ``--dry-run``)
 lists which stages would run without building a model.
 
-Two more kinds: ``arith`` (staged few-shot arithmetic, ``rl.arithmetic``, stage = ``depth``;
+Three more kinds: ``agent`` (terminal tasks in the sandbox, ``rl.terminal`` over the built-in
+``rl.terminal_tasks``: SFT on oracle trajectories whose observations come from running them, then
+multi-turn GRPO with the graded score as the episode reward, then the solve rate on held-out tasks;
+the openthoughts-agent launchers), ``arith`` (staged few-shot arithmetic, ``rl.arithmetic``, stage = ``depth``;
 train_delphi.py) and ``solve`` (the nine levels of test-graded ``def solve`` problems under the
 curriculum, ``rl.solve_problems``; train_curriculum.py).
 
 Ladders: ``coding`` -- few-shot only, SFT on 150 / 300 / 1000 transcripts, SFT 300 + GRPO;
 ``multiturn`` -- few-shot, SFT with repair rounds, SFT + multi-turn GRPO, on tiers 3-5; ``tools``
 -- few-shot and SFT + GRPO at depths 1, 2 and 3 (stages T0-T2); ``arithmetic`` -- SFT + GRPO at
-stages 0-3; ``curriculum`` -- few-shot, SFT, SFT + curriculum GRPO over levels 1-9.
+stages 0-3; ``curriculum`` -- few-shot, SFT, SFT + curriculum GRPO over levels 1-9; ``agent`` --
+few-shot, SFT on 120 trajectories, SFT + GRPO.
 """
 
 from __future__ import annotations
@@ -43,7 +47,7 @@ class Stage:
     sft_examples: int = 0
     sft_steps: int = 0  # 0 -> 2 passes over the transcripts at the batch size
     grpo_steps: int = 0
-    kind: str = "coding"  # coding | multiturn | tools | arith | solve
+    kind: str = "coding"  # coding | multiturn | tools | arith | solve | agent
     depth: int = 1  # tools: calculator calls per task
     tiers: tuple[int, ...] = code_tasks.TIERS
     lr_sft: float = 3e-4
@@ -66,6 +70,8 @@ EXPERIMENTS: dict[str, list[Stage]] = {
     "arithmetic": [Stage(f"s{k}", 200, grpo_steps=40, kind="arith", depth=k) for k in range(4)],
     "curriculum": [Stage("fewshot", kind="solve", tiers=_ALL_LEVELS), Stage("sft300", 300, kind="solve", tiers=_ALL_LEVELS),
                    Stage("sft300_grpo", 300, grpo_steps=80, kind="solve", tiers=_ALL_LEVELS)],
+    "agent": [Stage("fewshot", kind="agent"), Stage("sft120", 120, kind="agent"),
+              Stage("sft120_grpo", 120, grpo_steps=30, kind="agent", group_size=4)],
 }
 
 
@@ -97,8 +103,43 @@ def tool_transcript(task) -> list[tuple[str, int]]:
     return segs
 
 
-def _transcripts(stage: Stage, seed: int) -> list[list[tuple[str, int]]]:
+def agent_transcript(task, sandbox: str = "auto") -> list[tuple[str, int]]:
+    """The oracle trajectory of a terminal task as ChatML segments: actions trained, the task and the
+    terminal output (from actually running the actions) as context."""
+    from ..data.chat import IM_END, IM_START, render_chatml
+    from . import terminal, terminal_tasks
+
+    env = terminal.TerminalEnv(max_turns=4, sandbox=sandbox)
+    try:
+        msgs = env.reset(task)
+        segs = [(render_chatml(msgs[:1], add_generation_prompt=True), 0)]
+        for act in terminal_tasks.oracle_actions(task):
+            segs.append((act + IM_END, 1))
+            obs, done = env.step(act)
+            if done or obs is None:
+                break
+            segs.append((f"\n{IM_START}user\n{obs}{IM_END}\n{IM_START}assistant\n", 0))
+        return segs
+    finally:
+        env.close()
+
+
+def _agent_tasks(n: int, seed: int, root: str | None):
+    import tempfile
+
+    from . import terminal, terminal_tasks
+
+    root = root or tempfile.mkdtemp(prefix="mxk-terminal-tasks-")
+    d = os.path.join(root, f"seed{seed}-n{n}")
+    if not os.path.isdir(d):
+        terminal_tasks.write_tasks(d, n, seed)
+    return terminal.load_tasks(d)
+
+
+def _transcripts(stage: Stage, seed: int, sandbox: str = "auto", task_root: str | None = None):
     rng = random.Random(seed)
+    if stage.kind == "agent":
+        return [agent_transcript(t, sandbox) for t in _agent_tasks(stage.sft_examples, seed, task_root)]
     if stage.kind == "arith":
         from . import arithmetic
 
@@ -126,16 +167,17 @@ def _transcripts(stage: Stage, seed: int) -> list[list[tuple[str, int]]]:
 
 def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_per_family: int = 1,
               max_program_tokens: int = 160, sft_batch: int = 8, seq_len: int = 1024, max_rounds: int = 3,
-              eval_tools: int = 50) -> dict:
+              eval_tools: int = 50, sandbox: str = "auto", task_root: str | None = None,
+              agent_turns: int = 4) -> dict:
     model = make_model()
     t0 = time.time()
     out: dict = {"stage": asdict(stage), "seed": seed}
     if stage.sft_examples:
         steps = stage.sft_steps or max(1, 2 * stage.sft_examples // sft_batch)
         cfg = ChatSFTConfig(steps=steps, batch_size=sft_batch, lr=stage.lr_sft, max_seq_len=seq_len, seed=seed)
-        losses = run_segment_sft(model, tok, _transcripts(stage, seed), cfg)
+        losses = run_segment_sft(model, tok, _transcripts(stage, seed, sandbox, task_root), cfg)
         out["sft"] = {"steps": steps, "first_loss": losses[0], "last_loss": losses[-1]}
-    if stage.kind not in ("coding", "multiturn", "tools", "arith", "solve"):
+    if stage.kind not in ("coding", "multiturn", "tools", "arith", "solve", "agent"):
         raise ValueError(f"unknown stage kind {stage.kind!r}")
     if stage.grpo_steps:
         if stage.kind == "tools":
@@ -154,6 +196,18 @@ def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_pe
             lr = MultiTurnGRPO(model, tok, lambda: next(tasks),
                                lambda t: code_agent.CodeAgentEnv(t, max_rounds=max_rounds),
                                MultiTurnConfig(group_size=stage.group_size, lr=stage.lr_rl, stop="\nEND\n",
+                                               max_turn_tokens=max_program_tokens, max_total_tokens=seq_len,
+                                               seed=seed))
+        elif stage.kind == "agent":
+            import itertools
+
+            from ..data.chat import IM_END
+            from .multiturn import MultiTurnConfig, MultiTurnGRPO
+            from .terminal import ChatTerminalEnv
+
+            pool = itertools.cycle(_agent_tasks(max(8, stage.prompts_per_step * 4), seed + 7, task_root))
+            lr = MultiTurnGRPO(model, tok, lambda: next(pool), lambda t: ChatTerminalEnv(t, agent_turns, sandbox),
+                               MultiTurnConfig(group_size=stage.group_size, lr=stage.lr_rl, stop=IM_END,
                                                max_turn_tokens=max_program_tokens, max_total_tokens=seq_len,
                                                seed=seed))
         elif stage.kind == "arith":
@@ -181,7 +235,18 @@ def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_pe
         out["grpo"] = {"steps": len(hist), "reward_first": hist[0]["reward_mean"], "reward_last": hist[-1]["reward_mean"]}
     model.eval()
     ladder = [t for t in code_tasks.eval_tasks(eval_per_family) if t.tier in stage.tiers]
-    if stage.kind == "arith":
+    if stage.kind == "agent":
+        from ..data.chat import IM_END, render_chatml
+        from . import terminal
+
+        def model_fn(msgs):
+            text = complete(model, tok, render_chatml(msgs, add_generation_prompt=True), max_program_tokens,
+                            stops=(IM_END,))
+            return text.split(IM_END, 1)[0]
+
+        ev = terminal.evaluate(model_fn, _agent_tasks(eval_tools, 9_000_011, task_root), agent_turns, sandbox)
+        ev.pop("episodes")
+    elif stage.kind == "arith":
         from . import arithmetic
 
         erng = random.Random(3_000_017 + stage.depth)

@@ -20,7 +20,8 @@ an unparsable turn gets a corrective message instead. The episode ends when the 
 task complete with no commands left, or after ``max_turns``. Grading copies ``tests/`` into the
 sandbox, runs ``tests/test.sh`` under the verifier timeout and reads ``reward.txt`` (the first of
 ``logs/verifier/reward.txt``, ``tests/reward.txt``, ``reward.txt`` that exists); without one the
-script's exit status decides (0 -> 1.0). Solved means score >= 1.
+script's exit status decides (0 -> 1.0). Solved means score >= 1. ``ChatTerminalEnv`` presents the
+same loop as ChatML text to the multi-turn GRPO learner.
 """
 
 from __future__ import annotations
@@ -260,3 +261,44 @@ def load_agent_traces(path: str, limit: int | None = None):
         n += 1
         if limit is not None and n >= limit:
             return
+
+
+class ChatTerminalEnv:
+    """``TerminalEnv`` as text for ``rl.multiturn.MultiTurnGRPO``: ``render()`` is the ChatML of the
+    opening turn ending in an open assistant header, an assistant turn is what the policy writes up
+    to ``<|im_end|>``, ``feedback`` is the next user turn (the terminal output) plus a fresh
+    assistant header, and ``reward()`` grades the sandbox once and closes it."""
+
+    def __init__(self, task: TerminalTask, max_turns: int = 8, sandbox: str = "auto"):
+        from ..data.chat import IM_END, IM_START, render_chatml
+
+        self._im = (IM_START, IM_END)
+        self._render = render_chatml
+        self.env = TerminalEnv(max_turns, sandbox)
+        self.env.reset(task)
+        self._obs: str | None = None
+        self.done = False
+        self._reward: float | None = None
+
+    def render(self) -> str:
+        return self._render(self.env.episode.messages[:1], add_generation_prompt=True)
+
+    def step(self, text: str) -> bool:
+        reply = text.split(self._im[1], 1)[0].strip()
+        self._obs, self.done = self.env.step(reply)
+        return self.done
+
+    @property
+    def feedback(self) -> str | None:
+        if self.done or self._obs is None:
+            return None
+        s, e = self._im
+        return f"{s}user\n{self._obs}{e}\n{s}assistant\n"
+
+    def reward(self) -> float:
+        if self._reward is None:
+            try:
+                self._reward = self.env.final_reward()
+            finally:
+                self.env.close()
+        return self._reward
