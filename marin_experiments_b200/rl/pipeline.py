@@ -311,6 +311,8 @@ def main(argv=None) -> int:
     ap.add_argument("--results-dir", default="rl_results")
     ap.add_argument("--model-dir", default=os.environ.get("MXK_POLICY_DIR", ""),
                     help="Hugging Face Qwen3 checkpoint directory (safetensors + tokenizer.json)")
+    ap.add_argument("--model", default=os.environ.get("MXK_POLICY", ""),
+                    help="registered base model (models.registry): the checkpoint is checked against it")
     ap.add_argument("--dry-run", action="store_true")
     a = ap.parse_args(argv)
     for stage, done in plan(a.experiment, a.results_dir, a.stage):
@@ -323,10 +325,13 @@ def main(argv=None) -> int:
     import torch
 
     from ..data.tokenize import load_tokenizer
+    from ..models import registry
     from ..models.qwen3 import load_hf
 
     tok = load_tokenizer(a.model_dir)
     dev = "cuda" if torch.cuda.is_available() else "cpu"
+    if a.model:
+        registry.check_checkpoint(a.model, a.model_dir)
     res = run(a.experiment, lambda: load_hf(a.model_dir, device=dev, dtype=torch.float32), tok, a.results_dir,
               only=a.stage)
     for name, r in res.items():
