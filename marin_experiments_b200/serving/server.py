@@ -1,5 +1,13 @@
 """HTTP serving (tunix-delphi-rl/serving/serve.py:81-135,992-1068): ``GET /health``,
-``POST /generate`` (``prompt`` or ``prompts``), and an OpenAI-style ``POST /v1/completions``.
+``POST /generate`` (``prompt`` or ``prompts``), an OpenAI-style ``POST /v1/completions``, ``POST
+/calc`` (the calculator tool loop of the tool-calling RL task served live: the model writes
+``CALC(a * b)``, the server multiplies and answers ``Tool result: N``, until the model gives a
+final answer; the transcript, the calls and the answer come back) and a self-contained dashboard
+page at ``/`` (no external scripts) that posts to those endpoints.
+
+The engine's KV cache is shared state, and FastAPI runs synchronous endpoints on a thread pool,
+so every generation runs under one lock: requests are served one after another (a batch of
+prompts in one request still decodes together).
 
 Run: ``python -m marin_experiments_b200.serving.server --model-dir <hf snapshot> [--port 8000]``
 (``--random-tiny`` serves a small random-init model for smoke tests).
@@ -39,6 +47,13 @@ class GenerateResponse(BaseModel):
     texts: Optional[List[str]] = None
 
 
+class CalcRequest(BaseModel):
+    question: str  # e.g. "12 * 34 * 56" or "Q: 12 * 34 * 56"
+    max_turns: int = 0  # 0: one more than the number of multiplications
+    temperature: float = 0.0
+    seed: int = 0
+
+
 class CompletionRequest(BaseModel):
     prompt: str
     max_tokens: int = 256
@@ -48,10 +63,53 @@ class CompletionRequest(BaseModel):
     stop: Optional[List[str]] = None
 
 
+_DASHBOARD = """<!doctype html><html><head><meta charset="utf-8"><title>{name}</title>
+<style>body{{font-family:sans-serif;max-width:52em;margin:2em auto}}textarea{{width:100%;height:8em}}
+pre{{background:#f4f4f4;padding:1em;white-space:pre-wrap}}</style></head><body>
+<h2>{name}</h2>
+<h3>Generate</h3><textarea id="p">def fib(n):</textarea><br>
+max tokens <input id="m" value="64" size="4"> temperature <input id="t" value="0" size="4">
+<button onclick="gen()">generate</button><pre id="o"></pre>
+<h3>Calculator agent</h3><input id="q" value="12 * 34 * 56" size="30"> <button onclick="calc()">solve</button>
+<pre id="c"></pre>
+<script>
+async function post(url, body) {{
+  const r = await fetch(url, {{method: "POST", headers: {{"content-type": "application/json"}},
+                              body: JSON.stringify(body)}});
+  return r.json();
+}}
+async function gen() {{
+  const j = await post("/generate", {{prompt: document.getElementById("p").value,
+    max_tokens: parseInt(document.getElementById("m").value),
+    temperature: parseFloat(document.getElementById("t").value)}});
+  document.getElementById("o").textContent = j.text !== undefined ? j.text : JSON.stringify(j);
+}}
+async function calc() {{
+  const j = await post("/calc", {{question: document.getElementById("q").value}});
+  document.getElementById("c").textContent = j.transcript !== undefined ?
+    j.transcript + "\\n\\nanswer: " + j.answer + " (correct: " + j.correct + ")" : JSON.stringify(j);
+}}
+</script></body></html>"""
+
+
 def build_app(engine, model_name: str = "qwen3"):
+    import html
+    import threading
+
     from fastapi import FastAPI, HTTPException
+    from fastapi.responses import HTMLResponse
 
     app = FastAPI(title="marin_experiments_b200 serving", version="0.1.0")
+    lock = threading.Lock()
+
+    def run(prompts, **kw):
+        with lock:
+            return engine.generate(prompts, **kw)
+
+    @app.get("/", response_class=HTMLResponse)
+    @app.get("/dashboard", response_class=HTMLResponse)
+    def dashboard() -> str:
+        return _DASHBOARD.format(name=html.escape(model_name))
 
     @app.get("/health")
     def health() -> dict:
@@ -65,18 +123,41 @@ def build_app(engine, model_name: str = "qwen3"):
             prompts, batched = req.resolve_prompts()
         except ValueError as exc:
             raise HTTPException(status_code=400, detail=str(exc)) from exc
-        texts = engine.generate(prompts, max_tokens=req.max_tokens, temperature=req.temperature, top_p=req.top_p,
-                                seed=req.seed, stop=req.stop)
+        texts = run(prompts, max_tokens=req.max_tokens, temperature=req.temperature, top_p=req.top_p, seed=req.seed,
+                    stop=req.stop)
         return GenerateResponse(texts=texts) if batched else GenerateResponse(text=texts[0])
 
     @app.post("/v1/completions")
     def completions(req: CompletionRequest) -> dict:
         if not engine.ready:
             raise HTTPException(status_code=503, detail="model loading")
-        texts = engine.generate([req.prompt], max_tokens=req.max_tokens, temperature=req.temperature,
-                                top_p=req.top_p, seed=req.seed, stop=req.stop)
+        texts = run([req.prompt], max_tokens=req.max_tokens, temperature=req.temperature, top_p=req.top_p,
+                    seed=req.seed, stop=req.stop)
         return {"object": "text_completion", "model": model_name,
                 "choices": [{"index": 0, "text": texts[0], "finish_reason": "stop"}]}
+
+    @app.post("/calc")
+    def calc(req: CalcRequest) -> dict:
+        from ..rl import tools
+
+        if not engine.ready:
+            raise HTTPException(status_code=503, detail="model loading")
+        q = req.question.strip()
+        q = q[2:].strip() if q.startswith("Q:") else q
+        try:
+            ops = tuple(int(v) for v in q.split("*"))
+        except ValueError:
+            raise HTTPException(status_code=400, detail="question must be integers joined by '*'") from None
+        if len(ops) < 2:
+            raise HTTPException(status_code=400, detail="question needs at least two factors")
+        prod = 1
+        for v in ops:
+            prod *= v
+        task = tools.ChainTask("Q: " + " * ".join(map(str, ops)), ops, str(prod))
+        env = tools.rollout(lambda text: run([text], max_tokens=32, temperature=req.temperature, seed=req.seed,
+                                             stop=["\n"])[0], task, req.max_turns)
+        return {"transcript": env.render()[len(env.system) + 1:].rstrip("\n"), "answer": env.final_answer,
+                "calls": env.calls, "correct": env.reward() >= 1.0, "reward": tools.total_reward(env)}
 
     app.state.engine = engine
     return app

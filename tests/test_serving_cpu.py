@@ -85,3 +85,65 @@ def test_http_client_against_live_server():
     finally:
         server.should_exit = True
         th.join(timeout=10)
+
+
+class _ScriptedCalcEngine:
+    """Answers the calculator prompt like a perfect policy; records overlapping generate calls."""
+
+    ready = True
+
+    def __init__(self):
+        import threading
+
+        self.active = self.peak = 0
+        self.mu = threading.Lock()
+
+    def generate(self, prompts, **kw):
+        import time
+
+        with self.mu:
+            self.active += 1
+            self.peak = max(self.peak, self.active)
+        time.sleep(0.02)
+        outs = []
+        for text in prompts:
+            q = [ln for ln in text.split("\n") if ln.startswith("Q: ")][-1]
+            ops = [int(v) for v in q[3:].split(" * ")]
+            res = [int(ln.split(": ")[1]) for ln in text.split(q, 1)[1].split("\n") if ln.startswith("Tool result: ")]
+            if not res:
+                outs.append(f"CALC({ops[0]} * {ops[1]})")
+            elif len(res) < len(ops) - 1:
+                outs.append(f"CALC({res[-1]} * {ops[len(res) + 1]})")
+            else:
+                outs.append(str(res[-1]))
+        with self.mu:
+            self.active -= 1
+        return outs
+
+
+def test_calc_endpoint_dashboard_and_serialised_engine():
+    import threading
+
+    from fastapi.testclient import TestClient
+
+    eng = _ScriptedCalcEngine()
+    client = TestClient(build_app(eng, "calc-demo"))
+    page = client.get("/")
+    assert page.status_code == 200 and "calc-demo" in page.text and 'fetch(url' in page.text
+    assert "<script src" not in page.text  # self-contained
+    r = client.post("/calc", json={"question": "12 * 34 * 56"}).json()
+    assert r["answer"] == str(12 * 34 * 56) and r["calls"] == 2 and r["correct"] is True
+    assert r["transcript"].startswith("Q: 12 * 34 * 56\nCALC(12 * 34)\nTool result: 408")
+    assert client.post("/calc", json={"question": "Q: 7 * 6"}).json()["answer"] == "42"
+    assert client.post("/calc", json={"question": "7 + 6"}).status_code == 400
+    assert client.post("/calc", json={"question": "7"}).status_code == 400
+
+    def hit():
+        client.post("/calc", json={"question": "3 * 4 * 5"})
+
+    th = [threading.Thread(target=hit) for _ in range(6)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    assert eng.peak == 1  # generations never overlap on the shared engine
