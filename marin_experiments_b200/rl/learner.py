@@ -4,7 +4,13 @@ GRPO / Dr.GRPO learner role, tunix-delphi-rl/training/train_coding.py).
 One ``step``: sample ``group_size`` completions per prompt (temperature sampling from the current
 policy), score them with the environment, compute group advantages, and take one clipped
 policy-gradient step (optionally several PPO-style epochs on the same rollouts) with global-norm
-clipping. Generation uses the serving engine on GPU and the model's reference forward on CPU.
+clipping.
+
+Rollouts: by default each new token is sampled from the model's forward over the whole sequence so
+far (simple, exact, quadratic in length). With ``use_engine`` they come from the serving engine
+(``serving.engine.Engine``: KV cache, batched decode, CUDA graphs on a GPU), whose weight copies
+are refreshed in place from the policy before every step, and completions end at end-of-document;
+its token ids are trained as sampled.
 """
 
 from __future__ import annotations
@@ -27,6 +33,7 @@ class GRPOConfig:
     epochs: int = 1
     max_grad_norm: float = 1.0
     seed: int = 0
+    use_engine: bool = False
 
 
 class GRPOLearner:
@@ -39,6 +46,18 @@ class GRPOLearner:
     @torch.no_grad()
     def _sample(self, prompt_ids: list[int]) -> list[list[int]]:
         c = self.cfg
+        if c.use_engine:
+            from ..serving.engine import Engine, SamplingParams
+
+            if getattr(self, "engine", None) is None:
+                self.engine = Engine(self.model, self.tok, max_batch=c.group_size,
+                                     max_len=min(self.model.cfg.max_seq_len, 4096))
+                self._engine_calls = 0
+            self.engine.refresh_weights()
+            self._engine_calls += 1
+            params = SamplingParams(max_tokens=c.max_new_tokens, temperature=c.temperature,
+                                    seed=c.seed * 1_000_003 + self._engine_calls)
+            return [x or [self.tok.eos_id] for x in self.engine.generate_ids([prompt_ids] * c.group_size, params)]
         seqs = [list(prompt_ids) for _ in range(c.group_size)]
         for _ in range(c.max_new_tokens):
             logits = self.model.forward_logits(torch.tensor(seqs))[:, -1].float()

@@ -187,8 +187,48 @@ class Engine:
             outs += self._generate_batch(prompts[i:i + self.max_batch], p)
         return outs
 
+    @torch.no_grad()
+    def refresh_weights(self) -> None:
+        """Copy the model's current weights into the engine's own (bf16) copies, in place: the
+        buffers, the KV caches and any captured decode graphs stay valid, so an RL learner can
+        sample from its latest policy every step without rebuilding the engine. The CPU path reads
+        the model directly and has nothing to copy."""
+        if not self.cuda:
+            return
+        for W, L in zip(self.layers, self.model.layers):
+            W["attn_norm"].copy_(L.attn_norm.detach().float())
+            W["mlp_norm"].copy_(L.mlp_norm.detach().float())
+            W["q_norm"].copy_(L.q_norm.detach().float())
+            W["k_norm"].copy_(L.k_norm.detach().float())
+            W["w_qkv"].copy_(torch.cat([L.w_q, L.w_k, L.w_v], 0).detach())
+            W["w_o"].copy_(L.w_o.detach())
+            W["w_gate_up"].copy_(L.w_gate_up.detach())
+            W["w_down"].copy_(L.w_down.detach())
+        self.embed.copy_(self.model.embed.detach())
+        self.head.copy_(self.model.head_weight().detach())
+        self.final_norm.copy_(self.model.final_norm.detach().float())
+
+    def generate_ids(self, prompts: list[list[int]], params: SamplingParams) -> list[list[int]]:
+        """The sampled token ids of each prompt (end-of-document not included, stop strings not cut):
+        what a learner trains on, with no re-tokenisation of decoded text."""
+        outs: list[list[int]] = []
+        for i in range(0, len(prompts), self.max_batch):
+            outs += self._generate_ids_batch([list(x) or [self.tok.eos_id] for x in prompts[i:i + self.max_batch]],
+                                             params)
+        return outs
+
     def _generate_batch(self, prompts: list[str], p: SamplingParams) -> list[str]:
-        ids = [self.tok.encode(s) or [self.tok.eos_id] for s in prompts]
+        new = self._generate_ids_batch([self.tok.encode(s) or [self.tok.eos_id] for s in prompts], p)
+        texts = [self.tok.decode(x) for x in new]
+        for j, s in enumerate(texts):
+            for st in p.stop:
+                k = s.find(st)
+                if k >= 0:
+                    s = s[:k]
+            texts[j] = s
+        return texts
+
+    def _generate_ids_batch(self, ids: list[list[int]], p: SamplingParams) -> list[list[int]]:
         for x in ids:
             if len(x) + p.max_tokens > self.max_len:
                 raise ValueError(f"prompt of {len(x)} tokens + {p.max_tokens} new exceeds max_len {self.max_len}")
@@ -225,11 +265,4 @@ class Engine:
                     seqs[j].append(t_host[j])
                 logits = torch.cat([self.model.forward_reference(torch.tensor([s]))[:, -1] for s in seqs], 0)
             tok = sample_next(logits, p, gen)
-        texts = [self.tok.decode(x) for x in new]
-        for j, s in enumerate(texts):
-            for st in p.stop:
-                k = s.find(st)
-                if k >= 0:
-                    s = s[:k]
-            texts[j] = s
-        return texts
+        return new

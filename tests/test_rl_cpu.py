@@ -96,3 +96,25 @@ def test_toy_grpo_learns():
 
     r = train_toy(steps=25)
     assert r.first < 0.45 and r.last > 0.8, r.rewards
+
+
+def test_learner_with_engine_rollouts():
+    from marin_experiments_b200.data.tokenize import ByteTokenizer
+    from marin_experiments_b200.models.qwen3 import Qwen3Config, Qwen3Model
+    from marin_experiments_b200.rl.learner import GRPOConfig, GRPOLearner
+    from marin_experiments_b200.serving.engine import Engine, SamplingParams
+
+    cfg = Qwen3Config(vocab_size=257, hidden_dim=64, intermediate_dim=128, num_layers=1, num_heads=2, num_kv_heads=1,
+                      head_dim=32, max_seq_len=128)
+    m = Qwen3Model(cfg).init_weights(0)
+    tok = ByteTokenizer()
+    eng = Engine(m, tok, max_batch=4)
+    ids = eng.generate_ids([tok.encode("12+3="), tok.encode("ab")], SamplingParams(max_tokens=5, temperature=0.0))
+    assert [tok.decode(x) for x in ids] == eng.generate(["12+3=", "ab"], max_tokens=5, temperature=0.0)
+    before = m.layers[0].w_q.detach().clone()
+    lr = GRPOLearner(m, tok, CalculatorEnv(seed=0),
+                     GRPOConfig(group_size=4, max_new_tokens=6, lr=1e-2, use_engine=True))
+    met = lr.step(n_prompts=2)
+    assert torch.isfinite(torch.tensor(met["loss"])) and lr.engine is not None
+    assert not torch.equal(before, m.layers[0].w_q.detach())
+    lr.step(n_prompts=1)  # the engine is reused (weights refreshed in place)

@@ -54,3 +54,29 @@ def test_generate_on_gpu():
     a = eng.generate(["hello", "world"], max_tokens=12, temperature=0.0)
     b = eng.generate(["hello", "world"], max_tokens=12, temperature=0.0)
     assert a == b and all(isinstance(x, str) for x in a)
+
+
+def test_refresh_weights_in_place():
+    """After the policy's weights change, ``refresh_weights`` makes the engine (and its captured decode
+    graph) sample exactly what a freshly built engine over the new weights samples."""
+    from marin_experiments_b200.data.tokenize import ByteTokenizer
+    from marin_experiments_b200.models.qwen3 import Qwen3Config, Qwen3Model
+    from marin_experiments_b200.serving.engine import Engine, SamplingParams
+
+    cfg = Qwen3Config(vocab_size=512, hidden_dim=256, intermediate_dim=256, num_layers=2, num_heads=4,
+                      num_kv_heads=2, head_dim=64, rope_theta=10000.0, max_seq_len=256)
+    m = Qwen3Model(cfg).init_weights(5).cuda()
+    tok = ByteTokenizer()
+    eng = Engine(m, tok, max_batch=2, max_len=256)
+    p = SamplingParams(max_tokens=10, temperature=0.0)
+    prompts = [tok.encode("alpha"), tok.encode("beta gamma")]
+    first = eng.generate_ids(prompts, p)
+    with torch.no_grad():
+        for L in m.layers:
+            L.w_o.mul_(-1.5)
+            L.w_down.add_(0.05 * torch.randn_like(L.w_down))
+        m.embed.mul_(1.3)
+    eng.refresh_weights()
+    again = eng.generate_ids(prompts, p)
+    fresh = Engine(m, tok, max_batch=2, max_len=256).generate_ids(prompts, p)
+    assert again == fresh and again != first
