@@ -31,7 +31,7 @@ class GrugLaunchConfig:
     grug_trainer: GrugTrainerConfig = field(default_factory=GrugTrainerConfig)
     eval: GrugEvalConfig | None = None
     checkpointer: CheckpointerConfig | None = None
-    tracker: str = "jsonl"
+    tracker: str = field(default_factory=lambda: os.environ.get("MXK_TRACKER", "jsonl"))  # jsonl | wandb | noop
     k_schedule: tuple | None = None
     init_from: str | None = None
     per_device_parallelism: int = -1

@@ -3,6 +3,11 @@
 * ``JsonlTracker`` appends ``{"step": s, ...metrics}`` lines to ``<log_dir>/<run_id>/metrics.jsonl``
   (the role of the reference's W&B tracker with ``replicate_path``, which has no network here);
   ``NoopTracker`` drops everything (the reference's ``mode="disabled"`` on CPU).
+* ``WandbTracker`` (kind ``wandb``) logs to Weights & Biases where the ``wandb`` package is installed
+  (project, entity, group, tags and mode from ``WANDB_PROJECT`` / ``WANDB_ENTITY`` /
+  ``WANDB_RUN_GROUP`` / ``WANDB_TAGS`` / ``WANDB_MODE``, as the reference's ``WandbConfig``) and keeps
+  the JSONL copy beside it; without the package it fails at start-up with that message, never
+  silently.
 * ``ThroughputHook`` prints one line per step,
   ``[THRUPUT] step=N dt=1.234s tok_s=123456 mfu=0.213 bs=32``, the format the reference's sweep
   monitor parses (megagpt-speedrun/monitor.py:34-36, megagpt-speedrun/analyze_sweep.py:28);
@@ -71,11 +76,46 @@ def _plain(v):
     return v
 
 
+class WandbTracker:
+    def __init__(self, log_dir: str, run_id: str, config: dict | None = None, *, project: str | None = None,
+                 entity: str | None = None, group: str | None = None, tags: list[str] | None = None,
+                 mode: str | None = None):
+        try:
+            import wandb
+        except ImportError as e:
+            raise ImportError("tracker 'wandb' needs the wandb package; use 'jsonl' without it") from e
+        env = os.environ
+        tags = tags if tags is not None else [t for t in env.get("WANDB_TAGS", "").split(",") if t]
+        self.wandb = wandb
+        self.run = wandb.init(project=project or env.get("WANDB_PROJECT", "marin_moe"),
+                              entity=entity or env.get("WANDB_ENTITY"), group=group or env.get("WANDB_RUN_GROUP"),
+                              name=run_id, id=run_id, resume="allow", tags=tags,
+                              mode=mode or env.get("WANDB_MODE", "online"), config=config or {})
+        self.jsonl = JsonlTracker(log_dir, run_id, config)
+
+    def log(self, metrics: dict, step: int) -> None:
+        plain = {k: _plain(v) for k, v in metrics.items()}
+        self.run.log(plain, step=int(step))
+        self.jsonl.log(plain, step)
+
+    def log_summary(self, metrics: dict) -> None:
+        plain = {k: _plain(v) for k, v in metrics.items()}
+        for k, v in plain.items():
+            self.run.summary[k] = v
+        self.jsonl.log_summary(plain)
+
+    def finish(self) -> None:
+        self.run.finish()
+        self.jsonl.finish()
+
+
 def make_tracker(kind: str, log_dir: str, run_id: str, config: dict | None = None, rank: int = 0):
     if rank != 0 or kind in ("noop", "disabled", None):
         return NoopTracker()
     if kind == "jsonl":
         return JsonlTracker(log_dir, run_id, config)
+    if kind == "wandb":
+        return WandbTracker(log_dir, run_id, config)
     raise ValueError(f"unknown tracker {kind!r}")
 
 

@@ -78,3 +78,49 @@ def test_router_histogram_coarsening_and_layer_metrics():
                               "routing_counts_per_layer": torch.tensor([[3, 1], [2, 2]])})
     assert m["train/router/layer_1/routing_entropy"] == 2.0
     assert m["train/router/layer_0/routing_hist"] == [3.0, 1.0]
+
+
+def test_wandb_tracker_with_fake_module(tmp_path, monkeypatch):
+    import json
+    import sys
+    import types
+
+    import pytest
+
+    from marin_experiments_b200.utils import tracker as T
+
+    calls = {}
+
+    class Run:
+        def __init__(self):
+            self.summary, self.logged, self.finished = {}, [], False
+
+        def log(self, m, step):
+            self.logged.append((step, m))
+
+        def finish(self):
+            self.finished = True
+
+    def init(**kw):
+        calls["init"] = kw
+        calls["run"] = Run()
+        return calls["run"]
+
+    monkeypatch.setitem(sys.modules, "wandb", types.SimpleNamespace(init=init))
+    monkeypatch.setenv("WANDB_PROJECT", "proj")
+    monkeypatch.setenv("WANDB_TAGS", "a,b")
+    monkeypatch.setenv("WANDB_MODE", "offline")
+    t = T.make_tracker("wandb", str(tmp_path), "run-1", {"lr": 0.1})
+    t.log({"train/loss": 2.5}, 3)
+    t.log_summary({"final": 1.0})
+    t.finish()
+    kw = calls["init"]
+    assert kw["project"] == "proj" and kw["tags"] == ["a", "b"] and kw["mode"] == "offline" and kw["name"] == "run-1"
+    assert calls["run"].logged == [(3, {"train/loss": 2.5})] and calls["run"].summary == {"final": 1.0}
+    assert calls["run"].finished
+    line = json.loads(open(tmp_path / "run-1" / "metrics.jsonl").read().splitlines()[0])
+    assert line == {"step": 3, "train/loss": 2.5}  # the JSONL copy is kept
+    monkeypatch.setitem(sys.modules, "wandb", None)  # not installed: a clear error, not a silent no-op
+    with pytest.raises(ImportError, match="needs the wandb package"):
+        T.make_tracker("wandb", str(tmp_path), "run-2")
+    assert isinstance(T.make_tracker("wandb", str(tmp_path), "run-3", rank=1), T.NoopTracker)
