@@ -124,19 +124,16 @@ def agent_transcript(task, sandbox: str = "auto") -> list[tuple[str, int]]:
         env.close()
 
 
-def _agent_tasks(n: int, seed: int, root: str | None):
-    import tempfile
-
+def _agent_tasks(n: int, seed: int, root: str):
     from . import terminal, terminal_tasks
 
-    root = root or tempfile.mkdtemp(prefix="mxk-terminal-tasks-")
     d = os.path.join(root, f"seed{seed}-n{n}")
     if not os.path.isdir(d):
         terminal_tasks.write_tasks(d, n, seed)
     return terminal.load_tasks(d)
 
 
-def _transcripts(stage: Stage, seed: int, sandbox: str = "auto", task_root: str | None = None):
+def _transcripts(stage: Stage, seed: int, sandbox: str = "auto", task_root: str = ""):
     rng = random.Random(seed)
     if stage.kind == "agent":
         return [agent_transcript(t, sandbox) for t in _agent_tasks(stage.sft_examples, seed, task_root)]
@@ -169,6 +166,18 @@ def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_pe
               max_program_tokens: int = 160, sft_batch: int = 8, seq_len: int = 1024, max_rounds: int = 3,
               eval_tools: int = 50, sandbox: str = "auto", task_root: str | None = None,
               agent_turns: int = 4) -> dict:
+    if stage.kind == "agent" and task_root is None:  # generated task directories live for this stage only
+        import shutil
+        import tempfile
+
+        root = tempfile.mkdtemp(prefix="mxk-terminal-tasks-")
+        try:
+            return run_stage(stage, make_model, tok, seed=seed, eval_per_family=eval_per_family,
+                             max_program_tokens=max_program_tokens, sft_batch=sft_batch, seq_len=seq_len,
+                             max_rounds=max_rounds, eval_tools=eval_tools, sandbox=sandbox, task_root=root,
+                             agent_turns=agent_turns)
+        finally:
+            shutil.rmtree(root, ignore_errors=True)
     model = make_model()
     t0 = time.time()
     out: dict = {"stage": asdict(stage), "seed": seed}
