@@ -76,8 +76,15 @@ class HFTokenizer:
 
 
 def load_tokenizer(name: str):
+    """``bytes``, a ``tokenizer.json`` path or a directory holding one, or ``trained/<name>``: a
+    tokenizer this project trained, from the mirror under ``MXK_TOKENIZER_MIRROR``."""
     if name == "bytes":
         return ByteTokenizer()
+    if name.startswith("trained/") and not os.path.exists(name):
+        mirror = os.environ.get("MXK_TOKENIZER_MIRROR", "")
+        if not mirror:
+            raise FileNotFoundError(f"tokenizer {name!r}: set MXK_TOKENIZER_MIRROR to the trained-tokenizer mirror")
+        name = os.path.join(mirror, "tokenizers", name)
     path = name if name.endswith(".json") else os.path.join(name, "tokenizer.json")
     if not os.path.exists(path):
         raise FileNotFoundError(f"tokenizer {name!r}: no local tokenizer.json (no network access)")
