@@ -105,7 +105,7 @@ class DatasetSpec:
     revision: str
     adapter: Adapter
     metadata_columns: tuple[str, ...] = ()
-    subset: str = ""
+    subset: str | tuple[str, ...] = ""  # one config name, or several read one after another
     splits: tuple[str, ...] = ("train",)
 
 
@@ -142,6 +142,46 @@ DATASETS: dict[str, DatasetSpec] = {
     "smoltalk2-smolagents": DatasetSpec("HuggingFaceTB/smoltalk2", "fc6cc21", Adapter(), (), "SFT",
                                         ("smolagents_toolcalling_traces_think",)),
 }
+_OMR_META = ("expected_answer", "problem_source", "problem_type", "generation_model", "inference_mode",
+             "pass_rate_72b_tir", "used_in_kaggle")
+_GT_META = ("question_id", "question_url", "reference_answer", "model_name", "question_source", "task")
+_DOLPHIN_META = ("score", "refusal", "compliance_rating", "overall_quality")
+# Further entries of the full chat / reasoning SFT registry (tunix-delphi-rl/sft_data/
+# instruction_datasets_marin_original.py).
+DATASETS.update({
+    "TIGER-Lab/AceCode-89K": DatasetSpec(
+        "TIGER-Lab/AceCode-89K", "13216309a9f6cb40b60cb1a9750071efeac414ad",
+        Adapter("instruction_response", prompt_column="question", response_column="inferences",
+                content_key="completion", best_of="pass_rate"), ("id", "source")),
+    "cognitivecomputations/dolphin-r1-nonreasoning": DatasetSpec(
+        "cognitivecomputations/dolphin-r1", "f6ac651", Adapter(), _DOLPHIN_META, "nonreasoning"),
+    "cognitivecomputations/dolphin-r1-reasoning": DatasetSpec(
+        "cognitivecomputations/dolphin-r1", "f6ac651",
+        Adapter("message_list_response", prompt_column="messages", response_column="answer"), _DOLPHIN_META,
+        ("reasoning-deepseek", "reasoning-flash")),
+    "open-r1/OpenThoughts-114k-math": DatasetSpec("open-r1/OpenThoughts-114k-math", "2db609d", Adapter(),
+                                                  ("system", "source", "generated_token_count", "correct")),
+    "bespokelabs/Bespoke-Stratos-17k": DatasetSpec(
+        "bespokelabs/Bespoke-Stratos-17k", "9e9adba",
+        Adapter(conversation_column="conversations", role_key="from", content_key="value")),
+    "HuggingFaceTB/smoltalk": DatasetSpec("HuggingFaceTB/smoltalk", "2c849df", Adapter(), ("source",), "all"),
+    "PrimeIntellect/verifiable-math-problems": DatasetSpec(
+        "PrimeIntellect/verifiable-math-problems", "2ad7c92",
+        Adapter("instruction_response", prompt_column="prompt", response_column="gold_standard_solution"),
+        ("source", "task_type", "problem_id")),
+    "GeneralReasoning/GeneralThought-195K-modelanswer": DatasetSpec(
+        "GeneralReasoning/GeneralThought-195K", "64f7cb8",
+        Adapter("instruction_response", prompt_column="question", response_column="model_answer"), _GT_META),
+    "GeneralReasoning/GeneralThought-195K-modelreasoning": DatasetSpec(
+        "GeneralReasoning/GeneralThought-195K", "64f7cb8",
+        Adapter("instruction_response", prompt_column="question", response_column="model_reasoning"), _GT_META),
+    "open-thoughts/OpenThoughts3-1.2M": DatasetSpec("open-thoughts/OpenThoughts3-1.2M", "61bcf9d", _OPENHERMES,
+                                                    ("difficulty", "source", "domain")),
+    **{f"nvidia/OpenMathReasoning/{sp}": DatasetSpec(
+        "nvidia/OpenMathReasoning", "d3d0866",
+        Adapter("instruction_response", prompt_column="problem", response_column="generated_solution"), _OMR_META,
+        "", (sp,)) for sp in ("cot", "tir", "genselect")},
+})
 TULU = ("allenai/tulu-3-sft-mixture", "allenai/tulu-v2-sft-mixture", "allenai/tulu-v2-sft-mixture-olmo-4096",
         "sherryy/tulu-3-sft-personas-instruction-following-expanded")
 TOOLUSE = ("smoltalk2-xlam", "smoltalk2-hermes-fc", "smoltalk2-smolagents")
@@ -187,19 +227,25 @@ def snapshot_dir(root: str, spec: DatasetSpec) -> str:
 
 
 def iter_rows(root: str, spec: DatasetSpec, split: str | None = None) -> Iterator[dict]:
-    """Raw rows of ``spec`` from its local snapshot: files under ``<root>/<hf id>/[<subset>/]`` whose
-    path contains the split name (when the snapshot has per-split files), in sorted order."""
-    base = snapshot_dir(root, spec)
-    if spec.subset and os.path.isdir(os.path.join(base, spec.subset)):
-        base = os.path.join(base, spec.subset)
-    if not os.path.isdir(base):
-        raise FileNotFoundError(f"no local snapshot of {spec.hf_id} at {base} (rows are read from local files)")
-    files = sorted(p for ext in ("parquet", "jsonl", "jsonl.gz", "json")
-                   for p in glob.glob(os.path.join(base, "**", f"*.{ext}"), recursive=True))
-    for sp in ([split] if split else spec.splits):
-        chosen = [p for p in files if sp in os.path.relpath(p, base)] or (files if len(spec.splits) == 1 else [])
-        for p in chosen:
-            yield from _read_file(p)
+    """Raw rows of ``spec`` from its local snapshot: files under ``<root>/<hf id>/[<subset>/]`` (each
+    subset in turn when there are several) whose path contains the split name (when the snapshot has
+    per-split files), in sorted order."""
+    root_dir = snapshot_dir(root, spec)
+    subsets = (spec.subset,) if isinstance(spec.subset, str) else tuple(spec.subset)
+    for sub in subsets:
+        base = root_dir
+        if sub and os.path.isdir(os.path.join(base, sub)):
+            base = os.path.join(base, sub)
+        elif sub and len(subsets) > 1:
+            raise FileNotFoundError(f"no local snapshot of {spec.hf_id} config {sub!r} under {root_dir}")
+        if not os.path.isdir(base):
+            raise FileNotFoundError(f"no local snapshot of {spec.hf_id} at {base} (rows are read from local files)")
+        files = sorted(p for ext in ("parquet", "jsonl", "jsonl.gz", "json")
+                       for p in glob.glob(os.path.join(base, "**", f"*.{ext}"), recursive=True))
+        for sp in ([split] if split else spec.splits):
+            chosen = [p for p in files if sp in os.path.relpath(p, base)] or (files if len(spec.splits) == 1 else [])
+            for p in chosen:
+                yield from _read_file(p)
 
 
 def load_messages(name: str, root: str, limit: int | None = None, split: str | None = None) -> Iterator[dict]:

@@ -94,3 +94,29 @@ def test_snapshots_mixture_and_cache(tmp_path):
     assert I.write_messages_jsonl(mix[:50], path) == 50
     meta = write_chat_cache([path], str(tmp_path / "cache"), ByteTokenizer())
     assert meta["num_docs"] == 50 and meta["format"] == "chat"
+
+
+def test_more_registry_entries_and_multi_subset(tmp_path):
+    root = str(tmp_path / "snap")
+    spec = I.DATASETS["cognitivecomputations/dolphin-r1-reasoning"]
+    for sub, n in (("reasoning-deepseek", 3), ("reasoning-flash", 2)):
+        _snapshot(root, I.DatasetSpec(spec.hf_id, spec.revision, spec.adapter, spec.metadata_columns, sub),
+                  [{"messages": [{"role": "user", "content": f"{sub}-{i}"}], "answer": "a", "score": 5}
+                   for i in range(n)], "jsonl")
+    got = list(I.load_messages("cognitivecomputations/dolphin-r1-reasoning", root))
+    assert [r["messages"][0]["content"] for r in got] == ["reasoning-deepseek-0", "reasoning-deepseek-1",
+                                                          "reasoning-deepseek-2", "reasoning-flash-0",
+                                                          "reasoning-flash-1"]
+    assert got[0]["metadata"]["score"] == 5
+    omr = I.DATASETS["nvidia/OpenMathReasoning/tir"]
+    _snapshot(root, omr, [{"problem": "p", "generated_solution": "tir"}], "jsonl", "tir")
+    _snapshot(root, omr, [{"problem": "p", "generated_solution": "cot"}], "jsonl", "cot")
+    assert [r["messages"][1]["content"] for r in I.load_messages("nvidia/OpenMathReasoning/tir", root)] == ["tir"]
+    ace = I.transform_row({"question": "q", "inferences": [{"completion": "x", "pass_rate": 0.1},
+                                                           {"completion": "y", "pass_rate": 1.0}], "id": 1},
+                          I.DATASETS["TIGER-Lab/AceCode-89K"])
+    assert ace["messages"][1]["content"] == "y"
+    bs = I.transform_row({"conversations": [{"from": "user", "value": "u"}, {"from": "assistant", "value": "v"}]},
+                         I.DATASETS["bespokelabs/Bespoke-Stratos-17k"])
+    assert [m["role"] for m in bs["messages"]] == ["user", "assistant"]
+    assert len(I.DATASETS) >= 25
