@@ -165,7 +165,10 @@ def _transcripts(stage: Stage, seed: int, sandbox: str = "auto", task_root: str 
 def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_per_family: int = 1,
               max_program_tokens: int = 160, sft_batch: int = 8, seq_len: int = 1024, max_rounds: int = 3,
               eval_tools: int = 50, sandbox: str = "auto", task_root: str | None = None,
-              agent_turns: int = 4) -> dict:
+              agent_turns: int = 4, save_dir: str | None = None) -> dict:
+    """Run one stage from a fresh policy; with ``save_dir`` the trained policy is exported there as a
+    Hugging Face Qwen3 checkpoint (safetensors + config.json), so a separate evaluation, RL or
+    serving job can load it."""
     if stage.kind == "agent" and task_root is None:  # generated task directories live for this stage only
         import shutil
         import tempfile
@@ -175,7 +178,7 @@ def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_pe
             return run_stage(stage, make_model, tok, seed=seed, eval_per_family=eval_per_family,
                              max_program_tokens=max_program_tokens, sft_batch=sft_batch, seq_len=seq_len,
                              max_rounds=max_rounds, eval_tools=eval_tools, sandbox=sandbox, task_root=root,
-                             agent_turns=agent_turns)
+                             agent_turns=agent_turns, save_dir=save_dir)
         finally:
             shutil.rmtree(root, ignore_errors=True)
     model = make_model()
@@ -286,6 +289,10 @@ def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_pe
     else:
         ev = code_tasks.evaluate(lambda p: complete(model, tok, p, max_program_tokens), ladder)
     out["eval"] = ev
+    if save_dir:
+        from ..models.qwen3_export import export_hf
+
+        out["checkpoint"] = export_hf(model, os.path.join(save_dir, stage.name))
     out["seconds"] = time.time() - t0
     return out
 
@@ -322,6 +329,7 @@ def main(argv=None) -> int:
                     help="Hugging Face Qwen3 checkpoint directory (safetensors + tokenizer.json)")
     ap.add_argument("--model", default=os.environ.get("MXK_POLICY", ""),
                     help="registered base model (models.registry): the checkpoint is checked against it")
+    ap.add_argument("--save-policies", default="", help="export each stage's trained policy under this directory")
     ap.add_argument("--dry-run", action="store_true")
     a = ap.parse_args(argv)
     for stage, done in plan(a.experiment, a.results_dir, a.stage):
@@ -342,8 +350,15 @@ def main(argv=None) -> int:
     if a.model:
         registry.check_checkpoint(a.model, a.model_dir)
     res = run(a.experiment, lambda: load_hf(a.model_dir, device=dev, dtype=torch.float32), tok, a.results_dir,
-              only=a.stage)
+              only=a.stage, save_dir=(os.path.join(a.save_policies, a.experiment) if a.save_policies else None))
+    import shutil
+
     for name, r in res.items():
+        ck = r.get("checkpoint")
+        if ck and os.path.isdir(ck):  # the exported policy loads with its tokenizer
+            for fn in ("tokenizer.json", "tokenizer_config.json"):
+                if os.path.exists(os.path.join(a.model_dir, fn)):
+                    shutil.copy(os.path.join(a.model_dir, fn), os.path.join(ck, fn))
         print(name, json.dumps(r["eval"]))
     return 0
 

@@ -74,7 +74,12 @@ def test_ladder_runs_idempotently(tmp_path, monkeypatch):
     assert set(ev) == {"first_solve", "best_solve", "mean_rounds"} and 1.0 <= ev["mean_rounds"] <= 2.0
     tl = pipeline.run("tools", make, tok, d, seq_len=512, eval_tools=3)["t1"]
     assert set(tl["eval"]) == {"tool/tool_call_rate", "tool/arg_acc", "arithmetic/solve_ratio"} and "grpo" in tl
-    ar = pipeline.run("arithmetic", make, tok, d, seq_len=512, eval_tools=4)["s2"]["eval"]
+    saved = pipeline.run("arithmetic", make, tok, d, seq_len=512, eval_tools=4, save_dir=str(tmp_path / "pol"))
+    ar = saved["s2"]["eval"]
+    from marin_experiments_b200.models.qwen3 import load_hf
+
+    back = load_hf(saved["s2"]["checkpoint"], dtype=torch.float32)
+    assert back.cfg.num_layers == 1 and os.path.exists(os.path.join(saved["s2"]["checkpoint"], "config.json"))
     assert set(ar) == {"arith/solve_ratio", "arith/solve_all", "arith/solve_none", "arith/format_rate"}
     cu = pipeline.run("curriculum", make, tok, d, seq_len=512, max_program_tokens=8)["sft_grpo"]
     assert set(cu["eval"]) == {"level1", "level7"} and "grpo" in cu
