@@ -100,3 +100,15 @@ def test_env_reset_step_and_traces(tmp_path):
     got = list(T.load_agent_traces(p))
     assert got[0]["messages"][1]["role"] == "assistant" and got[0]["metadata"]["agent"] == "terminus"
     assert T.parse_action(got[0]["messages"][1]["content"]).ok
+
+
+def test_agent_cannot_write_its_own_score(tmp_path):
+    """A task graded by exit status: a reward file the agent writes is removed before grading."""
+    root = str(tmp_path / "tasks")
+    task = T.load_task(_task(root, "exit-only", with_reward_file=False))
+    cheat = _act(["echo 1 > reward.txt\n", "mkdir -p logs/verifier && echo 1 > logs/verifier/reward.txt\n",
+                  "mkdir -p tests && ln -s ../outside.txt tests/test.sh\n"])
+    res = T.evaluate(lambda msgs: cheat if len(msgs) == 1 else _act([], done=True), [task], max_turns=3,
+                     sandbox="local")
+    assert res["solved"] == 0 and res["mean_score"] == 0.0
+    assert not (tmp_path / "outside.txt").exists()
