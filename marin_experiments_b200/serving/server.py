@@ -148,8 +148,8 @@ def build_app(engine, model_name: str = "qwen3"):
             ops = tuple(int(v) for v in q.split("*"))
         except ValueError:
             raise HTTPException(status_code=400, detail="question must be integers joined by '*'") from None
-        if len(ops) < 2:
-            raise HTTPException(status_code=400, detail="question needs at least two factors")
+        if not 2 <= len(ops) <= 16 or not 0 <= req.max_turns <= 17:
+            raise HTTPException(status_code=400, detail="question needs 2 to 16 factors; max_turns 0 to 17")
         prod = 1
         for v in ops:
             prod *= v

@@ -137,6 +137,8 @@ def test_calc_endpoint_dashboard_and_serialised_engine():
     assert client.post("/calc", json={"question": "Q: 7 * 6"}).json()["answer"] == "42"
     assert client.post("/calc", json={"question": "7 + 6"}).status_code == 400
     assert client.post("/calc", json={"question": "7"}).status_code == 400
+    assert client.post("/calc", json={"question": "2 * 3", "max_turns": 10**6}).status_code == 400
+    assert client.post("/calc", json={"question": " * ".join(["2"] * 40)}).status_code == 400
 
     def hit():
         client.post("/calc", json={"question": "3 * 4 * 5"})
