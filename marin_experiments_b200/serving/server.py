@@ -104,7 +104,10 @@ def build_app(engine, model_name: str = "qwen3"):
 
     def run(prompts, **kw):
         with lock:
-            return engine.generate(prompts, **kw)
+            try:
+                return engine.generate(prompts, **kw)
+            except ValueError as exc:  # e.g. prompt + max_tokens beyond the KV cache: the request's fault
+                raise HTTPException(status_code=400, detail=str(exc)) from exc
 
     @app.get("/", response_class=HTMLResponse)
     @app.get("/dashboard", response_class=HTMLResponse)

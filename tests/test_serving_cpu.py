@@ -48,6 +48,8 @@ def test_http_api():
     assert client.post("/generate", json={"prompt": "a", "prompts": ["b"]}).status_code == 400
     r = client.post("/v1/completions", json={"prompt": "hey", "max_tokens": 3, "temperature": 0.0})
     assert r.json()["object"] == "text_completion" and len(r.json()["choices"]) == 1
+    too_long = client.post("/generate", json={"prompt": "hi", "max_tokens": 100000})
+    assert too_long.status_code == 400 and "max_len" in too_long.json()["detail"]
 
 
 def test_http_client_against_live_server():
