@@ -277,15 +277,18 @@ class GrugEvalConfig:
 @dataclass(frozen=True)
 class DataConfig:
     """Data source. ``synthetic`` reproduces megagpt-speedrun/synth_data.py:25-70; ``cache``
-    reads a token cache written by the tokenize step; ``mixture`` weights several caches."""
+    reads a token cache written by the tokenize step; ``mixture`` weights several caches; ``remote``
+    is the named object-store mixture ``mix`` (``data.remote.MIXES``), mirrored under ``cache_dir``
+    when the dataset is built (so a launch config can name it without touching the network)."""
 
-    source: Literal["synthetic", "uniform", "cache", "mixture"] = "synthetic"
+    source: Literal["synthetic", "uniform", "cache", "mixture", "remote"] = "synthetic"
     seq_len: int = 4096
     cache_dir: str | None = None
     components: tuple[tuple[str, str, float], ...] = ()  # (name, cache_dir, weight)
     doc_len: int = 1024
     seed: int = 0
     prefetch: int = 4
+    mix: str = ""
 
 
 @dataclass(frozen=True)

@@ -43,6 +43,12 @@ def open_cache(cache_dir: str, seq_len: int, seed: int, shuffle: bool = True):
 def build_dataset(cfg, seq_len: int, vocab_size: int, *, block_size: int = 2048, stop_strategy: str = "restart"):
     m = rt()
     seed = int(cfg.seed)
+    if cfg.source == "remote":
+        from .remote import MIXES, data_config
+
+        if cfg.mix not in MIXES:
+            raise ValueError(f"unknown remote mixture {cfg.mix!r}; one of {sorted(MIXES)}")
+        cfg = data_config(MIXES[cfg.mix], cfg.cache_dir or os.environ.get("MXK_DATA_ROOT", "data_cache"), seed=seed)
     if cfg.source in ("synthetic", "uniform"):
         comps = [m.SyntheticDataset(seq_len, vocab_size, cfg.doc_len if cfg.source == "synthetic" else seq_len, seed)]
         weights = [[1.0]]

@@ -8,7 +8,9 @@ throughput levers (``SP_EMBED``, ``SP_SEQ``, ``SP_INTERMEDIATE``, ``SP_GLOBAL_EV
 (``SP_SCHEDULE``, ``SP_WARMUP``, ``SP_DECAY``, ``SP_MIN_LR``, ``SP_REWARMUP``), the mesh (``SP_EP``,
 ``SP_TP``, ``SP_REPLICA``), adaptive sparsity (``SPARSITY_MODE=adaptive``, ``SP_MIN_K``, ``SP_COEF``,
 ``SP_TEMP``), the k-curriculum (``SP_CURRICULUM="k:frac,..."``), weights-only init (``SP_INIT_FROM``),
-raw overrides (``SP_BATCH``, ``SP_STEPS``), data (``SP_DATA``: ``synthetic`` or a token cache path;
+raw overrides (``SP_BATCH``, ``SP_STEPS``), data (``SP_DATA``: ``synthetic``, a token cache path, or a
+named object-store mixture -- ``datakit`` / ``nemotron``, ``nemotron-full``, ``sft`` -- mirrored under
+``MXK_DATA_ROOT`` from ``MXK_CORPUS_PREFIX`` when training starts;
 ``SP_SYNTH_DATA=1`` forces synthetic), eval (``SP_EVAL``, ``SP_EVAL_ONLY``, ``SP_EVAL_BS``,
 ``SP_EVAL_MAXB``) and ``SP_TAG``. ``SP_PP_MODE=async|sync`` runs the pipeline-parallel entry points
 instead. The ``[arm]`` line printed per launch is the one the sweep monitor parses.
@@ -114,8 +116,13 @@ def make_launch(env=None) -> tuple[GrugLaunchConfig, str]:
     if env.get("SP_TAG"):
         run_id += f"-{env['SP_TAG']}"
     data_kind = _env(env, "SP_DATA", "synthetic")
+    remote_mix = {"datakit": "nemotron", "datakit_eval": "nemotron", "nemotron": "nemotron",
+                  "nemotron-full": "nemotron-full", "sft": "sft-chat", "sft-chat": "sft-chat"}.get(data_kind)
     if env.get("SP_SYNTH_DATA", "").strip().lower() in ("1", "true", "yes") or data_kind == "synthetic":
         data = DataConfig(source="synthetic", seed=seed)
+    elif remote_mix:  # the reference's object-store mixtures, mirrored under MXK_DATA_ROOT at run time
+        data = DataConfig(source="remote", mix=remote_mix, cache_dir=os.environ.get("MXK_DATA_ROOT", "data_cache"),
+                          seed=seed)
     else:
         data = DataConfig(source="cache", cache_dir=data_kind, seed=seed)
     ev = None

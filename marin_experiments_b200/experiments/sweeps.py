@@ -40,6 +40,11 @@ BASE = {
     "SP_BATCH": "32", "SP_REMAT": "none", "SP_ATTN": "sm100_flash",
 }
 
+# real data at constant LR (the stable phase of a warmup-stable-decay schedule)
+_REAL = {"SP_SYNTH_DATA": "0", "SP_DATA": "datakit", "SP_SCHEDULE": "constant", "SP_WARMUP": "0.02",
+         "SP_TOKENS": "5400000000"}
+NEEDS_INIT = ("cool", "eval")
+
 SWEEPS: dict[str, dict[str, dict[str, str]]] = {
     # the expert ladder at the headline geometry
     "anchor": {
@@ -67,7 +72,53 @@ SWEEPS: dict[str, dict[str, dict[str, str]]] = {
     # short runs for a profile capture
     "prof": {"prof": {"SP_STEPS": "12"}},
     # weak scaling at 32 sequences per GPU
-    "scale": {f"g{g}": {"_GPUS": str(g), "_BATCH_PER_GPU": "32"} for g in (1, 2, 4, 8)},
+    "weak": {f"g{g}": {"_GPUS": str(g), "_BATCH_PER_GPU": "32"} for g in (1, 2, 4, 8)},
+    # loss against wall-clock on real data, constant LR: more experts vs wider experts vs the base; each
+    # arm's step count sized to end near the same time (megagpt-speedrun/iris_jobs.py "lossab")
+    "lossab": {
+        "a_thin": {"SP_TOPK": "8", "SP_BATCH": "16", "SP_REMAT": "save_moe", **_REAL, "SP_STEPS": "23000"},
+        "b_bigE": {"SP_EXPERTS": "256", "SP_TOPK": "8", "SP_BATCH": "8", "SP_REMAT": "save_moe", **_REAL,
+                   "SP_STEPS": "48000"},
+        "c_chonky": {"SP_TOPK": "8", "SP_BATCH": "16", "SP_INTERMEDIATE": "1536", "SP_REMAT": "recompute_all",
+                     **_REAL, "SP_STEPS": "13000"},
+    },
+    # wider experts at batches that fit
+    "best": {
+        "chonky2x_b16": {"SP_TOPK": "8", "SP_BATCH": "16", "SP_REMAT": "recompute_all", "SP_INTERMEDIATE": "1536"},
+        "chonky4x_b8": {"SP_TOPK": "8", "SP_BATCH": "8", "SP_REMAT": "recompute_all", "SP_INTERMEDIATE": "3072"},
+    },
+    # model-size ladder at b16: more experts, wider experts, wider model (the reference's scale rounds)
+    "scale": {
+        "e128k8": {"SP_EXPERTS": "128", "SP_TOPK": "8", "SP_BATCH": "16", "SP_REMAT": "save_moe"},
+        "e256k8": {"SP_EXPERTS": "256", "SP_TOPK": "8", "SP_BATCH": "16", "SP_REMAT": "save_moe"},
+        "e256k16": {"SP_EXPERTS": "256", "SP_TOPK": "16", "SP_BATCH": "16", "SP_REMAT": "save_moe"},
+        "e128i1536": {"SP_EXPERTS": "128", "SP_TOPK": "8", "SP_BATCH": "16", "SP_INTERMEDIATE": "1536",
+                      "SP_REMAT": "recompute_all"},
+        "d2048e128": {"SP_HIDDEN": "2048", "SP_EXPERTS": "128", "SP_TOPK": "8", "SP_BATCH": "16",
+                      "SP_REMAT": "save_moe"},
+    },
+    "scale2": {
+        "e192k8": {"SP_EXPERTS": "192", "SP_TOPK": "8", "SP_BATCH": "16", "SP_REMAT": "save_moe"},
+        "e64i1536": {"SP_TOPK": "8", "SP_BATCH": "16", "SP_INTERMEDIATE": "1536", "SP_REMAT": "recompute_all"},
+        "e128i1024": {"SP_EXPERTS": "128", "SP_TOPK": "8", "SP_BATCH": "16", "SP_INTERMEDIATE": "1024",
+                      "SP_REMAT": "recompute_all"},
+        "e256k8b8": {"SP_EXPERTS": "256", "SP_TOPK": "8", "SP_BATCH": "8", "SP_REMAT": "save_moe"},
+        "d2048e64": {"SP_HIDDEN": "2048", "SP_TOPK": "8", "SP_BATCH": "16", "SP_REMAT": "save_moe"},
+    },
+    "scale3": {f"e{e}k8": {"SP_EXPERTS": str(e), "SP_TOPK": "8", "SP_BATCH": "16", "SP_REMAT": "save_moe"}
+               for e in (144, 160, 176)},
+    # the production pretraining arm: E128 / K8 at sequence 4096 on real data, constant LR
+    "run2": {"e128k8": {"SP_EXPERTS": "128", "SP_TOPK": "8", "SP_BATCH": "16", "SP_SEQ": "4096",
+                        "SP_REMAT": "save_moe", **_REAL, "SP_MIN_LR": "0", "SP_TOKENS": "13500000000",
+                        "SP_STEPS": "205000"}},
+    # SFT cooldown of a run2 checkpoint (weights only; needs --init-from): chat data, linear decay to 0
+    "cool": {"sft": {"SP_EXPERTS": "128", "SP_TOPK": "8", "SP_BATCH": "16", "SP_SEQ": "4096", "SP_REMAT": "save_moe",
+                     "SP_SYNTH_DATA": "0", "SP_DATA": "sft", "SP_SCHEDULE": "linear", "SP_MIN_LR": "0",
+                     "SP_WARMUP": "0.02", "SP_TOKENS": "13500000000", "SP_STEPS": "20000"}},
+    # held-out evaluation of a checkpoint, no training (needs --init-from)
+    "eval": {"spr1": {"SP_TOPK": "8", "SP_BATCH": "16", "SP_SEQ": "4096", "SP_REMAT": "save_moe",
+                      "SP_SYNTH_DATA": "0", "SP_DATA": "datakit_eval", "SP_STEPS": "1000", "SP_EVAL": "1",
+                      "SP_EVAL_ONLY": "1", "SP_EVAL_BS": "16"}},
     # adaptive sparsity and the k curriculum
     "sparsity": {
         "fixed": {},
@@ -198,10 +249,16 @@ def main(argv=None):
     ap.add_argument("--timeout", type=float, default=3600.0)
     ap.add_argument("--warmup", type=int, default=8, help="steps excluded from the tokens/s median")
     ap.add_argument("--dry-run", action="store_true")
+    ap.add_argument("--init-from", default=None, help="checkpoint for weights-only init (SP_INIT_FROM)")
     ap.add_argument("--submit", action="store_true", help="send the arms to a job scheduler instead of running them")
     ap.add_argument("--wait", action="store_true", help="with --submit: wait and analyse the logs")
     a = ap.parse_args(argv)
+    if a.sweep in NEEDS_INIT and not a.init_from:
+        raise SystemExit(f"sweep {a.sweep} needs --init-from <checkpoint directory>")
     jobs = plan(a.sweep, gpus=a.gpus, tag=a.tag, only=a.only.split(",") if a.only else None)
+    if a.init_from:
+        for j in jobs:
+            j.env["SP_INIT_FROM"] = a.init_from
     if a.submit and not a.dry_run:
         from ..cluster import current_client
 

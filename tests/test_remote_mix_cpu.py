@@ -119,3 +119,27 @@ def test_mirror_between_stores(client, tmp_path):
     import json
 
     assert json.loads(client.get("dst", "mirror/MANIFEST.json")) == man
+
+
+def test_remote_source_resolves_when_the_dataset_is_built(client, tmp_path, monkeypatch):
+    """``DataConfig(source="remote", mix=...)`` names a mixture; the mirror happens in build_dataset."""
+    rng = np.random.default_rng(1)
+    rows = [{"input_ids": rng.integers(1, 500, size=rng.integers(40, 90)).astype(np.int32)} for _ in range(30)]
+    write_tree_cache(str(tmp_path / "src"), rows)
+    _upload(client, str(tmp_path / "src"), "bkt", "root/tokenized/tiny-1/train")
+    monkeypatch.setitem(remote.MIXES, "tiny", remote.RemoteMix("tiny", {"t": ("tokenized/tiny-1", 1.0)}))
+    for k, v in {"MXK_CORPUS_PREFIX": "s3://bkt/root", "AWS_ENDPOINT_URL": client.endpoint, "AWS_ACCESS_KEY_ID": AK,
+                 "AWS_SECRET_ACCESS_KEY": SK, "AWS_DEFAULT_REGION": "us-east-1"}.items():
+        monkeypatch.setenv(k, v)
+    rt = pytest.importorskip("marin_experiments_b200.runtime")
+    try:
+        rt.rt()
+    except Exception as e:
+        pytest.skip(f"native runtime unavailable: {e}")
+    from marin_experiments_b200.config import DataConfig
+    from marin_experiments_b200.data.loader import build_dataset
+
+    ds = build_dataset(DataConfig(source="remote", mix="tiny", cache_dir=str(tmp_path / "local")), 32, 512)
+    assert ds.seq_len() == 32 and os.path.exists(tmp_path / "local" / "native" / "t" / "meta.json")
+    with pytest.raises(ValueError, match="unknown remote mixture"):
+        build_dataset(DataConfig(source="remote", mix="nope"), 32, 512)

@@ -17,7 +17,7 @@ def test_plan_expands_arms():
     assert "torch.distributed.run" in j.argv and "--nproc-per-node=8" in j.argv and "127.0.0.1" in j.argv
     assert j.argv[-2:] == ["-m", sweeps.LAUNCHER]
     # per-arm GPU counts and batch per GPU (weak scaling)
-    sc = {j.name: j for j in sweeps.plan("scale", tag="s")}
+    sc = {j.name: j for j in sweeps.plan("weak", tag="s")}
     assert sc["s-g1"].gpus == 1 and sc["s-g1"].argv == [sys.executable, "-m", sweeps.LAUNCHER]
     assert sc["s-g4"].env["SP_BATCH"] == "128" and sc["s-g4"].env["SP_EP"] == "4"
     assert [j.name for j in sweeps.plan("lever", only=["embed512"], tag="x")] == ["x-embed512"]
@@ -112,3 +112,18 @@ def test_submit_arms_to_scheduler(tmp_path):
     r = Rec()
     sweeps.submit([two], r)
     assert list(r.req.entrypoint.command) == [sys.executable, "-m", sweeps.LAUNCHER] and r.req.resources.gpus == 2
+
+
+def test_reference_grids_and_init_from(monkeypatch, capsys):
+    for name in ("lossab", "best", "scale", "scale2", "scale3", "run2", "cool", "eval", "weak"):
+        assert name in sweeps.SWEEPS
+    la = {j.name: j for j in sweeps.plan("lossab", gpus=8, tag="l")}
+    assert la["l-b_bigE"].env["SP_EXPERTS"] == "256" and la["l-a_thin"].env["SP_DATA"] == "datakit"
+    launch, _ = megagpt.make_launch(la["l-a_thin"].env)
+    assert launch.data.source == "remote" and launch.data.mix == "nemotron"
+    cool = sweeps.plan("cool", gpus=8, tag="c")[0]
+    assert megagpt.make_launch(cool.env)[0].data.mix == "sft-chat"
+    with pytest.raises(SystemExit, match="needs --init-from"):
+        sweeps.main(["cool", "--dry-run"])
+    assert sweeps.main(["eval", "--dry-run", "--init-from", "/ckpt/run2", "--log-dir", "/tmp/x"]) == 0
+    assert "SP_INIT_FROM=/ckpt/run2" in capsys.readouterr().out
