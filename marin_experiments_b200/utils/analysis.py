@@ -194,6 +194,59 @@ def iso_step(dirs: list[str], step: int, keys: list[str]) -> list[dict]:
     return out
 
 
+def smooth(values, window: int):
+    """Centred rolling mean that averages only the points that exist near the ends (no zero padding,
+    which would pull the final values -- the plateau this analysis reads -- towards zero)."""
+    import numpy as np
+
+    v = np.asarray(values, dtype=np.float64)
+    if window <= 1 or len(v) == 0:
+        return v
+    c = np.concatenate([[0.0], np.cumsum(v)])
+    h = window // 2
+    lo = np.clip(np.arange(len(v)) - h, 0, len(v))
+    hi = np.clip(np.arange(len(v)) + window - h, 0, len(v))
+    return (c[hi] - c[lo]) / (hi - lo)
+
+
+def isoloss(histories: dict[str, list[tuple[int, float]]], sync: str, *, tail_frac: float = 0.1,
+            window: int = 25) -> list[dict]:
+    """Token overhead of delayed / pipelined runs against a synchronous reference
+    (delayed-gradient-pp/analyze_isoloss.py). Per run, from its ``(step, loss)`` history:
+
+    * ``plateau``: mean of the raw losses over the last ``tail_frac`` of the steps;
+    * ``gap``: plateau minus the reference's plateau;
+    * ``slope_per_1k``: least-squares slope over that tail, per 1000 steps (still negative: the run
+      is still descending -- a token tax, not a floor);
+    * ``overhead``: the first step at which the run's smoothed loss reaches its own plateau, over the
+      first step at which the reference's smoothed loss reaches that same value (tokens scale with
+      steps at a fixed batch); ``None`` when the reference never gets there."""
+    import numpy as np
+
+    def stats(h):
+        h = sorted(h)
+        steps = np.array([s for s, _ in h], dtype=np.float64)
+        loss = np.array([v for _, v in h], dtype=np.float64)
+        n = max(2, int(round(len(h) * tail_frac)))
+        ts, tl = steps[-n:], loss[-n:]
+        slope = float(np.polyfit(ts, tl, 1)[0]) * 1000 if len(ts) >= 2 and ts[-1] > ts[0] else 0.0
+        return steps, loss, smooth(loss, window), float(tl.mean()), slope
+
+    if sync not in histories:
+        raise KeyError(f"reference run {sync!r} not among {sorted(histories)}")
+    s_steps, _, s_sm, s_plat, _ = stats(histories[sync])
+    out = []
+    for name, h in histories.items():
+        steps, _, sm, plat, slope = stats(h)
+        reach = np.nonzero(sm <= plat)[0]
+        own = float(steps[reach[0]]) if len(reach) else float(steps[-1])
+        ref = np.nonzero(s_sm <= plat)[0]
+        overhead = own / float(s_steps[ref[0]]) if len(ref) and s_steps[ref[0]] > 0 else None
+        out.append({"run": name, "plateau": plat, "gap": plat - s_plat, "slope_per_1k": slope,
+                    "overhead": overhead, "steps": int(steps[-1])})
+    return out
+
+
 def rows_table(rows: list[dict], keys: list[str]) -> str:
     head = ["run", "max_step"] + keys
     lines = ["| " + " | ".join(head) + " |", "|" + "---|" * len(head)]
@@ -311,6 +364,13 @@ def main(argv=None):
     i.add_argument("--step", type=int, required=True)
     i.add_argument("--match", default=None)
     i.add_argument("--keys", default="train/loss")
+    q = sub.add_parser("isoloss", help="token overhead of runs against a synchronous reference run")
+    q.add_argument("log_dir")
+    q.add_argument("--sync", required=True, help="run id of the synchronous reference")
+    q.add_argument("--match", default=None)
+    q.add_argument("--key", default="train/loss")
+    q.add_argument("--tail", type=float, default=0.1)
+    q.add_argument("--window", type=int, default=25)
     p = sub.add_parser("profile", help="device-time breakdown of a torch.profiler Chrome trace")
     p.add_argument("trace")
     p.add_argument("--steps", type=int, default=1)
@@ -328,6 +388,12 @@ def main(argv=None):
             if a.watch <= 0 or (a.rounds and n >= a.rounds):
                 break
             time.sleep(a.watch)
+    elif a.cmd == "isoloss":
+        hist = {os.path.basename(d): [(int(r["step"]), float(r[a.key])) for r in load_history(d)
+                                      if r.get(a.key) is not None] for d in run_dirs(a.log_dir, a.match)}
+        rows = isoloss({k: v for k, v in hist.items() if v}, a.sync, tail_frac=a.tail, window=a.window)
+        keys = ["plateau", "gap", "slope_per_1k", "overhead"]
+        print(rows_table([{**r, "max_step": r["steps"]} for r in rows], keys))
     elif a.cmd in ("results", "iso-step"):
         keys = a.keys.split(",")
         dirs = run_dirs(a.log_dir, a.match)

@@ -92,3 +92,33 @@ def test_sweep_cli_watch_and_glob(tmp_path, capsys):
     an.main(["sweep", str(tmp_path / "*.log"), "--warmup", "8", "--watch", "0.01", "--rounds", "2"])
     out = capsys.readouterr().out
     assert out.count("| run |") == 2 and "sw-d1536-e64-k4" in out
+
+
+def test_isoloss_token_overhead(tmp_path):
+    import pytest
+
+    import json
+    import os
+
+    import numpy as np
+
+    from marin_experiments_b200.utils import analysis as A
+
+    steps = np.arange(0, 6001, 20)
+    sync = 2.0 + 3.0 * np.exp(-steps / 1000.0)
+    slow = 2.0 + 3.0 * np.exp(-steps / 1500.0)  # the same curve, 1.5x more steps to each loss
+    floor = 2.3 + 3.0 * np.exp(-steps / 1000.0)  # converged above the reference
+    hist = {"sync": list(zip(steps, sync)), "delayed": list(zip(steps, slow)), "floor": list(zip(steps, floor))}
+    rows = {r["run"]: r for r in A.isoloss(hist, "sync", tail_frac=0.05, window=5)}
+    assert abs(rows["sync"]["gap"]) < 1e-12 and rows["sync"]["overhead"] == pytest.approx(1.0, abs=0.02)
+    assert rows["delayed"]["overhead"] == pytest.approx(1.5, rel=0.05) and rows["delayed"]["slope_per_1k"] < 0
+    assert rows["floor"]["gap"] == pytest.approx(0.3, abs=0.01)
+    sm = A.smooth([1.0, 1.0, 1.0, 1.0], 3)
+    assert np.allclose(sm, 1.0)  # ends are not pulled toward zero
+    for name, h in hist.items():
+        d = tmp_path / name
+        os.makedirs(d)
+        with open(d / "metrics.jsonl", "w") as f:
+            for s, v in h:
+                f.write(json.dumps({"step": int(s), "train/loss": float(v)}) + "\n")
+    A.main(["isoloss", str(tmp_path), "--sync", "sync", "--tail", "0.05", "--window", "5"])
