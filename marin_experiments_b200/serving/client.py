@@ -3,6 +3,9 @@ prompt or a batch through ``POST /generate``) and ``complete`` (``POST /v1/compl
 plain HTTP with a timeout, plus a command line. The reference resolves its endpoint through its
 cluster's proxy; here the caller passes the server's base URL (``--url`` or ``MXK_SERVE_URL``).
 
+``chat_policy`` / ``text_policy`` wrap a served model as the policy callables the RL environments
+and agent evaluations take.
+
 ``python -m marin_experiments_b200.serving.client --url http://127.0.0.1:8000 --prompt "def f():"
 --max-tokens 64 --temperature 0``
 """
@@ -51,6 +54,30 @@ def complete(url: str, prompt: str, *, max_tokens: int = 256, temperature: float
     out = _post(url, "/v1/completions", {"prompt": prompt, "max_tokens": max_tokens, "temperature": temperature,
                                          "top_p": top_p, "seed": seed, "stop": stop}, timeout_s)
     return out["choices"][0]["text"]
+
+
+def chat_policy(url: str, *, max_tokens: int = 512, temperature: float = 0.0, timeout_s: float = 300.0):
+    """A served model as an agent policy (openthoughts-agent/eval/model_serving.py): ``messages ->
+    reply``, rendering the conversation as ChatML with an open assistant turn and stopping at the end
+    marker -- the ``model_fn`` that ``rl.terminal.evaluate`` and ``rl.agent.run_episode`` take."""
+    from ..data.chat import IM_END, render_chatml
+
+    def policy(messages: list[dict]) -> str:
+        text = generate(url, render_chatml(messages, add_generation_prompt=True), max_tokens=max_tokens,
+                        temperature=temperature, stop=[IM_END], timeout_s=timeout_s)
+        return text.split(IM_END, 1)[0]
+
+    return policy
+
+
+def text_policy(url: str, *, max_tokens: int = 64, temperature: float = 0.0, stop: list[str] | None = None,
+                timeout_s: float = 300.0):
+    """A served model as a raw-text policy (``text -> continuation``), for the few-shot environments."""
+
+    def policy(text: str) -> str:
+        return generate(url, text, max_tokens=max_tokens, temperature=temperature, stop=stop, timeout_s=timeout_s)
+
+    return policy
 
 
 def main(argv=None) -> int:

@@ -151,3 +151,54 @@ def test_calc_endpoint_dashboard_and_serialised_engine():
     for t in th:
         t.join()
     assert eng.peak == 1  # generations never overlap on the shared engine
+
+
+def test_served_model_as_agent_policy(tmp_path):
+    """A terminal task solved by a served model: the chat policy renders the conversation, stops at the
+    end marker and returns the reply."""
+    import json
+    import socket
+    import threading
+    import time
+
+    import uvicorn
+
+    from marin_experiments_b200.data.chat import IM_END
+    from marin_experiments_b200.rl import terminal, terminal_tasks
+    from marin_experiments_b200.serving import client
+
+    terminal_tasks.write_tasks(str(tmp_path / "tasks"), 2, seed=3)
+    tasks = terminal.load_tasks(str(tmp_path / "tasks"))
+    acts = {t.instruction: terminal_tasks.oracle_actions(t) for t in tasks}
+
+    class OracleEngine:
+        ready = True
+
+        def generate(self, prompts, stop=None, **kw):
+            out = []
+            for p in prompts:
+                inst = next(k for k in acts if k in p)
+                n = p.count("<|im_start|>assistant") - 1  # assistant turns already taken
+                out.append(acts[inst][n] + IM_END + "trailing text")
+                assert stop == [IM_END]
+            return out
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    srv = uvicorn.Server(uvicorn.Config(build_app(OracleEngine(), "oracle"), host="127.0.0.1", port=port,
+                                       log_level="warning"))
+    th = threading.Thread(target=srv.run, daemon=True)
+    th.start()
+    try:
+        t0 = time.time()
+        while not srv.started:
+            assert time.time() - t0 < 30
+            time.sleep(0.05)
+        res = terminal.evaluate(client.chat_policy(f"http://127.0.0.1:{port}"), tasks, max_turns=4, sandbox="local")
+        assert res["solved"] == 2
+        assert json.loads(res["episodes"][0].messages[1]["content"])["commands"]
+    finally:
+        srv.should_exit = True
+        th.join(timeout=10)
