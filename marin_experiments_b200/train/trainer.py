@@ -186,14 +186,20 @@ class Trainer:
                     "tokens": int(batch["tokens"].numel()) * (self.dist.world if self.dist else 1),
                     "batch_size": int(batch["tokens"].shape[0]) * (self.dist.world if self.dist else 1),
                     "metrics": met}
+            t_h = time.perf_counter()
             for h in hooks:
                 h(self, info)
+            hook_time = time.perf_counter() - t_h
             if tracker is not None and self.step % log_every == 0:
                 from ..utils.tracker import router_layer_metrics
 
+                perf = {"throughput/step_duration": dt, "throughput/loading_time": t_load,
+                        "throughput/hook_time": hook_time}
+                for h in hooks:  # e.g. the throughput hook's tokens/s and MFU of this step
+                    perf.update(getattr(h, "last", None) or {})
                 tracker.log({**{k: (float(v.float().mean()) if torch.is_tensor(v) else v) for k, v in met.items()
-                                if not (torch.is_tensor(v) and v.numel() > 1)}, **router_layer_metrics(met)},
-                            step=self.step)
+                                if not (torch.is_tensor(v) and v.numel() > 1)}, **router_layer_metrics(met),
+                             **perf}, step=self.step)
             if checkpointer is not None:
                 checkpointer.on_step(self, self.step)
             last = info

@@ -93,3 +93,21 @@ def test_watch_stats_sums_expert_shards_over_ranks():
         assert math.isclose(w["watch/grad_norm/attn.w_o"], 5.0)  # replicated: not summed
         assert math.isclose(w["watch/grad_norm/mlp.w_down"], math.sqrt(4 * 1 + 4 * 4))  # both ranks' shards
         assert math.isclose(w["watch/grad_norm/total"], math.sqrt(25 + 20))
+
+
+def test_tracker_gets_throughput_loading_and_hook_time(tmp_path):
+    import io
+    import json
+
+    from marin_experiments_b200.utils.tracker import JsonlTracker, ThroughputHook
+
+    tr = _trainer(steps=3)
+    trk = JsonlTracker(str(tmp_path), "run")
+    thr = ThroughputHook(TINY, 1, stream=io.StringIO())
+    tr.fit(iter(_batches(3)), 3, hooks=[thr], tracker=trk, log_every=1)
+    trk.finish()
+    rows = [json.loads(x) for x in open(tmp_path / "run" / "metrics.jsonl")]
+    assert len(rows) == 3
+    for r in rows:
+        assert r["throughput/tokens_per_second"] > 0 and r["throughput/loading_time"] >= 0
+        assert r["throughput/hook_time"] >= 0 and r["throughput/step_duration"] > 0 and "train/loss" in r
