@@ -187,3 +187,22 @@ def test_max_inflight_microbatches():
     assert max_inflight("zb", 4, 16) <= 4
     assert max_inflight("1f1b", 4, 16, mode="async") == 4
     assert max_inflight("1f1b", 1, 8) == 1
+
+
+def _p2p_rank(rank, world):
+    import torch.distributed as tdist
+
+    from marin_experiments_b200.benchmarks.p2p_probe import probe
+
+    tdist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        return probe((0.25, 1), iters=2)
+    finally:
+        tdist.destroy_process_group()
+
+
+def test_p2p_ring_probe():
+    res = run_ranks(_p2p_rank, 3, timeout=120)
+    rows = res[0]
+    assert [r["mb"] for r in rows] == [0.25, 1] and all(r["gbs_per_direction"] > 0 for r in rows)
+    assert rows[0]["ms"] == res[1][0]["ms"]  # max over ranks, the same on every rank
