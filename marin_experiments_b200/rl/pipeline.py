@@ -14,7 +14,9 @@ evaluates greedily on held-out tasks and writes
 re-running resumes the ladder; deleting one file re-runs that stage. ``plan`` (and ``--dry-run``)
 lists which stages would run without building a model.
 
-Three more kinds: ``agent`` (terminal tasks in the sandbox, ``rl.terminal`` over the built-in
+Four more kinds: ``chat`` (conversational SFT on the instruction / tool-use mixture of
+``data.instruct`` read from local snapshots under ``MXK_SFT_SNAPSHOTS``, evaluated as the held-out
+assistant-token loss before and after; launch_chat_sft.py), ``agent`` (terminal tasks in the sandbox, ``rl.terminal`` over the built-in
 ``rl.terminal_tasks``: SFT on oracle trajectories whose observations come from running them, then
 multi-turn GRPO with the graded score as the episode reward, then the solve rate on held-out tasks;
 the openthoughts-agent launchers), ``arith`` (staged few-shot arithmetic, ``rl.arithmetic``, stage = ``depth``;
@@ -25,7 +27,7 @@ Ladders: ``coding`` -- few-shot only, SFT on 150 / 300 / 1000 transcripts, SFT 3
 ``multiturn`` -- few-shot, SFT with repair rounds, SFT + multi-turn GRPO, on tiers 3-5; ``tools``
 -- few-shot and SFT + GRPO at depths 1, 2 and 3 (stages T0-T2); ``arithmetic`` -- SFT + GRPO at
 stages 0-3; ``curriculum`` -- few-shot, SFT, SFT + curriculum GRPO over levels 1-9; ``agent`` --
-few-shot, SFT on 120 trajectories, SFT + GRPO.
+few-shot, SFT on 120 trajectories, SFT + GRPO; ``chat`` -- SFT on 2000 conversations.
 """
 
 from __future__ import annotations
@@ -47,7 +49,7 @@ class Stage:
     sft_examples: int = 0
     sft_steps: int = 0  # 0 -> 2 passes over the transcripts at the batch size
     grpo_steps: int = 0
-    kind: str = "coding"  # coding | multiturn | tools | arith | solve | agent
+    kind: str = "coding"  # coding | multiturn | tools | arith | solve | agent | chat
     depth: int = 1  # tools: calculator calls per task
     tiers: tuple[int, ...] = code_tasks.TIERS
     lr_sft: float = 3e-4
@@ -70,6 +72,7 @@ EXPERIMENTS: dict[str, list[Stage]] = {
     "arithmetic": [Stage(f"s{k}", 200, grpo_steps=40, kind="arith", depth=k) for k in range(4)],
     "curriculum": [Stage("fewshot", kind="solve", tiers=_ALL_LEVELS), Stage("sft300", 300, kind="solve", tiers=_ALL_LEVELS),
                    Stage("sft300_grpo", 300, grpo_steps=80, kind="solve", tiers=_ALL_LEVELS)],
+    "chat": [Stage("sft2000", 2000, kind="chat")],
     "agent": [Stage("fewshot", kind="agent"), Stage("sft120", 120, kind="agent"),
               Stage("sft120_grpo", 120, grpo_steps=30, kind="agent", group_size=4)],
 }
@@ -133,8 +136,32 @@ def _agent_tasks(n: int, seed: int, root: str):
     return terminal.load_tasks(d)
 
 
-def _transcripts(stage: Stage, seed: int, sandbox: str = "auto", task_root: str = ""):
+CHAT_HELDOUT = 32  # the first conversations of the stream are held out; training reads the ones after
+
+
+def chat_segments(messages: list[dict]) -> list[tuple[str, int]]:
+    """A conversation as ChatML segments: assistant contents with their end marker trained, the rest
+    context (the masking of ``data.chat.encode_chat``)."""
+    from ..data.chat import IM_END, IM_START
+
+    segs = []
+    for m in messages:
+        segs.append((f"{IM_START}{m['role']}\n", 0))
+        segs.append((f"{m['content']}{IM_END}\n", int(m["role"] == "assistant")))
+    return segs
+
+
+def _chat_rows(n: int, seed: int, root: str, skip: int = 0) -> list[list[dict]]:
+    from ..data import instruct
+
+    rows = list(instruct.chat_tooluse_mixture(root, seed=seed, limit=skip + n))
+    return [r["messages"] for r in rows[skip:]]
+
+
+def _transcripts(stage: Stage, seed: int, sandbox: str = "auto", task_root: str = "", chat_root: str = ""):
     rng = random.Random(seed)
+    if stage.kind == "chat":
+        return [chat_segments(m) for m in _chat_rows(stage.sft_examples, seed, chat_root, skip=CHAT_HELDOUT)]
     if stage.kind == "agent":
         return [agent_transcript(t, sandbox) for t in _agent_tasks(stage.sft_examples, seed, task_root)]
     if stage.kind == "arith":
@@ -165,7 +192,7 @@ def _transcripts(stage: Stage, seed: int, sandbox: str = "auto", task_root: str 
 def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_per_family: int = 1,
               max_program_tokens: int = 160, sft_batch: int = 8, seq_len: int = 1024, max_rounds: int = 3,
               eval_tools: int = 50, sandbox: str = "auto", task_root: str | None = None,
-              agent_turns: int = 4, save_dir: str | None = None) -> dict:
+              agent_turns: int = 4, save_dir: str | None = None, chat_root: str | None = None) -> dict:
     """Run one stage from a fresh policy; with ``save_dir`` the trained policy is exported there as a
     Hugging Face Qwen3 checkpoint (safetensors + config.json), so a separate evaluation, RL or
     serving job can load it."""
@@ -178,18 +205,33 @@ def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_pe
             return run_stage(stage, make_model, tok, seed=seed, eval_per_family=eval_per_family,
                              max_program_tokens=max_program_tokens, sft_batch=sft_batch, seq_len=seq_len,
                              max_rounds=max_rounds, eval_tools=eval_tools, sandbox=sandbox, task_root=root,
-                             agent_turns=agent_turns, save_dir=save_dir)
+                             agent_turns=agent_turns, save_dir=save_dir, chat_root=chat_root)
         finally:
             shutil.rmtree(root, ignore_errors=True)
     model = make_model()
     t0 = time.time()
     out: dict = {"stage": asdict(stage), "seed": seed}
+    chat_root = chat_root or os.environ.get("MXK_SFT_SNAPSHOTS", "")
+    held_chat = None
+    if stage.kind == "chat":  # held-out conversations: the assistant-token loss before and after SFT
+        import torch
+
+        from .chat_sft import masked_lm_loss, pack_segments
+
+        held_chat = pack_segments([chat_segments(m) for m in _chat_rows(CHAT_HELDOUT, seed, chat_root)], tok, seq_len)
+
+        def held_loss():
+            dev = next(model.parameters()).device
+            with torch.no_grad():
+                return float(masked_lm_loss(model, held_chat[0].to(dev), held_chat[1].to(dev)))
+
+        out["eval_before"] = {"heldout_assistant_loss": held_loss()}
     if stage.sft_examples:
         steps = stage.sft_steps or max(1, 2 * stage.sft_examples // sft_batch)
         cfg = ChatSFTConfig(steps=steps, batch_size=sft_batch, lr=stage.lr_sft, max_seq_len=seq_len, seed=seed)
-        losses = run_segment_sft(model, tok, _transcripts(stage, seed, sandbox, task_root), cfg)
+        losses = run_segment_sft(model, tok, _transcripts(stage, seed, sandbox, task_root, chat_root), cfg)
         out["sft"] = {"steps": steps, "first_loss": losses[0], "last_loss": losses[-1]}
-    if stage.kind not in ("coding", "multiturn", "tools", "arith", "solve", "agent"):
+    if stage.kind not in ("coding", "multiturn", "tools", "arith", "solve", "agent", "chat"):
         raise ValueError(f"unknown stage kind {stage.kind!r}")
     if stage.grpo_steps:
         if stage.kind == "tools":
@@ -247,7 +289,9 @@ def run_stage(stage: Stage, make_model: Callable, tok, *, seed: int = 0, eval_pe
         out["grpo"] = {"steps": len(hist), "reward_first": hist[0]["reward_mean"], "reward_last": hist[-1]["reward_mean"]}
     model.eval()
     ladder = [t for t in code_tasks.eval_tasks(eval_per_family) if t.tier in stage.tiers]
-    if stage.kind == "agent":
+    if stage.kind == "chat":
+        ev = {"heldout_assistant_loss": held_loss()}
+    elif stage.kind == "agent":
         from ..data.chat import IM_END, render_chatml
         from . import terminal
 

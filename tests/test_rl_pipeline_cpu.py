@@ -96,3 +96,26 @@ def test_tool_transcript_matches_environment():
     assert tools.total_reward(env) == pytest.approx(1.9)
     # the transcript is exactly what the environment renders for that episode
     assert "".join(t for t, _ in segs) == env.render()
+
+
+def test_chat_stage_on_local_snapshot(tmp_path, monkeypatch):
+    import json as _json
+
+    from marin_experiments_b200.data import instruct
+    from marin_experiments_b200.data.tokenize import ByteTokenizer
+
+    root = tmp_path / "snap"
+    d = root / "allenai/tulu-3-sft-mixture"
+    d.mkdir(parents=True)
+    with open(d / "train-0.jsonl", "w") as f:
+        for i in range(80):
+            f.write(_json.dumps({"messages": [{"role": "user", "content": f"say {i % 3}"},
+                                             {"role": "assistant", "content": f"ok {i % 3}"}]}) + "\n")
+    monkeypatch.setattr(instruct, "DEFAULT_MIX", {"allenai/tulu-3-sft-mixture": 1.0})
+    monkeypatch.setattr(pipeline, "EXPERIMENTS", {"chat": [pipeline.Stage("sft", 40, sft_steps=30, kind="chat",
+                                                                          lr_sft=3e-3)]})
+    res = pipeline.run("chat", _tiny, ByteTokenizer(), str(tmp_path / "res"), seq_len=128, chat_root=str(root))["sft"]
+    before, after = res["eval_before"]["heldout_assistant_loss"], res["eval"]["heldout_assistant_loss"]
+    assert after < 0.7 * before
+    segs = pipeline.chat_segments([{"role": "user", "content": "u"}, {"role": "assistant", "content": "a"}])
+    assert [m for _, m in segs] == [0, 0, 0, 1] and segs[3][0] == "a<|im_end|>\n"
