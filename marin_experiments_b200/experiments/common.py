@@ -38,6 +38,8 @@ class GrugLaunchConfig:
     save_interval_s: float = 30 * 60
     keep: tuple | None = None
     eval_only: bool = False
+    # a models.looped.LoopedConfig: train the re-entrant (looped) variant of ``model`` instead
+    looped: object = None
 
 
 def to_run_config(c: GrugLaunchConfig) -> GrugRunConfig:
@@ -56,4 +58,10 @@ def to_run_config(c: GrugLaunchConfig) -> GrugRunConfig:
 def run_inline(c: GrugLaunchConfig) -> dict:
     from ..train.run import run_grug
 
-    return run_grug(to_run_config(c), tracker=c.tracker, eval_only=c.eval_only)
+    factory = None
+    if c.looped is not None:
+        from ..models.looped import LoopedTransformer
+
+        lc = dataclasses.replace(c.looped, model=c.model)
+        factory = lambda cfg, local: LoopedTransformer(dataclasses.replace(lc, model=cfg))  # noqa: E731
+    return run_grug(to_run_config(c), tracker=c.tracker, eval_only=c.eval_only, model_factory=factory)

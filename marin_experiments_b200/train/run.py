@@ -38,7 +38,7 @@ def _device() -> torch.device:
 
 
 def run_grug(cfg: GrugRunConfig, *, tracker: str = "jsonl", hooks=(), eval_only: bool = False,
-             device: torch.device | None = None, peak_flops_per_gpu: float = 2.25e15) -> dict:
+             device: torch.device | None = None, peak_flops_per_gpu: float = 2.25e15, model_factory=None) -> dict:
     tcfg = cfg.trainer.trainer
     dist_ctx = None
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
@@ -50,7 +50,8 @@ def run_grug(cfg: GrugRunConfig, *, tracker: str = "jsonl", hooks=(), eval_only:
     world = dist_ctx.world if dist_ctx else 1
     run_id = tcfg.id or "grug"
     micro = tcfg.per_device_parallelism if tcfg.per_device_parallelism > 0 else None
-    trainer = Trainer(cfg, device=device, micro_batch=micro, num_train_steps=tcfg.num_train_steps, dist=dist_ctx)
+    trainer = Trainer(cfg, device=device, micro_batch=micro, num_train_steps=tcfg.num_train_steps, dist=dist_ctx,
+                      model_factory=model_factory)
     ck_cfg = tcfg.checkpointer
     if not os.path.isabs(ck_cfg.base_path):
         import dataclasses

@@ -196,7 +196,9 @@ class Trainer:
                 perf = {"throughput/step_duration": dt, "throughput/loading_time": t_load,
                         "throughput/hook_time": hook_time}
                 for h in hooks:  # e.g. the throughput hook's tokens/s and MFU of this step
-                    perf.update(getattr(h, "last", None) or {})
+                    last_h = getattr(h, "last", None)
+                    if isinstance(last_h, dict):
+                        perf.update(last_h)
                 tracker.log({**{k: (float(v.float().mean()) if torch.is_tensor(v) else v) for k, v in met.items()
                                 if not (torch.is_tensor(v) and v.numel() > 1)}, **router_layer_metrics(met),
                              **perf}, step=self.step)

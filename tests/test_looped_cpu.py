@@ -104,3 +104,40 @@ def test_depth_sweep_and_tagged_eval():
     assert abs(tagged["eval/R2/micro_loss"] - (2 * lw + lc_) / 3) < 1e-9
     plain = evaluate_tagged(tr, {"web": web}, prefix="x")
     assert set(plain) == {"x/web/loss", "x/macro_loss", "x/micro_loss"}
+
+
+def test_reentrant_launcher_trains_looped_variant(tmp_path, monkeypatch):
+    """The launcher's looped config reaches the trainer (a LoopedTransformer is built and trained)."""
+    from marin_experiments_b200.config import DataConfig
+    from marin_experiments_b200.experiments import reentrant
+    from marin_experiments_b200.experiments.common import GrugLaunchConfig, run_inline
+    from marin_experiments_b200.optim import GrugMoeAdamHConfig
+    from marin_experiments_b200.train import trainer as T
+
+    lc = LoopedConfig(model=M, num_prelude_layers=1, num_coda_layers=1, recurrence_steps=2, iteration_film=True)
+    built = []
+    orig = T.Trainer._build
+
+    def spy(self):
+        orig(self)
+        built.append(type(self.model).__name__)
+
+    monkeypatch.setattr(T.Trainer, "_build", spy)
+    cfg = GrugLaunchConfig(model=M, looped=lc, data=DataConfig(source="synthetic"), output_path=str(tmp_path),
+                           run_id="loop", steps=2, batch_size=2, optimizer=GrugMoeAdamHConfig(warmup=0.0),
+                           mp="params=float32,compute=float32,output=float32", save_interval_s=1e9)
+    try:
+        run_inline(cfg)
+    except Exception as e:  # the native data loader is part of the package build
+        if "runtime" not in str(e).lower() and "_mxrt" not in str(e):
+            raise
+        pytest.skip(f"native runtime unavailable: {e}")
+    assert built == ["LoopedTransformer"]
+    monkeypatch.setenv("GRUG_EXPERIMENT", "e0,e3,e64")
+    names = [s.name for s in reentrant.build_steps()]
+    assert names == ["grug/reentrant_e0", "grug/reentrant_e3", "grug/reentrant_e64"]
+    exps = reentrant.experiments()
+    assert exps["e3"][1].recurrence_choices == (2, 4, 8) and exps["e64"][1].anytime_supervision
+    assert exps["e0"][1] is None and exps["e1"][1].effective_depth() == exps["e0"][0].num_layers
+    with pytest.raises(KeyError, match="unknown experiment"):
+        reentrant.build_steps(["e9"])
