@@ -1,6 +1,6 @@
 """Instruction / chat SFT datasets: rows of several source layouts normalised to chat messages, a
 registry of the datasets used for chat and tool-use SFT, and a weighted interleave of them
-(tunix-delphi-rl/sft_data/instruction_datasets.py).
+(tunix-delphi-rl/sft_data/instruction_datasets.py:80-682).
 
 Every source row becomes ``{"messages": [{"role", "content"}, ...], "metadata": {...}}`` with roles
 in ``system / user / assistant / tool``, or ``None`` when the row cannot be turned into a

@@ -1,5 +1,5 @@
 """Staged single-turn arithmetic for GRPO on a base (non-chat) model
-(tunix-delphi-rl/problems/arithmetic.py, tunix-delphi-rl/training/train_delphi.py).
+(tunix-delphi-rl/problems/arithmetic.py:1-389, tunix-delphi-rl/training/train_delphi.py:1-222).
 
 A base model follows a format only when the demonstrations in front of the query are of the same
 kind of task, so every stage carries its own few-shot block and the prompt ends exactly where the

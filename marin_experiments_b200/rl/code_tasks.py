@@ -1,6 +1,6 @@
 """Tiered, parameterised coding tasks for single-turn program-writing RL, a held-out evaluation
-ladder and the transcript format shared by SFT and RL (tunix-delphi-rl/environments/coding_env.py,
-tunix-delphi-rl/problems/coding_tasks.py, tunix-delphi-rl/training/train_coding.py).
+ladder and the transcript format shared by SFT and RL (tunix-delphi-rl/environments/coding_env.py:1-1173,
+tunix-delphi-rl/problems/coding_tasks.py:1-1001, tunix-delphi-rl/training/train_coding.py:1-326).
 
 The policy sees ``CODE_FEWSHOT`` + ``Task: <prompt>`` and writes a program ended by a line ``END``;
 the sandboxed interpreter (``rl.micropy``) runs it and the reward compares its stdout with the

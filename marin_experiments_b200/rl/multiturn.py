@@ -1,6 +1,6 @@
 """Multi-turn GRPO: whole episodes (assistant turns interleaved with tool / interpreter output) as
-one trained sequence per rollout (tunix-delphi-rl/training/train_multiturn.py,
-tunix-delphi-rl/training/train_agentic.py).
+one trained sequence per rollout (tunix-delphi-rl/training/train_multiturn.py:1-492,
+tunix-delphi-rl/training/train_agentic.py:1-805).
 
 An environment exposes ``render()`` (the opening text), ``step(text) -> done``, ``feedback`` (the
 text it answers the last turn with, ``None`` once done) and ``reward()``; ``rl.tools.CalcToolEnv``

@@ -1,5 +1,5 @@
-"""Idempotent runner of the coding tuning ladders (tunix-delphi-rl/training/pipeline.py,
-tunix-delphi-rl/training/train_coding.py, tunix-delphi-rl/training/train_multiturn.py).
+"""Idempotent runner of the coding tuning ladders (tunix-delphi-rl/training/pipeline.py:72-311,
+tunix-delphi-rl/training/train_coding.py:1-326, tunix-delphi-rl/training/train_multiturn.py:1-492).
 
 Each round of tuning is a ``Stage`` declared as data: how many SFT transcripts to warm up on, how
 many GRPO steps to take afterwards, and the kind of episode -- ``coding`` (write one program,

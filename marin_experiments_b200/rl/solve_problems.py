@@ -1,6 +1,6 @@
 """Function-writing problems graded on many test cases: nine levels of parameterised ``def solve``
-families with public and hidden tests, for curriculum RL (tunix-delphi-rl/problems/coding_problems.py,
-tunix-delphi-rl/environments/curriculum_env.py).
+families with public and hidden tests, for curriculum RL (tunix-delphi-rl/problems/coding_problems.py:93-1260,
+tunix-delphi-rl/environments/curriculum_env.py:1-397).
 
 A problem asks for ``def solve(...)``; the prompt shows its signature, a description and the
 public tests, and the grade runs the submitted program on every public and hidden test through

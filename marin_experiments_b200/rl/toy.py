@@ -1,5 +1,5 @@
 """A toy GRPO run that shows the learner learning in seconds on a CPU
-(tunix-delphi-rl/examples/toy_cats.py).
+(tunix-delphi-rl/examples/toy_cats.py:64-470).
 
 A word-level tokenizer over a dozen words, a one-layer Qwen3 policy from random weights, prompts
 that are a fixed opener, and a reward equal to the share of generated words that are ``cat``. A

@@ -1,4 +1,4 @@
-"""Client of the serving API (tunix-delphi-rl/serving/query.py): ``health``, ``generate`` (one
+"""Client of the serving API (tunix-delphi-rl/serving/query.py:1-187): ``health``, ``generate`` (one
 prompt or a batch through ``POST /generate``) and ``complete`` (``POST /v1/completions``), over
 plain HTTP with a timeout, plus a command line. The reference resolves its endpoint through its
 cluster's proxy; here the caller passes the server's base URL (``--url`` or ``MXK_SERVE_URL``).

@@ -1,7 +1,7 @@
 """Train this project's own tokenizers: a domain-weighted raw-text corpus, plain BPE / SuperBPE
 arms trained on it, exported as Hugging Face ``tokenizer.json`` + ``tokenizer_config.json`` and
 published to a tokenizer mirror that ``data.tokenize.load_tokenizer("trained/<name>")`` reads
-(tokenization/corpus.py, tokenization/train_tokenizer.py).
+(tokenization/corpus.py:74-182, tokenization/train_tokenizer.py:66-362).
 
 * ``build_corpus(source_root, out_dir)``: each domain of ``TRAIN_DOMAINS`` (English web, code,
   several languages, math) gets ``total_bytes`` x its weight, split evenly over its sources; from
