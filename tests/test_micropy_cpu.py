@@ -109,3 +109,63 @@ def test_output_limit_keeps_prefix():
 def test_deterministic():
     src = "def fib(n):\n  return n if n < 2 else fib(n - 1) + fib(n - 2)\nprint(fib(12))"
     assert run(src) == run(src)
+
+
+_AGREE = [
+    "print(7, 'a', True, None)",
+    "print(17 // 5, -17 // 5, 17 % 5, -17 % 5, 2 ** 10, 7 / 2)",
+    "print(0.1 + 0.2, 3.5 * 2, round(2.675, 2), -2 ** 2)",
+    "print(not 0, -(-3), +4, ~5)",
+    "a, b = 1, 2\na, b = b, a\nprint(a, b)",
+    "x = [1, 2, 3]\nx[1] = 9\nx[-1] += 1\nprint(x)",
+    "print(1 < 2 < 3, 3 > 2 > 2, 1 == 1.0, 'a' < 'b')",
+    "print(0 or 'x', 1 and 0, [] or [1], 2 in [1, 2], 'bc' in 'abc', 3 not in (1, 2))",
+    "print('y' if 2 > 1 else 'n')",
+    "n = 0\nwhile True:\n  n += 1\n  if n % 2:\n    continue\n  if n > 6:\n    break\nprint(n)",
+    "for i in range(3):\n  pass\nelse:\n  print('done', i)",
+    "for i in range(5):\n  if i == 2:\n    break\nelse:\n  print('no')\nprint(i)",
+    "def f(a, b=2, c=3):\n  return a + b * c\nprint(f(1), f(1, c=10), f(b=0, a=5))",
+    "g = 5\ndef h():\n  x = g + 1\n  return x\nprint(h())",
+    "def fib(n):\n  return n if n < 2 else fib(n - 1) + fib(n - 2)\nprint(fib(15))",
+    "def nothing():\n  pass\nprint(nothing())",
+    "print([i * i for i in range(6) if i % 2])",
+    "xs = list(range(10))\nprint(xs[2:8:2], xs[::-3], xs[-2:], len(xs))",
+    "print([1, 2] + [3] * 2, 'ab' * 3)",
+    "x = [3, 1, 2]\nx.append(5)\nx = sorted(x)\nx.insert(0, 9)\nprint(x, x.pop(), x.index(3), x.count(9))",
+    "print(sum([1, 2, 3]), min(4, 2, 8), max([1, 9, 3]), sorted([3, 1, 2], reverse=True), abs(-4))",
+    "print(list(enumerate('ab', 1)), list(zip([1, 2], 'xy')), list(reversed([1, 2, 3])))",
+    "s = 'Hello World'\nprint(s.lower(), s.upper(), s.split(), s.replace('l', 'L'), s.startswith('He'), s.find('o'))",
+    "print(' x '.strip(), ','.join(['a', 'b']), 'abc'[1], 'abc'[::-1], 'a-b-c'.split('-'))",
+    "v = 3.14159\nn = 42\nprint(f'{n:5d}|{v:.2f}|{n * 2}|{\"q\"}')",
+    "print('%d items at %.1f %s' % (3, 2.25, 'each'))",
+    "print(1, 2, sep='-', end='!\\n')\nprint()\nprint('a', 'b', sep='')",
+    "print(int('12') + int(3.9), float('2.5'), str(7) + '!', bool(''), divmod(17, 5))",
+]
+
+
+@pytest.mark.parametrize("src", _AGREE)
+def test_agrees_with_cpython(src):
+    import contextlib
+    import io
+
+    buf = io.StringIO()
+    with contextlib.redirect_stdout(buf):
+        exec(compile(src, "<p>", "exec"), {})  # the programs above, written in this file
+    r = run(src)
+    assert r.ok, r.error
+    assert r.stdout == buf.getvalue()
+
+
+@pytest.mark.parametrize("src,kind", [
+    ("print(1 +", "SyntaxError"), ("print(zz)", "NameError"), ("print(1 / 0)", "ZeroDivisionError"),
+    ("print([1][3])", "IndexError"), ("print(1 + 'a')", "TypeError"), ("x = 3\nx()", "TypeError"),
+    ("a, b = [1, 2, 3]", "ValueError"), ("while True:\n  pass", "StepLimit"),
+    ("def f():\n  return f()\nf()", "RecursionError"), ("import os", "UnsupportedSyntax"),
+    ("from os import path", "UnsupportedSyntax"), ("class A:\n  pass", "UnsupportedSyntax"),
+    ("with open('x') as f:\n  pass", "UnsupportedSyntax"),
+    ("[].sort()", "AttributeError"),  # in-place sort is outside the whitelisted list methods
+    ("def f(*a):\n  return a", "UnsupportedSyntax"),
+])
+def test_error_kinds(src, kind):
+    r = run(src, max_steps=20_000)
+    assert not r.ok and r.error.startswith(kind), r.error
