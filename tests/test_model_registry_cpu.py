@@ -45,3 +45,24 @@ def test_checkpoint_checks_and_load(tmp_path, monkeypatch):
     json.dump(cfg, open(os.path.join(d, "config.json"), "w"))
     with pytest.raises(ValueError, match="Llama-3 RoPE scaling"):
         R.check_checkpoint("tiny", d)
+
+
+def test_llama3_rope_matches_transformers():
+    """The Llama-3 RoPE frequency scaling (Delphi's rope setup) against transformers' own implementation."""
+    import warnings
+
+    from transformers import Qwen3Config as HFQwen3Config
+    from transformers.modeling_rope_utils import ROPE_INIT_FUNCTIONS
+
+    from marin_experiments_b200.ops import reference as OR
+
+    spec = R.get_spec("delphi").config
+    hf = HFQwen3Config(hidden_size=spec.hidden_dim, num_attention_heads=spec.num_heads, head_dim=spec.head_dim,
+                       rope_theta=spec.rope_theta, rope_scaling=dict(spec.rope_scaling), max_position_embeddings=16384)
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        want, _ = ROPE_INIT_FUNCTIONS["llama3"](hf, "cpu")
+    base = 1.0 / (spec.rope_theta ** (torch.arange(0, spec.head_dim, 2, dtype=torch.float64) / spec.head_dim))
+    got = OR.llama3_scale_inv_freq(base, **spec.llama3())
+    assert torch.allclose(got.double(), want.double(), rtol=1e-6, atol=0)
+    assert not torch.allclose(base, want.double(), rtol=1e-3)  # the scaling changes most components
