@@ -202,3 +202,27 @@ def test_served_model_as_agent_policy(tmp_path):
     finally:
         srv.should_exit = True
         th.join(timeout=10)
+
+
+def test_logits_match_transformers_qwen3(tmp_path):
+    """Our Qwen3 forward (learned q/k norms, GQA, Llama-3 RoPE scaling, SwiGLU) against transformers'
+    Qwen3ForCausalLM loaded from our export."""
+    import warnings
+
+    from transformers import Qwen3ForCausalLM
+
+    cfg = Qwen3Config(vocab_size=300, hidden_dim=64, intermediate_dim=128, num_layers=2, num_heads=4, num_kv_heads=2,
+                      head_dim=32, rope_theta=500000.0,
+                      rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                    "high_freq_factor": 4.0, "original_max_position_embeddings": 64},
+                      norm_eps=1e-5, max_seq_len=256)
+    m = Qwen3Model(cfg).init_weights(2)
+    d = export_hf(m, str(tmp_path / "hf"), dtype=torch.float32)
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        hf = Qwen3ForCausalLM.from_pretrained(d, torch_dtype=torch.float32).eval()
+    tok = torch.randint(0, 300, (2, 40), generator=torch.Generator().manual_seed(1))
+    with torch.no_grad():
+        want = hf(input_ids=tok).logits
+        got = m.forward_reference(tok)
+    assert torch.allclose(got.float(), want.float(), atol=2e-4, rtol=2e-4), (got - want).abs().max()
