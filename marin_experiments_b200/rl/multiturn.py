@@ -10,7 +10,8 @@ mask 0), and the policy is conditioned on that transcript rather than on a re-en
 environment's text, so the trained tokens are exactly the sampled ones. A turn ends at the stop
 string or after ``max_turn_tokens`` tokens. Each group of ``group_size`` episodes of one task gets
 group-relative advantages from the episode rewards, and the clipped policy-gradient loss runs over
-the assistant tokens of every turn.
+the assistant tokens of every turn. With ``use_engine`` each turn is decoded by the serving engine
+(KV cache) from the transcript so far, its weights refreshed from the policy once per step.
 """
 
 from __future__ import annotations
@@ -38,9 +39,27 @@ class MultiTurnGRPO(GRPOLearner):
         self.reward_fn = reward_fn or (lambda env: env.reward())
         super().__init__(model, tokenizer, None, cfg or MultiTurnConfig())
 
+    def _engine(self):
+        from ..serving.engine import Engine
+
+        if getattr(self, "engine", None) is None:
+            self.engine = Engine(self.model, self.tok, max_batch=1, max_len=min(self.model.cfg.max_seq_len, 4096))
+            self._engine_calls = 0
+        return self.engine
+
     @torch.no_grad()
     def _turn(self, ids: list[int]) -> list[int]:
         c = self.cfg
+        if c.use_engine:  # KV-cache decode; the turn ends at the stop string, end of document or budget
+            from ..serving.engine import SamplingParams
+
+            budget = min(c.max_turn_tokens, c.max_total_tokens - len(ids), self.engine.max_len - len(ids))
+            if budget <= 0:
+                return []
+            self._engine_calls += 1
+            p = SamplingParams(max_tokens=budget, temperature=c.temperature, stop=(c.stop,),
+                               seed=c.seed * 1_000_003 + self._engine_calls)
+            return self.engine.generate_ids([ids], p)[0]
         out: list[int] = []
         for _ in range(c.max_turn_tokens):
             if len(ids) + len(out) >= c.max_total_tokens:
@@ -70,6 +89,8 @@ class MultiTurnGRPO(GRPOLearner):
 
     def step(self, n_prompts: int = 2) -> dict:
         c = self.cfg
+        if c.use_engine:  # this step's rollouts sample from the current weights
+            self._engine().refresh_weights()
         rows, masks, rewards, envs = [], [], [], []
         for _ in range(n_prompts):
             task = self.sample_task()

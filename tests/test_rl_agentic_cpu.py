@@ -170,3 +170,22 @@ def test_multiturn_transcript_masks_feedback():
     assert text.endswith("CALC(12 * 13)\nTool result: 156\n156\n")
     trained = tok.decode([t for t, k in zip(ids, mask) if k])
     assert trained == "CALC(12 * 13)\n156\n" and abs(tools.total_reward(env) - 1.9) < 1e-9
+
+
+def test_multiturn_grpo_with_engine_turns():
+    from marin_experiments_b200.data.tokenize import ByteTokenizer
+    from marin_experiments_b200.models.qwen3 import Qwen3Config, Qwen3Model
+    from marin_experiments_b200.rl.multiturn import MultiTurnConfig, MultiTurnGRPO
+
+    cfg = Qwen3Config(vocab_size=257, hidden_dim=64, intermediate_dim=128, num_layers=1, num_heads=2, num_kv_heads=1,
+                      head_dim=32, max_seq_len=1024)
+    m = Qwen3Model(cfg).init_weights(0)
+    before = m.layers[0].w_q.detach().clone()
+    tasks = iter(tools.chain_tasks(8, seed=1, depth=1))
+    lr = MultiTurnGRPO(m, ByteTokenizer(), lambda: next(tasks),
+                       lambda t: tools.CalcToolEnv(t, system="CALC(x * y), then the result.\n"),
+                       MultiTurnConfig(group_size=2, max_turn_tokens=6, lr=1e-2, max_total_tokens=96, use_engine=True),
+                       reward_fn=tools.total_reward)
+    met = lr.step(n_prompts=2)
+    assert lr.engine is not None and met["trained_tokens"] > 0 and torch.isfinite(torch.tensor(met["loss"]))
+    assert not torch.equal(before, m.layers[0].w_q.detach())
